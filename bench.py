@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""YOLO26n FP32 640x640 inference throughput on B200 (images/s).
+
+Workload: the YOLO26n forward (backbone, neck, Detect head, top-300 decode)
+on seeded U[0,1) 640x640 images with seeded random-init weights in the
+converter's .bin layout, 64 images per GPU per step.  64 is the batch of the
+8-GPU benchmark configuration; each GPU runs its own 64-image shard
+(image-parallel, no collective), so scaling is weak.
+
+  value    images/s of the whole job with the inputs already in HBM:
+           K graph launches of yb_cuda_forward_device, timed with CUDA events
+           on the launching stream, max over ranks.
+  e2e      the same through the host API yb_cuda_forward: pinned host input
+           copied to HBM every step, detections copied back every step.
+  roofline the tcgen05 convolution family (every conv launch of a forward),
+           algorithmic bytes / measured time against the measured HBM copy
+           bandwidth, plus conv TFLOP/s against the measured bf16 peak.
+  cpu_baseline  the reference's own C forward (compiled from its sources under
+           oracle/_ref) on the host cores, one process per core.
+
+`--impl reference` times that CPU reference alone, on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "yolo-baremetal_b200")
+sys.path.insert(0, PKG)
+
+METRIC = "images/sec YOLO26n 640² FP32 & INT8 at 1/2/4/8 B200; conv TFLOPS/TOPS vs peak"
+UNIT = "images/s"
+DATA = ("synthetic: seeded U[0,1) 640x640 images (numpy PCG64), seeded random-init YOLO26n weights "
+        "(Kaiming conv, BN gamma 1+-0.1, beta/mean N(0,0.1), var U(0.5,1.5)) in the converter .bin layout")
+# DRAM bytes (read + write) of the conv family per image, from the ncu capture
+# summarised in profiles/conv_tc_yolo26n_640.md; None until captured.
+CONV_DRAM_BYTES_PER_IMAGE = None
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        p = json.load(open(path))
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str | None):
+        self.bus_id = bus_id
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        try:
+            self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+            if self.bus_id:
+                cmd += ["-i", self.bus_id]
+            self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.out:
+            return None
+        try:
+            rows = [r.split(",") for r in open(self.out.name).read().strip().splitlines() if r.strip()]
+            os.unlink(self.out.name)
+        except Exception:
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for i, n in enumerate(names):
+                    if r[5 + i].strip().lower().startswith("active"):
+                        reasons.add(n)
+            except Exception:
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def bus_id_of(dev: int):
+    try:
+        import torch
+
+        p = torch.cuda.get_device_properties(dev)
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- CPU reference
+def _ref_worker(conn, weights, H, W, seed, use_ref):
+    """One host core: loads the CPU implementation once, then runs one forward
+    per 'go' message and replies with the elapsed seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np  # noqa: F401
+    import yb_weights as yw
+
+    img = yw.make_input(seed, H, W).reshape(-1)
+    if use_ref:
+        import oracle as orc
+
+        lib = orc.Reference.lib()
+        lib.ref_open.restype = C.c_void_p
+        lib.ref_open.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int]
+        lib.ref_run.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
+        h = lib.ref_open(weights.encode(), H, W, 1)
+        run = lambda: lib.ref_run(h, img.ctypes.data, None)  # noqa: E731
+    else:
+        import oracle as orc
+
+        o = orc.Oracle(weights)
+        run = lambda: o.forward(img.reshape(1, 3, H, W))  # noqa: E731
+    conn.send("ready")
+    while True:
+        msg = conn.recv()
+        if msg == "stop":
+            break
+        t0 = time.perf_counter()
+        st = run()
+        conn.send((time.perf_counter() - t0, st if isinstance(st, int) else 0))
+
+
+class CpuPool:
+    def __init__(self, procs, weights, H, W, use_ref):
+        ctx = mp.get_context("spawn")
+        self.conns, self.ps = [], []
+        for i in range(procs):
+            a, b = ctx.Pipe()
+            p = ctx.Process(target=_ref_worker, args=(b, weights, H, W, 1000 + i, use_ref), daemon=True)
+            p.start()
+            self.conns.append(a)
+            self.ps.append(p)
+        for c in self.conns:
+            assert c.recv() == "ready"
+
+    def step(self):
+        t0 = time.perf_counter()
+        for c in self.conns:
+            c.send("go")
+        res = [c.recv() for c in self.conns]
+        if any(r[1] != 0 for r in res):
+            raise RuntimeError("CPU reference forward failed")
+        return time.perf_counter() - t0
+
+    def close(self):
+        for c in self.conns:
+            c.send("stop")
+        for p in self.ps:
+            p.join(timeout=10)
+
+
+def cpu_kind():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+
+    return ("reference", True) if orc.Reference.available() else ("port", False)
+
+
+def cpu_baseline(weights, H, W, procs, steps):
+    kind, use_ref = cpu_kind()
+    pool = CpuPool(procs, weights, H, W, use_ref)
+    try:
+        total = sum(pool.step() for _ in range(steps))
+    finally:
+        pool.close()
+    return {"value": procs * steps / total, "unit": UNIT, "cores": procs, "kind": kind,
+            "sample": f"{procs} processes x {steps} single-image {W}x{H} forwards (one per core), wall time"}
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+# --------------------------------------------------------------------- main
+def make_weights(tmpdir):
+    import yb_weights as yw
+
+    path = os.path.join(tmpdir, "yolo26n_seed0.bin")
+    yw.write_bin(path, yw.random_state("n", 0))
+    return path
+
+
+def config(n, batch, hw):
+    return {"workload": f"YOLO26n FP32 forward + top-300 decode, {hw}x{hw}, {batch} images per GPU "
+                        f"(the batch-64 benchmark shard), image-parallel",
+            "images_per_gpu": batch, "global_batch": batch * n, "input_hw": [hw, hw],
+            "parallelism": f"dp{n} (image sharding, no collective)",
+            "l2_policy": "inputs larger than L2 (315 MB of input and >3 GB of activations per GPU per step)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    with tempfile.TemporaryDirectory() as td:
+        weights = make_weights(td)
+        procs = os.cpu_count() or 1
+        kind, use_ref = cpu_kind()
+        pool = CpuPool(procs, weights, args.hw, args.hw, use_ref)
+        try:
+            for _ in range(args.warmup):
+                pool.step()
+            total = sum(pool.step() for _ in range(args.steps))
+        finally:
+            pool.close()
+    value = procs * args.steps / total
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": DATA,
+            "config": config(args.gpus, args.batch, args.hw), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": procs, "kind": kind,
+                             "sample": f"each step: {procs} processes run one {args.hw}x{args.hw} forward each "
+                                       f"({cpu_model()})"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    B, H = args.batch, args.hw
+    tmpdir = tempfile.mkdtemp(prefix=f"yb_bench_{rank}_")
+    weights = make_weights(tmpdir)
+    model = yb.Model(weights, device=local)
+    imgs = yw.make_batch(range(rank * B + 1, rank * B + B + 1), H, H)
+    host_in = torch.from_numpy(imgs).pin_memory()
+    host_out = torch.empty((B, 300, 6), dtype=torch.float32).pin_memory()
+    L = yb.lib()
+
+    def e2e_step():
+        yb.check(L.yb_cuda_forward(model.ctx, host_in.data_ptr(), B, H, H, host_out.data_ptr(), 300, None, None, None),
+                 "yb_cuda_forward")
+
+    e2e_step()  # builds the plan and leaves this rank's images resident in HBM
+    d_in, d_out = model.plan_io(B, H, H)
+    stream = torch.cuda.current_stream()
+
+    def dev_step():
+        model.forward_device(d_in, d_out, B, H, H, 300, stream.cuda_stream)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        dev_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(bus_id_of(local) if rank == 0 else None) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            dev_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    clocks = clk.summary() if rank == 0 else None
+
+    # End to end through the host API: H2D of the pinned batch, forward, D2H.
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+
+    n_ops = C.c_int()
+    yb.check(L.yb_cuda_profile_ops(model.ctx, B, H, H, 300, 0, None, 0, C.byref(n_ops)), "yb_cuda_profile_ops")
+    line = None
+    if rank == 0:
+        stats = (OpStat * n_ops.value)()
+        yb.check(L.yb_cuda_profile_ops(model.ctx, B, H, H, 300, 3, stats, n_ops.value, C.byref(n_ops)),
+                 "yb_cuda_profile_ops")
+        conv = [s for s in stats if s.kind == 0]
+        conv_ms = sum(s.ms for s in conv)
+        conv_bytes = sum(s.bytes for s in conv)
+        conv_flops = sum(s.flops for s in conv)
+        all_ms = sum(s.ms for s in stats)
+        hbm, bf16, src = peaks()
+        achieved = conv_bytes / (conv_ms * 1e-3) / 1e9
+        per_kind = {}
+        for s in stats:
+            k = ["conv_tc", "stem", "dwconv", "maxpool", "attention", "decode", "topk"][s.kind]
+            d = per_kind.setdefault(k, {"launches": 0, "ms": 0.0})
+            d["launches"] += 1
+            d["ms"] += s.ms
+        for d in per_kind.values():
+            d["share"] = d["ms"] / all_ms
+        value = world * B * args.steps / (dev_ms * 1e-3)
+        traffic = CONV_DRAM_BYTES_PER_IMAGE * B / len(conv) if CONV_DRAM_BYTES_PER_IMAGE else None
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "precision": "fp32 activations in HBM; conv products as bf16 hi/lo pairs (3 tcgen05 UMMAs) "
+                             "with fp32 accumulation in TMEM",
+                "data": DATA, "config": config(world, B, H),
+                "e2e": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
+                        "h2d_bytes_per_step": world * host_in.numel() * 4,
+                        "d2h_bytes_per_step": world * host_out.numel() * 4},
+                "gpu_launches": n_ops.value * args.steps,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                             "frac": achieved / hbm, "traffic": traffic,
+                             "kernel": "conv_tc_kernel (all tcgen05 convolution launches of one forward)",
+                             "launches": len(conv), "bytes_per_launch": conv_bytes / len(conv),
+                             "ms_per_launch": conv_ms / len(conv), "peak_source": src},
+                "conv_tflops": {"achieved": conv_flops / (conv_ms * 1e-3) / 1e12, "peak": bf16,
+                                "frac": conv_flops / (conv_ms * 1e-3) / 1e12 / bf16, "peak_source": src,
+                                "note": "algorithmic FP32 FLOPs; the tensor pipe executes 3x (split-bf16)"},
+                "forward_breakdown_ms": {k: round(v["ms"], 4) for k, v in per_kind.items()},
+                "forward_share": {k: round(v["share"], 4) for k, v in per_kind.items()},
+                "clocks": clocks}
+    model.close()
+    if dist:
+        dist.barrier()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        procs = min(os.cpu_count() or 1, 64)
+        line["cpu_baseline"] = cpu_baseline(weights, H, H, procs, 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+class OpStat(C.Structure):
+    _fields_ = [("kind", C.c_int), ("step", C.c_int), ("ms", C.c_double), ("flops", C.c_double),
+                ("bytes", C.c_double)]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--hw", type=int, default=640)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,116 @@
+#ifndef YB_CUDA_H
+#define YB_CUDA_H
+
+/* C-ABI shim between the YOLO26 host API and the B200 (sm_100a) backend.
+ *
+ * Plain pointers and sizes only.  The reference has no device boundary; these
+ * entry points replace the layer calls that src/model.c makes inside
+ * model_forward_ex (model.c:764-903) and the Detect head call
+ * detect_forward_one2one (detect.c:253-454) of phucb2/yolo-baremetal, so a
+ * GPU-enabled model.c calls yb_cuda_forward where the reference walks its 24
+ * layer steps.  One context = one device replica; contexts are independent
+ * and may live on different GPUs (image-sharded multi-GPU needs no
+ * collective: see yb_cuda_forward_sharded).
+ *
+ * All entry points return status_t (status.h).  CUDA failures map to
+ * ERROR_OUT_OF_MEMORY (allocation) or ERROR_DEVICE (anything else, including a
+ * kernel that reported a bounded-wait timeout); yb_cuda_last_error() returns a
+ * one-line description of the last failure on the calling thread. */
+
+#include "model.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    /* FP32 semantics: fp32 activations in HBM, convolutions as split-bf16
+     * (hi+lo, three tcgen05 products) with fp32 accumulation in TMEM. */
+    YB_PRECISION_FP32 = 0,
+    /* Reserved for the int8 path (kind::i8, int32 accumulation). */
+    YB_PRECISION_INT8 = 1
+} yb_precision;
+
+/* Stage callback: called once per stage tensor (NCHW float32 host data of
+ * image 0) with the reference's stage names stage_00_input .. stage_25_detect. */
+typedef void (*yb_stage_cb)(void* user, const char* name, const float* nchw, int n, int c, int h, int w);
+
+/* Creates a context on CUDA device `device` (its own stream and arena). */
+status_t yb_cuda_init(int device, void** ctx);
+
+/* Packs and uploads the BN-folded weights of `m` (after model_load_weights /
+ * fold_all_bn).  qparams is reserved for YB_PRECISION_INT8 and must be NULL. */
+status_t yb_cuda_upload_weights(void* ctx, const model_t* m, yb_precision p, const void* qparams);
+
+/* Convenience for hosts without a model_t: reads a converter-layout .bin,
+ * folds BatchNorm like model_load_weights and uploads. */
+status_t yb_cuda_load_bin(void* ctx, const char* path);
+
+/* Forward on host buffers: in_nchw [B,3,H,W] float32 (H, W multiples of 32),
+ * out_dets [B,max_det,6] float32.  The input is copied to HBM, the captured
+ * graph for (B,H,W) runs, and the detections come back; the call returns
+ * when they are in out_dets.  dump (nullable) receives the stage tensors;
+ * step_ms (nullable, MODEL_FORWARD_PROFILE_STEPS doubles) receives per-step
+ * device times.  Either one makes the forward run eagerly instead of from the
+ * captured graph. */
+status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int H, int W,
+                         float* out_dets, int max_det,
+                         yb_stage_cb dump, void* user, double* step_ms);
+
+/* Forward on device buffers already in this context's GPU memory:
+ * d_in [B,3,H,W], d_out [B,max_det,6].  Enqueued on `stream` (a
+ * cudaStream_t; NULL = the context's own stream); does not synchronize. */
+status_t yb_cuda_forward_device(void* ctx, const float* d_in, int B, int H, int W,
+                                float* d_out, int max_det, void* stream);
+
+/* The HBM input [B,3,H,W] and output [B,max_det,6] buffers of the plan for
+ * (B,H,W,max_det), creating the plan if needed.  Writing the input there and
+ * calling yb_cuda_forward_device with the same pointers runs the captured
+ * graph with no extra device copies. */
+status_t yb_cuda_plan_io(void* ctx, int B, int H, int W, int max_det, float** d_in, float** d_out);
+
+/* Copies the head tensors of the last forward, image-major:
+ * logits [B,N,nc] (pre-sigmoid class logits) and boxes [B,N,4] (xyxy pixels),
+ * N = anchors per image.  Either pointer may be NULL.  *n_anchors and *nc
+ * receive N and nc when non-NULL. */
+status_t yb_cuda_get_head(void* ctx, float* logits, float* boxes, int* n_anchors, int* nc);
+
+/* Image-sharded forward over G contexts (one per GPU): image range
+ * [g*B/G, (g+1)*B/G) runs on ctxs[g] from its own host thread; results land
+ * at the matching rows of out_dets.  Each shard is waited on with a host
+ * deadline of timeout_ms (<= 0: no deadline); an expired deadline returns
+ * ERROR_TIMEOUT after the other shards have finished or timed out. */
+status_t yb_cuda_forward_sharded(void* const* ctxs, int G, const float* in_nchw, int B, int H, int W,
+                                 float* out_dets, int max_det, int timeout_ms);
+
+/* One kernel launch of a plan, as measured by yb_cuda_profile_ops. */
+typedef struct {
+    int kind;     /* 0 tcgen05 conv, 1 stem conv, 2 depthwise, 3 max pool, 4 attention, 5 decode, 6 top-k */
+    int step;     /* model_forward_profile_t step index */
+    double ms;    /* mean device time of the launch */
+    double flops; /* algorithmic FLOPs (2 x MACs) */
+    double bytes; /* algorithmic HBM bytes: inputs and weights read once, outputs written once */
+} yb_op_stat;
+
+/* Runs the plan for (B,H,W,max_det) eagerly `reps` times with an event pair
+ * around every launch.  *n_ops receives the number of launches in one
+ * forward; stats (nullable, capacity cap) receives one record per launch. */
+status_t yb_cuda_profile_ops(void* ctx, int B, int H, int W, int max_det, int reps, yb_op_stat* stats, int cap,
+                             int* n_ops);
+
+/* Host-side fault injection for deadline tests: the context's next sharded
+ * calls sleep `ms` milliseconds on the host before enqueueing any GPU work
+ * (0 disables).  No GPU work is stalled or faulted. */
+status_t yb_cuda_debug_inject_stall(void* ctx, int ms);
+
+/* Releases the context's device memory, graphs and stream. */
+status_t yb_cuda_destroy(void* ctx);
+
+/* Last failure on the calling thread ("" when none). */
+const char* yb_cuda_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,183 @@
+"""ctypes access to the CPU oracle -- TEST INFRASTRUCTURE ONLY.
+
+`Oracle` wraps liboracle.so (our C restatement of the reference forward, see
+yolo_oracle.c) and `Reference` wraps _ref/libyolo_ref.so (the reference's own
+sources compiled by oracle/Makefile plus ref_harness.c).  Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline leg use this module; the
+product never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from collections import OrderedDict
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libyolo_ref.so")
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+STAGE_CB = C.CFUNCTYPE(None, C.c_void_p, C.c_char_p, C.POINTER(C.c_float), C.c_int, C.c_int, C.c_int, C.c_int)
+
+
+def build() -> None:
+    """Builds liboracle.so (and _ref when the reference sources are present)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _collector(store: "OrderedDict[str, np.ndarray]"):
+    def cb(_user, name, data, n, c, h, w):
+        cnt = n * c * h * w
+        arr = np.ctypeslib.as_array(data, shape=(cnt,)).copy().reshape(n, c, h, w)
+        store[name.decode()] = arr
+
+    return STAGE_CB(cb)
+
+
+class Oracle:
+    _lib = None
+
+    @classmethod
+    def lib(cls):
+        if cls._lib is None:
+            if not os.path.exists(ORACLE_SO):
+                build()
+            lib = C.CDLL(ORACLE_SO)
+            lib.orc_new.restype = C.c_void_p
+            lib.orc_new.argtypes = [C.c_int]
+            lib.orc_load.restype = C.c_void_p
+            lib.orc_load.argtypes = [C.c_char_p]
+            lib.orc_free.argtypes = [C.c_void_p]
+            lib.orc_add.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_int), _f32p]
+            lib.orc_fold.argtypes = [C.c_void_p]
+            lib.orc_get.restype = C.c_long
+            lib.orc_get.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_long]
+            lib.orc_forward.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_int, C.c_int, _f32p, C.c_void_p, C.c_void_p,
+                                        STAGE_CB, C.c_void_p]
+            lib.orc_anchors.argtypes = [C.c_int, C.c_int]
+            lib.orc_postprocess.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+            lib.orc_conv_block.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                           C.c_int, _f32p]
+            lib.orc_c3k2.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, _f32p,
+                                     C.c_int]
+            lib.orc_c3k2_c3k.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int]
+            lib.orc_sppf.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int, C.c_int,
+                                     C.c_int, _f32p, C.c_int]
+            lib.orc_c2psa.argtypes = [C.c_void_p, C.c_char_p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int]
+            lib.orc_dwconv.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+            cls._lib = lib
+        return cls._lib
+
+    def __init__(self, path: str | None = None, nc: int = 80):
+        lib = self.lib()
+        self.h = lib.orc_load(path.encode()) if path else lib.orc_new(nc)
+        if not self.h:
+            raise RuntimeError(f"oracle could not load {path}")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib().orc_free(self.h)
+            self.h = None
+
+    def add(self, name: str, arr: np.ndarray) -> None:
+        a = np.ascontiguousarray(arr, dtype=np.float32)
+        dims = list(a.shape) + [1] * (4 - a.ndim)
+        if a.ndim == 1:
+            dims = [a.shape[0], 1, 1, 1]
+        d = (C.c_int * 4)(*dims)
+        if self.lib().orc_add(self.h, name.encode(), d, a.reshape(-1)) != 0:
+            raise RuntimeError("orc_add failed")
+
+    def fold(self) -> None:
+        self.lib().orc_fold(self.h)
+
+    def get(self, name: str) -> np.ndarray | None:
+        n = self.lib().orc_get(self.h, name.encode(), None, 0)
+        if n < 0:
+            return None
+        out = np.empty(n, dtype=np.float32)
+        self.lib().orc_get(self.h, name.encode(), out.ctypes.data, n)
+        return out
+
+    def forward(self, img: np.ndarray, max_det: int = 300, stages: bool = False):
+        """img [1,3,H,W] -> dict(dets [max_det,6], logits [N,nc], boxes [N,4], stages)."""
+        x = np.ascontiguousarray(img, dtype=np.float32).reshape(-1)
+        H, W = img.shape[-2], img.shape[-1]
+        N = self.lib().orc_anchors(H, W)
+        dets = np.zeros(max_det * 6, dtype=np.float32)
+        logits = np.zeros(N * 80, dtype=np.float32)
+        boxes = np.zeros(N * 4, dtype=np.float32)
+        store: "OrderedDict[str, np.ndarray]" = OrderedDict()
+        cb = _collector(store) if stages else STAGE_CB()
+        st = self.lib().orc_forward(self.h, x, H, W, max_det, dets, logits.ctypes.data, boxes.ctypes.data, cb, None)
+        if st != 0:
+            raise RuntimeError(f"orc_forward status {st}")
+        return {"dets": dets.reshape(max_det, 6), "logits": logits.reshape(N, -1), "boxes": boxes.reshape(N, 4),
+                "stages": store}
+
+    @classmethod
+    def postprocess(cls, pred: np.ndarray, nc: int, max_det: int, cap: int) -> np.ndarray:
+        out = np.zeros(cap * 6, dtype=np.float32)
+        p = np.ascontiguousarray(pred, dtype=np.float32).reshape(-1)
+        n = p.size // (4 + nc)
+        cls.lib().orc_postprocess(p if p.size else np.zeros(1, np.float32), n, nc, max_det, cap, out)
+        return out.reshape(cap, 6)
+
+
+class Reference:
+    """The reference implementation compiled from its own sources."""
+
+    _lib = None
+
+    @classmethod
+    def available(cls) -> bool:
+        return os.path.exists(REF_SO)
+
+    @classmethod
+    def lib(cls):
+        if cls._lib is None:
+            lib = C.CDLL(REF_SO)
+            lib.ref_forward.argtypes = [C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, C.c_char_p,
+                                        C.c_void_p]
+            lib.ref_time_forwards.restype = C.c_double
+            lib.ref_time_forwards.argtypes = [C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int]
+            lib.ref_postprocess.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+            cls._lib = lib
+        return cls._lib
+
+    @classmethod
+    def forward(cls, weights: str, img: np.ndarray, width_mult: int = 1, max_det: int = 300,
+                stage_path: str | None = None, logits: bool = True, nc: int = 80):
+        H, W = img.shape[-2], img.shape[-1]
+        x = np.ascontiguousarray(img, dtype=np.float32).reshape(-1)
+        N = (H // 8) * (W // 8) + (H // 16) * (W // 16) + (H // 32) * (W // 32)
+        dets = np.zeros(max_det * 6, dtype=np.float32)
+        lg = np.zeros(N * nc, dtype=np.float32) if logits else None
+        st = cls.lib().ref_forward(weights.encode(), x, H, W, width_mult, max_det, dets,
+                                   stage_path.encode() if stage_path else None,
+                                   lg.ctypes.data if lg is not None else None)
+        if st != 0:
+            raise RuntimeError(f"reference forward status {st}")
+        return {"dets": dets.reshape(max_det, 6), "logits": lg.reshape(N, nc) if lg is not None else None}
+
+    @classmethod
+    def time_forwards(cls, weights: str, img: np.ndarray, reps: int, width_mult: int = 1) -> float:
+        H, W = img.shape[-2], img.shape[-1]
+        x = np.ascontiguousarray(img, dtype=np.float32).reshape(-1)
+        t = cls.lib().ref_time_forwards(weights.encode(), x, H, W, width_mult, reps)
+        if t < 0:
+            raise RuntimeError(f"reference timing failed ({t})")
+        return t
+
+    @classmethod
+    def postprocess(cls, pred: np.ndarray, nc: int, max_det: int, cap: int) -> np.ndarray:
+        out = np.zeros(cap * 6, dtype=np.float32)
+        p = np.ascontiguousarray(pred, dtype=np.float32).reshape(-1)
+        n = p.size // (4 + nc)
+        st = cls.lib().ref_postprocess(p if p.size else np.zeros(1, np.float32), n, nc, max_det, cap, out)
+        if st != 0:
+            raise RuntimeError(f"reference postprocess status {st}")
+        return out.reshape(cap, 6)

@@ -1,0 +1,114 @@
+"""Full-model parity: the CUDA forward (yb_cuda_forward / model_forward_ex)
+against the CPU oracle on seeded random-init YOLO26 weights and seeded U[0,1)
+inputs, stage by stage, on the pre-sigmoid class logits, and on the top-k
+detections."""
+import numpy as np
+import pytest
+
+from parity import LOGIT_ATOL, STAGE_RTOL, compare_dets, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def model_n0(weights_n0):
+    import yolo_b200 as yb
+
+    m = yb.Model(weights_n0)
+    yield m
+    m.close()
+
+
+def _oracle(path):
+    from oracle import Oracle
+
+    return Oracle(path)
+
+
+@pytest.mark.parametrize("hw", [640, 128])
+def test_stages_logits_dets(model_n0, weights_n0, hw):
+    import yb_weights as yw
+
+    img = yw.make_input(1, hw, hw)
+    got = model_n0.forward(img, stages=True)
+    logits, boxes = model_n0.head(1)
+    ref = _oracle(weights_n0).forward(img, stages=True)
+    worst = 0.0
+    for name, want in ref["stages"].items():
+        if name.startswith("stage_24") or name.startswith("stage_25"):
+            continue
+        have = got["stages"][name]
+        assert have.shape == want.shape, name
+        e = rel_err(have, want)
+        worst = max(worst, e)
+        print(f"{name}: rel err {e:.2e}")
+        assert e <= STAGE_RTOL, name
+    lerr = float(np.max(np.abs(logits[0] - ref["logits"])))
+    print(f"logits max abs err {lerr:.3e} (max |logit| {np.abs(ref['logits']).max():.1f}); worst stage {worst:.2e}")
+    assert lerr <= LOGIT_ATOL
+    n, mism, miou, sdiff = compare_dets(got["dets"][0], ref["dets"])
+    print(f"dets: {n} separated rows, {mism} class mismatches, min IoU {miou:.4f}, max score diff {sdiff:.2e}")
+    assert mism == 0 and miou >= 0.99
+
+
+def test_dets_non_saturating(weights_n0_soft):
+    """With scores below saturation the ranking is decided by scores: the
+    detections must match row for row."""
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    m = yb.Model(weights_n0_soft)
+    img = yw.make_input(7, 640, 640)
+    got = m.forward(img)["dets"][0]
+    ref = _oracle(weights_n0_soft).forward(img)["dets"]
+    n, mism, miou, sdiff = compare_dets(got, ref)
+    print(f"soft weights: {n} separated rows, {mism} mismatches, min IoU {miou:.5f}, max score diff {sdiff:.2e}")
+    assert n >= 250 and mism == 0 and miou >= 0.99 and sdiff <= 1e-4
+    m.close()
+
+
+def test_batch_equals_single(model_n0):
+    """Images are independent: a batch of 3 gives each image's B=1 result bit for bit."""
+    import yb_weights as yw
+
+    imgs = yw.make_batch([11, 12, 13], 256, 320)
+    batch = model_n0.forward(imgs)["dets"]
+    for i in range(3):
+        single = model_n0.forward(imgs[i : i + 1])["dets"][0]
+        assert np.array_equal(batch[i], single), i
+
+
+def test_repeatable(model_n0):
+    import yb_weights as yw
+
+    img = yw.make_input(3, 320, 320)
+    a = model_n0.forward(img)["dets"]
+    b = model_n0.forward(img)["dets"]
+    assert np.array_equal(a, b)
+
+
+def test_profile_steps(model_n0):
+    import yb_weights as yw
+
+    out = model_n0.forward(yw.make_input(1, 640, 640), profile=True)
+    ms = out["step_ms"]
+    assert len(ms) == 25 and all(v >= 0 for v in ms)
+    assert ms[0] > 0 and ms[23] > 0
+
+
+def test_s_width_model(weights_s0):
+    """The width-0.5 (s) model: widths come from the weights, same kernels."""
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    m = yb.Model(weights_s0)
+    img = yw.make_input(5, 256, 256)
+    got = m.forward(img, stages=True)
+    logits, _ = m.head(1)
+    ref = _oracle(weights_s0).forward(img, stages=True)
+    for name, want in ref["stages"].items():
+        if name.startswith("stage_2") and name >= "stage_24":
+            continue
+        assert rel_err(got["stages"][name], want) <= STAGE_RTOL, name
+    assert float(np.max(np.abs(logits[0] - ref["logits"]))) <= LOGIT_ATOL
+    m.close()

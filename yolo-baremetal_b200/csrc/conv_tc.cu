@@ -1,0 +1,424 @@
+// Implicit-GEMM convolution for sm_100a on the 5th-generation tensor cores.
+//
+// Replaces the reference's conv2d_forward (layers.c:41-81: a direct 7-deep
+// loop, or tensor_gemm for 1x1) together with the SiLU / residual / concat
+// work around it (layers.c:83-108, :145-153, :259-263).
+//
+// GEMM view: M = B*Ho*Wo output pixels (128 per tile), N = Co (one tile of up
+// to 256 channels, so the activation tile is read once), K = kh*kw*Ci ordered
+// (ky, kx, ci) and cut in 64-wide chunks.  FP32 semantics are kept by splitting
+// both operands into bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi),
+// 16 significant bits together) and accumulating hi*hi + hi*lo + lo*hi in fp32
+// in tensor memory: three kind::f16 UMMAs per 16-wide K step.
+//
+// Persistent, warp-specialised CTA (288 threads, one CTA per SM):
+//   warps 0-3  producers: gather the im2col rows of the activation tile
+//              straight from NHWC fp32 (zero padding, upsample and two-source
+//              concat handled in the address computation), split to hi/lo
+//              bf16 and store them in the 128B-swizzled K-major layout; thread
+//              0 also starts one bulk copy (TMA engine) of the pre-packed,
+//              pre-swizzled weight chunk.
+//   warp 8     allocates tensor memory (two accumulators) and, from one lane,
+//              issues the UMMAs; tcgen05.commit frees each smem stage and
+//              publishes each finished accumulator.
+//   warps 4-7  epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 output
+//              pixels), + bias, SiLU, + residual, fp32 NHWC store into the
+//              destination channel slice.  Runs while warp 8 accumulates the
+//              next tile into the other TMEM buffer.
+// All barrier waits are bounded (sm100.cuh); a timeout sets *a.err, aborts
+// the other roles, drains outstanding UMMAs and frees tensor memory.
+#include <cstdio>
+#include <cstring>
+#include <vector>
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace yb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kProducerWarps = 4;
+constexpr int kEpilogueWarps = 4;
+constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
+constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr uint32_t kAPlaneBytes = kBM * 128;  // one 128 x 64 bf16 plane
+constexpr int kSmemLimit = 232448;            // 227 KB opt-in per CTA
+constexpr int kSmemExtra = 1024 + 512 + kBM * 16;
+
+__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) {
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// x = hi + lo with hi = bf16_rn(x), lo = bf16_rn(x - hi); x - hi is exact.
+__device__ __forceinline__ void split4(const float4& v, uint2& hi, uint2& lo) {
+  const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y);
+  const __nv_bfloat162 h23 = __floats2bfloat162_rn(v.z, v.w);
+  const float2 f01 = __bfloat1622float2(h01);
+  const float2 f23 = __bfloat1622float2(h23);
+  const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
+  const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+  hi = make_uint2(bf16x2_bits(h01), bf16x2_bits(h23));
+  lo = make_uint2(bf16x2_bits(l01), bf16x2_bits(l23));
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ void raise_error(int* err, volatile int* abort_flag, int code) {
+  *abort_flag = 1;
+  if (err) atomicCAS(err, 0, code);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, const int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  // Swizzle atoms need 1024-byte alignment in the shared window.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t chunk_bytes = static_cast<uint32_t>(a.n_tile) * 256u;
+  const uint32_t stage_bytes = 2u * kAPlaneBytes + chunk_bytes;
+
+  uint8_t* tail = smem + stages * stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + stages;
+  uint64_t* acc_full = empty + stages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int4* row_info = reinterpret_cast<int4*>(tail + 512);
+
+  uint32_t ncols = 32;
+  while (ncols < 2u * static_cast<uint32_t>(a.n_tile)) ncols <<= 1;
+  const uint32_t acc_stride = ncols >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], kProducerWarps * 32);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpilogueWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = a.m_tiles * a.n_tiles;
+  const int HoWo = a.Ho * a.Wo;
+  const int M = a.B * HoWo;
+
+  if (warp < kProducerWarps) {
+    // ------------------------------------------------------------ producers
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const int mt = t / a.n_tiles;
+      const int nt = t - mt * a.n_tiles;
+      const int m0 = mt * kBM;
+      {
+        __syncwarp();  // the previous tile's reads of row_info are done
+        const int row = warp * 32 + lane;
+        const int m = m0 + row;
+        int4 ri = make_int4(0, 0, 0, 0);
+        if (m < M) {
+          const int b = m / HoWo;
+          const int r = m - b * HoWo;
+          const int oy = r / a.Wo;
+          const int ox = r - oy * a.Wo;
+          ri = make_int4(b, oy * a.stride - a.pad, ox * a.stride - a.pad, 1);
+        }
+        row_info[row] = ri;
+        __syncwarp();
+      }
+      const uint8_t* wsrc = a.wpack + static_cast<size_t>(nt) * a.num_kc * chunk_bytes;
+      for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
+        const uint32_t s = it % stages;
+        const uint32_t ph = (it / stages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+          raise_error(a.err, abort_flag, kErrWaitEmpty);
+          goto producer_done;
+        }
+        uint8_t* sa_hi = smem + s * stage_bytes;
+        uint8_t* sa_lo = sa_hi + kAPlaneBytes;
+        uint8_t* sb = sa_hi + 2 * kAPlaneBytes;
+        if (threadIdx.x == 0) {
+          mbar_expect_tx(&full[s], chunk_bytes);
+          bulk_g2s(sb, wsrc + static_cast<size_t>(kc) * chunk_bytes, chunk_bytes, &full[s]);
+        }
+        // This lane's 4 consecutive K indices (same tap, same source).
+        const int f4 = lane & 15;
+        const int k = kc * kBK + f4 * 4;
+        const bool kvalid = k < a.K;
+        int ky = 0, kx = 0, c = 0;
+        if (kvalid) {
+          const int tap = k / a.Ci;
+          c = k - tap * a.Ci;
+          ky = tap / a.kw;
+          kx = tap - ky * a.kw;
+        }
+        const bool first = c < a.c_split;
+        const float* sptr = first ? a.src0.ptr : a.src1.ptr;
+        const long long sb_stride = first ? a.src0.bstride : a.src1.bstride;
+        const int scs = first ? a.src0.cstride : a.src1.cstride;
+        const int sco = (first ? a.src0.coff + c : a.src1.coff + (c - a.c_split));
+        const int lg = first ? a.lg_up0 : a.lg_up1;
+        const int ws = a.W >> lg;
+
+        float4 v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int row = warp * 32 + 2 * i + (lane >> 4);
+          const int4 ri = row_info[row];
+          const int iy = ri.y + ky;
+          const int ix = ri.z + kx;
+          const bool ok = kvalid && ri.w && static_cast<unsigned>(iy) < static_cast<unsigned>(a.H) &&
+                          static_cast<unsigned>(ix) < static_cast<unsigned>(a.W);
+          if (ok) {
+            const float* p = sptr + static_cast<long long>(ri.x) * sb_stride +
+                             static_cast<long long>((iy >> lg) * ws + (ix >> lg)) * scs + sco;
+            v[i] = __ldg(reinterpret_cast<const float4*>(p));
+          } else {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t row = warp * 32 + 2 * i + (lane >> 4);
+          const uint32_t off = sw128_offset(row, static_cast<uint32_t>(f4 >> 1)) + (f4 & 1) * 8;
+          uint2 hi, lo;
+          split4(v[i], hi, lo);
+          *reinterpret_cast<uint2*>(sa_hi + off) = hi;
+          *reinterpret_cast<uint2*>(sa_lo + off) = lo;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full[s]);
+      }
+    }
+  producer_done:;
+  } else if (warp < kMmaWarp) {
+    // ------------------------------------------------------------- epilogue
+    const int q = warp - kProducerWarps;  // TMEM lane quarter (= warp % 4)
+    int lt = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
+      const int acc = lt & 1;
+      const uint32_t aph = (lt >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], aph, abort_flag)) {
+        raise_error(a.err, abort_flag, kErrWaitAccFull);
+        break;
+      }
+      tc_fence_after();
+      const int mt = t / a.n_tiles;
+      const int nt = t - mt * a.n_tiles;
+      const int n0 = nt * a.n_tile;
+      const int nvalid = min(a.n_tile, a.Co - n0);
+      const int m = mt * kBM + q * 32 + lane;
+      const bool valid = m < M;
+      int b = 0, p = 0;
+      if (valid) {
+        b = m / HoWo;
+        p = m - b * HoWo;
+      }
+      float* orow = a.out.ptr + static_cast<long long>(b) * a.out.bstride +
+                    static_cast<long long>(p) * a.out.cstride + a.out.coff + n0;
+      const float* rrow = a.res.ptr ? a.res.ptr + static_cast<long long>(b) * a.res.bstride +
+                                          static_cast<long long>(p) * a.res.cstride + a.res.coff + n0
+                                    : nullptr;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_stride;
+      for (int c0 = 0; c0 < nvalid; c0 += 16) {
+        uint32_t r[16];
+        tc_ld_32x32b_x16(tbase + c0, r);
+        tc_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4) {
+            const int n = c0 + j4 * 4;
+            if (n < nvalid) {
+              float4 x = make_float4(__uint_as_float(r[4 * j4 + 0]), __uint_as_float(r[4 * j4 + 1]),
+                                     __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3]));
+              if (a.bias) {
+                const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bias + n0 + n));
+                x.x += bb.x;
+                x.y += bb.y;
+                x.z += bb.z;
+                x.w += bb.w;
+              }
+              if (a.act == kActSiLU) {
+                x.x = silu(x.x);
+                x.y = silu(x.y);
+                x.z = silu(x.z);
+                x.w = silu(x.w);
+              }
+              if (rrow) {
+                const float4 rr = *reinterpret_cast<const float4*>(rrow + n);
+                x.x += rr.x;
+                x.y += rr.y;
+                x.z += rr.z;
+                x.w += rr.w;
+              }
+              *reinterpret_cast<float4*>(orow + n) = x;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  } else {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, a.n_tile);
+      uint32_t it = 0;
+      int lt = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
+        const int acc = lt & 1;
+        const uint32_t aph = (lt >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag)) {
+          raise_error(a.err, abort_flag, kErrWaitAccEmpty);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * acc_stride;
+        bool ok = true;
+        for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
+          const uint32_t s = it % stages;
+          const uint32_t ph = (it / stages) & 1u;
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            raise_error(a.err, abort_flag, kErrWaitFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(smem + s * stage_bytes);
+          const uint32_t a_lo = a_hi + kAPlaneBytes;
+          const uint32_t b_hi = a_hi + 2 * kAPlaneBytes;
+          const uint32_t b_lo = b_hi + static_cast<uint32_t>(a.n_tile) * 128u;
+#pragma unroll
+          for (int ks = 0; ks < kBK / 16; ++ks) {
+            const uint32_t koff = ks * 32;
+            const uint64_t dah = sw128_kmajor_desc(a_hi + koff);
+            const uint64_t dal = sw128_kmajor_desc(a_lo + koff);
+            const uint64_t dbh = sw128_kmajor_desc(b_hi + koff);
+            const uint64_t dbl = sw128_kmajor_desc(b_lo + koff);
+            tc_mma_bf16(d_tmem, dah, dbh, idesc, (kc | ks) != 0 ? 1u : 0u);
+            tc_mma_bf16(d_tmem, dah, dbl, idesc, 1u);
+            tc_mma_bf16(d_tmem, dal, dbh, idesc, 1u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);
+      }
+      // Drain: every UMMA issued above completes before tensor memory is freed.
+      tc_commit(drain);
+      bool drained = mbar_try_wait(drain, 0);
+      const uint64_t t0 = globaltimer_ns();
+      while (!drained && globaltimer_ns() - t0 < kWaitNs) drained = mbar_try_wait(drain, 0);
+      if (!drained) raise_error(a.err, abort_flag, kErrDrain);
+    }
+    __syncwarp();
+  }
+
+  // An aborted producer may have left a bulk copy in flight: give it time to land.
+  if (*abort_flag) __nanosleep(100000);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, ncols);
+  }
+}
+
+inline uint16_t host_bf16_rn(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  const uint32_t lsb = (u >> 16) & 1u;
+  u += 0x7FFFu + lsb;
+  return static_cast<uint16_t>(u >> 16);
+}
+inline float host_bf16_to_float(uint16_t h) {
+  const uint32_t u = static_cast<uint32_t>(h) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+}  // namespace
+
+void choose_n_tiling(int co, int* n_tile, int* n_tiles) {
+  const int tiles = (co + 255) / 256;
+  const int per = (co + tiles - 1) / tiles;
+  *n_tile = ((per + 15) / 16) * 16;
+  *n_tiles = tiles;
+}
+
+size_t pack_conv_weights(const float* w, int co, int ci, int kh, int kw, int n_tile, uint8_t* dst) {
+  const int K = kh * kw * ci;
+  const int num_kc = (K + kBK - 1) / kBK;
+  const int n_tiles = (co + n_tile - 1) / n_tile;
+  const size_t chunk = conv_chunk_bytes(n_tile);
+  const size_t total = static_cast<size_t>(n_tiles) * num_kc * chunk;
+  if (!dst) return total;
+  std::memset(dst, 0, total);
+  for (int nt = 0; nt < n_tiles; ++nt) {
+    for (int kc = 0; kc < num_kc; ++kc) {
+      uint8_t* hi_plane = dst + (static_cast<size_t>(nt) * num_kc + kc) * chunk;
+      uint8_t* lo_plane = hi_plane + static_cast<size_t>(n_tile) * 128;
+      for (int r = 0; r < n_tile; ++r) {
+        const int n = nt * n_tile + r;
+        if (n >= co) continue;
+        for (int kk = 0; kk < kBK; ++kk) {
+          const int k = kc * kBK + kk;
+          if (k >= K) break;
+          const int tap = k / ci;
+          const int c = k - tap * ci;
+          const int ky = tap / kw;
+          const int kx = tap - ky * kw;
+          const float v = w[((static_cast<size_t>(n) * ci + c) * kh + ky) * kw + kx];
+          const uint16_t h = host_bf16_rn(v);
+          const uint16_t l = host_bf16_rn(v - host_bf16_to_float(h));
+          const uint32_t off = sw128_offset(r, kk >> 3) + (kk & 7) * 2;
+          std::memcpy(hi_plane + off, &h, 2);
+          std::memcpy(lo_plane + off, &l, 2);
+        }
+      }
+    }
+  }
+  return total;
+}
+
+// Opts the kernel into the full 227 KB of shared memory on the current device.
+// Called once per device before any launch (and outside stream capture).
+cudaError_t init_conv_kernel_attributes() {
+  return cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+}
+
+cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
+  if (a.n_tile < 16 || a.n_tile > 256 || (a.n_tile % 16) != 0 || a.Ci % 4 != 0 || a.c_split % 4 != 0 ||
+      a.Co % 4 != 0)
+    return cudaErrorInvalidValue;
+  const int stage_bytes = 2 * kAPlaneBytes + static_cast<int>(conv_chunk_bytes(a.n_tile));
+  int stages = (kSmemLimit - kSmemExtra) / stage_bytes;
+  if (stages > 8) stages = 8;
+  if (stages < 2) return cudaErrorInvalidValue;
+  const int smem = kSmemExtra + stages * stage_bytes;
+  const int total = a.m_tiles * a.n_tiles;
+  if (total <= 0) return cudaSuccess;
+  const int grid = total < num_sms ? total : num_sms;
+  conv_tc_kernel<<<grid, kThreads, smem, s>>>(a, stages);
+  return cudaGetLastError();
+}
+
+}  // namespace yb

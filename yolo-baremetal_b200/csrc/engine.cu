@@ -1,0 +1,896 @@
+// Lowering of the YOLO26 graph to sm_100a kernel launches (see engine.h).
+#include "engine.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+
+namespace yb {
+
+namespace {
+
+TView tv(const Buf& b, int coff = 0) {
+  TView v;
+  v.ptr = b.ptr;
+  v.bstride = b.bstride;
+  v.cstride = b.C;
+  v.coff = coff;
+  return v;
+}
+OView ov(const Buf& b, int coff = 0) {
+  OView v;
+  v.ptr = b.ptr;
+  v.bstride = b.bstride;
+  v.cstride = b.C;
+  v.coff = coff;
+  return v;
+}
+Src src_of(const Buf& b, int coff, int c) {
+  Src s;
+  s.v0 = tv(b, coff);
+  s.c0 = c;
+  s.H = b.H;
+  s.W = b.W;
+  return s;
+}
+Src src_cat(const Buf& a, int lg_a, const Buf& b, int H, int W) {
+  Src s;
+  s.v0 = tv(a);
+  s.c0 = a.C;
+  s.lg0 = lg_a;
+  s.v1 = tv(b);
+  s.c1 = b.C;
+  s.H = H;
+  s.W = W;
+  return s;
+}
+
+bool ends_with(const std::string& s, const std::string& suf) {
+  return s.size() >= suf.size() && s.compare(s.size() - suf.size(), suf.size(), suf) == 0;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- weight files
+bool read_weight_bin(const char* path, WeightMap* out, int* num_classes, std::string* why) {
+  FILE* f = std::fopen(path, "rb");
+  if (!f) {
+    *why = std::string("cannot open ") + path;
+    return false;
+  }
+  int32_t nc = 0, count = 0;
+  if (std::fread(&nc, 4, 1, f) != 1 || std::fread(&count, 4, 1, f) != 1 || count < 0) {
+    std::fclose(f);
+    *why = "truncated header";
+    return false;
+  }
+  for (int i = 0; i < count; ++i) {
+    int32_t nl = 0;
+    if (std::fread(&nl, 4, 1, f) != 1 || nl <= 0 || nl >= 128) {
+      std::fclose(f);
+      *why = "bad record name length";
+      return false;
+    }
+    std::string name(static_cast<size_t>(nl), '\0');
+    int32_t nd = 0;
+    if (std::fread(&name[0], 1, nl, f) != static_cast<size_t>(nl) || std::fread(&nd, 4, 1, f) != 1 || nd < 0 ||
+        nd > 4) {
+      std::fclose(f);
+      *why = "bad record header for " + name;
+      return false;
+    }
+    HostTensor t;
+    t.ndim = nd;
+    size_t n = 1;
+    for (int d = 0; d < nd; ++d) {
+      int32_t v = 0;
+      if (std::fread(&v, 4, 1, f) != 1 || v < 0) {
+        std::fclose(f);
+        *why = "bad dims for " + name;
+        return false;
+      }
+      t.dims[d] = v;
+      n *= static_cast<size_t>(v);
+    }
+    t.data.resize(n);
+    if (n && std::fread(t.data.data(), 4, n, f) != n) {
+      std::fclose(f);
+      *why = "truncated data for " + name;
+      return false;
+    }
+    (*out)[name] = std::move(t);
+  }
+  std::fclose(f);
+  *num_classes = nc;
+  return true;
+}
+
+// Folds every <p>.bn.{weight,bias,running_mean,running_var} into
+// <p>.conv.weight / <p>.conv.bias (created as zeros when absent) and drops the
+// BN records, with the reference's fp32 arithmetic (utils.c:81-106).
+void fold_all_bn_map(WeightMap* w) {
+  std::vector<std::string> convs;
+  for (const auto& kv : *w)
+    if (ends_with(kv.first, ".conv.weight")) convs.push_back(kv.first);
+  for (const std::string& cname : convs) {
+    const std::string p = cname.substr(0, cname.size() - std::strlen(".conv.weight"));
+    auto g = w->find(p + ".bn.weight");
+    auto be = w->find(p + ".bn.bias");
+    auto mu = w->find(p + ".bn.running_mean");
+    auto var = w->find(p + ".bn.running_var");
+    if (g == w->end() || be == w->end() || mu == w->end() || var == w->end()) continue;
+    HostTensor& cw = (*w)[cname];
+    const int out_c = cw.dims[0];
+    const size_t per = cw.data.size() / static_cast<size_t>(out_c);
+    const std::string bname = p + ".conv.bias";
+    if (w->find(bname) == w->end()) {
+      HostTensor b;
+      b.ndim = 4;
+      b.dims[0] = 1;
+      b.dims[1] = out_c;
+      b.data.assign(static_cast<size_t>(out_c), 0.0f);
+      (*w)[bname] = std::move(b);
+    }
+    HostTensor& cb = (*w)[bname];
+    const float eps = 1e-5f;
+    for (int i = 0; i < out_c; ++i) {
+      const float gamma = g->second.data[i];
+      const float beta = be->second.data[i];
+      const float mean = mu->second.data[i];
+      const float v = var->second.data[i];
+      const float scale = gamma / std::sqrt(v + eps);
+      for (size_t j = 0; j < per; ++j) cw.data[i * per + j] *= scale;
+      const float b0 = cb.data[i];
+      const float t = b0 - mean;
+      const float t2 = t * scale;
+      cb.data[i] = t2 + beta;
+    }
+    w->erase(p + ".bn.weight");
+    w->erase(p + ".bn.bias");
+    w->erase(p + ".bn.running_mean");
+    w->erase(p + ".bn.running_var");
+    w->erase(p + ".bn.num_batches_tracked");
+  }
+}
+
+// ------------------------------------------------------------------- engine
+Engine::Engine(int device) : device_(device) {
+  cudaSetDevice(device);
+  cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device);
+  cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking);
+  cudaMalloc(&d_err_, sizeof(int));
+  cudaMemset(d_err_, 0, sizeof(int));
+  init_conv_kernel_attributes();
+}
+
+Engine::~Engine() {
+  cudaSetDevice(device_);
+  for (auto& p : plans_) release_plan(p.get());
+  for (void* q : weight_allocs_) cudaFree(q);
+  if (d_err_) cudaFree(d_err_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Engine::release_plan(Plan* p) {
+  if (p->graph) cudaGraphExecDestroy(p->graph);
+  p->graph = nullptr;
+  for (void* q : p->allocs) cudaFree(q);
+  p->allocs.clear();
+}
+
+cudaError_t Engine::dev_alloc(size_t bytes, void** p) {
+  cudaError_t e = cudaMalloc(p, bytes < 256 ? 256 : bytes);
+  if (e == cudaSuccess) weight_allocs_.push_back(*p);
+  return e;
+}
+
+int Engine::take_kernel_error() {
+  int v = 0;
+  cudaSetDevice(device_);
+  if (cudaMemcpy(&v, d_err_, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (v) cudaMemset(d_err_, 0, sizeof(int));
+  return v;
+}
+
+const HostTensor* Engine::find(const std::string& name) const {
+  auto it = hw_.find(name);
+  return it == hw_.end() ? nullptr : &it->second;
+}
+
+cudaError_t Engine::set_weights(WeightMap&& w, int num_classes, std::string* why) {
+  cudaSetDevice(device_);
+  for (auto& p : plans_) release_plan(p.get());
+  plans_.clear();
+  for (void* q : weight_allocs_) cudaFree(q);
+  weight_allocs_.clear();
+  convs_.clear();
+  dws_.clear();
+  stem_ = DevStem();
+  hw_ = std::move(w);
+  nc_ = num_classes;
+  const HostTensor* sw = find("model.0.conv.weight");
+  const HostTensor* sb = find("model.0.conv.bias");
+  if (!sw || !sb) {
+    *why = "missing model.0.conv.weight/bias";
+    return cudaErrorInvalidValue;
+  }
+  stem_.co = sw->dims[0];
+  stem_.ci = sw->dims[1];
+  stem_.k = sw->dims[2];
+  cudaError_t e = dev_alloc(sw->data.size() * 4, reinterpret_cast<void**>(&stem_.w));
+  if (e != cudaSuccess) return e;
+  e = dev_alloc(sb->data.size() * 4, reinterpret_cast<void**>(&stem_.bias));
+  if (e != cudaSuccess) return e;
+  cudaMemcpy(stem_.w, sw->data.data(), sw->data.size() * 4, cudaMemcpyHostToDevice);
+  return cudaMemcpy(stem_.bias, sb->data.data(), sb->data.size() * 4, cudaMemcpyHostToDevice);
+}
+
+cudaError_t Engine::conv_w(const std::string& prefix, bool plain, DevConv** out, std::string* why) {
+  auto it = convs_.find(prefix);
+  if (it != convs_.end()) {
+    *out = &it->second;
+    return cudaSuccess;
+  }
+  const std::string wn = prefix + (plain ? ".weight" : ".conv.weight");
+  const std::string bn = prefix + (plain ? ".bias" : ".conv.bias");
+  const HostTensor* w = find(wn);
+  const HostTensor* b = find(bn);
+  if (!w || !b) {
+    *why = "missing weight " + (w ? bn : wn);
+    return cudaErrorInvalidValue;
+  }
+  DevConv d;
+  d.co = w->dims[0];
+  d.ci = w->dims[1];
+  d.kh = w->dims[2];
+  d.kw = w->dims[3];
+  if (d.ci % 4 || d.co % 4 || static_cast<int>(b->data.size()) != d.co) {
+    *why = "unsupported conv shape at " + prefix;
+    return cudaErrorInvalidValue;
+  }
+  d.K = d.kh * d.kw * d.ci;
+  d.num_kc = (d.K + 63) / 64;
+  choose_n_tiling(d.co, &d.n_tile, &d.n_tiles);
+  const size_t bytes = pack_conv_weights(w->data.data(), d.co, d.ci, d.kh, d.kw, d.n_tile, nullptr);
+  std::vector<uint8_t> pack(bytes);
+  pack_conv_weights(w->data.data(), d.co, d.ci, d.kh, d.kw, d.n_tile, pack.data());
+  cudaError_t e = dev_alloc(bytes, reinterpret_cast<void**>(&d.wpack));
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpy(d.wpack, pack.data(), bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return e;
+  e = dev_alloc(static_cast<size_t>(d.n_tile) * d.n_tiles * 4, reinterpret_cast<void**>(&d.bias));
+  if (e != cudaSuccess) return e;
+  cudaMemset(d.bias, 0, static_cast<size_t>(d.n_tile) * d.n_tiles * 4);
+  e = cudaMemcpy(d.bias, b->data.data(), b->data.size() * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return e;
+  auto ins = convs_.emplace(prefix, d);
+  *out = &ins.first->second;
+  return cudaSuccess;
+}
+
+cudaError_t Engine::dw_w(const std::string& prefix, DevDw** out, std::string* why) {
+  auto it = dws_.find(prefix);
+  if (it != dws_.end()) {
+    *out = &it->second;
+    return cudaSuccess;
+  }
+  const HostTensor* w = find(prefix + ".conv.weight");
+  const HostTensor* b = find(prefix + ".conv.bias");
+  if (!w || !b || w->dims[1] != 1 || w->dims[2] != 3 || w->dims[3] != 3 || w->dims[0] % 4) {
+    *why = "missing or unsupported depthwise weight " + prefix;
+    return cudaErrorInvalidValue;
+  }
+  DevDw d;
+  d.c = w->dims[0];
+  std::vector<float> t(static_cast<size_t>(9) * d.c);
+  for (int c = 0; c < d.c; ++c)
+    for (int k = 0; k < 9; ++k) t[static_cast<size_t>(k) * d.c + c] = w->data[static_cast<size_t>(c) * 9 + k];
+  cudaError_t e = dev_alloc(t.size() * 4, reinterpret_cast<void**>(&d.w));
+  if (e != cudaSuccess) return e;
+  cudaMemcpy(d.w, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+  e = dev_alloc(static_cast<size_t>(d.c) * 4, reinterpret_cast<void**>(&d.bias));
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpy(d.bias, b->data.data(), static_cast<size_t>(d.c) * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return e;
+  auto ins = dws_.emplace(prefix, d);
+  *out = &ins.first->second;
+  return cudaSuccess;
+}
+
+#define YB_TRY(x)                          \
+  do {                                     \
+    cudaError_t e_ = (x);                  \
+    if (e_ != cudaSuccess) return e_;      \
+  } while (0)
+
+cudaError_t Engine::build(Plan* p, std::string* why) {
+  const int B = p->B;
+  int step = 0;
+  std::vector<Op>& ops = p->ops;
+
+  auto alloc_buf = [&](int H, int W, int C, Buf* b) -> cudaError_t {
+    b->H = H;
+    b->W = W;
+    b->C = C;
+    b->bstride = static_cast<long long>(H) * W * C;
+    const size_t bytes = static_cast<size_t>(B) * b->bstride * 4;
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, bytes);
+    if (e != cudaSuccess) return e;
+    p->allocs.push_back(q);
+    p->arena_bytes += bytes;
+    b->ptr = static_cast<float*>(q);
+    return cudaSuccess;
+  };
+  auto alloc_raw = [&](size_t bytes, float** q) -> cudaError_t {
+    void* r = nullptr;
+    cudaError_t e = cudaMalloc(&r, bytes);
+    if (e != cudaSuccess) return e;
+    p->allocs.push_back(r);
+    p->arena_bytes += bytes;
+    *q = static_cast<float*>(r);
+    return cudaSuccess;
+  };
+  auto add_conv = [&](const DevConv* w, const Src& in, int stride, int pad, int act, OView out,
+                      TView res) -> cudaError_t {
+    if (in.c0 + in.c1 != w->ci || in.c0 % 4) {
+      *why = "conv input channel mismatch";
+      return cudaErrorInvalidValue;
+    }
+    ConvArgs a;
+    a.B = B;
+    a.H = in.H;
+    a.W = in.W;
+    a.Ci = w->ci;
+    a.Co = w->co;
+    a.kh = w->kh;
+    a.kw = w->kw;
+    a.stride = stride;
+    a.pad = pad;
+    a.Ho = (in.H + 2 * pad - w->kh) / stride + 1;
+    a.Wo = (in.W + 2 * pad - w->kw) / stride + 1;
+    a.K = w->K;
+    a.num_kc = w->num_kc;
+    a.n_tile = w->n_tile;
+    a.n_tiles = w->n_tiles;
+    a.m_tiles = static_cast<int>((static_cast<long long>(B) * a.Ho * a.Wo + 127) / 128);
+    a.src0 = in.v0;
+    a.lg_up0 = in.lg0;
+    if (in.c1) {
+      a.c_split = in.c0;
+      a.src1 = in.v1;
+      a.lg_up1 = 0;
+    } else {
+      a.c_split = w->ci;
+      a.src1 = in.v0;
+      a.lg_up1 = in.lg0;
+    }
+    a.wpack = w->wpack;
+    a.bias = w->bias;
+    a.act = act;
+    a.out = out;
+    a.res = res;
+    a.err = d_err_;
+    const int sms = num_sms_;
+    Op op{step, [a, sms](cudaStream_t s) { return launch_conv_tc(a, s, sms); }};
+    op.kind = kOpConv;
+    const double pix_out = static_cast<double>(B) * a.Ho * a.Wo;
+    op.flops = 2.0 * pix_out * a.Co * a.K;
+    const double in0 = static_cast<double>(B) * (in.H >> in.lg0) * (in.W >> in.lg0) * in.c0;
+    const double in1 = static_cast<double>(B) * in.H * in.W * in.c1;
+    op.bytes = 4.0 * (in0 + in1 + static_cast<double>(a.Co) * (a.K + 1) + pix_out * a.Co * (res.ptr ? 2 : 1));
+    ops.push_back(op);
+    return cudaSuccess;
+  };
+  auto add_op = [&](int kind, double flops, double bytes, std::function<cudaError_t(cudaStream_t)> fn) {
+    Op op{step, std::move(fn)};
+    op.kind = kind;
+    op.flops = flops;
+    op.bytes = bytes;
+    ops.push_back(op);
+  };
+  auto conv = [&](const std::string& prefix, DevConv** w) { return conv_w(prefix, false, w, why); };
+  auto exists = [&](const std::string& n) { return find(n) != nullptr; };
+
+  auto downconv = [&](int li, const Buf& in, Buf* out) -> cudaError_t {
+    DevConv* w;
+    YB_TRY(conv("model." + std::to_string(li), &w));
+    YB_TRY(alloc_buf((in.H + 2 - w->kh) / 2 + 1, (in.W + 2 - w->kw) / 2 + 1, w->co, out));
+    return add_conv(w, src_of(in, 0, in.C), 2, (w->kh - 1) / 2, kActSiLU, ov(*out), TView());
+  };
+  // Bottleneck (layers.c:92-108): cv1+SiLU -> cv2+SiLU (+ input).
+  auto bottleneck = [&](const std::string& pre, const Src& in, OView out, bool shortcut) -> cudaError_t {
+    DevConv *w1, *w2;
+    YB_TRY(conv(pre + ".cv1", &w1));
+    YB_TRY(conv(pre + ".cv2", &w2));
+    Buf t;
+    YB_TRY(alloc_buf(in.H, in.W, w1->co, &t));
+    YB_TRY(add_conv(w1, in, 1, (w1->kh - 1) / 2, kActSiLU, ov(t), TView()));
+    return add_conv(w2, src_of(t, 0, t.C), 1, (w2->kh - 1) / 2, kActSiLU, out, shortcut ? in.v0 : TView());
+  };
+  // C3k2 without C3k (layers.c:110-154, model.c:208-283), shortcut bottlenecks.
+  auto c3k2_plain = [&](int li, const Src& in, Buf* out) -> cudaError_t {
+    const std::string L = "model." + std::to_string(li);
+    DevConv *cv1, *cv2;
+    YB_TRY(conv(L + ".cv1", &cv1));
+    YB_TRY(conv(L + ".cv2", &cv2));
+    const int c = cv1->co / 2;
+    int n = 0;
+    while (exists(L + ".m." + std::to_string(n) + ".cv1.conv.weight")) ++n;
+    if (n < 1) {
+      *why = L + ": no bottlenecks";
+      return cudaErrorInvalidValue;
+    }
+    Buf cat;
+    YB_TRY(alloc_buf(in.H, in.W, (2 + n) * c, &cat));
+    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(cat, 0), TView()));
+    int prev = c;
+    for (int i = 0; i < n; ++i) {
+      YB_TRY(bottleneck(L + ".m." + std::to_string(i), src_of(cat, prev, c), ov(cat, (2 + i) * c), true));
+      prev = (2 + i) * c;
+    }
+    YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
+    return add_conv(cv2, src_of(cat, 0, (2 + n) * c), 1, 0, kActSiLU, ov(*out), TView());
+  };
+  // C3k2 with an inner C3k (layers.c:156-189, model.c:415-557).
+  auto c3k2_c3k = [&](int li, const Src& in, Buf* out) -> cudaError_t {
+    const std::string L = "model." + std::to_string(li);
+    DevConv *cv1, *cv2, *k1, *k2, *k3;
+    YB_TRY(conv(L + ".cv1", &cv1));
+    YB_TRY(conv(L + ".cv2", &cv2));
+    YB_TRY(conv(L + ".m.0.cv1", &k1));
+    YB_TRY(conv(L + ".m.0.cv2", &k2));
+    YB_TRY(conv(L + ".m.0.cv3", &k3));
+    const int c = cv1->co / 2;
+    int nb = 0;
+    while (exists(L + ".m.0.m." + std::to_string(nb) + ".cv1.conv.weight")) ++nb;
+    if (nb < 1) {
+      *why = L + ": no C3k bottlenecks";
+      return cudaErrorInvalidValue;
+    }
+    Buf catO, y, catC;
+    YB_TRY(alloc_buf(in.H, in.W, 2 * c + k3->co, &catO));
+    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(catO, 0), TView()));
+    const Src b = src_of(catO, c, c);
+    const int cm = k1->co;
+    YB_TRY(alloc_buf(in.H, in.W, cm, &y));
+    YB_TRY(alloc_buf(in.H, in.W, cm + k2->co, &catC));
+    YB_TRY(add_conv(k1, b, 1, 0, kActSiLU, ov(y), TView()));
+    YB_TRY(add_conv(k2, b, 1, 0, kActSiLU, ov(catC, cm), TView()));
+    Src cur = src_of(y, 0, cm);
+    for (int i = 0; i < nb; ++i) {
+      const std::string pre = L + ".m.0.m." + std::to_string(i);
+      if (i == nb - 1) {
+        YB_TRY(bottleneck(pre, cur, ov(catC, 0), true));
+      } else {
+        Buf nxt;
+        YB_TRY(alloc_buf(in.H, in.W, cm, &nxt));
+        YB_TRY(bottleneck(pre, cur, ov(nxt), true));
+        cur = src_of(nxt, 0, cm);
+      }
+    }
+    YB_TRY(add_conv(k3, src_of(catC, 0, catC.C), 1, 0, kActSiLU, ov(catO, 2 * c), TView()));
+    YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
+    return add_conv(cv2, src_of(catO, 0, catO.C), 1, 0, kActSiLU, ov(*out), TView());
+  };
+  // SPPF k=5, 3 pools, shortcut (layers.c:230-265, model.c:285-320, :825).
+  auto sppf = [&](int li, const Buf& in, Buf* out) -> cudaError_t {
+    const std::string L = "model." + std::to_string(li);
+    DevConv *cv1, *cv2;
+    YB_TRY(conv(L + ".cv1", &cv1));
+    YB_TRY(conv(L + ".cv2", &cv2));
+    const int c = cv1->co;
+    Buf cat;
+    YB_TRY(alloc_buf(in.H, in.W, 4 * c, &cat));
+    YB_TRY(add_conv(cv1, src_of(in, 0, in.C), 1, 0, kActNone, ov(cat, 0), TView()));
+    for (int j = 0; j < 3; ++j) {
+      PoolArgs pa;
+      pa.in = tv(cat, j * c);
+      pa.B = B;
+      pa.H = in.H;
+      pa.W = in.W;
+      pa.C = c;
+      pa.k = 5;
+      pa.out = ov(cat, (j + 1) * c);
+      const double n = static_cast<double>(B) * in.H * in.W * c;
+      add_op(kOpPool, 0.0, 8.0 * n, [pa](cudaStream_t s) { return launch_maxpool(pa, s); });
+    }
+    YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
+    const bool res = in.C == cv2->co;
+    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), res ? tv(in) : TView());
+  };
+  // PSABlock (layers.c:407-453) with attention (layers.c:310-405).
+  auto psablock = [&](const std::string& pre, const Src& x, int c, OView y, int heads) -> cudaError_t {
+    DevConv *qkv, *proj, *f0, *f1;
+    DevDw* pe;
+    YB_TRY(conv(pre + ".attn.qkv", &qkv));
+    YB_TRY(conv(pre + ".attn.proj", &proj));
+    YB_TRY(conv(pre + ".ffn.0", &f0));
+    YB_TRY(conv(pre + ".ffn.1", &f1));
+    YB_TRY(dw_w(pre + ".attn.pe", &pe, why));
+    if (c % heads) {
+      *why = pre + ": channels not divisible by heads";
+      return cudaErrorInvalidValue;
+    }
+    const int hd = c / heads;
+    const int kd = static_cast<int>(static_cast<float>(hd) * 0.5f);
+    if (qkv->co != c + 2 * kd * heads || pe->c != c) {
+      *why = pre + ": qkv/pe width mismatch";
+      return cudaErrorInvalidValue;
+    }
+    Buf q, ao, x1, f;
+    YB_TRY(alloc_buf(x.H, x.W, qkv->co, &q));
+    YB_TRY(add_conv(qkv, x, 1, 0, kActNone, ov(q), TView()));
+    YB_TRY(alloc_buf(x.H, x.W, c, &ao));
+    AttnArgs aa;
+    aa.qkv = tv(q);
+    aa.B = B;
+    aa.H = x.H;
+    aa.W = x.W;
+    aa.heads = heads;
+    aa.kd = kd;
+    aa.hd = hd;
+    aa.scale = std::pow(static_cast<float>(kd), -0.5f);
+    aa.pe_w = pe->w;
+    aa.pe_b = pe->bias;
+    aa.out = ov(ao);
+    {
+      const double ntok = static_cast<double>(x.H) * x.W;
+      const double fl = static_cast<double>(B) * heads * (2.0 * ntok * ntok * (kd + hd) + 18.0 * ntok * hd);
+      const double by = 4.0 * B * ntok * (qkv->co + c) + 4.0 * 10.0 * c;
+      add_op(kOpAttn, fl, by, [aa](cudaStream_t s) { return launch_attention(aa, s); });
+    }
+    YB_TRY(alloc_buf(x.H, x.W, c, &x1));
+    YB_TRY(add_conv(proj, src_of(ao, 0, c), 1, 0, kActNone, ov(x1), x.v0));
+    YB_TRY(alloc_buf(x.H, x.W, f0->co, &f));
+    YB_TRY(add_conv(f0, src_of(x1, 0, c), 1, 0, kActSiLU, ov(f), TView()));
+    return add_conv(f1, src_of(f, 0, f.C), 1, 0, kActNone, y, tv(x1));
+  };
+  // C2PSA (layers.c:455-496, model.c:322-412); blocks update the b half in place.
+  auto c2psa = [&](int li, const Buf& in, Buf* out) -> cudaError_t {
+    const std::string L = "model." + std::to_string(li);
+    DevConv *cv1, *cv2;
+    YB_TRY(conv(L + ".cv1", &cv1));
+    YB_TRY(conv(L + ".cv2", &cv2));
+    const int ch = static_cast<int>(static_cast<float>(in.C) * 0.5f);
+    if (cv1->co != 2 * ch) {
+      *why = L + ": cv1 width mismatch";
+      return cudaErrorInvalidValue;
+    }
+    int heads = ch / 64;
+    if (heads < 1) heads = 1;
+    Buf cat;
+    YB_TRY(alloc_buf(in.H, in.W, 2 * ch, &cat));
+    YB_TRY(add_conv(cv1, src_of(in, 0, in.C), 1, 0, kActSiLU, ov(cat), TView()));
+    int nb = 0;
+    while (exists(L + ".m." + std::to_string(nb) + ".attn.qkv.conv.weight")) {
+      YB_TRY(psablock(L + ".m." + std::to_string(nb), src_of(cat, ch, ch), ch, ov(cat, ch), heads));
+      ++nb;
+    }
+    if (nb < 1) {
+      *why = L + ": no PSA blocks";
+      return cudaErrorInvalidValue;
+    }
+    YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
+    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), TView());
+  };
+  // Head C3k2 with Bottleneck + PSABlock (model.c:560-665).
+  auto c3k2_attn = [&](int li, const Src& in, Buf* out) -> cudaError_t {
+    const std::string L = "model." + std::to_string(li);
+    DevConv *cv1, *cv2;
+    YB_TRY(conv(L + ".cv1", &cv1));
+    YB_TRY(conv(L + ".cv2", &cv2));
+    const int c = cv1->co / 2;
+    Buf cat, bo;
+    YB_TRY(alloc_buf(in.H, in.W, 3 * c, &cat));
+    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(cat, 0), TView()));
+    YB_TRY(alloc_buf(in.H, in.W, c, &bo));
+    YB_TRY(bottleneck(L + ".m.0.0", src_of(cat, c, c), ov(bo), true));
+    int heads = c / 64;
+    if (heads < 1) heads = 1;
+    YB_TRY(psablock(L + ".m.0.1", src_of(bo, 0, c), c, ov(cat, 2 * c), heads));
+    YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
+    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), TView());
+  };
+
+  Buf* S = p->stage;
+  const int H = p->H, W = p->W;
+  // step 0: stem (model.0), NCHW input read directly.
+  step = 0;
+  YB_TRY(alloc_raw(static_cast<size_t>(B) * 3 * H * W * 4, &p->d_in));
+  {
+    YB_TRY(alloc_buf((H + 2 - stem_.k) / 2 + 1, (W + 2 - stem_.k) / 2 + 1, stem_.co, &S[0]));
+    StemArgs sa;
+    sa.in = p->d_in;
+    sa.B = B;
+    sa.Ci = stem_.ci;
+    sa.H = H;
+    sa.W = W;
+    sa.Co = stem_.co;
+    sa.Ho = S[0].H;
+    sa.Wo = S[0].W;
+    sa.k = stem_.k;
+    sa.w = stem_.w;
+    sa.bias = stem_.bias;
+    sa.act = kActSiLU;
+    sa.out = ov(S[0]);
+    if (stem_.ci != 3 || stem_.k != 3) {
+      *why = "unsupported stem";
+      return cudaErrorInvalidValue;
+    }
+    const double po = static_cast<double>(B) * sa.Ho * sa.Wo;
+    add_op(kOpStem, 2.0 * po * sa.Co * sa.Ci * 9, 4.0 * (static_cast<double>(B) * 3 * H * W + po * sa.Co),
+           [sa](cudaStream_t s) { return launch_stem(sa, s); });
+  }
+  step = 1;
+  YB_TRY(downconv(1, S[0], &S[1]));
+  step = 2;
+  YB_TRY(c3k2_plain(2, src_of(S[1], 0, S[1].C), &S[2]));
+  step = 3;
+  YB_TRY(downconv(3, S[2], &S[3]));
+  step = 4;
+  YB_TRY(c3k2_plain(4, src_of(S[3], 0, S[3].C), &S[4]));
+  step = 5;
+  YB_TRY(downconv(5, S[4], &S[5]));
+  step = 6;
+  YB_TRY(c3k2_c3k(6, src_of(S[5], 0, S[5].C), &S[6]));
+  step = 7;
+  YB_TRY(downconv(7, S[6], &S[7]));
+  step = 8;
+  YB_TRY(c3k2_c3k(8, src_of(S[7], 0, S[7].C), &S[8]));
+  step = 9;
+  YB_TRY(sppf(9, S[8], &S[9]));
+  step = 10;
+  YB_TRY(c2psa(10, S[9], &S[10]));
+  // steps 11-12: upsample(buf10) ++ buf6, read in place by model.13's cv1.
+  step = 13;
+  YB_TRY(c3k2_c3k(13, src_cat(S[10], 1, S[6], S[6].H, S[6].W), &S[13]));
+  // steps 14-15: upsample(buf13) ++ buf4.
+  step = 16;
+  YB_TRY(c3k2_c3k(16, src_cat(S[13], 1, S[4], S[4].H, S[4].W), &S[16]));
+  step = 17;
+  YB_TRY(downconv(17, S[16], &S[17]));
+  // step 18: buf17 ++ buf13.
+  step = 19;
+  YB_TRY(c3k2_c3k(19, src_cat(S[17], 0, S[13], S[13].H, S[13].W), &S[19]));
+  step = 20;
+  YB_TRY(downconv(20, S[19], &S[20]));
+  // step 21: buf20 ++ buf10.
+  step = 22;
+  YB_TRY(c3k2_attn(22, src_cat(S[20], 0, S[10], S[10].H, S[10].W), &S[22]));
+
+  // step 23: Detect one2one (detect.c:253-454).
+  step = 23;
+  {
+    const std::string d = "model." + std::to_string(23);
+    const bool o2o = exists(d + ".one2one_cv2.0.0.conv.weight");
+    const std::string b2 = d + (o2o ? ".one2one_cv2." : ".cv2.");
+    const std::string b3 = d + (o2o ? ".one2one_cv3." : ".cv3.");
+    const Buf* feats[3] = {&S[16], &S[19], &S[22]};
+    const int strides[3] = {8, 16, 32};
+    int N = 0, base[3];
+    for (int s = 0; s < 3; ++s) {
+      base[s] = N;
+      N += feats[s]->H * feats[s]->W;
+    }
+    p->n_anchors = N;
+    const int nc = nc_;
+    if (nc < 1 || nc % 4) {
+      *why = "num_classes must be a positive multiple of 4";
+      return cudaErrorInvalidValue;
+    }
+    YB_TRY(alloc_raw(static_cast<size_t>(B) * N * 4 * 4, &p->d_dist));
+    YB_TRY(alloc_raw(static_cast<size_t>(B) * N * nc * 4, &p->d_logits));
+    YB_TRY(alloc_raw(static_cast<size_t>(B) * N * 4 * 4, &p->d_boxes));
+    YB_TRY(alloc_raw(static_cast<size_t>(B) * N * 4, &p->d_maxscore));
+    YB_TRY(alloc_raw(static_cast<size_t>(B) * p->max_det * 6 * 4, &p->d_out));
+    for (int s = 0; s < 3; ++s) {
+      const Buf& f = *feats[s];
+      const std::string si = std::to_string(s);
+      DevConv *w0, *w1, *w2, *pw0, *pw1, *wf;
+      DevDw *dw0, *dw1;
+      YB_TRY(conv(b2 + si + ".0", &w0));
+      YB_TRY(conv(b2 + si + ".1", &w1));
+      YB_TRY(conv_w(b2 + si + ".2", true, &w2, why));
+      YB_TRY(dw_w(b3 + si + ".0.0", &dw0, why));
+      YB_TRY(conv(b3 + si + ".0.1", &pw0));
+      YB_TRY(dw_w(b3 + si + ".1.0", &dw1, why));
+      YB_TRY(conv(b3 + si + ".1.1", &pw1));
+      YB_TRY(conv_w(b3 + si + ".2", true, &wf, why));
+      if (w2->co != 4 || wf->co != nc) {
+        *why = "detect head output widths";
+        return cudaErrorInvalidValue;
+      }
+      // box branch (detect.c:168-191)
+      Buf t1, t2;
+      YB_TRY(alloc_buf(f.H, f.W, w0->co, &t1));
+      YB_TRY(add_conv(w0, src_of(f, 0, f.C), 1, 1, kActSiLU, ov(t1), TView()));
+      YB_TRY(alloc_buf(f.H, f.W, w1->co, &t2));
+      YB_TRY(add_conv(w1, src_of(t1, 0, t1.C), 1, 1, kActSiLU, ov(t2), TView()));
+      OView dv;
+      dv.ptr = p->d_dist + static_cast<size_t>(base[s]) * 4;
+      dv.bstride = static_cast<long long>(N) * 4;
+      dv.cstride = 4;
+      YB_TRY(add_conv(w2, src_of(t2, 0, t2.C), 1, 0, kActNone, dv, TView()));
+      // class branch (detect.c:193-232)
+      Buf d0, p0, d1, p1;
+      YB_TRY(alloc_buf(f.H, f.W, f.C, &d0));
+      DwArgs da;
+      da.in = tv(f);
+      da.B = B;
+      da.H = f.H;
+      da.W = f.W;
+      da.C = f.C;
+      da.w = dw0->w;
+      da.bias = dw0->bias;
+      da.act = kActSiLU;
+      da.out = ov(d0);
+      if (dw0->c != f.C) {
+        *why = "detect dw width";
+        return cudaErrorInvalidValue;
+      }
+      const double px = static_cast<double>(B) * f.H * f.W;
+      add_op(kOpDw, 18.0 * px * f.C, 8.0 * px * f.C, [da](cudaStream_t st) { return launch_dwconv3x3(da, st); });
+      YB_TRY(alloc_buf(f.H, f.W, pw0->co, &p0));
+      YB_TRY(add_conv(pw0, src_of(d0, 0, d0.C), 1, 0, kActSiLU, ov(p0), TView()));
+      YB_TRY(alloc_buf(f.H, f.W, p0.C, &d1));
+      DwArgs db = da;
+      db.in = tv(p0);
+      db.C = p0.C;
+      db.w = dw1->w;
+      db.bias = dw1->bias;
+      db.out = ov(d1);
+      if (dw1->c != p0.C) {
+        *why = "detect dw width";
+        return cudaErrorInvalidValue;
+      }
+      add_op(kOpDw, 18.0 * px * p0.C, 8.0 * px * p0.C, [db](cudaStream_t st) { return launch_dwconv3x3(db, st); });
+      YB_TRY(alloc_buf(f.H, f.W, pw1->co, &p1));
+      YB_TRY(add_conv(pw1, src_of(d1, 0, d1.C), 1, 0, kActSiLU, ov(p1), TView()));
+      OView lv;
+      lv.ptr = p->d_logits + static_cast<size_t>(base[s]) * nc;
+      lv.bstride = static_cast<long long>(N) * nc;
+      lv.cstride = nc;
+      YB_TRY(add_conv(wf, src_of(p1, 0, p1.C), 1, 0, kActNone, lv, TView()));
+    }
+    DecodeArgs de;
+    de.dist = p->d_dist;
+    de.logits = p->d_logits;
+    de.boxes = p->d_boxes;
+    de.maxscore = p->d_maxscore;
+    de.B = B;
+    de.N = N;
+    de.nc = nc;
+    de.nscales = 3;
+    for (int s = 0; s < 3; ++s) {
+      de.base[s] = base[s];
+      de.w[s] = feats[s]->W;
+      de.stride[s] = strides[s];
+    }
+    add_op(kOpDecode, 0.0, 4.0 * B * N * (4.0 + nc + 4.0 + 1.0), [de](cudaStream_t st) { return launch_decode(de, st); });
+    TopkArgs ta;
+    ta.maxscore = p->d_maxscore;
+    ta.scores = p->d_logits;
+    ta.s_bstride = static_cast<long long>(N) * nc;
+    ta.s_rstride = nc;
+    ta.apply_sigmoid = 1;
+    ta.boxes = p->d_boxes;
+    ta.b_bstride = static_cast<long long>(N) * 4;
+    ta.b_rstride = 4;
+    ta.dets = p->d_out;
+    ta.B = B;
+    ta.N = N;
+    ta.nc = nc;
+    ta.max_det = p->max_det;
+    ta.cap = p->max_det;
+    add_op(kOpTopk, 0.0, 4.0 * B * (N + static_cast<double>(p->max_det) * (nc + 4 + 6)),
+           [ta](cudaStream_t st) { return launch_topk(ta, st); });
+  }
+  return cudaSuccess;
+}
+
+cudaError_t Engine::profile_ops(Plan* p, int reps, std::vector<double>* ms) {
+  const size_t n = p->ops.size();
+  ms->assign(n, 0.0);
+  std::vector<cudaEvent_t> ev(2 * n, nullptr);
+  cudaError_t e = cudaSuccess;
+  for (auto& x : ev)
+    if (e == cudaSuccess) e = cudaEventCreate(&x);
+  for (int r = 0; r < reps && e == cudaSuccess; ++r) {
+    for (size_t i = 0; i < n && e == cudaSuccess; ++i) {
+      cudaEventRecord(ev[2 * i], stream_);
+      e = p->ops[i].run(stream_);
+      cudaEventRecord(ev[2 * i + 1], stream_);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+    for (size_t i = 0; i < n && e == cudaSuccess; ++i) {
+      float t = 0.f;
+      cudaEventElapsedTime(&t, ev[2 * i], ev[2 * i + 1]);
+      (*ms)[i] += t / reps;
+    }
+  }
+  for (auto& x : ev)
+    if (x) cudaEventDestroy(x);
+  return e;
+}
+
+cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::string* why) {
+  for (auto& p : plans_) {
+    if (p->B == B && p->H == H && p->W == W && p->max_det == max_det) {
+      *out = p.get();
+      return cudaSuccess;
+    }
+  }
+  if (hw_.empty()) {
+    *why = "no weights uploaded";
+    return cudaErrorInvalidValue;
+  }
+  if (B < 1 || H < 32 || W < 32 || H % 32 || W % 32 || max_det < 1 || max_det > kTopkMax) {
+    *why = "unsupported input shape (H, W must be multiples of 32; 1 <= max_det <= 1024)";
+    return cudaErrorInvalidValue;
+  }
+  cudaSetDevice(device_);
+  std::unique_ptr<Plan> p(new Plan());
+  p->B = B;
+  p->H = H;
+  p->W = W;
+  p->max_det = max_det;
+  cudaError_t e = build(p.get(), why);
+  if (e != cudaSuccess) {
+    release_plan(p.get());
+    return e;
+  }
+  // One eager pass validates every launch before the graph is captured.
+  cudaMemsetAsync(p->d_in, 0, static_cast<size_t>(B) * 3 * H * W * 4, stream_);
+  e = run(p.get(), stream_, nullptr);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+  if (e != cudaSuccess) {
+    *why = std::string("validation pass: ") + cudaGetErrorString(e);
+    release_plan(p.get());
+    return e;
+  }
+  const int kerr = take_kernel_error();
+  if (kerr) {
+    *why = "kernel error flag " + std::to_string(kerr) + " in validation pass";
+    release_plan(p.get());
+    return cudaErrorLaunchFailure;
+  }
+  cudaGraph_t g = nullptr;
+  e = cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal);
+  if (e == cudaSuccess) {
+    for (const Op& op : p->ops) {
+      e = op.run(stream_);
+      if (e != cudaSuccess) break;
+    }
+    cudaError_t e2 = cudaStreamEndCapture(stream_, &g);
+    if (e == cudaSuccess) e = e2;
+  }
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&p->graph, g, 0);
+  if (g) cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    *why = std::string("graph capture: ") + cudaGetErrorString(e);
+    release_plan(p.get());
+    return e;
+  }
+  *out = p.get();
+  plans_.push_back(std::move(p));
+  return cudaSuccess;
+}
+
+cudaError_t Engine::run(Plan* p, cudaStream_t s, cudaEvent_t* ev) {
+  if (!ev && p->graph) return cudaGraphLaunch(p->graph, s);
+  int cur = -1;
+  for (const Op& op : p->ops) {
+    if (ev && op.step != cur) {
+      if (cur >= 0) cudaEventRecord(ev[2 * cur + 1], s);
+      cur = op.step;
+      cudaEventRecord(ev[2 * cur], s);
+    }
+    cudaError_t e = op.run(s);
+    if (e != cudaSuccess) return e;
+  }
+  if (ev && cur >= 0) cudaEventRecord(ev[2 * cur + 1], s);
+  return cudaSuccess;
+}
+
+}  // namespace yb

@@ -1,0 +1,147 @@
+// Device replica of a YOLO26 model and its execution plans.
+//
+// The reference walks a fixed 24-step graph in model_forward_ex
+// (model.c:764-903), allocating scratch per block.  Here the same graph is
+// lowered once per input shape (B, H, W) into a flat list of kernel launches
+// over a single HBM arena: every concat is a channel slice of a shared buffer,
+// every upsample is an addressing mode of the consumer's loads, and the whole
+// list is captured as one CUDA graph.  Widths come from the weight shapes, so
+// any YOLO26 width (n, s, ...) runs unchanged.
+#pragma once
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+#include <cuda_runtime.h>
+#include "kernels.h"
+
+namespace yb {
+
+struct HostTensor {
+  int dims[4] = {1, 1, 1, 1};
+  int ndim = 0;
+  std::vector<float> data;
+};
+using WeightMap = std::map<std::string, HostTensor>;
+
+struct DevConv {
+  uint8_t* wpack = nullptr;
+  float* bias = nullptr;
+  int co = 0, ci = 0, kh = 0, kw = 0;
+  int n_tile = 0, n_tiles = 0, num_kc = 0, K = 0;
+};
+struct DevDw {
+  float* w = nullptr;  // [9][C]
+  float* bias = nullptr;
+  int c = 0;
+};
+struct DevStem {
+  float* w = nullptr;  // [Co][Ci][3][3]
+  float* bias = nullptr;
+  int co = 0, ci = 0, k = 0;
+};
+
+// A full NHWC activation tensor [B, H, W, C] in the arena.
+struct Buf {
+  float* ptr = nullptr;
+  int H = 0, W = 0, C = 0;
+  long long bstride = 0;
+};
+
+// An input of a convolution: one tensor, or the channel concat of an
+// (optionally nearest-upsampled) first source and a second source.
+struct Src {
+  TView v0;
+  int c0 = 0;
+  int lg0 = 0;
+  TView v1;
+  int c1 = 0;
+  int H = 0, W = 0;
+};
+
+enum OpKind : int { kOpConv = 0, kOpStem = 1, kOpDw = 2, kOpPool = 3, kOpAttn = 4, kOpDecode = 5, kOpTopk = 6 };
+
+struct Op {
+  int step;  // profile step (model_forward_profile_t index)
+  std::function<cudaError_t(cudaStream_t)> run;
+  int kind = kOpConv;
+  double flops = 0;  // algorithmic FLOPs of the launch (2 x MACs)
+  double bytes = 0;  // algorithmic HBM bytes: inputs + weights read once, outputs written once
+};
+
+struct Plan {
+  int B = 0, H = 0, W = 0;
+  int max_det = 300;
+  std::vector<Op> ops;
+  std::vector<void*> allocs;
+  float* d_in = nullptr;    // [B,3,H,W]
+  float* d_out = nullptr;   // [B,max_det,6]
+  float* d_dist = nullptr;  // [B,N,4]
+  float* d_logits = nullptr;
+  float* d_boxes = nullptr;
+  float* d_maxscore = nullptr;
+  int n_anchors = 0;
+  Buf stage[23];  // model->buffers[0..22] equivalents (concat/upsample ones unset)
+  cudaGraphExec_t graph = nullptr;
+  size_t arena_bytes = 0;
+};
+
+class Engine {
+ public:
+  explicit Engine(int device);
+  ~Engine();
+  Engine(const Engine&) = delete;
+  Engine& operator=(const Engine&) = delete;
+
+  // Takes BN-folded host weights (names as written by the converter).
+  cudaError_t set_weights(WeightMap&& w, int num_classes, std::string* why);
+  bool has_weights() const { return !hw_.empty(); }
+
+  // Plan for (B, H, W, max_det), built and captured on first use.
+  cudaError_t get_plan(int B, int H, int W, int max_det, Plan** out, std::string* why);
+
+  // Enqueues the forward of `p` on `s` (graph launch, or eager when
+  // step_events != nullptr: then events[2*step], events[2*step+1] bracket
+  // each profile step's launches).
+  cudaError_t run(Plan* p, cudaStream_t s, cudaEvent_t* step_events);
+
+  // Runs the plan's launches eagerly `reps` times with an event pair around
+  // each launch; ms[i] receives launch i's mean device time.
+  cudaError_t profile_ops(Plan* p, int reps, std::vector<double>* ms);
+
+  // Reads and clears the kernel error word; returns its value.
+  int take_kernel_error();
+
+  int device() const { return device_; }
+  cudaStream_t stream() const { return stream_; }
+  int num_classes() const { return nc_; }
+  int num_sms() const { return num_sms_; }
+
+ private:
+  const HostTensor* find(const std::string& name) const;
+  cudaError_t conv_w(const std::string& prefix, bool plain, DevConv** out, std::string* why);
+  cudaError_t dw_w(const std::string& prefix, DevDw** out, std::string* why);
+  cudaError_t dev_alloc(size_t bytes, void** p);
+  cudaError_t build(Plan* p, std::string* why);
+  void release_plan(Plan* p);
+
+  int device_ = 0;
+  int num_sms_ = 148;
+  int nc_ = 80;
+  cudaStream_t stream_ = nullptr;
+  int* d_err_ = nullptr;
+  WeightMap hw_;
+  std::map<std::string, DevConv> convs_;
+  std::map<std::string, DevDw> dws_;
+  DevStem stem_;
+  std::vector<void*> weight_allocs_;
+  std::vector<std::unique_ptr<Plan>> plans_;
+};
+
+// Reads the converter's .bin layout (int32 nc, int32 count, records) and folds
+// BatchNorm exactly like the reference (model.c:121-180, utils.c:81-106).
+bool read_weight_bin(const char* path, WeightMap* out, int* num_classes, std::string* why);
+void fold_all_bn_map(WeightMap* w);
+
+}  // namespace yb

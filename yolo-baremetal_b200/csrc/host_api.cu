@@ -1,0 +1,1008 @@
+// Host entry points: the reference's model/tensor/utils/detect/detection API
+// (phucb2/yolo-baremetal include/*.h) and the yb_cuda_* C-ABI shim, on top of
+// the device engine.  Every status code follows status.h; CUDA failures are
+// mapped by cuda_status() and described by yb_cuda_last_error().
+#include <time.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "detect.h"
+#include "detection.h"
+#include "engine.h"
+#include "model.h"
+#include "runtime.h"
+#include "tensor.h"
+#include "utils.h"
+#include "yb_cuda.h"
+
+namespace yb {
+
+namespace {
+thread_local std::string g_err;
+}
+
+void set_error(const std::string& msg) { g_err = msg; }
+const char* last_error() { return g_err.c_str(); }
+
+status_t cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return SUCCESS;
+  set_error(std::string(what) + ": " + cudaGetErrorString(e));
+  return e == cudaErrorMemoryAllocation ? ERROR_OUT_OF_MEMORY : ERROR_DEVICE;
+}
+
+DevScope* current_scope() {
+  thread_local std::map<int, DevScope> scopes;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error(std::string("no CUDA device: ") + cudaGetErrorString(e));
+    return nullptr;
+  }
+  auto it = scopes.find(dev);
+  if (it != scopes.end()) return &it->second;
+  DevScope s;
+  s.device = dev;
+  if ((e = cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking)) != cudaSuccess ||
+      (e = cudaMalloc(&s.d_err, sizeof(int))) != cudaSuccess || (e = cudaMemset(s.d_err, 0, sizeof(int))) != cudaSuccess ||
+      (e = init_conv_kernel_attributes()) != cudaSuccess) {
+    set_error(std::string("device scope: ") + cudaGetErrorString(e));
+    return nullptr;
+  }
+  cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev);
+  return &scopes.emplace(dev, s).first->second;
+}
+
+// One device replica behind a void* context.
+struct Ctx {
+  std::unique_ptr<Engine> eng;
+  Plan* last = nullptr;
+  cudaEvent_t ev[2 * MODEL_FORWARD_PROFILE_STEPS] = {};
+  cudaEvent_t h2d_done = nullptr;
+  cudaEvent_t done = nullptr;
+  float* h_stage = nullptr;  // pinned staging for detections of a sharded call
+  size_t h_stage_bytes = 0;
+  bool inflight = false;
+  int stall_ms = 0;  // host-side fault injection for deadline tests
+};
+
+namespace {
+
+Ctx* as_ctx(void* p) { return static_cast<Ctx*>(p); }
+
+status_t ctx_ready(Ctx* c) {
+  if (!c) return ERROR_NULL_POINTER;
+  cudaError_t e = cudaSetDevice(c->eng->device());
+  if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  if (c->inflight) {
+    e = cudaEventSynchronize(c->done);
+    if (e != cudaSuccess) return cuda_status(e, "previous call");
+    c->inflight = false;
+  }
+  return SUCCESS;
+}
+
+status_t check_kernel_flag(Ctx* c) {
+  const int k = c->eng->take_kernel_error();
+  if (k) {
+    set_error("device kernel reported error code " + std::to_string(k));
+    return ERROR_DEVICE;
+  }
+  return SUCCESS;
+}
+
+status_t plan_for(Ctx* c, int B, int H, int W, int max_det, Plan** p) {
+  std::string why;
+  cudaError_t e = c->eng->get_plan(B, H, W, max_det, p, &why);
+  if (e == cudaSuccess) return SUCCESS;
+  if (e == cudaErrorInvalidValue) {
+    set_error("plan: " + why);
+    return why.rfind("missing", 0) == 0 ? ERROR_FILE_NOT_FOUND : ERROR_INVALID_DIMS;
+  }
+  const status_t st = cuda_status(e, "plan");
+  set_error(std::string(last_error()) + (why.empty() ? "" : " (" + why + ")"));
+  return st;
+}
+
+// Stage tensors of image 0 in the reference's order and names (model.c:782-887).
+status_t dump_stages(Ctx* c, Plan* p, const float* in_nchw, yb_stage_cb cb, void* user) {
+  cudaStream_t s = c->eng->stream();
+  const Buf* S = p->stage;
+  size_t maxe = static_cast<size_t>(3) * p->H * p->W;
+  for (int i = 0; i < 23; ++i)
+    if (S[i].ptr) maxe = std::max(maxe, static_cast<size_t>(S[i].H) * S[i].W * S[i].C * 2);
+  DevMem t0, t1;
+  cudaError_t e = t0.alloc(maxe * 4);
+  if (e == cudaSuccess) e = t1.alloc(maxe * 4);
+  if (e != cudaSuccess) return cuda_status(e, "stage dump buffers");
+  std::vector<float> host(maxe);
+  auto tv = [](const Buf& b) {
+    TView v;
+    v.ptr = b.ptr;
+    v.bstride = b.bstride;
+    v.cstride = b.C;
+    return v;
+  };
+  auto emit = [&](const char* name, TView v, int C, int H, int W) -> status_t {
+    cudaError_t er = launch_nhwc_to_nchw(v, 1, C, H, W, t1.f(), s);
+    if (er == cudaSuccess) er = cudaMemcpyAsync(host.data(), t1.p, static_cast<size_t>(C) * H * W * 4, cudaMemcpyDeviceToHost, s);
+    if (er == cudaSuccess) er = cudaStreamSynchronize(s);
+    if (er != cudaSuccess) return cuda_status(er, name);
+    cb(user, name, host.data(), 1, C, H, W);
+    return SUCCESS;
+  };
+  auto emit_buf = [&](const char* name, int k) { return emit(name, tv(S[k]), S[k].C, S[k].H, S[k].W); };
+  auto emit_cat = [&](const char* name, const Buf& a, int up, const Buf* b, int H, int W) -> status_t {
+    OView o;
+    o.ptr = t0.f();
+    o.cstride = a.C + (b ? b->C : 0);
+    o.bstride = static_cast<long long>(H) * W * o.cstride;
+    TView bv = b ? tv(*b) : tv(a);
+    cudaError_t er = launch_gather_concat(tv(a), a.C, up, bv, b ? b->C : 0, 1, H, W, o, s);
+    if (er != cudaSuccess) return cuda_status(er, name);
+    TView v;
+    v.ptr = t0.f();
+    v.cstride = o.cstride;
+    v.bstride = o.bstride;
+    return emit(name, v, o.cstride, H, W);
+  };
+  status_t st;
+  cb(user, "stage_00_input", in_nchw, 1, 3, p->H, p->W);
+  static const char* direct[11] = {"stage_01_buf0", "stage_02_buf1", "stage_03_buf2", "stage_04_buf3",
+                                   "stage_05_buf4", "stage_06_buf5", "stage_07_buf6", "stage_08_buf7",
+                                   "stage_09_buf8", "stage_10_buf9", "stage_11_buf10"};
+  for (int k = 0; k <= 10; ++k)
+    if ((st = emit_buf(direct[k], k)) != SUCCESS) return st;
+  if ((st = emit_cat("stage_12_buf11", S[10], 2, nullptr, S[6].H, S[6].W)) != SUCCESS) return st;
+  if ((st = emit_cat("stage_13_buf12", S[10], 2, &S[6], S[6].H, S[6].W)) != SUCCESS) return st;
+  if ((st = emit_buf("stage_14_buf13", 13)) != SUCCESS) return st;
+  if ((st = emit_cat("stage_15_buf14", S[13], 2, nullptr, S[4].H, S[4].W)) != SUCCESS) return st;
+  if ((st = emit_cat("stage_16_buf15", S[13], 2, &S[4], S[4].H, S[4].W)) != SUCCESS) return st;
+  if ((st = emit_buf("stage_17_buf16", 16)) != SUCCESS) return st;
+  if ((st = emit_buf("stage_18_buf17", 17)) != SUCCESS) return st;
+  if ((st = emit_cat("stage_19_buf18", S[17], 1, &S[13], S[13].H, S[13].W)) != SUCCESS) return st;
+  if ((st = emit_buf("stage_20_buf19", 19)) != SUCCESS) return st;
+  if ((st = emit_buf("stage_21_buf20", 20)) != SUCCESS) return st;
+  if ((st = emit_cat("stage_22_buf21", S[20], 1, &S[10], S[10].H, S[10].W)) != SUCCESS) return st;
+  if ((st = emit_buf("stage_23_buf22", 22)) != SUCCESS) return st;
+  std::vector<float> dets(static_cast<size_t>(p->max_det) * 6);
+  e = cudaMemcpy(dets.data(), p->d_out, dets.size() * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "stage dump detections");
+  cb(user, "stage_24_buf23", dets.data(), 1, p->max_det, 6, 1);
+  cb(user, "stage_25_detect", dets.data(), 1, p->max_det, 6, 1);
+  return SUCCESS;
+}
+
+void weights_from_model(const model_t* m, WeightMap* out) {
+  for (int i = 0; i < m->num_weights; ++i) {
+    const tensor_t& t = m->weights[i].tensor;
+    HostTensor h;
+    h.ndim = 4;
+    size_t n = 1;
+    for (int d = 0; d < 4; ++d) {
+      h.dims[d] = t.dims[d];
+      n *= static_cast<size_t>(t.dims[d]);
+    }
+    h.data.assign(t.data, t.data + n);
+    (*out)[m->weights[i].name] = std::move(h);
+  }
+}
+
+// Model side table: device replicas keyed by model_t*, so model_t keeps the
+// reference's layout.
+std::mutex g_models_mu;
+std::map<const model_t*, Ctx*> g_models;
+
+Ctx* model_ctx(const model_t* m) {
+  std::lock_guard<std::mutex> lk(g_models_mu);
+  auto it = g_models.find(m);
+  return it == g_models.end() ? nullptr : it->second;
+}
+
+}  // namespace
+}  // namespace yb
+
+using namespace yb;
+
+// ====================================================================== shim
+extern "C" const char* yb_cuda_last_error(void) { return yb::last_error(); }
+
+extern "C" status_t yb_cuda_init(int device, void** ctx) {
+  if (!ctx) return ERROR_NULL_POINTER;
+  *ctx = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= n) {
+    set_error("device index out of range");
+    return ERROR_INVALID_DIMS;
+  }
+  if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  std::unique_ptr<Ctx> c(new Ctx());
+  c->eng.reset(new Engine(device));
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "engine init");
+  for (auto& ev : c->ev)
+    if ((e = cudaEventCreate(&ev)) != cudaSuccess) return cuda_status(e, "cudaEventCreate");
+  if ((e = cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming)) != cudaSuccess ||
+      (e = cudaEventCreateWithFlags(&c->h2d_done, cudaEventDisableTiming)) != cudaSuccess)
+    return cuda_status(e, "cudaEventCreate");
+  *ctx = c.release();
+  return SUCCESS;
+}
+
+extern "C" status_t yb_cuda_destroy(void* ctx) {
+  Ctx* c = as_ctx(ctx);
+  if (!c) return ERROR_NULL_POINTER;
+  cudaSetDevice(c->eng->device());
+  if (c->inflight) cudaEventSynchronize(c->done);
+  for (auto& ev : c->ev)
+    if (ev) cudaEventDestroy(ev);
+  if (c->done) cudaEventDestroy(c->done);
+  if (c->h2d_done) cudaEventDestroy(c->h2d_done);
+  if (c->h_stage) cudaFreeHost(c->h_stage);
+  c->eng.reset();
+  delete c;
+  return SUCCESS;
+}
+
+extern "C" status_t yb_cuda_upload_weights(void* ctx, const model_t* m, yb_precision p, const void* qparams) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !m) return ERROR_NULL_POINTER;
+  if (p != YB_PRECISION_FP32 || qparams) {
+    set_error("only YB_PRECISION_FP32 is implemented");
+    return ERROR_NOT_IMPLEMENTED;
+  }
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  WeightMap w;
+  weights_from_model(m, &w);
+  std::string why;
+  cudaError_t e = c->eng->set_weights(std::move(w), m->num_classes, &why);
+  if (e == cudaErrorInvalidValue) {
+    set_error(why);
+    return ERROR_FILE_NOT_FOUND;
+  }
+  c->last = nullptr;
+  return cuda_status(e, "upload weights");
+}
+
+extern "C" status_t yb_cuda_load_bin(void* ctx, const char* path) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !path) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  WeightMap w;
+  int nc = 0;
+  std::string why;
+  if (!read_weight_bin(path, &w, &nc, &why)) {
+    set_error(why);
+    return why.rfind("cannot open", 0) == 0 ? ERROR_FILE_NOT_FOUND : ERROR_INVALID_FORMAT;
+  }
+  fold_all_bn_map(&w);
+  cudaError_t e = c->eng->set_weights(std::move(w), nc, &why);
+  if (e == cudaErrorInvalidValue) {
+    set_error(why);
+    return ERROR_FILE_NOT_FOUND;
+  }
+  c->last = nullptr;
+  return cuda_status(e, "upload weights");
+}
+
+extern "C" status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int H, int W, float* out_dets,
+                                    int max_det, yb_stage_cb dump, void* user, double* step_ms) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !in_nchw || !out_dets) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  Plan* p = nullptr;
+  if ((st = plan_for(c, B, H, W, max_det, &p)) != SUCCESS) return st;
+  cudaStream_t s = c->eng->stream();
+  cudaError_t e = cudaMemcpyAsync(p->d_in, in_nchw, static_cast<size_t>(B) * 3 * H * W * 4, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_status(e, "input copy");
+  if (step_ms) {
+    for (int i = 0; i < 2 * MODEL_FORWARD_PROFILE_STEPS; ++i) cudaEventRecord(c->ev[i], s);
+  }
+  e = c->eng->run(p, s, step_ms ? c->ev : nullptr);
+  if (e != cudaSuccess) return cuda_status(e, "forward launch");
+  if (step_ms) cudaEventRecord(c->ev[2 * 24], s);
+  e = cudaMemcpyAsync(out_dets, p->d_out, static_cast<size_t>(B) * max_det * 6 * 4, cudaMemcpyDeviceToHost, s);
+  if (step_ms) cudaEventRecord(c->ev[2 * 24 + 1], s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e, "forward");
+  if ((st = check_kernel_flag(c)) != SUCCESS) return st;
+  c->last = p;
+  if (step_ms) {
+    bool has[MODEL_FORWARD_PROFILE_STEPS] = {};
+    for (const Op& op : p->ops) has[op.step] = true;
+    has[24] = true;
+    for (int i = 0; i < MODEL_FORWARD_PROFILE_STEPS; ++i) {
+      float ms = 0.f;
+      if (has[i]) cudaEventElapsedTime(&ms, c->ev[2 * i], c->ev[2 * i + 1]);
+      step_ms[i] = ms;
+    }
+  }
+  if (dump) return dump_stages(c, p, in_nchw, dump, user);
+  return SUCCESS;
+}
+
+extern "C" status_t yb_cuda_plan_io(void* ctx, int B, int H, int W, int max_det, float** d_in, float** d_out) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !d_in || !d_out) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  Plan* p = nullptr;
+  if ((st = plan_for(c, B, H, W, max_det, &p)) != SUCCESS) return st;
+  *d_in = p->d_in;
+  *d_out = p->d_out;
+  return SUCCESS;
+}
+
+extern "C" status_t yb_cuda_forward_device(void* ctx, const float* d_in, int B, int H, int W, float* d_out,
+                                           int max_det, void* stream) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !d_in || !d_out) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  Plan* p = nullptr;
+  if ((st = plan_for(c, B, H, W, max_det, &p)) != SUCCESS) return st;
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->eng->stream();
+  cudaError_t e = cudaSuccess;
+  if (d_in != p->d_in)
+    e = cudaMemcpyAsync(p->d_in, d_in, static_cast<size_t>(B) * 3 * H * W * 4, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess) e = c->eng->run(p, s, nullptr);
+  if (e == cudaSuccess && d_out != p->d_out)
+    e = cudaMemcpyAsync(d_out, p->d_out, static_cast<size_t>(B) * max_det * 6 * 4, cudaMemcpyDeviceToDevice, s);
+  c->last = p;
+  return cuda_status(e, "forward_device");
+}
+
+extern "C" status_t yb_cuda_get_head(void* ctx, float* logits, float* boxes, int* n_anchors, int* nc) {
+  Ctx* c = as_ctx(ctx);
+  if (!c) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  Plan* p = c->last;
+  if (!p) {
+    set_error("no forward has run on this context");
+    return ERROR_INVALID_DIMS;
+  }
+  cudaError_t e = cudaStreamSynchronize(c->eng->stream());
+  const size_t n = static_cast<size_t>(p->B) * p->n_anchors;
+  if (e == cudaSuccess && logits)
+    e = cudaMemcpy(logits, p->d_logits, n * c->eng->num_classes() * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && boxes) e = cudaMemcpy(boxes, p->d_boxes, n * 4 * 4, cudaMemcpyDeviceToHost);
+  if (n_anchors) *n_anchors = p->n_anchors;
+  if (nc) *nc = c->eng->num_classes();
+  return cuda_status(e, "get_head");
+}
+
+extern "C" status_t yb_cuda_profile_ops(void* ctx, int B, int H, int W, int max_det, int reps, yb_op_stat* stats,
+                                        int cap, int* n_ops) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !n_ops) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  Plan* p = nullptr;
+  if ((st = plan_for(c, B, H, W, max_det, &p)) != SUCCESS) return st;
+  *n_ops = static_cast<int>(p->ops.size());
+  if (!stats) return SUCCESS;
+  std::vector<double> ms;
+  cudaError_t e = c->eng->profile_ops(p, reps < 1 ? 1 : reps, &ms);
+  if (e != cudaSuccess) return cuda_status(e, "profile_ops");
+  if ((st = check_kernel_flag(c)) != SUCCESS) return st;
+  for (int i = 0; i < *n_ops && i < cap; ++i) {
+    stats[i].kind = p->ops[i].kind;
+    stats[i].step = p->ops[i].step;
+    stats[i].ms = ms[i];
+    stats[i].flops = p->ops[i].flops;
+    stats[i].bytes = p->ops[i].bytes;
+  }
+  return SUCCESS;
+}
+
+extern "C" status_t yb_cuda_debug_inject_stall(void* ctx, int ms) {
+  Ctx* c = as_ctx(ctx);
+  if (!c) return ERROR_NULL_POINTER;
+  c->stall_ms = ms;
+  return SUCCESS;
+}
+
+namespace {
+
+// One shard of yb_cuda_forward_sharded, run on its own host thread.
+status_t run_shard(Ctx* c, const float* in, int B, int H, int W, float* out, int max_det,
+                   std::chrono::steady_clock::time_point deadline, bool has_deadline, std::string* msg) {
+  using clock = std::chrono::steady_clock;
+  auto expired = [&] { return has_deadline && clock::now() >= deadline; };
+  cudaError_t e = cudaSetDevice(c->eng->device());
+  if (e != cudaSuccess) {
+    *msg = cudaGetErrorString(e);
+    return ERROR_DEVICE;
+  }
+  if (c->inflight) {
+    while (cudaEventQuery(c->done) == cudaErrorNotReady) {
+      if (expired()) {
+        *msg = "previous call still running at the deadline";
+        return ERROR_TIMEOUT;
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    c->inflight = false;
+  }
+  if (c->stall_ms > 0) std::this_thread::sleep_for(std::chrono::milliseconds(c->stall_ms));
+  if (expired()) {
+    *msg = "shard did not start before the deadline";
+    return ERROR_TIMEOUT;
+  }
+  Plan* p = nullptr;
+  status_t st = plan_for(c, B, H, W, max_det, &p);
+  if (st != SUCCESS) {
+    *msg = last_error();
+    return st;
+  }
+  const size_t det_bytes = static_cast<size_t>(B) * max_det * 6 * 4;
+  if (c->h_stage_bytes < det_bytes) {
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    c->h_stage = nullptr;
+    c->h_stage_bytes = 0;
+    if ((e = cudaMallocHost(&c->h_stage, det_bytes)) != cudaSuccess) {
+      *msg = cudaGetErrorString(e);
+      return ERROR_OUT_OF_MEMORY;
+    }
+    c->h_stage_bytes = det_bytes;
+  }
+  cudaStream_t s = c->eng->stream();
+  e = cudaMemcpyAsync(p->d_in, in, static_cast<size_t>(B) * 3 * H * W * 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaEventRecord(c->h2d_done, s);
+  if (e == cudaSuccess) e = c->eng->run(p, s, nullptr);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(c->h_stage, p->d_out, det_bytes, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaEventRecord(c->done, s);
+  if (e != cudaSuccess) {
+    *msg = cudaGetErrorString(e);
+    return ERROR_DEVICE;
+  }
+  c->inflight = true;
+  c->last = p;
+  while (true) {
+    e = cudaEventQuery(c->done);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) {
+      *msg = cudaGetErrorString(e);
+      return ERROR_DEVICE;
+    }
+    if (expired()) {
+      // The input may still be read by the copy engine: let that copy finish
+      // before returning control of the caller's buffer.
+      const auto t0 = clock::now();
+      while (cudaEventQuery(c->h2d_done) == cudaErrorNotReady && clock::now() - t0 < std::chrono::seconds(1))
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+      *msg = "shard on device " + std::to_string(c->eng->device()) + " missed the deadline";
+      return ERROR_TIMEOUT;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  c->inflight = false;
+  const int k = c->eng->take_kernel_error();
+  if (k) {
+    *msg = "device kernel reported error code " + std::to_string(k);
+    return ERROR_DEVICE;
+  }
+  std::memcpy(out, c->h_stage, det_bytes);
+  return SUCCESS;
+}
+
+}  // namespace
+
+extern "C" status_t yb_cuda_forward_sharded(void* const* ctxs, int G, const float* in_nchw, int B, int H, int W,
+                                            float* out_dets, int max_det, int timeout_ms) {
+  if (!ctxs || !in_nchw || !out_dets) return ERROR_NULL_POINTER;
+  if (G < 1 || B < 1) return ERROR_INVALID_DIMS;
+  for (int g = 0; g < G; ++g)
+    if (!ctxs[g]) return ERROR_NULL_POINTER;
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms > 0 ? timeout_ms : 0);
+  std::vector<status_t> st(G, SUCCESS);
+  std::vector<std::string> msg(G);
+  std::vector<std::thread> th;
+  const size_t img = static_cast<size_t>(3) * H * W;
+  const size_t det = static_cast<size_t>(max_det) * 6;
+  for (int g = 0; g < G; ++g) {
+    const int b0 = static_cast<int>(static_cast<long long>(g) * B / G);
+    const int b1 = static_cast<int>(static_cast<long long>(g + 1) * B / G);
+    if (b1 == b0) continue;
+    th.emplace_back([&, g, b0, b1] {
+      st[g] = run_shard(as_ctx(ctxs[g]), in_nchw + b0 * img, b1 - b0, H, W, out_dets + b0 * det, max_det, deadline,
+                        timeout_ms > 0, &msg[g]);
+    });
+  }
+  for (auto& t : th) t.join();
+  status_t result = SUCCESS;
+  for (int g = 0; g < G; ++g) {
+    if (st[g] != SUCCESS && (result == SUCCESS || st[g] == ERROR_TIMEOUT)) {
+      result = st[g];
+      set_error("shard " + std::to_string(g) + ": " + msg[g]);
+    }
+  }
+  return result;
+}
+
+// ================================================================ tensor.h
+extern "C" void* malloc_aligned(size_t size, size_t alignment) {
+  void* p = nullptr;
+  if (posix_memalign(&p, alignment, size ? size : alignment) != 0) return nullptr;
+  return p;
+}
+extern "C" void free_aligned(void* ptr) { free(ptr); }
+
+extern "C" status_t tensor_allocate(tensor_t* t, int n, int c, int h, int w) {
+  if (!t) return ERROR_NULL_POINTER;
+  t->dims[0] = n;
+  t->dims[1] = c;
+  t->dims[2] = h;
+  t->dims[3] = w;
+  t->stride[3] = 1;
+  t->stride[2] = w;
+  t->stride[1] = h * w;
+  t->stride[0] = c * h * w;
+  const size_t bytes = static_cast<size_t>(n) * c * h * w * sizeof(float);
+  t->data = static_cast<float*>(malloc_aligned(bytes, 64));
+  t->is_owner = t->data != nullptr;
+  return t->data ? SUCCESS : ERROR_OUT_OF_MEMORY;
+}
+
+extern "C" status_t tensor_free(tensor_t* t) {
+  if (!t) return ERROR_NULL_POINTER;
+  if (t->is_owner && t->data) {
+    free_aligned(t->data);
+    t->data = nullptr;
+  }
+  return SUCCESS;
+}
+
+extern "C" status_t tensor_fill(tensor_t* t, float v) {
+  if (!t || !t->data) return ERROR_NULL_POINTER;
+  const size_t n = static_cast<size_t>(t->dims[0]) * t->dims[1] * t->dims[2] * t->dims[3];
+  std::fill(t->data, t->data + n, v);
+  return SUCCESS;
+}
+
+extern "C" status_t tensor_copy(tensor_t* dst, const tensor_t* src) {
+  if (!dst || !src || !dst->data || !src->data) return ERROR_NULL_POINTER;
+  for (int i = 0; i < 4; ++i)
+    if (dst->dims[i] != src->dims[i]) return ERROR_INVALID_DIMS;
+  const size_t n = static_cast<size_t>(src->dims[0]) * src->dims[1] * src->dims[2] * src->dims[3];
+  std::memcpy(dst->data, src->data, n * sizeof(float));
+  return SUCCESS;
+}
+
+// ================================================================= utils.h
+extern "C" void timer_start(yb_timer_t* t) {
+  timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  t->start = static_cast<uint64_t>(ts.tv_sec) * 1000000000ull + static_cast<uint64_t>(ts.tv_nsec);
+}
+extern "C" void timer_stop(yb_timer_t* t) {
+  timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  t->end = static_cast<uint64_t>(ts.tv_sec) * 1000000000ull + static_cast<uint64_t>(ts.tv_nsec);
+}
+extern "C" double timer_elapsed_ms(const yb_timer_t* t) { return static_cast<double>(t->end - t->start) / 1e6; }
+
+extern "C" status_t load_named_tensor(FILE* f, char* name, tensor_t* tensor) {
+  if (!f || !name || !tensor) return ERROR_NULL_POINTER;
+  int32_t nl = 0;
+  if (std::fread(&nl, 4, 1, f) != 1) return ERROR_FILE_NOT_FOUND;
+  if (nl < 0 || nl >= 128 || std::fread(name, 1, static_cast<size_t>(nl), f) != static_cast<size_t>(nl))
+    return ERROR_INVALID_FORMAT;
+  name[nl] = '\0';
+  int32_t nd = 0;
+  if (std::fread(&nd, 4, 1, f) != 1 || nd < 0 || nd > 4) return ERROR_INVALID_FORMAT;
+  int dims[4] = {1, 1, 1, 1};
+  for (int d = 0; d < nd; ++d)
+    if (std::fread(&dims[d], 4, 1, f) != 1 || dims[d] < 0) return ERROR_INVALID_FORMAT;
+  status_t st = tensor_allocate(tensor, dims[0], dims[1], dims[2], dims[3]);
+  if (st != SUCCESS) return st;
+  const size_t n = static_cast<size_t>(dims[0]) * dims[1] * dims[2] * dims[3];
+  if (std::fread(tensor->data, sizeof(float), n, f) != n) {
+    tensor_free(tensor);
+    return ERROR_INVALID_FORMAT;
+  }
+  return SUCCESS;
+}
+
+extern "C" status_t save_named_tensor(FILE* f, const char* name, const tensor_t* t) {
+  if (!f || !name || !t || !t->data) return ERROR_NULL_POINTER;
+  const int32_t nl = static_cast<int32_t>(std::strlen(name));
+  const int32_t nd = 4;
+  if (std::fwrite(&nl, 4, 1, f) != 1 || std::fwrite(name, 1, static_cast<size_t>(nl), f) != static_cast<size_t>(nl) ||
+      std::fwrite(&nd, 4, 1, f) != 1 || std::fwrite(t->dims, 4, 4, f) != 4)
+    return ERROR_FILE_NOT_FOUND;
+  const size_t n = static_cast<size_t>(t->dims[0]) * t->dims[1] * t->dims[2] * t->dims[3];
+  if (std::fwrite(t->data, sizeof(float), n, f) != n) return ERROR_FILE_NOT_FOUND;
+  return SUCCESS;
+}
+
+extern "C" void fold_bn(tensor_t* conv_w, tensor_t* conv_b, const tensor_t* bn_w, const tensor_t* bn_b,
+                        const tensor_t* bn_rm, const tensor_t* bn_rv) {
+  const int out_c = conv_w->dims[0];
+  const size_t per = static_cast<size_t>(conv_w->dims[1]) * conv_w->dims[2] * conv_w->dims[3];
+  const float eps = 1e-5f;
+  for (int i = 0; i < out_c; ++i) {
+    const float scale = bn_w->data[i] / std::sqrt(bn_rv->data[i] + eps);
+    for (size_t j = 0; j < per; ++j) conv_w->data[i * per + j] *= scale;
+    if (conv_b) {
+      const float t = conv_b->data[i] - bn_rm->data[i];
+      const float t2 = t * scale;
+      conv_b->data[i] = t2 + bn_b->data[i];
+    }
+  }
+}
+
+// ============================================================= detection.h
+extern "C" status_t decode_detections(detection_results_t* results, const tensor_t* head, float threshold) {
+  if (!results || !head) return ERROR_NULL_POINTER;
+  if (head->dims[0] < 1) return ERROR_INVALID_DIMS;
+  const int rows = head->dims[1];
+  const int feat = head->dims[2];
+  const int w = head->dims[3];
+  if (feat < 6 || w < 1) return ERROR_INVALID_DIMS;
+  const int rs = feat * w;
+  results->count = 0;
+  for (int i = 0; i < rows; ++i) {
+    const float* r = head->data + static_cast<size_t>(i) * rs;
+    if (!(r[4] > threshold)) continue;
+    if (results->count >= results->capacity) break;
+    detection_t* d = &results->detections[results->count++];
+    d->x1 = r[0];
+    d->y1 = r[1];
+    d->x2 = r[2];
+    d->y2 = r[3];
+    d->score = r[4];
+    d->class_id = static_cast<int>(r[5]);
+  }
+  return SUCCESS;
+}
+
+// ================================================================ detect.h
+extern "C" status_t detect_postprocess_from_pred(const float* pred, int N, int nc, int max_det, tensor_t* out) {
+  if (!pred || !out || !out->data) return ERROR_NULL_POINTER;
+  if (out->dims[0] != 1 || out->dims[2] < 6 || out->dims[3] < 1) return ERROR_INVALID_DIMS;
+  if (N < 0 || nc < 1) return ERROR_INVALID_DIMS;
+  const int cap = out->dims[1];
+  int k = std::min(max_det, N);
+  k = std::min(k, cap);
+  const int rs = out->dims[2] * out->dims[3];
+  std::vector<float> rows(static_cast<size_t>(cap) * 6, 0.f);
+  if (k > 0) {
+    if (k > kTopkMax) {
+      set_error("k exceeds the device top-k limit");
+      return ERROR_INVALID_DIMS;
+    }
+    DevScope* sc = current_scope();
+    if (!sc) return ERROR_DEVICE;
+    DevMem dp, dd;
+    cudaError_t e = dp.alloc(static_cast<size_t>(N) * (4 + nc) * 4);
+    if (e == cudaSuccess) e = dd.alloc(static_cast<size_t>(k) * 6 * 4);
+    if (e != cudaSuccess) return cuda_status(e, "postprocess buffers");
+    e = cudaMemcpyAsync(dp.p, pred, static_cast<size_t>(N) * (4 + nc) * 4, cudaMemcpyHostToDevice, sc->stream);
+    TopkArgs ta;
+    ta.scores = dp.f() + 4;
+    ta.s_bstride = 0;
+    ta.s_rstride = 4 + nc;
+    ta.apply_sigmoid = 0;
+    ta.boxes = dp.f();
+    ta.b_rstride = 4 + nc;
+    ta.dets = dd.f();
+    ta.B = 1;
+    ta.N = N;
+    ta.nc = nc;
+    ta.max_det = k;
+    ta.cap = k;
+    if (e == cudaSuccess) e = launch_topk(ta, sc->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(rows.data(), dd.p, static_cast<size_t>(k) * 6 * 4, cudaMemcpyDeviceToHost, sc->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(sc->stream);
+    if (e != cudaSuccess) return cuda_status(e, "postprocess");
+  }
+  for (int t = 0; t < cap; ++t) {
+    float* r = out->data + static_cast<size_t>(t) * rs;
+    for (int u = 0; u < 6; ++u) r[u] = rows[static_cast<size_t>(t) * 6 + u];
+  }
+  return SUCCESS;
+}
+
+// ================================================================= model.h
+static const char* const k_step_names[MODEL_FORWARD_PROFILE_STEPS] = {
+    "conv model.0 /2 + SiLU",
+    "conv model.1 /2 + SiLU",
+    "C3k2 model.2 (n=1)",
+    "conv model.3 /2 + SiLU",
+    "C3k2 model.4 (n=1)",
+    "conv model.5 /2 + SiLU",
+    "C3k2 inner model.6",
+    "conv model.7 /2 + SiLU",
+    "C3k2 inner model.8",
+    "SPPF model.9",
+    "C2PSA model.10",
+    "upsample 2x \xe2\x86\x92 buf11",
+    "concat(buf11, buf6) \xe2\x86\x92 buf12",
+    "C3k2 inner model.13",
+    "upsample 2x \xe2\x86\x92 buf14",
+    "concat(buf14, buf4) \xe2\x86\x92 buf15",
+    "C3k2 inner model.16 (P3)",
+    "conv model.17 /2 + SiLU",
+    "concat(buf17, buf13) \xe2\x86\x92 buf18",
+    "C3k2 inner model.19 (P4)",
+    "conv model.20 /2 + SiLU",
+    "concat(buf20, buf10) \xe2\x86\x92 buf21",
+    "C3k2 attn head model.22 (P5)",
+    "Detect one2one \xe2\x86\x92 buf23",
+    "tensor_copy buf23 \xe2\x86\x92 output",
+};
+
+extern "C" void model_forward_profile_reset(model_forward_profile_t* p) {
+  if (!p) return;
+  std::memset(p, 0, sizeof(*p));
+}
+
+extern "C" const char* model_forward_profile_step_name(int i) {
+  if (i < 0 || i >= MODEL_FORWARD_PROFILE_STEPS) return "?";
+  return k_step_names[i];
+}
+
+extern "C" void model_forward_profile_print_last(const model_forward_profile_t* p, FILE* fp, const char* title) {
+  if (!p || !fp || p->runs == 0) return;
+  std::fprintf(fp, "%s\n", title);
+  std::fprintf(fp, "%-4s %-44s %12s %8s\n", "#", "step", "ms", "% fwd");
+  double tot = 0;
+  for (int i = 0; i < MODEL_FORWARD_PROFILE_STEPS; ++i) tot += p->ms_last[i];
+  for (int i = 0; i < MODEL_FORWARD_PROFILE_STEPS; ++i)
+    std::fprintf(fp, "%2d   %-44s %12.4f %7.2f%%\n", i + 1, k_step_names[i], p->ms_last[i],
+                 tot > 0 ? 100.0 * p->ms_last[i] / tot : 0.0);
+  std::fprintf(fp, "%-4s %-44s %12.4f\n", "", "total (timed steps)", tot);
+}
+
+extern "C" void model_forward_profile_print_aggregate(const model_forward_profile_t* p, FILE* fp) {
+  if (!fp) return;
+  if (!p || p->runs == 0) {
+    std::fprintf(fp, "No model_forward profile (no successful runs).\n");
+    return;
+  }
+  std::fprintf(fp, "\n=== model_forward per-step (avg over %u run(s)) ===\n", p->runs);
+  std::fprintf(fp, "%-4s %-44s %12s %8s\n", "#", "step", "avg ms", "% fwd");
+  double avg[MODEL_FORWARD_PROFILE_STEPS], tot = 0;
+  int hot = 0;
+  for (int i = 0; i < MODEL_FORWARD_PROFILE_STEPS; ++i) {
+    avg[i] = p->ms_sum[i] / p->runs;
+    tot += avg[i];
+    if (avg[i] > avg[hot]) hot = i;
+  }
+  for (int i = 0; i < MODEL_FORWARD_PROFILE_STEPS; ++i)
+    std::fprintf(fp, "%2d   %-44s %12.4f %7.2f%%\n", i + 1, k_step_names[i], avg[i], tot > 0 ? 100.0 * avg[i] / tot : 0.0);
+  std::fprintf(fp, "%-4s %-44s %12.4f\n", "", "total (sum of steps)", tot);
+  std::fprintf(fp, "\nHot step inside model_forward: #%d %s (~%.1f%% of forward).\n", hot + 1, k_step_names[hot],
+               tot > 0 ? 100.0 * avg[hot] / tot : 0.0);
+}
+
+extern "C" status_t model_create(model_t* m, int input_w, int input_h) {
+  if (!m) return ERROR_NULL_POINTER;
+  m->input_w = input_w;
+  m->input_h = input_h;
+  m->weights = nullptr;
+  m->num_weights = 0;
+  m->num_classes = 80;
+  m->num_buffers = 24;
+  m->buffers = static_cast<tensor_t*>(std::calloc(24, sizeof(tensor_t)));
+  if (!m->buffers) return ERROR_OUT_OF_MEMORY;
+  return tensor_allocate(&m->buffers[23], 1, 300, 6, 1);
+}
+
+extern "C" status_t model_destroy(model_t* m) {
+  if (!m) return ERROR_NULL_POINTER;
+  Ctx* c = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_models_mu);
+    auto it = g_models.find(m);
+    if (it != g_models.end()) {
+      c = it->second;
+      g_models.erase(it);
+    }
+  }
+  if (c) yb_cuda_destroy(c);
+  for (int i = 0; i < m->num_weights; ++i) tensor_free(&m->weights[i].tensor);
+  std::free(m->weights);
+  m->weights = nullptr;
+  m->num_weights = 0;
+  if (m->buffers) {
+    for (int i = 0; i < m->num_buffers; ++i) tensor_free(&m->buffers[i]);
+    std::free(m->buffers);
+    m->buffers = nullptr;
+  }
+  return SUCCESS;
+}
+
+extern "C" tensor_t* model_get_weight(model_t* m, const char* name) {
+  if (!m || !name) return nullptr;
+  for (int i = 0; i < m->num_weights; ++i)
+    if (std::strcmp(m->weights[i].name, name) == 0) return &m->weights[i].tensor;
+  return nullptr;
+}
+
+extern "C" status_t model_load_weights(model_t* m, const char* path) {
+  if (!m || !path) return ERROR_NULL_POINTER;
+  WeightMap w;
+  int nc = 0;
+  std::string why;
+  int raw_count = 0;
+  {
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return ERROR_FILE_NOT_FOUND;
+    int32_t hdr[2] = {0, 0};
+    if (std::fread(hdr, 4, 2, f) == 2) raw_count = hdr[1];
+    std::fclose(f);
+  }
+  if (!read_weight_bin(path, &w, &nc, &why)) {
+    set_error(why);
+    return ERROR_INVALID_FORMAT;
+  }
+  fold_all_bn_map(&w);
+  for (int i = 0; i < m->num_weights; ++i) tensor_free(&m->weights[i].tensor);
+  std::free(m->weights);
+  m->weights = static_cast<named_tensor_t*>(std::calloc(w.size() ? w.size() : 1, sizeof(named_tensor_t)));
+  if (!m->weights) return ERROR_OUT_OF_MEMORY;
+  m->num_weights = 0;
+  for (const auto& kv : w) {
+    named_tensor_t& nt = m->weights[m->num_weights];
+    std::strncpy(nt.name, kv.first.c_str(), sizeof(nt.name) - 1);
+    const HostTensor& h = kv.second;
+    status_t st = tensor_allocate(&nt.tensor, h.dims[0], h.dims[1], h.dims[2], h.dims[3]);
+    if (st != SUCCESS) return st;
+    std::memcpy(nt.tensor.data, h.data.data(), h.data.size() * 4);
+    ++m->num_weights;
+  }
+  m->num_classes = nc;
+  std::printf("Successfully loaded %d tensors (after BN fold, %d tensors in memory)\n", raw_count, m->num_weights);
+
+  Ctx* c = model_ctx(m);
+  if (!c) {
+    int dev = 0;
+    const char* env = std::getenv("YB_DEVICE");
+    if (env && *env) dev = std::atoi(env);
+    else if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    void* vc = nullptr;
+    status_t st = yb_cuda_init(dev, &vc);
+    if (st != SUCCESS) return st;
+    c = as_ctx(vc);
+    std::lock_guard<std::mutex> lk(g_models_mu);
+    g_models[m] = c;
+  }
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  cudaError_t e = c->eng->set_weights(std::move(w), nc, &why);
+  if (e == cudaErrorInvalidValue) {
+    set_error(why);
+    return ERROR_FILE_NOT_FOUND;
+  }
+  return cuda_status(e, "upload weights");
+}
+
+namespace {
+void stage_to_file(void* user, const char* name, const float* data, int n, int c, int h, int w) {
+  FILE* f = static_cast<FILE*>(user);
+  tensor_t t;
+  t.data = const_cast<float*>(data);
+  t.dims[0] = n;
+  t.dims[1] = c;
+  t.dims[2] = h;
+  t.dims[3] = w;
+  t.is_owner = false;
+  save_named_tensor(f, name, &t);
+}
+}  // namespace
+
+extern "C" status_t model_forward_ex(model_t* m, const tensor_t* input, tensor_t* output, FILE* stage_dump,
+                                     model_forward_profile_t* profile) {
+  if (!m || !input || !output || !input->data || !output->data) return ERROR_NULL_POINTER;
+  Ctx* c = model_ctx(m);
+  if (!c) {
+    set_error("model has no weights loaded");
+    return ERROR_FILE_NOT_FOUND;
+  }
+  const int B = input->dims[0], C = input->dims[1], H = input->dims[2], W = input->dims[3];
+  if (B < 1 || C != 3 || H % 32 || W % 32 || H < 32 || W < 32) return ERROR_INVALID_DIMS;
+  const int max_det = output->dims[1];
+  if (output->dims[0] != B || output->dims[2] < 6 || output->dims[3] < 1 || max_det < 1) return ERROR_INVALID_DIMS;
+  const int rs = output->dims[2] * output->dims[3];
+  std::vector<float> tmp;
+  float* dst = output->data;
+  if (rs != 6) {
+    tmp.resize(static_cast<size_t>(B) * max_det * 6);
+    dst = tmp.data();
+  }
+  double ms[MODEL_FORWARD_PROFILE_STEPS] = {0};
+  status_t st = yb_cuda_forward(c, input->data, B, H, W, dst, max_det, stage_dump ? stage_to_file : nullptr,
+                                stage_dump, profile ? ms : nullptr);
+  if (st != SUCCESS) return st;
+  if (rs != 6) {
+    for (int b = 0; b < B; ++b)
+      for (int t = 0; t < max_det; ++t)
+        for (int u = 0; u < 6; ++u)
+          output->data[(static_cast<size_t>(b) * max_det + t) * rs + u] = tmp[(static_cast<size_t>(b) * max_det + t) * 6 + u];
+  }
+  tensor_t* b23 = m->buffers && m->num_buffers > 23 ? &m->buffers[23] : nullptr;
+  if (b23 && b23->data && b23->dims[1] == max_det && b23->dims[2] * b23->dims[3] == rs)
+    std::memcpy(b23->data, output->data, static_cast<size_t>(max_det) * rs * 4);
+  if (profile) {
+    for (int i = 0; i < MODEL_FORWARD_PROFILE_STEPS; ++i) {
+      profile->ms_sum[i] += ms[i];
+      profile->ms_last[i] = ms[i];
+    }
+    profile->runs++;
+  }
+  return SUCCESS;
+}
+
+extern "C" status_t model_forward(model_t* m, const tensor_t* input, tensor_t* output) {
+  return model_forward_ex(m, input, output, nullptr, nullptr);
+}
+
+extern "C" status_t model_forward_batch(model_t* m, const tensor_t* input, tensor_t* output) {
+  return model_forward_ex(m, input, output, nullptr, nullptr);
+}
+
+extern "C" status_t detect_forward_one2one(model_t* m, int detect_module_idx, const tensor_t* p3, const tensor_t* p4,
+                                           const tensor_t* p5, tensor_t* out) {
+  if (!m || !p3 || !p4 || !p5 || !out || !out->data) return ERROR_NULL_POINTER;
+  if (detect_module_idx != YOLO26_DETECT_IDX) {
+    set_error("the device graph wires the Detect head at model.23");
+    return ERROR_NOT_IMPLEMENTED;
+  }
+  Ctx* c = model_ctx(m);
+  if (!c) return ERROR_FILE_NOT_FOUND;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  const int H = p3->dims[2] * 8, W = p3->dims[3] * 8;
+  const int max_det = out->dims[1];
+  if (out->dims[0] != 1 || out->dims[2] < 6 || out->dims[3] < 1) return ERROR_INVALID_DIMS;
+  Plan* p = nullptr;
+  if ((st = plan_for(c, 1, H, W, max_det, &p)) != SUCCESS) return st;
+  const tensor_t* f[3] = {p3, p4, p5};
+  const Buf* dst[3] = {&p->stage[16], &p->stage[19], &p->stage[22]};
+  cudaStream_t s = c->eng->stream();
+  DevMem tmp;
+  size_t maxe = 0;
+  for (int i = 0; i < 3; ++i) {
+    if (f[i]->dims[1] != dst[i]->C || f[i]->dims[2] != dst[i]->H || f[i]->dims[3] != dst[i]->W) return ERROR_INVALID_DIMS;
+    maxe = std::max(maxe, static_cast<size_t>(dst[i]->C) * dst[i]->H * dst[i]->W);
+  }
+  cudaError_t e = tmp.alloc(maxe * 4);
+  for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
+    const size_t n = static_cast<size_t>(dst[i]->C) * dst[i]->H * dst[i]->W;
+    e = cudaMemcpyAsync(tmp.p, f[i]->data, n * 4, cudaMemcpyHostToDevice, s);
+    OView o;
+    o.ptr = dst[i]->ptr;
+    o.bstride = dst[i]->bstride;
+    o.cstride = dst[i]->C;
+    if (e == cudaSuccess) e = launch_nchw_to_nhwc(tmp.f(), 1, dst[i]->C, dst[i]->H, dst[i]->W, o, s);
+  }
+  for (const Op& op : p->ops)
+    if (e == cudaSuccess && op.step == 23) e = op.run(s);
+  std::vector<float> rows(static_cast<size_t>(max_det) * 6);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(rows.data(), p->d_out, rows.size() * 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e, "detect head");
+  if ((st = check_kernel_flag(c)) != SUCCESS) return st;
+  c->last = p;
+  const int rs = out->dims[2] * out->dims[3];
+  for (int t = 0; t < max_det; ++t)
+    for (int u = 0; u < 6; ++u) out->data[static_cast<size_t>(t) * rs + u] = rows[static_cast<size_t>(t) * 6 + u];
+  return SUCCESS;
+}

@@ -1,0 +1,172 @@
+// Host-visible descriptions of the device kernels of the YOLO26 sm_100a path
+// and their launchers.  All activations are NHWC float32 in HBM; a tensor is
+// addressed through a view {ptr, bstride, cstride, coff}: element (b, pixel p,
+// channel c) lives at ptr[b*bstride + p*cstride + coff + c].  Views let a
+// kernel read or write a channel slice of a larger buffer, which is how every
+// concat of the reference (layers.c:145-153, :185-186, :251-254, :493,
+// model.c:547-550, :657-660) is folded away: producers write straight into
+// their slice and consumers read the whole buffer.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace yb {
+
+struct TView {
+  const float* ptr = nullptr;
+  long long bstride = 0;  // elements between images
+  int cstride = 0;        // elements between pixels
+  int coff = 0;           // first channel of the slice
+};
+
+struct OView {
+  float* ptr = nullptr;
+  long long bstride = 0;
+  int cstride = 0;
+  int coff = 0;
+};
+
+enum Act : int { kActNone = 0, kActSiLU = 1 };
+
+// Implicit-GEMM convolution on tcgen05: M = B*Ho*Wo output pixels, N = Co,
+// K = kh*kw*Ci ordered (ky, kx, ci).  Input channels [0, c_split) come from
+// src0 and [c_split, Ci) from src1; a source with lg_up = 1 is a nearest x2
+// upsample of a map half the logical size (the reference's upsample+concat,
+// layers.c:23-39 and :219-228, read in place).  Epilogue: + bias, optional
+// SiLU, optional + residual (after the activation, as in layers.c:103-106,
+// :259-263, :422-450), store into `out`.
+struct ConvArgs {
+  int B = 0, H = 0, W = 0;  // logical input size (after upsampling)
+  int Ci = 0, Co = 0;
+  int kh = 1, kw = 1, stride = 1, pad = 0;
+  int Ho = 0, Wo = 0;
+  int K = 0, num_kc = 0;  // K = kh*kw*Ci, num_kc = ceil(K / 64)
+  int n_tile = 0, n_tiles = 0, m_tiles = 0;
+  int c_split = 0;
+  TView src0, src1;
+  int lg_up0 = 0, lg_up1 = 0;
+  const uint8_t* wpack = nullptr;  // packed split-bf16 weights (see pack_conv_weights)
+  const float* bias = nullptr;     // [Co] or null
+  int act = kActNone;
+  OView out;
+  TView res;  // res.ptr == nullptr: no residual
+  int* err = nullptr;
+};
+
+// Bytes of one packed weight chunk: hi and lo planes of n_tile rows x 128 B.
+inline size_t conv_chunk_bytes(int n_tile) { return static_cast<size_t>(n_tile) * 256; }
+
+// Packs w[co][ci][kh][kw] (fp32) into the tcgen05 operand image used by the
+// convolution kernel: for each N tile and each 64-wide K chunk, the hi plane
+// (bf16 round-to-nearest of w) then the lo plane (bf16 of w - hi), each as
+// n_tile rows of 128 bytes in the 128B-swizzled K-major layout.  Rows past Co
+// and K past kh*kw*ci are zero.  Returns the byte size; dst may be null to
+// query it.
+size_t pack_conv_weights(const float* w, int co, int ci, int kh, int kw, int n_tile, uint8_t* dst);
+
+// Chooses n_tile (multiple of 16, <= 256) and n_tiles for Co output channels.
+void choose_n_tiling(int co, int* n_tile, int* n_tiles);
+
+cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms);
+// Must run once per device before the first launch_conv_tc (not under capture).
+cudaError_t init_conv_kernel_attributes();
+
+// ---------------------------------------------------------------- SIMT kernels
+// First convolution, reading the NCHW host-layout input directly:
+// 3x3 stride 2 pad 1, Ci <= 4, Co <= 64, + bias + SiLU, NHWC output.
+struct StemArgs {
+  const float* in = nullptr;  // [B, Ci, H, W]
+  int B = 0, Ci = 0, H = 0, W = 0, Co = 0, Ho = 0, Wo = 0, stride = 2, pad = 1, k = 3;
+  const float* w = nullptr;   // device copy of [Co][Ci][k][k]
+  const float* bias = nullptr;
+  int act = kActSiLU;
+  OView out;
+};
+cudaError_t launch_stem(const StemArgs& a, cudaStream_t s);
+
+// Depthwise 3x3, pad 1, + bias, optional SiLU (layers.c:269-290 plus
+// detect.c:219-228).  w: device [C][9].
+struct DwArgs {
+  TView in;
+  int B = 0, H = 0, W = 0, C = 0;
+  const float* w = nullptr;
+  const float* bias = nullptr;
+  int act = kActNone;
+  OView out;
+};
+cudaError_t launch_dwconv3x3(const DwArgs& a, cudaStream_t s);
+
+// Max pool with padding k/2 excluded from the max (layers.c:191-217).
+// Output size Ho x Wo (0 = same as the input, for stride 1).
+struct PoolArgs {
+  TView in;
+  int B = 0, H = 0, W = 0, C = 0, k = 5, stride = 1, Ho = 0, Wo = 0;
+  OView out;
+};
+cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s);
+
+// Multi-head attention of the PSA block (layers.c:310-405): per head h the
+// qkv channels [h*(2kd+hd), +kd) are q, the next kd are k, the next hd are v;
+// S = q.k * kd^-0.5, row softmax, out = P.v; then + depthwise 3x3 of v
+// (pe conv, weight [heads*hd][9] + bias).  out channels h*hd + d.
+struct AttnArgs {
+  TView qkv;
+  int B = 0, H = 0, W = 0, heads = 0, kd = 0, hd = 0;
+  float scale = 1.f;
+  const float* pe_w = nullptr;
+  const float* pe_b = nullptr;
+  OView out;
+};
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+
+// Detect decode (detect.c:21-61, :407-418): from box distances dist
+// [B, N, 4] (l, t, r, b in grid units) and class logits [B, N, nc], write
+// xyxy pixel boxes [B, N, 4] and the per-anchor maximum class score
+// max_c sigmoid(logit) [B, N].  Scales: anchors [0, n0) stride s0, ... .
+struct DecodeArgs {
+  const float* dist = nullptr;
+  const float* logits = nullptr;
+  float* boxes = nullptr;
+  float* maxscore = nullptr;
+  int B = 0, N = 0, nc = 0;
+  int nscales = 0;
+  int base[4] = {0, 0, 0, 0};
+  int w[4] = {0, 0, 0, 0};
+  int stride[4] = {0, 0, 0, 0};
+};
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s);
+
+// Two-stage top-k of detect_postprocess_from_pred (detect.c:63-166), one CTA
+// per image, total order (score desc, index asc) in both stages; writes
+// dets [B, cap, 6] (rows >= k zero-filled).
+// Class values are read as scores[b*s_bstride + anchor*s_rstride + c]
+// (sigmoid applied first when apply_sigmoid), boxes as
+// boxes[b*b_bstride + anchor*b_rstride + 0..3].  maxscore (nullable) holds
+// the per-anchor maximum class score; when null it is recomputed.
+struct TopkArgs {
+  const float* maxscore = nullptr;
+  const float* scores = nullptr;
+  long long s_bstride = 0;
+  int s_rstride = 0;
+  int apply_sigmoid = 1;
+  const float* boxes = nullptr;
+  long long b_bstride = 0;
+  int b_rstride = 4;
+  float* dets = nullptr;  // [B, cap, 6]
+  int B = 0, N = 0, nc = 0, max_det = 300, cap = 300;
+};
+cudaError_t launch_topk(const TopkArgs& a, cudaStream_t s);
+// Largest k supported by the top-k kernel.
+constexpr int kTopkMax = 1024;
+
+// Layout conversions for the host API and stage dumps.
+cudaError_t launch_nchw_to_nhwc(const float* in, int B, int C, int H, int W, OView out, cudaStream_t s);
+cudaError_t launch_nhwc_to_nchw(TView in, int B, int C, int H, int W, float* out, cudaStream_t s);
+// out[B,H,W,c0+c1] = nearest-upsample(src0 by the integer factor up0) ++ src1
+// along channels (stage dumps and the layer-level API).
+cudaError_t launch_gather_concat(TView src0, int c0, int up0, TView src1, int c1, int B, int H, int W, OView out,
+                                 cudaStream_t s);
+// In-place SiLU on an NHWC view.
+cudaError_t launch_silu(OView t, int B, int HW, int C, cudaStream_t s);
+
+}  // namespace yb

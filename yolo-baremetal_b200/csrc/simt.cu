@@ -1,0 +1,418 @@
+// CUDA-core kernels of the YOLO26 path: the ops that are not contractions
+// (depthwise, pooling, decode, layout) or too small to tile (the 3-channel stem
+// convolution), plus the PSA attention.  All are HBM- or latency-bound; they
+// read and write NHWC fp32 through channel-slice views (kernels.h) with
+// 16-byte vector accesses.  Summation orders follow the reference loops so
+// that results stay within a few ulps of it.
+#include <cfloat>
+#include "kernels.h"
+
+namespace yb {
+namespace {
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+inline int blocks_for(long long n, int t) { return static_cast<int>((n + t - 1) / t); }
+
+// ------------------------------------------------------------------ stem conv
+// Reference loop order (layers.c:60-79): sum = bias; for ci, ky, kx: sum += x*w,
+// without contraction to FMA, as the reference is compiled.
+template <int CO>
+__global__ void stem_kernel(const StemArgs a) {
+  __shared__ float sw[CO * 4 * 9];
+  __shared__ float sb[CO];
+  const int wn = CO * a.Ci * a.k * a.k;
+  for (int i = threadIdx.x; i < wn; i += blockDim.x) sw[i] = a.w[i];
+  for (int i = threadIdx.x; i < CO; i += blockDim.x) sb[i] = a.bias ? a.bias[i] : 0.f;
+  __syncthreads();
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(a.B) * a.Ho * a.Wo;
+  if (idx >= total) return;
+  const int b = static_cast<int>(idx / (a.Ho * a.Wo));
+  const int r = static_cast<int>(idx - static_cast<long long>(b) * a.Ho * a.Wo);
+  const int oy = r / a.Wo, ox = r - (r / a.Wo) * a.Wo;
+  float acc[CO];
+#pragma unroll
+  for (int c = 0; c < CO; ++c) acc[c] = sb[c];
+  const long long plane = static_cast<long long>(a.H) * a.W;
+  const float* inb = a.in + static_cast<long long>(b) * a.Ci * plane;
+  for (int ci = 0; ci < a.Ci; ++ci) {
+    for (int ky = 0; ky < a.k; ++ky) {
+      const int iy = oy * a.stride - a.pad + ky;
+      for (int kx = 0; kx < a.k; ++kx) {
+        const int ix = ox * a.stride - a.pad + kx;
+        if (iy < 0 || iy >= a.H || ix < 0 || ix >= a.W) continue;
+        const float x = __ldg(inb + ci * plane + static_cast<long long>(iy) * a.W + ix);
+        const int wo = (ci * a.k + ky) * a.k + kx;
+        const int wstride = a.Ci * a.k * a.k;
+#pragma unroll
+        for (int c = 0; c < CO; ++c) acc[c] = __fadd_rn(acc[c], __fmul_rn(x, sw[c * wstride + wo]));
+      }
+    }
+  }
+  float* o = a.out.ptr + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(r) * a.out.cstride +
+             a.out.coff;
+#pragma unroll
+  for (int c = 0; c < CO; c += 4) {
+    float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+    if (a.act == kActSiLU) {
+      v.x = silu(v.x);
+      v.y = silu(v.y);
+      v.z = silu(v.z);
+      v.w = silu(v.w);
+    }
+    *reinterpret_cast<float4*>(o + c) = v;
+  }
+}
+
+// ------------------------------------------------------------- depthwise 3x3
+// w is [9][C] (tap-major, transposed on the host) for 16-byte loads.
+__global__ void dw3x3_kernel(const DwArgs a) {
+  const int C4 = a.C >> 2;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(a.B) * a.H * a.W * C4;
+  if (idx >= total) return;
+  const int c = static_cast<int>(idx % C4) * 4;
+  const long long pix = idx / C4;
+  const int b = static_cast<int>(pix / (a.H * a.W));
+  const int p = static_cast<int>(pix - static_cast<long long>(b) * a.H * a.W);
+  const int y = p / a.W, x = p - (p / a.W) * a.W;
+  float4 s = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* base = a.in.ptr + static_cast<long long>(b) * a.in.bstride + a.in.coff + c;
+#pragma unroll
+  for (int ky = 0; ky < 3; ++ky) {
+    const int iy = y - 1 + ky;
+    if (iy < 0 || iy >= a.H) continue;
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx) {
+      const int ix = x - 1 + kx;
+      if (ix < 0 || ix >= a.W) continue;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(iy * a.W + ix) * a.in.cstride));
+      const float4 w = __ldg(reinterpret_cast<const float4*>(a.w + (ky * 3 + kx) * a.C + c));
+      s.x = __fadd_rn(s.x, __fmul_rn(v.x, w.x));
+      s.y = __fadd_rn(s.y, __fmul_rn(v.y, w.y));
+      s.z = __fadd_rn(s.z, __fmul_rn(v.z, w.z));
+      s.w = __fadd_rn(s.w, __fmul_rn(v.w, w.w));
+    }
+  }
+  if (a.act == kActSiLU) {
+    s.x = silu(s.x);
+    s.y = silu(s.y);
+    s.z = silu(s.z);
+    s.w = silu(s.w);
+  }
+  float* o = a.out.ptr + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(p) * a.out.cstride +
+             a.out.coff + c;
+  *reinterpret_cast<float4*>(o) = s;
+}
+
+// ------------------------------------------------------------------ max pool
+__global__ void maxpool_kernel(const PoolArgs a) {
+  const int C4 = a.C >> 2;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(a.B) * a.Ho * a.Wo * C4;
+  if (idx >= total) return;
+  const int c = static_cast<int>(idx % C4) * 4;
+  const long long pix = idx / C4;
+  const int b = static_cast<int>(pix / (a.Ho * a.Wo));
+  const int p = static_cast<int>(pix - static_cast<long long>(b) * a.Ho * a.Wo);
+  const int y = (p / a.Wo) * a.stride, x = (p - (p / a.Wo) * a.Wo) * a.stride;
+  const int pad = a.k / 2;
+  float4 m = make_float4(-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX);
+  const float* base = a.in.ptr + static_cast<long long>(b) * a.in.bstride + a.in.coff + c;
+  for (int ky = 0; ky < a.k; ++ky) {
+    const int iy = y - pad + ky;
+    if (iy < 0 || iy >= a.H) continue;
+    for (int kx = 0; kx < a.k; ++kx) {
+      const int ix = x - pad + kx;
+      if (ix < 0 || ix >= a.W) continue;
+      const float4 v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(iy * a.W + ix) * a.in.cstride));
+      if (v.x > m.x) m.x = v.x;
+      if (v.y > m.y) m.y = v.y;
+      if (v.z > m.z) m.z = v.z;
+      if (v.w > m.w) m.w = v.w;
+    }
+  }
+  float* o = a.out.ptr + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(p) * a.out.cstride +
+             a.out.coff + c;
+  *reinterpret_cast<float4*>(o) = m;
+}
+
+// ----------------------------------------------------------------- attention
+// One thread per query token, QB queries per CTA, keys streamed through shared
+// memory in tiles of KB.  Two passes over the keys: the row maximum, then
+// exp(s - max) weights with their sum and the weighted sum of v, mirroring the
+// reference's materialised softmax (layers.c:292-308, :352-371) without the
+// N x N matrix.  The epilogue adds the depthwise 3x3 positional conv of v
+// (layers.c:373-395) and writes head h's hd channels.
+template <int KD, int HD, int QB, int KB>
+__global__ void __launch_bounds__(QB) attention_kernel(const AttnArgs a) {
+  __shared__ float sk[KB][KD];
+  __shared__ float sv[KB][HD];
+  const int N = a.H * a.W;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int qi = blockIdx.x * QB + threadIdx.x;
+  const bool active = qi < N;
+  const int blk = 2 * KD + HD;
+  const float* base = a.qkv.ptr + static_cast<long long>(b) * a.qkv.bstride + a.qkv.coff + h * blk;
+  float q[KD];
+  if (active) {
+    const float* qp = base + static_cast<long long>(qi) * a.qkv.cstride;
+#pragma unroll
+    for (int d = 0; d < KD; d += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(qp + d));
+      q[d] = v.x;
+      q[d + 1] = v.y;
+      q[d + 2] = v.z;
+      q[d + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int d = 0; d < KD; ++d) q[d] = 0.f;
+  }
+  // Pass 1: row maximum of the scaled logits.
+  float mx = -FLT_MAX;
+  for (int k0 = 0; k0 < N; k0 += KB) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < KB * (KD / 4); i += QB) {
+      const int kk = i / (KD / 4), d4 = (i - kk * (KD / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + kk < N) v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + KD + d4));
+      *reinterpret_cast<float4*>(&sk[kk][d4]) = v;
+    }
+    __syncthreads();
+    const int kn = min(KB, N - k0);
+    for (int kk = 0; kk < kn; ++kk) {
+      float s = 0.f;
+#pragma unroll
+      for (int d = 0; d < KD; ++d) s = __fadd_rn(s, __fmul_rn(q[d], sk[kk][d]));
+      mx = fmaxf(mx, __fmul_rn(s, a.scale));
+    }
+  }
+  // Pass 2: weights, their sum and the weighted sum of v.
+  float o[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) o[d] = 0.f;
+  float sum = 0.f;
+  for (int k0 = 0; k0 < N; k0 += KB) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < KB * (KD / 4); i += QB) {
+      const int kk = i / (KD / 4), d4 = (i - kk * (KD / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + kk < N) v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + KD + d4));
+      *reinterpret_cast<float4*>(&sk[kk][d4]) = v;
+    }
+    for (int i = threadIdx.x; i < KB * (HD / 4); i += QB) {
+      const int kk = i / (HD / 4), d4 = (i - kk * (HD / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + kk < N) v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + 2 * KD + d4));
+      *reinterpret_cast<float4*>(&sv[kk][d4]) = v;
+    }
+    __syncthreads();
+    const int kn = min(KB, N - k0);
+    for (int kk = 0; kk < kn; ++kk) {
+      float s = 0.f;
+#pragma unroll
+      for (int d = 0; d < KD; ++d) s = __fadd_rn(s, __fmul_rn(q[d], sk[kk][d]));
+      const float e = expf(__fsub_rn(__fmul_rn(s, a.scale), mx));
+      sum += e;
+#pragma unroll
+      for (int d = 0; d < HD; ++d) o[d] = fmaf(e, sv[kk][d], o[d]);
+    }
+  }
+  if (!active) return;
+  const float inv = sum > 1e-12f ? 1.0f / sum : 1.0f;
+  // Positional term: depthwise 3x3 of v around the query pixel, + pe bias.
+  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
+  float* op = a.out.ptr + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(qi) * a.out.cstride +
+              a.out.coff + h * HD;
+#pragma unroll
+  for (int d0 = 0; d0 < HD; d0 += 4) {
+    const int ch = h * HD + d0;
+    float4 pe = __ldg(reinterpret_cast<const float4*>(a.pe_b + ch));
+    for (int ky = 0; ky < 3; ++ky) {
+      const int iy = y - 1 + ky;
+      if (iy < 0 || iy >= a.H) continue;
+      for (int kx = 0; kx < 3; ++kx) {
+        const int ix = x - 1 + kx;
+        if (ix < 0 || ix >= a.W) continue;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * KD + d0));
+        const float4 w = __ldg(reinterpret_cast<const float4*>(a.pe_w + (ky * 3 + kx) * (a.heads * HD) + ch));
+        pe.x = __fadd_rn(pe.x, __fmul_rn(v.x, w.x));
+        pe.y = __fadd_rn(pe.y, __fmul_rn(v.y, w.y));
+        pe.z = __fadd_rn(pe.z, __fmul_rn(v.z, w.z));
+        pe.w = __fadd_rn(pe.w, __fmul_rn(v.w, w.w));
+      }
+    }
+    float4 r;
+    r.x = o[d0] * inv + pe.x;
+    r.y = o[d0 + 1] * inv + pe.y;
+    r.z = o[d0 + 2] * inv + pe.z;
+    r.w = o[d0 + 3] * inv + pe.w;
+    *reinterpret_cast<float4*>(op + d0) = r;
+  }
+}
+
+// -------------------------------------------------------------------- decode
+__global__ void decode_kernel(const DecodeArgs a) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(a.B) * a.N;
+  if (idx >= total) return;
+  const int j = static_cast<int>(idx % a.N);
+  int s = 0;
+  while (s + 1 < a.nscales && j >= a.base[s + 1]) ++s;
+  const int local = j - a.base[s];
+  const int gy = local / a.w[s], gx = local - (local / a.w[s]) * a.w[s];
+  const float ax = static_cast<float>(gx) + 0.5f;
+  const float ay = static_cast<float>(gy) + 0.5f;
+  const float st = static_cast<float>(a.stride[s]);
+  const float4 d = __ldg(reinterpret_cast<const float4*>(a.dist + idx * 4));
+  float4 bx;
+  bx.x = __fmul_rn(__fsub_rn(ax, d.x), st);
+  bx.y = __fmul_rn(__fsub_rn(ay, d.y), st);
+  bx.z = __fmul_rn(__fadd_rn(ax, d.z), st);
+  bx.w = __fmul_rn(__fadd_rn(ay, d.w), st);
+  *reinterpret_cast<float4*>(a.boxes + idx * 4) = bx;
+  const float* lg = a.logits + idx * a.nc;
+  float m = -FLT_MAX;
+  for (int c = 0; c < a.nc; ++c) {
+    const float v = sigmoid(__ldg(lg + c));
+    if (v > m) m = v;
+  }
+  a.maxscore[idx] = m;
+}
+
+// -------------------------------------------------------------------- layout
+__global__ void nchw_to_nhwc_kernel(const float* in, int B, int C, int H, int W, OView out) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(B) * C * H * W;
+  if (idx >= total) return;
+  const long long hw = static_cast<long long>(H) * W;
+  const int c = static_cast<int>(idx % C);
+  const long long pix = idx / C;
+  const int b = static_cast<int>(pix / hw);
+  const long long p = pix - b * hw;
+  out.ptr[b * out.bstride + p * out.cstride + out.coff + c] = in[(static_cast<long long>(b) * C + c) * hw + p];
+}
+
+__global__ void nhwc_to_nchw_kernel(TView in, int B, int C, int H, int W, float* out) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(B) * C * H * W;
+  if (idx >= total) return;
+  const long long hw = static_cast<long long>(H) * W;
+  const long long p = idx % hw;
+  const long long bc = idx / hw;
+  const int c = static_cast<int>(bc % C);
+  const int b = static_cast<int>(bc / C);
+  out[idx] = in.ptr[b * in.bstride + p * in.cstride + in.coff + c];
+}
+
+__global__ void gather_concat_kernel(TView s0, int c0, int up0, TView s1, int c1, int B, int H, int W, OView out) {
+  const int C = c0 + c1;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(B) * H * W * C;
+  if (idx >= total) return;
+  const int c = static_cast<int>(idx % C);
+  const long long pix = idx / C;
+  const int b = static_cast<int>(pix / (static_cast<long long>(H) * W));
+  const int p = static_cast<int>(pix - static_cast<long long>(b) * H * W);
+  const int y = p / W, x = p - (p / W) * W;
+  float v;
+  if (c < c0) {
+    const int w0 = W / up0;
+    v = s0.ptr[b * s0.bstride + static_cast<long long>((y / up0) * w0 + (x / up0)) * s0.cstride + s0.coff + c];
+  } else {
+    v = s1.ptr[b * s1.bstride + static_cast<long long>(p) * s1.cstride + s1.coff + (c - c0)];
+  }
+  out.ptr[b * out.bstride + static_cast<long long>(p) * out.cstride + out.coff + c] = v;
+}
+
+__global__ void silu_kernel(OView t, int B, int HW, int C) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(B) * HW * C;
+  if (idx >= total) return;
+  const int c = static_cast<int>(idx % C);
+  const long long pix = idx / C;
+  const int b = static_cast<int>(pix / HW);
+  const long long p = pix - static_cast<long long>(b) * HW;
+  float* q = t.ptr + b * t.bstride + p * t.cstride + t.coff + c;
+  *q = silu(*q);
+}
+
+}  // namespace
+
+cudaError_t launch_stem(const StemArgs& a, cudaStream_t s) {
+  if (a.Ci > 4 || a.k != 3 || (a.Co != 16 && a.Co != 32 && a.Co != 64)) return cudaErrorInvalidValue;
+  const long long total = static_cast<long long>(a.B) * a.Ho * a.Wo;
+  const int t = 128;
+  if (a.Co == 16) stem_kernel<16><<<blocks_for(total, t), t, 0, s>>>(a);
+  else if (a.Co == 32) stem_kernel<32><<<blocks_for(total, t), t, 0, s>>>(a);
+  else stem_kernel<64><<<blocks_for(total, t), t, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dwconv3x3(const DwArgs& a, cudaStream_t s) {
+  if (a.C % 4) return cudaErrorInvalidValue;
+  const long long total = static_cast<long long>(a.B) * a.H * a.W * (a.C / 4);
+  dw3x3_kernel<<<blocks_for(total, 256), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {
+  if (a.C % 4) return cudaErrorInvalidValue;
+  const long long total = static_cast<long long>(a.B) * a.H * a.W * (a.C / 4);
+  PoolArgs b = a;
+  if (b.Ho <= 0 || b.Wo <= 0) {
+    b.Ho = a.H;
+    b.Wo = a.W;
+  }
+  if (b.stride < 1) return cudaErrorInvalidValue;
+  const long long total_out = static_cast<long long>(b.B) * b.Ho * b.Wo * (b.C / 4);
+  (void)total;
+  maxpool_kernel<<<blocks_for(total_out, 256), 256, 0, s>>>(b);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
+  if (a.kd != 32 || a.hd != 64) return cudaErrorInvalidValue;
+  constexpr int QB = 128, KB = 64;
+  const int N = a.H * a.W;
+  dim3 grid((N + QB - 1) / QB, a.heads, a.B);
+  attention_kernel<32, 64, QB, KB><<<grid, QB, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
+  const long long total = static_cast<long long>(a.B) * a.N;
+  decode_kernel<<<blocks_for(total, 256), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nchw_to_nhwc(const float* in, int B, int C, int H, int W, OView out, cudaStream_t s) {
+  const long long total = static_cast<long long>(B) * C * H * W;
+  nchw_to_nhwc_kernel<<<blocks_for(total, 256), 256, 0, s>>>(in, B, C, H, W, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nhwc_to_nchw(TView in, int B, int C, int H, int W, float* out, cudaStream_t s) {
+  const long long total = static_cast<long long>(B) * C * H * W;
+  nhwc_to_nchw_kernel<<<blocks_for(total, 256), 256, 0, s>>>(in, B, C, H, W, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_concat(TView src0, int c0, int up0, TView src1, int c1, int B, int H, int W, OView out,
+                                 cudaStream_t s) {
+  const long long total = static_cast<long long>(B) * H * W * (c0 + c1);
+  gather_concat_kernel<<<blocks_for(total, 256), 256, 0, s>>>(src0, c0, up0, src1, c1, B, H, W, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu(OView t, int B, int HW, int C, cudaStream_t s) {
+  const long long total = static_cast<long long>(B) * HW * C;
+  silu_kernel<<<blocks_for(total, 256), 256, 0, s>>>(t, B, HW, C);
+  return cudaGetLastError();
+}
+
+}  // namespace yb
