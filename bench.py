@@ -287,7 +287,9 @@ def run_ours(args):
 
     e2e_step()  # builds the plan and leaves this rank's images resident in HBM
     d_in, d_out = model.plan_io(B, H, H)
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: the library launches on exactly this stream, so the
+    # CUDA events below bracket the forward's kernels.
+    stream = torch.cuda.Stream()
 
     def dev_step():
         model.forward_device(d_in, d_out, B, H, H, 300, stream.cuda_stream)

@@ -5,16 +5,22 @@ accumulation):
   * stage tensors: max |gpu - oracle| <= STAGE_RTOL * max(1, max |oracle|);
   * pre-sigmoid class logits: max |gpu - oracle| <= LOGIT_ATOL (the stated
     target of the task: 1e-2);
-  * detections: identical (anchor, class) rows in identical order wherever the
-    oracle's scores are separated by more than SCORE_GAP from their neighbours,
-    box IoU >= 0.99 and |score diff| <= SCORE_ATOL for every matched row.
+  * detections: rows matched one to one (same class, |score diff| <=
+    SCORE_ATOL, box corners within BOX_RTOL of the box's magnitude); every
+    unmatched row must sit at the top-k selection boundary (score within
+    SCORE_ATOL of the k-th score); matched rows keep the oracle's order except
+    among scores within SCORE_ATOL; IoU >= 0.99 on every matched well-formed
+    box (both sides >= WELL_FORMED pixels; random-init heads also emit
+    degenerate boxes with x2 < x1 or near-zero extent, where IoU is
+    ill-conditioned and the corner tolerance is the check).
 """
 import numpy as np
 
 STAGE_RTOL = 2e-3
 LOGIT_ATOL = 1e-2
 SCORE_ATOL = 1e-4
-SCORE_GAP = 2e-4
+BOX_RTOL = 1e-3
+WELL_FORMED = 4.0
 
 
 def rel_err(a, b) -> float:
@@ -36,18 +42,56 @@ def iou(a, b) -> np.ndarray:
     return np.where(union > 0, inter / np.maximum(union, 1e-12), 1.0)
 
 
-def compare_dets(gpu: np.ndarray, ref: np.ndarray):
-    """Returns (n_checked, n_mismatch, min_iou, max_score_diff) over rows whose
-    oracle score is separated from both neighbours by more than SCORE_GAP."""
-    s = ref[:, 4].astype(np.float64)
-    k = len(s)
-    sep = np.ones(k, dtype=bool)
-    if k > 1:
-        d = np.abs(np.diff(s))
-        sep[:-1] &= d > SCORE_GAP
-        sep[1:] &= d > SCORE_GAP
-    rows = np.nonzero(sep & (s > 0))[0]
-    mism = int(np.sum(gpu[rows, 5] != ref[rows, 5]))
-    ious = iou(gpu[rows, :4].astype(np.float64), ref[rows, :4].astype(np.float64)) if len(rows) else np.ones(1)
-    sdiff = float(np.max(np.abs(gpu[rows, 4] - ref[rows, 4]))) if len(rows) else 0.0
-    return len(rows), mism, float(np.min(ious)), sdiff
+def compare_dets(gpu: np.ndarray, ref: np.ndarray) -> dict:
+    """Matches detection rows one to one: same class, IoU >= 0.99 and score
+    within SCORE_ATOL (nearest score first).  Returns
+      identical: rows equal position by position (class, IoU >= 0.99, score tol)
+      matched:   rows matched anywhere in the list
+      unmatched_off_boundary: unmatched rows whose score is NOT within
+                 SCORE_ATOL of the list's last (k-th) score, i.e. not explained
+                 by a near-tie at the selection boundary
+      order_violations: matched pairs ordered differently with scores further
+                 apart than SCORE_ATOL
+      min_iou, max_score_diff over matched rows."""
+    k = int(np.sum(ref[:, 4] != 0)) if np.any(ref[:, 4] != 0) else 0
+    k = max(k, int(np.sum(gpu[:, 4] != 0)))
+    g = gpu[:k].astype(np.float64)
+    r = ref[:k].astype(np.float64)
+    used = np.zeros(k, dtype=bool)
+    match = -np.ones(k, dtype=int)
+    ious_m, sd_m = [], []
+    for i in range(k):
+        cand = np.nonzero((~used) & (r[:, 5] == g[i, 5]) & (np.abs(r[:, 4] - g[i, 4]) <= SCORE_ATOL))[0]
+        if len(cand) == 0:
+            continue
+        scale = np.maximum(1.0, np.max(np.abs(r[cand, :4]), axis=1))
+        close = np.max(np.abs(r[cand, :4] - g[i, :4]), axis=1) <= BOX_RTOL * scale
+        ok = cand[close]
+        if len(ok) == 0:
+            continue
+        j = ok[np.argmin(np.abs(ok - i))]
+        used[j] = True
+        match[i] = j
+        w, h = abs(r[j, 2] - r[j, 0]), abs(r[j, 3] - r[j, 1])
+        if w >= WELL_FORMED and h >= WELL_FORMED:
+            ious_m.append(float(iou(g[i : i + 1, :4], r[j : j + 1, :4])[0]))
+        sd_m.append(abs(g[i, 4] - r[j, 4]))
+    kth = min(r[k - 1, 4], g[k - 1, 4]) if k else 0.0
+    off = [i for i in range(k) if match[i] < 0 and g[i, 4] - kth > SCORE_ATOL]
+    off += [j for j in range(k) if not used[j] and r[j, 4] - kth > SCORE_ATOL]
+    viol = 0
+    mi = np.nonzero(match >= 0)[0]
+    for a in range(len(mi)):
+        for b in range(a + 1, min(len(mi), a + 64)):
+            i, j = mi[a], mi[b]
+            if match[i] > match[j] and abs(g[i, 4] - g[j, 4]) > SCORE_ATOL:
+                viol += 1
+    ident = int(np.sum(match[:k] == np.arange(k)))
+    return {"k": k, "identical": ident, "matched": int(np.sum(match >= 0)), "unmatched_off_boundary": len(off),
+            "order_violations": viol, "min_iou": min(ious_m) if ious_m else 1.0,
+            "max_score_diff": max(sd_m) if sd_m else 0.0}
+
+
+def dets_ok(c: dict) -> bool:
+    return c["unmatched_off_boundary"] == 0 and c["order_violations"] == 0 and c["min_iou"] >= 0.99 and \
+        c["max_score_diff"] <= SCORE_ATOL

@@ -5,7 +5,7 @@ detections."""
 import numpy as np
 import pytest
 
-from parity import LOGIT_ATOL, STAGE_RTOL, compare_dets, rel_err
+from parity import LOGIT_ATOL, STAGE_RTOL, compare_dets, dets_ok, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -46,9 +46,9 @@ def test_stages_logits_dets(model_n0, weights_n0, hw):
     lerr = float(np.max(np.abs(logits[0] - ref["logits"])))
     print(f"logits max abs err {lerr:.3e} (max |logit| {np.abs(ref['logits']).max():.1f}); worst stage {worst:.2e}")
     assert lerr <= LOGIT_ATOL
-    n, mism, miou, sdiff = compare_dets(got["dets"][0], ref["dets"])
-    print(f"dets: {n} separated rows, {mism} class mismatches, min IoU {miou:.4f}, max score diff {sdiff:.2e}")
-    assert mism == 0 and miou >= 0.99
+    c = compare_dets(got["dets"][0], ref["dets"])
+    print(f"dets: {c}")
+    assert dets_ok(c)
 
 
 def test_dets_non_saturating(weights_n0_soft):
@@ -61,9 +61,9 @@ def test_dets_non_saturating(weights_n0_soft):
     img = yw.make_input(7, 640, 640)
     got = m.forward(img)["dets"][0]
     ref = _oracle(weights_n0_soft).forward(img)["dets"]
-    n, mism, miou, sdiff = compare_dets(got, ref)
-    print(f"soft weights: {n} separated rows, {mism} mismatches, min IoU {miou:.5f}, max score diff {sdiff:.2e}")
-    assert n >= 250 and mism == 0 and miou >= 0.99 and sdiff <= 1e-4
+    c = compare_dets(got, ref)
+    print(f"soft weights dets: {c}")
+    assert c["k"] == 300 and dets_ok(c) and c["matched"] >= 290
     m.close()
 
 
