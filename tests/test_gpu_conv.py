@@ -61,6 +61,16 @@ def test_conv_edge_shapes(ci, co, k, stride, H):
     assert err <= _tol(ref, ci * k * k)
 
 
+@pytest.mark.parametrize("ci,co,k,stride,H", [(2, 3, 1, 1, 2), (16, 32, 3, 2, 64), (64, 64, 1, 1, 40)])
+def test_conv_repeat_deterministic(ci, co, k, stride, H):
+    """The device path has no atomics or races: repeated calls are bit-identical."""
+    first, ref = _run(ci, co, k, stride, H)
+    assert max_abs(first, ref) <= _tol(ref, ci * k * k)
+    for _ in range(15):
+        again, _ = _run(ci, co, k, stride, H)
+        assert np.array_equal(again, first)
+
+
 def test_conv_non_square():
     out, ref = _run(32, 48, 3, 1, 24, W=40)
     assert max_abs(out, ref) <= _tol(ref, 288)

@@ -6,32 +6,36 @@
 //
 // GEMM view: M = B*Ho*Wo output pixels (128 per tile), N = Co (one tile of up
 // to 256 channels, so the activation tile is read once), K = kh*kw*Ci ordered
-// (ky, kx, ci) and cut in 64-wide chunks.  FP32 semantics are kept by splitting
-// both operands into bf16 pairs x = hi + lo (hi = bf16(x), lo = bf16(x - hi),
-// 16 significant bits together) and accumulating hi*hi + hi*lo + lo*hi in fp32
-// in tensor memory: three kind::f16 UMMAs per 16-wide K step.
+// (ky, kx, ci) and cut in 64-wide chunks.  FP32 semantics come from split
+// operands: activations are stored as bf16 hi/lo planes (kernels.h) and the
+// weights are packed the same way, and each 16-wide K step issues three
+// kind::f16 UMMAs, hi*hi + hi*lo + lo*hi, accumulating in fp32 in tensor
+// memory.
 //
 // Persistent, warp-specialised CTA (288 threads, one CTA per SM):
-//   warps 0-3  producers: gather the im2col rows of the activation tile
-//              straight from NHWC fp32 (zero padding, upsample and two-source
-//              concat handled in the address computation), split to hi/lo
-//              bf16 and store them in the 128B-swizzled K-major layout; thread
-//              0 also starts one bulk copy (TMA engine) of the pre-packed,
-//              pre-swizzled weight chunk.
+//   warps 0-3  producers: each K chunk of the activation tile is gathered with
+//              16-byte cp.async copies straight from the hi and lo planes into
+//              the 128B-swizzled K-major operand layout (zero fill for padding
+//              and K tails; upsample and two-source concat in the address
+//              computation), kept PD chunks deep, then published on the
+//              stage's mbarrier.  Thread 0 also starts one bulk copy (TMA
+//              engine) of the pre-packed, pre-swizzled weight chunk.
 //   warp 8     allocates tensor memory (two accumulators) and, from one lane,
 //              issues the UMMAs; tcgen05.commit frees each smem stage and
 //              publishes each finished accumulator.
 //   warps 4-7  epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 output
-//              pixels), + bias, SiLU, + residual, fp32 NHWC store into the
-//              destination channel slice.  Runs while warp 8 accumulates the
-//              next tile into the other TMEM buffer.
+//              pixels), + bias, SiLU, + residual, split (or fp32) NHWC store
+//              into the destination channel slice.  Runs while warp 8
+//              accumulates the next tile into the other TMEM buffer.
 // All barrier waits are bounded (sm100.cuh); a timeout sets *a.err, aborts
-// the other roles, drains outstanding UMMAs and frees tensor memory.
+// the other roles, drains outstanding copies and UMMAs and frees tensor
+// memory.
 #include <cstdio>
 #include <cstring>
 #include <vector>
 #include "kernels.h"
 #include "sm100.cuh"
+#include "split.cuh"
 
 namespace yb {
 namespace {
@@ -39,34 +43,26 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kProducerWarps = 4;
-constexpr int kEpilogueWarps = 4;
+constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, splitting the columns
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr uint32_t kAPlaneBytes = kBM * 128;  // one 128 x 64 bf16 plane
 constexpr int kSmemLimit = 232448;            // 227 KB opt-in per CTA
-constexpr int kSmemExtra = 1024 + 512 + kBM * 16;
-
-__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) {
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// x = hi + lo with hi = bf16_rn(x), lo = bf16_rn(x - hi); x - hi is exact.
-__device__ __forceinline__ void split4(const float4& v, uint2& hi, uint2& lo) {
-  const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y);
-  const __nv_bfloat162 h23 = __floats2bfloat162_rn(v.z, v.w);
-  const float2 f01 = __bfloat1622float2(h01);
-  const float2 f23 = __bfloat1622float2(h23);
-  const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
-  const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
-  hi = make_uint2(bf16x2_bits(h01), bf16x2_bits(h23));
-  lo = make_uint2(bf16x2_bits(l01), bf16x2_bits(l23));
-}
-
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+constexpr int kSmemExtra = 1024 + 512;
 
 __device__ __forceinline__ void raise_error(int* err, volatile int* abort_flag, int code) {
   *abort_flag = 1;
   if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Arrives on `bar` (counting as one of its expected arrivals) once every
+// cp.async this thread issued so far has landed in shared memory.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, const int stages) {
@@ -88,7 +84,6 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int4* row_info = reinterpret_cast<int4*>(tail + 512);
 
   uint32_t ncols = 32;
   while (ncols < 2u * static_cast<uint32_t>(a.n_tile)) ncols <<= 1;
@@ -122,44 +117,50 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
 
   if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producers
-    uint32_t it = 0;
+    // Thread t copies the 16-byte column j = t % 8 (8 K indices) of rows
+    // t / 8 + 16 i, i = 0..7, for both planes.
+    const int ptid = threadIdx.x;
+    const int j = ptid & 7;
+    const int r0 = ptid >> 3;
+    uint32_t it = 0;  // chunks issued
+    const uint32_t smem_base = smem_u32(smem);
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const int mt = t / a.n_tiles;
       const int nt = t - mt * a.n_tiles;
       const int m0 = mt * kBM;
-      {
-        __syncwarp();  // the previous tile's reads of row_info are done
-        const int row = warp * 32 + lane;
-        const int m = m0 + row;
-        int4 ri = make_int4(0, 0, 0, 0);
+      int rb[8], ry[8], rx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int m = m0 + r0 + 16 * i;
         if (m < M) {
           const int b = m / HoWo;
           const int r = m - b * HoWo;
           const int oy = r / a.Wo;
-          const int ox = r - oy * a.Wo;
-          ri = make_int4(b, oy * a.stride - a.pad, ox * a.stride - a.pad, 1);
+          rb[i] = b;
+          ry[i] = oy * a.stride - a.pad;
+          rx[i] = (r - oy * a.Wo) * a.stride - a.pad;
+        } else {
+          rb[i] = 0;
+          ry[i] = -(1 << 28);  // never in bounds
+          rx[i] = 0;
         }
-        row_info[row] = ri;
-        __syncwarp();
       }
       const uint8_t* wsrc = a.wpack + static_cast<size_t>(nt) * a.num_kc * chunk_bytes;
-      for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
+      for (int kc = 0; kc < a.num_kc; ++kc) {
         const uint32_t s = it % stages;
         const uint32_t ph = (it / stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
           raise_error(a.err, abort_flag, kErrWaitEmpty);
           goto producer_done;
         }
-        uint8_t* sa_hi = smem + s * stage_bytes;
-        uint8_t* sa_lo = sa_hi + kAPlaneBytes;
-        uint8_t* sb = sa_hi + 2 * kAPlaneBytes;
-        if (threadIdx.x == 0) {
+        const uint32_t sa_hi = smem_base + s * stage_bytes;
+        const uint32_t sa_lo = sa_hi + kAPlaneBytes;
+        if (ptid == 0) {
           mbar_expect_tx(&full[s], chunk_bytes);
-          bulk_g2s(sb, wsrc + static_cast<size_t>(kc) * chunk_bytes, chunk_bytes, &full[s]);
+          bulk_g2s(smem + s * stage_bytes + 2 * kAPlaneBytes, wsrc + static_cast<size_t>(kc) * chunk_bytes,
+                   chunk_bytes, &full[s]);
         }
-        // This lane's 4 consecutive K indices (same tap, same source).
-        const int f4 = lane & 15;
-        const int k = kc * kBK + f4 * 4;
+        const int k = kc * kBK + j * 8;
         const bool kvalid = k < a.K;
         int ky = 0, kx = 0, c = 0;
         if (kvalid) {
@@ -169,47 +170,41 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
           kx = tap - ky * a.kw;
         }
         const bool first = c < a.c_split;
-        const float* sptr = first ? a.src0.ptr : a.src1.ptr;
-        const long long sb_stride = first ? a.src0.bstride : a.src1.bstride;
+        const uint16_t* sp = first ? a.src0.hi : a.src1.hi;
+        const long long splane = first ? a.src0.plane : a.src1.plane;
+        const long long sbs = first ? a.src0.bstride : a.src1.bstride;
         const int scs = first ? a.src0.cstride : a.src1.cstride;
-        const int sco = (first ? a.src0.coff + c : a.src1.coff + (c - a.c_split));
+        const int sco = first ? a.src0.coff + c : a.src1.coff + (c - a.c_split);
         const int lg = first ? a.lg_up0 : a.lg_up1;
         const int ws = a.W >> lg;
-
-        float4 v[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int row = warp * 32 + 2 * i + (lane >> 4);
-          const int4 ri = row_info[row];
-          const int iy = ri.y + ky;
-          const int ix = ri.z + kx;
-          const bool ok = kvalid && ri.w && static_cast<unsigned>(iy) < static_cast<unsigned>(a.H) &&
+        for (int i = 0; i < 8; ++i) {
+          const int row = r0 + 16 * i;
+          const int iy = ry[i] + ky;
+          const int ix = rx[i] + kx;
+          const bool ok = kvalid && static_cast<unsigned>(iy) < static_cast<unsigned>(a.H) &&
                           static_cast<unsigned>(ix) < static_cast<unsigned>(a.W);
-          if (ok) {
-            const float* p = sptr + static_cast<long long>(ri.x) * sb_stride +
-                             static_cast<long long>((iy >> lg) * ws + (ix >> lg)) * scs + sco;
-            v[i] = __ldg(reinterpret_cast<const float4*>(p));
-          } else {
-            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-          }
+          const uint16_t* p = ok ? sp + static_cast<long long>(rb[i]) * sbs +
+                                       static_cast<long long>((iy >> lg) * ws + (ix >> lg)) * scs + sco
+                                 : sp;
+          const uint32_t off = sw128_offset(static_cast<uint32_t>(row), static_cast<uint32_t>(j));
+          cp_async16(sa_hi + off, p, ok ? 16u : 0u);
+          cp_async16(sa_lo + off, p + (ok ? splane : 0), ok ? 16u : 0u);
         }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t row = warp * 32 + 2 * i + (lane >> 4);
-          const uint32_t off = sw128_offset(row, static_cast<uint32_t>(f4 >> 1)) + (f4 & 1) * 8;
-          uint2 hi, lo;
-          split4(v[i], hi, lo);
-          *reinterpret_cast<uint2*>(sa_hi + off) = hi;
-          *reinterpret_cast<uint2*>(sa_lo + off) = lo;
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&full[s]);
+        // The stage is published by the copies themselves: this thread's
+        // arrival on full[s] fires when all its copies so far have landed.
+        cp_async_arrive_noinc(&full[s]);
+        ++it;
       }
     }
-  producer_done:;
+  producer_done:
+    cp_async_wait_all();
   } else if (warp < kMmaWarp) {
     // ------------------------------------------------------------- epilogue
-    const int q = warp - kProducerWarps;  // TMEM lane quarter (= warp % 4)
+    const int e_idx = warp - kProducerWarps;  // 0..7
+    const int q = e_idx & 3;                  // TMEM lane quarter (= warp % 4)
+    const int half = e_idx >> 2;              // which 32-column chunks this warp takes
+    const bool f32out = a.out_f32.ptr != nullptr;
     int lt = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
       const int acc = lt & 1;
@@ -230,45 +225,56 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
         b = m / HoWo;
         p = m - b * HoWo;
       }
-      float* orow = a.out.ptr + static_cast<long long>(b) * a.out.bstride +
-                    static_cast<long long>(p) * a.out.cstride + a.out.coff + n0;
-      const float* rrow = a.res.ptr ? a.res.ptr + static_cast<long long>(b) * a.res.bstride +
-                                          static_cast<long long>(p) * a.res.cstride + a.res.coff + n0
-                                    : nullptr;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_stride;
-      for (int c0 = 0; c0 < nvalid; c0 += 16) {
-        uint32_t r[16];
-        tc_ld_32x32b_x16(tbase + c0, r);
+      for (int c0 = 32 * half; c0 < nvalid; c0 += 64) {
+        // Two 16-column TMEM loads, one wait; never past this accumulator.
+        uint32_t r[32];
+        uint32_t(&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[0]);
+        uint32_t(&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[16]);
+        tc_ld_32x32b_x16(tbase + c0, r0);
+        if (c0 + 16 < a.n_tile) tc_ld_32x32b_x16(tbase + c0 + 16, r1);
         tc_wait_ld();
-        if (valid) {
+        if (!valid) continue;
 #pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4) {
-            const int n = c0 + j4 * 4;
-            if (n < nvalid) {
-              float4 x = make_float4(__uint_as_float(r[4 * j4 + 0]), __uint_as_float(r[4 * j4 + 1]),
-                                     __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3]));
-              if (a.bias) {
-                const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bias + n0 + n));
-                x.x += bb.x;
-                x.y += bb.y;
-                x.z += bb.z;
-                x.w += bb.w;
-              }
-              if (a.act == kActSiLU) {
-                x.x = silu(x.x);
-                x.y = silu(x.y);
-                x.z = silu(x.z);
-                x.w = silu(x.w);
-              }
-              if (rrow) {
-                const float4 rr = *reinterpret_cast<const float4*>(rrow + n);
-                x.x += rr.x;
-                x.y += rr.y;
-                x.z += rr.z;
-                x.w += rr.w;
-              }
-              *reinterpret_cast<float4*>(orow + n) = x;
-            }
+        for (int g = 0; g < 4; ++g) {
+          const int n = c0 + 8 * g;  // column within the tile
+          if (n >= nvalid) break;
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(r[8 * g + e]);
+          if (a.bias) {
+            const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.bias + n0 + n));
+            const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.bias + n0 + n + 4));
+            x[0] += b0.x;
+            x[1] += b0.y;
+            x[2] += b0.z;
+            x[3] += b0.w;
+            x[4] += b1.x;
+            x[5] += b1.y;
+            x[6] += b1.z;
+            x[7] += b1.w;
+          }
+          if (a.act == kActSiLU) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = silu_fast(x[e]);
+          }
+          if (a.res.hi) {
+            float rv[8];
+            load8_rw(a.res.hi + static_cast<long long>(b) * a.res.bstride + static_cast<long long>(p) * a.res.cstride +
+                         a.res.coff + n0 + n,
+                     a.res.plane, rv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] += rv[e];
+          }
+          if (f32out) {
+            float* o = a.out_f32.ptr + static_cast<long long>(b) * a.out_f32.bstride +
+                       static_cast<long long>(p) * a.out_f32.cstride + a.out_f32.coff + n0 + n;
+            *reinterpret_cast<float4*>(o) = make_float4(x[0], x[1], x[2], x[3]);
+            if (n + 4 < nvalid) *reinterpret_cast<float4*>(o + 4) = make_float4(x[4], x[5], x[6], x[7]);
+          } else {
+            store8(a.out.hi + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(p) * a.out.cstride +
+                       a.out.coff + n0 + n,
+                   a.out.plane, x);
           }
         }
       }
@@ -300,6 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
             ok = false;
             break;
           }
+          // The stage's activation tile was written by cp.async; order it
+          // before the tensor core's (async-proxy) operand reads.
+          fence_proxy_async_smem();
           tc_fence_after();
           const uint32_t a_hi = smem_u32(smem + s * stage_bytes);
           const uint32_t a_lo = a_hi + kAPlaneBytes;
@@ -355,6 +364,12 @@ inline float host_bf16_to_float(uint16_t h) {
   return f;
 }
 
+int stages_for(int n_tile) {
+  const int stage_bytes = 2 * kAPlaneBytes + static_cast<int>(conv_chunk_bytes(n_tile));
+  int stages = (kSmemLimit - kSmemExtra) / stage_bytes;
+  return stages > 8 ? 8 : stages;
+}
+
 }  // namespace
 
 void choose_n_tiling(int co, int* n_tile, int* n_tiles) {
@@ -399,20 +414,20 @@ size_t pack_conv_weights(const float* w, int co, int ci, int kh, int kw, int n_t
   return total;
 }
 
-// Opts the kernel into the full 227 KB of shared memory on the current device.
-// Called once per device before any launch (and outside stream capture).
+// Opts the kernels into the full 227 KB of shared memory on the current
+// device.  Called once per device before any launch (and outside capture).
 cudaError_t init_conv_kernel_attributes() {
   return cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
 }
 
 cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
-  if (a.n_tile < 16 || a.n_tile > 256 || (a.n_tile % 16) != 0 || a.Ci % 4 != 0 || a.c_split % 4 != 0 ||
-      a.Co % 4 != 0)
+  const bool f32 = a.out_f32.ptr != nullptr;
+  if (a.n_tile < 16 || a.n_tile > 256 || (a.n_tile % 16) != 0 || a.Ci % 8 != 0 || a.c_split % 8 != 0 ||
+      a.Co % (f32 ? 4 : 8) != 0)
     return cudaErrorInvalidValue;
-  const int stage_bytes = 2 * kAPlaneBytes + static_cast<int>(conv_chunk_bytes(a.n_tile));
-  int stages = (kSmemLimit - kSmemExtra) / stage_bytes;
-  if (stages > 8) stages = 8;
+  const int stages = stages_for(a.n_tile);
   if (stages < 2) return cudaErrorInvalidValue;
+  const int stage_bytes = 2 * kAPlaneBytes + static_cast<int>(conv_chunk_bytes(a.n_tile));
   const int smem = kSmemExtra + stages * stage_bytes;
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;

@@ -9,17 +9,19 @@ namespace yb {
 
 namespace {
 
-TView tv(const Buf& b, int coff = 0) {
-  TView v;
-  v.ptr = b.ptr;
+SView tv(const Buf& b, int coff = 0) {
+  SView v;
+  v.hi = b.hi;
+  v.plane = b.plane;
   v.bstride = b.bstride;
   v.cstride = b.C;
   v.coff = coff;
   return v;
 }
-OView ov(const Buf& b, int coff = 0) {
-  OView v;
-  v.ptr = b.ptr;
+SOut ov(const Buf& b, int coff = 0) {
+  SOut v;
+  v.hi = b.hi;
+  v.plane = b.plane;
   v.bstride = b.bstride;
   v.cstride = b.C;
   v.coff = coff;
@@ -244,7 +246,7 @@ cudaError_t Engine::conv_w(const std::string& prefix, bool plain, DevConv** out,
   d.ci = w->dims[1];
   d.kh = w->dims[2];
   d.kw = w->dims[3];
-  if (d.ci % 4 || d.co % 4 || static_cast<int>(b->data.size()) != d.co) {
+  if (d.ci % 8 || d.co % 4 || static_cast<int>(b->data.size()) != d.co) {
     *why = "unsupported conv shape at " + prefix;
     return cudaErrorInvalidValue;
   }
@@ -276,7 +278,7 @@ cudaError_t Engine::dw_w(const std::string& prefix, DevDw** out, std::string* wh
   }
   const HostTensor* w = find(prefix + ".conv.weight");
   const HostTensor* b = find(prefix + ".conv.bias");
-  if (!w || !b || w->dims[1] != 1 || w->dims[2] != 3 || w->dims[3] != 3 || w->dims[0] % 4) {
+  if (!w || !b || w->dims[1] != 1 || w->dims[2] != 3 || w->dims[3] != 3 || w->dims[0] % 8) {
     *why = "missing or unsupported depthwise weight " + prefix;
     return cudaErrorInvalidValue;
   }
@@ -313,13 +315,14 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     b->W = W;
     b->C = C;
     b->bstride = static_cast<long long>(H) * W * C;
-    const size_t bytes = static_cast<size_t>(B) * b->bstride * 4;
+    b->plane = static_cast<long long>(B) * b->bstride;
+    const size_t bytes = static_cast<size_t>(b->plane) * 2 * sizeof(uint16_t);
     void* q = nullptr;
     cudaError_t e = cudaMalloc(&q, bytes);
     if (e != cudaSuccess) return e;
     p->allocs.push_back(q);
     p->arena_bytes += bytes;
-    b->ptr = static_cast<float*>(q);
+    b->hi = static_cast<uint16_t*>(q);
     return cudaSuccess;
   };
   auto alloc_raw = [&](size_t bytes, float** q) -> cudaError_t {
@@ -331,10 +334,14 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     *q = static_cast<float*>(r);
     return cudaSuccess;
   };
-  auto add_conv = [&](const DevConv* w, const Src& in, int stride, int pad, int act, OView out,
-                      TView res) -> cudaError_t {
-    if (in.c0 + in.c1 != w->ci || in.c0 % 4) {
-      *why = "conv input channel mismatch";
+  auto add_conv = [&](const DevConv* w, const Src& in, int stride, int pad, int act, SOut out, SView res,
+                      FOut fout = FOut()) -> cudaError_t {
+    if (in.c0 + in.c1 != w->ci || in.c0 % 8 || w->ci % 8) {
+      *why = "conv input channels must match and be multiples of 8";
+      return cudaErrorInvalidValue;
+    }
+    if (!fout.ptr && w->co % 8) {
+      *why = "conv output channels must be a multiple of 8";
       return cudaErrorInvalidValue;
     }
     ConvArgs a;
@@ -369,6 +376,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     a.bias = w->bias;
     a.act = act;
     a.out = out;
+    a.out_f32 = fout;
     a.res = res;
     a.err = d_err_;
     const int sms = num_sms_;
@@ -378,7 +386,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     op.flops = 2.0 * pix_out * a.Co * a.K;
     const double in0 = static_cast<double>(B) * (in.H >> in.lg0) * (in.W >> in.lg0) * in.c0;
     const double in1 = static_cast<double>(B) * in.H * in.W * in.c1;
-    op.bytes = 4.0 * (in0 + in1 + static_cast<double>(a.Co) * (a.K + 1) + pix_out * a.Co * (res.ptr ? 2 : 1));
+    op.bytes = 4.0 * (in0 + in1 + static_cast<double>(a.Co) * (a.K + 1) + pix_out * a.Co * (res.hi ? 2 : 1));
     ops.push_back(op);
     return cudaSuccess;
   };
@@ -396,17 +404,17 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     DevConv* w;
     YB_TRY(conv("model." + std::to_string(li), &w));
     YB_TRY(alloc_buf((in.H + 2 - w->kh) / 2 + 1, (in.W + 2 - w->kw) / 2 + 1, w->co, out));
-    return add_conv(w, src_of(in, 0, in.C), 2, (w->kh - 1) / 2, kActSiLU, ov(*out), TView());
+    return add_conv(w, src_of(in, 0, in.C), 2, (w->kh - 1) / 2, kActSiLU, ov(*out), SView());
   };
   // Bottleneck (layers.c:92-108): cv1+SiLU -> cv2+SiLU (+ input).
-  auto bottleneck = [&](const std::string& pre, const Src& in, OView out, bool shortcut) -> cudaError_t {
+  auto bottleneck = [&](const std::string& pre, const Src& in, SOut out, bool shortcut) -> cudaError_t {
     DevConv *w1, *w2;
     YB_TRY(conv(pre + ".cv1", &w1));
     YB_TRY(conv(pre + ".cv2", &w2));
     Buf t;
     YB_TRY(alloc_buf(in.H, in.W, w1->co, &t));
-    YB_TRY(add_conv(w1, in, 1, (w1->kh - 1) / 2, kActSiLU, ov(t), TView()));
-    return add_conv(w2, src_of(t, 0, t.C), 1, (w2->kh - 1) / 2, kActSiLU, out, shortcut ? in.v0 : TView());
+    YB_TRY(add_conv(w1, in, 1, (w1->kh - 1) / 2, kActSiLU, ov(t), SView()));
+    return add_conv(w2, src_of(t, 0, t.C), 1, (w2->kh - 1) / 2, kActSiLU, out, shortcut ? in.v0 : SView());
   };
   // C3k2 without C3k (layers.c:110-154, model.c:208-283), shortcut bottlenecks.
   auto c3k2_plain = [&](int li, const Src& in, Buf* out) -> cudaError_t {
@@ -423,14 +431,14 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     }
     Buf cat;
     YB_TRY(alloc_buf(in.H, in.W, (2 + n) * c, &cat));
-    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(cat, 0), TView()));
+    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(cat, 0), SView()));
     int prev = c;
     for (int i = 0; i < n; ++i) {
       YB_TRY(bottleneck(L + ".m." + std::to_string(i), src_of(cat, prev, c), ov(cat, (2 + i) * c), true));
       prev = (2 + i) * c;
     }
     YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
-    return add_conv(cv2, src_of(cat, 0, (2 + n) * c), 1, 0, kActSiLU, ov(*out), TView());
+    return add_conv(cv2, src_of(cat, 0, (2 + n) * c), 1, 0, kActSiLU, ov(*out), SView());
   };
   // C3k2 with an inner C3k (layers.c:156-189, model.c:415-557).
   auto c3k2_c3k = [&](int li, const Src& in, Buf* out) -> cudaError_t {
@@ -450,13 +458,13 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     }
     Buf catO, y, catC;
     YB_TRY(alloc_buf(in.H, in.W, 2 * c + k3->co, &catO));
-    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(catO, 0), TView()));
+    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(catO, 0), SView()));
     const Src b = src_of(catO, c, c);
     const int cm = k1->co;
     YB_TRY(alloc_buf(in.H, in.W, cm, &y));
     YB_TRY(alloc_buf(in.H, in.W, cm + k2->co, &catC));
-    YB_TRY(add_conv(k1, b, 1, 0, kActSiLU, ov(y), TView()));
-    YB_TRY(add_conv(k2, b, 1, 0, kActSiLU, ov(catC, cm), TView()));
+    YB_TRY(add_conv(k1, b, 1, 0, kActSiLU, ov(y), SView()));
+    YB_TRY(add_conv(k2, b, 1, 0, kActSiLU, ov(catC, cm), SView()));
     Src cur = src_of(y, 0, cm);
     for (int i = 0; i < nb; ++i) {
       const std::string pre = L + ".m.0.m." + std::to_string(i);
@@ -469,9 +477,9 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
         cur = src_of(nxt, 0, cm);
       }
     }
-    YB_TRY(add_conv(k3, src_of(catC, 0, catC.C), 1, 0, kActSiLU, ov(catO, 2 * c), TView()));
+    YB_TRY(add_conv(k3, src_of(catC, 0, catC.C), 1, 0, kActSiLU, ov(catO, 2 * c), SView()));
     YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
-    return add_conv(cv2, src_of(catO, 0, catO.C), 1, 0, kActSiLU, ov(*out), TView());
+    return add_conv(cv2, src_of(catO, 0, catO.C), 1, 0, kActSiLU, ov(*out), SView());
   };
   // SPPF k=5, 3 pools, shortcut (layers.c:230-265, model.c:285-320, :825).
   auto sppf = [&](int li, const Buf& in, Buf* out) -> cudaError_t {
@@ -482,7 +490,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     const int c = cv1->co;
     Buf cat;
     YB_TRY(alloc_buf(in.H, in.W, 4 * c, &cat));
-    YB_TRY(add_conv(cv1, src_of(in, 0, in.C), 1, 0, kActNone, ov(cat, 0), TView()));
+    YB_TRY(add_conv(cv1, src_of(in, 0, in.C), 1, 0, kActNone, ov(cat, 0), SView()));
     for (int j = 0; j < 3; ++j) {
       PoolArgs pa;
       pa.in = tv(cat, j * c);
@@ -497,10 +505,10 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     }
     YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
     const bool res = in.C == cv2->co;
-    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), res ? tv(in) : TView());
+    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), res ? tv(in) : SView());
   };
   // PSABlock (layers.c:407-453) with attention (layers.c:310-405).
-  auto psablock = [&](const std::string& pre, const Src& x, int c, OView y, int heads) -> cudaError_t {
+  auto psablock = [&](const std::string& pre, const Src& x, int c, SOut y, int heads) -> cudaError_t {
     DevConv *qkv, *proj, *f0, *f1;
     DevDw* pe;
     YB_TRY(conv(pre + ".attn.qkv", &qkv));
@@ -520,7 +528,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     }
     Buf q, ao, x1, f;
     YB_TRY(alloc_buf(x.H, x.W, qkv->co, &q));
-    YB_TRY(add_conv(qkv, x, 1, 0, kActNone, ov(q), TView()));
+    YB_TRY(add_conv(qkv, x, 1, 0, kActNone, ov(q), SView()));
     YB_TRY(alloc_buf(x.H, x.W, c, &ao));
     AttnArgs aa;
     aa.qkv = tv(q);
@@ -543,7 +551,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     YB_TRY(alloc_buf(x.H, x.W, c, &x1));
     YB_TRY(add_conv(proj, src_of(ao, 0, c), 1, 0, kActNone, ov(x1), x.v0));
     YB_TRY(alloc_buf(x.H, x.W, f0->co, &f));
-    YB_TRY(add_conv(f0, src_of(x1, 0, c), 1, 0, kActSiLU, ov(f), TView()));
+    YB_TRY(add_conv(f0, src_of(x1, 0, c), 1, 0, kActSiLU, ov(f), SView()));
     return add_conv(f1, src_of(f, 0, f.C), 1, 0, kActNone, y, tv(x1));
   };
   // C2PSA (layers.c:455-496, model.c:322-412); blocks update the b half in place.
@@ -561,7 +569,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     if (heads < 1) heads = 1;
     Buf cat;
     YB_TRY(alloc_buf(in.H, in.W, 2 * ch, &cat));
-    YB_TRY(add_conv(cv1, src_of(in, 0, in.C), 1, 0, kActSiLU, ov(cat), TView()));
+    YB_TRY(add_conv(cv1, src_of(in, 0, in.C), 1, 0, kActSiLU, ov(cat), SView()));
     int nb = 0;
     while (exists(L + ".m." + std::to_string(nb) + ".attn.qkv.conv.weight")) {
       YB_TRY(psablock(L + ".m." + std::to_string(nb), src_of(cat, ch, ch), ch, ov(cat, ch), heads));
@@ -572,7 +580,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       return cudaErrorInvalidValue;
     }
     YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
-    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), TView());
+    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), SView());
   };
   // Head C3k2 with Bottleneck + PSABlock (model.c:560-665).
   auto c3k2_attn = [&](int li, const Src& in, Buf* out) -> cudaError_t {
@@ -583,14 +591,14 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     const int c = cv1->co / 2;
     Buf cat, bo;
     YB_TRY(alloc_buf(in.H, in.W, 3 * c, &cat));
-    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(cat, 0), TView()));
+    YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(cat, 0), SView()));
     YB_TRY(alloc_buf(in.H, in.W, c, &bo));
     YB_TRY(bottleneck(L + ".m.0.0", src_of(cat, c, c), ov(bo), true));
     int heads = c / 64;
     if (heads < 1) heads = 1;
     YB_TRY(psablock(L + ".m.0.1", src_of(bo, 0, c), c, ov(cat, 2 * c), heads));
     YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
-    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), TView());
+    return add_conv(cv2, src_of(cat, 0, cat.C), 1, 0, kActSiLU, ov(*out), SView());
   };
 
   Buf* S = p->stage;
@@ -704,14 +712,14 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       // box branch (detect.c:168-191)
       Buf t1, t2;
       YB_TRY(alloc_buf(f.H, f.W, w0->co, &t1));
-      YB_TRY(add_conv(w0, src_of(f, 0, f.C), 1, 1, kActSiLU, ov(t1), TView()));
+      YB_TRY(add_conv(w0, src_of(f, 0, f.C), 1, 1, kActSiLU, ov(t1), SView()));
       YB_TRY(alloc_buf(f.H, f.W, w1->co, &t2));
-      YB_TRY(add_conv(w1, src_of(t1, 0, t1.C), 1, 1, kActSiLU, ov(t2), TView()));
-      OView dv;
+      YB_TRY(add_conv(w1, src_of(t1, 0, t1.C), 1, 1, kActSiLU, ov(t2), SView()));
+      FOut dv;
       dv.ptr = p->d_dist + static_cast<size_t>(base[s]) * 4;
       dv.bstride = static_cast<long long>(N) * 4;
       dv.cstride = 4;
-      YB_TRY(add_conv(w2, src_of(t2, 0, t2.C), 1, 0, kActNone, dv, TView()));
+      YB_TRY(add_conv(w2, src_of(t2, 0, t2.C), 1, 0, kActNone, SOut(), SView(), dv));
       // class branch (detect.c:193-232)
       Buf d0, p0, d1, p1;
       YB_TRY(alloc_buf(f.H, f.W, f.C, &d0));
@@ -732,7 +740,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       const double px = static_cast<double>(B) * f.H * f.W;
       add_op(kOpDw, 18.0 * px * f.C, 8.0 * px * f.C, [da](cudaStream_t st) { return launch_dwconv3x3(da, st); });
       YB_TRY(alloc_buf(f.H, f.W, pw0->co, &p0));
-      YB_TRY(add_conv(pw0, src_of(d0, 0, d0.C), 1, 0, kActSiLU, ov(p0), TView()));
+      YB_TRY(add_conv(pw0, src_of(d0, 0, d0.C), 1, 0, kActSiLU, ov(p0), SView()));
       YB_TRY(alloc_buf(f.H, f.W, p0.C, &d1));
       DwArgs db = da;
       db.in = tv(p0);
@@ -746,12 +754,12 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       }
       add_op(kOpDw, 18.0 * px * p0.C, 8.0 * px * p0.C, [db](cudaStream_t st) { return launch_dwconv3x3(db, st); });
       YB_TRY(alloc_buf(f.H, f.W, pw1->co, &p1));
-      YB_TRY(add_conv(pw1, src_of(d1, 0, d1.C), 1, 0, kActSiLU, ov(p1), TView()));
-      OView lv;
+      YB_TRY(add_conv(pw1, src_of(d1, 0, d1.C), 1, 0, kActSiLU, ov(p1), SView()));
+      FOut lv;
       lv.ptr = p->d_logits + static_cast<size_t>(base[s]) * nc;
       lv.bstride = static_cast<long long>(N) * nc;
       lv.cstride = nc;
-      YB_TRY(add_conv(wf, src_of(p1, 0, p1.C), 1, 0, kActNone, lv, TView()));
+      YB_TRY(add_conv(wf, src_of(p1, 0, p1.C), 1, 0, kActNone, SOut(), SView(), lv));
     }
     DecodeArgs de;
     de.dist = p->d_dist;

@@ -42,20 +42,22 @@ struct DevStem {
   int co = 0, ci = 0, k = 0;
 };
 
-// A full NHWC activation tensor [B, H, W, C] in the arena.
+// A full split NHWC activation tensor [B, H, W, C] in the arena: the hi plane
+// followed by the lo plane (kernels.h).
 struct Buf {
-  float* ptr = nullptr;
+  uint16_t* hi = nullptr;
   int H = 0, W = 0, C = 0;
   long long bstride = 0;
+  long long plane = 0;
 };
 
 // An input of a convolution: one tensor, or the channel concat of an
 // (optionally nearest-upsampled) first source and a second source.
 struct Src {
-  TView v0;
+  SView v0;
   int c0 = 0;
   int lg0 = 0;
-  TView v1;
+  SView v1;
   int c1 = 0;
   int H = 0, W = 0;
 };

@@ -119,21 +119,22 @@ status_t dump_stages(Ctx* c, Plan* p, const float* in_nchw, yb_stage_cb cb, void
   const Buf* S = p->stage;
   size_t maxe = static_cast<size_t>(3) * p->H * p->W;
   for (int i = 0; i < 23; ++i)
-    if (S[i].ptr) maxe = std::max(maxe, static_cast<size_t>(S[i].H) * S[i].W * S[i].C * 2);
+    if (S[i].hi) maxe = std::max(maxe, static_cast<size_t>(S[i].H) * S[i].W * S[i].C * 2);
   DevMem t0, t1;
   cudaError_t e = t0.alloc(maxe * 4);
   if (e == cudaSuccess) e = t1.alloc(maxe * 4);
   if (e != cudaSuccess) return cuda_status(e, "stage dump buffers");
   std::vector<float> host(maxe);
   auto tv = [](const Buf& b) {
-    TView v;
-    v.ptr = b.ptr;
+    SView v;
+    v.hi = b.hi;
+    v.plane = b.plane;
     v.bstride = b.bstride;
     v.cstride = b.C;
     return v;
   };
-  auto emit = [&](const char* name, TView v, int C, int H, int W) -> status_t {
-    cudaError_t er = launch_nhwc_to_nchw(v, 1, C, H, W, t1.f(), s);
+  auto emit = [&](const char* name, SView v, int C, int H, int W) -> status_t {
+    cudaError_t er = launch_split_to_nchw(v, 1, C, H, W, t1.f(), s);
     if (er == cudaSuccess) er = cudaMemcpyAsync(host.data(), t1.p, static_cast<size_t>(C) * H * W * 4, cudaMemcpyDeviceToHost, s);
     if (er == cudaSuccess) er = cudaStreamSynchronize(s);
     if (er != cudaSuccess) return cuda_status(er, name);
@@ -142,15 +143,17 @@ status_t dump_stages(Ctx* c, Plan* p, const float* in_nchw, yb_stage_cb cb, void
   };
   auto emit_buf = [&](const char* name, int k) { return emit(name, tv(S[k]), S[k].C, S[k].H, S[k].W); };
   auto emit_cat = [&](const char* name, const Buf& a, int up, const Buf* b, int H, int W) -> status_t {
-    OView o;
-    o.ptr = t0.f();
+    SOut o;
+    o.hi = static_cast<uint16_t*>(t0.p);
     o.cstride = a.C + (b ? b->C : 0);
     o.bstride = static_cast<long long>(H) * W * o.cstride;
-    TView bv = b ? tv(*b) : tv(a);
+    o.plane = o.bstride;
+    SView bv = b ? tv(*b) : tv(a);
     cudaError_t er = launch_gather_concat(tv(a), a.C, up, bv, b ? b->C : 0, 1, H, W, o, s);
     if (er != cudaSuccess) return cuda_status(er, name);
-    TView v;
-    v.ptr = t0.f();
+    SView v;
+    v.hi = o.hi;
+    v.plane = o.plane;
     v.cstride = o.cstride;
     v.bstride = o.bstride;
     return emit(name, v, o.cstride, H, W);
@@ -987,11 +990,12 @@ extern "C" status_t detect_forward_one2one(model_t* m, int detect_module_idx, co
   for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
     const size_t n = static_cast<size_t>(dst[i]->C) * dst[i]->H * dst[i]->W;
     e = cudaMemcpyAsync(tmp.p, f[i]->data, n * 4, cudaMemcpyHostToDevice, s);
-    OView o;
-    o.ptr = dst[i]->ptr;
+    SOut o;
+    o.hi = dst[i]->hi;
+    o.plane = dst[i]->plane;
     o.bstride = dst[i]->bstride;
     o.cstride = dst[i]->C;
-    if (e == cudaSuccess) e = launch_nchw_to_nhwc(tmp.f(), 1, dst[i]->C, dst[i]->H, dst[i]->W, o, s);
+    if (e == cudaSuccess) e = launch_nchw_to_split(tmp.f(), 1, dst[i]->C, dst[i]->H, dst[i]->W, o, s);
   }
   for (const Op& op : p->ops)
     if (e == cudaSuccess && op.step == 23) e = op.run(s);

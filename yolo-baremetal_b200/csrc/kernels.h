@@ -1,25 +1,52 @@
 // Host-visible descriptions of the device kernels of the YOLO26 sm_100a path
-// and their launchers.  All activations are NHWC float32 in HBM; a tensor is
-// addressed through a view {ptr, bstride, cstride, coff}: element (b, pixel p,
-// channel c) lives at ptr[b*bstride + p*cstride + coff + c].  Views let a
-// kernel read or write a channel slice of a larger buffer, which is how every
-// concat of the reference (layers.c:145-153, :185-186, :251-254, :493,
-// model.c:547-550, :657-660) is folded away: producers write straight into
-// their slice and consumers read the whole buffer.
+// and their launchers.
+//
+// Activation format.  Every activation is an NHWC tensor stored as two bf16
+// planes in one allocation: hi = bf16_rn(v) and lo = bf16_rn(v - hi), so
+// v = hi + lo carries ~16 significant bits (relative representation error
+// <= 2^-17) in the same 4 bytes per element as fp32.  The tcgen05 convolution
+// consumes the planes directly as its split-bf16 operands (hi*hi + hi*lo +
+// lo*hi), so operand tiles are plain asynchronous copies; CUDA-core kernels
+// read hi + lo as fp32 and write results split again.
+//
+// A tensor is addressed through a view {hi, plane, bstride, cstride, coff}:
+// element (b, pixel p, channel c) is hi[b*bstride + p*cstride + coff + c] and
+// its low part sits `plane` elements later.  Views let a kernel read or write
+// a channel slice of a larger buffer, which is how every concat of the
+// reference (layers.c:145-153, :185-186, :251-254, :493, model.c:547-550,
+// :657-660) is folded away: producers write straight into their slice and
+// consumers read the whole buffer.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
 
 namespace yb {
 
-struct TView {
-  const float* ptr = nullptr;
+struct SView {
+  const uint16_t* hi = nullptr;
+  long long plane = 0;    // elements from the hi plane to the lo plane
   long long bstride = 0;  // elements between images
   int cstride = 0;        // elements between pixels
   int coff = 0;           // first channel of the slice
 };
 
-struct OView {
+struct SOut {
+  uint16_t* hi = nullptr;
+  long long plane = 0;
+  long long bstride = 0;
+  int cstride = 0;
+  int coff = 0;
+};
+
+// Plain fp32 views (Detect head outputs, NCHW host-layout tensors).
+struct FView {
+  const float* ptr = nullptr;
+  long long bstride = 0;
+  int cstride = 0;
+  int coff = 0;
+};
+
+struct FOut {
   float* ptr = nullptr;
   long long bstride = 0;
   int cstride = 0;
@@ -34,7 +61,10 @@ enum Act : int { kActNone = 0, kActSiLU = 1 };
 // upsample of a map half the logical size (the reference's upsample+concat,
 // layers.c:23-39 and :219-228, read in place).  Epilogue: + bias, optional
 // SiLU, optional + residual (after the activation, as in layers.c:103-106,
-// :259-263, :422-450), store into `out`.
+// :259-263, :422-450), stored split into `out`, or as fp32 into `out_f32`
+// when out_f32.ptr is set.  Ci, c_split, view offsets and strides must be
+// multiples of 8 (16-byte copies of bf16); Co a multiple of 8 for split
+// output, of 4 for fp32 output.
 struct ConvArgs {
   int B = 0, H = 0, W = 0;  // logical input size (after upsampling)
   int Ci = 0, Co = 0;
@@ -43,13 +73,14 @@ struct ConvArgs {
   int K = 0, num_kc = 0;  // K = kh*kw*Ci, num_kc = ceil(K / 64)
   int n_tile = 0, n_tiles = 0, m_tiles = 0;
   int c_split = 0;
-  TView src0, src1;
+  SView src0, src1;
   int lg_up0 = 0, lg_up1 = 0;
   const uint8_t* wpack = nullptr;  // packed split-bf16 weights (see pack_conv_weights)
-  const float* bias = nullptr;     // [Co] or null
+  const float* bias = nullptr;     // [n_tile * n_tiles] (zero padded) or null
   int act = kActNone;
-  OView out;
-  TView res;  // res.ptr == nullptr: no residual
+  SOut out;
+  FOut out_f32;  // used instead of `out` when out_f32.ptr != nullptr
+  SView res;     // res.hi == nullptr: no residual
   int* err = nullptr;
 };
 
@@ -72,50 +103,50 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms);
 cudaError_t init_conv_kernel_attributes();
 
 // ---------------------------------------------------------------- SIMT kernels
-// First convolution, reading the NCHW host-layout input directly:
-// 3x3 stride 2 pad 1, Ci <= 4, Co <= 64, + bias + SiLU, NHWC output.
+// First convolution, reading the NCHW host-layout fp32 input directly:
+// 3x3 stride 2 pad 1, Ci <= 4, Co in {16, 32, 64}, + bias + SiLU.
 struct StemArgs {
   const float* in = nullptr;  // [B, Ci, H, W]
   int B = 0, Ci = 0, H = 0, W = 0, Co = 0, Ho = 0, Wo = 0, stride = 2, pad = 1, k = 3;
   const float* w = nullptr;   // device copy of [Co][Ci][k][k]
   const float* bias = nullptr;
   int act = kActSiLU;
-  OView out;
+  SOut out;
 };
 cudaError_t launch_stem(const StemArgs& a, cudaStream_t s);
 
 // Depthwise 3x3, pad 1, + bias, optional SiLU (layers.c:269-290 plus
-// detect.c:219-228).  w: device [C][9].
+// detect.c:219-228).  w: device [9][C] (tap-major).  C a multiple of 8.
 struct DwArgs {
-  TView in;
+  SView in;
   int B = 0, H = 0, W = 0, C = 0;
   const float* w = nullptr;
   const float* bias = nullptr;
   int act = kActNone;
-  OView out;
+  SOut out;
 };
 cudaError_t launch_dwconv3x3(const DwArgs& a, cudaStream_t s);
 
 // Max pool with padding k/2 excluded from the max (layers.c:191-217).
 // Output size Ho x Wo (0 = same as the input, for stride 1).
 struct PoolArgs {
-  TView in;
+  SView in;
   int B = 0, H = 0, W = 0, C = 0, k = 5, stride = 1, Ho = 0, Wo = 0;
-  OView out;
+  SOut out;
 };
 cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s);
 
 // Multi-head attention of the PSA block (layers.c:310-405): per head h the
 // qkv channels [h*(2kd+hd), +kd) are q, the next kd are k, the next hd are v;
 // S = q.k * kd^-0.5, row softmax, out = P.v; then + depthwise 3x3 of v
-// (pe conv, weight [heads*hd][9] + bias).  out channels h*hd + d.
+// (pe conv, weight [9][heads*hd] tap-major + bias).  out channels h*hd + d.
 struct AttnArgs {
-  TView qkv;
+  SView qkv;
   int B = 0, H = 0, W = 0, heads = 0, kd = 0, hd = 0;
   float scale = 1.f;
   const float* pe_w = nullptr;
   const float* pe_b = nullptr;
-  OView out;
+  SOut out;
 };
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 
@@ -160,13 +191,15 @@ cudaError_t launch_topk(const TopkArgs& a, cudaStream_t s);
 constexpr int kTopkMax = 1024;
 
 // Layout conversions for the host API and stage dumps.
-cudaError_t launch_nchw_to_nhwc(const float* in, int B, int C, int H, int W, OView out, cudaStream_t s);
-cudaError_t launch_nhwc_to_nchw(TView in, int B, int C, int H, int W, float* out, cudaStream_t s);
+// NCHW fp32 [B,C,H,W] -> split NHWC view (channels [0, C) of the view).
+cudaError_t launch_nchw_to_split(const float* in, int B, int C, int H, int W, SOut out, cudaStream_t s);
+// Split NHWC view -> NCHW fp32 [B,C,H,W] (value hi + lo).
+cudaError_t launch_split_to_nchw(SView in, int B, int C, int H, int W, float* out, cudaStream_t s);
 // out[B,H,W,c0+c1] = nearest-upsample(src0 by the integer factor up0) ++ src1
 // along channels (stage dumps and the layer-level API).
-cudaError_t launch_gather_concat(TView src0, int c0, int up0, TView src1, int c1, int B, int H, int W, OView out,
+cudaError_t launch_gather_concat(SView src0, int c0, int up0, SView src1, int c1, int B, int H, int W, SOut out,
                                  cudaStream_t s);
-// In-place SiLU on an NHWC view.
-cudaError_t launch_silu(OView t, int B, int HW, int C, cudaStream_t s);
+// In-place SiLU on a split view.
+cudaError_t launch_silu(SOut t, int B, int HW, int C, cudaStream_t s);
 
 }  // namespace yb

@@ -1,7 +1,8 @@
 // Layer-level entry points of layers.h (reference: src/layers.c of
 // phucb2/yolo-baremetal) and tensor_gemm (src/tensor.c:64-113), each running
-// on the current CUDA device.  Host NCHW tensors are staged into HBM as NHWC
-// with the channel count padded to a multiple of 4 (zeros), weights are packed
+// on the current CUDA device.  Host NCHW tensors are staged into HBM in the
+// split NHWC format with the channel count padded to a multiple of 8 (zeros),
+// all on one stream (allocation zero-fill, copies, kernels), weights are packed
 // for the tcgen05 convolution per call, the block runs with the same kernels
 // as the model graph, and the result is copied back.  These calls exist for
 // drop-in completeness and per-block parity tests; the model path
@@ -20,24 +21,28 @@
 namespace yb {
 namespace {
 
-inline int pad4(int c) { return (c + 3) & ~3; }
+inline int pad8(int c) { return (c + 7) & ~7; }
 
-// Device tensor [1, H, W, Cp] with C logical channels.
+// Split device tensor [1, H, W, Cp] (hi plane then lo plane) with C logical
+// channels; channels C..Cp-1 are zero.
 struct DT {
-  float* ptr = nullptr;
+  uint16_t* hi = nullptr;
   int H = 0, W = 0, C = 0, Cp = 0;
-  TView v(int coff = 0) const {
-    TView t;
-    t.ptr = ptr;
-    t.bstride = static_cast<long long>(H) * W * Cp;
+  long long plane() const { return static_cast<long long>(H) * W * Cp; }
+  SView v(int coff = 0) const {
+    SView t;
+    t.hi = hi;
+    t.plane = plane();
+    t.bstride = plane();
     t.cstride = Cp;
     t.coff = coff;
     return t;
   }
-  OView o(int coff = 0) const {
-    OView t;
-    t.ptr = ptr;
-    t.bstride = static_cast<long long>(H) * W * Cp;
+  SOut o(int coff = 0) const {
+    SOut t;
+    t.hi = hi;
+    t.plane = plane();
+    t.bstride = plane();
     t.cstride = Cp;
     t.coff = coff;
     return t;
@@ -61,6 +66,11 @@ class Kit {
     if (!sc) st = ERROR_DEVICE;
   }
   bool ok() const { return st == SUCCESS && err == cudaSuccess; }
+  // Host -> device copy on the scope's stream, so it is ordered after the
+  // stream's zero-fill of the destination (alloc) and before the kernels.
+  cudaError_t h2d(void* dst, const void* src, size_t bytes) {
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, sc->stream);
+  }
 
   float* alloc(size_t n) {
     if (!ok()) return nullptr;
@@ -75,8 +85,9 @@ class Kit {
     d.H = H;
     d.W = W;
     d.C = C;
-    d.Cp = pad4(C);
-    d.ptr = alloc(static_cast<size_t>(H) * W * d.Cp);
+    d.Cp = pad8(C);
+    // two bf16 planes: the same bytes as one fp32 tensor
+    d.hi = reinterpret_cast<uint16_t*>(alloc(static_cast<size_t>(H) * W * d.Cp));
     return d;
   }
   // Image 0 of a host NCHW tensor.
@@ -87,7 +98,7 @@ class Kit {
     float* tmp = alloc(n);
     if (!ok()) return d;
     err = cudaMemcpyAsync(tmp, t->data, n * 4, cudaMemcpyHostToDevice, sc->stream);
-    if (ok()) err = launch_nchw_to_nhwc(tmp, 1, d.C, d.H, d.W, d.o(), sc->stream);
+    if (ok()) err = launch_nchw_to_split(tmp, 1, d.C, d.H, d.W, d.o(), sc->stream);
     return d;
   }
   // Writes image 0 of `out` (NCHW host) from the first C channels of d.
@@ -96,7 +107,7 @@ class Kit {
     const size_t n = static_cast<size_t>(d.C) * d.H * d.W;
     float* tmp = alloc(n);
     if (!ok()) return;
-    err = launch_nhwc_to_nchw(d.v(), 1, d.C, d.H, d.W, tmp, sc->stream);
+    err = launch_split_to_nchw(d.v(), 1, d.C, d.H, d.W, tmp, sc->stream);
     if (ok()) err = cudaMemcpyAsync(out->data, tmp, n * 4, cudaMemcpyDeviceToHost, sc->stream);
     if (ok()) err = cudaStreamSynchronize(sc->stream);
     if (ok()) {
@@ -114,7 +125,7 @@ class Kit {
     PackedConv p;
     if (!ok()) return p;
     p.co = w->dims[0];
-    p.cop = pad4(p.co);
+    p.cop = pad8(p.co);
     const int ci = w->dims[1];
     p.cip = cip;
     p.kh = w->dims[2];
@@ -131,11 +142,11 @@ class Kit {
     std::vector<uint8_t> pk(bytes);
     pack_conv_weights(wp.data(), p.cop, cip, p.kh, p.kw, p.n_tile, pk.data());
     p.wpack = reinterpret_cast<uint8_t*>(alloc((bytes + 3) / 4));
-    if (ok()) err = cudaMemcpy(p.wpack, pk.data(), bytes, cudaMemcpyHostToDevice);
+    if (ok()) err = h2d(p.wpack, pk.data(), bytes);
     std::vector<float> bp(static_cast<size_t>(p.n_tile) * p.n_tiles, 0.f);
     if (b) std::copy(b->data, b->data + p.co, bp.begin());
     p.bias = alloc(bp.size());
-    if (ok()) err = cudaMemcpy(p.bias, bp.data(), bp.size() * 4, cudaMemcpyHostToDevice);
+    if (ok()) err = h2d(p.bias, bp.data(), bp.size() * 4);
     return p;
   }
   // Convolution of in (channels [coff, coff+cin) of x) into out slice.
@@ -177,7 +188,7 @@ class Kit {
   void dw(const tensor_t* w, const tensor_t* b, const DT& x, int coff, int act, const DT& y, int ycoff) {
     if (!ok()) return;
     const int C = w->dims[0];
-    const int Cp = pad4(C);
+    const int Cp = pad8(C);
     std::vector<float> t(static_cast<size_t>(9) * Cp, 0.f), bb(Cp, 0.f);
     for (int c = 0; c < C; ++c)
       for (int k = 0; k < 9; ++k) t[static_cast<size_t>(k) * Cp + c] = w->data[static_cast<size_t>(c) * 9 + k];
@@ -185,8 +196,8 @@ class Kit {
     float* dw = alloc(t.size());
     float* db = alloc(bb.size());
     if (!ok()) return;
-    cudaMemcpy(dw, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
-    err = cudaMemcpy(db, bb.data(), bb.size() * 4, cudaMemcpyHostToDevice);
+    err = h2d(dw, t.data(), t.size() * 4);
+    if (ok()) err = h2d(db, bb.data(), bb.size() * 4);
     DwArgs a;
     a.in = x.v(coff);
     a.B = 1;
@@ -208,8 +219,8 @@ class Kit {
     float* dw = alloc(t.size());
     float* db = alloc(bb.size());
     if (!ok()) return;
-    cudaMemcpy(dw, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
-    err = cudaMemcpy(db, bb.data(), bb.size() * 4, cudaMemcpyHostToDevice);
+    err = h2d(dw, t.data(), t.size() * 4);
+    if (ok()) err = h2d(db, bb.data(), bb.size() * 4);
     AttnArgs a;
     a.qkv = qkv.v();
     a.B = 1;
@@ -231,7 +242,7 @@ class Kit {
     a.B = 1;
     a.H = x.H;
     a.W = x.W;
-    a.C = pad4(C);
+    a.C = pad8(C);
     a.k = k;
     a.stride = stride;
     a.Ho = y.H;
@@ -248,9 +259,9 @@ class Kit {
   std::vector<std::unique_ptr<DevMem>> mem_;
 };
 
-bool all_mult4(std::initializer_list<int> cs) {
+bool all_mult8(std::initializer_list<int> cs) {
   for (int c : cs)
-    if (c % 4) return false;
+    if (c % 8) return false;
   return true;
 }
 
@@ -376,7 +387,7 @@ extern "C" status_t bottleneck_forward(tensor_t* output, const tensor_t* input, 
                                        bool shortcut, tensor_t* temp) {
   (void)temp;
   if (!output || !input || !cv1_w || !cv2_w) return ERROR_NULL_POINTER;
-  if (!all_mult4({input->dims[1], cv1_w->dims[0], cv2_w->dims[0]})) return ERROR_INVALID_DIMS;
+  if (!all_mult8({input->dims[1], cv1_w->dims[0], cv2_w->dims[0]})) return ERROR_INVALID_DIMS;
   Kit k;
   DT x = k.upload(input);
   const PackedConv p1 = k.pack(cv1_w, cv1_b, x.Cp);
@@ -395,7 +406,7 @@ extern "C" status_t c3k2_forward(tensor_t* output, const tensor_t* input, int n,
   (void)buffers;
   if (!output || !input || !cv1_w || !cv2_w || (n > 0 && !bw)) return ERROR_NULL_POINTER;
   const int ct = cv1_w->dims[0], ch = ct / 2;
-  if (!all_mult4({input->dims[1], ct, ch, cv2_w->dims[0]}) || cv2_w->dims[1] != (2 + n) * ch) return ERROR_INVALID_DIMS;
+  if (!all_mult8({input->dims[1], ct, ch, cv2_w->dims[0]}) || cv2_w->dims[1] != (2 + n) * ch) return ERROR_INVALID_DIMS;
   Kit k;
   DT x = k.upload(input);
   const PackedConv p1 = k.pack(cv1_w, cv1_b, x.Cp);
@@ -406,7 +417,7 @@ extern "C" status_t c3k2_forward(tensor_t* output, const tensor_t* input, int n,
     const PackedConv b1 = k.pack(&bw[4 * i + 0], &bw[4 * i + 1], ch);
     const PackedConv b2 = k.pack(&bw[4 * i + 2], &bw[4 * i + 3], b1.cop);
     if (!k.ok()) break;
-    if (b2.co != ch || b1.co % 4) return ERROR_INVALID_DIMS;
+    if (b2.co != ch || b1.co % 8) return ERROR_INVALID_DIMS;
     DT t = k.tensor(x.H, x.W, b1.co);
     k.conv(b1, cat, prev, 1, (b1.kh - 1) / 2, kActSiLU, t, 0);
     k.conv(b2, t, 0, 1, (b2.kh - 1) / 2, kActSiLU, cat, (2 + i) * ch, shortcut ? &cat : nullptr, prev);
@@ -426,7 +437,7 @@ extern "C" status_t c3_forward(tensor_t* output, const tensor_t* input, const te
   if (!output || !input || !cv1_w || !cv1_b || !cv2_w || !cv2_b || !cv3_w || !cv3_b || !bw || !buffers)
     return ERROR_NULL_POINTER;
   const int cm = cv1_w->dims[0], c2 = cv2_w->dims[0];
-  if (!all_mult4({input->dims[1], cm, c2, cv3_w->dims[0]}) || cv3_w->dims[1] != cm + c2) return ERROR_INVALID_DIMS;
+  if (!all_mult8({input->dims[1], cm, c2, cv3_w->dims[0]}) || cv3_w->dims[1] != cm + c2) return ERROR_INVALID_DIMS;
   Kit k;
   DT x = k.upload(input);
   const PackedConv p1 = k.pack(cv1_w, cv1_b, x.Cp);
@@ -440,7 +451,7 @@ extern "C" status_t c3_forward(tensor_t* output, const tensor_t* input, const te
     const PackedConv b1 = k.pack(&bw[4 * i + 0], &bw[4 * i + 1], cm);
     const PackedConv b2 = k.pack(&bw[4 * i + 2], &bw[4 * i + 3], b1.cop);
     if (!k.ok()) break;
-    if (b2.co != cm || b1.co % 4) return ERROR_INVALID_DIMS;
+    if (b2.co != cm || b1.co % 8) return ERROR_INVALID_DIMS;
     DT t = k.tensor(x.H, x.W, b1.co);
     k.conv(b1, cur, 0, 1, (b1.kh - 1) / 2, kActSiLU, t, 0);
     if (i == n_bottles - 1) {
@@ -466,7 +477,7 @@ extern "C" status_t sppf_forward(tensor_t* output, const tensor_t* input, const 
   if (!output || !input || !cv1_w || !cv1_b || !cv2_w || !cv2_b || !buffers) return ERROR_NULL_POINTER;
   if (n_pool < 1) return ERROR_INVALID_DIMS;
   const int c = cv1_w->dims[0];
-  if (!all_mult4({input->dims[1], c, cv2_w->dims[0]}) || cv2_w->dims[1] != c * (n_pool + 1)) return ERROR_INVALID_DIMS;
+  if (!all_mult8({input->dims[1], c, cv2_w->dims[0]}) || cv2_w->dims[1] != c * (n_pool + 1)) return ERROR_INVALID_DIMS;
   Kit k;
   DT x = k.upload(input);
   const PackedConv p1 = k.pack(cv1_w, cv1_b, x.Cp);
@@ -491,7 +502,7 @@ extern "C" status_t psablock_forward(tensor_t* output, const tensor_t* input, bo
       !ffn1_w || !ffn1_b)
     return ERROR_NULL_POINTER;
   const int c = input->dims[1];
-  if (num_heads < 1 || c % num_heads || !all_mult4({c, ffn0_w->dims[0]})) return ERROR_INVALID_DIMS;
+  if (num_heads < 1 || c % num_heads || !all_mult8({c, ffn0_w->dims[0]})) return ERROR_INVALID_DIMS;
   const tensor_t w[10] = {*qkv_w, *qkv_b, *proj_w, *proj_b, *pe_w, *pe_b, *ffn0_w, *ffn0_b, *ffn1_w, *ffn1_b};
   Kit k;
   DT x = k.upload(input);
@@ -507,7 +518,7 @@ extern "C" status_t c2psa_forward(tensor_t* output, const tensor_t* input, int n
   if (!output || !input || !cv1_w || !cv1_b || !cv2_w || !cv2_b || !psa_weights || !buffers) return ERROR_NULL_POINTER;
   const int c1 = input->dims[1];
   const int ch = static_cast<int>(static_cast<float>(c1) * e);
-  if (ch < 1 || n_blocks < 1 || cv1_w->dims[0] != 2 * ch || !all_mult4({c1, ch})) return ERROR_INVALID_DIMS;
+  if (ch < 1 || n_blocks < 1 || cv1_w->dims[0] != 2 * ch || !all_mult8({c1, ch})) return ERROR_INVALID_DIMS;
   int heads = ch / 64;
   if (heads < 1) heads = 1;
   Kit k;

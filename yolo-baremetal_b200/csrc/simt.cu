@@ -1,11 +1,12 @@
 // CUDA-core kernels of the YOLO26 path: the ops that are not contractions
 // (depthwise, pooling, decode, layout) or too small to tile (the 3-channel stem
 // convolution), plus the PSA attention.  All are HBM- or latency-bound; they
-// read and write NHWC fp32 through channel-slice views (kernels.h) with
-// 16-byte vector accesses.  Summation orders follow the reference loops so
-// that results stay within a few ulps of it.
+// read and write split NHWC views (kernels.h) 8 channels (two 16-byte
+// accesses) at a time.  Summation orders follow the reference loops so that
+// results stay within a few ulps of it.
 #include <cfloat>
 #include "kernels.h"
+#include "split.cuh"
 
 namespace yb {
 namespace {
@@ -14,6 +15,11 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 inline int blocks_for(long long n, int t) { return static_cast<int>((n + t - 1) / t); }
+
+template <typename V>
+__device__ __forceinline__ long long vaddr(const V& v, int b, long long p) {
+  return static_cast<long long>(b) * v.bstride + p * v.cstride + v.coff;
+}
 
 // ------------------------------------------------------------------ stem conv
 // Reference loop order (layers.c:60-79): sum = bias; for ci, ky, kx: sum += x*w,
@@ -37,6 +43,7 @@ __global__ void stem_kernel(const StemArgs a) {
   for (int c = 0; c < CO; ++c) acc[c] = sb[c];
   const long long plane = static_cast<long long>(a.H) * a.W;
   const float* inb = a.in + static_cast<long long>(b) * a.Ci * plane;
+  const int wstride = a.Ci * a.k * a.k;
   for (int ci = 0; ci < a.Ci; ++ci) {
     for (int ky = 0; ky < a.k; ++ky) {
       const int iy = oy * a.stride - a.pad + ky;
@@ -45,41 +52,37 @@ __global__ void stem_kernel(const StemArgs a) {
         if (iy < 0 || iy >= a.H || ix < 0 || ix >= a.W) continue;
         const float x = __ldg(inb + ci * plane + static_cast<long long>(iy) * a.W + ix);
         const int wo = (ci * a.k + ky) * a.k + kx;
-        const int wstride = a.Ci * a.k * a.k;
 #pragma unroll
         for (int c = 0; c < CO; ++c) acc[c] = __fadd_rn(acc[c], __fmul_rn(x, sw[c * wstride + wo]));
       }
     }
   }
-  float* o = a.out.ptr + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(r) * a.out.cstride +
-             a.out.coff;
+  uint16_t* o = a.out.hi + vaddr(a.out, b, r);
 #pragma unroll
-  for (int c = 0; c < CO; c += 4) {
-    float4 v = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-    if (a.act == kActSiLU) {
-      v.x = silu(v.x);
-      v.y = silu(v.y);
-      v.z = silu(v.z);
-      v.w = silu(v.w);
-    }
-    *reinterpret_cast<float4*>(o + c) = v;
+  for (int c = 0; c < CO; c += 8) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = a.act == kActSiLU ? silu(acc[c + e]) : acc[c + e];
+    store8(o + c, a.out.plane, v);
   }
 }
 
 // ------------------------------------------------------------- depthwise 3x3
-// w is [9][C] (tap-major, transposed on the host) for 16-byte loads.
+// w is [9][C] (tap-major, transposed on the host); 8 channels per thread.
 __global__ void dw3x3_kernel(const DwArgs a) {
-  const int C4 = a.C >> 2;
+  const int C8 = a.C >> 3;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(a.B) * a.H * a.W * C4;
+  const long long total = static_cast<long long>(a.B) * a.H * a.W * C8;
   if (idx >= total) return;
-  const int c = static_cast<int>(idx % C4) * 4;
-  const long long pix = idx / C4;
+  const int c = static_cast<int>(idx % C8) * 8;
+  const long long pix = idx / C8;
   const int b = static_cast<int>(pix / (a.H * a.W));
   const int p = static_cast<int>(pix - static_cast<long long>(b) * a.H * a.W);
   const int y = p / a.W, x = p - (p / a.W) * a.W;
-  float4 s = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
-  const float* base = a.in.ptr + static_cast<long long>(b) * a.in.bstride + a.in.coff + c;
+  float s[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[e] = a.bias ? __ldg(a.bias + c + e) : 0.f;
+  const uint16_t* base = a.in.hi + vaddr(a.in, b, 0) + c;
 #pragma unroll
   for (int ky = 0; ky < 3; ++ky) {
     const int iy = y - 1 + ky;
@@ -88,55 +91,50 @@ __global__ void dw3x3_kernel(const DwArgs a) {
     for (int kx = 0; kx < 3; ++kx) {
       const int ix = x - 1 + kx;
       if (ix < 0 || ix >= a.W) continue;
-      const float4 v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(iy * a.W + ix) * a.in.cstride));
-      const float4 w = __ldg(reinterpret_cast<const float4*>(a.w + (ky * 3 + kx) * a.C + c));
-      s.x = __fadd_rn(s.x, __fmul_rn(v.x, w.x));
-      s.y = __fadd_rn(s.y, __fmul_rn(v.y, w.y));
-      s.z = __fadd_rn(s.z, __fmul_rn(v.z, w.z));
-      s.w = __fadd_rn(s.w, __fmul_rn(v.w, w.w));
+      float v[8];
+      load8(base + static_cast<long long>(iy * a.W + ix) * a.in.cstride, a.in.plane, v);
+      const float* w = a.w + (ky * 3 + kx) * a.C + c;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s[e] = __fadd_rn(s[e], __fmul_rn(v[e], __ldg(w + e)));
     }
   }
   if (a.act == kActSiLU) {
-    s.x = silu(s.x);
-    s.y = silu(s.y);
-    s.z = silu(s.z);
-    s.w = silu(s.w);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[e] = silu(s[e]);
   }
-  float* o = a.out.ptr + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(p) * a.out.cstride +
-             a.out.coff + c;
-  *reinterpret_cast<float4*>(o) = s;
+  store8(a.out.hi + vaddr(a.out, b, p) + c, a.out.plane, s);
 }
 
 // ------------------------------------------------------------------ max pool
 __global__ void maxpool_kernel(const PoolArgs a) {
-  const int C4 = a.C >> 2;
+  const int C8 = a.C >> 3;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(a.B) * a.Ho * a.Wo * C4;
+  const long long total = static_cast<long long>(a.B) * a.Ho * a.Wo * C8;
   if (idx >= total) return;
-  const int c = static_cast<int>(idx % C4) * 4;
-  const long long pix = idx / C4;
+  const int c = static_cast<int>(idx % C8) * 8;
+  const long long pix = idx / C8;
   const int b = static_cast<int>(pix / (a.Ho * a.Wo));
   const int p = static_cast<int>(pix - static_cast<long long>(b) * a.Ho * a.Wo);
   const int y = (p / a.Wo) * a.stride, x = (p - (p / a.Wo) * a.Wo) * a.stride;
   const int pad = a.k / 2;
-  float4 m = make_float4(-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX);
-  const float* base = a.in.ptr + static_cast<long long>(b) * a.in.bstride + a.in.coff + c;
+  float m[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) m[e] = -FLT_MAX;
+  const uint16_t* base = a.in.hi + vaddr(a.in, b, 0) + c;
   for (int ky = 0; ky < a.k; ++ky) {
     const int iy = y - pad + ky;
     if (iy < 0 || iy >= a.H) continue;
     for (int kx = 0; kx < a.k; ++kx) {
       const int ix = x - pad + kx;
       if (ix < 0 || ix >= a.W) continue;
-      const float4 v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(iy * a.W + ix) * a.in.cstride));
-      if (v.x > m.x) m.x = v.x;
-      if (v.y > m.y) m.y = v.y;
-      if (v.z > m.z) m.z = v.z;
-      if (v.w > m.w) m.w = v.w;
+      float v[8];
+      load8_rw(base + static_cast<long long>(iy * a.W + ix) * a.in.cstride, a.in.plane, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (v[e] > m[e]) m[e] = v[e];
     }
   }
-  float* o = a.out.ptr + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(p) * a.out.cstride +
-             a.out.coff + c;
-  *reinterpret_cast<float4*>(o) = m;
+  store8(a.out.hi + vaddr(a.out, b, p) + c, a.out.plane, m);
 }
 
 // ----------------------------------------------------------------- attention
@@ -156,32 +154,36 @@ __global__ void __launch_bounds__(QB) attention_kernel(const AttnArgs a) {
   const int qi = blockIdx.x * QB + threadIdx.x;
   const bool active = qi < N;
   const int blk = 2 * KD + HD;
-  const float* base = a.qkv.ptr + static_cast<long long>(b) * a.qkv.bstride + a.qkv.coff + h * blk;
+  const uint16_t* base = a.qkv.hi + vaddr(a.qkv, b, 0) + h * blk;
+  const long long pl = a.qkv.plane;
   float q[KD];
   if (active) {
-    const float* qp = base + static_cast<long long>(qi) * a.qkv.cstride;
+    const uint16_t* qp = base + static_cast<long long>(qi) * a.qkv.cstride;
 #pragma unroll
-    for (int d = 0; d < KD; d += 4) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(qp + d));
-      q[d] = v.x;
-      q[d + 1] = v.y;
-      q[d + 2] = v.z;
-      q[d + 3] = v.w;
+    for (int d = 0; d < KD; d += 8) {
+      float v[8];
+      load8(qp + d, pl, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) q[d + e] = v[e];
     }
   } else {
 #pragma unroll
     for (int d = 0; d < KD; ++d) q[d] = 0.f;
   }
+  auto load_k = [&](int k0) {
+    for (int i = threadIdx.x; i < KB * (KD / 8); i += QB) {
+      const int kk = i / (KD / 8), d8 = (i - kk * (KD / 8)) * 8;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (k0 + kk < N) load8(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + KD + d8, pl, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sk[kk][d8 + e] = v[e];
+    }
+  };
   // Pass 1: row maximum of the scaled logits.
   float mx = -FLT_MAX;
   for (int k0 = 0; k0 < N; k0 += KB) {
     __syncthreads();
-    for (int i = threadIdx.x; i < KB * (KD / 4); i += QB) {
-      const int kk = i / (KD / 4), d4 = (i - kk * (KD / 4)) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + kk < N) v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + KD + d4));
-      *reinterpret_cast<float4*>(&sk[kk][d4]) = v;
-    }
+    load_k(k0);
     __syncthreads();
     const int kn = min(KB, N - k0);
     for (int kk = 0; kk < kn; ++kk) {
@@ -198,17 +200,13 @@ __global__ void __launch_bounds__(QB) attention_kernel(const AttnArgs a) {
   float sum = 0.f;
   for (int k0 = 0; k0 < N; k0 += KB) {
     __syncthreads();
-    for (int i = threadIdx.x; i < KB * (KD / 4); i += QB) {
-      const int kk = i / (KD / 4), d4 = (i - kk * (KD / 4)) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + kk < N) v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + KD + d4));
-      *reinterpret_cast<float4*>(&sk[kk][d4]) = v;
-    }
-    for (int i = threadIdx.x; i < KB * (HD / 4); i += QB) {
-      const int kk = i / (HD / 4), d4 = (i - kk * (HD / 4)) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + kk < N) v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + 2 * KD + d4));
-      *reinterpret_cast<float4*>(&sv[kk][d4]) = v;
+    load_k(k0);
+    for (int i = threadIdx.x; i < KB * (HD / 8); i += QB) {
+      const int kk = i / (HD / 8), d8 = (i - kk * (HD / 8)) * 8;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (k0 + kk < N) load8(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + 2 * KD + d8, pl, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sv[kk][d8 + e] = v[e];
     }
     __syncthreads();
     const int kn = min(KB, N - k0);
@@ -226,32 +224,30 @@ __global__ void __launch_bounds__(QB) attention_kernel(const AttnArgs a) {
   const float inv = sum > 1e-12f ? 1.0f / sum : 1.0f;
   // Positional term: depthwise 3x3 of v around the query pixel, + pe bias.
   const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
-  float* op = a.out.ptr + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(qi) * a.out.cstride +
-              a.out.coff + h * HD;
+  uint16_t* op = a.out.hi + vaddr(a.out, b, qi) + h * HD;
 #pragma unroll
-  for (int d0 = 0; d0 < HD; d0 += 4) {
+  for (int d0 = 0; d0 < HD; d0 += 8) {
     const int ch = h * HD + d0;
-    float4 pe = __ldg(reinterpret_cast<const float4*>(a.pe_b + ch));
+    float pe[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) pe[e] = __ldg(a.pe_b + ch + e);
     for (int ky = 0; ky < 3; ++ky) {
       const int iy = y - 1 + ky;
       if (iy < 0 || iy >= a.H) continue;
       for (int kx = 0; kx < 3; ++kx) {
         const int ix = x - 1 + kx;
         if (ix < 0 || ix >= a.W) continue;
-        const float4 v = __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * KD + d0));
-        const float4 w = __ldg(reinterpret_cast<const float4*>(a.pe_w + (ky * 3 + kx) * (a.heads * HD) + ch));
-        pe.x = __fadd_rn(pe.x, __fmul_rn(v.x, w.x));
-        pe.y = __fadd_rn(pe.y, __fmul_rn(v.y, w.y));
-        pe.z = __fadd_rn(pe.z, __fmul_rn(v.z, w.z));
-        pe.w = __fadd_rn(pe.w, __fmul_rn(v.w, w.w));
+        float v[8];
+        load8(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * KD + d0, pl, v);
+        const float* w = a.pe_w + (ky * 3 + kx) * (a.heads * HD) + ch;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v[e], __ldg(w + e)));
       }
     }
-    float4 r;
-    r.x = o[d0] * inv + pe.x;
-    r.y = o[d0 + 1] * inv + pe.y;
-    r.z = o[d0 + 2] * inv + pe.z;
-    r.w = o[d0 + 3] * inv + pe.w;
-    *reinterpret_cast<float4*>(op + d0) = r;
+    float r[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r[e] = o[d0 + e] * inv + pe[e];
+    store8(op + d0, a.out.plane, r);
   }
 }
 
@@ -285,7 +281,7 @@ __global__ void decode_kernel(const DecodeArgs a) {
 }
 
 // -------------------------------------------------------------------- layout
-__global__ void nchw_to_nhwc_kernel(const float* in, int B, int C, int H, int W, OView out) {
+__global__ void nchw_to_split_kernel(const float* in, int B, int C, int H, int W, SOut out) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * C * H * W;
   if (idx >= total) return;
@@ -294,10 +290,14 @@ __global__ void nchw_to_nhwc_kernel(const float* in, int B, int C, int H, int W,
   const long long pix = idx / C;
   const int b = static_cast<int>(pix / hw);
   const long long p = pix - b * hw;
-  out.ptr[b * out.bstride + p * out.cstride + out.coff + c] = in[(static_cast<long long>(b) * C + c) * hw + p];
+  uint32_t hi, lo;
+  split1(in[(static_cast<long long>(b) * C + c) * hw + p], hi, lo);
+  const long long o = vaddr(out, b, p) + c;
+  out.hi[o] = static_cast<uint16_t>(hi);
+  out.hi[o + out.plane] = static_cast<uint16_t>(lo);
 }
 
-__global__ void nhwc_to_nchw_kernel(TView in, int B, int C, int H, int W, float* out) {
+__global__ void split_to_nchw_kernel(SView in, int B, int C, int H, int W, float* out) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * C * H * W;
   if (idx >= total) return;
@@ -306,10 +306,11 @@ __global__ void nhwc_to_nchw_kernel(TView in, int B, int C, int H, int W, float*
   const long long bc = idx / hw;
   const int c = static_cast<int>(bc % C);
   const int b = static_cast<int>(bc / C);
-  out[idx] = in.ptr[b * in.bstride + p * in.cstride + in.coff + c];
+  const long long o = vaddr(in, b, p) + c;
+  out[idx] = join1(in.hi[o], in.hi[o + in.plane]);
 }
 
-__global__ void gather_concat_kernel(TView s0, int c0, int up0, TView s1, int c1, int B, int H, int W, OView out) {
+__global__ void gather_concat_kernel(SView s0, int c0, int up0, SView s1, int c1, int B, int H, int W, SOut out) {
   const int C = c0 + c1;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * H * W * C;
@@ -319,17 +320,25 @@ __global__ void gather_concat_kernel(TView s0, int c0, int up0, TView s1, int c1
   const int b = static_cast<int>(pix / (static_cast<long long>(H) * W));
   const int p = static_cast<int>(pix - static_cast<long long>(b) * H * W);
   const int y = p / W, x = p - (p / W) * W;
-  float v;
+  long long i;
+  const uint16_t* src;
+  long long pl;
   if (c < c0) {
     const int w0 = W / up0;
-    v = s0.ptr[b * s0.bstride + static_cast<long long>((y / up0) * w0 + (x / up0)) * s0.cstride + s0.coff + c];
+    i = vaddr(s0, b, static_cast<long long>((y / up0) * w0 + (x / up0))) + c;
+    src = s0.hi;
+    pl = s0.plane;
   } else {
-    v = s1.ptr[b * s1.bstride + static_cast<long long>(p) * s1.cstride + s1.coff + (c - c0)];
+    i = vaddr(s1, b, p) + (c - c0);
+    src = s1.hi;
+    pl = s1.plane;
   }
-  out.ptr[b * out.bstride + static_cast<long long>(p) * out.cstride + out.coff + c] = v;
+  const long long o = vaddr(out, b, p) + c;
+  out.hi[o] = src[i];
+  out.hi[o + out.plane] = src[i + pl];
 }
 
-__global__ void silu_kernel(OView t, int B, int HW, int C) {
+__global__ void silu_kernel(SOut t, int B, int HW, int C) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * HW * C;
   if (idx >= total) return;
@@ -337,8 +346,11 @@ __global__ void silu_kernel(OView t, int B, int HW, int C) {
   const long long pix = idx / C;
   const int b = static_cast<int>(pix / HW);
   const long long p = pix - static_cast<long long>(b) * HW;
-  float* q = t.ptr + b * t.bstride + p * t.cstride + t.coff + c;
-  *q = silu(*q);
+  const long long o = vaddr(t, b, p) + c;
+  uint32_t hi, lo;
+  split1(silu(join1(t.hi[o], t.hi[o + t.plane])), hi, lo);
+  t.hi[o] = static_cast<uint16_t>(hi);
+  t.hi[o + t.plane] = static_cast<uint16_t>(lo);
 }
 
 }  // namespace
@@ -354,24 +366,22 @@ cudaError_t launch_stem(const StemArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_dwconv3x3(const DwArgs& a, cudaStream_t s) {
-  if (a.C % 4) return cudaErrorInvalidValue;
-  const long long total = static_cast<long long>(a.B) * a.H * a.W * (a.C / 4);
+  if (a.C % 8) return cudaErrorInvalidValue;
+  const long long total = static_cast<long long>(a.B) * a.H * a.W * (a.C / 8);
   dw3x3_kernel<<<blocks_for(total, 256), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {
-  if (a.C % 4) return cudaErrorInvalidValue;
-  const long long total = static_cast<long long>(a.B) * a.H * a.W * (a.C / 4);
+  if (a.C % 8) return cudaErrorInvalidValue;
   PoolArgs b = a;
   if (b.Ho <= 0 || b.Wo <= 0) {
     b.Ho = a.H;
     b.Wo = a.W;
   }
   if (b.stride < 1) return cudaErrorInvalidValue;
-  const long long total_out = static_cast<long long>(b.B) * b.Ho * b.Wo * (b.C / 4);
-  (void)total;
-  maxpool_kernel<<<blocks_for(total_out, 256), 256, 0, s>>>(b);
+  const long long total = static_cast<long long>(b.B) * b.Ho * b.Wo * (b.C / 8);
+  maxpool_kernel<<<blocks_for(total, 256), 256, 0, s>>>(b);
   return cudaGetLastError();
 }
 
@@ -390,26 +400,26 @@ cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_nchw_to_nhwc(const float* in, int B, int C, int H, int W, OView out, cudaStream_t s) {
+cudaError_t launch_nchw_to_split(const float* in, int B, int C, int H, int W, SOut out, cudaStream_t s) {
   const long long total = static_cast<long long>(B) * C * H * W;
-  nchw_to_nhwc_kernel<<<blocks_for(total, 256), 256, 0, s>>>(in, B, C, H, W, out);
+  nchw_to_split_kernel<<<blocks_for(total, 256), 256, 0, s>>>(in, B, C, H, W, out);
   return cudaGetLastError();
 }
 
-cudaError_t launch_nhwc_to_nchw(TView in, int B, int C, int H, int W, float* out, cudaStream_t s) {
+cudaError_t launch_split_to_nchw(SView in, int B, int C, int H, int W, float* out, cudaStream_t s) {
   const long long total = static_cast<long long>(B) * C * H * W;
-  nhwc_to_nchw_kernel<<<blocks_for(total, 256), 256, 0, s>>>(in, B, C, H, W, out);
+  split_to_nchw_kernel<<<blocks_for(total, 256), 256, 0, s>>>(in, B, C, H, W, out);
   return cudaGetLastError();
 }
 
-cudaError_t launch_gather_concat(TView src0, int c0, int up0, TView src1, int c1, int B, int H, int W, OView out,
+cudaError_t launch_gather_concat(SView src0, int c0, int up0, SView src1, int c1, int B, int H, int W, SOut out,
                                  cudaStream_t s) {
   const long long total = static_cast<long long>(B) * H * W * (c0 + c1);
   gather_concat_kernel<<<blocks_for(total, 256), 256, 0, s>>>(src0, c0, up0, src1, c1, B, H, W, out);
   return cudaGetLastError();
 }
 
-cudaError_t launch_silu(OView t, int B, int HW, int C, cudaStream_t s) {
+cudaError_t launch_silu(SOut t, int B, int HW, int C, cudaStream_t s) {
   const long long total = static_cast<long long>(B) * HW * C;
   silu_kernel<<<blocks_for(total, 256), 256, 0, s>>>(t, B, HW, C);
   return cudaGetLastError();
