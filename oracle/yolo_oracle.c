@@ -177,6 +177,11 @@ static void conv(fmap* out, const fmap* in, const orc_tensor* w, const orc_tenso
     const int H = in->h, W = in->w, Ho = out->h, Wo = out->w;
     if (kh == 1 && kw == 1 && stride == 1 && pad == 0) {
         const int P = H * W;
+        /* tensor_gemm's AVX2 loop fuses multiply-add on 16- and 8-wide blocks
+         * of columns and leaves a scalar tail computed as multiply then add
+         * (tensor.c:83-109, built without FP contraction). */
+        const int P16 = (P / 16) * 16;
+        const int Pv = P16 + ((P - P16) >= 8 ? 8 : 0);
         for (int o = 0; o < oc; ++o) {
             float* y = out->d + (size_t)o * P;
             for (int p = 0; p < P; ++p) y[p] = 0.0f;
@@ -184,7 +189,11 @@ static void conv(fmap* out, const fmap* in, const orc_tensor* w, const orc_tenso
                 const float a = w->data[(size_t)o * ic + c];
                 if (a == 0.0f) continue;
                 const float* x = in->d + (size_t)c * P;
-                for (int p = 0; p < P; ++p) y[p] = fmaf(a, x[p], y[p]);
+                for (int p = 0; p < Pv; ++p) y[p] = fmaf(a, x[p], y[p]);
+                for (int p = Pv; p < P; ++p) {
+                    const float prod = a * x[p];
+                    y[p] = y[p] + prod;
+                }
             }
             if (b)
                 for (int p = 0; p < P; ++p) y[p] += b->data[o];
@@ -349,20 +358,27 @@ static int c3(orc_model* m, const char* P, int shortcut, fmap* out, const fmap* 
 }
 
 /* C3k2 with inner C3k (model.c:415-557). */
+/* The reference wires exactly one C3k (m.0); C3k blocks m.1, m.2, ... when
+ * present chain on the previous block's output as in the C2f layout
+ * (cat(a, b, m0(b), m1(m0(b)), ...) -> cv2), which is identical for n = 1. */
 static int c3k2_c3k(orc_model* m, const char* L, fmap* out, const fmap* in) {
     char nm[220];
     orc_tensor* w1 = findf(m, "%s.cv1.conv.weight", L);
     orc_tensor* k3 = findf(m, "%s.m.0.cv3.conv.weight", L);
     if (!w1 || !k3) return ORC_ERR_MISSING;
     const int ch = w1->dims[0] / 2;
-    fmap cat = fm_new(2 * ch + k3->dims[0], in->h, in->w);
+    int n = 0;
+    while (findf(m, "%s.m.%d.cv3.conv.weight", L, n)) ++n;
+    fmap cat = fm_new(2 * ch + n * k3->dims[0], in->h, in->w);
     fmap a = fm_view(&cat, 0, 2 * ch);
     snprintf(nm, sizeof nm, "%s.cv1", L);
     int st = conv_named(m, nm, &a, in, 1, 0, 1);
-    fmap b = fm_view(&cat, ch, ch);
-    fmap o = fm_view(&cat, 2 * ch, k3->dims[0]);
-    snprintf(nm, sizeof nm, "%s.m.0", L);
-    if (st == ORC_OK) st = c3(m, nm, 1, &o, &b);
+    for (int i = 0; i < n && st == ORC_OK; ++i) {
+        fmap b = fm_view(&cat, i == 0 ? ch : 2 * ch + (i - 1) * k3->dims[0], i == 0 ? ch : k3->dims[0]);
+        fmap o = fm_view(&cat, 2 * ch + i * k3->dims[0], k3->dims[0]);
+        snprintf(nm, sizeof nm, "%s.m.%d", L, i);
+        st = c3(m, nm, 1, &o, &b);
+    }
     snprintf(nm, sizeof nm, "%s.cv2", L);
     if (st == ORC_OK) st = conv_named(m, nm, out, &cat, 1, 0, 1);
     fm_free(&cat);
