@@ -285,11 +285,18 @@ def run_ours(args):
         yb.check(L.yb_cuda_forward(model.ctx, host_in.data_ptr(), B, H, H, host_out.data_ptr(), 300, None, None, None),
                  "yb_cuda_forward")
 
-    e2e_step()  # builds the plan and leaves this rank's images resident in HBM
+    e2e_step()  # builds the pipelined plans (16-image sub-batches)
+    # Device-resident leg: the whole batch as one plan; its input buffer is
+    # filled once with this rank's images, outside the timed region.
     d_in, d_out = model.plan_io(B, H, H)
+    dev_imgs = host_in.to(f"cuda:{local}")
     # A dedicated stream: the library launches on exactly this stream, so the
     # CUDA events below bracket the forward's kernels.
     stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    model.forward_device(dev_imgs.data_ptr(), d_out, B, H, H, 300, stream.cuda_stream)
+    torch.cuda.synchronize()
+    del dev_imgs
 
     def dev_step():
         model.forward_device(d_in, d_out, B, H, H, 300, stream.cuda_stream)

@@ -52,7 +52,11 @@ status_t yb_cuda_load_bin(void* ctx, const char* path);
  * when they are in out_dets.  dump (nullable) receives the stage tensors;
  * step_ms (nullable, MODEL_FORWARD_PROFILE_STEPS doubles) receives per-step
  * device times.  Either one makes the forward run eagerly instead of from the
- * captured graph. */
+ * captured graph.  Without them, a batch of B >= 32 images with B a multiple
+ * of 16 is pipelined: 16-image sub-batches alternate between two captured
+ * graphs so that each sub-batch's input copy overlaps the previous one's
+ * compute (use pinned host buffers for the overlap to happen); the head
+ * tensors of such a forward are not kept (yb_cuda_get_head). */
 status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int H, int W,
                          float* out_dets, int max_det,
                          yb_stage_cb dump, void* user, double* step_ms);
@@ -69,7 +73,8 @@ status_t yb_cuda_forward_device(void* ctx, const float* d_in, int B, int H, int 
  * graph with no extra device copies. */
 status_t yb_cuda_plan_io(void* ctx, int B, int H, int W, int max_det, float** d_in, float** d_out);
 
-/* Copies the head tensors of the last forward, image-major:
+/* Copies the head tensors of the last forward, image-major (not available
+ * after a pipelined yb_cuda_forward: ERROR_INVALID_DIMS):
  * logits [B,N,nc] (pre-sigmoid class logits) and boxes [B,N,4] (xyxy pixels),
  * N = anchors per image.  Either pointer may be NULL.  *n_anchors and *nc
  * receive N and nc when non-NULL. */

@@ -78,6 +78,29 @@ def test_batch_equals_single(model_n0):
         assert np.array_equal(batch[i], single), i
 
 
+def test_pipelined_batch_equals_device_batch(model_n0):
+    """A host batch of 48 runs as three pipelined 16-image sub-batches; it gives
+    the same detections as the one-plan device forward of the same 48 images,
+    bit for bit, and keeps no head tensors."""
+    import torch
+
+    import yb_weights as yw
+
+    B, H, W = 48, 128, 160
+    imgs = yw.make_batch(range(100, 100 + B), H, W)
+    piped = model_n0.forward(imgs)["dets"]
+    with pytest.raises(RuntimeError):
+        model_n0.head(B)
+    d_in = torch.from_numpy(imgs).cuda()
+    d_out = torch.empty((B, 300, 6), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    model_n0.forward_device(d_in.data_ptr(), d_out.data_ptr(), B, H, W)
+    torch.cuda.synchronize()
+    dev = d_out.cpu().numpy()
+    for i in range(B):
+        assert np.array_equal(piped[i], dev[i]), i
+
+
 def test_repeatable(model_n0):
     import yb_weights as yw
 

@@ -42,7 +42,8 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kProducerWarps = 4;
+constexpr int kProducerWarps = 8;  // two per sub-partition: the im2col address stream is the long pole
+constexpr int kRowsPerThread = kBM * 8 / (kProducerWarps * 32);  // 16-byte columns per row = 8
 constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, splitting the columns
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
@@ -118,31 +119,51 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
   if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producers
     // Thread t copies the 16-byte column j = t % 8 (8 K indices) of rows
-    // t / 8 + 16 i, i = 0..7, for both planes.
+    // t / 8 + 32 i, i = 0..3, for both planes.  Per tile each row's pixel
+    // offset in both sources is computed once; per chunk only the tap and
+    // channel of column j change, so a copy costs a few adds and compares.
     const int ptid = threadIdx.x;
     const int j = ptid & 7;
     const int r0 = ptid >> 3;
     uint32_t it = 0;  // chunks issued
     const uint32_t smem_base = smem_u32(smem);
+    const int ws0 = a.W >> a.lg_up0, ws1 = a.W >> a.lg_up1;
+    const float inv_ci = 1.0f / static_cast<float>(a.Ci);
+    uint32_t row_off[kRowsPerThread];
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i)
+      row_off[i] = sw128_offset(static_cast<uint32_t>(r0 + 32 * i), static_cast<uint32_t>(j));
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const int mt = t / a.n_tiles;
       const int nt = t - mt * a.n_tiles;
-      const int m0 = mt * kBM;
-      int rb[8], ry[8], rx[8];
+      int iy0[kRowsPerThread], ix0[kRowsPerThread];
+      long long off0[kRowsPerThread], off1[kRowsPerThread];
+      {
+        // Row r0 of the tile, then step 32 pixels per row without dividing.
+        const int m = mt * kBM + r0;
+        int b = m / HoWo;
+        int r = m - b * HoWo;
+        int oy = r / a.Wo;
+        int ox = r - oy * a.Wo;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int m = m0 + r0 + 16 * i;
-        if (m < M) {
-          const int b = m / HoWo;
-          const int r = m - b * HoWo;
-          const int oy = r / a.Wo;
-          rb[i] = b;
-          ry[i] = oy * a.stride - a.pad;
-          rx[i] = (r - oy * a.Wo) * a.stride - a.pad;
-        } else {
-          rb[i] = 0;
-          ry[i] = -(1 << 28);  // never in bounds
-          rx[i] = 0;
+        for (int i = 0; i < kRowsPerThread; ++i) {
+          const bool valid = m + 32 * i < M;
+          const int iy = oy * a.stride - a.pad;
+          const int ix = ox * a.stride - a.pad;
+          iy0[i] = valid ? iy : -(1 << 28);  // never in bounds
+          ix0[i] = ix;
+          off0[i] = static_cast<long long>(b) * a.src0.bstride +
+                    static_cast<long long>((iy >> a.lg_up0) * ws0 + (ix >> a.lg_up0)) * a.src0.cstride;
+          off1[i] = static_cast<long long>(b) * a.src1.bstride +
+                    static_cast<long long>((iy >> a.lg_up1) * ws1 + (ix >> a.lg_up1)) * a.src1.cstride;
+          ox += 32;
+          while (ox >= a.Wo) {
+            ox -= a.Wo;
+            if (++oy == a.Ho) {
+              oy = 0;
+              ++b;
+            }
+          }
         }
       }
       const uint8_t* wsrc = a.wpack + static_cast<size_t>(nt) * a.num_kc * chunk_bytes;
@@ -162,34 +183,28 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
         }
         const int k = kc * kBK + j * 8;
         const bool kvalid = k < a.K;
-        int ky = 0, kx = 0, c = 0;
-        if (kvalid) {
-          const int tap = k / a.Ci;
-          c = k - tap * a.Ci;
-          ky = tap / a.kw;
-          kx = tap - ky * a.kw;
-        }
+        // tap = k / Ci via a float reciprocal with an exact integer fix-up.
+        int tap = __float2int_rz(static_cast<float>(k) * inv_ci);
+        if (tap * a.Ci > k) --tap;
+        if ((tap + 1) * a.Ci <= k) ++tap;
+        const int c = k - tap * a.Ci;
+        int ky = 0;
+        while ((ky + 1) * a.kw <= tap) ++ky;
+        const int kx = tap - ky * a.kw;
         const bool first = c < a.c_split;
         const uint16_t* sp = first ? a.src0.hi : a.src1.hi;
         const long long splane = first ? a.src0.plane : a.src1.plane;
-        const long long sbs = first ? a.src0.bstride : a.src1.bstride;
-        const int scs = first ? a.src0.cstride : a.src1.cstride;
-        const int sco = first ? a.src0.coff + c : a.src1.coff + (c - a.c_split);
-        const int lg = first ? a.lg_up0 : a.lg_up1;
-        const int ws = a.W >> lg;
+        const int tap_off = first ? (ky * ws0 + kx) * a.src0.cstride + a.src0.coff + c
+                                  : (ky * ws1 + kx) * a.src1.cstride + a.src1.coff + (c - a.c_split);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int row = r0 + 16 * i;
-          const int iy = ry[i] + ky;
-          const int ix = rx[i] + kx;
+        for (int i = 0; i < kRowsPerThread; ++i) {
+          const int iy = iy0[i] + ky;
+          const int ix = ix0[i] + kx;
           const bool ok = kvalid && static_cast<unsigned>(iy) < static_cast<unsigned>(a.H) &&
                           static_cast<unsigned>(ix) < static_cast<unsigned>(a.W);
-          const uint16_t* p = ok ? sp + static_cast<long long>(rb[i]) * sbs +
-                                       static_cast<long long>((iy >> lg) * ws + (ix >> lg)) * scs + sco
-                                 : sp;
-          const uint32_t off = sw128_offset(static_cast<uint32_t>(row), static_cast<uint32_t>(j));
-          cp_async16(sa_hi + off, p, ok ? 16u : 0u);
-          cp_async16(sa_lo + off, p + (ok ? splane : 0), ok ? 16u : 0u);
+          const uint16_t* p = ok ? sp + (first ? off0[i] : off1[i]) + tap_off : sp;
+          cp_async16(sa_hi + row_off[i], p, ok ? 16u : 0u);
+          cp_async16(sa_lo + row_off[i], p + (ok ? splane : 0), ok ? 16u : 0u);
         }
         // The stage is published by the copies themselves: this thread's
         // arrival on full[s] fires when all its copies so far have landed.
@@ -310,20 +325,19 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
           // before the tensor core's (async-proxy) operand reads.
           fence_proxy_async_smem();
           tc_fence_after();
+          // Descriptors of the stage's four operand planes; a 16-wide K step
+          // advances the start address by 32 bytes (2 in the >>4 field).
           const uint32_t a_hi = smem_u32(smem + s * stage_bytes);
-          const uint32_t a_lo = a_hi + kAPlaneBytes;
-          const uint32_t b_hi = a_hi + 2 * kAPlaneBytes;
-          const uint32_t b_lo = b_hi + static_cast<uint32_t>(a.n_tile) * 128u;
+          const uint64_t dah0 = sw128_kmajor_desc(a_hi);
+          const uint64_t dal0 = sw128_kmajor_desc(a_hi + kAPlaneBytes);
+          const uint64_t dbh0 = sw128_kmajor_desc(a_hi + 2 * kAPlaneBytes);
+          const uint64_t dbl0 = sw128_kmajor_desc(a_hi + 2 * kAPlaneBytes + static_cast<uint32_t>(a.n_tile) * 128u);
 #pragma unroll
           for (int ks = 0; ks < kBK / 16; ++ks) {
-            const uint32_t koff = ks * 32;
-            const uint64_t dah = sw128_kmajor_desc(a_hi + koff);
-            const uint64_t dal = sw128_kmajor_desc(a_lo + koff);
-            const uint64_t dbh = sw128_kmajor_desc(b_hi + koff);
-            const uint64_t dbl = sw128_kmajor_desc(b_lo + koff);
-            tc_mma_bf16(d_tmem, dah, dbh, idesc, (kc | ks) != 0 ? 1u : 0u);
-            tc_mma_bf16(d_tmem, dah, dbl, idesc, 1u);
-            tc_mma_bf16(d_tmem, dal, dbh, idesc, 1u);
+            const uint64_t koff = static_cast<uint64_t>(ks * 2);
+            tc_mma_bf16(d_tmem, dah0 + koff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
+            tc_mma_bf16(d_tmem, dah0 + koff, dbl0 + koff, idesc, 1u);
+            tc_mma_bf16(d_tmem, dal0 + koff, dbh0 + koff, idesc, 1u);
           }
           tc_commit(&empty[s]);
         }
@@ -424,6 +438,10 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
   const bool f32 = a.out_f32.ptr != nullptr;
   if (a.n_tile < 16 || a.n_tile > 256 || (a.n_tile % 16) != 0 || a.Ci % 8 != 0 || a.c_split % 8 != 0 ||
       a.Co % (f32 ? 4 : 8) != 0)
+    return cudaErrorInvalidValue;
+  // Upsampled sources are read by 1x1, stride-1, unpadded convolutions only
+  // (the producer resolves their pixel once per row, not per tap).
+  if ((a.lg_up0 || a.lg_up1) && (a.kh != 1 || a.kw != 1 || a.stride != 1 || a.pad != 0))
     return cudaErrorInvalidValue;
   const int stages = stages_for(a.n_tile);
   if (stages < 2) return cudaErrorInvalidValue;

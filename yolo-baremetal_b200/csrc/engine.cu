@@ -822,9 +822,9 @@ cudaError_t Engine::profile_ops(Plan* p, int reps, std::vector<double>* ms) {
   return e;
 }
 
-cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::string* why) {
+cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::string* why, int slot) {
   for (auto& p : plans_) {
-    if (p->B == B && p->H == H && p->W == W && p->max_det == max_det) {
+    if (p->B == B && p->H == H && p->W == W && p->max_det == max_det && p->slot == slot) {
       *out = p.get();
       return cudaSuccess;
     }
@@ -843,6 +843,7 @@ cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::
   p->H = H;
   p->W = W;
   p->max_det = max_det;
+  p->slot = slot;
   cudaError_t e = build(p.get(), why);
   if (e != cudaSuccess) {
     release_plan(p.get());

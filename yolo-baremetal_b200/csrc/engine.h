@@ -75,6 +75,7 @@ struct Op {
 struct Plan {
   int B = 0, H = 0, W = 0;
   int max_det = 300;
+  int slot = 0;  // several plans of one shape can coexist (pipelined forwards)
   std::vector<Op> ops;
   std::vector<void*> allocs;
   float* d_in = nullptr;    // [B,3,H,W]
@@ -100,8 +101,9 @@ class Engine {
   cudaError_t set_weights(WeightMap&& w, int num_classes, std::string* why);
   bool has_weights() const { return !hw_.empty(); }
 
-  // Plan for (B, H, W, max_det), built and captured on first use.
-  cudaError_t get_plan(int B, int H, int W, int max_det, Plan** out, std::string* why);
+  // Plan for (B, H, W, max_det), built and captured on first use.  Plans with
+  // different `slot` values have separate buffers and graphs.
+  cudaError_t get_plan(int B, int H, int W, int max_det, Plan** out, std::string* why, int slot = 0);
 
   // Enqueues the forward of `p` on `s` (graph launch, or eager when
   // step_events != nullptr: then events[2*step], events[2*step+1] bracket

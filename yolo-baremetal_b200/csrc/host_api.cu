@@ -73,7 +73,15 @@ struct Ctx {
   size_t h_stage_bytes = 0;
   bool inflight = false;
   int stall_ms = 0;  // host-side fault injection for deadline tests
+  // Pipelined host forwards: input copies run on copy_stream while the
+  // previous sub-batch computes; one event pair per plan slot.
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t in_ready[2] = {nullptr, nullptr};
+  cudaEvent_t slot_free[2] = {nullptr, nullptr};
 };
+
+// Sub-batch of a pipelined host forward (yb_cuda_forward with B >= 2 chunks).
+constexpr int kPipeChunk = 16;
 
 namespace {
 
@@ -100,9 +108,9 @@ status_t check_kernel_flag(Ctx* c) {
   return SUCCESS;
 }
 
-status_t plan_for(Ctx* c, int B, int H, int W, int max_det, Plan** p) {
+status_t plan_for(Ctx* c, int B, int H, int W, int max_det, Plan** p, int slot = 0) {
   std::string why;
-  cudaError_t e = c->eng->get_plan(B, H, W, max_det, p, &why);
+  cudaError_t e = c->eng->get_plan(B, H, W, max_det, p, &why, slot);
   if (e == cudaSuccess) return SUCCESS;
   if (e == cudaErrorInvalidValue) {
     set_error("plan: " + why);
@@ -238,6 +246,12 @@ extern "C" status_t yb_cuda_init(int device, void** ctx) {
   if ((e = cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming)) != cudaSuccess ||
       (e = cudaEventCreateWithFlags(&c->h2d_done, cudaEventDisableTiming)) != cudaSuccess)
     return cuda_status(e, "cudaEventCreate");
+  if ((e = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking)) != cudaSuccess)
+    return cuda_status(e, "cudaStreamCreate");
+  for (int i = 0; i < 2; ++i)
+    if ((e = cudaEventCreateWithFlags(&c->in_ready[i], cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&c->slot_free[i], cudaEventDisableTiming)) != cudaSuccess)
+      return cuda_status(e, "cudaEventCreate");
   *ctx = c.release();
   return SUCCESS;
 }
@@ -251,6 +265,14 @@ extern "C" status_t yb_cuda_destroy(void* ctx) {
     if (ev) cudaEventDestroy(ev);
   if (c->done) cudaEventDestroy(c->done);
   if (c->h2d_done) cudaEventDestroy(c->h2d_done);
+  for (int i = 0; i < 2; ++i) {
+    if (c->in_ready[i]) cudaEventDestroy(c->in_ready[i]);
+    if (c->slot_free[i]) cudaEventDestroy(c->slot_free[i]);
+  }
+  if (c->copy_stream) {
+    cudaStreamSynchronize(c->copy_stream);
+    cudaStreamDestroy(c->copy_stream);
+  }
   if (c->h_stage) cudaFreeHost(c->h_stage);
   c->eng.reset();
   delete c;
@@ -307,8 +329,50 @@ extern "C" status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int 
   status_t st = ctx_ready(c);
   if (st != SUCCESS) return st;
   Plan* p = nullptr;
-  if ((st = plan_for(c, B, H, W, max_det, &p)) != SUCCESS) return st;
   cudaStream_t s = c->eng->stream();
+  if (!dump && !step_ms && B >= 2 * kPipeChunk && B % kPipeChunk == 0) {
+    // Pipelined: sub-batches of kPipeChunk images alternate between two plans.
+    // Chunk i's input copy (copy stream) overlaps chunk i-1's graph (compute
+    // stream); a slot's input is refilled only after its previous graph ran.
+    Plan* slots[2] = {nullptr, nullptr};
+    for (int k = 0; k < 2; ++k)
+      if ((st = plan_for(c, kPipeChunk, H, W, max_det, &slots[k], 1 + k)) != SUCCESS) return st;
+    const size_t in_elems = static_cast<size_t>(kPipeChunk) * 3 * H * W;
+    const size_t det_elems = static_cast<size_t>(kPipeChunk) * max_det * 6;
+    const int n = B / kPipeChunk;
+    // Input copy of chunk j into its slot, after the slot's previous graph.
+    auto prefetch = [&](int j) {
+      const int k = j & 1;
+      cudaError_t r = j >= 2 ? cudaStreamWaitEvent(c->copy_stream, c->slot_free[k], 0) : cudaSuccess;
+      if (r == cudaSuccess)
+        r = cudaMemcpyAsync(slots[k]->d_in, in_nchw + j * in_elems, in_elems * 4, cudaMemcpyHostToDevice,
+                            c->copy_stream);
+      if (r == cudaSuccess) r = cudaEventRecord(c->in_ready[k], c->copy_stream);
+      return r;
+    };
+    cudaError_t e = prefetch(0);
+    for (int i = 0; i < n && e == cudaSuccess; ++i) {
+      const int k = i & 1;
+      Plan* q = slots[k];
+      e = cudaStreamWaitEvent(s, c->in_ready[k], 0);
+      if (e == cudaSuccess) e = c->eng->run(q, s, nullptr);
+      // The next input copy is enqueued before this chunk's result copy, which
+      // blocks the host when out_dets is pageable.
+      if (e == cudaSuccess && i + 1 < n) e = prefetch(i + 1);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(out_dets + i * det_elems, q->d_out, det_elems * 4, cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess) e = cudaEventRecord(c->slot_free[k], s);
+    }
+    // Head tensors of a pipelined forward are spread over both slots and
+    // partly overwritten; yb_cuda_get_head reports that none are kept.
+    c->last = nullptr;
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    const cudaError_t e2 = cudaStreamSynchronize(c->copy_stream);
+    if (e == cudaSuccess) e = e2;
+    if (e != cudaSuccess) return cuda_status(e, "pipelined forward");
+    return check_kernel_flag(c);
+  }
+  if ((st = plan_for(c, B, H, W, max_det, &p)) != SUCCESS) return st;
   cudaError_t e = cudaMemcpyAsync(p->d_in, in_nchw, static_cast<size_t>(B) * 3 * H * W * 4, cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return cuda_status(e, "input copy");
   if (step_ms) {
@@ -375,7 +439,7 @@ extern "C" status_t yb_cuda_get_head(void* ctx, float* logits, float* boxes, int
   if (st != SUCCESS) return st;
   Plan* p = c->last;
   if (!p) {
-    set_error("no forward has run on this context");
+    set_error("no head tensors kept: no forward has run on this context, or the last one was pipelined");
     return ERROR_INVALID_DIMS;
   }
   cudaError_t e = cudaStreamSynchronize(c->eng->stream());
