@@ -80,6 +80,31 @@ status_t yb_cuda_plan_io(void* ctx, int B, int H, int W, int max_det, float** d_
  * receive N and nc when non-NULL. */
 status_t yb_cuda_get_head(void* ctx, float* logits, float* boxes, int* n_anchors, int* nc);
 
+/* Detect-head top-k on head tensors already in GPU memory, allocating
+ * nothing.  No counterpart in the reference (its top-k,
+ * detect_postprocess_from_pred, works on host memory).  For callers that
+ * cannot allocate device memory: a serving process whose GPU memory is all
+ * owned by its own pool allocator, or a per-frame loop that cannot take the
+ * stall of cudaMalloc/cudaFree (cudaFree waits for all work on the device).
+ *
+ * d_logits [B,N,nc] pre-sigmoid class logits and d_boxes [B,N,4] xyxy, as
+ * yb_cuda_get_head returns them; d_dets [B,max_det,6] receives
+ * [x1,y1,x2,y2,score,class] rows in the order of yb_cuda_forward's output,
+ * rows beyond min(max_det, N) zero-filled.  All three on the current device.
+ * Enqueued on `stream` (a cudaStream_t; NULL = the default stream); does not
+ * synchronize.
+ *
+ * Scratch (the per-anchor best scores) lives in one fixed array of 2^20
+ * floats (4 MiB) inside the library's device code, held by every GPU that
+ * loads the library until the process exits: B*N above 1048576 anchors, or
+ * min(max_det, N) above 1024, returns ERROR_INVALID_DIMS before any launch.
+ * The first call on each device looks the array's address up (with that
+ * device current); make that first call before any stream capture.  All calls
+ * on a device share the array, so calls that overlap in time (other streams,
+ * other threads) race: order them on one stream or with events. */
+status_t yb_cuda_detect_topk_noalloc(const float* d_logits, const float* d_boxes, int B, int N, int nc,
+                                     int max_det, float* d_dets, void* stream);
+
 /* Image-sharded forward over G contexts (one per GPU): image range
  * [g*B/G, (g+1)*B/G) runs on ctxs[g] from its own host thread; results land
  * at the matching rows of out_dets.  Each shard is waited on with a host

@@ -37,7 +37,8 @@ EXPORTS = {
     "detection.h": ["decode_detections"],
     "utils.h": ["timer_start", "timer_stop", "timer_elapsed_ms", "load_named_tensor", "save_named_tensor", "fold_bn"],
     "yb_cuda.h": ["yb_cuda_init", "yb_cuda_upload_weights", "yb_cuda_load_bin", "yb_cuda_forward",
-                  "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_forward_sharded",
+                  "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_detect_topk_noalloc",
+                  "yb_cuda_forward_sharded",
                   "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error"],
 }
 
@@ -94,6 +95,8 @@ def lib() -> C.CDLL:
         L.yb_cuda_forward_device.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
                                              C.c_void_p]
         L.yb_cuda_get_head.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.yb_cuda_detect_topk_noalloc.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                  C.c_void_p, C.c_void_p]
         L.yb_cuda_forward_sharded.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                               C.c_void_p, C.c_int, C.c_int]
         L.yb_cuda_debug_inject_stall.argtypes = [C.c_void_p, C.c_int]
