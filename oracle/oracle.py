@@ -67,6 +67,8 @@ class Oracle:
             lib.orc_sppf.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int, C.c_int,
                                      C.c_int, _f32p, C.c_int]
             lib.orc_c2psa.argtypes = [C.c_void_p, C.c_char_p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int]
+            lib.orc_c3.argtypes = [C.c_void_p, C.c_char_p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int]
+            lib.orc_psablock.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
             lib.orc_dwconv.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
             cls._lib = lib
         return cls._lib

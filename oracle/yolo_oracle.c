@@ -891,6 +891,16 @@ int orc_c2psa(void* h, const char* prefix, int n_blocks, const float* in, int c,
     return c2psa((orc_model*)h, prefix, n_blocks, 0.5f, 0.5f, &y, &x);
 }
 
+int orc_c3(void* h, const char* prefix, int shortcut, const float* in, int c, int hh, int ww, float* out, int co) {
+    fmap x = {(float*)in, c, hh, ww}, y = {out, co, hh, ww};
+    return c3((orc_model*)h, prefix, shortcut, &y, &x);
+}
+
+int orc_psablock(void* h, const char* prefix, const float* in, int c, int hh, int ww, int heads, float* out) {
+    fmap x = {(float*)in, c, hh, ww}, y = {out, c, hh, ww};
+    return psablock((orc_model*)h, prefix, heads, 0.5f, 1, &y, &x);
+}
+
 int orc_dwconv(void* h, const char* prefix, const float* in, int c, int hh, int ww, int act, float* out) {
     orc_model* m = (orc_model*)h;
     orc_tensor* w = findf(m, "%s.conv.weight", prefix);

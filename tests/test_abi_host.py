@@ -167,3 +167,42 @@ def test_no_device_fails_cleanly():
     st = yb.lib().yb_cuda_init(0, C.byref(ctx))
     assert st != yb.SUCCESS and not ctx.value
     assert yb.last_error()
+
+
+def test_fold_bn_matches_oracle():
+    """fold_bn (utils.c:81-106 arithmetic) on the reference's raw Conv+BN
+    records gives the oracle's folded weights and bias bit for bit."""
+    import yolo_b200 as yb
+    from conftest import golden
+    from oracle import Oracle
+
+    r = golden("c3k2_test.bin")
+    o = Oracle(nc=80)
+    for k, v in r.items():
+        if k not in ("input", "output"):
+            o.add(f"X.{k}", v if v.ndim else v.reshape(1))
+    o.fold()
+    for prefix in ("cv1", "m.0.m.1.cv2", "m.1.cv3"):
+        w = np.array(r[f"{prefix}.conv.weight"], dtype=np.float32, copy=True)
+        b = np.zeros(w.shape[0], dtype=np.float32)
+        tv = lambda a: C.byref(yb.tensor_view(a))  # noqa: E731
+        yb.lib().fold_bn(tv(w), tv(b), tv(r[f"{prefix}.bn.weight"]), tv(r[f"{prefix}.bn.bias"]),
+                         tv(r[f"{prefix}.bn.running_mean"]), tv(r[f"{prefix}.bn.running_var"]))
+        assert np.array_equal(w.reshape(-1), o.get(f"X.{prefix}.conv.weight")), prefix
+        assert np.array_equal(b, o.get(f"X.{prefix}.conv.bias")), prefix
+
+
+def test_tensor_view_keeps_its_array_alive():
+    """A tensor_t view over a temporary array stays valid after the caller drops it."""
+    import gc
+    import weakref
+
+    import yolo_b200 as yb
+
+    a = np.arange(12, dtype=np.float32)
+    wr = weakref.ref(a)
+    t = yb.tensor_view(a)
+    del a
+    gc.collect()
+    assert wr() is not None
+    assert np.ctypeslib.as_array(t.data, shape=(12,))[11] == 11.0

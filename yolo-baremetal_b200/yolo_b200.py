@@ -129,6 +129,7 @@ def tensor_view(a: np.ndarray) -> Tensor:
     t.dims[:] = dims
     t.stride[:] = [dims[1] * dims[2] * dims[3], dims[2] * dims[3], dims[3], 1]
     t.is_owner = False
+    t._array = a  # the view must keep its array alive: tensor_t holds only the raw pointer
     return t
 
 
