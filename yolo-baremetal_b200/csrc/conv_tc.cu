@@ -12,26 +12,32 @@
 // kind::f16 UMMAs, hi*hi + hi*lo + lo*hi, accumulating in fp32 in tensor
 // memory.
 //
-// Persistent, warp-specialised CTA (288 threads, one CTA per SM):
-//   warps 0-3  producers: each K chunk of the activation tile is gathered with
-//              16-byte cp.async copies straight from the hi and lo planes into
-//              the 128B-swizzled K-major operand layout (zero fill for padding
-//              and K tails; upsample and two-source concat in the address
-//              computation), kept PD chunks deep, then published on the
-//              stage's mbarrier.  Thread 0 also starts one bulk copy (TMA
-//              engine) of the pre-packed, pre-swizzled weight chunk.
-//   warp 8     allocates tensor memory (two accumulators) and, from one lane,
-//              issues the UMMAs; tcgen05.commit frees each smem stage and
-//              publishes each finished accumulator.
-//   warps 4-7  epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 output
-//              pixels), + bias, SiLU, + residual, split (or fp32) NHWC store
-//              into the destination channel slice.  Runs while warp 8
-//              accumulates the next tile into the other TMEM buffer.
+// Persistent, warp-specialised CTA (544 threads, one CTA per SM):
+//   warps 0-7   producers: each K chunk of the activation tile is gathered
+//               with 16-byte cp.async copies straight from the hi and lo
+//               planes into the 128B-swizzled K-major operand layout (zero
+//               fill for padding and K tails; upsample and two-source concat
+//               in the address computation), several stages deep; each
+//               thread's copies arrive on the stage's mbarrier as they land.
+//               Thread 0 also starts one bulk copy (TMA engine) of the
+//               pre-packed, pre-swizzled weight chunk.
+//   warp 16     allocates tensor memory (2-4 accumulators) and, from one
+//               lane, issues the UMMAs; tcgen05.commit frees each smem stage
+//               and publishes each finished accumulator.
+//   warps 8-15  epilogue in two groups of four taking alternate tiles, one
+//               warp per TMEM lane quarter (32 output pixels): tcgen05.ld,
+//               + bias (staged in shared memory), SiLU, + residual, split (or
+//               fp32) NHWC store into the destination channel slice.  Runs
+//               while warp 16 accumulates the next tiles into the other TMEM
+//               buffers.
 // All barrier waits are bounded (sm100.cuh); a timeout sets *a.err, aborts
 // the other roles, drains outstanding copies and UMMAs and frees tensor
 // memory.
+#include <cudaTypedefs.h>
+
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <vector>
 #include "kernels.h"
 #include "sm100.cuh"
@@ -44,12 +50,14 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kProducerWarps = 8;  // two per sub-partition: the im2col address stream is the long pole
 constexpr int kRowsPerThread = kBM * 8 / (kProducerWarps * 32);  // 16-byte columns per row = 8
-constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, splitting the columns
+constexpr int kEpilogueWarps = 8;  // two groups of four (one warp per TMEM lane quarter), alternate tiles
+constexpr int kMaxAcc = 4;         // TMEM accumulators when n_tile allows (4 x n_tile <= 512 columns)
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr uint32_t kAPlaneBytes = kBM * 128;  // one 128 x 64 bf16 plane
 constexpr int kSmemLimit = 232448;            // 227 KB opt-in per CTA
-constexpr int kSmemExtra = 1024 + 512;
+constexpr int kSmemExtra = 1024 + 512;          // alignment slack + barriers; the bias follows
+
 
 __device__ __forceinline__ void raise_error(int* err, volatile int* abort_flag, int code) {
   *abort_flag = 1;
@@ -66,7 +74,7 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, const int stages) {
+__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_constant__ ConvArgs a, const int stages) {
   extern __shared__ uint8_t smem_raw[];
   // Swizzle atoms need 1024-byte alignment in the shared window.
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -81,23 +89,29 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + kMaxAcc;
+  uint64_t* drain = acc_empty + kMaxAcc;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sbias = reinterpret_cast<float*>(tail + 512);  // n_tile * n_tiles floats, zero past Co
+  const int nbias = a.n_tile * a.n_tiles;
+  for (int i = threadIdx.x; i < nbias; i += kThreads) sbias[i] = (a.bias && i < a.Co) ? a.bias[i] : 0.0f;
 
-  uint32_t ncols = 32;
-  while (ncols < 2u * static_cast<uint32_t>(a.n_tile)) ncols <<= 1;
-  const uint32_t acc_stride = ncols >> 1;
+  // Accumulators of acc_stride (power of two >= n_tile) columns, as many as
+  // fit in the 512 TMEM columns up to kMaxAcc.
+  uint32_t acc_stride = 32;
+  while (acc_stride < static_cast<uint32_t>(a.n_tile)) acc_stride <<= 1;
+  const int nacc = min(kMaxAcc, static_cast<int>(512u / acc_stride));
+  const uint32_t ncols = static_cast<uint32_t>(nacc) * acc_stride;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
-      mbar_init(&full[s], kProducerWarps * 32);
+      mbar_init(&full[s], a.a_tma ? 1 : kProducerWarps * 32);
       mbar_init(&empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < nacc; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kEpilogueWarps);
+      mbar_init(&acc_empty[i], kEpilogueWarps / 2);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -113,10 +127,63 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
   const uint32_t tmem_base = *tmem_slot;
 
   const int total_tiles = a.m_tiles * a.n_tiles;
+  // The last K chunk holds K - 64 (num_kc - 1) real values: only its first
+  // ks_last 16-wide steps are copied and multiplied.
+  const int ks_last = (a.K - (a.num_kc - 1) * kBK + 15) / 16;
   const int HoWo = a.Ho * a.Wo;
   const int M = a.B * HoWo;
 
-  if (warp < kProducerWarps) {
+  if (warp < kProducerWarps && a.a_tma) {
+    // ------------------------------------------------------- TMA producer
+    // One thread: per K chunk, the packed weight chunk (bulk copy) and one
+    // im2col copy per filter tap and plane into the chunk's a_cpp-channel
+    // sub-tiles, all completing on the stage's full barrier.
+    if (threadIdx.x == 0) {
+      const int taps = a.kh * a.kw;
+      const int cpp = a.a_cpp;
+      const int tps = cpp == 64 ? 1 : 64 / cpp;                   // taps per chunk
+      const int cblocks = cpp == 64 ? (taps == 1 ? a.num_kc : a.Ci / 64) : 1;  // chunks per tap
+      const uint32_t sub_bytes = static_cast<uint32_t>(kBM * cpp * 2);
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+        const int mt = t / a.n_tiles;
+        const int nt = t - mt * a.n_tiles;
+        const int m0 = mt * kBM;
+        const int b = m0 / HoWo;
+        const int r = m0 - b * HoWo;
+        const int oy = r / a.Wo;
+        const int ox = r - oy * a.Wo;
+        const int w0 = ox * a.stride - a.pad;
+        const int h0 = oy * a.stride - a.pad;
+        const uint8_t* wsrc = a.wpack + static_cast<size_t>(nt) * a.num_kc * chunk_bytes;
+        for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
+          const uint32_t s = it % stages;
+          const uint32_t ph = (it / stages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+            raise_error(a.err, abort_flag, kErrWaitEmpty);
+            goto tma_producer_done;
+          }
+          const int t0 = cpp == 64 ? kc / cblocks : kc * tps;
+          const int c0 = cpp == 64 ? (kc - t0 * cblocks) * 64 : 0;
+          const int ntap = cpp == 64 ? 1 : min(tps, taps - t0);
+          uint8_t* stage = smem + s * stage_bytes;
+          mbar_arrive_expect_tx(&full[s], 2u * static_cast<uint32_t>(ntap) * sub_bytes + chunk_bytes);
+          bulk_g2s(stage + 2 * kAPlaneBytes, wsrc + static_cast<size_t>(kc) * chunk_bytes, chunk_bytes, &full[s]);
+          for (int i = 0; i < ntap; ++i) {
+            const int tap = t0 + i;
+            const int ky = tap / a.kw;
+            const int kx = tap - ky * a.kw;
+            uint8_t* dst = stage + i * sub_bytes;
+            tma_im2col_4d(dst, &a.tm_hi, c0, w0, h0, b, static_cast<uint16_t>(kx), static_cast<uint16_t>(ky),
+                          &full[s]);
+            tma_im2col_4d(dst + kAPlaneBytes, &a.tm_lo, c0, w0, h0, b, static_cast<uint16_t>(kx),
+                          static_cast<uint16_t>(ky), &full[s]);
+          }
+        }
+      }
+    }
+  tma_producer_done:;
+  } else if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producers
     // Thread t copies the 16-byte column j = t % 8 (8 K indices) of rows
     // t / 8 + 32 i, i = 0..3, for both planes.  Per tile each row's pixel
@@ -183,6 +250,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
         }
         const int k = kc * kBK + j * 8;
         const bool kvalid = k < a.K;
+        if (kc == a.num_kc - 1 && j >= 2 * ks_last) {
+          // Past the last multiplied step: nothing to copy.
+          cp_async_arrive_noinc(&full[s]);
+          ++it;
+          continue;
+        }
         // tap = k / Ci via a float reciprocal with an exact integer fix-up.
         int tap = __float2int_rz(static_cast<float>(k) * inv_ci);
         if (tap * a.Ci > k) --tap;
@@ -218,12 +291,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
     // ------------------------------------------------------------- epilogue
     const int e_idx = warp - kProducerWarps;  // 0..7
     const int q = e_idx & 3;                  // TMEM lane quarter (= warp % 4)
-    const int half = e_idx >> 2;              // which 32-column chunks this warp takes
+    const int grp = e_idx >> 2;               // this group takes every other tile
     const bool f32out = a.out_f32.ptr != nullptr;
-    int lt = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
-      const int acc = lt & 1;
-      const uint32_t aph = (lt >> 1) & 1;
+    for (int t = blockIdx.x + grp * gridDim.x, lt = grp; t < total_tiles; t += 2 * gridDim.x, lt += 2) {
+      const int acc = lt % nacc;
+      const uint32_t aph = (lt / nacc) & 1;
       if (!mbar_wait(&acc_full[acc], aph, abort_flag)) {
         raise_error(a.err, abort_flag, kErrWaitAccFull);
         break;
@@ -241,55 +313,84 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
         p = m - b * HoWo;
       }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_stride;
-      for (int c0 = 32 * half; c0 < nvalid; c0 += 64) {
-        // Two 16-column TMEM loads, one wait; never past this accumulator.
-        uint32_t r[32];
-        uint32_t(&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[0]);
-        uint32_t(&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[16]);
-        tc_ld_32x32b_x16(tbase + c0, r0);
-        if (c0 + 16 < a.n_tile) tc_ld_32x32b_x16(tbase + c0 + 16, r1);
+      const float* bias_t = sbias + n0;
+      // Output element offset of this lane's pixel (also read by the store
+      // shuffle below); invalid lanes compute but never store.
+      const long long po = f32out ? static_cast<long long>(b) * a.out_f32.bstride +
+                                        static_cast<long long>(p) * a.out_f32.cstride + a.out_f32.coff + n0
+                                  : static_cast<long long>(b) * a.out.bstride +
+                                        static_cast<long long>(p) * a.out.cstride + a.out.coff + n0;
+      // Per 16-column unit: one TMEM load, bias and SiLU, residual loads,
+      // then the stores.
+      for (int c = 0; c < nvalid; c += 16) {
+        uint32_t r[16];
+        tc_ld_32x32b_x16(tbase + c, r);
         tc_wait_ld();
-        if (!valid) continue;
+        float v[16];
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int n = c0 + 8 * g;  // column within the tile
-          if (n >= nvalid) break;
-          float x[8];
+        for (int e = 0; e < 16; e += 4) {
+          const float4 bb = *reinterpret_cast<const float4*>(bias_t + c + e);
+          v[e + 0] = __uint_as_float(r[e + 0]) + bb.x;
+          v[e + 1] = __uint_as_float(r[e + 1]) + bb.y;
+          v[e + 2] = __uint_as_float(r[e + 2]) + bb.z;
+          v[e + 3] = __uint_as_float(r[e + 3]) + bb.w;
+        }
+        if (a.act == kActSiLU) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(r[8 * g + e]);
-          if (a.bias) {
-            const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.bias + n0 + n));
-            const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.bias + n0 + n + 4));
-            x[0] += b0.x;
-            x[1] += b0.y;
-            x[2] += b0.z;
-            x[3] += b0.w;
-            x[4] += b1.x;
-            x[5] += b1.y;
-            x[6] += b1.z;
-            x[7] += b1.w;
+          for (int e = 0; e < 16; ++e) v[e] = silu_fast(v[e]);
+        }
+        const bool second = c + 8 < nvalid;
+        if (a.res.hi) {
+          const uint16_t* rb = a.res.hi + static_cast<long long>(b) * a.res.bstride +
+                               static_cast<long long>(p) * a.res.cstride + a.res.coff + n0 + c;
+          float rv[16];
+          load8_rw(rb, a.res.plane, *reinterpret_cast<float(*)[8]>(&rv[0]));
+          if (second) load8_rw(rb + 8, a.res.plane, *reinterpret_cast<float(*)[8]>(&rv[8]));
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (e < 8 || second) v[e] += rv[e];
+        }
+        if (f32out) {
+          if (valid) {
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+              const int n = c + 8 * g;
+              if (g == 1 && !second) break;
+              float* o = a.out_f32.ptr + po + n;
+              *reinterpret_cast<float4*>(o) = make_float4(v[8 * g], v[8 * g + 1], v[8 * g + 2], v[8 * g + 3]);
+              if (n + 4 < nvalid)
+                *reinterpret_cast<float4*>(o + 4) =
+                    make_float4(v[8 * g + 4], v[8 * g + 5], v[8 * g + 6], v[8 * g + 7]);
+            }
           }
-          if (a.act == kActSiLU) {
+        } else {
+          // Split to bf16 hi/lo words (channel pairs), then regroup across
+          // the warp so that lanes 2k and 2k+1 write the two 16-byte halves
+          // of one pixel's 32-byte run: every store fills whole sectors.
+          uint32_t hw[8], lw[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] = silu_fast(x[e]);
-          }
-          if (a.res.hi) {
-            float rv[8];
-            load8_rw(a.res.hi + static_cast<long long>(b) * a.res.bstride + static_cast<long long>(p) * a.res.cstride +
-                         a.res.coff + n0 + n,
-                     a.res.plane, rv);
+          for (int i = 0; i < 8; ++i) split2(v[2 * i], v[2 * i + 1], hw[i], lw[i]);
+          const int h = lane & 1;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] += rv[e];
-          }
-          if (f32out) {
-            float* o = a.out_f32.ptr + static_cast<long long>(b) * a.out_f32.bstride +
-                       static_cast<long long>(p) * a.out_f32.cstride + a.out_f32.coff + n0 + n;
-            *reinterpret_cast<float4*>(o) = make_float4(x[0], x[1], x[2], x[3]);
-            if (n + 4 < nvalid) *reinterpret_cast<float4*>(o + 4) = make_float4(x[4], x[5], x[6], x[7]);
-          } else {
-            store8(a.out.hi + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(p) * a.out.cstride +
-                       a.out.coff + n0 + n,
-                   a.out.plane, x);
+          for (int i = 0; i < 2; ++i) {
+            const int src = (lane >> 1) + 16 * i;
+            uint32_t oh[4], ol[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t h0 = __shfl_sync(0xffffffffu, hw[j], src);
+              const uint32_t h1 = __shfl_sync(0xffffffffu, hw[4 + j], src);
+              const uint32_t l0 = __shfl_sync(0xffffffffu, lw[j], src);
+              const uint32_t l1 = __shfl_sync(0xffffffffu, lw[4 + j], src);
+              oh[j] = h ? h1 : h0;
+              ol[j] = h ? l1 : l0;
+            }
+            const long long spo = __shfl_sync(0xffffffffu, po, src);
+            const bool svalid = __shfl_sync(0xffffffffu, valid, src);
+            if (svalid && (h == 0 || second)) {
+              uint16_t* o = a.out.hi + spo + c + 8 * h;
+              *reinterpret_cast<uint4*>(o) = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+              *reinterpret_cast<uint4*>(o + a.out.plane) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+            }
           }
         }
       }
@@ -301,11 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(kBM, a.n_tile);
+      const int a_cpp = a.a_tma ? a.a_cpp : 64;
       uint32_t it = 0;
       int lt = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
-        const int acc = lt & 1;
-        const uint32_t aph = (lt >> 1) & 1;
+        const int acc = lt % nacc;
+        const uint32_t aph = (lt / nacc) & 1;
         if (!mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag)) {
           raise_error(a.err, abort_flag, kErrWaitAccEmpty);
           break;
@@ -328,16 +430,27 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const ConvArgs a, 
           // Descriptors of the stage's four operand planes; a 16-wide K step
           // advances the start address by 32 bytes (2 in the >>4 field).
           const uint32_t a_hi = smem_u32(smem + s * stage_bytes);
-          const uint64_t dah0 = sw128_kmajor_desc(a_hi);
-          const uint64_t dal0 = sw128_kmajor_desc(a_hi + kAPlaneBytes);
+          // Activation sub-tiles: 128B swizzle (rows of 64 channels) unless
+          // TMA copies of 16 or 32 channels per tap (32B / 64B swizzle, one
+          // sub-tile per tap).
+          const uint32_t a_layout = a_cpp == 16 ? 6u : a_cpp == 32 ? 4u : 2u;
+          const uint32_t a_sbo = a_cpp == 16 ? 256u : a_cpp == 32 ? 512u : 1024u;
+          const uint64_t dah0 = kmajor_desc(a_hi, a_layout, a_sbo);
+          const uint64_t dal0 = kmajor_desc(a_hi + kAPlaneBytes, a_layout, a_sbo);
           const uint64_t dbh0 = sw128_kmajor_desc(a_hi + 2 * kAPlaneBytes);
           const uint64_t dbl0 = sw128_kmajor_desc(a_hi + 2 * kAPlaneBytes + static_cast<uint32_t>(a.n_tile) * 128u);
+          const int nks = kc == a.num_kc - 1 ? ks_last : kBK / 16;
 #pragma unroll
           for (int ks = 0; ks < kBK / 16; ++ks) {
+            if (ks >= nks) break;
+            // Start-address advance (16-byte units) of K step ks in A and B.
             const uint64_t koff = static_cast<uint64_t>(ks * 2);
-            tc_mma_bf16(d_tmem, dah0 + koff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
-            tc_mma_bf16(d_tmem, dah0 + koff, dbl0 + koff, idesc, 1u);
-            tc_mma_bf16(d_tmem, dal0 + koff, dbh0 + koff, idesc, 1u);
+            const uint64_t aoff = a_cpp == 16   ? static_cast<uint64_t>(ks * 256)
+                                  : a_cpp == 32 ? static_cast<uint64_t>((ks >> 1) * 512 + (ks & 1) * 2)
+                                                : koff;
+            tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
+            tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + koff, idesc, 1u);
+            tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
           }
           tc_commit(&empty[s]);
         }
@@ -378,9 +491,11 @@ inline float host_bf16_to_float(uint16_t h) {
   return f;
 }
 
-int stages_for(int n_tile) {
+int bias_bytes(int n_tile, int n_tiles) { return (n_tile * n_tiles * 4 + 15) & ~15; }
+
+int stages_for(int n_tile, int n_tiles) {
   const int stage_bytes = 2 * kAPlaneBytes + static_cast<int>(conv_chunk_bytes(n_tile));
-  int stages = (kSmemLimit - kSmemExtra) / stage_bytes;
+  int stages = (kSmemLimit - kSmemExtra - bias_bytes(n_tile, n_tiles)) / stage_bytes;
   return stages > 8 ? 8 : stages;
 }
 
@@ -430,6 +545,71 @@ size_t pack_conv_weights(const float* w, int co, int ci, int kh, int kw, int n_t
 
 // Opts the kernels into the full 227 KB of shared memory on the current
 // device.  Called once per device before any launch (and outside capture).
+namespace {
+
+// cuTensorMapEncodeIm2col from the driver, looked up once through the
+// runtime (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeIm2col_v12000 im2col_encoder() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+  });
+  return fn;
+}
+
+// im2col map over one plane of a split NHWC view: dims (C, W, H, N) with
+// C = a.Ci channels starting at the view's channel offset.
+bool encode_plane(CUtensorMap* map, const ConvArgs& a, const uint16_t* base, int cpp) {
+  const auto enc = im2col_encoder();
+  if (!enc) return false;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(base);
+  const long long cs = a.src0.cstride;
+  if (addr % 16 || (cs * 2) % 16 || (a.src0.bstride * 2) % 16) return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Ci), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
+                        static_cast<cuuint64_t>(a.B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(cs * 2), static_cast<cuuint64_t>(cs * 2 * a.W),
+                           static_cast<cuuint64_t>(a.src0.bstride * 2)};
+  // Window origins run from -pad to (extent - 1) + pad - (k - 1).
+  int lower[2] = {-a.pad, -a.pad};
+  int upper[2] = {a.pad - (a.kw - 1), a.pad - (a.kh - 1)};
+  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(a.stride), static_cast<cuuint32_t>(a.stride), 1};
+  const CUtensorMapSwizzle sw = cpp == 16   ? CU_TENSOR_MAP_SWIZZLE_32B
+                                : cpp == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<uint16_t*>(base), dims, strides, lower,
+                         upper, static_cast<cuuint32_t>(cpp), static_cast<cuuint32_t>(kBM), estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+void conv_setup_tma(ConvArgs* a) {
+  if (a->lg_up0 || a->lg_up1 || a->c_split != a->Ci || a->Ci % 16 || !a->src0.hi) return;
+  const int taps = a->kh * a->kw;
+  if (a->K != taps * a->Ci) return;
+  int cpp = 0;
+  if (taps == 1) cpp = 64;  // 64-channel boxes; channels past Ci arrive as zeros
+  else if (a->Ci == 16 || a->Ci == 32) cpp = a->Ci;
+  else if (a->Ci % 64 == 0) cpp = 64;
+  else return;
+  // Window origins reach (extent - 1) + upper corner; the corners must give
+  // exactly the Ho x Wo output raster.
+  if ((a->W - 1 + a->pad - (a->kw - 1) + a->pad) / a->stride + 1 != a->Wo ||
+      (a->H - 1 + a->pad - (a->kh - 1) + a->pad) / a->stride + 1 != a->Ho)
+    return;
+  const uint16_t* hi = a->src0.hi + a->src0.coff;
+  if (!encode_plane(&a->tm_hi, *a, hi, cpp) || !encode_plane(&a->tm_lo, *a, hi + a->src0.plane, cpp)) return;
+  a->a_tma = 1;
+  a->a_cpp = cpp;
+}
+
 cudaError_t init_conv_kernel_attributes() {
   return cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
 }
@@ -443,10 +623,11 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
   // (the producer resolves their pixel once per row, not per tap).
   if ((a.lg_up0 || a.lg_up1) && (a.kh != 1 || a.kw != 1 || a.stride != 1 || a.pad != 0))
     return cudaErrorInvalidValue;
-  const int stages = stages_for(a.n_tile);
+  if (a.n_tiles < 1 || a.n_tile * a.n_tiles < a.Co) return cudaErrorInvalidValue;
+  const int stages = stages_for(a.n_tile, a.n_tiles);
   if (stages < 2) return cudaErrorInvalidValue;
   const int stage_bytes = 2 * kAPlaneBytes + static_cast<int>(conv_chunk_bytes(a.n_tile));
-  const int smem = kSmemExtra + stages * stage_bytes;
+  const int smem = kSmemExtra + bias_bytes(a.n_tile, a.n_tiles) + stages * stage_bytes;
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
   const int grid = total < num_sms ? total : num_sms;

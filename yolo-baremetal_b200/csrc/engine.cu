@@ -379,6 +379,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     a.out_f32 = fout;
     a.res = res;
     a.err = d_err_;
+    conv_setup_tma(&a);
     const int sms = num_sms_;
     Op op{step, [a, sms](cudaStream_t s) { return launch_conv_tc(a, s, sms); }};
     op.kind = kOpConv;

@@ -18,6 +18,7 @@
 // consumers read the whole buffer.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace yb {
@@ -82,7 +83,23 @@ struct ConvArgs {
   FOut out_f32;  // used instead of `out` when out_f32.ptr != nullptr
   SView res;     // res.hi == nullptr: no residual
   int* err = nullptr;
+  // Activation operand source.  a_tma == 0: the producer warps gather it with
+  // cp.async (any view, upsampled or two-source inputs).  a_tma == 1: one
+  // thread loads it with TMA im2col copies through tm_hi / tm_lo (one
+  // single-source, non-upsampled input; see conv_setup_tma), a_cpp channels
+  // of one filter tap per copy (16, 32 or 64).
+  int a_tma = 0;
+  int a_cpp = 0;
+  alignas(64) CUtensorMap tm_hi;
+  alignas(64) CUtensorMap tm_lo;
 };
+
+// Switches `a` (fully set up for the cp.async path) to TMA im2col operand
+// loads when its input allows it: one source (c_split == Ci), no upsampling,
+// Ci a multiple of 16, and for kh*kw > 1 Ci in {16, 32} or a multiple of 64
+// (each 64-wide K chunk then holds whole taps).  Leaves `a` unchanged
+// otherwise or when the tensor maps cannot be encoded.
+void conv_setup_tma(ConvArgs* a);
 
 // Bytes of one packed weight chunk: hi and lo planes of n_tile rows x 128 B.
 inline size_t conv_chunk_bytes(int n_tile) { return static_cast<size_t>(n_tile) * 256; }

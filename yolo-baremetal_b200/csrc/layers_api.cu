@@ -183,6 +183,7 @@ class Kit {
     a.out = y.o(ycoff);
     if (res) a.res = res->v(rcoff);
     a.err = sc->d_err;
+    conv_setup_tma(&a);
     err = launch_conv_tc(a, sc->stream, sc->num_sms);
   }
   void dw(const tensor_t* w, const tensor_t* b, const DT& x, int coff, int act, const DT& y, int ycoff) {

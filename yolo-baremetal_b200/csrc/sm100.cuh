@@ -4,6 +4,7 @@
 // so that a kernel can record an error, drain and exit instead of hanging.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
@@ -95,6 +96,26 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Arrives on `bar` and adds `bytes` to the transaction count of its current
+// phase (the phase completes when the copies have delivered them).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// TMA load in im2col mode from a 4-D NHWC tensor map (dims C, W, H, N):
+// pixelsPerColumn consecutive output pixels starting at the window origin
+// (w, h) of image n, channels [c, c + channelsPerPixel), filter tap (ow, oh).
+// Out-of-bounds elements arrive as zeros.  c * element size must be a
+// multiple of 16 bytes; dst aligned to the map's swizzle span.
+__device__ __forceinline__ void tma_im2col_4d(void* dst, const CUtensorMap* map, int c, int w, int h, int n,
+                                              uint16_t ow, uint16_t oh, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)), "h"(ow), "h"(oh)
+      : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy reads (tensor-core operand fetch).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -158,6 +179,15 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
          (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
          (static_cast<uint64_t>(2) << 61);
+}
+
+// K-major operand descriptor for any swizzle mode: layout 2 (128B, rows of
+// 128 bytes), 4 (64B) or 6 (32B); 8-row groups sbo bytes apart (8 x row
+// bytes when packed).  The tile base must be aligned to 8 x row bytes.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr, uint32_t layout, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(sbo >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(layout) << 61);
 }
 
 // Instruction descriptor for kind::f16 with bf16 A/B, fp32 D, both K-major:
