@@ -53,6 +53,20 @@ def test_conv_sweep_shapes(ci, co, k, stride, H):
     assert err <= _tol(ref, ci * k * k)
 
 
+# 3x3 stride-1 shapes of the resident-weight patch mode (16 x 8 output tiles):
+# Ci = 16, 32, 48; Co 8-48; maps whose sides are not multiples of the tile.
+PATCH = [(16, 8, 160, 160), (16, 16, 20, 20), (32, 32, 40, 40), (16, 32, 37, 29), (32, 16, 80, 72),
+         (48, 48, 23, 41), (16, 16, 7, 5)]
+
+
+@pytest.mark.parametrize("ci,co,H,W", PATCH)
+def test_conv_patch_mode_shapes(ci, co, H, W):
+    out, ref = _run(ci, co, 3, 1, H, W=W, act=True, seed=ci + co + H)
+    err = max_abs(out, ref)
+    print(f"conv {ci}->{co} 3x3 s1 @{H}x{W}: max abs err {err:.3e}")
+    assert err <= _tol(ref, ci * 9)
+
+
 @pytest.mark.parametrize("ci,co,k,stride,H", EDGE)
 def test_conv_edge_shapes(ci, co, k, stride, H):
     out, ref = _run(ci, co, k, stride, H, act=(co % 2 == 0))

@@ -56,7 +56,15 @@ constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr uint32_t kAPlaneBytes = kBM * 128;  // one 128 x 64 bf16 plane
 constexpr int kSmemLimit = 232448;            // 227 KB opt-in per CTA
-constexpr int kSmemExtra = 1024 + 512;          // alignment slack + barriers; the bias follows
+constexpr int kSmemExtra = 1024 + 512;
+// Patch mode: one 8-channel chunk of a tile's 18 x 10 input patch (16 bytes
+// per pixel, pixel-major), padded to a 128-byte multiple.
+constexpr int kPatchH = 18, kPatchW = 10;
+constexpr uint32_t kPatchBox = kPatchH * kPatchW * 16;  // 2880 bytes written by one box copy
+constexpr uint32_t kPatchChunk = 2944;
+__host__ __device__ constexpr uint32_t patch_stage_bytes(int ci) {
+  return ((static_cast<uint32_t>(ci / 8) * 2u * kPatchChunk) + 1023u) & ~1023u;
+}          // alignment slack + barriers; the bias follows
 
 
 __device__ __forceinline__ void raise_error(int* err, volatile int* abort_flag, int code) {
@@ -82,16 +90,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const bool patch = a.a_tma == 2;
   const uint32_t chunk_bytes = static_cast<uint32_t>(a.n_tile) * 256u;
-  const uint32_t stage_bytes = 2u * kAPlaneBytes + chunk_bytes;
+  // Patch mode keeps every weight chunk resident in front of the stages.
+  const uint32_t wres_bytes = patch ? static_cast<uint32_t>(a.num_kc) * chunk_bytes : 0u;
+  const uint32_t stage_bytes = patch ? patch_stage_bytes(a.Ci) : 2u * kAPlaneBytes + chunk_bytes;
+  uint8_t* stage0 = smem + wres_bytes;
 
-  uint8_t* tail = smem + stages * stage_bytes;
+  uint8_t* tail = stage0 + stages * stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;
   uint64_t* acc_empty = acc_full + kMaxAcc;
   uint64_t* drain = acc_empty + kMaxAcc;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* wbar = drain + 1;  // resident weights landed (patch mode)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sbias = reinterpret_cast<float*>(tail + 512);  // n_tile * n_tiles floats, zero past Co
   const int nbias = a.n_tile * a.n_tiles;
@@ -99,8 +112,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
 
   // Accumulators of acc_stride (power of two >= n_tile) columns, as many as
   // fit in the 512 TMEM columns up to kMaxAcc.
+  // Patch mode (MMA-issue bound: many small K steps per tile) with
+  // n_tile <= 128: each K step is two UMMAs of N = 2 n_tile against the
+  // stacked [B_hi; B_lo] chunk (columns [0, n) += A*B_hi, [n, 2n) += A*B_lo,
+  // summed by the epilogue).  Otherwise three UMMAs of N = n_tile, which
+  // keeps the epilogue (the long pole there) to one TMEM load per unit.
+  const bool stacked = patch && a.n_tile <= 128;
+  const uint32_t acc_cols = static_cast<uint32_t>(stacked ? 2 * a.n_tile : a.n_tile);
   uint32_t acc_stride = 32;
-  while (acc_stride < static_cast<uint32_t>(a.n_tile)) acc_stride <<= 1;
+  while (acc_stride < acc_cols) acc_stride <<= 1;
   const int nacc = min(kMaxAcc, static_cast<int>(512u / acc_stride));
   const uint32_t ncols = static_cast<uint32_t>(nacc) * acc_stride;
 
@@ -114,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       mbar_init(&acc_empty[i], kEpilogueWarps / 2);
     }
     mbar_init(drain, 1);
+    mbar_init(wbar, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -133,7 +154,38 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   const int HoWo = a.Ho * a.Wo;
   const int M = a.B * HoWo;
 
-  if (warp < kProducerWarps && a.a_tma) {
+  if (warp < kProducerWarps && patch) {
+    // ----------------------------------------------------- patch producer
+    // One thread: the resident weights once, then per tile one box copy per
+    // 8-channel chunk and plane of its 18 x 10 input patch.
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(wbar, wres_bytes);
+      for (int kc = 0; kc < a.num_kc; ++kc)
+        bulk_g2s(smem + static_cast<size_t>(kc) * chunk_bytes, a.wpack + static_cast<size_t>(kc) * chunk_bytes,
+                 chunk_bytes, wbar);
+      const int nch = a.Ci / 8;
+      const int per = a.tiles_y * a.tiles_x;
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
+        const uint32_t s = it % stages;
+        const uint32_t ph = (it / stages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+          raise_error(a.err, abort_flag, kErrWaitEmpty);
+          break;
+        }
+        const int b = t / per;
+        const int rem = t - b * per;
+        const int ty = rem / a.tiles_x;
+        const int tx = rem - ty * a.tiles_x;
+        uint8_t* stage = stage0 + s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], 2u * static_cast<uint32_t>(nch) * kPatchBox);
+        for (int ch = 0; ch < nch; ++ch) {
+          tma_tile_4d(stage + ch * kPatchChunk, &a.tm_hi, 8 * ch, tx * 8 - 1, ty * 16 - 1, b, &full[s]);
+          tma_tile_4d(stage + (nch + ch) * kPatchChunk, &a.tm_lo, 8 * ch, tx * 8 - 1, ty * 16 - 1, b, &full[s]);
+        }
+      }
+    }
+  } else if (warp < kProducerWarps && a.a_tma) {
     // ------------------------------------------------------- TMA producer
     // One thread: per K chunk, the packed weight chunk (bulk copy) and one
     // im2col copy per filter tap and plane into the chunk's a_cpp-channel
@@ -166,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           const int t0 = cpp == 64 ? kc / cblocks : kc * tps;
           const int c0 = cpp == 64 ? (kc - t0 * cblocks) * 64 : 0;
           const int ntap = cpp == 64 ? 1 : min(tps, taps - t0);
-          uint8_t* stage = smem + s * stage_bytes;
+          uint8_t* stage = stage0 + s * stage_bytes;
           mbar_arrive_expect_tx(&full[s], 2u * static_cast<uint32_t>(ntap) * sub_bytes + chunk_bytes);
           bulk_g2s(stage + 2 * kAPlaneBytes, wsrc + static_cast<size_t>(kc) * chunk_bytes, chunk_bytes, &full[s]);
           for (int i = 0; i < ntap; ++i) {
@@ -193,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     const int j = ptid & 7;
     const int r0 = ptid >> 3;
     uint32_t it = 0;  // chunks issued
-    const uint32_t smem_base = smem_u32(smem);
+    const uint32_t smem_base = smem_u32(stage0);
     const int ws0 = a.W >> a.lg_up0, ws1 = a.W >> a.lg_up1;
     const float inv_ci = 1.0f / static_cast<float>(a.Ci);
     uint32_t row_off[kRowsPerThread];
@@ -245,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const uint32_t sa_lo = sa_hi + kAPlaneBytes;
         if (ptid == 0) {
           mbar_expect_tx(&full[s], chunk_bytes);
-          bulk_g2s(smem + s * stage_bytes + 2 * kAPlaneBytes, wsrc + static_cast<size_t>(kc) * chunk_bytes,
+          bulk_g2s(stage0 + s * stage_bytes + 2 * kAPlaneBytes, wsrc + static_cast<size_t>(kc) * chunk_bytes,
                    chunk_bytes, &full[s]);
         }
         const int k = kc * kBK + j * 8;
@@ -305,12 +357,29 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       const int nt = t - mt * a.n_tiles;
       const int n0 = nt * a.n_tile;
       const int nvalid = min(a.n_tile, a.Co - n0);
-      const int m = mt * kBM + q * 32 + lane;
-      const bool valid = m < M;
+      bool valid;
       int b = 0, p = 0;
-      if (valid) {
-        b = m / HoWo;
-        p = m - b * HoWo;
+      if (patch) {
+        // Tile of 16 rows x 8 columns; TMEM lane r is pixel (r / 8, r % 8).
+        const int per = a.tiles_y * a.tiles_x;
+        const int tb = t / per;
+        const int rem = t - tb * per;
+        const int ty = rem / a.tiles_x;
+        const int r = q * 32 + lane;
+        const int oy = ty * 16 + (r >> 3);
+        const int ox = (rem - ty * a.tiles_x) * 8 + (r & 7);
+        valid = oy < a.Ho && ox < a.Wo;
+        if (valid) {
+          b = tb;
+          p = oy * a.Wo + ox;
+        }
+      } else {
+        const int m = mt * kBM + q * 32 + lane;
+        valid = m < M;
+        if (valid) {
+          b = m / HoWo;
+          p = m - b * HoWo;
+        }
       }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_stride;
       const float* bias_t = sbias + n0;
@@ -323,17 +392,20 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       // Per 16-column unit: one TMEM load, bias and SiLU, residual loads,
       // then the stores.
       for (int c = 0; c < nvalid; c += 16) {
-        uint32_t r[16];
+        uint32_t r[16], r2[16];
         tc_ld_32x32b_x16(tbase + c, r);
+        if (stacked) tc_ld_32x32b_x16(tbase + a.n_tile + c, r2);
         tc_wait_ld();
         float v[16];
 #pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]) + (stacked ? __uint_as_float(r2[e]) : 0.0f);
+#pragma unroll
         for (int e = 0; e < 16; e += 4) {
           const float4 bb = *reinterpret_cast<const float4*>(bias_t + c + e);
-          v[e + 0] = __uint_as_float(r[e + 0]) + bb.x;
-          v[e + 1] = __uint_as_float(r[e + 1]) + bb.y;
-          v[e + 2] = __uint_as_float(r[e + 2]) + bb.z;
-          v[e + 3] = __uint_as_float(r[e + 3]) + bb.w;
+          v[e + 0] += bb.x;
+          v[e + 1] += bb.y;
+          v[e + 2] += bb.z;
+          v[e + 3] += bb.w;
         }
         if (a.act == kActSiLU) {
 #pragma unroll
@@ -401,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   } else {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kBM, a.n_tile);
+      const uint32_t idesc = idesc_bf16_f32(kBM, stacked ? 2 * a.n_tile : a.n_tile);
       const int a_cpp = a.a_tma ? a.a_cpp : 64;
       uint32_t it = 0;
       int lt = 0;
@@ -415,6 +487,55 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * acc_stride;
         bool ok = true;
+        if (patch) {
+          // One stage per tile: 9 taps x Ci/16 K steps, each A operand a
+          // shifted window of the patch, each B step in the resident weights.
+          if (lt == 0 && !mbar_wait(wbar, 0, abort_flag)) {
+            raise_error(a.err, abort_flag, kErrWaitFull);
+            break;
+          }
+          const uint32_t s = it % stages;
+          const uint32_t ph = (it / stages) & 1u;
+          ++it;
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            raise_error(a.err, abort_flag, kErrWaitFull);
+            break;
+          }
+          tc_fence_after();
+          const int nch = a.Ci / 8;
+          const int cbs = a.Ci / 16;
+          // Descriptors at the patch origin and at weight chunk 0; every
+          // step adds a start-address offset (16-byte units) to them.
+          const uint32_t pa = smem_u32(stage0 + s * stage_bytes);
+          const uint64_t dah0 = kmajor_desc_noswizzle(pa, kPatchChunk, kPatchW * 16);
+          const uint64_t dal0 = kmajor_desc_noswizzle(pa + static_cast<uint32_t>(nch) * kPatchChunk, kPatchChunk,
+                                                      kPatchW * 16);
+          const uint64_t dbh0 = sw128_kmajor_desc(smem_u32(smem));
+          const uint64_t dbl0 = sw128_kmajor_desc(smem_u32(smem) + static_cast<uint32_t>(a.n_tile) * 128u);
+          const uint64_t chunk_units = chunk_bytes >> 4;
+          int step = 0;
+          for (int ky = 0; ky < 3; ++ky) {
+            for (int kx = 0; kx < 3; ++kx) {
+              const uint64_t toff = static_cast<uint64_t>(ky * kPatchW + kx);  // window shift, 16-byte rows
+              for (int cb = 0; cb < cbs; ++cb, ++step) {
+                const uint64_t aoff = toff + static_cast<uint64_t>(cb) * (2 * kPatchChunk / 16);
+                const uint64_t boff = static_cast<uint64_t>(step >> 2) * chunk_units + static_cast<uint64_t>((step & 3) * 2);
+                const uint32_t accum = step != 0 ? 1u : 0u;
+                if (stacked) {
+                  tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + boff, idesc, accum);
+                  tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + boff, idesc, 1u);
+                } else {
+                  tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + boff, idesc, accum);
+                  tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + boff, idesc, 1u);
+                  tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + boff, idesc, 1u);
+                }
+              }
+            }
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&acc_full[acc]);
+          continue;
+        }
         for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
           const uint32_t s = it % stages;
           const uint32_t ph = (it / stages) & 1u;
@@ -429,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           tc_fence_after();
           // Descriptors of the stage's four operand planes; a 16-wide K step
           // advances the start address by 32 bytes (2 in the >>4 field).
-          const uint32_t a_hi = smem_u32(smem + s * stage_bytes);
+          const uint32_t a_hi = smem_u32(stage0 + s * stage_bytes);
           // Activation sub-tiles: 128B swizzle (rows of 64 channels) unless
           // TMA copies of 16 or 32 channels per tap (32B / 64B swizzle, one
           // sub-tile per tap).
@@ -448,9 +569,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             const uint64_t aoff = a_cpp == 16   ? static_cast<uint64_t>(ks * 256)
                                   : a_cpp == 32 ? static_cast<uint64_t>((ks >> 1) * 512 + (ks & 1) * 2)
                                                 : koff;
-            tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
-            tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + koff, idesc, 1u);
-            tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
+            if (stacked) {
+              tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
+              tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
+            } else {
+              tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
+              tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + koff, idesc, 1u);
+              tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
+            }
           }
           tc_commit(&empty[s]);
         }
@@ -493,11 +619,6 @@ inline float host_bf16_to_float(uint16_t h) {
 
 int bias_bytes(int n_tile, int n_tiles) { return (n_tile * n_tiles * 4 + 15) & ~15; }
 
-int stages_for(int n_tile, int n_tiles) {
-  const int stage_bytes = 2 * kAPlaneBytes + static_cast<int>(conv_chunk_bytes(n_tile));
-  int stages = (kSmemLimit - kSmemExtra - bias_bytes(n_tile, n_tiles)) / stage_bytes;
-  return stages > 8 ? 8 : stages;
-}
 
 }  // namespace
 
@@ -588,9 +709,72 @@ bool encode_plane(CUtensorMap* map, const ConvArgs& a, const uint16_t* base, int
   return r == CUDA_SUCCESS;
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 tiled_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tiled map over one plane of a split NHWC view, dims (C, W, H, N), with
+// boxes of 8 channels x kPatchW x kPatchH pixels of one image.
+bool encode_patch_plane(CUtensorMap* map, const ConvArgs& a, const uint16_t* base) {
+  const auto enc = tiled_encoder();
+  if (!enc) return false;
+  const long long cs = a.src0.cstride;
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (cs * 2) % 16 || (a.src0.bstride * 2) % 16) return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Ci), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
+                        static_cast<cuuint64_t>(a.B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(cs * 2), static_cast<cuuint64_t>(cs * 2 * a.W),
+                           static_cast<cuuint64_t>(a.src0.bstride * 2)};
+  cuuint32_t box[4] = {8, kPatchW, kPatchH, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<uint16_t*>(base), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int conv_stage_bytes(const ConvArgs& a) {
+  return a.a_tma == 2 ? static_cast<int>(patch_stage_bytes(a.Ci))
+                      : 2 * static_cast<int>(kAPlaneBytes) + static_cast<int>(conv_chunk_bytes(a.n_tile));
+}
+int conv_resident_bytes(const ConvArgs& a) {
+  return a.a_tma == 2 ? a.num_kc * static_cast<int>(conv_chunk_bytes(a.n_tile)) : 0;
+}
+int conv_stages(const ConvArgs& a) {
+  const int st = (kSmemLimit - kSmemExtra - bias_bytes(a.n_tile, a.n_tiles) - conv_resident_bytes(a)) /
+                 conv_stage_bytes(a);
+  return st > 8 ? 8 : st;
+}
+
 }  // namespace
 
+bool conv_setup_patch(ConvArgs* a) {
+  if (a->kh != 3 || a->kw != 3 || a->stride != 1 || a->pad != 1) return false;
+  if (a->lg_up0 || a->lg_up1 || a->c_split != a->Ci || a->Ci % 16 || !a->src0.hi || a->n_tiles != 1) return false;
+  if (a->K != 9 * a->Ci || a->Ho != a->H || a->Wo != a->W) return false;
+  ConvArgs t = *a;
+  t.a_tma = 2;
+  if (conv_stages(t) < 3) return false;  // resident weights leave too little room
+  const uint16_t* hi = a->src0.hi + a->src0.coff;
+  if (!encode_patch_plane(&t.tm_hi, t, hi) || !encode_patch_plane(&t.tm_lo, t, hi + a->src0.plane)) return false;
+  t.a_cpp = 0;
+  t.tiles_y = (a->Ho + 15) / 16;
+  t.tiles_x = (a->Wo + 7) / 8;
+  t.m_tiles = a->B * t.tiles_y * t.tiles_x;
+  *a = t;
+  return true;
+}
+
 void conv_setup_tma(ConvArgs* a) {
+  if (conv_setup_patch(a)) return;
   if (a->lg_up0 || a->lg_up1 || a->c_split != a->Ci || a->Ci % 16 || !a->src0.hi) return;
   const int taps = a->kh * a->kw;
   if (a->K != taps * a->Ci) return;
@@ -624,10 +808,12 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
   if ((a.lg_up0 || a.lg_up1) && (a.kh != 1 || a.kw != 1 || a.stride != 1 || a.pad != 0))
     return cudaErrorInvalidValue;
   if (a.n_tiles < 1 || a.n_tile * a.n_tiles < a.Co) return cudaErrorInvalidValue;
-  const int stages = stages_for(a.n_tile, a.n_tiles);
+  if (a.a_tma == 2 && (a.n_tiles != 1 || a.kh != 3 || a.kw != 3 || a.Ci % 16 || a.tiles_x < 1 || a.tiles_y < 1 ||
+                       a.m_tiles != a.B * a.tiles_y * a.tiles_x))
+    return cudaErrorInvalidValue;
+  const int stages = conv_stages(a);
   if (stages < 2) return cudaErrorInvalidValue;
-  const int stage_bytes = 2 * kAPlaneBytes + static_cast<int>(conv_chunk_bytes(a.n_tile));
-  const int smem = kSmemExtra + bias_bytes(a.n_tile, a.n_tiles) + stages * stage_bytes;
+  const int smem = kSmemExtra + bias_bytes(a.n_tile, a.n_tiles) + conv_resident_bytes(a) + stages * conv_stage_bytes(a);
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
   const int grid = total < num_sms ? total : num_sms;

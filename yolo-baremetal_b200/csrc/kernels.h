@@ -90,6 +90,11 @@ struct ConvArgs {
   // of one filter tap per copy (16, 32 or 64).
   int a_tma = 0;
   int a_cpp = 0;
+  // a_tma == 2 (3x3 stride-1 convolutions, see conv_setup_patch): tiles of
+  // 16 x 8 output pixels, tiles_y x tiles_x per image; the 18 x 10 input
+  // patch of a tile is loaded once per 8-channel chunk and plane, and the
+  // weights stay resident in shared memory.
+  int tiles_y = 0, tiles_x = 0;
   alignas(64) CUtensorMap tm_hi;
   alignas(64) CUtensorMap tm_lo;
 };
@@ -100,6 +105,12 @@ struct ConvArgs {
 // (each 64-wide K chunk then holds whole taps).  Leaves `a` unchanged
 // otherwise or when the tensor maps cannot be encoded.
 void conv_setup_tma(ConvArgs* a);
+
+// Switches a 3x3, stride-1, pad-1 convolution with one non-upsampled source,
+// Ci a multiple of 16, Co <= 256 and weights small enough to stay resident
+// in shared memory to the patch mode (a_tma == 2); returns whether it did.
+// Changes m_tiles to the 2-D tile count.
+bool conv_setup_patch(ConvArgs* a);
 
 // Bytes of one packed weight chunk: hi and lo planes of n_tile rows x 128 B.
 inline size_t conv_chunk_bytes(int n_tile) { return static_cast<size_t>(n_tile) * 256; }

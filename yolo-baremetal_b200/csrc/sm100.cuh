@@ -116,6 +116,18 @@ __device__ __forceinline__ void tma_im2col_4d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
+// TMA load of one box of a 4-D tiled tensor map at coordinates (c0..c3),
+// innermost first; out-of-bounds elements arrive as zeros.  c0 * element
+// size must be a multiple of 16 bytes; dst 128-byte aligned.
+__device__ __forceinline__ void tma_tile_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy reads (tensor-core operand fetch).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -188,6 +200,14 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr, uint32_t layout,
   return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
          (static_cast<uint64_t>(sbo >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
          (static_cast<uint64_t>(layout) << 61);
+}
+
+// K-major operand descriptor without swizzle: core matrices of 8 rows x 16
+// bytes stored as 128 contiguous bytes (rows 16 bytes apart), the two core
+// matrices of a 16-wide K step lbo bytes apart, 8-row groups sbo bytes apart.
+__device__ __forceinline__ uint64_t kmajor_desc_noswizzle(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(lbo >> 4) << 16) |
+         (static_cast<uint64_t>(sbo >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
 }
 
 // Instruction descriptor for kind::f16 with bf16 A/B, fp32 D, both K-major:
