@@ -795,7 +795,8 @@ void conv_setup_tma(ConvArgs* a) {
 }
 
 cudaError_t init_conv_kernel_attributes() {
-  return cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  return e == cudaSuccess ? init_stem_kernel_attributes() : e;
 }
 
 cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {

@@ -142,6 +142,8 @@ struct StemArgs {
   SOut out;
 };
 cudaError_t launch_stem(const StemArgs& a, cudaStream_t s);
+// Must run once per device before the first launch_stem (not under capture).
+cudaError_t init_stem_kernel_attributes();
 
 // Depthwise 3x3, pad 1, + bias, optional SiLU (layers.c:269-290 plus
 // detect.c:219-228).  w: device [9][C] (tap-major).  C a multiple of 8.

@@ -22,48 +22,136 @@ __device__ __forceinline__ long long vaddr(const V& v, int b, long long p) {
 }
 
 // ------------------------------------------------------------------ stem conv
-// Reference loop order (layers.c:60-79): sum = bias; for ci, ky, kx: sum += x*w,
-// without contraction to FMA, as the reference is compiled.
+// Direct 3x3 stride-2 pad-1 convolution of the NCHW fp32 input (Ci <= 4),
+// + bias + SiLU, into the split NHWC stage-0 buffer (layers.c:41-81 for the
+// arithmetic, here with fused multiply-add).  Persistent CTAs of 128 threads
+// walk tiles of 8 output rows x (16 * P) columns.  A tile's 17 x (32 P + 1)
+// input patch (every channel) is fetched with 4-byte asynchronous copies
+// into one of two shared buffers while the previous tile computes; thread
+// (r, x) computes the P pixels x, x + 16, ... of row r for all CO channels,
+// so a half-warp's stores cover 16 consecutive pixels.
 template <int CO>
-__global__ void stem_kernel(const StemArgs a) {
-  __shared__ float sw[CO * 4 * 9];
-  __shared__ float sb[CO];
-  const int wn = CO * a.Ci * a.k * a.k;
-  for (int i = threadIdx.x; i < wn; i += blockDim.x) sw[i] = a.w[i];
-  for (int i = threadIdx.x; i < CO; i += blockDim.x) sb[i] = a.bias ? a.bias[i] : 0.f;
-  __syncthreads();
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(a.B) * a.Ho * a.Wo;
-  if (idx >= total) return;
-  const int b = static_cast<int>(idx / (a.Ho * a.Wo));
-  const int r = static_cast<int>(idx - static_cast<long long>(b) * a.Ho * a.Wo);
-  const int oy = r / a.Wo, ox = r - (r / a.Wo) * a.Wo;
-  float acc[CO];
-#pragma unroll
-  for (int c = 0; c < CO; ++c) acc[c] = sb[c];
+struct StemTile {
+  static constexpr int P = 64 / CO;  // pixels per thread
+  static constexpr int TW = 16 * P, TH = 8;
+  // Patch columns start at input column 2 * ox0 - 4 (16-byte aligned when W
+  // is a multiple of 4); the conv reads columns 3 .. 2 TW + 3 of it.
+  static constexpr int PR = 2 * TH + 1, PC = 2 * TW + 4, PCS = PC;
+  static constexpr int kBuf = 4 * PR * PCS;  // floats per patch buffer (Ci <= 4)
+  static constexpr int kSmem = (2 * kBuf + 4 * 9 * CO + CO) * 4;
+};
+
+template <int CO>
+__device__ __forceinline__ void stem_fetch(const StemArgs& a, float* sx, int t, int tiles_x, int tiles_y) {
+  using T = StemTile<CO>;
+  const int b = t / (tiles_x * tiles_y);
+  const int rem = t - b * tiles_x * tiles_y;
+  const int iy0 = (rem / tiles_x) * T::TH * 2 - 1, ix0 = (rem % tiles_x) * T::TW * 2 - 4;
   const long long plane = static_cast<long long>(a.H) * a.W;
   const float* inb = a.in + static_cast<long long>(b) * a.Ci * plane;
-  const int wstride = a.Ci * a.k * a.k;
-  for (int ci = 0; ci < a.Ci; ++ci) {
-    for (int ky = 0; ky < a.k; ++ky) {
-      const int iy = oy * a.stride - a.pad + ky;
-      for (int kx = 0; kx < a.k; ++kx) {
-        const int ix = ox * a.stride - a.pad + kx;
-        if (iy < 0 || iy >= a.H || ix < 0 || ix >= a.W) continue;
-        const float x = __ldg(inb + ci * plane + static_cast<long long>(iy) * a.W + ix);
-        const int wo = (ci * a.k + ky) * a.k + kx;
-#pragma unroll
-        for (int c = 0; c < CO; ++c) acc[c] = __fadd_rn(acc[c], __fmul_rn(x, sw[c * wstride + wo]));
-      }
+  if ((a.W & 3) == 0) {
+    // 16-byte copies of 4 columns; partial or outside chunks zero-filled.
+    constexpr int Q = T::PC / 4;
+    for (int i = threadIdx.x; i < a.Ci * T::PR * Q; i += 128) {
+      const int row = i / Q;
+      const int q = i - row * Q;
+      const int c = row / T::PR;
+      const int rr = row - c * T::PR;
+      const int iy = iy0 + rr, ix = ix0 + 4 * q;
+      const int nvalid = (iy >= 0 && iy < a.H && ix >= 0) ? min(4, a.W - ix) : 0;
+      const float* src = nvalid > 0 ? inb + c * plane + static_cast<long long>(iy) * a.W + ix : inb;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(static_cast<uint32_t>(
+                       __cvta_generic_to_shared(sx + (c * T::PR + rr) * T::PCS + 4 * q))),
+                   "l"(src), "r"(nvalid > 0 ? 4 * nvalid : 0)
+                   : "memory");
+    }
+  } else {
+    for (int i = threadIdx.x; i < a.Ci * T::PR * T::PC; i += 128) {
+      const int c = i / (T::PR * T::PC);
+      const int rr = (i / T::PC) % T::PR;
+      const int cc = i % T::PC;
+      const int iy = iy0 + rr, ix = ix0 + cc;
+      const bool ok = iy >= 0 && iy < a.H && ix >= 0 && ix < a.W;
+      const float* src = ok ? inb + c * plane + static_cast<long long>(iy) * a.W + ix : inb;
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(static_cast<uint32_t>(
+                       __cvta_generic_to_shared(sx + (c * T::PR + rr) * T::PCS + cc))),
+                   "l"(src), "r"(ok ? 4 : 0)
+                   : "memory");
     }
   }
-  uint16_t* o = a.out.hi + vaddr(a.out, b, r);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int CO>
+__global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
+  using T = StemTile<CO>;
+  constexpr int P = T::P;
+  extern __shared__ __align__(16) float stem_smem[];
+  float* sxb = stem_smem;                      // two patch buffers
+  float* sw = stem_smem + 2 * T::kBuf;         // [ci*9 + tap][co]
+  float* sb = sw + 4 * 9 * CO;
+  const int tid = threadIdx.x;
+  const int taps = a.Ci * 9;
+  for (int i = tid; i < CO * taps; i += 128) sw[(i % taps) * CO + i / taps] = a.w[i];
+  for (int i = tid; i < CO; i += 128) sb[i] = a.bias ? a.bias[i] : 0.f;
+  const int tiles_x = (a.Wo + T::TW - 1) / T::TW, tiles_y = (a.Ho + T::TH - 1) / T::TH;
+  const int total = a.B * tiles_x * tiles_y;
+  const int r = tid >> 4, x0 = tid & 15;
+  int k = 0;
+  if (static_cast<int>(blockIdx.x) < total) stem_fetch<CO>(a, sxb, blockIdx.x, tiles_x, tiles_y);
+  for (int t = blockIdx.x; t < total; t += gridDim.x, ++k) {
+    const int tn = t + gridDim.x;
+    if (tn < total) stem_fetch<CO>(a, sxb + ((k + 1) & 1) * T::kBuf, tn, tiles_x, tiles_y);
+    if (tn < total) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const float* sx = sxb + (k & 1) * T::kBuf;
+    float acc[P][CO];
 #pragma unroll
-  for (int c = 0; c < CO; c += 8) {
-    float v[8];
+    for (int j = 0; j < P; ++j)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = a.act == kActSiLU ? silu(acc[c + e]) : acc[c + e];
-    store8(o + c, a.out.plane, v);
+      for (int c = 0; c < CO; ++c) acc[j][c] = sb[c];
+    for (int ci = 0; ci < a.Ci; ++ci) {
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky) {
+        const float* row = sx + (ci * T::PR + 2 * r + ky) * T::PCS;
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          float xv[P];
+#pragma unroll
+          for (int j = 0; j < P; ++j) xv[j] = row[2 * (x0 + 16 * j) + kx + 3];
+          const float* wr = sw + (ci * 9 + ky * 3 + kx) * CO;
+#pragma unroll
+          for (int c = 0; c < CO; c += 4) {
+            const float4 w = *reinterpret_cast<const float4*>(wr + c);
+#pragma unroll
+            for (int j = 0; j < P; ++j) {
+              acc[j][c + 0] = fmaf(xv[j], w.x, acc[j][c + 0]);
+              acc[j][c + 1] = fmaf(xv[j], w.y, acc[j][c + 1]);
+              acc[j][c + 2] = fmaf(xv[j], w.z, acc[j][c + 2]);
+              acc[j][c + 3] = fmaf(xv[j], w.w, acc[j][c + 3]);
+            }
+          }
+        }
+      }
+    }
+    const int b = t / (tiles_x * tiles_y);
+    const int rem = t - b * tiles_x * tiles_y;
+    const int oy = (rem / tiles_x) * T::TH + r;
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const int ox = (rem % tiles_x) * T::TW + x0 + 16 * j;
+      if (oy >= a.Ho || ox >= a.Wo) continue;
+      uint16_t* o = a.out.hi + vaddr(a.out, b, static_cast<long long>(oy) * a.Wo + ox);
+#pragma unroll
+      for (int c = 0; c < CO; c += 8) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = a.act == kActSiLU ? silu_fast(acc[j][c + e]) : acc[j][c + e];
+        store8(o + c, a.out.plane, v);
+      }
+    }
+    __syncthreads();  // this buffer is refilled by the next iteration's prefetch
   }
 }
 
@@ -355,13 +443,29 @@ __global__ void silu_kernel(SOut t, int B, int HW, int C) {
 
 }  // namespace
 
+cudaError_t init_stem_kernel_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(stem_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, StemTile<16>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(stem_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, StemTile<32>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(stem_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, StemTile<64>::kSmem);
+  return e;
+}
+
 cudaError_t launch_stem(const StemArgs& a, cudaStream_t s) {
-  if (a.Ci > 4 || a.k != 3 || (a.Co != 16 && a.Co != 32 && a.Co != 64)) return cudaErrorInvalidValue;
-  const long long total = static_cast<long long>(a.B) * a.Ho * a.Wo;
-  const int t = 128;
-  if (a.Co == 16) stem_kernel<16><<<blocks_for(total, t), t, 0, s>>>(a);
-  else if (a.Co == 32) stem_kernel<32><<<blocks_for(total, t), t, 0, s>>>(a);
-  else stem_kernel<64><<<blocks_for(total, t), t, 0, s>>>(a);
+  if (a.Ci < 1 || a.Ci > 4 || a.k != 3 || a.stride != 2 || a.pad != 1 || (a.Co != 16 && a.Co != 32 && a.Co != 64))
+    return cudaErrorInvalidValue;
+  if (a.Ho != (a.H - 1) / 2 + 1 || a.Wo != (a.W - 1) / 2 + 1) return cudaErrorInvalidValue;
+  const int tw = 16 * (64 / a.Co);
+  const long long tiles = static_cast<long long>(a.B) * ((a.Ho + 7) / 8) * ((a.Wo + tw - 1) / tw);
+  if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned grid = static_cast<unsigned>(tiles < 3LL * sms ? tiles : 3LL * sms);
+  if (a.Co == 16) stem_kernel<16><<<grid, 128, StemTile<16>::kSmem, s>>>(a);
+  else if (a.Co == 32) stem_kernel<32><<<grid, 128, StemTile<32>::kSmem, s>>>(a);
+  else stem_kernel<64><<<grid, 128, StemTile<64>::kSmem, s>>>(a);
   return cudaGetLastError();
 }
 
