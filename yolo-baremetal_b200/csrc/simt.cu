@@ -258,51 +258,42 @@ __global__ void __launch_bounds__(QB) attention_kernel(const AttnArgs a) {
 #pragma unroll
     for (int d = 0; d < KD; ++d) q[d] = 0.f;
   }
-  auto load_k = [&](int k0) {
-    for (int i = threadIdx.x; i < KB * (KD / 8); i += QB) {
-      const int kk = i / (KD / 8), d8 = (i - kk * (KD / 8)) * 8;
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (k0 + kk < N) load8(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + KD + d8, pl, v);
+  // One pass with a running maximum (layers.c:292-308 restated online): for
+  // each key, s = q.k * scale; when s exceeds the running maximum m the
+  // accumulated weights are rescaled by exp(m_old - m_new); then p = exp(s - m)
+  // is added to the sum and p * v to the output.
 #pragma unroll
-      for (int e = 0; e < 8; ++e) sk[kk][d8 + e] = v[e];
-    }
-  };
-  // Pass 1: row maximum of the scaled logits.
-  float mx = -FLT_MAX;
-  for (int k0 = 0; k0 < N; k0 += KB) {
-    __syncthreads();
-    load_k(k0);
-    __syncthreads();
-    const int kn = min(KB, N - k0);
-    for (int kk = 0; kk < kn; ++kk) {
-      float s = 0.f;
-#pragma unroll
-      for (int d = 0; d < KD; ++d) s = __fadd_rn(s, __fmul_rn(q[d], sk[kk][d]));
-      mx = fmaxf(mx, __fmul_rn(s, a.scale));
-    }
-  }
-  // Pass 2: weights, their sum and the weighted sum of v.
+  for (int d = 0; d < KD; ++d) q[d] *= a.scale;
   float o[HD];
 #pragma unroll
   for (int d = 0; d < HD; ++d) o[d] = 0.f;
-  float sum = 0.f;
+  float mx = -FLT_MAX, sum = 0.f;
   for (int k0 = 0; k0 < N; k0 += KB) {
     __syncthreads();
-    load_k(k0);
-    for (int i = threadIdx.x; i < KB * (HD / 8); i += QB) {
-      const int kk = i / (HD / 8), d8 = (i - kk * (HD / 8)) * 8;
+    for (int i = threadIdx.x; i < KB * ((KD + HD) / 8); i += QB) {
+      const int kk = i / ((KD + HD) / 8), d8 = (i - kk * ((KD + HD) / 8)) * 8;
       float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (k0 + kk < N) load8(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + 2 * KD + d8, pl, v);
+      if (k0 + kk < N) load8(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + KD + d8, pl, v);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) sv[kk][d8 + e] = v[e];
+      for (int e = 0; e < 8; ++e) {
+        if (d8 < KD) sk[kk][d8 + e] = v[e];
+        else sv[kk][d8 - KD + e] = v[e];
+      }
     }
     __syncthreads();
     const int kn = min(KB, N - k0);
     for (int kk = 0; kk < kn; ++kk) {
-      float s = 0.f;
+      float sc = 0.f;
 #pragma unroll
-      for (int d = 0; d < KD; ++d) s = __fadd_rn(s, __fmul_rn(q[d], sk[kk][d]));
-      const float e = expf(__fsub_rn(__fmul_rn(s, a.scale), mx));
+      for (int d = 0; d < KD; ++d) sc = fmaf(q[d], sk[kk][d], sc);
+      if (sc > mx) {
+        const float c = __expf(mx - sc);
+        sum *= c;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) o[d] *= c;
+        mx = sc;
+      }
+      const float e = __expf(sc - mx);
       sum += e;
 #pragma unroll
       for (int d = 0; d < HD; ++d) o[d] = fmaf(e, sv[kk][d], o[d]);
@@ -491,7 +482,7 @@ cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
   if (a.kd != 32 || a.hd != 64) return cudaErrorInvalidValue;
-  constexpr int QB = 128, KB = 64;
+  constexpr int QB = 64, KB = 64;
   const int N = a.H * a.W;
   dim3 grid((N + QB - 1) / QB, a.heads, a.B);
   attention_kernel<32, 64, QB, KB><<<grid, QB, 0, s>>>(a);
