@@ -1,0 +1,597 @@
+// INT8 implicit-GEMM convolution for sm_100a: tcgen05.mma kind::i8 with
+// int32 accumulation in tensor memory and the requantisation (bias, 64-bit
+// fixed-point multiply, round-half-even shift, optional SiLU table) fused
+// into the epilogue.  The reference has no INT8 path; the arithmetic is the
+// scheme declared in yb_int8.h.
+//
+// GEMM view as in conv_tc.cu: M = B*Ho*Wo pixels (128 per tile), N = Co
+// (tiles of up to 256), K = kh*kw*ci_pad ordered (ky, kx, ci) in 128-wide
+// chunks, one 128-byte operand row per pixel and chunk.  One 32-wide K step
+// is one UMMA.  Persistent CTA of 320 threads, one per SM:
+//   warp 9     one thread: per chunk the packed weight chunk (bulk copy) and
+//              one TMA im2col copy per filter tap of a_cpp channels (32, 64
+//              or 128: 32B / 64B / 128B swizzled sub-tiles), all completing
+//              on the stage's full barrier.
+//   warp 8     TMEM (2-4 accumulators) and, from one lane, the UMMAs.
+//   warps 0-7  two epilogue groups on alternate tiles, one warp per TMEM
+//              lane quarter: tcgen05.ld, requantise, SiLU table, 16-byte
+//              int8 stores.
+// Every barrier wait is bounded; a timeout sets the error word, stops the
+// other roles, drains the tensor core and frees tensor memory.
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "runtime.h"
+#include "sm100.cuh"
+#include "status.h"
+#include "yb_int8.h"
+
+namespace yb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kKB = 128;                      // K values (= bytes) per chunk
+constexpr uint32_t kATile = kBM * 128;        // activation tile of one chunk
+constexpr int kMmaWarp = 8, kProdWarp = 9;
+constexpr int kThreads = 320;
+constexpr int kSmemLimit = 232448;
+constexpr int kMaxAcc = 4;
+constexpr int kMaxCo = 1024;
+
+struct I8Args {
+  int B = 0, H = 0, W = 0, Ci = 0, Co = 0, kh = 1, kw = 1, stride = 1, pad = 0, Ho = 0, Wo = 0;
+  int K = 0, num_kc = 0, n_tile = 0, n_tiles = 0, m_tiles = 0, a_cpp = 0;
+  const uint8_t* wpack = nullptr;
+  const int32_t* bias = nullptr;
+  const int32_t* mult = nullptr;
+  const int32_t* shift = nullptr;
+  const int8_t* lut = nullptr;
+  int8_t* out = nullptr;
+  int* err = nullptr;
+  alignas(64) CUtensorMap tm;
+};
+
+// Instruction descriptor, kind::i8: signed 8-bit A and B, int32 D, K-major.
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// (p >> sh) rounded half to even, sh >= 1.
+__device__ __forceinline__ long long rshift_rne(long long p, int sh) {
+  long long q = p >> sh;
+  const long long rem = p - (q << sh);
+  const long long half = 1LL << (sh - 1);
+  if (rem > half || (rem == half && (q & 1))) q += 1;
+  return q;
+}
+
+__device__ __forceinline__ void raise_err(int* err, volatile int* abort_flag, int code) {
+  *abort_flag = 1;
+  if (err) atomicCAS(err, 0, code);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_constant__ I8Args a, const int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t chunk_bytes = static_cast<uint32_t>(a.n_tile) * 128u;
+  const uint32_t stage_bytes = kATile + chunk_bytes;
+
+  uint8_t* tail = smem + stages * stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + stages;
+  uint64_t* acc_full = empty + stages;
+  uint64_t* acc_empty = acc_full + kMaxAcc;
+  uint64_t* drain = acc_empty + kMaxAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int nq = a.n_tile * a.n_tiles;
+  int32_t* sbias = reinterpret_cast<int32_t*>(tail + 512);
+  int32_t* smult = sbias + nq;
+  int32_t* sshift = smult + nq;
+  int8_t* slut = reinterpret_cast<int8_t*>(sshift + nq);
+  for (int i = threadIdx.x; i < nq; i += kThreads) {
+    const bool ok = i < a.Co;
+    sbias[i] = ok ? a.bias[i] : 0;
+    smult[i] = ok ? a.mult[i] : 0;
+    sshift[i] = ok ? a.shift[i] : 1;
+  }
+  for (int i = threadIdx.x; i < 256; i += kThreads) slut[i] = a.lut ? a.lut[i] : 0;
+
+  uint32_t acc_stride = 32;
+  while (acc_stride < static_cast<uint32_t>(a.n_tile)) acc_stride <<= 1;
+  const int nacc = min(kMaxAcc, static_cast<int>(512u / acc_stride));
+  const uint32_t ncols = static_cast<uint32_t>(nacc) * acc_stride;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < nacc; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = a.m_tiles * a.n_tiles;
+  const int ks_last = (a.K - (a.num_kc - 1) * kKB + 31) / 32;
+  const int HoWo = a.Ho * a.Wo;
+  const int M = a.B * HoWo;
+
+  if (warp == kProdWarp) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int taps = a.kh * a.kw;
+      const int cpp = a.a_cpp;
+      const int tps = cpp == 128 ? 1 : 128 / cpp;
+      const int cblocks = cpp == 128 ? (taps == 1 ? a.num_kc : a.Ci / 128) : 1;
+      const uint32_t sub_bytes = static_cast<uint32_t>(kBM * cpp);
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+        const int mt = t / a.n_tiles;
+        const int nt = t - mt * a.n_tiles;
+        const int m0 = mt * kBM;
+        const int b = m0 / HoWo;
+        const int r = m0 - b * HoWo;
+        const int oy = r / a.Wo;
+        const int ox = r - oy * a.Wo;
+        const int w0 = ox * a.stride - a.pad, h0 = oy * a.stride - a.pad;
+        const uint8_t* wsrc = a.wpack + static_cast<size_t>(nt) * a.num_kc * chunk_bytes;
+        for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
+          const uint32_t s = it % stages;
+          const uint32_t ph = (it / stages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+            raise_err(a.err, abort_flag, kErrWaitEmpty);
+            goto producer_done;
+          }
+          const int t0 = cpp == 128 ? kc / cblocks : kc * tps;
+          const int c0 = cpp == 128 ? (kc - t0 * cblocks) * 128 : 0;
+          const int ntap = cpp == 128 ? 1 : min(tps, taps - t0);
+          uint8_t* stage = smem + s * stage_bytes;
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ntap) * sub_bytes + chunk_bytes);
+          bulk_g2s(stage + kATile, wsrc + static_cast<size_t>(kc) * chunk_bytes, chunk_bytes, &full[s]);
+          for (int i = 0; i < ntap; ++i) {
+            const int tap = t0 + i;
+            const int ky = tap / a.kw;
+            const int kx = tap - ky * a.kw;
+            tma_im2col_4d(stage + i * sub_bytes, &a.tm, c0, w0, h0, b, static_cast<uint16_t>(kx),
+                          static_cast<uint16_t>(ky), &full[s]);
+          }
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_s8_s32(kBM, a.n_tile);
+      const int cpp = a.a_cpp;
+      const uint32_t layout = cpp == 32 ? 6u : cpp == 64 ? 4u : 2u;
+      const uint32_t sbo = cpp == 32 ? 256u : cpp == 64 ? 512u : 1024u;
+      uint32_t it = 0;
+      int lt = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
+        const int acc = lt % nacc;
+        const uint32_t aph = (lt / nacc) & 1;
+        if (!mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag)) {
+          raise_err(a.err, abort_flag, kErrWaitAccEmpty);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * acc_stride;
+        bool ok = true;
+        for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
+          const uint32_t s = it % stages;
+          const uint32_t ph = (it / stages) & 1u;
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            raise_err(a.err, abort_flag, kErrWaitFull);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * stage_bytes);
+          const uint64_t da0 = kmajor_desc(sa, layout, sbo);
+          const uint64_t db0 = sw128_kmajor_desc(sa + kATile);
+          const int nks = kc == a.num_kc - 1 ? ks_last : kKB / 32;
+#pragma unroll
+          for (int ks = 0; ks < kKB / 32; ++ks) {
+            if (ks >= nks) break;
+            // 16-byte units: a 32-wide K step is one 32B sub-tile, half a 64B
+            // row, or a quarter of a 128B row.
+            const uint64_t aoff = cpp == 32   ? static_cast<uint64_t>(ks * 256)
+                                  : cpp == 64 ? static_cast<uint64_t>((ks >> 1) * 512 + (ks & 1) * 2)
+                                              : static_cast<uint64_t>(ks * 2);
+            tc_mma_i8(d_tmem, da0 + aoff, db0 + static_cast<uint64_t>(ks * 2), idesc, (kc | ks) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);
+      }
+      tc_commit(drain);
+      bool drained = mbar_try_wait(drain, 0);
+      const uint64_t t0 = globaltimer_ns();
+      while (!drained && globaltimer_ns() - t0 < kWaitNs) drained = mbar_try_wait(drain, 0);
+      if (!drained) raise_err(a.err, abort_flag, kErrDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int grp = warp >> 2;
+    for (int t = blockIdx.x + grp * gridDim.x, lt = grp; t < total_tiles; t += 2 * gridDim.x, lt += 2) {
+      const int acc = lt % nacc;
+      const uint32_t aph = (lt / nacc) & 1;
+      if (!mbar_wait(&acc_full[acc], aph, abort_flag)) {
+        raise_err(a.err, abort_flag, kErrWaitAccFull);
+        break;
+      }
+      tc_fence_after();
+      const int mt = t / a.n_tiles;
+      const int nt = t - mt * a.n_tiles;
+      const int n0 = nt * a.n_tile;
+      const int nvalid = min(a.n_tile, a.Co - n0);
+      const int m = mt * kBM + q * 32 + lane;
+      const bool valid = m < M;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_stride;
+      int8_t* op = a.out + static_cast<long long>(valid ? m : 0) * a.Co + n0;
+      for (int c = 0; c < nvalid; c += 16) {
+        uint32_t r[16];
+        tc_ld_32x32b_x16(tbase + c, r);
+        tc_wait_ld();
+        uint32_t packed[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int ch = n0 + c + e;
+          const long long v = static_cast<long long>(static_cast<int32_t>(r[e])) + sbias[ch];
+          const long long y = rshift_rne(v * smult[ch], sshift[ch]);
+          int o;
+          if (a.lut) {
+            const int idx = static_cast<int>(y < -128 ? -128 : y > 127 ? 127 : y);
+            o = slut[idx + 128];
+          } else {
+            o = static_cast<int>(y < -127 ? -127 : y > 127 ? 127 : y);
+          }
+          packed[e >> 2] |= (static_cast<uint32_t>(o) & 0xFFu) << (8 * (e & 3));
+        }
+        if (valid) *reinterpret_cast<uint4*>(op + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  if (*abort_flag) __nanosleep(100000);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, ncols);
+  }
+}
+
+// ------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeIm2col_v12000 i8_im2col_encoder() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+  });
+  return fn;
+}
+
+inline uint32_t sw128_off(uint32_t row, uint32_t chunk16) {
+  return (row >> 3) * 1024u + (row & 7u) * 128u + ((chunk16 ^ (row & 7u)) << 4);
+}
+
+struct Int8Conv {
+  int device = 0;
+  int co = 0, ci = 0, ci_pad = 0, kh = 1, kw = 1, stride = 1, pad = 0;
+  int n_tile = 0, n_tiles = 0, K = 0, num_kc = 0, a_cpp = 0;
+  uint8_t* wpack = nullptr;
+  int32_t* bias = nullptr;
+  int32_t* mult = nullptr;
+  int32_t* shift = nullptr;
+  int8_t* lut = nullptr;
+  int* err = nullptr;
+  int sms = 148;
+};
+
+int stages_for_i8(int n_tile, int n_tiles) {
+  const int stage = static_cast<int>(kATile) + n_tile * 128;
+  const int extra = 1024 + 512 + 3 * 4 * n_tile * n_tiles + 256;
+  const int st = (kSmemLimit - extra) / stage;
+  return st > 8 ? 8 : st;
+}
+
+status_t free_conv(Int8Conv* c) {
+  if (!c) return SUCCESS;
+  cudaSetDevice(c->device);
+  for (void* p : {static_cast<void*>(c->wpack), static_cast<void*>(c->bias), static_cast<void*>(c->mult),
+                  static_cast<void*>(c->shift), static_cast<void*>(c->lut), static_cast<void*>(c->err)})
+    if (p) cudaFree(p);
+  delete c;
+  return SUCCESS;
+}
+
+}  // namespace
+}  // namespace yb
+
+using namespace yb;
+
+extern "C" status_t yb_int8_quantize_conv(const float* w, const float* b, int co, int ci, int kh, int kw, float s_in,
+                                          float s_pre, float s_out, int act_silu, int8_t* wq, int32_t* bq,
+                                          int32_t* mult, int32_t* shift, int8_t* lut) {
+  if (!w || !wq || !bq || !mult || !shift || (act_silu && !lut)) return ERROR_NULL_POINTER;
+  if (co < 1 || ci < 1 || kh < 1 || kw < 1 || !(s_in > 0.f) || !(s_out > 0.f) || (act_silu && !(s_pre > 0.f)))
+    return ERROR_INVALID_DIMS;
+  const size_t per = static_cast<size_t>(ci) * kh * kw;
+  for (int c = 0; c < co; ++c) {
+    const float* wc = w + c * per;
+    float m = 0.f;
+    for (size_t i = 0; i < per; ++i) m = std::fmax(m, std::fabs(wc[i]));
+    const float sw = m > 0.f ? m / 127.0f : 1.0f;
+    for (size_t i = 0; i < per; ++i) {
+      const float qv = std::nearbyint(wc[i] / sw);
+      wq[c * per + i] = static_cast<int8_t>(qv < -127.f ? -127 : qv > 127.f ? 127 : static_cast<int>(qv));
+    }
+    long long bv = b ? std::llrint(static_cast<double>(b[c]) / (static_cast<double>(s_in) * sw)) : 0;
+    bv = bv < -INT_MAX ? -INT_MAX : bv > INT_MAX ? INT_MAX : bv;
+    bq[c] = static_cast<int32_t>(bv);
+    const double ratio = static_cast<double>(s_in) * sw / static_cast<double>(act_silu ? s_pre : s_out);
+    int e = 0;
+    const double f = std::frexp(ratio, &e);
+    long long mm = std::llrint(f * 2147483648.0);
+    if (mm == 2147483648LL) {
+      mm = 1073741824LL;
+      e += 1;
+    }
+    const int sh = 31 - e;
+    if (sh < 1) {
+      set_error("int8 requantisation ratio s_in*s_w/s_t is 2^30 or more");
+      return ERROR_INVALID_DIMS;
+    }
+    if (sh > 62) {
+      mult[c] = 0;
+      shift[c] = 1;
+    } else {
+      mult[c] = static_cast<int32_t>(mm);
+      shift[c] = sh;
+    }
+  }
+  if (act_silu) {
+    for (int i = 0; i < 256; ++i) {
+      const double x = static_cast<double>(i - 128) * s_pre;
+      const double y = x / (1.0 + std::exp(-x));
+      const long long qv = std::llrint(y / static_cast<double>(s_out));
+      lut[i] = static_cast<int8_t>(qv < -127 ? -127 : qv > 127 ? 127 : qv);
+    }
+  }
+  return SUCCESS;
+}
+
+extern "C" status_t yb_int8_conv_create(int device, const int8_t* wq, const int32_t* bq, const int32_t* mult,
+                                        const int32_t* shift, const int8_t* lut, int co, int ci, int kh, int kw,
+                                        int stride, int pad, void** conv) {
+  if (!wq || !bq || !mult || !shift || !conv) return ERROR_NULL_POINTER;
+  *conv = nullptr;
+  if (co < 16 || co > kMaxCo || co % 16 || ci < 1 || kh != kw || (kh != 1 && kh != 3) || stride < 1 || pad < 0) {
+    set_error("int8 conv: co must be a multiple of 16 (<= 1024), kernel 1x1 or 3x3");
+    return ERROR_INVALID_DIMS;
+  }
+  for (int c = 0; c < co; ++c)
+    if (shift[c] < 1 || shift[c] > 62) {
+      set_error("int8 conv: shift outside [1, 62]");
+      return ERROR_INVALID_DIMS;
+    }
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  auto* c = new Int8Conv();
+  c->device = device;
+  c->co = co;
+  c->ci = ci;
+  c->kh = kh;
+  c->kw = kw;
+  c->stride = stride;
+  c->pad = pad;
+  const int taps = kh * kw;
+  if (taps == 1) {
+    c->ci_pad = (ci + 31) / 32 * 32;
+    c->a_cpp = 128;
+  } else {
+    c->ci_pad = ci <= 32 ? 32 : ci <= 64 ? 64 : (ci + 127) / 128 * 128;
+    c->a_cpp = c->ci_pad <= 64 ? c->ci_pad : 128;
+  }
+  c->K = taps * c->ci_pad;
+  c->num_kc = (c->K + kKB - 1) / kKB;
+  const int tiles = (co + 255) / 256;
+  const int per = (co + tiles - 1) / tiles;
+  c->n_tile = (per + 15) / 16 * 16;
+  c->n_tiles = tiles;
+  cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
+  // Packed weights: per N tile and K chunk, n_tile rows of 128 bytes, 128B
+  // swizzled, K = (ky, kx, ci) with ci < ci_pad.
+  const size_t chunk = static_cast<size_t>(c->n_tile) * 128;
+  std::vector<uint8_t> pk(static_cast<size_t>(c->n_tiles) * c->num_kc * chunk, 0);
+  for (int nt = 0; nt < c->n_tiles; ++nt)
+    for (int kc = 0; kc < c->num_kc; ++kc) {
+      uint8_t* dst = pk.data() + (static_cast<size_t>(nt) * c->num_kc + kc) * chunk;
+      for (int rrow = 0; rrow < c->n_tile; ++rrow) {
+        const int n = nt * c->n_tile + rrow;
+        if (n >= co) continue;
+        for (int kk = 0; kk < kKB; ++kk) {
+          const int k = kc * kKB + kk;
+          if (k >= c->K) break;
+          const int tap = k / c->ci_pad;
+          const int cc = k - tap * c->ci_pad;
+          if (cc >= ci) continue;
+          const int ky = tap / kw, kx = tap - (tap / kw) * kw;
+          const int8_t v = wq[((static_cast<size_t>(n) * ci + cc) * kh + ky) * kw + kx];
+          dst[sw128_off(static_cast<uint32_t>(rrow), static_cast<uint32_t>(kk >> 4)) + (kk & 15)] =
+              static_cast<uint8_t>(v);
+        }
+      }
+    }
+  const size_t nq = static_cast<size_t>(c->n_tile) * c->n_tiles;
+  std::vector<int32_t> hb(nq, 0), hm(nq, 0), hs(nq, 1);
+  for (int i = 0; i < co; ++i) {
+    hb[i] = bq[i];
+    hm[i] = mult[i];
+    hs[i] = shift[i];
+  }
+  if ((e = cudaMalloc(&c->wpack, pk.size())) == cudaSuccess &&
+      (e = cudaMalloc(&c->bias, nq * 4)) == cudaSuccess && (e = cudaMalloc(&c->mult, nq * 4)) == cudaSuccess &&
+      (e = cudaMalloc(&c->shift, nq * 4)) == cudaSuccess && (e = cudaMalloc(&c->err, sizeof(int))) == cudaSuccess &&
+      (!lut || (e = cudaMalloc(&c->lut, 256)) == cudaSuccess)) {
+    e = cudaMemcpy(c->wpack, pk.data(), pk.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->bias, hb.data(), nq * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->mult, hm.data(), nq * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->shift, hs.data(), nq * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && lut) e = cudaMemcpy(c->lut, lut, 256, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof(int));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(conv_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  }
+  if (e != cudaSuccess) {
+    const status_t st = cuda_status(e, "int8 conv upload");
+    free_conv(c);
+    return st;
+  }
+  if (stages_for_i8(c->n_tile, c->n_tiles) < 2) {
+    free_conv(c);
+    set_error("int8 conv: tile does not fit in shared memory");
+    return ERROR_INVALID_DIMS;
+  }
+  *conv = c;
+  return SUCCESS;
+}
+
+extern "C" int yb_int8_conv_ci_pad(void* conv) { return conv ? static_cast<Int8Conv*>(conv)->ci_pad : 0; }
+
+extern "C" status_t yb_int8_conv_run(void* conv, const int8_t* d_x, int B, int H, int W, int8_t* d_y, void* stream) {
+  auto* c = static_cast<Int8Conv*>(conv);
+  if (!c || !d_x || !d_y) return ERROR_NULL_POINTER;
+  if (B < 1 || H < 1 || W < 1) return ERROR_INVALID_DIMS;
+  const int Ho = (H + 2 * c->pad - c->kh) / c->stride + 1, Wo = (W + 2 * c->pad - c->kw) / c->stride + 1;
+  if (Ho < 1 || Wo < 1) return ERROR_INVALID_DIMS;
+  const long long M = static_cast<long long>(B) * Ho * Wo;
+  if (M > INT_MAX - 256 || static_cast<long long>(B) * H * W * c->ci_pad > (1LL << 40)) return ERROR_INVALID_DIMS;
+  if (reinterpret_cast<uintptr_t>(d_x) % 16 || reinterpret_cast<uintptr_t>(d_y) % 16) {
+    set_error("int8 conv: buffers must be 16-byte aligned");
+    return ERROR_INVALID_DIMS;
+  }
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  I8Args a;
+  a.B = B;
+  a.H = H;
+  a.W = W;
+  a.Ci = c->ci_pad;
+  a.Co = c->co;
+  a.kh = c->kh;
+  a.kw = c->kw;
+  a.stride = c->stride;
+  a.pad = c->pad;
+  a.Ho = Ho;
+  a.Wo = Wo;
+  a.K = c->K;
+  a.num_kc = c->num_kc;
+  a.n_tile = c->n_tile;
+  a.n_tiles = c->n_tiles;
+  a.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  a.a_cpp = c->a_cpp;
+  a.wpack = c->wpack;
+  a.bias = c->bias;
+  a.mult = c->mult;
+  a.shift = c->shift;
+  a.lut = c->lut;
+  a.out = d_y;
+  a.err = c->err;
+  const auto enc = i8_im2col_encoder();
+  if (!enc) {
+    set_error("int8 conv: cuTensorMapEncodeIm2col unavailable");
+    return ERROR_DEVICE;
+  }
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(c->ci_pad), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(c->ci_pad), static_cast<cuuint64_t>(c->ci_pad) * W,
+                           static_cast<cuuint64_t>(c->ci_pad) * W * H};
+  int lower[2] = {-c->pad, -c->pad};
+  int upper[2] = {c->pad - (c->kw - 1), c->pad - (c->kh - 1)};
+  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(c->stride), static_cast<cuuint32_t>(c->stride), 1};
+  const CUtensorMapSwizzle sw = c->a_cpp == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                                : c->a_cpp == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                 : CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUresult cr = enc(&a.tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(d_x), dims, strides, lower,
+                          upper, static_cast<cuuint32_t>(c->a_cpp), static_cast<cuuint32_t>(kBM), estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) {
+    set_error("int8 conv: tensor map encoding failed (code " + std::to_string(static_cast<int>(cr)) + ")");
+    return ERROR_INVALID_DIMS;
+  }
+  const int stages = stages_for_i8(c->n_tile, c->n_tiles);
+  const int smem = 1024 + 512 + 3 * 4 * c->n_tile * c->n_tiles + 256 + stages * (static_cast<int>(kATile) + c->n_tile * 128);
+  const int total = a.m_tiles * a.n_tiles;
+  const int grid = total < c->sms ? total : c->sms;
+  conv_i8_kernel<<<grid, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(a, stages);
+  return cuda_status(cudaGetLastError(), "int8 conv launch");
+}
+
+extern "C" status_t yb_int8_conv_check(void* conv) {
+  auto* c = static_cast<Int8Conv*>(conv);
+  if (!c) return ERROR_NULL_POINTER;
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  int k = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&k, c->err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "int8 conv check");
+  if (k) {
+    cudaMemset(c->err, 0, sizeof(int));
+    set_error("int8 conv kernel reported error code " + std::to_string(k));
+    return ERROR_DEVICE;
+  }
+  return SUCCESS;
+}
+
+extern "C" status_t yb_int8_conv_destroy(void* conv) {
+  if (!conv) return ERROR_NULL_POINTER;
+  const status_t st = yb_int8_conv_check(conv);
+  free_conv(static_cast<Int8Conv*>(conv));
+  return st;
+}
