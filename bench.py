@@ -386,6 +386,8 @@ def run_ours(args):
                 "forward_share": {k: round(v["share"], 4) for k, v in per_kind.items()},
                 "clocks": clocks}
     model.close()
+    if rank == 0 and not args.no_int8_sweep:
+        line["int8_conv_sweep"] = int8_conv_sweep(peaks()[0])
     if dist:
         dist.barrier()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -395,6 +397,73 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
+
+
+# The isolated conv shapes of the benchmark's conv-GEMM sweep: (ci, co, k, stride, H = W).
+INT8_SWEEP = [(3, 16, 3, 2, 640), (16, 32, 3, 2, 320), (64, 64, 1, 1, 160), (128, 128, 3, 1, 40), (256, 256, 3, 1, 20)]
+INT8_PEAK_TOPS_NOMINAL = 4500.0  # dense int8 tensor throughput of one B200 (datasheet; not measured on this pool)
+
+
+def int8_conv_sweep(hbm_gbs, batch=16, reps=30):
+    """Device-resident timing of the INT8 convolution (yb_int8_conv_run) on
+    the sweep shapes, 16 images per launch, CUDA events on a dedicated stream
+    over `reps` launches after 5 warm-up launches.  ops = 2 x MACs of the
+    real channels; bytes = int8 input + output + weights once."""
+    import numpy as np
+    import torch
+
+    import yolo_b200 as yb
+
+    L = yb.lib()
+    stream = torch.cuda.Stream()
+    rows = []
+    tot_ops = tot_ms = 0.0
+    for ci, co, k, stride, hw in INT8_SWEEP:
+        rng = np.random.default_rng(ci * 1000 + co)
+        w = (rng.standard_normal((co, ci, k, k)) * np.sqrt(2.0 / (ci * k * k))).astype(np.float32)
+        b = (rng.standard_normal(co) * 0.1).astype(np.float32)
+        wq = np.zeros((co, ci, k, k), np.int8)
+        bq, mult, shift = (np.zeros(co, np.int32) for _ in range(3))
+        lut = np.zeros(256, np.int8)
+        yb.check(L.yb_int8_quantize_conv(w.ctypes.data, b.ctypes.data, co, ci, k, k, 0.02, 0.05, 0.05, 1,
+                                         wq.ctypes.data, bq.ctypes.data, mult.ctypes.data, shift.ctypes.data,
+                                         lut.ctypes.data), "yb_int8_quantize_conv")
+        h = C.c_void_p()
+        pad = (k - 1) // 2
+        yb.check(L.yb_int8_conv_create(torch.cuda.current_device(), wq.ctypes.data, bq.ctypes.data,
+                                       mult.ctypes.data, shift.ctypes.data, lut.ctypes.data, co, ci, k, k, stride,
+                                       pad, C.byref(h)), "yb_int8_conv_create")
+        cp = L.yb_int8_conv_ci_pad(h)
+        x = torch.zeros((batch, hw, hw, cp), dtype=torch.int8, device="cuda")
+        x[..., :ci] = torch.randint(-127, 128, (batch, hw, hw, ci), dtype=torch.int8, device="cuda")
+        ho = (hw + 2 * pad - k) // stride + 1
+        y = torch.empty((batch, ho, ho, co), dtype=torch.int8, device="cuda")
+        torch.cuda.synchronize()
+        run = lambda: yb.check(L.yb_int8_conv_run(h, x.data_ptr(), batch, hw, hw, y.data_ptr(),  # noqa: E731
+                                                  C.c_void_p(stream.cuda_stream)), "yb_int8_conv_run")
+        for _ in range(5):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        yb.check(L.yb_int8_conv_check(h), "yb_int8_conv_check")
+        L.yb_int8_conv_destroy(h)
+        ops = 2.0 * batch * ho * ho * co * ci * k * k
+        nbytes = batch * hw * hw * ci + batch * ho * ho * co + co * ci * k * k
+        tot_ops += ops
+        tot_ms += ms
+        rows.append({"shape": f"{ci}->{co} {k}x{k} s{stride} @{hw}x{hw}", "ms": round(ms, 5),
+                     "tops": round(ops / (ms * 1e-3) / 1e12, 2), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                     "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm_gbs, 3)})
+    tops = tot_ops / (tot_ms * 1e-3) / 1e12
+    return {"images_per_launch": batch, "shapes": rows, "tops_all_shapes": round(tops, 2),
+            "peak_tops": INT8_PEAK_TOPS_NOMINAL, "frac": round(tops / INT8_PEAK_TOPS_NOMINAL, 4),
+            "peak_source": "nominal dense int8 (datasheet), not measured",
+            "note": "bit-exact against the CPU INT8 oracle (tests/test_gpu_int8.py); small maps fit in L2"}
 
 
 class OpStat(C.Structure):
@@ -411,6 +480,7 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--hw", type=int, default=640)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-int8-sweep", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

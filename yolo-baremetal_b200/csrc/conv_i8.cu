@@ -73,13 +73,11 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint6
       : "memory");
 }
 
-// (p >> sh) rounded half to even, sh >= 1.
+// (p >> sh) rounded half to even, sh >= 1, without branches: with
+// p = q*2^sh + r (q = floor), adding 2^(sh-1) - 1 + (q & 1) carries into q
+// exactly when r > half, or r == half and q is odd.  |p| <= 2^62 here.
 __device__ __forceinline__ long long rshift_rne(long long p, int sh) {
-  long long q = p >> sh;
-  const long long rem = p - (q << sh);
-  const long long half = 1LL << (sh - 1);
-  if (rem > half || (rem == half && (q & 1))) q += 1;
-  return q;
+  return (p + ((1LL << (sh - 1)) - 1) + ((p >> sh) & 1)) >> sh;
 }
 
 __device__ __forceinline__ void raise_err(int* err, volatile int* abort_flag, int code) {
@@ -264,14 +262,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       const int m = mt * kBM + q * 32 + lane;
       const bool valid = m < M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_stride;
-      int8_t* op = a.out + static_cast<long long>(valid ? m : 0) * a.Co + n0;
-      for (int c = 0; c < nvalid; c += 16) {
-        uint32_t r[16];
-        tc_ld_32x32b_x16(tbase + c, r);
+      const long long po = static_cast<long long>(valid ? m : 0) * a.Co + n0;
+      // Units of 32 channels: two TMEM loads, requantise, then lanes 2k and
+      // 2k+1 write the two 16-byte halves of one pixel's 32-byte run.
+      for (int c = 0; c < nvalid; c += 32) {
+        const bool two = c + 16 < nvalid;
+        uint32_t r[32];
+        uint32_t(&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[0]);
+        uint32_t(&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[16]);
+        tc_ld_32x32b_x16(tbase + c, r0);
+        if (two) tc_ld_32x32b_x16(tbase + c + 16, r1);
         tc_wait_ld();
-        uint32_t packed[4] = {0u, 0u, 0u, 0u};
+        uint32_t packed[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
+        for (int e = 0; e < 32; ++e) {
+          if (e >= 16 && !two) break;
           const int ch = n0 + c + e;
           const long long v = static_cast<long long>(static_cast<int32_t>(r[e])) + sbias[ch];
           const long long y = rshift_rne(v * smult[ch], sshift[ch]);
@@ -284,7 +289,22 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
           }
           packed[e >> 2] |= (static_cast<uint32_t>(o) & 0xFFu) << (8 * (e & 3));
         }
-        if (valid) *reinterpret_cast<uint4*>(op + c) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        const int h = lane & 1;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int src = (lane >> 1) + 16 * i;
+          uint32_t w[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = __shfl_sync(0xffffffffu, packed[j], src);
+            const uint32_t hi = __shfl_sync(0xffffffffu, packed[4 + j], src);
+            w[j] = h ? hi : lo;
+          }
+          const long long spo = __shfl_sync(0xffffffffu, po, src);
+          const bool svalid = __shfl_sync(0xffffffffu, valid, src);
+          if (svalid && (h == 0 || two))
+            *reinterpret_cast<uint4*>(a.out + spo + c + 16 * h) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
       tc_fence_before();
       __syncwarp();
