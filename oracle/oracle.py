@@ -37,6 +37,10 @@ def _collector(store: "OrderedDict[str, np.ndarray]"):
     return STAGE_CB(cb)
 
 
+I8_STAGE_CB = C.CFUNCTYPE(None, C.c_void_p, C.c_char_p, C.POINTER(C.c_int8), C.POINTER(C.c_float), C.c_int,
+                          C.c_int, C.c_int)
+
+
 class Oracle:
     _lib = None
 
@@ -68,6 +72,13 @@ class Oracle:
                                      C.c_int, _f32p, C.c_int]
             lib.orc_c2psa.argtypes = [C.c_void_p, C.c_char_p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int]
             lib.orc_c3.argtypes = [C.c_void_p, C.c_char_p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int]
+            lib.orc_stats_enable.argtypes = [C.c_void_p, C.c_int]
+            lib.orc_stats_count.argtypes = [C.c_void_p]
+            lib.orc_stats_entry.argtypes = [C.c_void_p, C.c_int, C.c_char_p, C.c_int, C.POINTER(C.c_float)]
+            lib.orc_nc.argtypes = [C.c_void_p]
+            lib.orc_i8_forward.argtypes = [C.c_void_p, C.POINTER(C.c_char_p), C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                           C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, I8_STAGE_CB,
+                                           C.c_void_p]
             lib.orc_psablock.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
             lib.orc_dwconv.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
             cls._lib = lib
@@ -118,6 +129,53 @@ class Oracle:
         if st != 0:
             raise RuntimeError(f"orc_forward status {st}")
         return {"dets": dets.reshape(max_det, 6), "logits": logits.reshape(N, -1), "boxes": boxes.reshape(N, 4),
+                "stages": store}
+
+    # ---------------------------------------------------------------- INT8
+    def calibrate(self, images) -> "OrderedDict[str, float]":
+        """Scale table (name -> max|x| / 127, 1.0 for an all-zero tensor) from
+        FP32 forwards of `images` ([n,3,H,W])."""
+        L = self.lib()
+        L.orc_stats_enable(self.h, 1)
+        try:
+            for img in images:
+                self.forward(img[None])
+            table: "OrderedDict[str, float]" = OrderedDict()
+            name = C.create_string_buffer(128)
+            v = C.c_float()
+            for i in range(L.orc_stats_count(self.h)):
+                L.orc_stats_entry(self.h, i, name, 128, C.byref(v))
+                a = np.float32(v.value)
+                table[name.value.decode()] = float(a / np.float32(127.0)) if a > 0 else 1.0
+        finally:
+            L.orc_stats_enable(self.h, 0)
+        return table
+
+    def forward_i8(self, img: np.ndarray, scales, max_det: int = 300, stages: bool = False):
+        """INT8 forward of img [1,3,H,W] under the scale table `scales`:
+        dict(dets, logits [N,nc], dist [N,4], stages {name: (int8 [C,H,W], scales [C])})."""
+        L = self.lib()
+        x = np.ascontiguousarray(img, dtype=np.float32).reshape(-1)
+        H, W = img.shape[-2], img.shape[-1]
+        N = L.orc_anchors(H, W)
+        nc = L.orc_nc(self.h)
+        names = (C.c_char_p * len(scales))(*[k.encode() for k in scales])
+        vals = np.array(list(scales.values()), dtype=np.float32)
+        dets = np.zeros(max_det * 6, np.float32)
+        logits = np.zeros(N * nc, np.float32)
+        dist = np.zeros(N * 4, np.float32)
+        store: "OrderedDict[str, tuple]" = OrderedDict()
+
+        def _cb(_u, name, data, sc, c, h, w):
+            store[name.decode()] = (np.ctypeslib.as_array(data, shape=(c * h * w,)).copy().reshape(c, h, w),
+                                    np.ctypeslib.as_array(sc, shape=(c,)).copy())
+
+        cb = I8_STAGE_CB(_cb) if stages else I8_STAGE_CB()
+        st = L.orc_i8_forward(self.h, names, vals.ctypes.data, len(vals), x.ctypes.data, H, W, max_det,
+                              dets.ctypes.data, logits.ctypes.data, dist.ctypes.data, cb, None)
+        if st != 0:
+            raise RuntimeError(f"orc_i8_forward status {st}")
+        return {"dets": dets.reshape(max_det, 6), "logits": logits.reshape(N, nc), "dist": dist.reshape(N, 4),
                 "stages": store}
 
     @classmethod

@@ -35,10 +35,50 @@ typedef struct {
 } orc_tensor;
 
 typedef struct {
+    char name[96];
+    float v;
+} orc_stat;
+
+typedef struct {
     orc_tensor* t;
     int n, cap;
     int nc;
+    /* Calibration statistics (max |x| per named tensor) when stats_on. */
+    orc_stat* st;
+    int st_n, st_cap, stats_on;
 } orc_model;
+
+/* Max |x| of the last conv/dwconv call: before the activation, and of its
+ * output (the oracle is single-threaded). */
+static float g_pre_absmax, g_out_absmax;
+
+static void stat_rec(orc_model* m, const char* name, float v) {
+    if (!m->stats_on) return;
+    for (int i = 0; i < m->st_n; ++i)
+        if (strcmp(m->st[i].name, name) == 0) {
+            if (v > m->st[i].v) m->st[i].v = v;
+            return;
+        }
+    if (m->st_n == m->st_cap) {
+        const int cap = m->st_cap ? 2 * m->st_cap : 256;
+        orc_stat* t = (orc_stat*)realloc(m->st, (size_t)cap * sizeof(orc_stat));
+        if (!t) return;
+        m->st = t;
+        m->st_cap = cap;
+    }
+    snprintf(m->st[m->st_n].name, sizeof m->st[m->st_n].name, "%s", name);
+    m->st[m->st_n].v = v;
+    m->st_n++;
+}
+
+static float absmax_of(const float* d, size_t n) {
+    float a = 0.0f;
+    for (size_t i = 0; i < n; ++i) {
+        const float v = fabsf(d[i]);
+        if (v > a) a = v;
+    }
+    return a;
+}
 
 typedef struct {
     float* d;
@@ -197,8 +237,12 @@ static void conv(fmap* out, const fmap* in, const orc_tensor* w, const orc_tenso
             }
             if (b)
                 for (int p = 0; p < P; ++p) y[p] += b->data[o];
+            for (int p = 0; p < P; ++p)
+                if (fabsf(y[p]) > g_pre_absmax) g_pre_absmax = fabsf(y[p]);
             if (act)
                 for (int p = 0; p < P; ++p) y[p] = silu1(y[p]);
+            for (int p = 0; p < P; ++p)
+                if (fabsf(y[p]) > g_out_absmax) g_out_absmax = fabsf(y[p]);
         }
         return;
     }
@@ -219,7 +263,10 @@ static void conv(fmap* out, const fmap* in, const orc_tensor* w, const orc_tenso
                         }
                     }
                 }
-                out->d[((size_t)o * Ho + oy) * Wo + ox] = act ? silu1(s) : s;
+                const float r = act ? silu1(s) : s;
+                if (fabsf(s) > g_pre_absmax) g_pre_absmax = fabsf(s);
+                if (fabsf(r) > g_out_absmax) g_out_absmax = fabsf(r);
+                out->d[((size_t)o * Ho + oy) * Wo + ox] = r;
             }
         }
     }
@@ -242,7 +289,10 @@ static void dwconv(fmap* out, const fmap* in, const orc_tensor* w, const orc_ten
                         s = s + prod;
                     }
                 }
-                out->d[((size_t)c * H + y) * W + x] = act ? silu1(s) : s;
+                const float r = act ? silu1(s) : s;
+                if (fabsf(s) > g_pre_absmax) g_pre_absmax = fabsf(s);
+                if (fabsf(r) > g_out_absmax) g_out_absmax = fabsf(r);
+                out->d[((size_t)c * H + y) * W + x] = r;
             }
         }
     }
@@ -279,8 +329,21 @@ static int conv_named(orc_model* m, const char* prefix, fmap* out, const fmap* i
     orc_tensor* b = findf(m, "%s.conv.bias", prefix);
     if (!w || !b) return ORC_ERR_MISSING;
     if (w->dims[1] != in->c || w->dims[0] != out->c) return ORC_ERR_DIMS;
+    g_pre_absmax = g_out_absmax = 0.0f;
     conv(out, in, w, b, stride, pad, act);
+    if (m->stats_on) {
+        char nm[120];
+        if (act) {
+            snprintf(nm, sizeof nm, "%s:pre", prefix);
+            stat_rec(m, nm, g_pre_absmax);
+        }
+        stat_rec(m, prefix, g_out_absmax);
+    }
     return ORC_OK;
+}
+
+static void stat_map(orc_model* m, const char* name, const fmap* f) {
+    if (m->stats_on) stat_rec(m, name, absmax_of(f->d, (size_t)f->c * f->h * f->w));
 }
 
 /* Bottleneck (layers.c:92-108). */
@@ -295,7 +358,10 @@ static int bottleneck(orc_model* m, const char* p, fmap* out, const fmap* in, in
     int st = conv_named(m, n1, &t, in, 1, (w1->dims[2] - 1) / 2, 1);
     if (st == ORC_OK) st = conv_named(m, n2, out, &t, 1, (w2->dims[2] - 1) / 2, 1);
     fm_free(&t);
-    if (st == ORC_OK && shortcut) add_into(out, in);
+    if (st == ORC_OK && shortcut) {
+        add_into(out, in);
+        stat_map(m, n2, out);
+    }
     return st;
 }
 
@@ -401,7 +467,11 @@ static int sppf(orc_model* m, const char* L, int k, int n_pool, int shortcut, fm
     }
     snprintf(nm, sizeof nm, "%s.cv2", L);
     if (st == ORC_OK) st = conv_named(m, nm, out, &cat, 1, 0, 1);
-    if (st == ORC_OK && shortcut && in->c == out->c) add_into(out, in);
+    if (st == ORC_OK && shortcut && in->c == out->c) {
+        add_into(out, in);
+        snprintf(nm, sizeof nm, "%s.cv2", L);
+        stat_map(m, nm, out);
+    }
     fm_free(&cat);
     return st;
 }
@@ -459,6 +529,8 @@ static int attention(orc_model* m, const char* P, int heads, float ratio, fmap* 
     fmap pe = fm_new(dim, in->h, in->w);
     dwconv(&pe, &vpe, pe_w, pe_b, 0);
     add_into(&ao, &pe);
+    snprintf(nm, sizeof nm, "%s.attn.ope", P);
+    stat_map(m, nm, &ao);
     snprintf(nm, sizeof nm, "%s.attn.proj", P);
     if (st == ORC_OK) st = conv_named(m, nm, out, &ao, 1, 0, 0);
     fm_free(&pe);
@@ -475,13 +547,21 @@ static int psablock(orc_model* m, const char* P, int heads, float ratio, int sho
     if (!f0) return ORC_ERR_MISSING;
     fmap x1 = fm_new(in->c, in->h, in->w);
     int st = attention(m, P, heads, ratio, &x1, in);
-    if (st == ORC_OK && shortcut) add_into(&x1, in);
+    if (st == ORC_OK && shortcut) {
+        add_into(&x1, in);
+        snprintf(nm, sizeof nm, "%s.attn.proj", P);
+        stat_map(m, nm, &x1);
+    }
     fmap f = fm_new(f0->dims[0], in->h, in->w);
     snprintf(nm, sizeof nm, "%s.ffn.0", P);
     if (st == ORC_OK) st = conv_named(m, nm, &f, &x1, 1, 0, 1);
     snprintf(nm, sizeof nm, "%s.ffn.1", P);
     if (st == ORC_OK) st = conv_named(m, nm, out, &f, 1, 0, 0);
-    if (st == ORC_OK && shortcut) add_into(out, &x1);
+    if (st == ORC_OK && shortcut) {
+        add_into(out, &x1);
+        snprintf(nm, sizeof nm, "%s.ffn.1", P);
+        stat_map(m, nm, out);
+    }
     fm_free(&f);
     fm_free(&x1);
     return st;
@@ -643,10 +723,20 @@ static int detect(orc_model* m, const fmap* feats[3], int max_det, float* dets, 
         if (st == ORC_OK) conv(&box, &s2, w2, bb2, 1, 0, 0);
         fmap d0 = fm_new(f->c, f->h, f->w), p0 = fm_new(c3, f->h, f->w), d1 = fm_new(c3, f->h, f->w),
              p1 = fm_new(c3, f->h, f->w), cls = fm_new(nc, f->h, f->w);
+        g_pre_absmax = g_out_absmax = 0.0f;
         if (st == ORC_OK) dwconv(&d0, f, dw0, db0, 1);
+        snprintf(nm, sizeof nm, "model.23.%s.%d.0.0:pre", b3, s);
+        stat_rec(m, nm, g_pre_absmax);
+        snprintf(nm, sizeof nm, "model.23.%s.%d.0.0", b3, s);
+        stat_rec(m, nm, g_out_absmax);
         snprintf(nm, sizeof nm, "model.23.%s.%d.0.1", b3, s);
         if (st == ORC_OK) st = conv_named(m, nm, &p0, &d0, 1, 0, 1);
+        g_pre_absmax = g_out_absmax = 0.0f;
         if (st == ORC_OK) dwconv(&d1, &p0, dw1, db1, 1);
+        snprintf(nm, sizeof nm, "model.23.%s.%d.1.0:pre", b3, s);
+        stat_rec(m, nm, g_pre_absmax);
+        snprintf(nm, sizeof nm, "model.23.%s.%d.1.0", b3, s);
+        stat_rec(m, nm, g_out_absmax);
         snprintf(nm, sizeof nm, "model.23.%s.%d.1.1", b3, s);
         if (st == ORC_OK) st = conv_named(m, nm, &p1, &d1, 1, 0, 1);
         if (st == ORC_OK) conv(&cls, &p1, wf, bf, 1, 0, 0);
@@ -693,6 +783,7 @@ void orc_free(void* h) {
     if (!m) return;
     for (int i = 0; i < m->n; ++i) free(m->t[i].data);
     free(m->t);
+    free(m->st);
     free(m);
 }
 
@@ -756,6 +847,32 @@ void* orc_load(const char* path) {
     return m;
 }
 
+/* Calibration statistics: on != 0 clears the table and starts recording
+ * max |x| per named tensor over the following forwards. */
+void orc_stats_enable(void* h, int on) {
+    orc_model* m = (orc_model*)h;
+    m->stats_on = on;
+    if (on) m->st_n = 0;
+}
+int orc_stats_count(void* h) { return ((orc_model*)h)->st_n; }
+int orc_stats_entry(void* h, int i, char* name, int cap, float* v) {
+    orc_model* m = (orc_model*)h;
+    if (i < 0 || i >= m->st_n) return -1;
+    snprintf(name, (size_t)cap, "%s", m->st[i].name);
+    *v = m->st[i].v;
+    return 0;
+}
+
+/* Pointer to a (folded) tensor's data and its dims, or NULL. */
+const float* orc_tensor_ptr(void* h, const char* name, int* dims4) {
+    orc_tensor* t = find((orc_model*)h, name);
+    if (!t) return NULL;
+    if (dims4)
+        for (int d = 0; d < 4; ++d) dims4[d] = t->dims[d];
+    return t->data;
+}
+int orc_nc(void* h) { return ((orc_model*)h)->nc; }
+
 int orc_anchors(int H, int W) { return (H / 8) * (W / 8) + (H / 16) * (W / 16) + (H / 32) * (W / 32); }
 
 static void emit(orc_stage_cb cb, void* user, const char* name, const fmap* f) {
@@ -772,6 +889,7 @@ int orc_forward(void* h, const float* in, int H, int W, int max_det, float* dets
     x.w = W;
     x.d = (float*)in;
     emit(cb, user, "stage_00_input", &x);
+    stat_map(m, "input", &x);
     fmap b[24];
     memset(b, 0, sizeof b);
     int st = ORC_OK;
