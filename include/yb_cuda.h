@@ -27,9 +27,26 @@ typedef enum {
     /* FP32 semantics: fp32 activations in HBM, convolutions as split-bf16
      * (hi+lo, three tcgen05 products) with fp32 accumulation in TMEM. */
     YB_PRECISION_FP32 = 0,
-    /* Reserved for the int8 path (kind::i8, int32 accumulation). */
+    /* INT8: int8 NHWC activations with per-tensor scales, int8 weights with
+     * per-output-channel scales, convolutions on tcgen05 kind::i8 with int32
+     * accumulation in TMEM and round-half-even requantisation (yb_int8.h
+     * gives the per-layer rules); Detect's last convolutions dequantise to
+     * fp32 for the decode and top-k. */
     YB_PRECISION_INT8 = 1
 } yb_precision;
+
+/* Scale table of an INT8 model: one positive float per named tensor.  A
+ * convolution with weight prefix P writes tensor "P" (after its residual) and,
+ * with SiLU, has the pre-activation scale "P:pre"; further "input" (the
+ * network input), "<psa>.attn.ope" (attention output plus positional term)
+ * for every attention block, and the Detect head's depthwise convolutions
+ * (their own prefixes, with ":pre").  The CPU oracle's calibration produces
+ * such a table from sample images (max |x| / 127 per tensor). */
+typedef struct {
+    const char* const* names;
+    const float* scales;
+    int n;
+} yb_int8_scales;
 
 /* Stage callback: called once per stage tensor (NCHW float32 host data of
  * image 0) with the reference's stage names stage_00_input .. stage_25_detect. */
@@ -39,8 +56,23 @@ typedef void (*yb_stage_cb)(void* user, const char* name, const float* nchw, int
 status_t yb_cuda_init(int device, void** ctx);
 
 /* Packs and uploads the BN-folded weights of `m` (after model_load_weights /
- * fold_all_bn).  qparams is reserved for YB_PRECISION_INT8 and must be NULL. */
+ * fold_all_bn).  YB_PRECISION_FP32: qparams must be NULL.  YB_PRECISION_INT8:
+ * qparams is a const yb_int8_scales* (as for yb_cuda_set_int8). */
 status_t yb_cuda_upload_weights(void* ctx, const model_t* m, yb_precision p, const void* qparams);
+
+/* Switches the context's precision: n > 0 makes every later forward INT8
+ * under this scale table (names[i] -> scales[i]; the weights are quantised
+ * when a plan is first built), n = 0 returns to FP32.  Plans are rebuilt on
+ * the next forward.  A scale the graph needs but the table lacks is reported
+ * then, as ERROR_INVALID_DIMS naming the tensor. */
+status_t yb_cuda_set_int8(void* ctx, const char* const* names, const float* scales, int n);
+
+/* Stage tensor `idx` (0..22: the reference's stage_01_buf0 .. stage_23_buf22)
+ * of image `image` of the last INT8 forward (not a pipelined one): out_nchw
+ * [c][h][w] int8 (nullable) and its per-channel scales [c] (nullable; the
+ * dequantised value is q * scales[channel]).  *c, *h, *w receive the shape. */
+status_t yb_cuda_get_int8_stage(void* ctx, int idx, int image, signed char* out_nchw, float* scales, int* c, int* h,
+                                int* w);
 
 /* Convenience for hosts without a model_t: reads a converter-layout .bin,
  * folds BatchNorm like model_load_weights and uploads. */

@@ -30,6 +30,7 @@
 #include "runtime.h"
 #include "sm100.cuh"
 #include "status.h"
+#include "int8.h"
 #include "yb_int8.h"
 
 namespace yb {
@@ -44,18 +45,9 @@ constexpr int kSmemLimit = 232448;
 constexpr int kMaxAcc = 4;
 constexpr int kMaxCo = 1024;
 
-struct I8Args {
-  int B = 0, H = 0, W = 0, Ci = 0, Co = 0, kh = 1, kw = 1, stride = 1, pad = 0, Ho = 0, Wo = 0;
-  int K = 0, num_kc = 0, n_tile = 0, n_tiles = 0, m_tiles = 0, a_cpp = 0;
-  const uint8_t* wpack = nullptr;
-  const int32_t* bias = nullptr;
-  const int32_t* mult = nullptr;
-  const int32_t* shift = nullptr;
-  const int8_t* lut = nullptr;
-  int8_t* out = nullptr;
-  int* err = nullptr;
-  alignas(64) CUtensorMap tm;
-};
+}  // namespace
+
+namespace {
 
 // Instruction descriptor, kind::i8: signed 8-bit A and B, int32 D, K-major.
 __host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
@@ -262,9 +254,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       const int m = mt * kBM + q * 32 + lane;
       const bool valid = m < M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_stride;
-      const long long po = static_cast<long long>(valid ? m : 0) * a.Co + n0;
-      // Units of 32 channels: two TMEM loads, requantise, then lanes 2k and
-      // 2k+1 write the two 16-byte halves of one pixel's 32-byte run.
+      const long long pm = valid ? m : 0;
+      const long long po = pm * a.out_cstride + a.out_coff + n0;
+      // Units of 32 channels: two TMEM loads, requantise (or dequantise),
+      // then lanes 2k and 2k+1 write the two 16-byte halves of one pixel's
+      // 32-byte run.
       for (int c = 0; c < nvalid; c += 32) {
         const bool two = c + 16 < nvalid;
         uint32_t r[32];
@@ -273,20 +267,46 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
         tc_ld_32x32b_x16(tbase + c, r0);
         if (two) tc_ld_32x32b_x16(tbase + c + 16, r1);
         tc_wait_ld();
+        if (a.out_f32) {
+          if (valid) {
+            const long long fb = pm / HoWo;
+            float* of = a.out_f32 + fb * a.f32_bstride + (pm - fb * HoWo) * a.f32_cstride + n0 + c;
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              if (n0 + c + e >= a.f32_co) break;
+              float4 v;
+              v.x = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e])) + sbias[n0 + c + e]) *
+                    a.deq[n0 + c + e];
+              v.y = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e + 1])) +
+                                       sbias[n0 + c + e + 1]) *
+                    a.deq[n0 + c + e + 1];
+              v.z = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e + 2])) +
+                                       sbias[n0 + c + e + 2]) *
+                    a.deq[n0 + c + e + 2];
+              v.w = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e + 3])) +
+                                       sbias[n0 + c + e + 3]) *
+                    a.deq[n0 + c + e + 3];
+              *reinterpret_cast<float4*>(of + e) = v;
+            }
+          }
+          continue;
+        }
+        int8_t rv[32];
+        if (a.res) {
+          const int8_t* rp = a.res + pm * a.res_cstride + a.res_coff + n0 + c;
+          *reinterpret_cast<uint4*>(&rv[0]) = *reinterpret_cast<const uint4*>(rp);
+          if (two) *reinterpret_cast<uint4*>(&rv[16]) = *reinterpret_cast<const uint4*>(rp + 16);
+        }
         uint32_t packed[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           if (e >= 16 && !two) break;
           const int ch = n0 + c + e;
           const long long v = static_cast<long long>(static_cast<int32_t>(r[e])) + sbias[ch];
-          const long long y = rshift_rne(v * smult[ch], sshift[ch]);
-          int o;
-          if (a.lut) {
-            const int idx = static_cast<int>(y < -128 ? -128 : y > 127 ? 127 : y);
-            o = slut[idx + 128];
-          } else {
-            o = static_cast<int>(y < -127 ? -127 : y > 127 ? 127 : y);
-          }
+          long long y = rshift_rne(v * smult[ch], sshift[ch]);
+          if (a.lut) y = slut[(y < -128 ? -128 : y > 127 ? 127 : y) + 128];
+          if (a.res) y += rshift_rne(static_cast<long long>(rv[e]) * a.res_mult, a.res_shift);
+          const int o = static_cast<int>(y < -127 ? -127 : y > 127 ? 127 : y);
           packed[e >> 2] |= (static_cast<uint32_t>(o) & 0xFFu) << (8 * (e & 3));
         }
         const int h = lane & 1;
@@ -339,6 +359,109 @@ inline uint32_t sw128_off(uint32_t row, uint32_t chunk16) {
   return (row >> 3) * 1024u + (row & 7u) * 128u + ((chunk16 ^ (row & 7u)) << 4);
 }
 
+int stages_for_i8(int n_tile, int n_tiles) {
+  const int stage = static_cast<int>(kATile) + n_tile * 128;
+  const int extra = 1024 + 512 + 3 * 4 * n_tile * n_tiles + 256;
+  const int st = (kSmemLimit - extra) / stage;
+  return st > 8 ? 8 : st;
+}
+
+
+}  // namespace
+
+void i8_tiling(int co, int ci, int kh, int kw, I8Tiling* t) {
+  const int taps = kh * kw;
+  if (taps == 1) {
+    t->ci_pad = (ci + 31) / 32 * 32;
+    t->a_cpp = 128;
+  } else {
+    t->ci_pad = ci <= 32 ? 32 : ci <= 64 ? 64 : (ci + 127) / 128 * 128;
+    t->a_cpp = t->ci_pad <= 64 ? t->ci_pad : 128;
+  }
+  t->K = taps * t->ci_pad;
+  t->num_kc = (t->K + kKB - 1) / kKB;
+  const int tiles = (co + 255) / 256;
+  const int per = (co + tiles - 1) / tiles;
+  t->n_tile = (per + 15) / 16 * 16;
+  t->n_tiles = tiles;
+}
+
+std::vector<uint8_t> i8_pack_weights(const int8_t* wq, int co, int ci, int kh, int kw, const I8Tiling& t) {
+  const size_t chunk = static_cast<size_t>(t.n_tile) * 128;
+  std::vector<uint8_t> pk(static_cast<size_t>(t.n_tiles) * t.num_kc * chunk, 0);
+  for (int nt = 0; nt < t.n_tiles; ++nt)
+    for (int kc = 0; kc < t.num_kc; ++kc) {
+      uint8_t* dst = pk.data() + (static_cast<size_t>(nt) * t.num_kc + kc) * chunk;
+      for (int rrow = 0; rrow < t.n_tile; ++rrow) {
+        const int n = nt * t.n_tile + rrow;
+        if (n >= co) continue;
+        for (int kk = 0; kk < kKB; ++kk) {
+          const int k = kc * kKB + kk;
+          if (k >= t.K) break;
+          const int tap = k / t.ci_pad;
+          const int cc = k - tap * t.ci_pad;
+          if (cc >= ci) continue;
+          const int ky = tap / kw, kx = tap - (tap / kw) * kw;
+          const int8_t v = wq[((static_cast<size_t>(n) * ci + cc) * kh + ky) * kw + kx];
+          dst[sw128_off(static_cast<uint32_t>(rrow), static_cast<uint32_t>(kk >> 4)) + (kk & 15)] =
+              static_cast<uint8_t>(v);
+        }
+      }
+    }
+  return pk;
+}
+
+int i8_bias_slots(const I8Tiling& t) { return t.n_tile * t.n_tiles; }
+
+cudaError_t i8_init_kernel() {
+  return cudaFuncSetAttribute(conv_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+}
+
+cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long long x_bstride, cudaStream_t s,
+                           int sms, std::string* why) {
+  if (a.Co < 16 || a.Co % 16 || a.n_tile < 16 || a.n_tile % 16 || a.n_tiles < 1 || a.n_tile * a.n_tiles < a.Co ||
+      (a.out && (a.out_cstride % 16 || a.out_coff % 16)) || (a.res && (a.res_cstride % 16 || a.res_coff % 16)) ||
+      (!a.out && !a.out_f32) || (a.out_f32 && (a.f32_cstride % 4 || a.f32_bstride % 4 || a.f32_co % 4 || !a.deq)) ||
+      a.res_shift < 1 ||
+      a.res_shift > 62 || x_cstride % 16 || x_bstride % 16 || reinterpret_cast<uintptr_t>(x) % 16) {
+    if (why) *why = "int8 conv: unsupported view alignment or tile";
+    return cudaErrorInvalidValue;
+  }
+  const auto enc = i8_im2col_encoder();
+  if (!enc) {
+    if (why) *why = "cuTensorMapEncodeIm2col unavailable";
+    return cudaErrorNotSupported;
+  }
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Ci), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
+                        static_cast<cuuint64_t>(a.B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(x_cstride), static_cast<cuuint64_t>(x_cstride) * a.W,
+                           static_cast<cuuint64_t>(x_bstride)};
+  int lower[2] = {-a.pad, -a.pad};
+  int upper[2] = {a.pad - (a.kw - 1), a.pad - (a.kh - 1)};
+  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(a.stride), static_cast<cuuint32_t>(a.stride), 1};
+  const CUtensorMapSwizzle sw = a.a_cpp == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                                : a.a_cpp == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUresult cr = enc(&a.tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(x), dims, strides, lower,
+                          upper, static_cast<cuuint32_t>(a.a_cpp), static_cast<cuuint32_t>(kBM), estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) {
+    if (why) *why = "int8 conv: tensor map encoding failed (code " + std::to_string(static_cast<int>(cr)) + ")";
+    return cudaErrorInvalidValue;
+  }
+  const int stages = stages_for_i8(a.n_tile, a.n_tiles);
+  if (stages < 2) return cudaErrorInvalidValue;
+  const int smem = 1024 + 512 + 3 * 4 * a.n_tile * a.n_tiles + 256 +
+                   stages * (static_cast<int>(kATile) + a.n_tile * 128);
+  const int total = a.m_tiles * a.n_tiles;
+  if (total <= 0) return cudaSuccess;
+  const int grid = total < sms ? total : sms;
+  conv_i8_kernel<<<grid, kThreads, smem, s>>>(a, stages);
+  return cudaGetLastError();
+}
+
+namespace {
 struct Int8Conv {
   int device = 0;
   int co = 0, ci = 0, ci_pad = 0, kh = 1, kw = 1, stride = 1, pad = 0;
@@ -351,13 +474,6 @@ struct Int8Conv {
   int* err = nullptr;
   int sms = 148;
 };
-
-int stages_for_i8(int n_tile, int n_tiles) {
-  const int stage = static_cast<int>(kATile) + n_tile * 128;
-  const int extra = 1024 + 512 + 3 * 4 * n_tile * n_tiles + 256;
-  const int st = (kSmemLimit - extra) / stage;
-  return st > 8 ? 8 : st;
-}
 
 status_t free_conv(Int8Conv* c) {
   if (!c) return SUCCESS;
@@ -449,45 +565,17 @@ extern "C" status_t yb_int8_conv_create(int device, const int8_t* wq, const int3
   c->kw = kw;
   c->stride = stride;
   c->pad = pad;
-  const int taps = kh * kw;
-  if (taps == 1) {
-    c->ci_pad = (ci + 31) / 32 * 32;
-    c->a_cpp = 128;
-  } else {
-    c->ci_pad = ci <= 32 ? 32 : ci <= 64 ? 64 : (ci + 127) / 128 * 128;
-    c->a_cpp = c->ci_pad <= 64 ? c->ci_pad : 128;
-  }
-  c->K = taps * c->ci_pad;
-  c->num_kc = (c->K + kKB - 1) / kKB;
-  const int tiles = (co + 255) / 256;
-  const int per = (co + tiles - 1) / tiles;
-  c->n_tile = (per + 15) / 16 * 16;
-  c->n_tiles = tiles;
+  I8Tiling t;
+  i8_tiling(co, ci, kh, kw, &t);
+  c->ci_pad = t.ci_pad;
+  c->a_cpp = t.a_cpp;
+  c->K = t.K;
+  c->num_kc = t.num_kc;
+  c->n_tile = t.n_tile;
+  c->n_tiles = t.n_tiles;
   cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
-  // Packed weights: per N tile and K chunk, n_tile rows of 128 bytes, 128B
-  // swizzled, K = (ky, kx, ci) with ci < ci_pad.
-  const size_t chunk = static_cast<size_t>(c->n_tile) * 128;
-  std::vector<uint8_t> pk(static_cast<size_t>(c->n_tiles) * c->num_kc * chunk, 0);
-  for (int nt = 0; nt < c->n_tiles; ++nt)
-    for (int kc = 0; kc < c->num_kc; ++kc) {
-      uint8_t* dst = pk.data() + (static_cast<size_t>(nt) * c->num_kc + kc) * chunk;
-      for (int rrow = 0; rrow < c->n_tile; ++rrow) {
-        const int n = nt * c->n_tile + rrow;
-        if (n >= co) continue;
-        for (int kk = 0; kk < kKB; ++kk) {
-          const int k = kc * kKB + kk;
-          if (k >= c->K) break;
-          const int tap = k / c->ci_pad;
-          const int cc = k - tap * c->ci_pad;
-          if (cc >= ci) continue;
-          const int ky = tap / kw, kx = tap - (tap / kw) * kw;
-          const int8_t v = wq[((static_cast<size_t>(n) * ci + cc) * kh + ky) * kw + kx];
-          dst[sw128_off(static_cast<uint32_t>(rrow), static_cast<uint32_t>(kk >> 4)) + (kk & 15)] =
-              static_cast<uint8_t>(v);
-        }
-      }
-    }
-  const size_t nq = static_cast<size_t>(c->n_tile) * c->n_tiles;
+  const std::vector<uint8_t> pk = i8_pack_weights(wq, co, ci, kh, kw, t);
+  const size_t nq = static_cast<size_t>(i8_bias_slots(t));
   std::vector<int32_t> hb(nq, 0), hm(nq, 0), hs(nq, 1);
   for (int i = 0; i < co; ++i) {
     hb[i] = bq[i];
@@ -504,8 +592,7 @@ extern "C" status_t yb_int8_conv_create(int device, const int8_t* wq, const int3
     if (e == cudaSuccess) e = cudaMemcpy(c->shift, hs.data(), nq * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && lut) e = cudaMemcpy(c->lut, lut, 256, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof(int));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(conv_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    if (e == cudaSuccess) e = i8_init_kernel();
   }
   if (e != cudaSuccess) {
     const status_t st = cuda_status(e, "int8 conv upload");
@@ -561,36 +648,16 @@ extern "C" status_t yb_int8_conv_run(void* conv, const int8_t* d_x, int B, int H
   a.shift = c->shift;
   a.lut = c->lut;
   a.out = d_y;
+  a.out_cstride = c->co;
   a.err = c->err;
-  const auto enc = i8_im2col_encoder();
-  if (!enc) {
-    set_error("int8 conv: cuTensorMapEncodeIm2col unavailable");
-    return ERROR_DEVICE;
-  }
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(c->ci_pad), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
-                        static_cast<cuuint64_t>(B)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(c->ci_pad), static_cast<cuuint64_t>(c->ci_pad) * W,
-                           static_cast<cuuint64_t>(c->ci_pad) * W * H};
-  int lower[2] = {-c->pad, -c->pad};
-  int upper[2] = {c->pad - (c->kw - 1), c->pad - (c->kh - 1)};
-  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(c->stride), static_cast<cuuint32_t>(c->stride), 1};
-  const CUtensorMapSwizzle sw = c->a_cpp == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
-                                : c->a_cpp == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                                                 : CU_TENSOR_MAP_SWIZZLE_128B;
-  const CUresult cr = enc(&a.tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(d_x), dims, strides, lower,
-                          upper, static_cast<cuuint32_t>(c->a_cpp), static_cast<cuuint32_t>(kBM), estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) {
-    set_error("int8 conv: tensor map encoding failed (code " + std::to_string(static_cast<int>(cr)) + ")");
+  std::string why;
+  e = launch_conv_i8(a, d_x, c->ci_pad, static_cast<long long>(c->ci_pad) * H * W, static_cast<cudaStream_t>(stream),
+                     c->sms, &why);
+  if (e == cudaErrorInvalidValue || e == cudaErrorNotSupported) {
+    set_error(why.empty() ? "int8 conv launch rejected" : why);
     return ERROR_INVALID_DIMS;
   }
-  const int stages = stages_for_i8(c->n_tile, c->n_tiles);
-  const int smem = 1024 + 512 + 3 * 4 * c->n_tile * c->n_tiles + 256 + stages * (static_cast<int>(kATile) + c->n_tile * 128);
-  const int total = a.m_tiles * a.n_tiles;
-  const int grid = total < c->sms ? total : c->sms;
-  conv_i8_kernel<<<grid, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(a, stages);
-  return cuda_status(cudaGetLastError(), "int8 conv launch");
+  return cuda_status(e, "int8 conv launch");
 }
 
 extern "C" status_t yb_int8_conv_check(void* conv) {

@@ -823,9 +823,24 @@ cudaError_t Engine::profile_ops(Plan* p, int reps, std::vector<double>* ms) {
   return e;
 }
 
+void Engine::set_int8_scales(std::map<std::string, float> s) {
+  cudaSetDevice(device_);
+  cudaStreamSynchronize(stream_);
+  for (auto it = plans_.begin(); it != plans_.end();) {
+    if ((*it)->int8) {
+      release_plan(it->get());
+      it = plans_.erase(it);
+    } else {
+      ++it;
+    }
+  }
+  i8_scales_ = std::move(s);
+}
+
 cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::string* why, int slot) {
   for (auto& p : plans_) {
-    if (p->B == B && p->H == H && p->W == W && p->max_det == max_det && p->slot == slot) {
+    if (p->B == B && p->H == H && p->W == W && p->max_det == max_det && p->slot == slot &&
+        p->int8 == int8_mode()) {
       *out = p.get();
       return cudaSuccess;
     }
@@ -845,7 +860,8 @@ cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::
   p->W = W;
   p->max_det = max_det;
   p->slot = slot;
-  cudaError_t e = build(p.get(), why);
+  p->int8 = int8_mode();
+  cudaError_t e = p->int8 ? build_i8(p.get(), why) : build(p.get(), why);
   if (e != cudaSuccess) {
     release_plan(p.get());
     return e;

@@ -88,6 +88,15 @@ struct Plan {
   Buf stage[23];  // model->buffers[0..22] equivalents (concat/upsample ones unset)
   cudaGraphExec_t graph = nullptr;
   size_t arena_bytes = 0;
+  // INT8 plans: stage tensors 01-23 as NHWC int8 with per-channel scales.
+  bool int8 = false;
+  struct I8Stage {
+    int8_t* p = nullptr;
+    long long cstride = 0, bstride = 0;
+    int C = 0, H = 0, W = 0;
+    std::vector<float> cs;
+  };
+  std::vector<I8Stage> i8stage;
 };
 
 class Engine {
@@ -117,6 +126,12 @@ class Engine {
   // Reads and clears the kernel error word; returns its value.
   int take_kernel_error();
 
+  // INT8 mode: a non-empty scale table (tensor name -> per-tensor scale)
+  // makes get_plan build INT8 plans; an empty one returns to FP32.  INT8
+  // plans built under the previous table are released.
+  void set_int8_scales(std::map<std::string, float> s);
+  bool int8_mode() const { return !i8_scales_.empty(); }
+
   int device() const { return device_; }
   cudaStream_t stream() const { return stream_; }
   int num_classes() const { return nc_; }
@@ -128,6 +143,7 @@ class Engine {
   cudaError_t dw_w(const std::string& prefix, DevDw** out, std::string* why);
   cudaError_t dev_alloc(size_t bytes, void** p);
   cudaError_t build(Plan* p, std::string* why);
+  cudaError_t build_i8(Plan* p, std::string* why);
   void release_plan(Plan* p);
 
   int device_ = 0;
@@ -141,6 +157,7 @@ class Engine {
   DevStem stem_;
   std::vector<void*> weight_allocs_;
   std::vector<std::unique_ptr<Plan>> plans_;
+  std::map<std::string, float> i8_scales_;
 };
 
 // Reads the converter's .bin layout (int32 nc, int32 count, records) and folds

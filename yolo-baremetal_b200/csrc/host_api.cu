@@ -19,6 +19,7 @@
 #include "detect.h"
 #include "detection.h"
 #include "engine.h"
+#include "i8k.h"
 #include "model.h"
 #include "runtime.h"
 #include "tensor.h"
@@ -193,6 +194,66 @@ status_t dump_stages(Ctx* c, Plan* p, const float* in_nchw, yb_stage_cb cb, void
   return SUCCESS;
 }
 
+// Stage tensor k of image `image` of an INT8 plan as NCHW int8 on the host.
+status_t fetch_i8_stage(Ctx* c, Plan* p, int k, int image, int8_t* out) {
+  const Plan::I8Stage& S = p->i8stage[k];
+  cudaStream_t s = c->eng->stream();
+  DevMem t;
+  const size_t n = static_cast<size_t>(S.C) * S.H * S.W;
+  cudaError_t e = t.alloc(n);
+  I8View v;
+  v.p = S.p + static_cast<long long>(image) * S.bstride;
+  v.cstride = S.cstride;
+  v.bstride = S.bstride;
+  if (e == cudaSuccess) e = launch_nhwc_to_nchw_i8(v, S.C, S.H, S.W, static_cast<int8_t*>(t.p), s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, t.p, n, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  return cuda_status(e, "int8 stage fetch");
+}
+
+// Stage tensors of image 0 of an INT8 forward, dequantised (q * scale of its
+// channel), under the reference's stage names.
+status_t dump_stages_i8(Ctx* c, Plan* p, const float* in_nchw, yb_stage_cb cb, void* user) {
+  cb(user, "stage_00_input", in_nchw, 1, 3, p->H, p->W);
+  std::vector<int8_t> q;
+  std::vector<float> f;
+  char name[32];
+  for (int k = 0; k < 23; ++k) {
+    const Plan::I8Stage& S = p->i8stage[k];
+    const size_t hw = static_cast<size_t>(S.H) * S.W;
+    q.resize(hw * S.C);
+    f.resize(hw * S.C);
+    const status_t st = fetch_i8_stage(c, p, k, 0, q.data());
+    if (st != SUCCESS) return st;
+    for (int ch = 0; ch < S.C; ++ch)
+      for (size_t i = 0; i < hw; ++i) f[ch * hw + i] = static_cast<float>(q[ch * hw + i]) * S.cs[ch];
+    snprintf(name, sizeof name, "stage_%02d_buf%d", k + 1, k);
+    cb(user, name, f.data(), 1, S.C, S.H, S.W);
+  }
+  std::vector<float> dets(static_cast<size_t>(p->max_det) * 6);
+  cudaError_t e = cudaMemcpy(dets.data(), p->d_out, dets.size() * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "stage dump detections");
+  cb(user, "stage_24_buf23", dets.data(), 1, p->max_det, 6, 1);
+  cb(user, "stage_25_detect", dets.data(), 1, p->max_det, 6, 1);
+  return SUCCESS;
+}
+
+status_t set_int8(Ctx* c, const char* const* names, const float* scales, int n) {
+  if (n < 0 || (n > 0 && (!names || !scales))) return n < 0 ? ERROR_INVALID_DIMS : ERROR_NULL_POINTER;
+  std::map<std::string, float> t;
+  for (int i = 0; i < n; ++i) {
+    if (!names[i]) return ERROR_NULL_POINTER;
+    if (!(scales[i] > 0.0f) || !std::isfinite(scales[i])) {
+      set_error(std::string("int8 scale not positive and finite: ") + names[i]);
+      return ERROR_INVALID_DIMS;
+    }
+    t[names[i]] = scales[i];
+  }
+  c->eng->set_int8_scales(std::move(t));
+  c->last = nullptr;
+  return SUCCESS;
+}
+
 void weights_from_model(const model_t* m, WeightMap* out) {
   for (int i = 0; i < m->num_weights; ++i) {
     const tensor_t& t = m->weights[i].tensor;
@@ -282,10 +343,11 @@ extern "C" status_t yb_cuda_destroy(void* ctx) {
 extern "C" status_t yb_cuda_upload_weights(void* ctx, const model_t* m, yb_precision p, const void* qparams) {
   Ctx* c = as_ctx(ctx);
   if (!c || !m) return ERROR_NULL_POINTER;
-  if (p != YB_PRECISION_FP32 || qparams) {
-    set_error("only YB_PRECISION_FP32 is implemented");
-    return ERROR_NOT_IMPLEMENTED;
+  if ((p != YB_PRECISION_FP32 && p != YB_PRECISION_INT8) || (p == YB_PRECISION_FP32 && qparams)) {
+    set_error("precision must be YB_PRECISION_FP32 (qparams NULL) or YB_PRECISION_INT8");
+    return ERROR_INVALID_DIMS;
   }
+  if (p == YB_PRECISION_INT8 && !qparams) return ERROR_NULL_POINTER;
   status_t st = ctx_ready(c);
   if (st != SUCCESS) return st;
   WeightMap w;
@@ -297,7 +359,44 @@ extern "C" status_t yb_cuda_upload_weights(void* ctx, const model_t* m, yb_preci
     return ERROR_FILE_NOT_FOUND;
   }
   c->last = nullptr;
-  return cuda_status(e, "upload weights");
+  st = cuda_status(e, "upload weights");
+  if (st != SUCCESS) return st;
+  if (p == YB_PRECISION_INT8) {
+    const auto* q = static_cast<const yb_int8_scales*>(qparams);
+    return set_int8(c, q->names, q->scales, q->n);
+  }
+  return set_int8(c, nullptr, nullptr, 0);
+}
+
+extern "C" status_t yb_cuda_set_int8(void* ctx, const char* const* names, const float* scales, int n) {
+  Ctx* c = as_ctx(ctx);
+  if (!c) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  return set_int8(c, names, scales, n);
+}
+
+extern "C" status_t yb_cuda_get_int8_stage(void* ctx, int idx, int image, signed char* out_nchw, float* scales,
+                                           int* c_out, int* h_out, int* w_out) {
+  Ctx* c = as_ctx(ctx);
+  if (!c) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  Plan* p = c->last;
+  if (!p || !p->int8) {
+    set_error("no int8 stage tensors kept: the last forward was not a non-pipelined INT8 forward");
+    return ERROR_INVALID_DIMS;
+  }
+  if (idx < 0 || idx >= static_cast<int>(p->i8stage.size()) || image < 0 || image >= p->B) return ERROR_INVALID_DIMS;
+  const Plan::I8Stage& S = p->i8stage[idx];
+  if (c_out) *c_out = S.C;
+  if (h_out) *h_out = S.H;
+  if (w_out) *w_out = S.W;
+  if (scales) std::copy(S.cs.begin(), S.cs.end(), scales);
+  if (!out_nchw) return SUCCESS;
+  cudaError_t e = cudaStreamSynchronize(c->eng->stream());
+  if (e != cudaSuccess) return cuda_status(e, "int8 stage");
+  return fetch_i8_stage(c, p, idx, image, reinterpret_cast<int8_t*>(out_nchw));
 }
 
 extern "C" status_t yb_cuda_load_bin(void* ctx, const char* path) {
@@ -397,7 +496,7 @@ extern "C" status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int 
       step_ms[i] = ms;
     }
   }
-  if (dump) return dump_stages(c, p, in_nchw, dump, user);
+  if (dump) return p->int8 ? dump_stages_i8(c, p, in_nchw, dump, user) : dump_stages(c, p, in_nchw, dump, user);
   return SUCCESS;
 }
 

@@ -1,0 +1,60 @@
+// INT8 convolution internals shared by the layer API (conv_i8.cu) and the
+// INT8 engine (engine_i8.cu).
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace yb {
+
+// One launch of the kind::i8 convolution.  Input: NHWC int8 view given to
+// launch_conv_i8 (channel stride, image stride; Ci channels read, the rest of
+// each a_cpp-channel box zero).  Output element (pixel m, channel n) lives at
+// out[m * out_cstride + out_coff + n]; the residual (res != null) is read the
+// same way and added after requantisation as rshift_rne(r * res_mult,
+// res_shift).  With out_f32 set the accumulator is dequantised instead:
+// out_f32[b * f32_bstride + p * f32_cstride + n] = float(acc) * deq[n] for
+// n < f32_co (pixel p of image b).
+struct I8Args {
+  int B = 0, H = 0, W = 0, Ci = 0, Co = 0, kh = 1, kw = 1, stride = 1, pad = 0, Ho = 0, Wo = 0;
+  int K = 0, num_kc = 0, n_tile = 0, n_tiles = 0, m_tiles = 0, a_cpp = 0;
+  const uint8_t* wpack = nullptr;
+  const int32_t* bias = nullptr;
+  const int32_t* mult = nullptr;
+  const int32_t* shift = nullptr;
+  const int8_t* lut = nullptr;
+  int8_t* out = nullptr;
+  long long out_cstride = 0, out_coff = 0;
+  const int8_t* res = nullptr;
+  long long res_cstride = 0, res_coff = 0;
+  int res_mult = 0, res_shift = 1;
+  float* out_f32 = nullptr;
+  long long f32_cstride = 0, f32_bstride = 0;  // element (b, p, n) at b*f32_bstride + p*f32_cstride + n
+  int f32_co = 0;                              // channels stored (the rest of the tile is padding)
+  const float* deq = nullptr;
+  int* err = nullptr;
+  alignas(64) CUtensorMap tm;
+};
+
+// K layout of a convolution: input channels padded to ci_pad (a multiple of
+// 32; for 3x3 kernels 32, 64 or a multiple of 128), K = kh*kw*ci_pad ordered
+// (ky, kx, ci) in 128-wide chunks; a_cpp channels per TMA copy.
+struct I8Tiling {
+  int ci_pad = 0, a_cpp = 0, K = 0, num_kc = 0, n_tile = 0, n_tiles = 0;
+};
+void i8_tiling(int co, int ci, int kh, int kw, I8Tiling* t);
+// wq [co][ci][kh][kw] -> per N tile and K chunk, n_tile 128-byte rows,
+// 128B-swizzled (what the kernel's bulk copies load).
+std::vector<uint8_t> i8_pack_weights(const int8_t* wq, int co, int ci, int kh, int kw, const I8Tiling& t);
+// Entries of the per-channel bias / multiplier / shift arrays: n_tile * n_tiles.
+int i8_bias_slots(const I8Tiling& t);
+cudaError_t i8_init_kernel();
+// Encodes the im2col map of the input view and launches.  a.Ci = channels
+// read (<= the view's channels); m_tiles = ceil(B*Ho*Wo / 128).
+cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long long x_bstride, cudaStream_t s,
+                           int sms, std::string* why);
+
+}  // namespace yb

@@ -37,6 +37,7 @@ EXPORTS = {
     "detection.h": ["decode_detections"],
     "utils.h": ["timer_start", "timer_stop", "timer_elapsed_ms", "load_named_tensor", "save_named_tensor", "fold_bn"],
     "yb_cuda.h": ["yb_cuda_init", "yb_cuda_upload_weights", "yb_cuda_load_bin", "yb_cuda_forward",
+                  "yb_cuda_set_int8", "yb_cuda_get_int8_stage",
                   "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_detect_topk_noalloc",
                   "yb_cuda_forward_sharded",
                   "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error"],
@@ -105,6 +106,9 @@ def lib() -> C.CDLL:
         L.yb_cuda_profile_ops.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                           C.c_int, C.POINTER(C.c_int)]
         L.yb_cuda_destroy.argtypes = [C.c_void_p]
+        L.yb_cuda_set_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.yb_cuda_get_int8_stage.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                             C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.yb_int8_quantize_conv.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
                                             C.c_float, C.c_float, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                             C.c_void_p, C.c_void_p]
@@ -189,6 +193,25 @@ class Model:
         if stages:
             out["stages"] = store
         return out
+
+    def set_int8(self, scales=None) -> None:
+        """INT8 mode under a scale table {tensor name: scale}; None or {} returns to FP32."""
+        scales = dict(scales or {})
+        n = len(scales)
+        names = (C.c_char_p * max(n, 1))(*[k.encode() for k in scales])
+        vals = np.ascontiguousarray(list(scales.values()) or [0.0], dtype=np.float32)
+        check(lib().yb_cuda_set_int8(self.ctx, names, vals.ctypes.data, n), "yb_cuda_set_int8")
+
+    def int8_stage(self, idx: int, image: int = 0):
+        """(int8 [C,H,W], per-channel scales [C]) of stage tensor idx (0..22) of the last INT8 forward."""
+        c, h, w = C.c_int(), C.c_int(), C.c_int()
+        check(lib().yb_cuda_get_int8_stage(self.ctx, idx, image, None, None, C.byref(c), C.byref(h), C.byref(w)),
+              "yb_cuda_get_int8_stage")
+        q = np.zeros((c.value, h.value, w.value), dtype=np.int8)
+        cs = np.zeros(c.value, dtype=np.float32)
+        check(lib().yb_cuda_get_int8_stage(self.ctx, idx, image, q.ctypes.data, cs.ctypes.data, None, None, None),
+              "yb_cuda_get_int8_stage")
+        return q, cs
 
     def head(self, batch: int):
         """(logits [B,N,nc], boxes [B,N,4]) of the last forward."""
