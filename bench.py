@@ -385,6 +385,10 @@ def run_ours(args):
                 "forward_breakdown_ms": {k: round(v["ms"], 4) for k, v in per_kind.items()},
                 "forward_share": {k: round(v["share"], 4) for k, v in per_kind.items()},
                 "clocks": clocks}
+    if not args.no_int8:
+        i8 = int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_over_ranks)
+        if rank == 0:
+            line["int8"] = i8
     model.close()
     if rank == 0 and not args.no_int8_sweep:
         line["int8_conv_sweep"] = int8_conv_sweep(peaks()[0])
@@ -397,6 +401,113 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
+
+
+INT8_KINDS = ["conv_i8", "quantize_input", "dw3x3_i8", "maxpool_concat_i8", "attention_i8", "decode", "topk"]
+INT8_CALIB_IMAGES = 32  # seeded U[0,1) calibration images (the benchmark's INT8 recipe)
+
+
+def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_over_ranks):
+    """INT8 YOLO26n on the same images: device calibration (FP32 forwards
+    with statistics over 32 seeded U[0,1) images), then the batch of this
+    rank timed device-resident (CUDA events) and end to end through
+    yb_cuda_forward (pinned host buffers, wall clock), and batch-1 latency.
+    Every rank runs the same steps; times are the max over ranks."""
+    import torch
+
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    L = yb.lib()
+    B, H = args.batch, args.hw
+    calib = yw.make_batch(range(10000, 10000 + INT8_CALIB_IMAGES), H, H)
+    t0 = time.perf_counter()
+    scales = model.calibrate_int8(calib, apply=True)
+    calib_s = time.perf_counter() - t0
+    del calib
+    d_in, d_out = model.plan_io(B, H, H)
+    torch.cuda.synchronize()
+    yb.check(L.yb_cuda_forward(model.ctx, host_in.data_ptr(), B, H, H, host_out.data_ptr(), 300, None, None, None),
+             "yb_cuda_forward")
+    torch.cuda.synchronize()
+    # Fill the device-resident plan's input once (outside the timed region).
+    dev_imgs = host_in.to("cuda")
+    model.forward_device(dev_imgs.data_ptr(), d_out, B, H, H, 300, stream.cuda_stream)
+    torch.cuda.synchronize()
+    del dev_imgs
+    for _ in range(args.warmup):
+        model.forward_device(d_in, d_out, B, H, H, 300, stream.cuda_stream)
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        model.forward_device(d_in, d_out, B, H, H, 300, stream.cuda_stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    # End to end (pipelined 16-image sub-batches, pinned host buffers).
+    for _ in range(max(1, args.warmup // 2)):
+        yb.check(L.yb_cuda_forward(model.ctx, host_in.data_ptr(), B, H, H, host_out.data_ptr(), 300, None, None,
+                                   None), "yb_cuda_forward")
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        yb.check(L.yb_cuda_forward(model.ctx, host_in.data_ptr(), B, H, H, host_out.data_ptr(), 300, None, None,
+                                   None), "yb_cuda_forward")
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    # Batch 1 (the single-image INT8 configuration): device-resident latency.
+    d1_in, d1_out = model.plan_io(1, H, H)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        model.forward_device(d1_in, d1_out, 1, H, H, 300, stream.cuda_stream)
+    ev0.record(stream)
+    reps1 = max(args.steps, 20)
+    for _ in range(reps1):
+        model.forward_device(d1_in, d1_out, 1, H, H, 300, stream.cuda_stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    b1_ms = max_over_ranks(ev0.elapsed_time(ev1)) / reps1
+    n_ops = C.c_int()
+    yb.check(L.yb_cuda_profile_ops(model.ctx, B, H, H, 300, 0, None, 0, C.byref(n_ops)), "yb_cuda_profile_ops")
+    out = None
+    if rank == 0:
+        stats = (OpStat * n_ops.value)()
+        yb.check(L.yb_cuda_profile_ops(model.ctx, B, H, H, 300, 3, stats, n_ops.value, C.byref(n_ops)),
+                 "yb_cuda_profile_ops")
+        conv = [s for s in stats if s.kind == 0]
+        conv_ms = sum(s.ms for s in conv)
+        conv_ops = sum(s.flops for s in conv)
+        all_ms = sum(s.ms for s in stats)
+        per_kind = {}
+        for s in stats:
+            d = per_kind.setdefault(INT8_KINDS[s.kind], {"launches": 0, "ms": 0.0})
+            d["launches"] += 1
+            d["ms"] += s.ms
+        tops = conv_ops / (conv_ms * 1e-3) / 1e12
+        out = {"metric": "images/sec YOLO26n 640x640 INT8", "value": world * B * args.steps / (dev_ms * 1e-3),
+               "unit": UNIT, "ms_per_step": dev_ms / args.steps, "dtype": "int8 (int32 accumulation)",
+               "config": {"workload": f"YOLO26n INT8 forward + top-300 decode, {H}x{H}, {B} images per GPU, "
+                                      "image-parallel", "images_per_gpu": B, "global_batch": B * world},
+               "calibration": {"images": INT8_CALIB_IMAGES, "source": "device (FP32 forwards with statistics), "
+                               "seeded U[0,1) images", "scales": len(scales), "seconds": round(calib_s, 3)},
+               "e2e": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
+                       "h2d_bytes_per_step": world * host_in.numel() * 4,
+                       "d2h_bytes_per_step": world * host_out.numel() * 4},
+               "batch1": {"ms_per_image": b1_ms, "images_per_s": world / (b1_ms * 1e-3),
+                          "note": "device-resident single-image forward, one per GPU"},
+               "gpu_launches": n_ops.value * args.steps,
+               "conv_tops": {"achieved": tops, "peak_nominal": INT8_PEAK_TOPS_NOMINAL,
+                             "frac_of_nominal": tops / INT8_PEAK_TOPS_NOMINAL,
+                             "note": "algorithmic int8 ops (2 x MACs) of the conv_i8 launches"},
+               "forward_breakdown_ms": {k: round(v["ms"], 4) for k, v in per_kind.items()},
+               "forward_share": {k: round(v["ms"] / all_ms, 4) for k, v in per_kind.items()}}
+    model.set_int8(None)
+    return out
 
 
 # The isolated conv shapes of the benchmark's conv-GEMM sweep: (ci, co, k, stride, H = W).
@@ -481,6 +592,7 @@ def main():
     ap.add_argument("--hw", type=int, default=640)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-int8-sweep", action="store_true")
+    ap.add_argument("--no-int8", action="store_true", help="skip the INT8 model leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

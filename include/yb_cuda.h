@@ -67,6 +67,20 @@ status_t yb_cuda_upload_weights(void* ctx, const model_t* m, yb_precision p, con
  * then, as ERROR_INVALID_DIMS naming the tensor. */
 status_t yb_cuda_set_int8(void* ctx, const char* const* names, const float* scales, int n);
 
+/* INT8 calibration on the device: FP32 forwards of n images [n,3,H,W]
+ * (host, float32; H, W multiples of 32) recording max |x| of every tensor the
+ * INT8 plan names (conv outputs after their residual, SiLU pre-activations,
+ * attention outputs, the input), giving scale = max|x| / 127 (1 for an
+ * all-zero tensor), the rule of the CPU oracle's calibration.  The table is
+ * kept in the context (yb_cuda_int8_scale_entry reads it, in name order);
+ * apply != 0 also switches the context to INT8 under it, as
+ * yb_cuda_set_int8 would.  *n_scales (nullable) receives its size. */
+status_t yb_cuda_calibrate_int8(void* ctx, const float* images, int n, int H, int W, int apply, int* n_scales);
+
+/* Entry i of the last calibration's table: name (NUL-terminated, cap bytes
+ * available; ERROR_INVALID_DIMS when too small) and scale; either nullable. */
+status_t yb_cuda_int8_scale_entry(void* ctx, int i, char* name, int cap, float* scale);
+
 /* Stage tensor `idx` (0..22: the reference's stage_01_buf0 .. stage_23_buf22)
  * of image `image` of the last INT8 forward (not a pipelined one): out_nchw
  * [c][h][w] int8 (nullable) and its per-channel scales [c] (nullable; the

@@ -125,3 +125,30 @@ def test_missing_scale_reported(weights_n0, calib):
             m.set_int8({"input": -1.0})
     finally:
         m.close()
+
+
+def test_device_calibration(weights_n0, calib):
+    """Device calibration (FP32 forwards with statistics) names the same
+    tensors as the oracle's and lands within the FP32 path's tolerance of its
+    scales; the INT8 forward under the device table is bit-exact with the
+    oracle under the same table."""
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    o, scales = calib
+    m = yb.Model(weights_n0)
+    try:
+        dev = m.calibrate_int8(yw.make_batch(range(1000, 1004), 96, 96))
+        assert set(dev) == set(scales)
+        worst = max(abs(dev[k] - scales[k]) / scales[k] for k in scales)
+        print(f"device vs oracle calibration: {len(dev)} scales, worst rel diff {worst:.2e}")
+        assert worst < 1e-2
+        img = yw.make_input(6, 160, 128)
+        got = m.forward(img)
+        lg, _ = m.head(1)
+        ref = o.forward_i8(img, dev, stages=True)
+        _check_image(m, ref, 0)
+        assert np.array_equal(lg[0], ref["logits"])
+        assert dets_ok(compare_dets(got["dets"][0], ref["dets"]))
+    finally:
+        m.close()

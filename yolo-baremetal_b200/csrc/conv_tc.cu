@@ -345,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     const int q = e_idx & 3;                  // TMEM lane quarter (= warp % 4)
     const int grp = e_idx >> 2;               // this group takes every other tile
     const bool f32out = a.out_f32.ptr != nullptr;
+    float mpre = 0.0f, mout = 0.0f;  // calibration statistics (a.amax)
     for (int t = blockIdx.x + grp * gridDim.x, lt = grp; t < total_tiles; t += 2 * gridDim.x, lt += 2) {
       const int acc = lt % nacc;
       const uint32_t aph = (lt / nacc) & 1;
@@ -407,9 +408,20 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           v[e + 2] += bb.z;
           v[e + 3] += bb.w;
         }
+        const bool stats = a.amax != nullptr && valid;
+        if (stats) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c + e < nvalid) mpre = fmaxf(mpre, fabsf(v[e]));
+        }
         if (a.act == kActSiLU) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = silu_fast(v[e]);
+        }
+        if (stats) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (c + e < nvalid) mout = fmaxf(mout, fabsf(v[e]));
         }
         const bool second = c + 8 < nvalid;
         if (a.res.hi) {
@@ -421,6 +433,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
 #pragma unroll
           for (int e = 0; e < 16; ++e)
             if (e < 8 || second) v[e] += rv[e];
+          if (stats) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c + e < nvalid) mout = fmaxf(mout, fabsf(v[e]));
+          }
         }
         if (f32out) {
           if (valid) {
@@ -469,6 +486,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+    if (a.amax) {
+      const unsigned am = __activemask();
+      const unsigned wp = __reduce_max_sync(am, __float_as_uint(mpre));
+      const unsigned wo = __reduce_max_sync(am, __float_as_uint(mout));
+      if (lane == __ffs(am) - 1) {
+        atomicMax(a.amax, wp);
+        atomicMax(a.amax + 1, wo);
+      }
     }
   } else {
     // ---------------------------------------------------------- MMA issuer

@@ -242,6 +242,7 @@ cudaError_t Engine::conv_w(const std::string& prefix, bool plain, DevConv** out,
     return cudaErrorInvalidValue;
   }
   DevConv d;
+  d.name = prefix;
   d.co = w->dims[0];
   d.ci = w->dims[1];
   d.kh = w->dims[2];
@@ -334,6 +335,22 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     *q = static_cast<float*>(r);
     return cudaSuccess;
   };
+  // Calibration plans: a pair of max-|x| words, [0] registered under `pre`
+  // (when non-empty) and [1] under `out`.
+  auto stat_slot = [&](const std::string& out, const std::string& pre) -> unsigned* {
+    if (!p->calib || p->amax_used + 2 > p->amax_cap) return nullptr;
+    const int k = p->amax_used;
+    p->amax_used += 2;
+    if (!pre.empty()) p->amax_names.emplace_back(pre, k);
+    p->amax_names.emplace_back(out, k + 1);
+    return p->d_amax + k;
+  };
+  if (p->calib) {
+    p->amax_cap = 2048;
+    YB_TRY(cudaMalloc(&p->d_amax, p->amax_cap * sizeof(unsigned)));
+    p->allocs.push_back(p->d_amax);
+    YB_TRY(cudaMemset(p->d_amax, 0, p->amax_cap * sizeof(unsigned)));
+  }
   auto add_conv = [&](const DevConv* w, const Src& in, int stride, int pad, int act, SOut out, SView res,
                       FOut fout = FOut()) -> cudaError_t {
     if (in.c0 + in.c1 != w->ci || in.c0 % 8 || w->ci % 8) {
@@ -379,6 +396,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     a.out_f32 = fout;
     a.res = res;
     a.err = d_err_;
+    if (p->calib && !fout.ptr) a.amax = stat_slot(w->name, act == kActSiLU ? w->name + ":pre" : std::string());
     conv_setup_tma(&a);
     const int sms = num_sms_;
     Op op{step, [a, sms](cudaStream_t s) { return launch_conv_tc(a, s, sms); }};
@@ -543,7 +561,14 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     aa.pe_w = pe->w;
     aa.pe_b = pe->bias;
     aa.out = ov(ao);
-    {
+    if (p->calib) {
+      // Attention output plus positional term: the INT8 plan's "<psa>.attn.ope".
+      unsigned* st = stat_slot(pre + ".attn.ope", std::string());
+      const SView av = tv(ao);
+      const int h = x.H, w = x.W;
+      add_op(kOpAttn, 0.0, 0.0, [aa](cudaStream_t s) { return launch_attention(aa, s); });
+      add_op(kOpPool, 0.0, 0.0, [=](cudaStream_t s) { return launch_absmax_split(av, B, h, w, c, st, s); });
+    } else {
       const double ntok = static_cast<double>(x.H) * x.W;
       const double fl = static_cast<double>(B) * heads * (2.0 * ntok * ntok * (kd + hd) + 18.0 * ntok * hd);
       const double by = 4.0 * B * ntok * (qkv->co + c) + 4.0 * 10.0 * c;
@@ -623,6 +648,13 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     sa.bias = stem_.bias;
     sa.act = kActSiLU;
     sa.out = ov(S[0]);
+    if (p->calib) {
+      unsigned* st = stat_slot("input", std::string());
+      const float* din = p->d_in;
+      const long long n = static_cast<long long>(B) * 3 * H * W;
+      add_op(kOpPool, 0.0, 0.0, [=](cudaStream_t s) { return launch_absmax_f32(din, n, st, s); });
+      sa.amax = stat_slot("model.0", "model.0:pre");
+    }
     if (stem_.ci != 3 || stem_.k != 3) {
       *why = "unsupported stem";
       return cudaErrorInvalidValue;
@@ -734,6 +766,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       da.bias = dw0->bias;
       da.act = kActSiLU;
       da.out = ov(d0);
+      da.amax = stat_slot(b3 + si + ".0.0", b3 + si + ".0.0:pre");
       if (dw0->c != f.C) {
         *why = "detect dw width";
         return cudaErrorInvalidValue;
@@ -749,6 +782,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       db.w = dw1->w;
       db.bias = dw1->bias;
       db.out = ov(d1);
+      db.amax = stat_slot(b3 + si + ".1.0", b3 + si + ".1.0:pre");
       if (dw1->c != p0.C) {
         *why = "detect dw width";
         return cudaErrorInvalidValue;
@@ -901,6 +935,57 @@ cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::
   *out = p.get();
   plans_.push_back(std::move(p));
   return cudaSuccess;
+}
+
+cudaError_t Engine::calibrate(const float* images, int n, int H, int W, std::map<std::string, float>* table,
+                              std::string* why) {
+  if (hw_.empty()) {
+    *why = "no weights uploaded";
+    return cudaErrorInvalidValue;
+  }
+  if (n < 1 || H < 32 || W < 32 || H % 32 || W % 32) {
+    *why = "calibration needs n >= 1 images with H, W multiples of 32";
+    return cudaErrorInvalidValue;
+  }
+  cudaSetDevice(device_);
+  Plan p;
+  p.B = 1;
+  p.H = H;
+  p.W = W;
+  p.calib = true;
+  cudaError_t e = build(&p, why);
+  if (e == cudaSuccess && p.amax_used > p.amax_cap) {
+    *why = "calibration statistics table too small";
+    e = cudaErrorInvalidValue;
+  }
+  const size_t img = static_cast<size_t>(3) * H * W;
+  for (int i = 0; i < n && e == cudaSuccess; ++i) {
+    e = cudaMemcpyAsync(p.d_in, images + i * img, img * 4, cudaMemcpyHostToDevice, stream_);
+    if (e == cudaSuccess) e = run(&p, stream_, nullptr);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+  std::vector<unsigned> words(p.amax_cap);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(words.data(), p.d_amax, words.size() * sizeof(unsigned), cudaMemcpyDeviceToHost);
+  const int kerr = take_kernel_error();
+  if (e == cudaSuccess && kerr) {
+    *why = "kernel error flag " + std::to_string(kerr) + " during calibration";
+    e = cudaErrorLaunchFailure;
+  }
+  if (e == cudaSuccess) {
+    std::map<std::string, float> amax;
+    for (const auto& nk : p.amax_names) {
+      float v;
+      std::memcpy(&v, &words[nk.second], sizeof v);
+      auto it = amax.find(nk.first);
+      if (it == amax.end()) amax[nk.first] = v;
+      else if (v > it->second) it->second = v;
+    }
+    table->clear();
+    for (const auto& kv : amax) (*table)[kv.first] = kv.second > 0.0f ? kv.second / 127.0f : 1.0f;
+  }
+  release_plan(&p);
+  return e;
 }
 
 cudaError_t Engine::run(Plan* p, cudaStream_t s, cudaEvent_t* ev) {

@@ -26,6 +26,7 @@ struct HostTensor {
 using WeightMap = std::map<std::string, HostTensor>;
 
 struct DevConv {
+  std::string name;  // weight prefix (the scale-table name of its output)
   uint8_t* wpack = nullptr;
   float* bias = nullptr;
   int co = 0, ci = 0, kh = 0, kw = 0;
@@ -97,6 +98,12 @@ struct Plan {
     std::vector<float> cs;
   };
   std::vector<I8Stage> i8stage;
+  // Calibration plans (FP32 with statistics): per named tensor the index of
+  // its max-|x| word in d_amax (float bits, atomically raised by the kernels).
+  bool calib = false;
+  unsigned* d_amax = nullptr;
+  int amax_used = 0, amax_cap = 0;
+  std::vector<std::pair<std::string, int>> amax_names;
 };
 
 class Engine {
@@ -131,6 +138,12 @@ class Engine {
   // plans built under the previous table are released.
   void set_int8_scales(std::map<std::string, float> s);
   bool int8_mode() const { return !i8_scales_.empty(); }
+
+  // FP32 forwards of n images [n,3,H,W] (host) with statistics: the INT8
+  // scale table max|x| / 127 (1 for an all-zero tensor) of every tensor the
+  // INT8 plan names.  Uses its own batch-1 plan, released on return.
+  cudaError_t calibrate(const float* images, int n, int H, int W, std::map<std::string, float>* table,
+                        std::string* why);
 
   int device() const { return device_; }
   cudaStream_t stream() const { return stream_; }

@@ -79,6 +79,8 @@ struct Ctx {
   cudaStream_t copy_stream = nullptr;
   cudaEvent_t in_ready[2] = {nullptr, nullptr};
   cudaEvent_t slot_free[2] = {nullptr, nullptr};
+  // Scale table of the last yb_cuda_calibrate_int8, in name order.
+  std::vector<std::pair<std::string, float>> calib;
 };
 
 // Sub-batch of a pipelined host forward (yb_cuda_forward with B >= 2 chunks).
@@ -374,6 +376,44 @@ extern "C" status_t yb_cuda_set_int8(void* ctx, const char* const* names, const 
   status_t st = ctx_ready(c);
   if (st != SUCCESS) return st;
   return set_int8(c, names, scales, n);
+}
+
+extern "C" status_t yb_cuda_calibrate_int8(void* ctx, const float* images, int n, int H, int W, int apply,
+                                           int* n_scales) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !images) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  std::map<std::string, float> table;
+  std::string why;
+  cudaError_t e = c->eng->calibrate(images, n, H, W, &table, &why);
+  if (e == cudaErrorInvalidValue) {
+    set_error("calibration: " + why);
+    return ERROR_INVALID_DIMS;
+  }
+  if (e != cudaSuccess) {
+    st = cuda_status(e, "calibration");
+    if (!why.empty()) set_error(std::string(last_error()) + " (" + why + ")");
+    return st;
+  }
+  c->calib.assign(table.begin(), table.end());
+  if (n_scales) *n_scales = static_cast<int>(c->calib.size());
+  if (apply) c->eng->set_int8_scales(std::move(table));
+  if (apply) c->last = nullptr;
+  return SUCCESS;
+}
+
+extern "C" status_t yb_cuda_int8_scale_entry(void* ctx, int i, char* name, int cap, float* scale) {
+  Ctx* c = as_ctx(ctx);
+  if (!c) return ERROR_NULL_POINTER;
+  if (i < 0 || i >= static_cast<int>(c->calib.size())) return ERROR_INVALID_DIMS;
+  const std::string& nm = c->calib[i].first;
+  if (name) {
+    if (cap < static_cast<int>(nm.size()) + 1) return ERROR_INVALID_DIMS;
+    std::memcpy(name, nm.c_str(), nm.size() + 1);
+  }
+  if (scale) *scale = c->calib[i].second;
+  return SUCCESS;
 }
 
 extern "C" status_t yb_cuda_get_int8_stage(void* ctx, int idx, int image, signed char* out_nchw, float* scales,

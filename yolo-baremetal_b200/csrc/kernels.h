@@ -83,6 +83,10 @@ struct ConvArgs {
   FOut out_f32;  // used instead of `out` when out_f32.ptr != nullptr
   SView res;     // res.hi == nullptr: no residual
   int* err = nullptr;
+  // Calibration statistics (null in inference plans): amax[0] |= max
+  // |pre-activation|, amax[1] |= max |output| over the SiLU output and the
+  // residual sum, as float bits (atomicMax on non-negative floats).
+  unsigned* amax = nullptr;
   // Activation operand source.  a_tma == 0: the producer warps gather it with
   // cp.async (any view, upsampled or two-source inputs).  a_tma == 1: one
   // thread loads it with TMA im2col copies through tm_hi / tm_lo (one
@@ -140,6 +144,7 @@ struct StemArgs {
   const float* bias = nullptr;
   int act = kActSiLU;
   SOut out;
+  unsigned* amax = nullptr;  // calibration statistics, as in ConvArgs
 };
 cudaError_t launch_stem(const StemArgs& a, cudaStream_t s);
 // Must run once per device before the first launch_stem (not under capture).
@@ -154,8 +159,14 @@ struct DwArgs {
   const float* bias = nullptr;
   int act = kActNone;
   SOut out;
+  unsigned* amax = nullptr;  // calibration statistics, as in ConvArgs
 };
 cudaError_t launch_dwconv3x3(const DwArgs& a, cudaStream_t s);
+
+// Calibration: *amax |= max |x| (float bits) over a split tensor view
+// [B, H, W, C] (value = hi + lo) or a plain fp32 array of n elements.
+cudaError_t launch_absmax_split(SView v, int B, int H, int W, int C, unsigned* amax, cudaStream_t s);
+cudaError_t launch_absmax_f32(const float* x, long long n, unsigned* amax, cudaStream_t s);
 
 // Max pool with padding k/2 excluded from the max (layers.c:191-217).
 // Output size Ho x Wo (0 = same as the input, for stride 1).

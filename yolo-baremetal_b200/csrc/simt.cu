@@ -82,6 +82,17 @@ __device__ __forceinline__ void stem_fetch(const StemArgs& a, float* sx, int t, 
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// Calibration statistics: one atomicMax per converged lane group.
+__device__ __forceinline__ void amax_warp(unsigned* amax, float mpre, float mout) {
+  const unsigned am = __activemask();
+  const unsigned wp = __reduce_max_sync(am, __float_as_uint(mpre));
+  const unsigned wo = __reduce_max_sync(am, __float_as_uint(mout));
+  if ((threadIdx.x & 31) == static_cast<unsigned>(__ffs(am) - 1)) {
+    atomicMax(amax, wp);
+    atomicMax(amax + 1, wo);
+  }
+}
+
 template <int CO>
 __global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
   using T = StemTile<CO>;
@@ -97,6 +108,7 @@ __global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
   const int tiles_x = (a.Wo + T::TW - 1) / T::TW, tiles_y = (a.Ho + T::TH - 1) / T::TH;
   const int total = a.B * tiles_x * tiles_y;
   const int r = tid >> 4, x0 = tid & 15;
+  float mpre = 0.0f, mout = 0.0f;  // calibration statistics (a.amax)
   int k = 0;
   if (static_cast<int>(blockIdx.x) < total) stem_fetch<CO>(a, sxb, blockIdx.x, tiles_x, tiles_y);
   for (int t = blockIdx.x; t < total; t += gridDim.x, ++k) {
@@ -148,11 +160,19 @@ __global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = a.act == kActSiLU ? silu_fast(acc[j][c + e]) : acc[j][c + e];
+        if (a.amax) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            mpre = fmaxf(mpre, fabsf(acc[j][c + e]));
+            mout = fmaxf(mout, fabsf(v[e]));
+          }
+        }
         store8(o + c, a.out.plane, v);
       }
     }
     __syncthreads();  // this buffer is refilled by the next iteration's prefetch
   }
+  if (a.amax) amax_warp(a.amax, mpre, mout);
 }
 
 // ------------------------------------------------------------- depthwise 3x3
@@ -186,11 +206,46 @@ __global__ void dw3x3_kernel(const DwArgs a) {
       for (int e = 0; e < 8; ++e) s[e] = __fadd_rn(s[e], __fmul_rn(v[e], __ldg(w + e)));
     }
   }
+  float mpre = 0.0f;
+  if (a.amax) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mpre = fmaxf(mpre, fabsf(s[e]));
+  }
   if (a.act == kActSiLU) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) s[e] = silu(s[e]);
   }
   store8(a.out.hi + vaddr(a.out, b, p) + c, a.out.plane, s);
+  if (a.amax) {
+    float mout = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mout = fmaxf(mout, fabsf(s[e]));
+    amax_warp(a.amax, mpre, mout);
+  }
+}
+
+// ------------------------------------------------------------- calibration
+__global__ void absmax_split_kernel(SView v, int B, int H, int W, int C, unsigned* amax) {
+  const long long total = static_cast<long long>(B) * H * W * C;
+  float m = 0.0f;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % C);
+    const long long pix = idx / C;
+    const int b = static_cast<int>(pix / (static_cast<long long>(H) * W));
+    const long long p = pix - static_cast<long long>(b) * H * W;
+    const long long o = vaddr(v, b, p) + c;
+    m = fmaxf(m, fabsf(join1(v.hi[o], v.hi[o + v.plane])));
+  }
+  amax_warp(amax, 0.0f, m);
+}
+
+__global__ void absmax_f32_kernel(const float* x, long long n, unsigned* amax) {
+  float m = 0.0f;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    m = fmaxf(m, fabsf(x[i]));
+  amax_warp(amax, 0.0f, m);
 }
 
 // ------------------------------------------------------------------ max pool
@@ -457,6 +512,21 @@ cudaError_t launch_stem(const StemArgs& a, cudaStream_t s) {
   if (a.Co == 16) stem_kernel<16><<<grid, 128, StemTile<16>::kSmem, s>>>(a);
   else if (a.Co == 32) stem_kernel<32><<<grid, 128, StemTile<32>::kSmem, s>>>(a);
   else stem_kernel<64><<<grid, 128, StemTile<64>::kSmem, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_absmax_split(SView v, int B, int H, int W, int C, unsigned* amax, cudaStream_t s) {
+  // The statistic lands in amax[1] (amax[0] receives 0).
+  const long long total = static_cast<long long>(B) * H * W * C;
+  const long long blocks = (total + 255) / 256;
+  absmax_split_kernel<<<static_cast<int>(blocks < 1184 ? (blocks < 1 ? 1 : blocks) : 1184), 256, 0, s>>>(v, B, H, W, C,
+                                                                                                     amax);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_absmax_f32(const float* x, long long n, unsigned* amax, cudaStream_t s) {
+  const long long blocks = (n + 255) / 256;
+  absmax_f32_kernel<<<static_cast<int>(blocks < 1184 ? (blocks < 1 ? 1 : blocks) : 1184), 256, 0, s>>>(x, n, amax);
   return cudaGetLastError();
 }
 

@@ -37,7 +37,8 @@ EXPORTS = {
     "detection.h": ["decode_detections"],
     "utils.h": ["timer_start", "timer_stop", "timer_elapsed_ms", "load_named_tensor", "save_named_tensor", "fold_bn"],
     "yb_cuda.h": ["yb_cuda_init", "yb_cuda_upload_weights", "yb_cuda_load_bin", "yb_cuda_forward",
-                  "yb_cuda_set_int8", "yb_cuda_get_int8_stage",
+                  "yb_cuda_set_int8", "yb_cuda_get_int8_stage", "yb_cuda_calibrate_int8",
+                  "yb_cuda_int8_scale_entry",
                   "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_detect_topk_noalloc",
                   "yb_cuda_forward_sharded",
                   "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error"],
@@ -107,6 +108,9 @@ def lib() -> C.CDLL:
                                           C.c_int, C.POINTER(C.c_int)]
         L.yb_cuda_destroy.argtypes = [C.c_void_p]
         L.yb_cuda_set_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.yb_cuda_calibrate_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                             C.POINTER(C.c_int)]
+        L.yb_cuda_int8_scale_entry.argtypes = [C.c_void_p, C.c_int, C.c_char_p, C.c_int, C.POINTER(C.c_float)]
         L.yb_cuda_get_int8_stage.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                              C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.yb_int8_quantize_conv.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
@@ -201,6 +205,20 @@ class Model:
         names = (C.c_char_p * max(n, 1))(*[k.encode() for k in scales])
         vals = np.ascontiguousarray(list(scales.values()) or [0.0], dtype=np.float32)
         check(lib().yb_cuda_set_int8(self.ctx, names, vals.ctypes.data, n), "yb_cuda_set_int8")
+
+    def calibrate_int8(self, images: np.ndarray, apply: bool = True) -> dict:
+        """Device calibration from FP32 forwards of images [n,3,H,W]: {name: scale}; apply switches to INT8."""
+        x = np.ascontiguousarray(images, dtype=np.float32)
+        n = C.c_int()
+        check(lib().yb_cuda_calibrate_int8(self.ctx, x.ctypes.data, x.shape[0], x.shape[2], x.shape[3],
+                                           1 if apply else 0, C.byref(n)), "yb_cuda_calibrate_int8")
+        out = {}
+        name = C.create_string_buffer(256)
+        v = C.c_float()
+        for i in range(n.value):
+            check(lib().yb_cuda_int8_scale_entry(self.ctx, i, name, 256, C.byref(v)), "yb_cuda_int8_scale_entry")
+            out[name.value.decode()] = float(v.value)
+        return out
 
     def int8_stage(self, idx: int, image: int = 0):
         """(int8 [C,H,W], per-channel scales [C]) of stage tensor idx (0..22) of the last INT8 forward."""
