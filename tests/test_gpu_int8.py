@@ -56,3 +56,17 @@ def test_int8_conv_bit_exact(ci, co, k, stride, H, W, B, act, bias):
     print(f"int8 conv {ci}->{co} k{k} s{stride} @{H}x{W} B{B}: {diff} of {want.size} differ; "
           f"{sat:.2%} saturated, {np.mean(want == 0):.2%} zero")
     assert diff == 0
+
+
+@pytest.mark.parametrize("shrink", [2e-3, 1e-4])
+def test_int8_conv_wide_requant(shrink):
+    """Output scales far below the accumulator scale push requantisation
+    shifts under 32, which the kernel serves with its 64-bit arithmetic
+    instead of the 32-bit word path; results stay bit-exact."""
+    lyr = make_layer(32, 48, 3, 20, 18, B=2, seed=5, act=False, bias=True)
+    lyr["s_pre"] = lyr["s_out"] = np.float32(lyr["s_out"] * shrink)
+    q = quantize_lib(lyr)
+    assert int(q["shift"].min()) < 32
+    got = _run_gpu(lyr, q, 3, 1)
+    want = conv_oracle(lyr["xq"], q, 3, 1, lyr["pad"])
+    assert np.count_nonzero(got != want) == 0

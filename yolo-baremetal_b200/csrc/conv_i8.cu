@@ -12,10 +12,10 @@
 //              one TMA im2col copy per filter tap of a_cpp channels (32, 64
 //              or 128: 32B / 64B / 128B swizzled sub-tiles), all completing
 //              on the stage's full barrier.
-//   warp 8     TMEM (2-4 accumulators) and, from one lane, the UMMAs.
-//   warps 0-7  two epilogue groups on alternate tiles, one warp per TMEM
-//              lane quarter: tcgen05.ld, requantise, SiLU table, 16-byte
-//              int8 stores.
+//   warp 16    TMEM (2-4 accumulators) and, from one lane, the UMMAs.
+//   warps 0-15 four epilogue groups taking tiles round robin (as many as
+//              there are accumulators), one warp per TMEM lane quarter:
+//              tcgen05.ld, requantise, SiLU table, 16-byte int8 stores.
 // Every barrier wait is bounded; a timeout sets the error word, stops the
 // other roles, drains the tensor core and frees tensor memory.
 #include <cudaTypedefs.h>
@@ -39,8 +39,9 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kKB = 128;                      // K values (= bytes) per chunk
 constexpr uint32_t kATile = kBM * 128;        // activation tile of one chunk
-constexpr int kMmaWarp = 8, kProdWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kEpiGroups = 3;                 // epilogue groups of 4 warps
+constexpr int kMmaWarp = 4 * kEpiGroups, kProdWarp = kMmaWarp + 1;
+constexpr int kThreads = 32 * (kProdWarp + 1);
 constexpr int kSmemLimit = 232448;
 constexpr int kMaxAcc = 4;
 constexpr int kMaxCo = 1024;
@@ -72,6 +73,85 @@ __device__ __forceinline__ long long rshift_rne(long long p, int sh) {
   return (p + ((1LL << (sh - 1)) - 1) + ((p >> sh) & 1)) >> sh;
 }
 
+// Requantises 16 channels of one pixel into 4 packed words: acc + bias,
+// fixed-point multiply, round-half-even shift, then the SiLU table (LUT) or
+// the clamp, plus the residual table term (RES).  FAST: one 64-bit
+// multiply-add per channel, acc * M + D with D = bias * M + 2^(sh-1) - 1,
+// whose high word shifted by sh - 32 is floor((p + 2^(sh-1) - 1) / 2^sh) for
+// p = (acc + bias) * M: the round-half-even result except at an exact tie,
+// where the low sh bits of the sum are all ones (so its low word is too) and
+// an odd quotient must be raised by one; such a unit is redone exactly.
+// Otherwise every intermediate is kept in 64 bits.
+// Exact path: every intermediate in 64 bits (rare: shifts below 32, table
+// terms too large for the fast path, or a unit with a tie).
+// Warp-collective (it reloads the 16 accumulators from tensor memory at
+// taddr): call with the whole warp.
+template <bool LUT, bool RES>
+__device__ __noinline__ uint4 requant16_exact(uint32_t taddr, const uint4 rw, const int4* qc, const int32_t* sb,
+                                              const int8_t* slut, const int32_t* srtab, int res_mult,
+                                              int res_shift) {
+  uint32_t r[16];
+  tc_ld_32x32b_x16(taddr, r);
+  tc_wait_ld();
+  uint32_t packed[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t rword = j == 0 ? rw.x : j == 1 ? rw.y : j == 2 ? rw.z : rw.w;
+    uint32_t w = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = 4 * j + k;
+      const int rve = static_cast<int>(static_cast<int8_t>((rword >> (8 * k)) & 0xFFu));
+      const long long v = static_cast<long long>(static_cast<int32_t>(r[e])) + sb[e];
+      long long y = rshift_rne(v * qc[e].x, qc[e].w + 32);
+      if (LUT) y = slut[(y < -128 ? -128 : y > 127 ? 127 : y) + 128];
+      if (RES) y += rshift_rne(static_cast<long long>(rve) * res_mult, res_shift);
+      const int o = static_cast<int>(y < -127 ? -127 : y > 127 ? 127 : y);
+      w |= (static_cast<uint32_t>(o) & 0xFFu) << (8 * k);
+    }
+    packed[j] = w;
+  }
+  return make_uint4(packed[0], packed[1], packed[2], packed[3]);
+}
+
+// Fast path (every shift >= 32): one 64-bit multiply-add per channel,
+// acc * M + D with D = bias * M + 2^(sh-1) - 1, whose high word shifted by
+// sh - 32 is floor((p + 2^(sh-1) - 1) / 2^sh) for p = (acc + bias) * M: the
+// round-half-even result except at an exact tie, where the low sh bits of the
+// sum are all ones (so its low word is too) and an odd quotient must be
+// raised by one.  Returns whether a low word was all ones; the caller then
+// redoes the unit on the exact path.
+template <bool LUT, bool RES>
+__device__ __forceinline__ bool requant16_fast(const uint32_t (&r)[16], const uint4 rw, const int4* qc,
+                                               const int8_t* slut, const int32_t* srtab, uint32_t (&packed)[4]) {
+  bool tie = false;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    int o[4];
+    const uint32_t rword = j == 0 ? rw.x : j == 1 ? rw.y : j == 2 ? rw.z : rw.w;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = 4 * j + k;
+      const int4 q = qc[e];
+      const long long d = (static_cast<long long>(q.z) << 32) | static_cast<unsigned>(q.y);
+      const long long p = static_cast<long long>(static_cast<int32_t>(r[e])) * q.x + d;
+      tie |= static_cast<unsigned>(p) == 0xFFFFFFFFu;
+      int v = static_cast<int>(p >> 32) >> q.w;
+      if (LUT) v = slut[min(max(v, -128), 127) + 128];
+      if (RES) {
+        // |table term| < 2^29: clamping v to +-2^30 first keeps the sum
+        // exact wherever the result is not saturated.
+        const int rve = static_cast<int>(static_cast<int8_t>((rword >> (8 * k)) & 0xFFu));
+        v = min(max(v, -(1 << 30)), 1 << 30) + srtab[rve + 128];
+      }
+      // Table values already lie in [-127, 127].
+      o[k] = (LUT && !RES) ? v : min(max(v, -127), 127);
+    }
+    packed[j] = __byte_perm(__byte_perm(o[0], o[1], 0x0040), __byte_perm(o[2], o[3], 0x0040), 0x5410);
+  }
+  return tie;
+}
+
 __device__ __forceinline__ void raise_err(int* err, volatile int* abort_flag, int code) {
   *abort_flag = 1;
   if (err) atomicCAS(err, 0, code);
@@ -93,18 +173,35 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
   uint64_t* drain = acc_empty + kMaxAcc;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Per output channel sq = {multiplier M, low and high word of
+  // D = bias * M + 2^(shift-1) - 1, shift - 32} and sb = bias; a zero
+  // multiplier gets shift 32 (its result is 0 under any shift).  With
+  // shift >= 32 for every channel (fast), y = (acc * M + D) >> shift is the
+  // rounded result except at exact ties, which requant16_fast detects.
   const int nq = a.n_tile * a.n_tiles;
-  int32_t* sbias = reinterpret_cast<int32_t*>(tail + 512);
-  int32_t* smult = sbias + nq;
-  int32_t* sshift = smult + nq;
-  int8_t* slut = reinterpret_cast<int8_t*>(sshift + nq);
+  int4* sq = reinterpret_cast<int4*>(tail + 512);
+  int32_t* sb = reinterpret_cast<int32_t*>(sq + nq);
+  int32_t* srtab = sb + nq;
+  int8_t* slut = reinterpret_cast<int8_t*>(srtab + 256);
+  int fast_ok = 1;
   for (int i = threadIdx.x; i < nq; i += kThreads) {
     const bool ok = i < a.Co;
-    sbias[i] = ok ? a.bias[i] : 0;
-    smult[i] = ok ? a.mult[i] : 0;
-    sshift[i] = ok ? a.shift[i] : 1;
+    const int b = ok ? a.bias[i] : 0;
+    const int m = ok ? a.mult[i] : 0;
+    const int sh = m == 0 ? 32 : a.shift[i];
+    if (sh < 32) fast_ok = 0;
+    const long long d = static_cast<long long>(b) * m + ((1LL << (sh - 1)) - 1);
+    sq[i] = make_int4(m, static_cast<int>(static_cast<unsigned long long>(d) & 0xFFFFFFFFull),
+                      static_cast<int>(d >> 32), sh - 32);
+    sb[i] = b;
   }
-  for (int i = threadIdx.x; i < 256; i += kThreads) slut[i] = a.lut ? a.lut[i] : 0;
+  // Residual term rshift_rne(r * res_mult, res_shift) of every int8 r (the
+  // fast path needs it below 2^29 in magnitude).
+  if (a.res && ((128LL * a.res_mult) >> a.res_shift) >= (1LL << 29)) fast_ok = 0;
+  for (int i = threadIdx.x; i < 256; i += kThreads) {
+    slut[i] = a.lut ? a.lut[i] : 0;
+    srtab[i] = a.res ? static_cast<int32_t>(rshift_rne(static_cast<long long>(i - 128) * a.res_mult, a.res_shift)) : 0;
+  }
 
   uint32_t acc_stride = 32;
   while (acc_stride < static_cast<uint32_t>(a.n_tile)) acc_stride <<= 1;
@@ -129,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
     tmem_relinquish();
   }
   tc_fence_before();
-  __syncthreads();
+  const bool fast = __syncthreads_and(fast_ok) != 0;
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -238,8 +335,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
+    // Groups take tiles round robin; each owns one accumulator, so only
+    // min(kEpiGroups, nacc) groups work.
     const int grp = warp >> 2;
-    for (int t = blockIdx.x + grp * gridDim.x, lt = grp; t < total_tiles; t += 2 * gridDim.x, lt += 2) {
+    const int ngrp = min(kEpiGroups, nacc);
+    for (int t = blockIdx.x + grp * gridDim.x, lt = grp; grp < ngrp && t < total_tiles;
+         t += ngrp * gridDim.x, lt += ngrp) {
       const int acc = lt % nacc;
       const uint32_t aph = (lt / nacc) & 1;
       if (!mbar_wait(&acc_full[acc], aph, abort_flag)) {
@@ -261,13 +362,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       // 32-byte run.
       for (int c = 0; c < nvalid; c += 32) {
         const bool two = c + 16 < nvalid;
-        uint32_t r[32];
-        uint32_t(&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[0]);
-        uint32_t(&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[16]);
-        tc_ld_32x32b_x16(tbase + c, r0);
-        if (two) tc_ld_32x32b_x16(tbase + c + 16, r1);
-        tc_wait_ld();
         if (a.out_f32) {
+          uint32_t r[32];
+          uint32_t(&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[0]);
+          uint32_t(&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[16]);
+          tc_ld_32x32b_x16(tbase + c, r0);
+          if (two) tc_ld_32x32b_x16(tbase + c + 16, r1);
+          tc_wait_ld();
           if (valid) {
             const long long fb = pm / HoWo;
             float* of = a.out_f32 + fb * a.f32_bstride + (pm - fb * HoWo) * a.f32_cstride + n0 + c;
@@ -275,40 +376,65 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
             for (int e = 0; e < 32; e += 4) {
               if (n0 + c + e >= a.f32_co) break;
               float4 v;
-              v.x = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e])) + sbias[n0 + c + e]) *
+              v.x = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e])) + sb[n0 + c + e]) *
                     a.deq[n0 + c + e];
               v.y = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e + 1])) +
-                                       sbias[n0 + c + e + 1]) *
+                                       sb[n0 + c + e + 1]) *
                     a.deq[n0 + c + e + 1];
               v.z = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e + 2])) +
-                                       sbias[n0 + c + e + 2]) *
+                                       sb[n0 + c + e + 2]) *
                     a.deq[n0 + c + e + 2];
               v.w = static_cast<float>(static_cast<long long>(static_cast<int32_t>(r[e + 3])) +
-                                       sbias[n0 + c + e + 3]) *
+                                       sb[n0 + c + e + 3]) *
                     a.deq[n0 + c + e + 3];
               *reinterpret_cast<float4*>(of + e) = v;
             }
           }
           continue;
         }
-        int8_t rv[32];
+        uint4 rvv[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
         if (a.res) {
           const int8_t* rp = a.res + pm * a.res_cstride + a.res_coff + n0 + c;
-          *reinterpret_cast<uint4*>(&rv[0]) = *reinterpret_cast<const uint4*>(rp);
-          if (two) *reinterpret_cast<uint4*>(&rv[16]) = *reinterpret_cast<const uint4*>(rp + 16);
+          rvv[0] = *reinterpret_cast<const uint4*>(rp);
+          if (two) rvv[1] = *reinterpret_cast<const uint4*>(rp + 16);
         }
-        uint32_t packed[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          if (e >= 16 && !two) break;
-          const int ch = n0 + c + e;
-          const long long v = static_cast<long long>(static_cast<int32_t>(r[e])) + sbias[ch];
-          long long y = rshift_rne(v * smult[ch], sshift[ch]);
-          if (a.lut) y = slut[(y < -128 ? -128 : y > 127 ? 127 : y) + 128];
-          if (a.res) y += rshift_rne(static_cast<long long>(rv[e]) * a.res_mult, a.res_shift);
-          const int o = static_cast<int>(y < -127 ? -127 : y > 127 ? 127 : y);
-          packed[e >> 2] |= (static_cast<uint32_t>(o) & 0xFFu) << (8 * (e & 3));
-        }
+        uint32_t p0[4] = {0u, 0u, 0u, 0u}, p1[4] = {0u, 0u, 0u, 0u};
+        const int mode = (a.lut ? 2 : 0) | (a.res ? 1 : 0);
+        // Two halves of 16 channels: one TMEM load each.
+        auto half = [&](int hh, uint32_t(&pk)[4]) {
+          uint32_t r[16];
+          tc_ld_32x32b_x16(tbase + c + 16 * hh, r);
+          tc_wait_ld();
+          const int4* qc = sq + n0 + c + 16 * hh;
+          const uint4 rh = rvv[hh];
+          const int32_t* sbh = sb + n0 + c + 16 * hh;
+          bool exact = !fast;
+          if (fast) {
+            switch (mode) {
+              case 0: exact = requant16_fast<false, false>(r, rh, qc, slut, srtab, pk); break;
+              case 1: exact = requant16_fast<false, true>(r, rh, qc, slut, srtab, pk); break;
+              case 2: exact = requant16_fast<true, false>(r, rh, qc, slut, srtab, pk); break;
+              default: exact = requant16_fast<true, true>(r, rh, qc, slut, srtab, pk); break;
+            }
+          }
+          // Warp-uniform: the exact path reloads the accumulators.
+          if (__any_sync(0xffffffffu, exact)) {
+            const uint32_t ta = tbase + c + 16 * hh;
+            uint4 w;
+            switch (mode) {
+              case 0: w = requant16_exact<false, false>(ta, rh, qc, sbh, slut, srtab, a.res_mult, a.res_shift); break;
+              case 1: w = requant16_exact<false, true>(ta, rh, qc, sbh, slut, srtab, a.res_mult, a.res_shift); break;
+              case 2: w = requant16_exact<true, false>(ta, rh, qc, sbh, slut, srtab, a.res_mult, a.res_shift); break;
+              default: w = requant16_exact<true, true>(ta, rh, qc, sbh, slut, srtab, a.res_mult, a.res_shift); break;
+            }
+            pk[0] = w.x;
+            pk[1] = w.y;
+            pk[2] = w.z;
+            pk[3] = w.w;
+          }
+        };
+        half(0, p0);
+        if (two) half(1, p1);
         const int h = lane & 1;
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
@@ -316,8 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
           uint32_t w[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t lo = __shfl_sync(0xffffffffu, packed[j], src);
-            const uint32_t hi = __shfl_sync(0xffffffffu, packed[4 + j], src);
+            const uint32_t lo = __shfl_sync(0xffffffffu, p0[j], src);
+            const uint32_t hi = __shfl_sync(0xffffffffu, p1[j], src);
             w[j] = h ? hi : lo;
           }
           const long long spo = __shfl_sync(0xffffffffu, po, src);
@@ -361,7 +487,7 @@ inline uint32_t sw128_off(uint32_t row, uint32_t chunk16) {
 
 int stages_for_i8(int n_tile, int n_tiles) {
   const int stage = static_cast<int>(kATile) + n_tile * 128;
-  const int extra = 1024 + 512 + 3 * 4 * n_tile * n_tiles + 256;
+  const int extra = 1024 + 512 + 20 * n_tile * n_tiles + 1024 + 256;
   const int st = (kSmemLimit - extra) / stage;
   return st > 8 ? 8 : st;
 }
@@ -452,7 +578,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
   }
   const int stages = stages_for_i8(a.n_tile, a.n_tiles);
   if (stages < 2) return cudaErrorInvalidValue;
-  const int smem = 1024 + 512 + 3 * 4 * a.n_tile * a.n_tiles + 256 +
+  const int smem = 1024 + 512 + 20 * a.n_tile * a.n_tiles + 1024 + 256 +
                    stages * (static_cast<int>(kATile) + a.n_tile * 128);
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
