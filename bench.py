@@ -403,7 +403,7 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-INT8_KINDS = ["conv_i8", "quantize_input", "dw3x3_i8", "maxpool_concat_i8", "attention_i8", "decode", "topk"]
+INT8_KINDS = ["conv_i8", "stem_i8", "dw3x3_i8", "maxpool_concat_i8", "attention_i8", "decode", "topk"]
 INT8_CALIB_IMAGES = 32  # seeded U[0,1) calibration images (the benchmark's INT8 recipe)
 
 

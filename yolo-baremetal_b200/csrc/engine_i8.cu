@@ -541,9 +541,15 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     YB_TRY(dalloc(static_cast<size_t>(B) * 3 * H * W * 4, &q));
     p->d_in = static_cast<float*>(q);
   }
+  // model.0 (3x3 stride 2 from the 3 input channels): one kernel quantises
+  // the fp32 input and convolves (stem_i8); other first layers take the
+  // quantised input through the general convolution.
+  const HostTensor* w0 = find("model.0.conv.weight");
+  const bool fused_stem = w0 && w0->ndim == 4 && w0->dims[1] == 3 && w0->dims[2] == 3 && w0->dims[3] == 3 &&
+                          (w0->dims[0] == 16 || w0->dims[0] == 32 || w0->dims[0] == 64);
   QT xin;
-  YB_TRY(tensor(3, H, W, &xin));
-  {
+  if (!fused_stem) {
+    YB_TRY(tensor(3, H, W, &xin));
     const I8View ov = xin.view();
     float* din = p->d_in;
     add_op(kOpStem, 0.0, 7.0 * B * H * W,
@@ -559,7 +565,54 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     return conv(P, false, b[i], src, 2, 1, true, nullptr);
   };
   auto outw = [&](const std::string& L) { return wdim0(L + ".cv2.conv.weight"); };
-  YB_TRY(down(0, xin));
+  if (fused_stem) {
+    const int co = w0->dims[0];
+    float s_out = 0.f, s_pre = 0.f;
+    if (!scale("model.0", &s_out) || !scale("model.0:pre", &s_pre)) return cudaErrorInvalidValue;
+    const float cs[3] = {s_in, s_in, s_in};
+    QWeights q;
+    if (!quantize(*w0, find("model.0.conv.bias"), cs, static_cast<double>(s_pre), &q))
+      return fail("int8: requantisation ratio out of range in model.0");
+    std::vector<uint32_t> wp(static_cast<size_t>(9) * co);
+    for (int o = 0; o < co; ++o)
+      for (int t = 0; t < 9; ++t) {
+        uint32_t v = 0;
+        for (int c = 0; c < 3; ++c)
+          v |= (static_cast<uint32_t>(q.wq[(static_cast<size_t>(o) * 3 + c) * 9 + t]) & 0xFFu) << (8 * c);
+        wp[static_cast<size_t>(t) * co + o] = v;
+      }
+    int8_t lut[256];
+    silu_lut(lut, s_pre, s_out);
+    void *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr, *dl = nullptr;
+    YB_TRY(upload(wp.data(), wp.size() * 4, &dw));
+    YB_TRY(upload(q.bq.data(), q.bq.size() * 4, &db));
+    YB_TRY(upload(q.mult.data(), q.mult.size() * 4, &dm));
+    YB_TRY(upload(q.shift.data(), q.shift.size() * 4, &ds));
+    YB_TRY(upload(lut, 256, &dl));
+    YB_TRY(tensor(co, (H - 1) / 2 + 1, (W - 1) / 2 + 1, &b[0]));
+    YB_TRY(init_stem_i8_attributes());
+    StemI8Args sa;
+    sa.in = p->d_in;
+    sa.B = B;
+    sa.H = H;
+    sa.W = W;
+    sa.Ho = b[0].H;
+    sa.Wo = b[0].W;
+    sa.Co = co;
+    sa.s_in = s_in;
+    sa.w = static_cast<const uint32_t*>(dw);
+    sa.bias = static_cast<const int32_t*>(db);
+    sa.mult = static_cast<const int32_t*>(dm);
+    sa.shift = static_cast<const int32_t*>(ds);
+    sa.lut = static_cast<const int8_t*>(dl);
+    sa.out = b[0].view();
+    const double po = static_cast<double>(B) * sa.Ho * sa.Wo;
+    add_op(kOpStem, 2.0 * po * co * 27, 4.0 * B * 3 * H * W + po * co,
+           [sa](cudaStream_t st) { return launch_stem_i8(sa, st); });
+    b[0].set_scale(s_out);
+  } else {
+    YB_TRY(down(0, xin));
+  }
   step = 1;
   YB_TRY(down(1, b[0]));
   step = 2;

@@ -37,6 +37,26 @@ struct I8AttnArgs {
 };
 
 cudaError_t launch_quantize_input(const float* in, int B, int C, int H, int W, float s, I8View out, cudaStream_t st);
+
+// The first convolution fused with the input quantisation: 3x3 stride 2
+// pad 1 from the NCHW fp32 input [B, 3, H, W] (quantised in shared memory
+// with the input rule, padding 0) to int8 NHWC [B, Ho, Wo, Co], Co in
+// {16, 32, 64}, with the convolution requantisation and SiLU table.
+// w: [9][Co] words, each the taps of input channels 0..2 of one output
+// channel (byte 3 zero); bias / mult / shift / lut as for the kind::i8 conv.
+struct StemI8Args {
+  const float* in = nullptr;
+  int B = 0, H = 0, W = 0, Ho = 0, Wo = 0, Co = 0;
+  float s_in = 1.f;
+  const uint32_t* w = nullptr;
+  const int32_t* bias = nullptr;
+  const int32_t* mult = nullptr;
+  const int32_t* shift = nullptr;
+  const int8_t* lut = nullptr;
+  I8View out;
+};
+cudaError_t launch_stem_i8(const StemI8Args& a, cudaStream_t st);
+cudaError_t init_stem_i8_attributes();
 cudaError_t launch_maxpool_i8(I8View in, I8View out, int B, int H, int W, int C, int k, cudaStream_t st);
 cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const int8_t* w, const int32_t* bq,
                             const int32_t* mult, const int32_t* shift, const int8_t* lut, cudaStream_t st);
