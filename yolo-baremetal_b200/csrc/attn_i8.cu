@@ -1,0 +1,284 @@
+// PSA attention of the INT8 forward (layers.c:310-405 for the graph; the
+// integer softmax rules are in i8k.h) with both contractions on the
+// tensor cores: tcgen05.mma kind::i8, int32 accumulation in tensor memory.
+//
+// One CTA of 128 threads per (128 queries, head, image); thread i owns query
+// row i (TMEM lane i).  Keys go in blocks of 128:
+//   pass 1  S = Q K^T (one UMMA, M 128, N 128, K 32) -> row maximum;
+//   pass 2  S again -> t = min(255, rne((max - S) * mt, sht)), p = E[t],
+//           l += p, and p split into ph = p >> 6 (0..64) and pl = p & 63,
+//           written as int8 A operands; O_h += Ph V, O_l += Pl V (4 UMMAs of
+//           K 32 each, N 64).  o = 64 O_h + O_l is exact: |o| <= N 4096 127.
+// Then out = div_rne(rne(o * mo, sho), l) + the positional depthwise term,
+// clamped.  Tensor memory: S in columns [0, 128), O_h [128, 192), O_l
+// [192, 256).  Operands are K-major without swizzle: core matrices of 8 rows
+// x 16 bytes, 128 contiguous bytes each, row-group major.  One elected thread
+// issues the UMMAs; completion is a tcgen05.commit on one mbarrier that every
+// thread waits on with a bound (a timeout sets the error word and ends the
+// kernel after freeing tensor memory).
+#include <climits>
+#include <cstdint>
+
+#include "i8k.h"
+#include "sm100.cuh"
+
+namespace yb {
+namespace {
+
+constexpr int kAQ = 128;  // queries per CTA (UMMA M)
+constexpr int kAK = 128;  // keys per block
+constexpr int KD = 32, HD = 64;
+constexpr int kErrAttnWait = 7;
+
+// Byte offset of (row, k) in a K-major no-swizzle operand whose rows hold
+// kb bytes: core matrix (row / 8, k / 16), 128 bytes each, row-group major.
+__device__ __forceinline__ uint32_t ops_off(int row, int k, int kb) {
+  return static_cast<uint32_t>(((row >> 3) * (kb >> 4) + (k >> 4)) * 128 + (row & 7) * 16 + (k & 15));
+}
+
+__device__ __forceinline__ long long rne64(long long p, int sh) {
+  return (p + ((1LL << (sh - 1)) - 1) + ((p >> sh) & 1)) >> sh;
+}
+// a / l rounded half to even (l > 0), floor-based for negative a.
+__device__ __forceinline__ long long div_rne64(long long a, long long l) {
+  long long q = a / l, r = a % l;
+  if (r < 0) {
+    q -= 1;
+    r += l;
+  }
+  if (2 * r > l || (2 * r == l && (q & 1))) q += 1;
+  return q;
+}
+
+struct AttnSmem {
+  uint8_t q[kAQ * KD];        // A of S: 128 x 32
+  uint8_t k[kAK * KD];        // B of S: 128 keys x 32
+  uint8_t vt[HD * kAK];       // B of O: 64 channels x 128 keys
+  uint8_t ph[kAQ * kAK];      // A of O_h: 128 queries x 128 keys
+  uint8_t pl[kAQ * kAK];      // A of O_l
+  int32_t E[256];
+  int8_t pe[9 * HD];          // positional weights of this head, [tap][d]
+  uint64_t bar;
+  uint32_t tmem;
+  int abort;
+};
+
+__global__ void __launch_bounds__(128, 1) attention_i8_tc_kernel(const I8AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t attn_smem_raw[];
+  AttnSmem& S = *reinterpret_cast<AttnSmem*>(attn_smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int N = a.H * a.W;
+  const int q0 = blockIdx.x * kAQ, h = blockIdx.y, b = blockIdx.z;
+  const int blk = 2 * KD + HD;
+  const int8_t* base = a.qkv.p + static_cast<long long>(b) * a.qkv.bstride + h * blk;
+  for (int i = tid; i < 256; i += 128) S.E[i] = a.E[i];
+  for (int i = tid; i < 9 * HD; i += 128) S.pe[i] = a.pe_w[(i / HD) * a.dim + h * HD + i % HD];
+  // Q rows (zero past N), two 16-byte chunks per row.
+  for (int i = tid; i < kAQ * 2; i += 128) {
+    const int r = i >> 1, c = i & 1;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (q0 + r < N) v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(q0 + r) * a.qkv.cstride + 16 * c);
+    *reinterpret_cast<uint4*>(S.q + ops_off(r, 16 * c, KD)) = v;
+  }
+  if (tid == 0) {
+    mbar_init(&S.bar, 1);
+    S.abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&S.tmem, 256);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = S.tmem;
+  const uint32_t trow = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+  volatile int* abort_flag = &S.abort;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  // Keys [k0, k0 + 128) into S.k (zero past N); with_v also V^T into S.vt.
+  auto stage = [&](int k0, bool with_v) {
+    for (int i = tid; i < kAK * 2; i += 128) {
+      const int j = i >> 1, c = i & 1;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (k0 + j < N)
+        v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(k0 + j) * a.qkv.cstride + KD + 16 * c);
+      *reinterpret_cast<uint4*>(S.k + ops_off(j, 16 * c, KD)) = v;
+    }
+    if (with_v) {
+      // Thread j transposes key j's 64 values into column j of V^T.
+      const int j = tid;
+      uint4 vv[4] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u),
+                     make_uint4(0u, 0u, 0u, 0u)};
+      if (k0 + j < N) {
+        const uint4* vp = reinterpret_cast<const uint4*>(base + static_cast<long long>(k0 + j) * a.qkv.cstride + 2 * KD);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) vv[c] = vp[c];
+      }
+      const uint8_t* vb = reinterpret_cast<const uint8_t*>(vv);
+#pragma unroll
+      for (int d = 0; d < HD; ++d) S.vt[ops_off(d, j, kAK)] = vb[d];
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  };
+  auto wait_mma = [&]() {
+    if (!ok) return;
+    if (!mbar_wait(&S.bar, phase, abort_flag)) {
+      *abort_flag = 1;
+      if (a.err) atomicCAS(a.err, 0, kErrAttnWait);
+      ok = false;
+    }
+    phase ^= 1u;
+    tc_fence_after();
+  };
+  auto mma_scores = [&]() {
+    if (tid == 0 && ok && !*abort_flag) {
+      const uint64_t da = kmajor_desc_noswizzle(smem_u32(S.q), 128, (KD / 16) * 128);
+      const uint64_t db = kmajor_desc_noswizzle(smem_u32(S.k), 128, (KD / 16) * 128);
+      tc_mma_i8(tbase, da, db, idesc_s8_s32(kAQ, kAK), 0u);
+      tc_commit(&S.bar);
+    }
+    wait_mma();
+  };
+  auto mma_values = [&](bool first) {
+    if (tid == 0 && ok && !*abort_flag) {
+      const uint32_t idesc = idesc_s8_s32(kAQ, HD);
+      const uint64_t dh = kmajor_desc_noswizzle(smem_u32(S.ph), 128, (kAK / 16) * 128);
+      const uint64_t dl = kmajor_desc_noswizzle(smem_u32(S.pl), 128, (kAK / 16) * 128);
+      const uint64_t dv = kmajor_desc_noswizzle(smem_u32(S.vt), 128, (kAK / 16) * 128);
+#pragma unroll
+      for (int s = 0; s < kAK / 32; ++s) {
+        // 32 keys = two core matrices = 256 bytes = 16 descriptor units.
+        const uint64_t off = static_cast<uint64_t>(16 * s);
+        const uint32_t acc = (first && s == 0) ? 0u : 1u;
+        tc_mma_i8(tbase + 128, dh + off, dv + off, idesc, acc);
+        tc_mma_i8(tbase + 192, dl + off, dv + off, idesc, acc);
+      }
+      tc_commit(&S.bar);
+    }
+    wait_mma();
+  };
+
+  // Pass 1: row maximum of the integer scores.
+  int mx = INT_MIN;
+  for (int k0 = 0; k0 < N; k0 += kAK) {
+    stage(k0, false);
+    mma_scores();
+#pragma unroll
+    for (int cc = 0; cc < kAK; cc += 16) {
+      uint32_t r[16];
+      tc_ld_32x32b_x16(trow + cc, r);
+      tc_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (k0 + cc + e < N) mx = max(mx, static_cast<int>(r[e]));
+    }
+    tc_fence_before();
+  }
+  // Pass 2: weights, their sum, and the two value products.
+  int l = 0;
+  for (int k0 = 0; k0 < N; k0 += kAK) {
+    __syncthreads();  // the previous block's UMMAs have completed (waited)
+    stage(k0, true);
+    mma_scores();
+#pragma unroll
+    for (int cc = 0; cc < kAK; cc += 16) {
+      uint32_t r[16];
+      tc_ld_32x32b_x16(trow + cc, r);
+      tc_wait_ld();
+      uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        int p = 0;
+        if (k0 + cc + e < N) {
+          const long long t = rne64(static_cast<long long>(mx - static_cast<int>(r[e])) * a.mt, a.sht);
+          p = S.E[t > 255 ? 255 : t];
+        }
+        l += p;
+        hw[e >> 2] |= static_cast<uint32_t>(p >> 6) << (8 * (e & 3));
+        lw[e >> 2] |= static_cast<uint32_t>(p & 63) << (8 * (e & 3));
+      }
+      *reinterpret_cast<uint4*>(S.ph + ops_off(tid, cc, kAK)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(S.pl + ops_off(tid, cc, kAK)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    mma_values(k0 == 0);
+  }
+  __syncthreads();
+  const bool good = S.abort == 0;
+  const int qi = q0 + tid;
+  const bool valid = qi < N && good;
+  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
+  int8_t* op = a.out.p + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(qi) * a.out.cstride +
+               h * HD;
+  for (int d0 = 0; d0 < HD; d0 += 16) {
+    uint32_t oh[16], ol[16];
+    tc_ld_32x32b_x16(trow + 128 + d0, oh);
+    tc_ld_32x32b_x16(trow + 192 + d0, ol);
+    tc_wait_ld();
+    if (!valid) continue;
+    // Positional term: depthwise 3x3 of v (channels h*HD + d) around the query.
+    int acc[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = 0;
+    for (int tap = 0; tap < 9; ++tap) {
+      const int iy = y - 1 + tap / 3, ix = x - 1 + tap % 3;
+      if (iy < 0 || iy >= a.H || ix < 0 || ix >= a.W) continue;
+      const uint4 v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride +
+                                                      2 * KD + d0);
+      const int8_t* vb = reinterpret_cast<const int8_t*>(&v);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[e] += static_cast<int>(vb[e]) * static_cast<int>(S.pe[tap * HD + d0 + e]);
+    }
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int ch = h * HD + d0 + e;
+      const long long o = 64LL * static_cast<int32_t>(oh[e]) + static_cast<int32_t>(ol[e]);
+      const long long av = div_rne64(rne64(o * a.mo, a.sho), l);
+      const long long pe = rne64((static_cast<long long>(acc[e]) + a.pe_bq[ch]) * a.pe_mult[ch], a.pe_shift[ch]);
+      const long long v = av + pe;
+      const int c = static_cast<int>(v < -127 ? -127 : v > 127 ? 127 : v);
+      w[e >> 2] |= (static_cast<uint32_t>(c) & 0xFFu) << (8 * (e & 3));
+    }
+    *reinterpret_cast<uint4*>(op + d0) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  if (!good) __nanosleep(100000);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 256);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_attention_i8(const I8AttnArgs& a, cudaStream_t st) {
+  const int N = a.H * a.W;
+  if (a.kd != KD || a.hd != HD || N < 1 || N > 4000 || a.qkv.cstride % 16 || a.out.cstride % 16 || a.qkv.bstride % 16 ||
+      a.out.bstride % 16 || reinterpret_cast<uintptr_t>(a.qkv.p) % 16 || reinterpret_cast<uintptr_t>(a.out.p) % 16 ||
+      a.dim != a.heads * HD || a.sht < 1 || a.sho < 1)
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(attention_i8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(sizeof(AttnSmem)));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  dim3 grid((N + kAQ - 1) / kAQ, a.heads, a.B);
+  attention_i8_tc_kernel<<<grid, 128, sizeof(AttnSmem), st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace yb

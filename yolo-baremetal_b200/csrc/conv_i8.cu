@@ -50,21 +50,6 @@ constexpr int kMaxCo = 1024;
 
 namespace {
 
-// Instruction descriptor, kind::i8: signed 8-bit A and B, int32 D, K-major.
-__host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
-         (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
 // (p >> sh) rounded half to even, sh >= 1, without branches: with
 // p = q*2^sh + r (q = floor), adding 2^(sh-1) - 1 + (q & 1) carries into q

@@ -482,6 +482,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     aa.pe_bq = static_cast<const int32_t*>(db);
     aa.pe_mult = static_cast<const int32_t*>(dm);
     aa.pe_shift = static_cast<const int32_t*>(ds);
+    aa.err = d_err_;
     const double N = static_cast<double>(in.H) * in.W;
     add_op(kOpAttn, 2.0 * B * heads * N * N * (kd + hd), static_cast<double>(B) * N * (cq + dim),
            [aa](cudaStream_t st) { return launch_attention_i8(aa, st); });

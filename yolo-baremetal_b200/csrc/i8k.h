@@ -9,7 +9,9 @@
 //                 rne((max S - S) * mt, sht)); p = E[t]; l = sum p,
 //                 o = sum p v; out = div_rne(rne(o * mo, sho), l) + the
 //                 positional depthwise term rne((pe_bq + sum v*pe_w) *
-//                 pe_mult, pe_shift), clamped.
+//                 pe_mult, pe_shift), clamped.  q.k and p.v run on the
+//                 tensor cores (attn_i8.cu, kind::i8), p split as
+//                 64 * (p >> 6) + (p & 63) so both factors fit int8.
 #pragma once
 #include <cstdint>
 
@@ -34,6 +36,7 @@ struct I8AttnArgs {
   const int32_t* pe_bq = nullptr;    // [dim]
   const int32_t* pe_mult = nullptr;  // [dim]
   const int32_t* pe_shift = nullptr;
+  int* err = nullptr;  // kernel error word (bounded waits that gave up)
 };
 
 cudaError_t launch_quantize_input(const float* in, int B, int C, int H, int W, float s, I8View out, cudaStream_t st);

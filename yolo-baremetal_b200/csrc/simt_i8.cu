@@ -1,6 +1,5 @@
-// CUDA-core kernels of the INT8 forward: input quantisation, max pool,
-// depthwise 3x3, upsample + concat, and the PSA attention with an exact
-// integer softmax.  All activations are NHWC int8 views {ptr, cstride (per
+// CUDA-core kernels of the INT8 forward: input quantisation (alone or fused
+// into the first convolution), max pool, depthwise 3x3, upsample + concat.  All activations are NHWC int8 views {ptr, cstride (per
 // pixel), bstride (per image)}; every rule is the integer arithmetic declared
 // in i8k.h, which the CPU INT8 oracle restates.
 #include <climits>
@@ -13,16 +12,6 @@ namespace {
 
 __device__ __forceinline__ long long rne(long long p, int sh) {
   return (p + ((1LL << (sh - 1)) - 1) + ((p >> sh) & 1)) >> sh;
-}
-// a / l rounded half to even (l > 0), floor-based for negative a.
-__device__ __forceinline__ long long div_rne(long long a, long long l) {
-  long long q = a / l, r = a % l;
-  if (r < 0) {
-    q -= 1;
-    r += l;
-  }
-  if (2 * r > l || (2 * r == l && (q & 1))) q += 1;
-  return q;
 }
 __device__ __forceinline__ int clamp127(long long v) { return static_cast<int>(v < -127 ? -127 : v > 127 ? 127 : v); }
 
@@ -329,114 +318,6 @@ __global__ void concat_i8_kernel(I8View s0, int c0, int lg0, I8View s1, int c1, 
       *reinterpret_cast<const uint4*>(src);
 }
 
-// ----------------------------------------------------------- attention
-// One thread per query, one CTA per (query block, head, image).  kd = 32,
-// hd = 64.  Keys and values are staged per tile of kKB tokens.
-constexpr int kQB = 64, kKB = 64;
-__global__ void __launch_bounds__(kQB) attention_i8_kernel(const I8AttnArgs a) {
-  constexpr int KD = 32, HD = 64;
-  __shared__ __align__(16) int8_t sk[kKB][KD];
-  __shared__ __align__(16) int8_t sv[kKB][HD];
-  __shared__ int32_t sE[256];
-  for (int i = threadIdx.x; i < 256; i += kQB) sE[i] = a.E[i];
-  const int N = a.H * a.W;
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int qi = blockIdx.x * kQB + threadIdx.x;
-  const bool active = qi < N;
-  const int blk = 2 * KD + HD;
-  const int8_t* base = a.qkv.p + b * a.qkv.bstride + h * blk;
-  int q4[KD / 4];
-  if (active) {
-    const int8_t* qp = base + static_cast<long long>(qi) * a.qkv.cstride;
-#pragma unroll
-    for (int j = 0; j < KD / 16; ++j) {
-      const uint4 v = *reinterpret_cast<const uint4*>(qp + 16 * j);
-      q4[4 * j] = static_cast<int>(v.x);
-      q4[4 * j + 1] = static_cast<int>(v.y);
-      q4[4 * j + 2] = static_cast<int>(v.z);
-      q4[4 * j + 3] = static_cast<int>(v.w);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < KD / 4; ++j) q4[j] = 0;
-  }
-  auto load_tile = [&](int k0, bool with_v) {
-    for (int i = threadIdx.x; i < kKB * ((KD + HD) / 16); i += kQB) {
-      const int kk = i / ((KD + HD) / 16), part = i - kk * ((KD + HD) / 16);
-      if (!with_v && part >= KD / 16) continue;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (k0 + kk < N) v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(k0 + kk) * a.qkv.cstride +
-                                                          KD + 16 * part);
-      if (part < KD / 16) *reinterpret_cast<uint4*>(&sk[kk][16 * part]) = v;
-      else *reinterpret_cast<uint4*>(&sv[kk][16 * (part - KD / 16)]) = v;
-    }
-  };
-  auto score = [&](int kk) {
-    const int* kr = reinterpret_cast<const int*>(sk[kk]);
-    int s = 0;
-#pragma unroll
-    for (int j = 0; j < KD / 4; ++j) s = __dp4a(q4[j], kr[j], s);
-    return s;
-  };
-  // Pass 1: row maximum of the integer scores.
-  int mx = INT_MIN;
-  for (int k0 = 0; k0 < N; k0 += kKB) {
-    __syncthreads();
-    load_tile(k0, false);
-    __syncthreads();
-    const int kn = min(kKB, N - k0);
-    for (int kk = 0; kk < kn; ++kk) mx = max(mx, score(kk));
-  }
-  // Pass 2: table weights, their sum and the weighted sum of v (int32: at
-  // most N * 4096 * 127, N <= 4000).
-  int o[HD];
-#pragma unroll
-  for (int d = 0; d < HD; ++d) o[d] = 0;
-  int l = 0;
-  for (int k0 = 0; k0 < N; k0 += kKB) {
-    __syncthreads();
-    load_tile(k0, true);
-    __syncthreads();
-    const int kn = min(kKB, N - k0);
-    for (int kk = 0; kk < kn; ++kk) {
-      long long t = rne(static_cast<long long>(mx - score(kk)) * a.mt, a.sht);
-      const int pw = sE[t > 255 ? 255 : t];
-      l += pw;
-      const int8_t* vr = sv[kk];
-#pragma unroll
-      for (int d = 0; d < HD; ++d) o[d] += pw * static_cast<int>(vr[d]);
-    }
-  }
-  if (!active) return;
-  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
-  int8_t* op = a.out.p + b * a.out.bstride + static_cast<long long>(qi) * a.out.cstride + h * HD;
-#pragma unroll
-  for (int d0 = 0; d0 < HD; d0 += 16) {
-    uint4 ov;
-    int8_t* ob = reinterpret_cast<int8_t*>(&ov);
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int d = d0 + e, ch = h * HD + d;
-      const long long av = div_rne(rne(static_cast<long long>(o[d]) * a.mo, a.sho), l);
-      // Positional term: depthwise 3x3 of v (channel ch) around the query.
-      long long acc = a.pe_bq[ch];
-      for (int ky = 0; ky < 3; ++ky) {
-        const int iy = y - 1 + ky;
-        if (iy < 0 || iy >= a.H) continue;
-        for (int kx = 0; kx < 3; ++kx) {
-          const int ix = x - 1 + kx;
-          if (ix < 0 || ix >= a.W) continue;
-          acc += static_cast<int>(base[static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * KD + d]) *
-                 static_cast<int>(a.pe_w[(ky * 3 + kx) * a.dim + ch]);
-        }
-      }
-      const long long pe = rne(acc * a.pe_mult[ch], a.pe_shift[ch]);
-      ob[e] = static_cast<int8_t>(clamp127(av + pe));
-    }
-    *reinterpret_cast<uint4*>(op + d0) = ov;
-  }
-}
-
 // ---------------------------------------------------- NHWC -> NCHW dump
 __global__ void nhwc_to_nchw_i8_kernel(I8View in, int C, int H, int W, int8_t* out) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -475,14 +356,6 @@ cudaError_t launch_concat_i8(I8View s0, int c0, int lg0, I8View s1, int c1, int 
   if ((c0 | c1) % 16 || s0.cstride % 16 || (c1 && s1.cstride % 16) || out.cstride % 16) return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(B) * H * W * ((c0 + c1) / 16);
   concat_i8_kernel<<<blocks_for(total, 256), 256, 0, st>>>(s0, c0, lg0, s1, c1, B, H, W, out);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_attention_i8(const I8AttnArgs& a, cudaStream_t st) {
-  const int N = a.H * a.W;
-  if (a.kd != 32 || a.hd != 64 || N > 4000 || a.qkv.cstride % 16 || a.out.cstride % 16) return cudaErrorInvalidValue;
-  dim3 grid((N + kQB - 1) / kQB, a.heads, a.B);
-  attention_i8_kernel<<<grid, kQB, 0, st>>>(a);
   return cudaGetLastError();
 }
 
