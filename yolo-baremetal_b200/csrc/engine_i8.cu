@@ -305,7 +305,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     if (!w || w->dims[0] != C || w->dims[2] != 3 || C % 16) return fail("int8: depthwise " + P);
     float s_out = 0.f, s_pre = 0.f;
     if (!scale(P, &s_out) || !scale(P + ":pre", &s_pre)) return cudaErrorInvalidValue;
-    std::vector<int8_t> wt(static_cast<size_t>(9) * C);
+    std::vector<uint32_t> wt(static_cast<size_t>(3) * C, 0u);
     std::vector<int32_t> bq(C), mu(C), sh(C);
     for (int c = 0; c < C; ++c) {
       HostTensor wc;
@@ -320,7 +320,9 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
       const float sc = in.scale(c);
       QWeights q;
       if (!quantize(wc, b ? &bc : nullptr, &sc, s_pre, &q)) return fail("int8: depthwise ratio " + P);
-      for (int k = 0; k < 9; ++k) wt[static_cast<size_t>(k) * C + c] = q.wq[k];
+      // Taps 0-3, 4-7 and 8 packed into words (byte k = tap 4 * word + k).
+      for (int k = 0; k < 9; ++k)
+        wt[static_cast<size_t>(k / 4) * C + c] |= (static_cast<uint32_t>(q.wq[k]) & 0xFFu) << (8 * (k % 4));
       bq[c] = q.bq[0];
       mu[c] = q.mult[0];
       sh[c] = q.shift[0];
@@ -328,7 +330,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     int8_t lut[256];
     silu_lut(lut, s_pre, s_out);
     void *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr, *dl = nullptr;
-    YB_TRY(upload(wt.data(), wt.size(), &dw));
+    YB_TRY(upload(wt.data(), wt.size() * 4, &dw));
     YB_TRY(upload(bq.data(), bq.size() * 4, &db));
     YB_TRY(upload(mu.data(), mu.size() * 4, &dm));
     YB_TRY(upload(sh.data(), sh.size() * 4, &ds));
@@ -336,7 +338,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     const I8View iv = in.view(), ovw = out.view();
     const int h = in.H, wd = in.W;
     add_op(kOpDw, 18.0 * B * h * wd * C, 2.0 * B * h * wd * C, [=](cudaStream_t st) {
-      return launch_dw3x3_i8(iv, ovw, B, h, wd, C, static_cast<const int8_t*>(dw), static_cast<const int32_t*>(db),
+      return launch_dw3x3_i8(iv, ovw, B, h, wd, C, static_cast<const uint32_t*>(dw), static_cast<const int32_t*>(db),
                              static_cast<const int32_t*>(dm), static_cast<const int32_t*>(ds),
                              static_cast<const int8_t*>(dl), st);
     });

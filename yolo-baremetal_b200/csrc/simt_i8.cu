@@ -1,7 +1,8 @@
 // CUDA-core kernels of the INT8 forward: input quantisation (alone or fused
-// into the first convolution), max pool, depthwise 3x3, upsample + concat.  All activations are NHWC int8 views {ptr, cstride (per
-// pixel), bstride (per image)}; every rule is the integer arithmetic declared
-// in i8k.h, which the CPU INT8 oracle restates.
+// into the first convolution), max pool, depthwise 3x3, upsample + concat.
+// All activations are NHWC int8 views {ptr, cstride (per pixel), bstride (per
+// image)}; every rule is the integer arithmetic declared in i8k.h, which the
+// CPU INT8 oracle restates.
 #include <climits>
 #include <cstdint>
 
@@ -253,9 +254,36 @@ __global__ void maxpool_i8_kernel(I8View in, I8View out, int B, int H, int W, in
 
 // ------------------------------------------------------- depthwise 3x3
 // y = rne((bq + sum x*wq) * mult, shift), then the SiLU table (lut != null)
-// or clamp to [-127, 127].  w: [9][C] int8 tap-major.  16 channels / thread.
-__global__ void dw3x3_i8_kernel(I8View in, I8View out, int B, int H, int W, int C, const int8_t* w,
-                                const int32_t* bq, const int32_t* mult, const int32_t* shift, const int8_t* lut) {
+// or clamp to [-127, 127].  16 channels of one pixel per thread.  The taps
+// of one channel are gathered four at a time into one word (a 4 x 4 byte
+// transpose of four tap vectors) and summed with dp4a against the weights
+// packed the same way on the host: wp[0][c] = taps 0-3, wp[1][c] = taps 4-7,
+// wp[2][c] = tap 8 (low byte).  The sum fits int32 (|sum| <= 9 * 128 * 127);
+// the requantisation is sum * M + (bq * M + 2^(sh-1) - 1) >> sh, redone in
+// 64 bits for shifts below 32 or a possible tie (low word all ones).
+__device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t (&y)[4]) {
+  const uint32_t t0 = __byte_perm(a, b, 0x5140), t1 = __byte_perm(a, b, 0x7362);
+  const uint32_t t2 = __byte_perm(c, d, 0x5140), t3 = __byte_perm(c, d, 0x7362);
+  y[0] = __byte_perm(t0, t2, 0x5410);
+  y[1] = __byte_perm(t0, t2, 0x7632);
+  y[2] = __byte_perm(t1, t3, 0x5410);
+  y[3] = __byte_perm(t1, t3, 0x7632);
+}
+
+__global__ void __launch_bounds__(256) dw3x3_i8_kernel(I8View in, I8View out, int B, int H, int W, int C,
+                                                       const uint32_t* wp, const int32_t* bq, const int32_t* mult,
+                                                       const int32_t* shift, const int8_t* lut) {
+  extern __shared__ __align__(16) int4 dw_rec[];  // [C] {M, D lo, D hi, sh - 32}
+  int8_t* slut = reinterpret_cast<int8_t*>(dw_rec + C);
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const int m = mult[i], b0 = bq[i];
+    const int sh = m == 0 ? 32 : shift[i];
+    const long long d = static_cast<long long>(b0) * m + ((1LL << (sh - 1)) - 1);
+    dw_rec[i] = make_int4(m, static_cast<int>(static_cast<unsigned long long>(d) & 0xFFFFFFFFull),
+                          static_cast<int>(d >> 32), sh - 32);
+  }
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) slut[i] = lut ? lut[i] : 0;
+  __syncthreads();
   const int C16 = C >> 4;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * H * W * C16;
@@ -265,33 +293,55 @@ __global__ void dw3x3_i8_kernel(I8View in, I8View out, int B, int H, int W, int 
   const int b = static_cast<int>(pix / (static_cast<long long>(H) * W));
   const int p = static_cast<int>(pix - static_cast<long long>(b) * H * W);
   const int y = p / W, x = p - (p / W) * W;
-  long long acc[16];
+  const int8_t* ib = in.p + b * in.bstride + c;
+  uint4 v[9];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) acc[e] = bq[c + e];
-  for (int ky = 0; ky < 3; ++ky) {
-    const int iy = y - 1 + ky;
-    if (iy < 0 || iy >= H) continue;
-    for (int kx = 0; kx < 3; ++kx) {
-      const int ix = x - 1 + kx;
-      if (ix < 0 || ix >= W) continue;
-      const uint4 v = *reinterpret_cast<const uint4*>(in.p + b * in.bstride +
-                                                      static_cast<long long>(iy * W + ix) * in.cstride + c);
-      const uint4 wv = *reinterpret_cast<const uint4*>(w + (ky * 3 + kx) * C + c);
-      const int8_t* vb = reinterpret_cast<const int8_t*>(&v);
-      const int8_t* wb = reinterpret_cast<const int8_t*>(&wv);
+  for (int t = 0; t < 9; ++t) {
+    const int iy = y - 1 + t / 3, ix = x - 1 + t % 3;
+    v[t] = (iy >= 0 && iy < H && ix >= 0 && ix < W)
+               ? *reinterpret_cast<const uint4*>(ib + static_cast<long long>(iy * W + ix) * in.cstride)
+               : make_uint4(0u, 0u, 0u, 0u);
+  }
+  int sum[16];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) acc[e] += static_cast<int>(vb[e]) * static_cast<int>(wb[e]);
+  for (int g = 0; g < 4; ++g) {  // channels 4g .. 4g+3
+    const auto word = [&](int t) {
+      return g == 0 ? v[t].x : g == 1 ? v[t].y : g == 2 ? v[t].z : v[t].w;
+    };
+    uint32_t y0[4], y1[4];
+    transpose4(word(0), word(1), word(2), word(3), y0);
+    transpose4(word(4), word(5), word(6), word(7), y1);
+    const uint32_t w8 = word(8);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int ch = c + 4 * g + e;
+      int acc = __dp4a(static_cast<int>(y0[e]), static_cast<int>(__ldg(wp + ch)), 0);
+      acc = __dp4a(static_cast<int>(y1[e]), static_cast<int>(__ldg(wp + C + ch)), acc);
+      const int x8 = static_cast<int>(static_cast<int8_t>((w8 >> (8 * e)) & 0xFFu));
+      acc += x8 * static_cast<int>(static_cast<int8_t>(__ldg(wp + 2 * C + ch) & 0xFFu));
+      sum[4 * g + e] = acc;
     }
   }
-  uint4 o;
-  int8_t* ob = reinterpret_cast<int8_t*>(&o);
+  uint32_t ow[4];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    long long yv = rne(acc[e] * mult[c + e], shift[c + e]);
-    if (lut) yv = lut[(yv < -128 ? -128 : yv > 127 ? 127 : yv) + 128];
-    ob[e] = static_cast<int8_t>(clamp127(yv));
+  for (int g = 0; g < 4; ++g) {
+    int o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int ch = c + 4 * g + e;
+      const int4 q = dw_rec[ch];
+      const long long d = (static_cast<long long>(q.z) << 32) | static_cast<unsigned>(q.y);
+      const long long pr = static_cast<long long>(sum[4 * g + e]) * q.x + d;
+      long long yv;
+      if (q.w >= 0 && static_cast<unsigned>(pr) != 0xFFFFFFFFu) yv = static_cast<int>(pr >> 32) >> q.w;
+      else yv = rne((static_cast<long long>(sum[4 * g + e]) + bq[ch]) * q.x, q.w + 32);
+      if (lut) o[e] = slut[(yv < -128 ? -128 : yv > 127 ? 127 : yv) + 128];
+      else o[e] = clamp127(yv);
+    }
+    ow[g] = __byte_perm(__byte_perm(o[0], o[1], 0x0040), __byte_perm(o[2], o[3], 0x0040), 0x5410);
   }
-  *reinterpret_cast<uint4*>(out.p + b * out.bstride + static_cast<long long>(p) * out.cstride + c) = o;
+  *reinterpret_cast<uint4*>(out.p + b * out.bstride + static_cast<long long>(p) * out.cstride + c) =
+      make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }
 
 // ------------------------------------------------- upsample and concat
@@ -343,11 +393,13 @@ cudaError_t launch_maxpool_i8(I8View in, I8View out, int B, int H, int W, int C,
   return cudaGetLastError();
 }
 
-cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const int8_t* w, const int32_t* bq,
+cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const uint32_t* wp, const int32_t* bq,
                             const int32_t* mult, const int32_t* shift, const int8_t* lut, cudaStream_t st) {
-  if (C % 16 || in.cstride % 16 || out.cstride % 16) return cudaErrorInvalidValue;
+  if (C % 16 || in.cstride % 16 || out.cstride % 16 || C > 4096) return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(B) * H * W * (C / 16);
-  dw3x3_i8_kernel<<<blocks_for(total, 256), 256, 0, st>>>(in, out, B, H, W, C, w, bq, mult, shift, lut);
+  if (total == 0) return cudaSuccess;
+  const size_t smem = static_cast<size_t>(C) * 16 + 256;
+  dw3x3_i8_kernel<<<blocks_for(total, 256), 256, smem, st>>>(in, out, B, H, W, C, wp, bq, mult, shift, lut);
   return cudaGetLastError();
 }
 
