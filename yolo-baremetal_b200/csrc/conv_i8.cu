@@ -45,6 +45,14 @@ constexpr int kThreads = 32 * (kProdWarp + 1);
 constexpr int kSmemLimit = 232448;
 constexpr int kMaxAcc = 4;
 constexpr int kMaxCo = 1024;
+// Patch mode: one 16-channel plane of a tile's 18 x 10 input patch (16 bytes
+// per pixel, pixel-major), padded to a 128-byte multiple.
+constexpr int kPatchH = 18, kPatchW = 10;
+constexpr uint32_t kPatchBox = kPatchH * kPatchW * 16;  // 2880 bytes written by one box copy
+constexpr uint32_t kPatchChunk = 2944;
+__host__ __device__ constexpr uint32_t patch_stage_bytes_i8(int ci_pad) {
+  return ((static_cast<uint32_t>(ci_pad / 16) * kPatchChunk) + 1023u) & ~1023u;
+}
 
 }  // namespace
 
@@ -148,15 +156,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t chunk_bytes = static_cast<uint32_t>(a.n_tile) * 128u;
-  const uint32_t stage_bytes = kATile + chunk_bytes;
+  // Patch mode keeps every weight chunk resident in front of the stages.
+  const bool patch = a.patch != 0;
+  const int ci_pad = a.K / (a.kh * a.kw);
+  const uint32_t wres_bytes = patch ? static_cast<uint32_t>(a.num_kc) * chunk_bytes : 0u;
+  const uint32_t stage_bytes = patch ? patch_stage_bytes_i8(ci_pad) : kATile + chunk_bytes;
+  uint8_t* stage0 = smem + wres_bytes;
 
-  uint8_t* tail = smem + stages * stage_bytes;
+  uint8_t* tail = stage0 + stages * stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;
   uint64_t* acc_empty = acc_full + kMaxAcc;
   uint64_t* drain = acc_empty + kMaxAcc;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* wbar = drain + 1;  // resident weights landed (patch mode)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Per output channel sq = {multiplier M, low and high word of
   // D = bias * M + 2^(shift-1) - 1, shift - 32} and sb = bias; a zero
@@ -203,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       mbar_init(&acc_empty[i], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(wbar, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -220,7 +235,37 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
   const int HoWo = a.Ho * a.Wo;
   const int M = a.B * HoWo;
 
-  if (warp == kProdWarp) {
+  if (warp == kProdWarp && patch) {
+    // ------------------------------------------------------ patch producer
+    // One thread: the resident weights once, then per tile one box copy per
+    // 16-channel plane of its 18 x 10 input patch (zero outside the image
+    // and past the view's channels).
+    if (lane == 0) {
+      mbar_arrive_expect_tx(wbar, wres_bytes);
+      for (int kc = 0; kc < a.num_kc; ++kc)
+        bulk_g2s(smem + static_cast<size_t>(kc) * chunk_bytes, a.wpack + static_cast<size_t>(kc) * chunk_bytes,
+                 chunk_bytes, wbar);
+      const int ncb = ci_pad / 16;
+      const int per = a.tiles_y * a.tiles_x;
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
+        const uint32_t s = it % stages;
+        const uint32_t ph = (it / stages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+          raise_err(a.err, abort_flag, kErrWaitEmpty);
+          break;
+        }
+        const int b = t / per;
+        const int rem = t - b * per;
+        const int ty = rem / a.tiles_x;
+        const int tx = rem - ty * a.tiles_x;
+        uint8_t* stage = stage0 + s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ncb) * kPatchBox);
+        for (int cb = 0; cb < ncb; ++cb)
+          tma_tile_4d(stage + cb * kPatchChunk, &a.tm, 16 * cb, tx * 8 - 1, ty * 16 - 1, b, &full[s]);
+      }
+    }
+  } else if (warp == kProdWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const int taps = a.kh * a.kw;
@@ -249,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
           const int t0 = cpp == 128 ? kc / cblocks : kc * tps;
           const int c0 = cpp == 128 ? (kc - t0 * cblocks) * 128 : 0;
           const int ntap = cpp == 128 ? 1 : min(tps, taps - t0);
-          uint8_t* stage = smem + s * stage_bytes;
+          uint8_t* stage = stage0 + s * stage_bytes;
           mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ntap) * sub_bytes + chunk_bytes);
           bulk_g2s(stage + kATile, wsrc + static_cast<size_t>(kc) * chunk_bytes, chunk_bytes, &full[s]);
           for (int i = 0; i < ntap; ++i) {
@@ -282,6 +327,41 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * acc_stride;
         bool ok = true;
+        if (patch) {
+          // One stage per tile: 9 taps x ci_pad / 32 K steps, each A operand
+          // a shifted window of the patch (two 16-channel planes), each B step
+          // in the resident weights.
+          if (lt == 0 && !mbar_wait(wbar, 0, abort_flag)) {
+            raise_err(a.err, abort_flag, kErrWaitFull);
+            break;
+          }
+          const uint32_t s = it % stages;
+          const uint32_t ph = (it / stages) & 1u;
+          ++it;
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            raise_err(a.err, abort_flag, kErrWaitFull);
+            break;
+          }
+          tc_fence_after();
+          // Descriptors at the patch origin and at weight chunk 0; every
+          // step adds a start-address offset (16-byte units).
+          const uint64_t da0 = kmajor_desc_noswizzle(smem_u32(stage0 + s * stage_bytes), kPatchChunk, kPatchW * 16);
+          const uint64_t db0 = sw128_kmajor_desc(smem_u32(smem));
+          const uint64_t chunk_units = chunk_bytes >> 4;
+          int step = 0;
+          for (int tap = 0; tap < 9; ++tap) {
+            const uint64_t toff = static_cast<uint64_t>((tap / 3) * kPatchW + tap % 3);  // window shift
+            for (int c2 = 0; c2 < ci_pad / 32; ++c2, ++step) {
+              const int k = tap * ci_pad + 32 * c2;
+              const uint64_t aoff = toff + static_cast<uint64_t>(c2) * (2 * kPatchChunk / 16);
+              const uint64_t boff = static_cast<uint64_t>(k / kKB) * chunk_units + static_cast<uint64_t>(((k % kKB) / 32) * 2);
+              tc_mma_i8(d_tmem, da0 + aoff, db0 + boff, idesc, step != 0 ? 1u : 0u);
+            }
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&acc_full[acc]);
+          continue;
+        }
         for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
           const uint32_t s = it % stages;
           const uint32_t ph = (it / stages) & 1u;
@@ -291,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * stage_bytes);
+          const uint32_t sa = smem_u32(stage0 + s * stage_bytes);
           const uint64_t da0 = kmajor_desc(sa, layout, sbo);
           const uint64_t db0 = sw128_kmajor_desc(sa + kATile);
           const int nks = kc == a.num_kc - 1 ? ks_last : kKB / 32;
@@ -337,10 +417,24 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       const int nt = t - mt * a.n_tiles;
       const int n0 = nt * a.n_tile;
       const int nvalid = min(a.n_tile, a.Co - n0);
-      const int m = mt * kBM + q * 32 + lane;
-      const bool valid = m < M;
+      bool valid;
+      long long pm = 0;
+      if (patch) {
+        // Tile of 16 rows x 8 columns; TMEM lane r is pixel (r / 8, r % 8).
+        const int per = a.tiles_y * a.tiles_x;
+        const int tb = mt / per;
+        const int rem = mt - tb * per;
+        const int ty = rem / a.tiles_x;
+        const int r = q * 32 + lane;
+        const int oy = ty * 16 + (r >> 3), ox = (rem - ty * a.tiles_x) * 8 + (r & 7);
+        valid = oy < a.Ho && ox < a.Wo;
+        if (valid) pm = static_cast<long long>(tb) * HoWo + oy * a.Wo + ox;
+      } else {
+        const int m = mt * kBM + q * 32 + lane;
+        valid = m < M;
+        if (valid) pm = m;
+      }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_stride;
-      const long long pm = valid ? m : 0;
       const long long po = pm * a.out_cstride + a.out_coff + n0;
       // Units of 32 channels: two TMEM loads, requantise (or dequantise),
       // then lanes 2k and 2k+1 write the two 16-byte halves of one pixel's
@@ -466,6 +560,19 @@ PFN_cuTensorMapEncodeIm2col_v12000 i8_im2col_encoder() {
   return fn;
 }
 
+PFN_cuTensorMapEncodeTiled_v12000 i8_tiled_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
 inline uint32_t sw128_off(uint32_t row, uint32_t chunk16) {
   return (row >> 3) * 1024u + (row & 7u) * 128u + ((chunk16 ^ (row & 7u)) << 4);
 }
@@ -537,6 +644,41 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
       a.res_shift > 62 || x_cstride % 16 || x_bstride % 16 || reinterpret_cast<uintptr_t>(x) % 16) {
     if (why) *why = "int8 conv: unsupported view alignment or tile";
     return cudaErrorInvalidValue;
+  }
+  const int tail = 512 + 20 * a.n_tile * a.n_tiles + 1024 + 256;
+  const int ci_pad = a.K / (a.kh * a.kw);
+  // Patch mode: 3x3 stride 1 pad 1, one N tile, 32 or 64 padded input
+  // channels, enough room for three stages next to the resident weights.
+  a.patch = 0;
+  if (a.kh == 3 && a.kw == 3 && a.stride == 1 && a.pad == 1 && a.Ho == a.H && a.Wo == a.W && a.n_tiles == 1 &&
+      (ci_pad == 32 || ci_pad == 64) && a.K == 9 * ci_pad && a.n_tile <= 128) {
+    const int wres = a.num_kc * a.n_tile * 128;
+    const int pst = static_cast<int>(patch_stage_bytes_i8(ci_pad));
+    int st = (kSmemLimit - 1024 - wres - tail) / pst;
+    st = st > 8 ? 8 : st;
+    const auto tenc = i8_tiled_encoder();
+    if (st >= 3 && tenc) {
+      cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Ci), static_cast<cuuint64_t>(a.W),
+                            static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.B)};
+      cuuint64_t strides[3] = {static_cast<cuuint64_t>(x_cstride), static_cast<cuuint64_t>(x_cstride) * a.W,
+                               static_cast<cuuint64_t>(x_bstride)};
+      cuuint32_t box[4] = {16, kPatchW, kPatchH, 1};
+      cuuint32_t estr[4] = {1, 1, 1, 1};
+      const CUresult cr = tenc(&a.tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(x), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (cr == CUDA_SUCCESS) {
+        a.patch = 1;
+        a.tiles_y = (a.Ho + 15) / 16;
+        a.tiles_x = (a.Wo + 7) / 8;
+        a.m_tiles = a.B * a.tiles_y * a.tiles_x;
+        const int smem = 1024 + wres + st * pst + tail;
+        if (a.m_tiles <= 0) return cudaSuccess;
+        const int grid = a.m_tiles < sms ? a.m_tiles : sms;
+        conv_i8_kernel<<<grid, kThreads, smem, s>>>(a, st);
+        return cudaGetLastError();
+      }
+    }
   }
   const auto enc = i8_im2col_encoder();
   if (!enc) {

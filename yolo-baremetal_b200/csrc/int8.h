@@ -21,6 +21,10 @@ namespace yb {
 struct I8Args {
   int B = 0, H = 0, W = 0, Ci = 0, Co = 0, kh = 1, kw = 1, stride = 1, pad = 0, Ho = 0, Wo = 0;
   int K = 0, num_kc = 0, n_tile = 0, n_tiles = 0, m_tiles = 0, a_cpp = 0;
+  // Patch mode (set by launch_conv_i8 for 3x3 stride-1 convolutions of at
+  // most 64 input channels with one N tile): tiles of 16 x 8 output pixels,
+  // m_tiles = B * tiles_y * tiles_x.
+  int patch = 0, tiles_y = 0, tiles_x = 0;
   const uint8_t* wpack = nullptr;
   const int32_t* bias = nullptr;
   const int32_t* mult = nullptr;
