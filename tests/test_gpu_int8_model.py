@@ -152,3 +152,39 @@ def test_device_calibration(weights_n0, calib):
         assert dets_ok(compare_dets(got["dets"][0], ref["dets"]))
     finally:
         m.close()
+
+
+def test_int8_s_width(weights_s0):
+    """The s width (channels x2: 4-head and 2-head attention, 32/64-channel
+    patch-mode convolutions) under a device-calibrated table, bit-exact with
+    the oracle under the same table."""
+    import yb_weights as yw
+    import yolo_b200 as yb
+    from oracle import Oracle
+
+    m = yb.Model(weights_s0)
+    try:
+        scales = m.calibrate_int8(yw.make_batch(range(1100, 1103), 128, 128))
+        img = yw.make_input(8, 192, 256)
+        got = m.forward(img)
+        lg, _ = m.head(1)
+        ref = Oracle(weights_s0).forward_i8(img, scales, stages=True)
+        _check_image(m, ref, 0)
+        assert np.array_equal(lg[0], ref["logits"])
+        assert dets_ok(compare_dets(got["dets"][0], ref["dets"]))
+    finally:
+        m.close()
+
+
+def test_int8_1280(model_i8, calib):
+    """1280 x 1280: attention over 1600 tokens (13 key blocks), bit-exact."""
+    import yb_weights as yw
+
+    o, scales = calib
+    img = yw.make_input(9, 1280, 1280)
+    got = model_i8.forward(img)
+    lg, _ = model_i8.head(1)
+    ref = o.forward_i8(img, scales, stages=True)
+    _check_image(model_i8, ref, 0)
+    assert np.array_equal(lg[0], ref["logits"])
+    assert dets_ok(compare_dets(got["dets"][0], ref["dets"]))
