@@ -1,0 +1,293 @@
+// PSA attention of the FP32 forward (layers.c:310-405) on the tensor cores:
+// tcgen05.mma kind::f16 with bf16 operands and fp32 accumulation in tensor
+// memory, on the split activation format (value = hi + lo, kernels.h).
+//
+// One CTA of 128 threads per (128 queries, head, image); thread i owns query
+// row i (TMEM lane i).  Keys go in blocks of 128:
+//   pass 1  S = Q K^T as Qh Kh + Qh Kl + Ql Kh (6 UMMAs: 3 products x 2 K
+//           steps of 16) -> row maximum of S * kd^-0.5;
+//   pass 2  S again; p = exp(S * scale - max) (zero past the last key),
+//           l += p; p split into bf16 hi + lo, written as A operands;
+//           O += Ph Vh + Ph Vl + Pl Vh (3 products x 8 K steps, N 64).
+// Then out = O / l + the positional depthwise term of v (layers.c:373-395,
+// same summation order as the reference: bias, then taps ky, kx), split.
+// The omitted lo x lo products are below 2^-16 of each term, the precision of
+// the split format itself.  Tensor memory: S in columns [0, 128), O in
+// [128, 192).  Operands are K-major without swizzle (core matrices of 8 rows
+// x 16 bytes, 128 contiguous bytes each, row-group major).  One thread issues
+// the UMMAs; completion is one mbarrier every thread waits on with a bound
+// (a timeout sets the error word and ends the kernel after freeing TMEM).
+#include <cfloat>
+#include <cstdint>
+
+#include "kernels.h"
+#include "sm100.cuh"
+#include "split.cuh"
+
+namespace yb {
+namespace {
+
+constexpr int kTQ = 128;  // queries per CTA (UMMA M)
+constexpr int kTK = 128;  // keys per block
+constexpr int TKD = 32, THD = 64;
+constexpr int kErrAttnWaitF = 8;
+
+__device__ __forceinline__ uint32_t opo(int row, int kbyte, int kb) {
+  return static_cast<uint32_t>(((row >> 3) * (kb >> 4) + (kbyte >> 4)) * 128 + (row & 7) * 16 + (kbyte & 15));
+}
+
+struct AttnTcSmem {
+  uint8_t qh[kTQ * TKD * 2], ql[kTQ * TKD * 2];    // A of S: 128 x 32 bf16
+  uint8_t kh[kTK * TKD * 2], kl[kTK * TKD * 2];    // B of S: 128 keys x 32 bf16
+  uint8_t vh[THD * kTK * 2], vl[THD * kTK * 2];    // B of O: 64 channels x 128 keys bf16
+  uint8_t ph[kTQ * kTK * 2], pl[kTQ * kTK * 2];    // A of O: 128 queries x 128 keys bf16
+  uint64_t bar;
+  uint32_t tmem;
+  int abort;
+};
+
+__global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, int* err) {
+  extern __shared__ __align__(1024) uint8_t attn_tc_raw[];
+  AttnTcSmem& S = *reinterpret_cast<AttnTcSmem*>(attn_tc_raw);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int N = a.H * a.W;
+  const int q0 = blockIdx.x * kTQ, h = blockIdx.y, b = blockIdx.z;
+  const int blk = 2 * TKD + THD;
+  const uint16_t* base = a.qkv.hi + static_cast<long long>(b) * a.qkv.bstride + a.qkv.coff + h * blk;
+  const long long pl = a.qkv.plane;
+  // Q rows, hi and lo planes (zero past N): 4 16-byte chunks per row each.
+  for (int i = tid; i < kTQ * 4; i += 128) {
+    const int r = i >> 2, c = i & 3;
+    uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
+    if (q0 + r < N) {
+      const uint16_t* p = base + static_cast<long long>(q0 + r) * a.qkv.cstride + 8 * c;
+      vh = *reinterpret_cast<const uint4*>(p);
+      vl = *reinterpret_cast<const uint4*>(p + pl);
+    }
+    *reinterpret_cast<uint4*>(S.qh + opo(r, 16 * c, 2 * TKD)) = vh;
+    *reinterpret_cast<uint4*>(S.ql + opo(r, 16 * c, 2 * TKD)) = vl;
+  }
+  if (tid == 0) {
+    mbar_init(&S.bar, 1);
+    S.abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&S.tmem, 256);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = S.tmem;
+  const uint32_t trow = tbase + (static_cast<uint32_t>(warp * 32) << 16);
+  volatile int* abort_flag = &S.abort;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  auto sync_async = [&]() {
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  };
+  // Keys [k0, k0 + 128) into kh / kl (zero past N); with_v also V^T.
+  auto stage = [&](int k0, bool with_v) {
+    for (int i = tid; i < kTK * 4; i += 128) {
+      const int j = i >> 2, c = i & 3;
+      uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
+      if (k0 + j < N) {
+        const uint16_t* p = base + static_cast<long long>(k0 + j) * a.qkv.cstride + TKD + 8 * c;
+        vh = *reinterpret_cast<const uint4*>(p);
+        vl = *reinterpret_cast<const uint4*>(p + pl);
+      }
+      *reinterpret_cast<uint4*>(S.kh + opo(j, 16 * c, 2 * TKD)) = vh;
+      *reinterpret_cast<uint4*>(S.kl + opo(j, 16 * c, 2 * TKD)) = vl;
+    }
+    if (with_v) {
+      // Thread j transposes key j's 64 values into column j of V^T.
+      const int j = tid;
+      const bool in = k0 + j < N;
+      const uint16_t* p = base + static_cast<long long>(in ? k0 + j : 0) * a.qkv.cstride + 2 * TKD;
+#pragma unroll
+      for (int c = 0; c < THD / 8; ++c) {
+        uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
+        if (in) {
+          vh = *reinterpret_cast<const uint4*>(p + 8 * c);
+          vl = *reinterpret_cast<const uint4*>(p + 8 * c + pl);
+        }
+        const uint16_t* eh = reinterpret_cast<const uint16_t*>(&vh);
+        const uint16_t* el = reinterpret_cast<const uint16_t*>(&vl);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t o = opo(8 * c + e, 2 * j, 2 * kTK);
+          *reinterpret_cast<uint16_t*>(S.vh + o) = eh[e];
+          *reinterpret_cast<uint16_t*>(S.vl + o) = el[e];
+        }
+      }
+    }
+    sync_async();
+  };
+  auto wait_mma = [&]() {
+    if (!ok) return;
+    if (!mbar_wait(&S.bar, phase, abort_flag)) {
+      *abort_flag = 1;
+      if (err) atomicCAS(err, 0, kErrAttnWaitF);
+      ok = false;
+    }
+    phase ^= 1u;
+    tc_fence_after();
+  };
+  auto mma_scores = [&]() {
+    if (tid == 0 && ok && !*abort_flag) {
+      const uint32_t idesc = idesc_bf16_f32(kTQ, kTK);
+      const uint32_t sbo = (2 * TKD / 16) * 128;
+      const uint64_t qh = kmajor_desc_noswizzle(smem_u32(S.qh), 128, sbo);
+      const uint64_t ql = kmajor_desc_noswizzle(smem_u32(S.ql), 128, sbo);
+      const uint64_t kh = kmajor_desc_noswizzle(smem_u32(S.kh), 128, sbo);
+      const uint64_t kl = kmajor_desc_noswizzle(smem_u32(S.kl), 128, sbo);
+#pragma unroll
+      for (int s = 0; s < TKD / 16; ++s) {
+        const uint64_t off = static_cast<uint64_t>(16 * s);  // 16 bf16 = two core matrices = 256 bytes
+        tc_mma_bf16(tbase, qh + off, kh + off, idesc, s == 0 ? 0u : 1u);
+        tc_mma_bf16(tbase, qh + off, kl + off, idesc, 1u);
+        tc_mma_bf16(tbase, ql + off, kh + off, idesc, 1u);
+      }
+      tc_commit(&S.bar);
+    }
+    wait_mma();
+  };
+  auto mma_values = [&](bool first) {
+    if (tid == 0 && ok && !*abort_flag) {
+      const uint32_t idesc = idesc_bf16_f32(kTQ, THD);
+      const uint32_t sbo = (2 * kTK / 16) * 128;
+      const uint64_t ph = kmajor_desc_noswizzle(smem_u32(S.ph), 128, sbo);
+      const uint64_t plo = kmajor_desc_noswizzle(smem_u32(S.pl), 128, sbo);
+      const uint64_t vh = kmajor_desc_noswizzle(smem_u32(S.vh), 128, sbo);
+      const uint64_t vl = kmajor_desc_noswizzle(smem_u32(S.vl), 128, sbo);
+#pragma unroll
+      for (int s = 0; s < kTK / 16; ++s) {
+        const uint64_t off = static_cast<uint64_t>(16 * s);
+        tc_mma_bf16(tbase + 128, ph + off, vh + off, idesc, (first && s == 0) ? 0u : 1u);
+        tc_mma_bf16(tbase + 128, ph + off, vl + off, idesc, 1u);
+        tc_mma_bf16(tbase + 128, plo + off, vh + off, idesc, 1u);
+      }
+      tc_commit(&S.bar);
+    }
+    wait_mma();
+  };
+
+  // Pass 1: row maximum of the scaled scores.
+  float mx = -FLT_MAX;
+  for (int k0 = 0; k0 < N; k0 += kTK) {
+    stage(k0, false);
+    mma_scores();
+#pragma unroll
+    for (int cc = 0; cc < kTK; cc += 16) {
+      uint32_t r[16];
+      tc_ld_32x32b_x16(trow + cc, r);
+      tc_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (k0 + cc + e < N) mx = fmaxf(mx, __uint_as_float(r[e]) * a.scale);
+    }
+    tc_fence_before();
+  }
+  // Pass 2: weights, their sum, and O.
+  float l = 0.f;
+  for (int k0 = 0; k0 < N; k0 += kTK) {
+    __syncthreads();  // the previous block's UMMAs have completed (waited)
+    stage(k0, true);
+    mma_scores();
+#pragma unroll
+    for (int cc = 0; cc < kTK; cc += 16) {
+      uint32_t r[16];
+      tc_ld_32x32b_x16(trow + cc, r);
+      tc_wait_ld();
+      uint32_t hw[8], lw[8];
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) {
+        const float p0 = k0 + cc + e < N ? __expf(__uint_as_float(r[e]) * a.scale - mx) : 0.f;
+        const float p1 = k0 + cc + e + 1 < N ? __expf(__uint_as_float(r[e + 1]) * a.scale - mx) : 0.f;
+        l += p0;
+        l += p1;
+        split2(p0, p1, hw[e >> 1], lw[e >> 1]);
+      }
+      *reinterpret_cast<uint4*>(S.ph + opo(tid, 2 * cc, 2 * kTK)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(S.ph + opo(tid, 2 * cc + 16, 2 * kTK)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+      *reinterpret_cast<uint4*>(S.pl + opo(tid, 2 * cc, 2 * kTK)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      *reinterpret_cast<uint4*>(S.pl + opo(tid, 2 * cc + 16, 2 * kTK)) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+    }
+    sync_async();
+    mma_values(k0 == 0);
+  }
+  __syncthreads();
+  const bool good = S.abort == 0;
+  const int qi = q0 + tid;
+  const bool valid = qi < N && good;
+  const float inv = l > 1e-12f ? 1.0f / l : 1.0f;
+  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
+  uint16_t* op = a.out.hi + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(qi) * a.out.cstride +
+                 a.out.coff + h * THD;
+  for (int d0 = 0; d0 < THD; d0 += 16) {
+    uint32_t ov[16];
+    tc_ld_32x32b_x16(trow + 128 + d0, ov);
+    tc_wait_ld();
+    if (!valid) continue;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int dd = d0 + 8 * half;
+      const int ch = h * THD + dd;
+      float pe[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pe[e] = __ldg(a.pe_b + ch + e);
+      for (int ky = 0; ky < 3; ++ky) {
+        const int iy = y - 1 + ky;
+        if (iy < 0 || iy >= a.H) continue;
+        for (int kx = 0; kx < 3; ++kx) {
+          const int ix = x - 1 + kx;
+          if (ix < 0 || ix >= a.W) continue;
+          float v[8];
+          load8(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * TKD + dd, pl, v);
+          const float* w = a.pe_w + (ky * 3 + kx) * (a.heads * THD) + ch;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v[e], __ldg(w + e)));
+        }
+      }
+      float res[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) res[e] = __uint_as_float(ov[8 * half + e]) * inv + pe[e];
+      store8(op + dd, a.out.plane, res);
+    }
+  }
+  if (!good) __nanosleep(100000);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 256);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
+  const int N = a.H * a.W;
+  if (a.kd != TKD || a.hd != THD || N < 1 || a.qkv.cstride % 8 || a.out.cstride % 8 || a.qkv.coff % 8 ||
+      a.out.coff % 8 || a.qkv.bstride % 8 || a.out.bstride % 8 || a.qkv.plane % 8 || a.out.plane % 8 ||
+      reinterpret_cast<uintptr_t>(a.qkv.hi) % 16 || reinterpret_cast<uintptr_t>(a.out.hi) % 16)
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(sizeof(AttnTcSmem)));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  dim3 grid((N + kTQ - 1) / kTQ, a.heads, a.B);
+  attention_tc_kernel<<<grid, 128, sizeof(AttnTcSmem), s>>>(a, a.err);
+  return cudaGetLastError();
+}
+
+}  // namespace yb

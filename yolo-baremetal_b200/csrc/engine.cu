@@ -561,6 +561,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     aa.pe_w = pe->w;
     aa.pe_b = pe->bias;
     aa.out = ov(ao);
+    aa.err = d_err_;
     if (p->calib) {
       // Attention output plus positional term: the INT8 plan's "<psa>.attn.ope".
       unsigned* st = stat_slot(pre + ".attn.ope", std::string());

@@ -188,7 +188,9 @@ struct AttnArgs {
   const float* pe_w = nullptr;
   const float* pe_b = nullptr;
   SOut out;
+  int* err = nullptr;  // kernel error word (bounded waits that gave up)
 };
+// tcgen05 kernel (attn_tc.cu): kd = 32, hd = 64.
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 
 // Detect decode (detect.c:21-61, :407-418): from box distances dist

@@ -1,6 +1,6 @@
 // CUDA-core kernels of the YOLO26 path: the ops that are not contractions
 // (depthwise, pooling, decode, layout) or too small to tile (the 3-channel stem
-// convolution), plus the PSA attention.  All are HBM- or latency-bound; they
+// convolution).  All are HBM- or latency-bound; they
 // read and write split NHWC views (kernels.h) 8 channels (two 16-byte
 // accesses) at a time.  Summation orders follow the reference loops so that
 // results stay within a few ulps of it.
@@ -280,111 +280,6 @@ __global__ void maxpool_kernel(const PoolArgs a) {
   store8(a.out.hi + vaddr(a.out, b, p) + c, a.out.plane, m);
 }
 
-// ----------------------------------------------------------------- attention
-// One thread per query token, QB queries per CTA, keys streamed through shared
-// memory in tiles of KB.  Two passes over the keys: the row maximum, then
-// exp(s - max) weights with their sum and the weighted sum of v, mirroring the
-// reference's materialised softmax (layers.c:292-308, :352-371) without the
-// N x N matrix.  The epilogue adds the depthwise 3x3 positional conv of v
-// (layers.c:373-395) and writes head h's hd channels.
-template <int KD, int HD, int QB, int KB>
-__global__ void __launch_bounds__(QB) attention_kernel(const AttnArgs a) {
-  __shared__ float sk[KB][KD];
-  __shared__ float sv[KB][HD];
-  const int N = a.H * a.W;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int qi = blockIdx.x * QB + threadIdx.x;
-  const bool active = qi < N;
-  const int blk = 2 * KD + HD;
-  const uint16_t* base = a.qkv.hi + vaddr(a.qkv, b, 0) + h * blk;
-  const long long pl = a.qkv.plane;
-  float q[KD];
-  if (active) {
-    const uint16_t* qp = base + static_cast<long long>(qi) * a.qkv.cstride;
-#pragma unroll
-    for (int d = 0; d < KD; d += 8) {
-      float v[8];
-      load8(qp + d, pl, v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) q[d + e] = v[e];
-    }
-  } else {
-#pragma unroll
-    for (int d = 0; d < KD; ++d) q[d] = 0.f;
-  }
-  // One pass with a running maximum (layers.c:292-308 restated online): for
-  // each key, s = q.k * scale; when s exceeds the running maximum m the
-  // accumulated weights are rescaled by exp(m_old - m_new); then p = exp(s - m)
-  // is added to the sum and p * v to the output.
-#pragma unroll
-  for (int d = 0; d < KD; ++d) q[d] *= a.scale;
-  float o[HD];
-#pragma unroll
-  for (int d = 0; d < HD; ++d) o[d] = 0.f;
-  float mx = -FLT_MAX, sum = 0.f;
-  for (int k0 = 0; k0 < N; k0 += KB) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < KB * ((KD + HD) / 8); i += QB) {
-      const int kk = i / ((KD + HD) / 8), d8 = (i - kk * ((KD + HD) / 8)) * 8;
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (k0 + kk < N) load8(base + static_cast<long long>(k0 + kk) * a.qkv.cstride + KD + d8, pl, v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (d8 < KD) sk[kk][d8 + e] = v[e];
-        else sv[kk][d8 - KD + e] = v[e];
-      }
-    }
-    __syncthreads();
-    const int kn = min(KB, N - k0);
-    for (int kk = 0; kk < kn; ++kk) {
-      float sc = 0.f;
-#pragma unroll
-      for (int d = 0; d < KD; ++d) sc = fmaf(q[d], sk[kk][d], sc);
-      if (sc > mx) {
-        const float c = __expf(mx - sc);
-        sum *= c;
-#pragma unroll
-        for (int d = 0; d < HD; ++d) o[d] *= c;
-        mx = sc;
-      }
-      const float e = __expf(sc - mx);
-      sum += e;
-#pragma unroll
-      for (int d = 0; d < HD; ++d) o[d] = fmaf(e, sv[kk][d], o[d]);
-    }
-  }
-  if (!active) return;
-  const float inv = sum > 1e-12f ? 1.0f / sum : 1.0f;
-  // Positional term: depthwise 3x3 of v around the query pixel, + pe bias.
-  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
-  uint16_t* op = a.out.hi + vaddr(a.out, b, qi) + h * HD;
-#pragma unroll
-  for (int d0 = 0; d0 < HD; d0 += 8) {
-    const int ch = h * HD + d0;
-    float pe[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) pe[e] = __ldg(a.pe_b + ch + e);
-    for (int ky = 0; ky < 3; ++ky) {
-      const int iy = y - 1 + ky;
-      if (iy < 0 || iy >= a.H) continue;
-      for (int kx = 0; kx < 3; ++kx) {
-        const int ix = x - 1 + kx;
-        if (ix < 0 || ix >= a.W) continue;
-        float v[8];
-        load8(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * KD + d0, pl, v);
-        const float* w = a.pe_w + (ky * 3 + kx) * (a.heads * HD) + ch;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v[e], __ldg(w + e)));
-      }
-    }
-    float r[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) r[e] = o[d0 + e] * inv + pe[e];
-    store8(op + d0, a.out.plane, r);
-  }
-}
-
 // -------------------------------------------------------------------- decode
 __global__ void decode_kernel(const DecodeArgs a) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -547,15 +442,6 @@ cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {
   if (b.stride < 1) return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(b.B) * b.Ho * b.Wo * (b.C / 8);
   maxpool_kernel<<<blocks_for(total, 256), 256, 0, s>>>(b);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
-  if (a.kd != 32 || a.hd != 64) return cudaErrorInvalidValue;
-  constexpr int QB = 64, KB = 64;
-  const int N = a.H * a.W;
-  dim3 grid((N + QB - 1) / QB, a.heads, a.B);
-  attention_kernel<32, 64, QB, KB><<<grid, QB, 0, s>>>(a);
   return cudaGetLastError();
 }
 
