@@ -99,10 +99,11 @@ status_t yb_cuda_load_bin(void* ctx, const char* path);
  * step_ms (nullable, MODEL_FORWARD_PROFILE_STEPS doubles) receives per-step
  * device times.  Either one makes the forward run eagerly instead of from the
  * captured graph.  Without them, a batch of B >= 32 images with B a multiple
- * of 16 is pipelined: 16-image sub-batches alternate between two captured
- * graphs so that each sub-batch's input copy overlaps the previous one's
- * compute (use pinned host buffers for the overlap to happen); the head
- * tensors of such a forward are not kept (yb_cuda_get_head). */
+ * of 16 is pipelined: 16-image sub-batches rotate over three captured
+ * graphs, each on its own stream, so that the input copies run back to back
+ * and each sub-batch's graph overlaps the copies and graphs after it (use
+ * pinned host buffers for the overlap to happen); the head tensors of such a
+ * forward are not kept (yb_cuda_get_head). */
 status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int H, int W,
                          float* out_dets, int max_det,
                          yb_stage_cb dump, void* user, double* step_ms);

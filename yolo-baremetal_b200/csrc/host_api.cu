@@ -64,6 +64,8 @@ DevScope* current_scope() {
 }
 
 // One device replica behind a void* context.
+constexpr int kPipeSlotsMax = 4;  // stream / event arrays of a context
+
 struct Ctx {
   std::unique_ptr<Engine> eng;
   Plan* last = nullptr;
@@ -77,14 +79,18 @@ struct Ctx {
   // Pipelined host forwards: input copies run on copy_stream while the
   // previous sub-batch computes; one event pair per plan slot.
   cudaStream_t copy_stream = nullptr;
-  cudaEvent_t in_ready[2] = {nullptr, nullptr};
-  cudaEvent_t slot_free[2] = {nullptr, nullptr};
+  cudaStream_t slot_stream[kPipeSlotsMax] = {};
+  cudaEvent_t in_ready[kPipeSlotsMax] = {};
+  cudaEvent_t slot_free[kPipeSlotsMax] = {};
   // Scale table of the last yb_cuda_calibrate_int8, in name order.
   std::vector<std::pair<std::string, float>> calib;
 };
 
-// Sub-batch of a pipelined host forward (yb_cuda_forward with B >= 2 chunks).
+// Sub-batch of a pipelined host forward (yb_cuda_forward with B >= 2 chunks)
+// and the number of plan slots (each with its own stream) it rotates over.
 constexpr int kPipeChunk = 16;
+constexpr int kPipeSlots = 3;
+static_assert(kPipeSlots <= kPipeSlotsMax, "pipeline slots");
 
 namespace {
 
@@ -311,9 +317,10 @@ extern "C" status_t yb_cuda_init(int device, void** ctx) {
     return cuda_status(e, "cudaEventCreate");
   if ((e = cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking)) != cudaSuccess)
     return cuda_status(e, "cudaStreamCreate");
-  for (int i = 0; i < 2; ++i)
+  for (int i = 0; i < kPipeSlots; ++i)
     if ((e = cudaEventCreateWithFlags(&c->in_ready[i], cudaEventDisableTiming)) != cudaSuccess ||
-        (e = cudaEventCreateWithFlags(&c->slot_free[i], cudaEventDisableTiming)) != cudaSuccess)
+        (e = cudaEventCreateWithFlags(&c->slot_free[i], cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&c->slot_stream[i], cudaStreamNonBlocking)) != cudaSuccess)
       return cuda_status(e, "cudaEventCreate");
   *ctx = c.release();
   return SUCCESS;
@@ -328,9 +335,13 @@ extern "C" status_t yb_cuda_destroy(void* ctx) {
     if (ev) cudaEventDestroy(ev);
   if (c->done) cudaEventDestroy(c->done);
   if (c->h2d_done) cudaEventDestroy(c->h2d_done);
-  for (int i = 0; i < 2; ++i) {
+  for (int i = 0; i < kPipeSlots; ++i) {
     if (c->in_ready[i]) cudaEventDestroy(c->in_ready[i]);
     if (c->slot_free[i]) cudaEventDestroy(c->slot_free[i]);
+    if (c->slot_stream[i]) {
+      cudaStreamSynchronize(c->slot_stream[i]);
+      cudaStreamDestroy(c->slot_stream[i]);
+    }
   }
   if (c->copy_stream) {
     cudaStreamSynchronize(c->copy_stream);
@@ -470,42 +481,47 @@ extern "C" status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int 
   Plan* p = nullptr;
   cudaStream_t s = c->eng->stream();
   if (!dump && !step_ms && B >= 2 * kPipeChunk && B % kPipeChunk == 0) {
-    // Pipelined: sub-batches of kPipeChunk images alternate between two plans.
-    // Chunk i's input copy (copy stream) overlaps chunk i-1's graph (compute
-    // stream); a slot's input is refilled only after its previous graph ran.
-    Plan* slots[2] = {nullptr, nullptr};
-    for (int k = 0; k < 2; ++k)
+    // Pipelined: sub-batches of kPipeChunk images rotate over kPipeSlots
+    // plans, each with its own stream.  The input copies run back to back on
+    // the copy stream; chunk i's graph starts when its copy lands and may
+    // overlap the graphs of the chunks before it (small sub-batches leave
+    // SMs idle in their late layers).  A slot's input is refilled only after
+    // its previous graph and result copy ran.
+    Plan* slots[kPipeSlots] = {};
+    for (int k = 0; k < kPipeSlots; ++k)
       if ((st = plan_for(c, kPipeChunk, H, W, max_det, &slots[k], 1 + k)) != SUCCESS) return st;
     const size_t in_elems = static_cast<size_t>(kPipeChunk) * 3 * H * W;
     const size_t det_elems = static_cast<size_t>(kPipeChunk) * max_det * 6;
     const int n = B / kPipeChunk;
-    // Input copy of chunk j into its slot, after the slot's previous graph.
     auto prefetch = [&](int j) {
-      const int k = j & 1;
-      cudaError_t r = j >= 2 ? cudaStreamWaitEvent(c->copy_stream, c->slot_free[k], 0) : cudaSuccess;
+      const int k = j % kPipeSlots;
+      cudaError_t r = j >= kPipeSlots ? cudaStreamWaitEvent(c->copy_stream, c->slot_free[k], 0) : cudaSuccess;
       if (r == cudaSuccess)
         r = cudaMemcpyAsync(slots[k]->d_in, in_nchw + j * in_elems, in_elems * 4, cudaMemcpyHostToDevice,
                             c->copy_stream);
       if (r == cudaSuccess) r = cudaEventRecord(c->in_ready[k], c->copy_stream);
       return r;
     };
-    cudaError_t e = prefetch(0);
+    cudaError_t e = cudaSuccess;
+    for (int j = 0; j < n && j < kPipeSlots && e == cudaSuccess; ++j) e = prefetch(j);
     for (int i = 0; i < n && e == cudaSuccess; ++i) {
-      const int k = i & 1;
+      const int k = i % kPipeSlots;
+      cudaStream_t ss = c->slot_stream[k];
       Plan* q = slots[k];
-      e = cudaStreamWaitEvent(s, c->in_ready[k], 0);
-      if (e == cudaSuccess) e = c->eng->run(q, s, nullptr);
-      // The next input copy is enqueued before this chunk's result copy, which
-      // blocks the host when out_dets is pageable.
-      if (e == cudaSuccess && i + 1 < n) e = prefetch(i + 1);
+      e = cudaStreamWaitEvent(ss, c->in_ready[k], 0);
+      if (e == cudaSuccess) e = c->eng->run(q, ss, nullptr);
       if (e == cudaSuccess)
-        e = cudaMemcpyAsync(out_dets + i * det_elems, q->d_out, det_elems * 4, cudaMemcpyDeviceToHost, s);
-      if (e == cudaSuccess) e = cudaEventRecord(c->slot_free[k], s);
+        e = cudaMemcpyAsync(out_dets + i * det_elems, q->d_out, det_elems * 4, cudaMemcpyDeviceToHost, ss);
+      if (e == cudaSuccess) e = cudaEventRecord(c->slot_free[k], ss);
+      if (e == cudaSuccess && i + kPipeSlots < n) e = prefetch(i + kPipeSlots);
     }
     // Head tensors of a pipelined forward are spread over both slots and
     // partly overwritten; yb_cuda_get_head reports that none are kept.
     c->last = nullptr;
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    for (int k = 0; k < kPipeSlots; ++k) {
+      const cudaError_t e2 = cudaStreamSynchronize(c->slot_stream[k]);
+      if (e == cudaSuccess) e = e2;
+    }
     const cudaError_t e2 = cudaStreamSynchronize(c->copy_stream);
     if (e == cudaSuccess) e = e2;
     if (e != cudaSuccess) return cuda_status(e, "pipelined forward");
