@@ -281,10 +281,37 @@ __global__ void maxpool_kernel(const PoolArgs a) {
 }
 
 // -------------------------------------------------------------------- decode
+// Four threads per anchor: the anchor's nc logits are read as float4 by the
+// four lanes in turn (a warp covers 8 consecutive anchors, 2.5 KB of
+// contiguous logits for nc = 80), reduced to the maximum logit with two
+// shuffles.  The maximum score is sigmoid(max logit): the reference takes the
+// maximum of the per-class sigmoids, which sigmoid's monotonicity makes the
+// same value up to the rounding of expf.  It only orders the anchors for the
+// top-k, which recomputes the chosen scores per class.  Lane 0 of the four
+// decodes the box.
 __global__ void decode_kernel(const DecodeArgs a) {
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long idx = t >> 2;
+  const int sub = static_cast<int>(t & 3);
   const long long total = static_cast<long long>(a.B) * a.N;
-  if (idx >= total) return;
+  const bool ok = idx < total;
+  float m = -FLT_MAX;
+  if (ok) {
+    const float* lg = a.logits + idx * a.nc;
+    if ((a.nc & 3) == 0) {
+      const int n4 = a.nc >> 2;
+      for (int c4 = sub; c4 < n4; c4 += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(lg) + c4);
+        m = fmaxf(fmaxf(m, v.x), fmaxf(v.y, fmaxf(v.z, v.w)));
+      }
+    } else {
+      for (int c = sub; c < a.nc; c += 4) m = fmaxf(m, __ldg(lg + c));
+    }
+  }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  if (!ok || sub != 0) return;
+  a.maxscore[idx] = sigmoid(m);
   const int j = static_cast<int>(idx % a.N);
   int s = 0;
   while (s + 1 < a.nscales && j >= a.base[s + 1]) ++s;
@@ -300,13 +327,6 @@ __global__ void decode_kernel(const DecodeArgs a) {
   bx.z = __fmul_rn(__fadd_rn(ax, d.z), st);
   bx.w = __fmul_rn(__fadd_rn(ay, d.w), st);
   *reinterpret_cast<float4*>(a.boxes + idx * 4) = bx;
-  const float* lg = a.logits + idx * a.nc;
-  float m = -FLT_MAX;
-  for (int c = 0; c < a.nc; ++c) {
-    const float v = sigmoid(__ldg(lg + c));
-    if (v > m) m = v;
-  }
-  a.maxscore[idx] = m;
 }
 
 // -------------------------------------------------------------------- layout
@@ -446,7 +466,8 @@ cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
-  const long long total = static_cast<long long>(a.B) * a.N;
+  const long long total = static_cast<long long>(a.B) * a.N * 4;
+  if (total == 0) return cudaSuccess;
   decode_kernel<<<blocks_for(total, 256), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
