@@ -19,6 +19,7 @@
 #include <climits>
 #include <cstdint>
 
+#include "pdl.cuh"
 #include "i8k.h"
 #include "sm100.cuh"
 
@@ -73,6 +74,7 @@ __global__ void __launch_bounds__(128, 1) attention_i8_tc_kernel(const I8AttnArg
   const int8_t* base = a.qkv.p + static_cast<long long>(b) * a.qkv.bstride + h * blk;
   for (int i = tid; i < 256; i += 128) S.E[i] = a.E[i];
   for (int i = tid; i < 9 * HD; i += 128) S.pe[i] = a.pe_w[(i / HD) * a.dim + h * HD + i % HD];
+  pdl_wait();
   // Q rows (zero past N), two 16-byte chunks per row.
   for (int i = tid; i < kAQ * 2; i += 128) {
     const int r = i >> 1, c = i & 1;
@@ -277,8 +279,7 @@ cudaError_t launch_attention_i8(const I8AttnArgs& a, cudaStream_t st) {
     attr = true;
   }
   dim3 grid((N + kAQ - 1) / kAQ, a.heads, a.B);
-  attention_i8_tc_kernel<<<grid, 128, sizeof(AttnSmem), st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(attention_i8_tc_kernel, grid, dim3(128), sizeof(AttnSmem), st, a);
 }
 
 }  // namespace yb

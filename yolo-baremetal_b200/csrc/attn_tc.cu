@@ -20,6 +20,7 @@
 #include <cfloat>
 #include <cstdint>
 
+#include "pdl.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
 #include "split.cuh"
@@ -55,6 +56,7 @@ __global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, 
   const int blk = 2 * TKD + THD;
   const uint16_t* base = a.qkv.hi + static_cast<long long>(b) * a.qkv.bstride + a.qkv.coff + h * blk;
   const long long pl = a.qkv.plane;
+  pdl_wait();
   // Q rows, hi and lo planes (zero past N): 4 16-byte chunks per row each.
   for (int i = tid; i < kTQ * 4; i += 128) {
     const int r = i >> 2, c = i & 3;
@@ -286,8 +288,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
     attr = true;
   }
   dim3 grid((N + kTQ - 1) / kTQ, a.heads, a.B);
-  attention_tc_kernel<<<grid, 128, sizeof(AttnTcSmem), s>>>(a, a.err);
-  return cudaGetLastError();
+  return launch_pdl(attention_tc_kernel, grid, dim3(128), sizeof(AttnTcSmem), s, a, a.err);
 }
 
 }  // namespace yb

@@ -27,6 +27,7 @@
 #include <string>
 #include <vector>
 
+#include "pdl.cuh"
 #include "runtime.h"
 #include "sm100.cuh"
 #include "status.h"
@@ -229,6 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
   const bool fast = __syncthreads_and(fast_ok) != 0;
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();
 
   const int total_tiles = a.m_tiles * a.n_tiles;
   const int ks_last = (a.K - (a.num_kc - 1) * kKB + 31) / 32;
@@ -675,8 +678,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
         const int smem = 1024 + wres + st * pst + tail;
         if (a.m_tiles <= 0) return cudaSuccess;
         const int grid = a.m_tiles < sms ? a.m_tiles : sms;
-        conv_i8_kernel<<<grid, kThreads, smem, s>>>(a, st);
-        return cudaGetLastError();
+        return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, st);
       }
     }
   }
@@ -710,8 +712,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
   const int grid = total < sms ? total : sms;
-  conv_i8_kernel<<<grid, kThreads, smem, s>>>(a, stages);
-  return cudaGetLastError();
+  return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, stages);
 }
 
 namespace {

@@ -39,6 +39,7 @@
 #include <cstring>
 #include <mutex>
 #include <vector>
+#include "pdl.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
 #include "split.cuh"
@@ -146,6 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();
 
   const int total_tiles = a.m_tiles * a.n_tiles;
   // The last K chunk holds K - 64 (num_kc - 1) real values: only its first
@@ -844,8 +847,7 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
   const int grid = total < num_sms ? total : num_sms;
-  conv_tc_kernel<<<grid, kThreads, smem, s>>>(a, stages);
-  return cudaGetLastError();
+  return launch_pdl(conv_tc_kernel, dim3(grid), dim3(kThreads), smem, s, a, stages);
 }
 
 }  // namespace yb

@@ -5,6 +5,7 @@
 // accesses) at a time.  Summation orders follow the reference loops so that
 // results stay within a few ulps of it.
 #include <cfloat>
+#include "pdl.cuh"
 #include "kernels.h"
 #include "split.cuh"
 
@@ -105,6 +106,7 @@ __global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
   const int taps = a.Ci * 9;
   for (int i = tid; i < CO * taps; i += 128) sw[(i % taps) * CO + i / taps] = a.w[i];
   for (int i = tid; i < CO; i += 128) sb[i] = a.bias ? a.bias[i] : 0.f;
+  pdl_wait();
   const int tiles_x = (a.Wo + T::TW - 1) / T::TW, tiles_y = (a.Ho + T::TH - 1) / T::TH;
   const int total = a.B * tiles_x * tiles_y;
   const int r = tid >> 4, x0 = tid & 15;
@@ -178,6 +180,7 @@ __global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
 // ------------------------------------------------------------- depthwise 3x3
 // w is [9][C] (tap-major, transposed on the host); 8 channels per thread.
 __global__ void dw3x3_kernel(const DwArgs a) {
+  pdl_wait();
   const int C8 = a.C >> 3;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(a.B) * a.H * a.W * C8;
@@ -226,6 +229,7 @@ __global__ void dw3x3_kernel(const DwArgs a) {
 
 // ------------------------------------------------------------- calibration
 __global__ void absmax_split_kernel(SView v, int B, int H, int W, int C, unsigned* amax) {
+  pdl_wait();
   const long long total = static_cast<long long>(B) * H * W * C;
   float m = 0.0f;
   for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
@@ -241,6 +245,7 @@ __global__ void absmax_split_kernel(SView v, int B, int H, int W, int C, unsigne
 }
 
 __global__ void absmax_f32_kernel(const float* x, long long n, unsigned* amax) {
+  pdl_wait();
   float m = 0.0f;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x)
@@ -250,6 +255,7 @@ __global__ void absmax_f32_kernel(const float* x, long long n, unsigned* amax) {
 
 // ------------------------------------------------------------------ max pool
 __global__ void maxpool_kernel(const PoolArgs a) {
+  pdl_wait();
   const int C8 = a.C >> 3;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(a.B) * a.Ho * a.Wo * C8;
@@ -290,6 +296,7 @@ __global__ void maxpool_kernel(const PoolArgs a) {
 // top-k, which recomputes the chosen scores per class.  Lane 0 of the four
 // decodes the box.
 __global__ void decode_kernel(const DecodeArgs a) {
+  pdl_wait();
   const long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long idx = t >> 2;
   const int sub = static_cast<int>(t & 3);
@@ -331,6 +338,7 @@ __global__ void decode_kernel(const DecodeArgs a) {
 
 // -------------------------------------------------------------------- layout
 __global__ void nchw_to_split_kernel(const float* in, int B, int C, int H, int W, SOut out) {
+  pdl_wait();
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * C * H * W;
   if (idx >= total) return;
@@ -347,6 +355,7 @@ __global__ void nchw_to_split_kernel(const float* in, int B, int C, int H, int W
 }
 
 __global__ void split_to_nchw_kernel(SView in, int B, int C, int H, int W, float* out) {
+  pdl_wait();
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * C * H * W;
   if (idx >= total) return;
@@ -360,6 +369,7 @@ __global__ void split_to_nchw_kernel(SView in, int B, int C, int H, int W, float
 }
 
 __global__ void gather_concat_kernel(SView s0, int c0, int up0, SView s1, int c1, int B, int H, int W, SOut out) {
+  pdl_wait();
   const int C = c0 + c1;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * H * W * C;
@@ -388,6 +398,7 @@ __global__ void gather_concat_kernel(SView s0, int c0, int up0, SView s1, int c1
 }
 
 __global__ void silu_kernel(SOut t, int B, int HW, int C) {
+  pdl_wait();
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * HW * C;
   if (idx >= total) return;
@@ -424,32 +435,29 @@ cudaError_t launch_stem(const StemArgs& a, cudaStream_t s) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned grid = static_cast<unsigned>(tiles < 3LL * sms ? tiles : 3LL * sms);
-  if (a.Co == 16) stem_kernel<16><<<grid, 128, StemTile<16>::kSmem, s>>>(a);
-  else if (a.Co == 32) stem_kernel<32><<<grid, 128, StemTile<32>::kSmem, s>>>(a);
-  else stem_kernel<64><<<grid, 128, StemTile<64>::kSmem, s>>>(a);
-  return cudaGetLastError();
+  if (a.Co == 16) return launch_pdl(stem_kernel<16>, dim3(grid), dim3(128), StemTile<16>::kSmem, s, a);
+  if (a.Co == 32) return launch_pdl(stem_kernel<32>, dim3(grid), dim3(128), StemTile<32>::kSmem, s, a);
+  return launch_pdl(stem_kernel<64>, dim3(grid), dim3(128), StemTile<64>::kSmem, s, a);
 }
 
 cudaError_t launch_absmax_split(SView v, int B, int H, int W, int C, unsigned* amax, cudaStream_t s) {
   // The statistic lands in amax[1] (amax[0] receives 0).
   const long long total = static_cast<long long>(B) * H * W * C;
   const long long blocks = (total + 255) / 256;
-  absmax_split_kernel<<<static_cast<int>(blocks < 1184 ? (blocks < 1 ? 1 : blocks) : 1184), 256, 0, s>>>(v, B, H, W, C,
-                                                                                                     amax);
-  return cudaGetLastError();
+  return launch_pdl(absmax_split_kernel, dim3(static_cast<unsigned>(blocks < 1184 ? (blocks < 1 ? 1 : blocks) : 1184)),
+                    dim3(256), 0, s, v, B, H, W, C, amax);
 }
 
 cudaError_t launch_absmax_f32(const float* x, long long n, unsigned* amax, cudaStream_t s) {
   const long long blocks = (n + 255) / 256;
-  absmax_f32_kernel<<<static_cast<int>(blocks < 1184 ? (blocks < 1 ? 1 : blocks) : 1184), 256, 0, s>>>(x, n, amax);
-  return cudaGetLastError();
+  return launch_pdl(absmax_f32_kernel, dim3(static_cast<unsigned>(blocks < 1184 ? (blocks < 1 ? 1 : blocks) : 1184)),
+                    dim3(256), 0, s, x, n, amax);
 }
 
 cudaError_t launch_dwconv3x3(const DwArgs& a, cudaStream_t s) {
   if (a.C % 8) return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(a.B) * a.H * a.W * (a.C / 8);
-  dw3x3_kernel<<<blocks_for(total, 256), 256, 0, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(dw3x3_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {
@@ -461,15 +469,13 @@ cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {
   }
   if (b.stride < 1) return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(b.B) * b.Ho * b.Wo * (b.C / 8);
-  maxpool_kernel<<<blocks_for(total, 256), 256, 0, s>>>(b);
-  return cudaGetLastError();
+  return launch_pdl(maxpool_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, s, b);
 }
 
 cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t s) {
   const long long total = static_cast<long long>(a.B) * a.N * 4;
   if (total == 0) return cudaSuccess;
-  decode_kernel<<<blocks_for(total, 256), 256, 0, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(decode_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_nchw_to_split(const float* in, int B, int C, int H, int W, SOut out, cudaStream_t s) {

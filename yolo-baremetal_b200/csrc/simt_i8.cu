@@ -6,6 +6,7 @@
 #include <climits>
 #include <cstdint>
 
+#include "pdl.cuh"
 #include "i8k.h"
 
 namespace yb {
@@ -20,6 +21,7 @@ inline unsigned blocks_for(long long n, int t) { return static_cast<unsigned>((n
 
 // --------------------------------------------------------------- input
 __global__ void quantize_input_kernel(const float* in, int B, int C, int H, int W, float s, I8View out) {
+  pdl_wait();
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * H * W;
   if (idx >= total) return;
@@ -115,6 +117,7 @@ __global__ void __launch_bounds__(128) stem_i8_kernel(const StemI8Args a) {
     sx2[i] = make_int2(b, sh);
   }
   for (int i = tid; i < 256; i += 128) slut[i] = a.lut[i];
+  pdl_wait();
   const int tiles_x = (a.Wo + T::TW - 1) / T::TW, tiles_y = (a.Ho + T::TH - 1) / T::TH;
   const int total = a.B * tiles_x * tiles_y;
   const int r = tid >> 4, x0 = tid & 15;
@@ -220,6 +223,7 @@ __global__ void __launch_bounds__(128) stem_i8_kernel(const StemI8Args a) {
 // k x k, stride 1, padding k / 2 excluded (the -128 sentinel is below every
 // quantised value); 16 channels per thread.
 __global__ void maxpool_i8_kernel(I8View in, I8View out, int B, int H, int W, int C, int k) {
+  pdl_wait();
   const int C16 = C >> 4;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * H * W * C16;
@@ -284,6 +288,7 @@ __global__ void __launch_bounds__(256) dw3x3_i8_kernel(I8View in, I8View out, in
   }
   for (int i = threadIdx.x; i < 256; i += blockDim.x) slut[i] = lut ? lut[i] : 0;
   __syncthreads();
+  pdl_wait();
   const int C16 = C >> 4;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * H * W * C16;
@@ -348,6 +353,7 @@ __global__ void __launch_bounds__(256) dw3x3_i8_kernel(I8View in, I8View out, in
 // out[b, y, x, 0:c0] = src0[b, y >> lg0, x >> lg0, :]; out[..., c0:] = src1.
 // 16 channels per thread (c0, c1 multiples of 16).
 __global__ void concat_i8_kernel(I8View s0, int c0, int lg0, I8View s1, int c1, int B, int H, int W, I8View out) {
+  pdl_wait();
   const int C16 = (c0 + c1) >> 4;
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(B) * H * W * C16;
@@ -370,6 +376,7 @@ __global__ void concat_i8_kernel(I8View s0, int c0, int lg0, I8View s1, int c1, 
 
 // ---------------------------------------------------- NHWC -> NCHW dump
 __global__ void nhwc_to_nchw_i8_kernel(I8View in, int C, int H, int W, int8_t* out) {
+  pdl_wait();
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(C) * H * W;
   if (idx >= total) return;
@@ -382,15 +389,13 @@ __global__ void nhwc_to_nchw_i8_kernel(I8View in, int C, int H, int W, int8_t* o
 
 cudaError_t launch_quantize_input(const float* in, int B, int C, int H, int W, float s, I8View out, cudaStream_t st) {
   const long long total = static_cast<long long>(B) * H * W;
-  quantize_input_kernel<<<blocks_for(total, 256), 256, 0, st>>>(in, B, C, H, W, s, out);
-  return cudaGetLastError();
+  return launch_pdl(quantize_input_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, st, in, B, C, H, W, s, out);
 }
 
 cudaError_t launch_maxpool_i8(I8View in, I8View out, int B, int H, int W, int C, int k, cudaStream_t st) {
   if (C % 16 || in.cstride % 16 || out.cstride % 16) return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(B) * H * W * (C / 16);
-  maxpool_i8_kernel<<<blocks_for(total, 256), 256, 0, st>>>(in, out, B, H, W, C, k);
-  return cudaGetLastError();
+  return launch_pdl(maxpool_i8_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, st, in, out, B, H, W, C, k);
 }
 
 cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const uint32_t* wp, const int32_t* bq,
@@ -399,16 +404,15 @@ cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, c
   const long long total = static_cast<long long>(B) * H * W * (C / 16);
   if (total == 0) return cudaSuccess;
   const size_t smem = static_cast<size_t>(C) * 16 + 256;
-  dw3x3_i8_kernel<<<blocks_for(total, 256), 256, smem, st>>>(in, out, B, H, W, C, wp, bq, mult, shift, lut);
-  return cudaGetLastError();
+  return launch_pdl(dw3x3_i8_kernel, dim3(blocks_for(total, 256)), dim3(256), smem, st, in, out, B, H, W, C, wp, bq, mult,
+                    shift, lut);
 }
 
 cudaError_t launch_concat_i8(I8View s0, int c0, int lg0, I8View s1, int c1, int B, int H, int W, I8View out,
                              cudaStream_t st) {
   if ((c0 | c1) % 16 || s0.cstride % 16 || (c1 && s1.cstride % 16) || out.cstride % 16) return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(B) * H * W * ((c0 + c1) / 16);
-  concat_i8_kernel<<<blocks_for(total, 256), 256, 0, st>>>(s0, c0, lg0, s1, c1, B, H, W, out);
-  return cudaGetLastError();
+  return launch_pdl(concat_i8_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, st, s0, c0, lg0, s1, c1, B, H, W, out);
 }
 
 cudaError_t launch_nhwc_to_nchw_i8(I8View in, int C, int H, int W, int8_t* out, cudaStream_t st) {
@@ -440,10 +444,9 @@ cudaError_t launch_stem_i8(const StemI8Args& a, cudaStream_t st) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned grid = static_cast<unsigned>(tiles < 3LL * sms ? tiles : 3LL * sms);
-  if (a.Co == 16) stem_i8_kernel<16><<<grid, 128, StemI8Tile<16>::kSmem, st>>>(a);
-  else if (a.Co == 32) stem_i8_kernel<32><<<grid, 128, StemI8Tile<32>::kSmem, st>>>(a);
-  else stem_i8_kernel<64><<<grid, 128, StemI8Tile<64>::kSmem, st>>>(a);
-  return cudaGetLastError();
+  if (a.Co == 16) return launch_pdl(stem_i8_kernel<16>, dim3(grid), dim3(128), StemI8Tile<16>::kSmem, st, a);
+  if (a.Co == 32) return launch_pdl(stem_i8_kernel<32>, dim3(grid), dim3(128), StemI8Tile<32>::kSmem, st, a);
+  return launch_pdl(stem_i8_kernel<64>, dim3(grid), dim3(128), StemI8Tile<64>::kSmem, st, a);
 }
 
 }  // namespace yb

@@ -10,6 +10,7 @@
 // on order-preserving float keys plus an index-ordered scan for ties at the
 // threshold, then a bitonic sort of the k survivors in shared memory.
 #include <cfloat>
+#include "pdl.cuh"
 #include "kernels.h"
 
 namespace yb {
@@ -166,6 +167,7 @@ __device__ void select_topk(const Get& get, int n, int k, int* out, TopkSmem& sm
 }
 
 __global__ void __launch_bounds__(kT) topk_kernel(const TopkArgs a) {
+  pdl_wait();
   __shared__ TopkSmem sm;
   const int b = blockIdx.x;
   int k = a.max_det < a.N ? a.max_det : a.N;
@@ -222,8 +224,7 @@ cudaError_t launch_topk(const TopkArgs& a, cudaStream_t s) {
   int k = a.max_det < a.N ? a.max_det : a.N;
   if (k > a.cap) k = a.cap;
   if (k > kTopkMax || a.B <= 0) return cudaErrorInvalidValue;
-  topk_kernel<<<a.B, kT, 0, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(topk_kernel, dim3(a.B), dim3(kT), 0, s, a);
 }
 
 }  // namespace yb
