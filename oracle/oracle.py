@@ -81,6 +81,9 @@ class Oracle:
                                            C.c_void_p]
             lib.orc_psablock.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
             lib.orc_dwconv.argtypes = [C.c_void_p, C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+            for fn in (lib.orc_resize_align_corners, lib.orc_resize_half_pixel):
+                fn.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int]
+            lib.orc_rgb_to_nchw.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
             cls._lib = lib
         return cls._lib
 
@@ -186,6 +189,22 @@ class Oracle:
         cls.lib().orc_postprocess(p if p.size else np.zeros(1, np.float32), n, nc, max_det, cap, out)
         return out.reshape(cap, 6)
 
+    @classmethod
+    def preprocess(cls, rgb: np.ndarray, H: int, W: int, mode: int = 0) -> np.ndarray:
+        """uint8 HWC RGB images [B, sh, sw, 3] -> fp32 NCHW [B, 3, H, W]: resize
+        (mode 0: src/main.c resize_rgb_bilinear; mode 1: the pixel-centred
+        resize of tests/dump_model_stages.c) then / 255."""
+        L = cls.lib()
+        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        B, sh, sw, _ = rgb.shape
+        out = np.zeros((B, 3, H, W), np.float32)
+        tmp = np.zeros((H, W, 3), np.uint8)
+        fn = L.orc_resize_align_corners if mode == 0 else L.orc_resize_half_pixel
+        for b in range(B):
+            fn(rgb[b].ctypes.data, sw, sh, tmp.ctypes.data, W, H)
+            L.orc_rgb_to_nchw(tmp.ctypes.data, W, H, out[b].ctypes.data)
+        return out
+
 
 class Reference:
     """The reference implementation compiled from its own sources."""
@@ -205,6 +224,12 @@ class Reference:
             lib.ref_time_forwards.restype = C.c_double
             lib.ref_time_forwards.argtypes = [C.c_char_p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int]
             lib.ref_postprocess.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+            lib.ref_resize_rgb_bilinear.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int]
+            lib.ref_preprocess.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+            lib.ref_load_rgb_resized.restype = C.c_void_p
+            lib.ref_load_rgb_resized.argtypes = [C.c_char_p, C.c_int, C.c_int]
+            lib.ref_free.argtypes = [C.c_void_p]
+            lib.visualize_write_bmp_rgb24.argtypes = [C.c_char_p, C.c_void_p, C.c_int, C.c_int]
             cls._lib = lib
         return cls._lib
 
