@@ -339,6 +339,10 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
+    # End to end from 8-bit frames (the reference's camera path: 640x640 RGB,
+    # resize_rgb_bilinear + preprocess on the device): a quarter of the bytes.
+    rgb8 = rgb8_frames(rank, B, H)
+    e2e8_s = timed_rgb8(L, model, rgb8, host_out, B, H, args, barrier, max_over_ranks)
 
     n_ops = C.c_int()
     yb.check(L.yb_cuda_profile_ops(model.ctx, B, H, H, 300, 0, None, 0, C.byref(n_ops)), "yb_cuda_profile_ops")
@@ -373,6 +377,12 @@ def run_ours(args):
                 "e2e": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
                         "h2d_bytes_per_step": world * host_in.numel() * 4,
                         "d2h_bytes_per_step": world * host_out.numel() * 4},
+                "e2e_rgb8": {"value": world * B * args.steps / e2e8_s, "unit": UNIT,
+                             "h2d_bytes_per_step": world * rgb8.numel(),
+                             "d2h_bytes_per_step": world * host_out.numel() * 4,
+                             "source": f"{B} seeded uint8 RGB frames {H}x{H} per GPU per step through "
+                                       "yb_cuda_forward_rgb8 (device resize_rgb_bilinear + /255, then the "
+                                       "forward); same metric, 8-bit inputs instead of the fp32 tensor"},
                 "gpu_launches": n_ops.value * args.steps,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic,
@@ -401,6 +411,38 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
+
+
+def rgb8_frames(rank, B, H):
+    import numpy as np
+    import torch
+
+    rng = np.random.default_rng(20000 + rank)
+    return torch.from_numpy(rng.integers(0, 256, size=(B, H, H, 3), dtype=np.uint8)).pin_memory()
+
+
+def timed_rgb8(L, model, rgb8, host_out, B, H, args, barrier, max_over_ranks):
+    """Wall time of K yb_cuda_forward_rgb8 calls (pinned 8-bit frames in,
+    detections out), max over ranks."""
+    import torch
+
+    import yolo_b200 as yb
+
+    def step():
+        yb.check(L.yb_cuda_forward_rgb8(model.ctx, rgb8.data_ptr(), B, H, H, 0, H, H, host_out.data_ptr(), 300),
+                 "yb_cuda_forward_rgb8")
+
+    for _ in range(max(1, args.warmup // 2)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    e = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    return e
 
 
 INT8_KINDS = ["conv_i8", "stem_i8", "dw3x3_i8", "maxpool_concat_i8", "attention_i8", "decode", "topk"]
@@ -460,6 +502,8 @@ def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_o
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
+    rgb8 = rgb8_frames(rank, B, H)
+    e2e8_s = timed_rgb8(L, model, rgb8, host_out, B, H, args, barrier, max_over_ranks)
     # Batch 1 (the single-image INT8 configuration): device-resident latency.
     d1_in, d1_out = model.plan_io(1, H, H)
     torch.cuda.synchronize()
@@ -498,6 +542,9 @@ def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_o
                "e2e": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
                        "h2d_bytes_per_step": world * host_in.numel() * 4,
                        "d2h_bytes_per_step": world * host_out.numel() * 4},
+               "e2e_rgb8": {"value": world * B * args.steps / e2e8_s, "unit": UNIT,
+                            "h2d_bytes_per_step": world * rgb8.numel(),
+                            "d2h_bytes_per_step": world * host_out.numel() * 4},
                "batch1": {"ms_per_image": b1_ms, "images_per_s": world / (b1_ms * 1e-3),
                           "note": "device-resident single-image forward, one per GPU"},
                "gpu_launches": n_ops.value * args.steps,

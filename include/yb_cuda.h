@@ -48,6 +48,17 @@ typedef struct {
     int n;
 } yb_int8_scales;
 
+/* Resize rule of the device preprocess (yb_cuda_forward_rgb8,
+ * yb_cuda_preprocess_rgb8), both the reference's, bit for bit. */
+typedef enum {
+    /* src/main.c:18-51 resize_rgb_bilinear (image and camera paths): corners
+     * aligned, source coordinate dx * (sw - 1) / (dw - 1), rounded half up. */
+    YB_RESIZE_ALIGN_CORNERS = 0,
+    /* tests/dump_model_stages.c:58-96 load_rgb_resized: pixel centres,
+     * source coordinate (x + 0.5) * sw / dw - 0.5, truncated. */
+    YB_RESIZE_HALF_PIXEL = 1
+} yb_resize_mode;
+
 /* Stage callback: called once per stage tensor (NCHW float32 host data of
  * image 0) with the reference's stage names stage_00_input .. stage_25_detect. */
 typedef void (*yb_stage_cb)(void* user, const char* name, const float* nchw, int n, int c, int h, int w);
@@ -107,6 +118,22 @@ status_t yb_cuda_load_bin(void* ctx, const char* path);
 status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int H, int W,
                          float* out_dets, int max_det,
                          yb_stage_cb dump, void* user, double* step_ms);
+
+/* Forward from 8-bit images: rgb_hwc [B, src_h, src_w, 3] uint8 RGB (host,
+ * pinned for full copy speed) is copied to the GPU (a quarter of the fp32
+ * input's bytes), resized to H x W by `resize` (yb_resize_mode), scaled by
+ * 1/255 into the plan's fp32 NCHW input (main.c:53-64) on the device, and
+ * run; out_dets [B, max_det, 6] as yb_cuda_forward.  The network input equals
+ * the reference's preprocess of the same pixels bit for bit.  The head
+ * tensors are kept (yb_cuda_get_head). */
+status_t yb_cuda_forward_rgb8(void* ctx, const unsigned char* rgb_hwc, int B, int src_h, int src_w, int resize,
+                              int H, int W, float* out_dets, int max_det);
+
+/* The device preprocess alone: d_rgb [B, src_h, src_w, 3] uint8 and d_nchw
+ * [B, 3, H, W] fp32 in the current device's memory; enqueued on `stream`
+ * (NULL = the default stream), does not synchronize. */
+status_t yb_cuda_preprocess_rgb8(const unsigned char* d_rgb, int B, int src_h, int src_w, int resize, float* d_nchw,
+                                 int H, int W, void* stream);
 
 /* Forward on device buffers already in this context's GPU memory:
  * d_in [B,3,H,W], d_out [B,max_det,6].  Enqueued on `stream` (a

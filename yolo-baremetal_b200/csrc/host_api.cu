@@ -82,6 +82,9 @@ struct Ctx {
   cudaStream_t slot_stream[kPipeSlotsMax] = {};
   cudaEvent_t in_ready[kPipeSlotsMax] = {};
   cudaEvent_t slot_free[kPipeSlotsMax] = {};
+  // Device staging of yb_cuda_forward_rgb8's 8-bit input (grown on demand).
+  uint8_t* d_rgb = nullptr;
+  size_t d_rgb_bytes = 0;
   // Scale table of the last yb_cuda_calibrate_int8, in name order.
   std::vector<std::pair<std::string, float>> calib;
 };
@@ -348,6 +351,7 @@ extern "C" status_t yb_cuda_destroy(void* ctx) {
     cudaStreamDestroy(c->copy_stream);
   }
   if (c->h_stage) cudaFreeHost(c->h_stage);
+  if (c->d_rgb) cudaFree(c->d_rgb);
   c->eng.reset();
   delete c;
   return SUCCESS;
@@ -554,6 +558,48 @@ extern "C" status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int 
   }
   if (dump) return p->int8 ? dump_stages_i8(c, p, in_nchw, dump, user) : dump_stages(c, p, in_nchw, dump, user);
   return SUCCESS;
+}
+
+extern "C" status_t yb_cuda_forward_rgb8(void* ctx, const unsigned char* rgb_hwc, int B, int src_h, int src_w,
+                                         int resize, int H, int W, float* out_dets, int max_det) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !rgb_hwc || !out_dets) return ERROR_NULL_POINTER;
+  if (B < 1 || src_h < 1 || src_w < 1 || (resize != YB_RESIZE_ALIGN_CORNERS && resize != YB_RESIZE_HALF_PIXEL))
+    return ERROR_INVALID_DIMS;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  Plan* p = nullptr;
+  if ((st = plan_for(c, B, H, W, max_det, &p)) != SUCCESS) return st;
+  const size_t bytes = static_cast<size_t>(B) * src_h * src_w * 3;
+  if (bytes > c->d_rgb_bytes) {
+    if (c->d_rgb) cudaFree(c->d_rgb);
+    c->d_rgb = nullptr;
+    c->d_rgb_bytes = 0;
+    cudaError_t e = cudaMalloc(&c->d_rgb, bytes);
+    if (e != cudaSuccess) return cuda_status(e, "rgb staging");
+    c->d_rgb_bytes = bytes;
+  }
+  cudaStream_t s = c->eng->stream();
+  cudaError_t e = cudaMemcpyAsync(c->d_rgb, rgb_hwc, bytes, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = launch_preprocess(c->d_rgb, B, src_h, src_w, resize, p->d_in, H, W, s);
+  if (e == cudaSuccess) e = c->eng->run(p, s, nullptr);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(out_dets, p->d_out, static_cast<size_t>(B) * max_det * 6 * 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e, "forward_rgb8");
+  if ((st = check_kernel_flag(c)) != SUCCESS) return st;
+  c->last = p;
+  return SUCCESS;
+}
+
+extern "C" status_t yb_cuda_preprocess_rgb8(const unsigned char* d_rgb, int B, int src_h, int src_w, int resize,
+                                            float* d_nchw, int H, int W, void* stream) {
+  if (!d_rgb || !d_nchw) return ERROR_NULL_POINTER;
+  if (B < 0 || src_h < 1 || src_w < 1 || H < 1 || W < 1 ||
+      (resize != YB_RESIZE_ALIGN_CORNERS && resize != YB_RESIZE_HALF_PIXEL))
+    return ERROR_INVALID_DIMS;
+  const cudaError_t e = launch_preprocess(d_rgb, B, src_h, src_w, resize, d_nchw, H, W, static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "preprocess_rgb8");
 }
 
 extern "C" status_t yb_cuda_plan_io(void* ctx, int B, int H, int W, int max_det, float** d_in, float** d_out) {

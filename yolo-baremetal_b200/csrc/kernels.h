@@ -190,6 +190,11 @@ struct AttnArgs {
   SOut out;
   int* err = nullptr;  // kernel error word (bounded waits that gave up)
 };
+// Device preprocess (preprocess.cu): uint8 HWC RGB [B, sh, sw, 3] -> resize
+// (mode: yb_resize_mode) -> / 255 -> fp32 NCHW [B, 3, H, W].
+cudaError_t launch_preprocess(const uint8_t* src, int B, int sh, int sw, int mode, float* dst, int H, int W,
+                              cudaStream_t s);
+
 // tcgen05 kernel (attn_tc.cu): kd = 32, hd = 64.
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 

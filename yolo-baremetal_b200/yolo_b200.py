@@ -38,7 +38,7 @@ EXPORTS = {
     "utils.h": ["timer_start", "timer_stop", "timer_elapsed_ms", "load_named_tensor", "save_named_tensor", "fold_bn"],
     "yb_cuda.h": ["yb_cuda_init", "yb_cuda_upload_weights", "yb_cuda_load_bin", "yb_cuda_forward",
                   "yb_cuda_set_int8", "yb_cuda_get_int8_stage", "yb_cuda_calibrate_int8",
-                  "yb_cuda_int8_scale_entry",
+                  "yb_cuda_int8_scale_entry", "yb_cuda_forward_rgb8", "yb_cuda_preprocess_rgb8",
                   "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_detect_topk_noalloc",
                   "yb_cuda_forward_sharded",
                   "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error"],
@@ -108,6 +108,10 @@ def lib() -> C.CDLL:
                                           C.c_int, C.POINTER(C.c_int)]
         L.yb_cuda_destroy.argtypes = [C.c_void_p]
         L.yb_cuda_set_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.yb_cuda_forward_rgb8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                           C.c_int, C.c_void_p, C.c_int]
+        L.yb_cuda_preprocess_rgb8.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                              C.c_int, C.c_void_p]
         L.yb_cuda_calibrate_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                              C.POINTER(C.c_int)]
         L.yb_cuda_int8_scale_entry.argtypes = [C.c_void_p, C.c_int, C.c_char_p, C.c_int, C.POINTER(C.c_float)]
@@ -230,6 +234,15 @@ class Model:
         check(lib().yb_cuda_get_int8_stage(self.ctx, idx, image, q.ctypes.data, cs.ctypes.data, None, None, None),
               "yb_cuda_get_int8_stage")
         return q, cs
+
+    def forward_rgb8(self, rgb: np.ndarray, H: int = 640, W: int = 640, resize: int = 0, max_det: int = 300):
+        """uint8 HWC RGB images [B, sh, sw, 3] -> dets [B, max_det, 6], preprocessed on the device."""
+        x = np.ascontiguousarray(rgb, dtype=np.uint8)
+        B, sh, sw, _ = x.shape
+        dets = np.zeros((B, max_det, 6), dtype=np.float32)
+        check(lib().yb_cuda_forward_rgb8(self.ctx, x.ctypes.data, B, sh, sw, resize, H, W, dets.ctypes.data, max_det),
+              "yb_cuda_forward_rgb8")
+        return dets
 
     def head(self, batch: int):
         """(logits [B,N,nc], boxes [B,N,4]) of the last forward."""
