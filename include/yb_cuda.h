@@ -17,6 +17,7 @@
  * kernel that reported a bounded-wait timeout); yb_cuda_last_error() returns a
  * one-line description of the last failure on the calling thread. */
 
+#include "detection.h"
 #include "model.h"
 
 #ifdef __cplusplus
@@ -134,6 +135,19 @@ status_t yb_cuda_forward_rgb8(void* ctx, const unsigned char* rgb_hwc, int B, in
  * (NULL = the default stream), does not synchronize. */
 status_t yb_cuda_preprocess_rgb8(const unsigned char* d_rgb, int B, int src_h, int src_w, int resize, float* d_nchw,
                                  int H, int W, void* stream);
+
+/* Detection lists of the last forward (not a pipelined one): for each image,
+ * decode_detections (detection.c:3-34) on the device -- the rows whose score
+ * is not <= threshold, in row order, at most `capacity` -- then copied out:
+ * out [B][capacity] detection_t, counts [B].  A compact alternative to
+ * reading the [B, max_det, 6] rows. */
+status_t yb_cuda_get_detections(void* ctx, float threshold, int capacity, detection_t* out, int* counts);
+
+/* The same on device buffers: d_dets [B, rows, 6] fp32, d_out [B][capacity]
+ * detection_t, d_counts [B]; enqueued on `stream` (NULL = the default
+ * stream), does not synchronize. */
+status_t yb_cuda_detections(const float* d_dets, int B, int rows, float threshold, int capacity, detection_t* d_out,
+                            int* d_counts, void* stream);
 
 /* Forward on device buffers already in this context's GPU memory:
  * d_in [B,3,H,W], d_out [B,max_det,6].  Enqueued on `stream` (a

@@ -84,6 +84,7 @@ class Oracle:
             for fn in (lib.orc_resize_align_corners, lib.orc_resize_half_pixel):
                 fn.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int]
             lib.orc_rgb_to_nchw.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+            lib.orc_decode_detections.argtypes = [_f32p, C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p]
             cls._lib = lib
         return cls._lib
 
@@ -188,6 +189,18 @@ class Oracle:
         n = p.size // (4 + nc)
         cls.lib().orc_postprocess(p if p.size else np.zeros(1, np.float32), n, nc, max_det, cap, out)
         return out.reshape(cap, 6)
+
+    DET_DTYPE = np.dtype([("x1", np.float32), ("y1", np.float32), ("x2", np.float32), ("y2", np.float32),
+                          ("score", np.float32), ("class_id", np.int32)])
+
+    @classmethod
+    def decode_detections(cls, rows: np.ndarray, threshold: float, capacity: int):
+        """decode_detections for one image's [n, 6] rows: (structured array [capacity], count)."""
+        r = np.ascontiguousarray(rows, dtype=np.float32)
+        out = np.zeros(max(capacity, 1), dtype=cls.DET_DTYPE)
+        n = cls.lib().orc_decode_detections(r.reshape(-1), r.shape[0], r.shape[1], threshold, capacity,
+                                            out.ctypes.data)
+        return out[:capacity], n
 
     @classmethod
     def preprocess(cls, rgb: np.ndarray, H: int, W: int, mode: int = 0) -> np.ndarray:

@@ -1,7 +1,8 @@
-/* CPU restatement of the reference's image preprocessing -- TEST
- * INFRASTRUCTURE ONLY (the checker of the device preprocess; nothing in the
- * product links it).  Compiled with -ffp-contract=off: every product and sum
- * is rounded on its own, in the reference's evaluation order.
+/* CPU restatement of the reference's image preprocessing and detection
+ * lists -- TEST INFRASTRUCTURE ONLY (the checker of the device preprocess and
+ * detection lists; nothing in the product links it).  Compiled with
+ * -ffp-contract=off: every product and sum is rounded on its own, in the
+ * reference's evaluation order.
  *
  *   orc_resize_align_corners  src/main.c:18-51 (resize_rgb_bilinear): source
  *       coordinate dx * (sw - 1) / (dw - 1), bilinear blend of the two rows'
@@ -69,4 +70,31 @@ void orc_rgb_to_nchw(const uint8_t* rgb, int w, int h, float* nchw) {
     const int plane = h * w;
     for (int i = 0; i < plane; i++)
         for (int c = 0; c < 3; c++) nchw[c * plane + i] = rgb[i * 3 + c] / 255.0f;
+}
+
+/* decode_detections (src/detection.c:3-34) for one image: rows [n][feat]
+ * (x1, y1, x2, y2, score, class, ...); keeps the rows whose score is not
+ * <= threshold, in row order, until `capacity` are kept.  out: per kept row
+ * 5 floats and the class as int (the layout of detection_t).  Returns the
+ * count. */
+typedef struct {
+    float x1, y1, x2, y2, score;
+    int class_id;
+} orc_det_t;
+
+int orc_decode_detections(const float* rows, int n, int feat, float threshold, int capacity, orc_det_t* out) {
+    int count = 0;
+    for (int i = 0; i < n; i++) {
+        const float* r = rows + (long)i * feat;
+        if (r[4] <= threshold) continue;
+        if (count >= capacity) break;
+        orc_det_t* d = &out[count++];
+        d->x1 = r[0];
+        d->y1 = r[1];
+        d->x2 = r[2];
+        d->y2 = r[3];
+        d->score = r[4];
+        d->class_id = (int)r[5];
+    }
+    return count;
 }

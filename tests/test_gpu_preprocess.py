@@ -57,3 +57,50 @@ def test_forward_rgb8_equals_forward(weights_n0, mode):
         assert np.array_equal(q8, qf)
     finally:
         m.close()
+
+
+@pytest.mark.parametrize("rows,cap", [(300, 100), (300, 7), (45, 100), (33, 0)])
+def test_device_detection_lists(rows, cap):
+    """yb_cuda_detections (batched decode_detections) against the oracle's
+    restatement, which is pinned to the reference: scores equal to the
+    threshold, NaN scores, capacity overflow."""
+    import torch
+
+    import yolo_b200 as yb
+    from oracle import Oracle
+
+    thr = np.float32(0.25)
+    rng = np.random.default_rng(rows + cap)
+    d = rng.standard_normal((3, rows, 6)).astype(np.float32) * 100
+    d[..., 4] = rng.choice([thr, np.nextafter(thr, np.float32(1)), 0.0, 0.9, -1.0, np.nan], size=(3, rows))
+    d[..., 5] = rng.integers(0, 80, (3, rows)).astype(np.float32)
+    dd = torch.from_numpy(d).cuda()
+    out = torch.zeros((3, max(cap, 1) * 6), dtype=torch.int32, device="cuda")
+    cnt = torch.full((3,), -1, dtype=torch.int32, device="cuda")
+    yb.check(yb.lib().yb_cuda_detections(dd.data_ptr(), 3, rows, thr, cap, out.data_ptr(), cnt.data_ptr(), None),
+             "yb_cuda_detections")
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(Oracle.DET_DTYPE).reshape(3, -1)
+    counts = cnt.cpu().numpy()
+    for b in range(3):
+        want, n = Oracle.decode_detections(d[b], thr, cap)
+        assert counts[b] == n
+        assert got[b, :n].tobytes() == want[:n].tobytes()
+
+
+def test_get_detections_after_forward(weights_n0_soft):
+    import yb_weights as yw
+    import yolo_b200 as yb
+    from oracle import Oracle
+
+    m = yb.Model(weights_n0_soft)
+    try:
+        x = yw.make_batch([51, 52], 256, 256)
+        dets = m.forward(x)["dets"]
+        lists, counts = m.detections(2, threshold=0.5, capacity=50)
+        for b in range(2):
+            want, n = Oracle.decode_detections(dets[b], np.float32(0.5), 50)
+            assert counts[b] == n
+            assert lists[b, :n].tobytes() == want[:n].tobytes()
+    finally:
+        m.close()

@@ -49,3 +49,38 @@ def test_half_pixel_resize(sh, sw, oh, ow, tmp_path):
     R.ref_preprocess(ref_nchw.ctypes.data, ref.ctypes.data, ow, oh)
     got = Oracle.preprocess(src[None], oh, ow, mode=1)[0]
     assert np.array_equal(got.view(np.uint32), ref_nchw.view(np.uint32))
+
+
+def _rows(n, seed, thr):
+    rng = np.random.default_rng(seed)
+    r = rng.standard_normal((n, 6)).astype(np.float32) * 100
+    r[:, 4] = rng.choice([thr, np.nextafter(np.float32(thr), np.float32(1)), 0.0, 0.9, -1.0, np.nan], size=n)
+    r[:, 5] = rng.integers(0, 80, n).astype(np.float32)
+    return r
+
+
+@pytest.mark.parametrize("n,cap", [(300, 100), (300, 5), (40, 100), (0, 10), (33, 0)])
+def test_decode_detections_oracle_vs_reference(n, cap):
+    """Our decode restatement against the reference's decode_detections
+    (detection.c:3-34), including scores equal to the threshold and NaN."""
+    import yolo_b200 as yb
+
+    thr = np.float32(0.25)
+    rows = _rows(n, n + cap, thr)
+    want, cnt = Oracle.decode_detections(rows, thr, cap)
+    R = Reference.lib()
+
+    class Res(C.Structure):
+        _fields_ = [("detections", C.c_void_p), ("count", C.c_int), ("capacity", C.c_int)]
+
+    buf = np.zeros(max(cap, 1), dtype=Oracle.DET_DTYPE)
+    res = Res(buf.ctypes.data, 0, cap)
+    src = np.ascontiguousarray(rows.reshape(1, n, 6, 1)) if n else np.zeros((1, 0, 6, 1), np.float32)
+    t = yb.Tensor()
+    t.data = src.ctypes.data_as(C.POINTER(C.c_float))
+    for i, d in enumerate((1, n, 6, 1)):
+        t.dims[i] = d
+    R.decode_detections.argtypes = [C.c_void_p, C.c_void_p, C.c_float]
+    assert R.decode_detections(C.byref(res), C.byref(t), thr) == 0
+    assert res.count == cnt
+    assert buf[:cnt].tobytes() == want[:cnt].tobytes()

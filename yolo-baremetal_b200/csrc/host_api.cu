@@ -592,6 +592,42 @@ extern "C" status_t yb_cuda_forward_rgb8(void* ctx, const unsigned char* rgb_hwc
   return SUCCESS;
 }
 
+extern "C" status_t yb_cuda_get_detections(void* ctx, float threshold, int capacity, detection_t* out, int* counts) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !out || !counts) return ERROR_NULL_POINTER;
+  if (capacity < 0) return ERROR_INVALID_DIMS;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  Plan* p = c->last;
+  if (!p) {
+    set_error("no detections kept: no forward has run on this context, or the last one was pipelined");
+    return ERROR_INVALID_DIMS;
+  }
+  cudaStream_t s = c->eng->stream();
+  const size_t n_out = static_cast<size_t>(p->B) * capacity;
+  DevMem d_out, d_cnt;
+  cudaError_t e = d_out.alloc(n_out * sizeof(detection_t) + 16);
+  if (e == cudaSuccess) e = d_cnt.alloc(static_cast<size_t>(p->B) * sizeof(int));
+  if (e == cudaSuccess)
+    e = launch_detections(p->d_out, p->B, p->max_det, threshold, capacity, static_cast<detection_t*>(d_out.p),
+                          static_cast<int*>(d_cnt.p), s);
+  if (e == cudaSuccess && n_out)
+    e = cudaMemcpyAsync(out, d_out.p, n_out * sizeof(detection_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(counts, d_cnt.p, static_cast<size_t>(p->B) * sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  return cuda_status(e, "get_detections");
+}
+
+extern "C" status_t yb_cuda_detections(const float* d_dets, int B, int rows, float threshold, int capacity,
+                                       detection_t* d_out, int* d_counts, void* stream) {
+  if (!d_dets || !d_out || !d_counts) return ERROR_NULL_POINTER;
+  if (B < 0 || rows < 0 || capacity < 0) return ERROR_INVALID_DIMS;
+  return cuda_status(launch_detections(d_dets, B, rows, threshold, capacity, d_out, d_counts,
+                                       static_cast<cudaStream_t>(stream)),
+                     "detections");
+}
+
 extern "C" status_t yb_cuda_preprocess_rgb8(const unsigned char* d_rgb, int B, int src_h, int src_w, int resize,
                                             float* d_nchw, int H, int W, void* stream) {
   if (!d_rgb || !d_nchw) return ERROR_NULL_POINTER;
@@ -926,7 +962,7 @@ extern "C" status_t decode_detections(detection_results_t* results, const tensor
   results->count = 0;
   for (int i = 0; i < rows; ++i) {
     const float* r = head->data + static_cast<size_t>(i) * rs;
-    if (!(r[4] > threshold)) continue;
+    if (r[4] <= threshold) continue;
     if (results->count >= results->capacity) break;
     detection_t* d = &results->detections[results->count++];
     d->x1 = r[0];

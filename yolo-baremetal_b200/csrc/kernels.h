@@ -21,6 +21,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "detection.h"
+
 namespace yb {
 
 struct SView {
@@ -194,6 +196,11 @@ struct AttnArgs {
 // (mode: yb_resize_mode) -> / 255 -> fp32 NCHW [B, 3, H, W].
 cudaError_t launch_preprocess(const uint8_t* src, int B, int sh, int sw, int mode, float* dst, int H, int W,
                               cudaStream_t s);
+
+// Batched decode_detections (detections.cu): dets [B, rows, 6] -> per image
+// the rows with score not <= threshold, in order, at most capacity.
+cudaError_t launch_detections(const float* dets, int B, int rows, float threshold, int capacity, detection_t* out,
+                              int* counts, cudaStream_t s);
 
 // tcgen05 kernel (attn_tc.cu): kd = 32, hd = 64.
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);

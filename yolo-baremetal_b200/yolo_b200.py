@@ -39,12 +39,18 @@ EXPORTS = {
     "yb_cuda.h": ["yb_cuda_init", "yb_cuda_upload_weights", "yb_cuda_load_bin", "yb_cuda_forward",
                   "yb_cuda_set_int8", "yb_cuda_get_int8_stage", "yb_cuda_calibrate_int8",
                   "yb_cuda_int8_scale_entry", "yb_cuda_forward_rgb8", "yb_cuda_preprocess_rgb8",
+                  "yb_cuda_get_detections", "yb_cuda_detections",
                   "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_detect_topk_noalloc",
                   "yb_cuda_forward_sharded",
                   "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error"],
     "yb_int8.h": ["yb_int8_quantize_conv", "yb_int8_conv_create", "yb_int8_conv_ci_pad", "yb_int8_conv_run",
                   "yb_int8_conv_check", "yb_int8_conv_destroy"],
 }
+
+
+# detection_t (include/detection.h)
+DET_DTYPE = np.dtype([("x1", np.float32), ("y1", np.float32), ("x2", np.float32), ("y2", np.float32),
+                      ("score", np.float32), ("class_id", np.int32)])
 
 
 class YBError(RuntimeError):
@@ -108,6 +114,9 @@ def lib() -> C.CDLL:
                                           C.c_int, C.POINTER(C.c_int)]
         L.yb_cuda_destroy.argtypes = [C.c_void_p]
         L.yb_cuda_set_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.yb_cuda_get_detections.argtypes = [C.c_void_p, C.c_float, C.c_int, C.c_void_p, C.c_void_p]
+        L.yb_cuda_detections.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p, C.c_void_p,
+                                         C.c_void_p]
         L.yb_cuda_forward_rgb8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                            C.c_int, C.c_void_p, C.c_int]
         L.yb_cuda_preprocess_rgb8.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
@@ -243,6 +252,14 @@ class Model:
         check(lib().yb_cuda_forward_rgb8(self.ctx, x.ctypes.data, B, sh, sw, resize, H, W, dets.ctypes.data, max_det),
               "yb_cuda_forward_rgb8")
         return dets
+
+    def detections(self, batch: int, threshold: float = 0.25, capacity: int = 100):
+        """Detection lists of the last forward: (structured array [B, capacity], counts [B])."""
+        out = np.zeros((batch, capacity), dtype=DET_DTYPE)
+        counts = np.zeros(batch, dtype=np.int32)
+        check(lib().yb_cuda_get_detections(self.ctx, threshold, capacity, out.ctypes.data, counts.ctypes.data),
+              "yb_cuda_get_detections")
+        return out, counts
 
     def head(self, batch: int):
         """(logits [B,N,nc], boxes [B,N,4]) of the last forward."""
