@@ -3,17 +3,18 @@
 // memory, on the split activation format (value = hi + lo, kernels.h).
 //
 // One CTA of 128 threads per (128 queries, head, image); thread i owns query
-// row i (TMEM lane i).  Keys go in blocks of 128:
+// row i (TMEM lane i).  Keys go in blocks of 64 (72 KB of shared memory and
+// 128 TMEM columns, so three CTAs share an SM):
 //   pass 1  S = Q K^T as Qh Kh + Qh Kl + Ql Kh (6 UMMAs: 3 products x 2 K
 //           steps of 16) -> row maximum of S * kd^-0.5;
 //   pass 2  S again; p = exp(S * scale - max) (zero past the last key),
 //           l += p; p split into bf16 hi + lo, written as A operands;
-//           O += Ph Vh + Ph Vl + Pl Vh (3 products x 8 K steps, N 64).
+//           O += Ph Vh + Ph Vl + Pl Vh (3 products x 4 K steps, N 64).
 // Then out = O / l + the positional depthwise term of v (layers.c:373-395,
 // same summation order as the reference: bias, then taps ky, kx), split.
 // The omitted lo x lo products are below 2^-16 of each term, the precision of
-// the split format itself.  Tensor memory: S in columns [0, 128), O in
-// [128, 192).  Operands are K-major without swizzle (core matrices of 8 rows
+// the split format itself.  Tensor memory: S in columns [0, 64), O in
+// [64, 128).  Operands are K-major without swizzle (core matrices of 8 rows
 // x 16 bytes, 128 contiguous bytes each, row-group major).  One thread issues
 // the UMMAs; completion is one mbarrier every thread waits on with a bound
 // (a timeout sets the error word and ends the kernel after freeing TMEM).
@@ -29,7 +30,9 @@ namespace yb {
 namespace {
 
 constexpr int kTQ = 128;  // queries per CTA (UMMA M)
-constexpr int kTK = 128;  // keys per block
+constexpr int kTK = 64;   // keys per block
+constexpr uint32_t kOCol = kTK;  // TMEM column of O (S in [0, kTK))
+constexpr uint32_t kTmemCols = kTK + 64 <= 128 ? 128u : 256u;
 constexpr int TKD = 32, THD = 64;
 constexpr int kErrAttnWaitF = 8;
 
@@ -39,15 +42,15 @@ __device__ __forceinline__ uint32_t opo(int row, int kbyte, int kb) {
 
 struct AttnTcSmem {
   uint8_t qh[kTQ * TKD * 2], ql[kTQ * TKD * 2];    // A of S: 128 x 32 bf16
-  uint8_t kh[kTK * TKD * 2], kl[kTK * TKD * 2];    // B of S: 128 keys x 32 bf16
-  uint8_t vh[THD * kTK * 2], vl[THD * kTK * 2];    // B of O: 64 channels x 128 keys bf16
-  uint8_t ph[kTQ * kTK * 2], pl[kTQ * kTK * 2];    // A of O: 128 queries x 128 keys bf16
+  uint8_t kh[kTK * TKD * 2], kl[kTK * TKD * 2];    // B of S: 64 keys x 32 bf16
+  uint8_t vh[THD * kTK * 2], vl[THD * kTK * 2];    // B of O: 64 channels x 64 keys bf16
+  uint8_t ph[kTQ * kTK * 2], pl[kTQ * kTK * 2];    // A of O: 128 queries x 64 keys bf16
   uint64_t bar;
   uint32_t tmem;
   int abort;
 };
 
-__global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, int* err) {
+__global__ void __launch_bounds__(128, 3) attention_tc_kernel(const AttnArgs a, int* err) {
   extern __shared__ __align__(1024) uint8_t attn_tc_raw[];
   AttnTcSmem& S = *reinterpret_cast<AttnTcSmem*>(attn_tc_raw);
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -75,7 +78,7 @@ __global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, 
     mbar_fence_init();
   }
   if (warp == 0) {
-    tmem_alloc(&S.tmem, 256);
+    tmem_alloc(&S.tmem, kTmemCols);
     tmem_relinquish();
   }
   fence_proxy_async_smem();
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, 
     __syncthreads();
     tc_fence_after();
   };
-  // Keys [k0, k0 + 128) into kh / kl (zero past N); with_v also V^T.
+  // Keys [k0, k0 + kTK) into kh / kl (zero past N); with_v also V^T.
   auto stage = [&](int k0, bool with_v) {
     for (int i = tid; i < kTK * 4; i += 128) {
       const int j = i >> 2, c = i & 3;
@@ -108,12 +111,13 @@ __global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, 
       *reinterpret_cast<uint4*>(S.kl + opo(j, 16 * c, 2 * TKD)) = vl;
     }
     if (with_v) {
-      // Thread j transposes key j's 64 values into column j of V^T.
+      // Thread j < kTK transposes key j's 64 values into column j of V^T.
       const int j = tid;
       const bool in = k0 + j < N;
       const uint16_t* p = base + static_cast<long long>(in ? k0 + j : 0) * a.qkv.cstride + 2 * TKD;
 #pragma unroll
       for (int c = 0; c < THD / 8; ++c) {
+        if (j >= kTK) break;
         uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
         if (in) {
           vh = *reinterpret_cast<const uint4*>(p + 8 * c);
@@ -171,9 +175,9 @@ __global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, 
 #pragma unroll
       for (int s = 0; s < kTK / 16; ++s) {
         const uint64_t off = static_cast<uint64_t>(16 * s);
-        tc_mma_bf16(tbase + 128, ph + off, vh + off, idesc, (first && s == 0) ? 0u : 1u);
-        tc_mma_bf16(tbase + 128, ph + off, vl + off, idesc, 1u);
-        tc_mma_bf16(tbase + 128, plo + off, vh + off, idesc, 1u);
+        tc_mma_bf16(tbase + kOCol, ph + off, vh + off, idesc, (first && s == 0) ? 0u : 1u);
+        tc_mma_bf16(tbase + kOCol, ph + off, vl + off, idesc, 1u);
+        tc_mma_bf16(tbase + kOCol, plo + off, vh + off, idesc, 1u);
       }
       tc_commit(&S.bar);
     }
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, 
                  a.out.coff + h * THD;
   for (int d0 = 0; d0 < THD; d0 += 16) {
     uint32_t ov[16];
-    tc_ld_32x32b_x16(trow + 128 + d0, ov);
+    tc_ld_32x32b_x16(trow + kOCol + d0, ov);
     tc_wait_ld();
     if (!valid) continue;
 #pragma unroll
@@ -268,7 +272,7 @@ __global__ void __launch_bounds__(128, 1) attention_tc_kernel(const AttnArgs a, 
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tbase, 256);
+    tmem_dealloc(tbase, kTmemCols);
   }
 }
 
