@@ -271,6 +271,24 @@ cudaError_t Engine::conv_w(const std::string& prefix, bool plain, DevConv** out,
   return cudaSuccess;
 }
 
+cudaError_t Engine::conv_narrow(DevConv* d, int n_tile, const uint8_t** wpack) {
+  const int slot = n_tile == 64 ? 0 : 1;
+  if (!d->wpack_n[slot]) {
+    const std::string wn = d->name + (find(d->name + ".conv.weight") ? ".conv.weight" : ".weight");
+    const HostTensor* w = find(wn);
+    if (!w) return cudaErrorInvalidValue;
+    const size_t bytes = pack_conv_weights(w->data.data(), d->co, d->ci, d->kh, d->kw, n_tile, nullptr);
+    std::vector<uint8_t> pack(bytes);
+    pack_conv_weights(w->data.data(), d->co, d->ci, d->kh, d->kw, n_tile, pack.data());
+    cudaError_t e = dev_alloc(bytes, reinterpret_cast<void**>(&d->wpack_n[slot]));
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy(d->wpack_n[slot], pack.data(), bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return e;
+  }
+  *wpack = d->wpack_n[slot];
+  return cudaSuccess;
+}
+
 cudaError_t Engine::dw_w(const std::string& prefix, DevDw** out, std::string* why) {
   auto it = dws_.find(prefix);
   if (it != dws_.end()) {
@@ -391,6 +409,16 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     }
     a.wpack = w->wpack;
     a.bias = w->bias;
+    // Fewer than two waves of tiles: narrower N tiles (64 or 128 columns,
+    // im2col operand mode) so that more SMs share the work.
+    if (a.n_tiles * a.m_tiles < 2 * num_sms_ && w->co >= 128 && !fout.ptr) {
+      const int nt = a.m_tiles * ((w->co + 127) / 128) >= 2 * num_sms_ ? 128 : 64;
+      const uint8_t* wp = nullptr;
+      YB_TRY(conv_narrow(const_cast<DevConv*>(w), nt, &wp));
+      a.wpack = const_cast<uint8_t*>(wp);
+      a.n_tile = nt;
+      a.n_tiles = (w->co + nt - 1) / nt;
+    }
     a.act = act;
     a.out = out;
     a.out_f32 = fout;

@@ -31,6 +31,9 @@ struct DevConv {
   float* bias = nullptr;
   int co = 0, ci = 0, kh = 0, kw = 0;
   int n_tile = 0, n_tiles = 0, num_kc = 0, K = 0;
+  // The same weights packed in narrower N tiles (64 and 128 columns), for
+  // launches with too few M tiles to fill the SMs (packed on first use).
+  uint8_t* wpack_n[2] = {nullptr, nullptr};
 };
 struct DevDw {
   float* w = nullptr;  // [9][C]
@@ -153,6 +156,8 @@ class Engine {
  private:
   const HostTensor* find(const std::string& name) const;
   cudaError_t conv_w(const std::string& prefix, bool plain, DevConv** out, std::string* why);
+  // Packing of `d` in N tiles of n_tile (64 or 128) columns, created on first use.
+  cudaError_t conv_narrow(DevConv* d, int n_tile, const uint8_t** wpack);
   cudaError_t dw_w(const std::string& prefix, DevDw** out, std::string* why);
   cudaError_t dev_alloc(size_t bytes, void** p);
   cudaError_t build(Plan* p, std::string* why);
