@@ -222,6 +222,17 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
       return fail("int8: padded output must own its tensor: " + P);
     I8Tiling t;
     i8_tiling(co_pad, ci, k, k, &t);
+    {
+      // Fewer than two waves of tiles: narrower N tiles (64 or 128 columns)
+      // so that more SMs share the work.
+      const int ho = (in.H + 2 * pad - k) / stride + 1, wo = (in.W + 2 * pad - k) / stride + 1;
+      const long long mt = (static_cast<long long>(B) * ho * wo + 127) / 128;
+      if (mt * t.n_tiles < 2LL * sms && co_pad >= 128 && !f32.ptr) {
+        const int nt = mt * ((co_pad + 127) / 128) >= 2LL * sms ? 128 : 64;
+        t.n_tile = nt;
+        t.n_tiles = (co_pad + nt - 1) / nt;
+      }
+    }
     std::vector<int8_t> wpad(static_cast<size_t>(co_pad) * ci * k * k, 0);
     std::copy(q.wq.begin(), q.wq.end(), wpad.begin());
     const std::vector<uint8_t> pk = i8_pack_weights(wpad.data(), co_pad, ci, k, k, t);
