@@ -38,16 +38,17 @@ __global__ void quantize_input_kernel(const float* in, int B, int C, int H, int 
 // Tiles of 8 output rows x 16 P columns (P = 64 / CO pixels per thread), as
 // the fp32 stem: the fp32 input patch (3 channels x 17 rows x (32 P + 4)
 // columns from input column 2 * ox0 - 4) arrives by 16-byte asynchronous
-// copies into one of two buffers while the previous tile computes, is
-// quantised into one word per input pixel (channels 0..2 in bytes 0..2),
-// and each output is 9 dp4a of such a word with the packed weights.
+// copies, is quantised into one word per input pixel (channels 0..2 in
+// bytes 0..2), and the next tile's copy lands while each output is computed
+// as 9 dp4a of such words with the packed weights.  36 KB of shared memory:
+// five or six CTAs per SM hide each other's latency.
 template <int CO>
 struct StemI8Tile {
   static constexpr int P = 64 / CO;
   static constexpr int TW = 16 * P, TH = 8;
   static constexpr int PR = 2 * TH + 1, PC = 2 * TW + 4;
   static constexpr int kBuf = 3 * PR * PC;  // floats per fp32 patch
-  static constexpr int kSmem = (2 * kBuf + PR * PC + 9 * CO) * 4 + CO * 16 + CO * 8 + 256;
+  static constexpr int kSmem = (kBuf + PR * PC + 9 * CO) * 4 + CO * 16 + CO * 8 + 256;
 };
 
 template <int CO>
@@ -90,9 +91,24 @@ __device__ __forceinline__ void stem_i8_fetch(const StemI8Args& a, float* sx, in
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-__device__ __forceinline__ uint32_t quant_byte(float v, float s) {
-  const float q = rintf(__fdiv_rn(v, s));
-  return static_cast<uint32_t>(static_cast<int>(q < -127.f ? -127.f : q > 127.f ? 127.f : q)) & 0xFFu;
+// clamp(rint(v / s), -127, 127) as a byte, v / s correctly rounded.  With
+// r = fl(1 / s), y = fl(v * r) lies within 2^-15 of fl(v / s) for |y| <= 200,
+// so when y is further than 2^-12 from a half-integer both round to the same
+// integer, read from the mantissa of y + 1.5 * 2^23 (round half to even,
+// like rintf).  Otherwise (near a rounding boundary, large, or NaN) the exact
+// quotient is used.
+__device__ __forceinline__ uint32_t quant_byte(float v, float s, float r) {
+  const float y = __fmul_rn(v, r);
+  const float m = __fadd_rn(y, 12582912.0f);
+  const float d = __fsub_rn(y, __fsub_rn(m, 12582912.0f));
+  int q;
+  if (fabsf(y) <= 200.f && fabsf(d) < 0.49975586f) {
+    q = __float_as_int(m) - 0x4B400000;
+  } else {
+    const float e = rintf(__fdiv_rn(v, s));
+    q = static_cast<int>(e < -127.f ? -127.f : e > 127.f ? 127.f : e);
+  }
+  return static_cast<uint32_t>(min(max(q, -127), 127)) & 0xFFu;
 }
 
 template <int CO>
@@ -101,7 +117,7 @@ __global__ void __launch_bounds__(128) stem_i8_kernel(const StemI8Args a) {
   constexpr int P = T::P;
   extern __shared__ __align__(16) float stem_i8_smem[];
   float* sxb = stem_i8_smem;
-  uint32_t* sq = reinterpret_cast<uint32_t*>(stem_i8_smem + 2 * T::kBuf);  // [PR][PC] packed int8 pixels
+  uint32_t* sq = reinterpret_cast<uint32_t*>(stem_i8_smem + T::kBuf);  // [PR][PC] packed int8 pixels
   uint32_t* sw = sq + T::PR * T::PC;                                      // [9][CO]
   int4* sp = reinterpret_cast<int4*>(sw + 9 * CO);                        // {M, D lo, D hi, shift - 32}
   int2* sx2 = reinterpret_cast<int2*>(sp + CO);                           // {bias, shift}
@@ -121,19 +137,21 @@ __global__ void __launch_bounds__(128) stem_i8_kernel(const StemI8Args a) {
   const int tiles_x = (a.Wo + T::TW - 1) / T::TW, tiles_y = (a.Ho + T::TH - 1) / T::TH;
   const int total = a.B * tiles_x * tiles_y;
   const int r = tid >> 4, x0 = tid & 15;
-  int k = 0;
-  if (static_cast<int>(blockIdx.x) < total) stem_i8_fetch<CO>(a, sxb, blockIdx.x, tiles_x, tiles_y);
-  for (int t = blockIdx.x; t < total; t += gridDim.x, ++k) {
+  const float rcp = __frcp_rn(a.s_in);
+  // One fp32 staging buffer: once a tile is quantised, the next tile's copy
+  // goes into it and lands while this tile computes.
+  if (static_cast<int>(blockIdx.x) < total) {
+    stem_i8_fetch<CO>(a, sxb, blockIdx.x, tiles_x, tiles_y);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+  }
+  __syncthreads();
+  for (int t = blockIdx.x; t < total; t += gridDim.x) {
     const int tn = t + gridDim.x;
-    if (tn < total) stem_i8_fetch<CO>(a, sxb + ((k + 1) & 1) * T::kBuf, tn, tiles_x, tiles_y);
-    if (tn < total) asm volatile("cp.async.wait_group 1;" ::: "memory");
-    else asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    const float* sx = sxb + (k & 1) * T::kBuf;
     for (int i = tid; i < T::PR * T::PC; i += 128)
-      sq[i] = quant_byte(sx[i], a.s_in) | (quant_byte(sx[T::PR * T::PC + i], a.s_in) << 8) |
-              (quant_byte(sx[2 * T::PR * T::PC + i], a.s_in) << 16);
+      sq[i] = quant_byte(sxb[i], a.s_in, rcp) | (quant_byte(sxb[T::PR * T::PC + i], a.s_in, rcp) << 8) |
+              (quant_byte(sxb[2 * T::PR * T::PC + i], a.s_in, rcp) << 16);
     __syncthreads();
+    if (tn < total) stem_i8_fetch<CO>(a, sxb, tn, tiles_x, tiles_y);
     int acc[P][CO];
 #pragma unroll
     for (int j = 0; j < P; ++j)
@@ -215,7 +233,8 @@ __global__ void __launch_bounds__(128) stem_i8_kernel(const StemI8Args a) {
         }
       }
     }
-    __syncthreads();  // both buffers are refilled / rewritten next iteration
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // the next tile has landed; the patch is rewritten next iteration
   }
 }
 
@@ -443,7 +462,7 @@ cudaError_t launch_stem_i8(const StemI8Args& a, cudaStream_t st) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const unsigned grid = static_cast<unsigned>(tiles < 3LL * sms ? tiles : 3LL * sms);
+  const unsigned grid = static_cast<unsigned>(tiles < 6LL * sms ? tiles : 6LL * sms);
   if (a.Co == 16) return launch_pdl(stem_i8_kernel<16>, dim3(grid), dim3(128), StemI8Tile<16>::kSmem, st, a);
   if (a.Co == 32) return launch_pdl(stem_i8_kernel<32>, dim3(grid), dim3(128), StemI8Tile<32>::kSmem, st, a);
   return launch_pdl(stem_i8_kernel<64>, dim3(grid), dim3(128), StemI8Tile<64>::kSmem, st, a);
