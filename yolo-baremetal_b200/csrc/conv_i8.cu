@@ -351,6 +351,26 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
           const uint64_t da0 = kmajor_desc_noswizzle(smem_u32(stage0 + s * stage_bytes), kPatchChunk, kPatchW * 16);
           const uint64_t db0 = sw128_kmajor_desc(smem_u32(smem));
           const uint64_t chunk_units = chunk_bytes >> 4;
+          if (ci_pad == 16) {
+            // At most 16 input channels: two taps per 32-byte K step.  The A
+            // operand's second core matrix is the next tap's window (LBO =
+            // the distance between the two windows); the weights hold the
+            // two taps' 16 channels back to back (K ordered (tap, channel),
+            // 16 channels per tap).  Tap 8 pairs with zero weights.
+            const uint32_t pa = smem_u32(stage0 + s * stage_bytes);
+            for (int s2 = 0; s2 < 5; ++s2) {
+              const int t0 = 2 * s2, t1 = t0 + 1 < 9 ? t0 + 1 : t0;
+              const uint32_t o0 = static_cast<uint32_t>(((t0 / 3) * kPatchW + t0 % 3) * 16);
+              const uint32_t o1 = static_cast<uint32_t>(((t1 / 3) * kPatchW + t1 % 3) * 16);
+              const uint64_t da = kmajor_desc_noswizzle(pa + o0, t1 == t0 ? 16u : o1 - o0, kPatchW * 16);
+              const int k = 32 * s2;
+              const uint64_t boff = static_cast<uint64_t>(k / kKB) * chunk_units + static_cast<uint64_t>(((k % kKB) / 32) * 2);
+              tc_mma_i8(d_tmem, da, db0 + boff, idesc, s2 != 0 ? 1u : 0u);
+            }
+            tc_commit(&empty[s]);
+            tc_commit(&acc_full[acc]);
+            continue;
+          }
           int step = 0;
           for (int tap = 0; tap < 9; ++tap) {
             const uint64_t toff = static_cast<uint64_t>((tap / 3) * kPatchW + tap % 3);  // window shift
@@ -590,6 +610,14 @@ int stages_for_i8(int n_tile, int n_tiles) {
 
 }  // namespace
 
+void i8_tiling_pair(int co, I8Tiling* t) {
+  i8_tiling(co, 16, 3, 3, t);
+  t->ci_pad = 16;
+  t->a_cpp = 16;
+  t->K = 9 * 16;
+  t->num_kc = (t->K + kKB - 1) / kKB;
+}
+
 void i8_tiling(int co, int ci, int kh, int kw, I8Tiling* t) {
   const int taps = kh * kw;
   if (taps == 1) {
@@ -650,11 +678,12 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
   }
   const int tail = 512 + 20 * a.n_tile * a.n_tiles + 1024 + 256;
   const int ci_pad = a.K / (a.kh * a.kw);
-  // Patch mode: 3x3 stride 1 pad 1, one N tile, 32 or 64 padded input
-  // channels, enough room for three stages next to the resident weights.
+  // Patch mode: 3x3 stride 1 pad 1, one N tile, 16 (two taps per K step),
+  // 32 or 64 padded input channels, enough room for three stages next to
+  // the resident weights.  16 padded channels exist only in patch mode.
   a.patch = 0;
   if (a.kh == 3 && a.kw == 3 && a.stride == 1 && a.pad == 1 && a.Ho == a.H && a.Wo == a.W && a.n_tiles == 1 &&
-      (ci_pad == 32 || ci_pad == 64) && a.K == 9 * ci_pad && a.n_tile <= 128) {
+      (ci_pad == 16 || ci_pad == 32 || ci_pad == 64) && a.K == 9 * ci_pad && a.n_tile <= 128) {
     const int wres = a.num_kc * a.n_tile * 128;
     const int pst = static_cast<int>(patch_stage_bytes_i8(ci_pad));
     int st = (kSmemLimit - 1024 - wres - tail) / pst;
@@ -681,6 +710,10 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
         return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, st);
       }
     }
+  }
+  if (ci_pad == 16) {
+    if (why) *why = "int8 conv: 16-channel K layout needs patch mode";
+    return cudaErrorInvalidValue;
   }
   const auto enc = i8_im2col_encoder();
   if (!enc) {

@@ -221,8 +221,9 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     if (!f32.ptr && co_pad != co && (out.c0 != 0 || out.cstride != co_pad))
       return fail("int8: padded output must own its tensor: " + P);
     I8Tiling t;
-    i8_tiling(co_pad, ci, k, k, &t);
-    {
+    if (k == 3 && stride == 1 && pad == 1 && ci <= 16 && co_pad <= 128 && !f32.ptr) i8_tiling_pair(co_pad, &t);
+    else i8_tiling(co_pad, ci, k, k, &t);
+    if (t.ci_pad != 16) {
       // Fewer than two waves of tiles: narrower N tiles (64 or 128 columns)
       // so that more SMs share the work.
       const int ho = (in.H + 2 * pad - k) / stride + 1, wo = (in.W + 2 * pad - k) / stride + 1;

@@ -50,6 +50,9 @@ struct I8Tiling {
   int ci_pad = 0, a_cpp = 0, K = 0, num_kc = 0, n_tile = 0, n_tiles = 0;
 };
 void i8_tiling(int co, int ci, int kh, int kw, I8Tiling* t);
+// 3x3 stride-1 convolutions of at most 16 input channels in patch mode: K
+// ordered (tap, channel) with 16 channels per tap, two taps per UMMA.
+void i8_tiling_pair(int co, I8Tiling* t);
 // wq [co][ci][kh][kw] -> per N tile and K chunk, n_tile 128-byte rows,
 // 128B-swizzled (what the kernel's bulk copies load).
 std::vector<uint8_t> i8_pack_weights(const int8_t* wq, int co, int ci, int kh, int kw, const I8Tiling& t);
