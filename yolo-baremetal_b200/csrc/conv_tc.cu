@@ -542,6 +542,35 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           const uint64_t dbh0 = sw128_kmajor_desc(smem_u32(smem));
           const uint64_t dbl0 = sw128_kmajor_desc(smem_u32(smem) + static_cast<uint32_t>(a.n_tile) * 128u);
           const uint64_t chunk_units = chunk_bytes >> 4;
+          if (a.Ci == 8) {
+            // Eight input channels (16 bytes per pixel and plane): two taps
+            // per 16-wide K step.  The A operand's second core matrix is the
+            // next tap's window (LBO = the distance between the windows);
+            // K is ordered (tap, channel) with 8 channels per tap, so the
+            // weights already hold the two taps back to back.  Tap 8 pairs
+            // with zero weights.
+            for (int s2 = 0; s2 < 5; ++s2) {
+              const int t0 = 2 * s2, t1 = t0 + 1 < 9 ? t0 + 1 : t0;
+              const uint32_t o0 = static_cast<uint32_t>(((t0 / 3) * kPatchW + t0 % 3) * 16);
+              const uint32_t o1 = static_cast<uint32_t>(((t1 / 3) * kPatchW + t1 % 3) * 16);
+              const uint32_t lbo = t1 == t0 ? 16u : o1 - o0;
+              const uint64_t dah = kmajor_desc_noswizzle(pa + o0, lbo, kPatchW * 16);
+              const uint64_t dal = kmajor_desc_noswizzle(pa + kPatchChunk + o0, lbo, kPatchW * 16);
+              const uint64_t boff = static_cast<uint64_t>(s2 >> 2) * chunk_units + static_cast<uint64_t>((s2 & 3) * 2);
+              const uint32_t accum = s2 != 0 ? 1u : 0u;
+              if (stacked) {
+                tc_mma_bf16(d_tmem, dah, dbh0 + boff, idesc, accum);
+                tc_mma_bf16(d_tmem, dal, dbh0 + boff, idesc, 1u);
+              } else {
+                tc_mma_bf16(d_tmem, dah, dbh0 + boff, idesc, accum);
+                tc_mma_bf16(d_tmem, dah, dbl0 + boff, idesc, 1u);
+                tc_mma_bf16(d_tmem, dal, dbh0 + boff, idesc, 1u);
+              }
+            }
+            tc_commit(&empty[s]);
+            tc_commit(&acc_full[acc]);
+            continue;
+          }
           int step = 0;
           for (int ky = 0; ky < 3; ++ky) {
             for (int kx = 0; kx < 3; ++kx) {
@@ -787,7 +816,8 @@ int conv_stages(const ConvArgs& a) {
 
 bool conv_setup_patch(ConvArgs* a) {
   if (a->kh != 3 || a->kw != 3 || a->stride != 1 || a->pad != 1) return false;
-  if (a->lg_up0 || a->lg_up1 || a->c_split != a->Ci || a->Ci % 16 || !a->src0.hi || a->n_tiles != 1) return false;
+  if (a->lg_up0 || a->lg_up1 || a->c_split != a->Ci || (a->Ci % 16 && a->Ci != 8) || !a->src0.hi || a->n_tiles != 1)
+    return false;
   if (a->K != 9 * a->Ci || a->Ho != a->H || a->Wo != a->W) return false;
   ConvArgs t = *a;
   t.a_tma = 2;
@@ -838,7 +868,7 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
   if ((a.lg_up0 || a.lg_up1) && (a.kh != 1 || a.kw != 1 || a.stride != 1 || a.pad != 0))
     return cudaErrorInvalidValue;
   if (a.n_tiles < 1 || a.n_tile * a.n_tiles < a.Co) return cudaErrorInvalidValue;
-  if (a.a_tma == 2 && (a.n_tiles != 1 || a.kh != 3 || a.kw != 3 || a.Ci % 16 || a.tiles_x < 1 || a.tiles_y < 1 ||
+  if (a.a_tma == 2 && (a.n_tiles != 1 || a.kh != 3 || a.kw != 3 || (a.Ci % 16 && a.Ci != 8) || a.tiles_x < 1 || a.tiles_y < 1 ||
                        a.m_tiles != a.B * a.tiles_y * a.tiles_x))
     return cudaErrorInvalidValue;
   const int stages = conv_stages(a);
