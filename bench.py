@@ -56,29 +56,69 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """SM clocks and throttle reasons while the timed region runs.
+
+    Reads NVML in a background thread every 10 ms (read-only queries), so
+    even a timed region of a few hundred milliseconds gets dozens of samples;
+    falls back to `nvidia-smi -lms 100` when NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits.
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
     def __init__(self, bus_id: str | None):
         self.bus_id = bus_id
         self.proc = None
         self.out = None
+        self.thread = None
+        self.stop = None
+        self.rows = []  # (sm_mhz, max_mhz, reason bits)
+
+    def _nvml_loop(self, nv, h):
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.rows.append((float(sm), float(mx), int(fn(h))))
+            except Exception:
+                pass
+            self.stop.wait(0.01)
 
     def __enter__(self):
+        if not self.bus_id:
+            return self
+        try:
+            import threading
+
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByPciBusId(self.bus_id.encode())
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
-            if self.bus_id:
-                cmd += ["-i", self.bus_id]
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                   "-i", self.bus_id]
             self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)  # let the first sample land before the timed region starts
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
+        if self.thread:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc:
             self.proc.terminate()
             try:
@@ -87,27 +127,38 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if not self.out:
-            return None
-        try:
-            rows = [r.split(",") for r in open(self.out.name).read().strip().splitlines() if r.strip()]
-            os.unlink(self.out.name)
-        except Exception:
-            return None
         sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = max(mx, float(r[2]))
-                for i, n in enumerate(names):
-                    if r[5 + i].strip().lower().startswith("active"):
+        if self.thread:
+            for s, m, bits in self.rows:
+                sm.append(s)
+                mx = max(mx, m)
+                for n, b in self.REASON_BITS.items():
+                    if bits & b:
                         reasons.add(n)
+            source = "nvml"
+        else:
+            if not self.out:
+                return None
+            try:
+                rows = [r.split(",") for r in open(self.out.name).read().strip().splitlines() if r.strip()]
+                os.unlink(self.out.name)
             except Exception:
-                continue
+                return None
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for r in rows:
+                try:
+                    sm.append(float(r[1]))
+                    mx = max(mx, float(r[2]))
+                    for i, n in enumerate(names):
+                        if r[5 + i].strip().lower().startswith("active"):
+                            reasons.add(n)
+                except Exception:
+                    continue
+            source = "nvidia-smi"
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": source}
 
 
 def bus_id_of(dev: int):
@@ -482,13 +533,15 @@ def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_o
     torch.cuda.synchronize()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        model.forward_device(d_in, d_out, B, H, H, 300, stream.cuda_stream)
-    ev1.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(bus_id_of(torch.cuda.current_device()) if rank == 0 else None) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            model.forward_device(d_in, d_out, B, H, H, 300, stream.cuda_stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
     barrier()
     dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    clocks = clk.summary() if rank == 0 else None
     # End to end (pipelined 16-image sub-batches, pinned host buffers).
     for _ in range(max(1, args.warmup // 2)):
         yb.check(L.yb_cuda_forward(model.ctx, host_in.data_ptr(), B, H, H, host_out.data_ptr(), 300, None, None,
@@ -547,6 +600,7 @@ def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_o
                             "d2h_bytes_per_step": world * host_out.numel() * 4},
                "batch1": {"ms_per_image": b1_ms, "images_per_s": world / (b1_ms * 1e-3),
                           "note": "device-resident single-image forward, one per GPU"},
+               "clocks": clocks,
                "gpu_launches": n_ops.value * args.steps,
                "conv_tops": {"achieved": tops, "peak_nominal": INT8_PEAK_TOPS_NOMINAL,
                              "frac_of_nominal": tops / INT8_PEAK_TOPS_NOMINAL,

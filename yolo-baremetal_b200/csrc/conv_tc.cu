@@ -143,6 +143,18 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     tmem_alloc(tmem_slot, ncols);
     tmem_relinquish();
   }
+  if (patch && a.Ci == 8) {
+    // The paired K step of tap 8 reads the pixel after its window (against
+    // zero weights); for the last patch row that is the pad after the box,
+    // which no copy writes.  Zero it so that stale bytes (possibly NaN or
+    // Inf as bf16) cannot turn the zero products into NaN.
+    const int pads = stages * 2;  // per stage: the hi and lo chunk
+    for (int i = threadIdx.x; i < pads * 4; i += kThreads) {
+      uint8_t* pad = stage0 + (i >> 3) * stage_bytes + ((i >> 2) & 1) * kPatchChunk + kPatchBox + (i & 3) * 16;
+      *reinterpret_cast<uint4*>(pad) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

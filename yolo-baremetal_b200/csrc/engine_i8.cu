@@ -332,9 +332,9 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
       const float sc = in.scale(c);
       QWeights q;
       if (!quantize(wc, b ? &bc : nullptr, &sc, s_pre, &q)) return fail("int8: depthwise ratio " + P);
-      // Taps 0-3, 4-7 and 8 packed into words (byte k = tap 4 * word + k).
+      // One word per filter row: wt[ky][c] byte kx = tap (ky, kx).
       for (int k = 0; k < 9; ++k)
-        wt[static_cast<size_t>(k / 4) * C + c] |= (static_cast<uint32_t>(q.wq[k]) & 0xFFu) << (8 * (k % 4));
+        wt[static_cast<size_t>(k / 3) * C + c] |= (static_cast<uint32_t>(q.wq[k]) & 0xFFu) << (8 * (k % 3));
       bq[c] = q.bq[0];
       mu[c] = q.mult[0];
       sh[c] = q.shift[0];

@@ -61,9 +61,10 @@ struct StemI8Args {
 cudaError_t launch_stem_i8(const StemI8Args& a, cudaStream_t st);
 cudaError_t init_stem_i8_attributes();
 cudaError_t launch_maxpool_i8(I8View in, I8View out, int B, int H, int W, int C, int k, cudaStream_t st);
-// Depthwise 3x3 pad 1; wp: [3][C] words of packed int8 taps (taps 0-3,
-// 4-7, and 8 in the low byte), bq / mult / shift per channel, lut nullable.
-cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const uint32_t* wp, const int32_t* bq,
+// Depthwise 3x3 pad 1; wr: [3][C] words of packed int8 taps, one per filter
+// row (byte kx of wr[ky][c] = tap (ky, kx)), bq / mult / shift per channel,
+// lut nullable.
+cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const uint32_t* wr, const int32_t* bq,
                             const int32_t* mult, const int32_t* shift, const int8_t* lut, cudaStream_t st);
 cudaError_t launch_concat_i8(I8View s0, int c0, int lg0, I8View s1, int c1, int B, int H, int W, I8View out,
                              cudaStream_t st);

@@ -5,6 +5,7 @@
 // accesses) at a time.  Summation orders follow the reference loops so that
 // results stay within a few ulps of it.
 #include <cfloat>
+#include <climits>
 #include "pdl.cuh"
 #include "kernels.h"
 #include "split.cuh"
@@ -178,53 +179,101 @@ __global__ void __launch_bounds__(128) stem_kernel(const StemArgs a) {
 }
 
 // ------------------------------------------------------------- depthwise 3x3
-// w is [9][C] (tap-major, transposed on the host); 8 channels per thread.
-__global__ void dw3x3_kernel(const DwArgs a) {
+// w is [9][C] (tap-major, transposed on the host).  A thread computes 2
+// channels of R consecutive output rows of one column: the 3 x 3 window
+// slides down the strip, so each input row (three pixels, hi and lo planes)
+// is loaded once and serves three outputs; weights and bias stay in
+// registers, and all loads of the strip are in flight together.
+// Out-of-image taps are skipped, not added as zeros: the sum is the
+// reference's (bias, then the taps in (ky, kx) order, every product and sum
+// rounded on its own).
+template <int R>
+__global__ void __launch_bounds__(256, 2) dw3x3_kernel(const DwArgs a) {
+  // 32-bit indexing: the launcher checks that threads and per-image offsets fit.
+  const int C2 = a.C >> 1;
+  const int strips = (a.H + R - 1) / R;
+  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= a.B * strips * a.W * C2) return;
+  const int c = (idx % C2) * 2;
+  int r = idx / C2;
+  const int x = r % a.W;
+  r /= a.W;
+  const int strip = r % strips;
+  const int b = r / strips;
+  float wk[9][2], bias[2] = {0.f, 0.f};
+#pragma unroll
+  for (int t = 0; t < 9; ++t) {
+    const float2 w2 = __ldg(reinterpret_cast<const float2*>(a.w + t * a.C + c));
+    wk[t][0] = w2.x;
+    wk[t][1] = w2.y;
+  }
+  if (a.bias) {
+    const float2 b2 = __ldg(reinterpret_cast<const float2*>(a.bias + c));
+    bias[0] = b2.x;
+    bias[1] = b2.y;
+  }
   pdl_wait();
-  const int C8 = a.C >> 3;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(a.B) * a.H * a.W * C8;
-  if (idx >= total) return;
-  const int c = static_cast<int>(idx % C8) * 8;
-  const long long pix = idx / C8;
-  const int b = static_cast<int>(pix / (a.H * a.W));
-  const int p = static_cast<int>(pix - static_cast<long long>(b) * a.H * a.W);
-  const int y = p / a.W, x = p - (p / a.W) * a.W;
-  float s[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) s[e] = a.bias ? __ldg(a.bias + c + e) : 0.f;
+  const bool cl = x > 0, cr = x < a.W - 1;
   const uint16_t* base = a.in.hi + vaddr(a.in, b, 0) + c;
+  const int y0 = strip * R;
+  // Every load of the strip (R + 2 rows x 3 pixels, both planes) is issued
+  // before the first sum; each value is joined (hi + lo) once.
+  uint32_t rh[R + 2][3], rl[R + 2][3];
 #pragma unroll
-  for (int ky = 0; ky < 3; ++ky) {
-    const int iy = y - 1 + ky;
-    if (iy < 0 || iy >= a.H) continue;
+  for (int k = 0; k < R + 2; ++k) {
+    const int iy = y0 - 1 + k;
+    const bool ok = iy >= 0 && iy < a.H;
+    const uint16_t* p = base + (iy * a.W + x - 1) * a.in.cstride;
 #pragma unroll
     for (int kx = 0; kx < 3; ++kx) {
-      const int ix = x - 1 + kx;
-      if (ix < 0 || ix >= a.W) continue;
-      float v[8];
-      load8(base + static_cast<long long>(iy * a.W + ix) * a.in.cstride, a.in.plane, v);
-      const float* w = a.w + (ky * 3 + kx) * a.C + c;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) s[e] = __fadd_rn(s[e], __fmul_rn(v[e], __ldg(w + e)));
+      const bool in = ok && (kx == 0 ? cl : kx == 2 ? cr : true);
+      rh[k][kx] = in ? __ldg(reinterpret_cast<const uint32_t*>(p + kx * a.in.cstride)) : 0u;
+      rl[k][kx] = in ? __ldg(reinterpret_cast<const uint32_t*>(p + kx * a.in.cstride + a.in.plane)) : 0u;
     }
   }
-  float mpre = 0.0f;
-  if (a.amax) {
+  float v[R + 2][3][2];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) mpre = fmaxf(mpre, fabsf(s[e]));
-  }
-  if (a.act == kActSiLU) {
+  for (int k = 0; k < R + 2; ++k) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) s[e] = silu(s[e]);
+    for (int kx = 0; kx < 3; ++kx) {
+      v[k][kx][0] = bf16_bits_to_f(rh[k][kx] & 0xFFFFu) + bf16_bits_to_f(rl[k][kx] & 0xFFFFu);
+      v[k][kx][1] = bf16_bits_to_f(rh[k][kx] >> 16) + bf16_bits_to_f(rl[k][kx] >> 16);
+    }
   }
-  store8(a.out.hi + vaddr(a.out, b, p) + c, a.out.plane, s);
-  if (a.amax) {
-    float mout = 0.0f;
+  float mpre = 0.0f, mout = 0.0f;
+  uint16_t* ob = a.out.hi + vaddr(a.out, b, 0) + c;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) mout = fmaxf(mout, fabsf(s[e]));
-    amax_warp(a.amax, mpre, mout);
+  for (int i = 0; i < R; ++i) {
+    const int y = y0 + i;
+    if (y >= a.H) break;
+    const bool rok[3] = {y > 0, true, y < a.H - 1};
+    float s[2] = {bias[0], bias[1]};
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        const bool ok = rok[ky] && (kx == 0 ? cl : kx == 2 ? cr : true);
+        const float p0 = __fmul_rn(v[i + ky][kx][0], wk[ky * 3 + kx][0]);
+        const float p1 = __fmul_rn(v[i + ky][kx][1], wk[ky * 3 + kx][1]);
+        if (ok) {
+          s[0] = __fadd_rn(s[0], p0);
+          s[1] = __fadd_rn(s[1], p1);
+        }
+      }
+    }
+    if (a.amax) mpre = fmaxf(mpre, fmaxf(fabsf(s[0]), fabsf(s[1])));
+    if (a.act == kActSiLU) {
+      s[0] = silu_fast(s[0]);
+      s[1] = silu_fast(s[1]);
+    }
+    uint32_t hw, lw;
+    split2(s[0], s[1], hw, lw);
+    uint16_t* o = ob + (y * a.W + x) * a.out.cstride;
+    *reinterpret_cast<uint32_t*>(o) = hw;
+    *reinterpret_cast<uint32_t*>(o + a.out.plane) = lw;
+    if (a.amax) mout = fmaxf(mout, fmaxf(fabsf(s[0]), fabsf(s[1])));
   }
+  if (a.amax) amax_warp(a.amax, mpre, mout);
 }
 
 // ------------------------------------------------------------- calibration
@@ -455,9 +504,24 @@ cudaError_t launch_absmax_f32(const float* x, long long n, unsigned* amax, cudaS
 }
 
 cudaError_t launch_dwconv3x3(const DwArgs& a, cudaStream_t s) {
-  if (a.C % 8) return cudaErrorInvalidValue;
-  const long long total = static_cast<long long>(a.B) * a.H * a.W * (a.C / 8);
-  return launch_pdl(dw3x3_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, s, a);
+  // 4-byte loads and stores of 2 channels per plane; float2 weight pairs.
+  if (a.C % 2 || a.in.cstride % 2 || a.in.coff % 2 || a.in.bstride % 2 || a.in.plane % 2 || a.out.cstride % 2 ||
+      a.out.coff % 2 || a.out.bstride % 2 || a.out.plane % 2 || reinterpret_cast<uintptr_t>(a.in.hi) % 4 ||
+      reinterpret_cast<uintptr_t>(a.out.hi) % 4 || reinterpret_cast<uintptr_t>(a.w) % 8 ||
+      reinterpret_cast<uintptr_t>(a.bias) % 8)
+    return cudaErrorInvalidValue;
+  if (a.B <= 0 || a.H <= 0 || a.W <= 0 || a.C <= 0) return cudaSuccess;
+  // 32-bit thread indices and per-image element offsets.
+  if (static_cast<long long>(a.B) * ((a.H + 3) / 4) * a.W * (a.C / 2) + 256 > INT_MAX ||
+      static_cast<long long>(a.H) * a.W * a.in.cstride > INT_MAX ||
+      static_cast<long long>(a.H) * a.W * a.out.cstride > INT_MAX)
+    return cudaErrorInvalidValue;
+  if (a.H >= 40) {
+    const long long total = static_cast<long long>(a.B) * ((a.H + 7) / 8) * a.W * (a.C / 2);
+    return launch_pdl(dw3x3_kernel<8>, dim3(blocks_for(total, 256)), dim3(256), 0, s, a);
+  }
+  const long long total = static_cast<long long>(a.B) * ((a.H + 3) / 4) * a.W * (a.C / 2);
+  return launch_pdl(dw3x3_kernel<4>, dim3(blocks_for(total, 256)), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {

@@ -15,7 +15,6 @@ namespace {
 __device__ __forceinline__ long long rne(long long p, int sh) {
   return (p + ((1LL << (sh - 1)) - 1) + ((p >> sh) & 1)) >> sh;
 }
-__device__ __forceinline__ int clamp127(long long v) { return static_cast<int>(v < -127 ? -127 : v > 127 ? 127 : v); }
 
 inline unsigned blocks_for(long long n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
 
@@ -277,11 +276,14 @@ __global__ void maxpool_i8_kernel(I8View in, I8View out, int B, int H, int W, in
 
 // ------------------------------------------------------- depthwise 3x3
 // y = rne((bq + sum x*wq) * mult, shift), then the SiLU table (lut != null)
-// or clamp to [-127, 127].  16 channels of one pixel per thread.  The taps
-// of one channel are gathered four at a time into one word (a 4 x 4 byte
-// transpose of four tap vectors) and summed with dp4a against the weights
-// packed the same way on the host: wp[0][c] = taps 0-3, wp[1][c] = taps 4-7,
-// wp[2][c] = tap 8 (low byte).  The sum fits int32 (|sum| <= 9 * 128 * 127);
+// or clamp to [-127, 127].  A thread computes 4 channels of R consecutive
+// output rows of one column.  Each input row's three pixels x-1, x, x+1 (one
+// word of 4 channels each) are transposed once into 4 per-channel words
+// (byte kx = pixel x-1+kx) and serve the outputs above, at and below the row,
+// each of which is then 3 dp4a per channel against the weights packed the
+// same way on the host: wr[ky][c] byte kx = wq[c][ky][kx].  Pixels outside
+// the image are zero words; all loads of a strip are in flight together.
+// The sum fits int32 (|sum| <= 9 * 128 * 127);
 // the requantisation is sum * M + (bq * M + 2^(sh-1) - 1) >> sh, redone in
 // 64 bits for shifts below 32 or a possible tie (low word all ones).
 __device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t (&y)[4]) {
@@ -293,79 +295,95 @@ __device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, u
   y[3] = __byte_perm(t1, t3, 0x7632);
 }
 
+template <int R>
 __global__ void __launch_bounds__(256) dw3x3_i8_kernel(I8View in, I8View out, int B, int H, int W, int C,
-                                                       const uint32_t* wp, const int32_t* bq, const int32_t* mult,
+                                                       const uint32_t* wr, const int32_t* bq, const int32_t* mult,
                                                        const int32_t* shift, const int8_t* lut) {
-  extern __shared__ __align__(16) int4 dw_rec[];  // [C] {M, D lo, D hi, sh - 32}
-  int8_t* slut = reinterpret_cast<int8_t*>(dw_rec + C);
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    const int m = mult[i], b0 = bq[i];
-    const int sh = m == 0 ? 32 : shift[i];
-    const long long d = static_cast<long long>(b0) * m + ((1LL << (sh - 1)) - 1);
-    dw_rec[i] = make_int4(m, static_cast<int>(static_cast<unsigned long long>(d) & 0xFFFFFFFFull),
-                          static_cast<int>(d >> 32), sh - 32);
-  }
+  __shared__ int8_t slut[256];
   for (int i = threadIdx.x; i < 256; i += blockDim.x) slut[i] = lut ? lut[i] : 0;
   __syncthreads();
+  // 32-bit indexing: the launcher checks that threads and per-image offsets fit.
+  const int C4 = C >> 2;
+  const int strips = (H + R - 1) / R;
+  const int idx = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= B * strips * W * C4) return;
+  const int c = (idx % C4) * 4;
+  int r = idx / C4;
+  const int x = r % W;
+  r /= W;
+  const int strip = r % strips;
+  const int b = r / strips;
+  uint32_t wk[3][4];
+#pragma unroll
+  for (int ky = 0; ky < 3; ++ky) {
+    const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(wr + ky * C + c));
+    wk[ky][0] = w4.x;
+    wk[ky][1] = w4.y;
+    wk[ky][2] = w4.z;
+    wk[ky][3] = w4.w;
+  }
+  int M[4], sx[4];
+  long long D[4];
+  bool fast = true;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int m = __ldg(mult + c + e);
+    const int sh = m == 0 ? 32 : __ldg(shift + c + e);
+    M[e] = m;
+    sx[e] = sh - 32;
+    fast = fast && sh >= 32;
+    D[e] = static_cast<long long>(__ldg(bq + c + e)) * m + ((1LL << (sh - 1)) - 1);
+  }
   pdl_wait();
-  const int C16 = C >> 4;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(B) * H * W * C16;
-  if (idx >= total) return;
-  const int c = static_cast<int>(idx % C16) * 16;
-  const long long pix = idx / C16;
-  const int b = static_cast<int>(pix / (static_cast<long long>(H) * W));
-  const int p = static_cast<int>(pix - static_cast<long long>(b) * H * W);
-  const int y = p / W, x = p - (p / W) * W;
+  const bool cl = x > 0, cr = x < W - 1;
+  const int y0 = strip * R;
   const int8_t* ib = in.p + b * in.bstride + c;
-  uint4 v[9];
+  // Every load of the strip is issued before the first sum (R + 2 rows x 3
+  // pixels in flight per thread), then each row is transposed once.
+  uint32_t raw[R + 2][3];
 #pragma unroll
-  for (int t = 0; t < 9; ++t) {
-    const int iy = y - 1 + t / 3, ix = x - 1 + t % 3;
-    v[t] = (iy >= 0 && iy < H && ix >= 0 && ix < W)
-               ? *reinterpret_cast<const uint4*>(ib + static_cast<long long>(iy * W + ix) * in.cstride)
-               : make_uint4(0u, 0u, 0u, 0u);
+  for (int k = 0; k < R + 2; ++k) {
+    const int iy = y0 - 1 + k;
+    const bool ok = iy >= 0 && iy < H;
+    const int8_t* rp = ib + (iy * W + x - 1) * static_cast<int>(in.cstride);
+    raw[k][0] = ok && cl ? __ldg(reinterpret_cast<const uint32_t*>(rp)) : 0u;
+    raw[k][1] = ok ? __ldg(reinterpret_cast<const uint32_t*>(rp + in.cstride)) : 0u;
+    raw[k][2] = ok && cr ? __ldg(reinterpret_cast<const uint32_t*>(rp + 2 * in.cstride)) : 0u;
   }
-  int sum[16];
+  uint32_t v[R + 2][4];
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {  // channels 4g .. 4g+3
-    const auto word = [&](int t) {
-      return g == 0 ? v[t].x : g == 1 ? v[t].y : g == 2 ? v[t].z : v[t].w;
-    };
-    uint32_t y0[4], y1[4];
-    transpose4(word(0), word(1), word(2), word(3), y0);
-    transpose4(word(4), word(5), word(6), word(7), y1);
-    const uint32_t w8 = word(8);
+  for (int k = 0; k < R + 2; ++k) transpose4(raw[k][0], raw[k][1], raw[k][2], 0u, v[k]);
+  int8_t* ob = out.p + b * out.bstride + c;
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const int y = y0 + i;
+    if (y >= H) break;
+    int acc[4], o[4];
+    bool exact = !fast;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int ch = c + 4 * g + e;
-      int acc = __dp4a(static_cast<int>(y0[e]), static_cast<int>(__ldg(wp + ch)), 0);
-      acc = __dp4a(static_cast<int>(y1[e]), static_cast<int>(__ldg(wp + C + ch)), acc);
-      const int x8 = static_cast<int>(static_cast<int8_t>((w8 >> (8 * e)) & 0xFFu));
-      acc += x8 * static_cast<int>(static_cast<int8_t>(__ldg(wp + 2 * C + ch) & 0xFFu));
-      sum[4 * g + e] = acc;
+      acc[e] = __dp4a(static_cast<int>(v[i][e]), static_cast<int>(wk[0][e]), 0);
+      acc[e] = __dp4a(static_cast<int>(v[i + 1][e]), static_cast<int>(wk[1][e]), acc[e]);
+      acc[e] = __dp4a(static_cast<int>(v[i + 2][e]), static_cast<int>(wk[2][e]), acc[e]);
+      const long long pr = static_cast<long long>(acc[e]) * M[e] + D[e];
+      exact = exact || static_cast<unsigned>(pr) == 0xFFFFFFFFu;
+      o[e] = static_cast<int>(pr >> 32) >> (sx[e] & 31);
     }
-  }
-  uint32_t ow[4];
+    if (__builtin_expect(exact, 0)) {
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    int o[4];
+      for (int e = 0; e < 4; ++e) {
+        const long long yv = rne((static_cast<long long>(acc[e]) + __ldg(bq + c + e)) * M[e], sx[e] + 32);
+        o[e] = static_cast<int>(yv < -128 ? -128 : yv > 127 ? 127 : yv);
+      }
+    }
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int ch = c + 4 * g + e;
-      const int4 q = dw_rec[ch];
-      const long long d = (static_cast<long long>(q.z) << 32) | static_cast<unsigned>(q.y);
-      const long long pr = static_cast<long long>(sum[4 * g + e]) * q.x + d;
-      long long yv;
-      if (q.w >= 0 && static_cast<unsigned>(pr) != 0xFFFFFFFFu) yv = static_cast<int>(pr >> 32) >> q.w;
-      else yv = rne((static_cast<long long>(sum[4 * g + e]) + bq[ch]) * q.x, q.w + 32);
-      if (lut) o[e] = slut[(yv < -128 ? -128 : yv > 127 ? 127 : yv) + 128];
-      else o[e] = clamp127(yv);
+      const int yv = min(max(o[e], -128), 127);
+      o[e] = lut ? slut[yv + 128] : max(yv, -127);
     }
-    ow[g] = __byte_perm(__byte_perm(o[0], o[1], 0x0040), __byte_perm(o[2], o[3], 0x0040), 0x5410);
+    *reinterpret_cast<uint32_t*>(ob + (y * W + x) * static_cast<int>(out.cstride)) =
+        __byte_perm(__byte_perm(o[0], o[1], 0x0040), __byte_perm(o[2], o[3], 0x0040), 0x5410);
   }
-  *reinterpret_cast<uint4*>(out.p + b * out.bstride + static_cast<long long>(p) * out.cstride + c) =
-      make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }
 
 // ------------------------------------------------- upsample and concat
@@ -417,14 +435,25 @@ cudaError_t launch_maxpool_i8(I8View in, I8View out, int B, int H, int W, int C,
   return launch_pdl(maxpool_i8_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, st, in, out, B, H, W, C, k);
 }
 
-cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const uint32_t* wp, const int32_t* bq,
+cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const uint32_t* wr, const int32_t* bq,
                             const int32_t* mult, const int32_t* shift, const int8_t* lut, cudaStream_t st) {
-  if (C % 16 || in.cstride % 16 || out.cstride % 16 || C > 4096) return cudaErrorInvalidValue;
-  const long long total = static_cast<long long>(B) * H * W * (C / 16);
-  if (total == 0) return cudaSuccess;
-  const size_t smem = static_cast<size_t>(C) * 16 + 256;
-  return launch_pdl(dw3x3_i8_kernel, dim3(blocks_for(total, 256)), dim3(256), smem, st, in, out, B, H, W, C, wp, bq, mult,
-                    shift, lut);
+  if (C % 16 || in.cstride % 16 || out.cstride % 16 || in.bstride % 16 || out.bstride % 16 ||
+      reinterpret_cast<uintptr_t>(in.p) % 16 || reinterpret_cast<uintptr_t>(out.p) % 16 ||
+      reinterpret_cast<uintptr_t>(wr) % 16)
+    return cudaErrorInvalidValue;
+  if (B <= 0 || H <= 0 || W <= 0) return cudaSuccess;
+  // 32-bit thread indices and per-image byte offsets.
+  if (static_cast<long long>(B) * ((H + 3) / 4) * W * (C / 4) + 256 > INT_MAX ||
+      static_cast<long long>(H) * W * in.cstride > INT_MAX || static_cast<long long>(H) * W * out.cstride > INT_MAX)
+    return cudaErrorInvalidValue;
+  if (H >= 40) {
+    const long long total = static_cast<long long>(B) * ((H + 7) / 8) * W * (C / 4);
+    return launch_pdl(dw3x3_i8_kernel<8>, dim3(blocks_for(total, 256)), dim3(256), 0, st, in, out, B, H, W, C, wr, bq,
+                      mult, shift, lut);
+  }
+  const long long total = static_cast<long long>(B) * ((H + 3) / 4) * W * (C / 4);
+  return launch_pdl(dw3x3_i8_kernel<4>, dim3(blocks_for(total, 256)), dim3(256), 0, st, in, out, B, H, W, C, wr, bq,
+                    mult, shift, lut);
 }
 
 cudaError_t launch_concat_i8(I8View s0, int c0, int lg0, I8View s1, int c1, int B, int H, int W, I8View out,
