@@ -271,13 +271,9 @@ cudaError_t launch_attention_i8(const I8AttnArgs& a, cudaStream_t st) {
       a.out.bstride % 16 || reinterpret_cast<uintptr_t>(a.qkv.p) % 16 || reinterpret_cast<uintptr_t>(a.out.p) % 16 ||
       a.dim != a.heads * HD || a.sht < 1 || a.sho < 1)
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(attention_i8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(sizeof(AttnSmem)));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};
+  const cudaError_t e = smem_attr_once(attention_i8_tc_kernel, static_cast<int>(sizeof(AttnSmem)), attr_done);
+  if (e != cudaSuccess) return e;
   dim3 grid((N + kAQ - 1) / kAQ, a.heads, a.B);
   return launch_pdl(attention_i8_tc_kernel, grid, dim3(128), sizeof(AttnSmem), st, a);
 }

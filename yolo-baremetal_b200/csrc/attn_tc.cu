@@ -284,13 +284,9 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
       a.out.coff % 8 || a.qkv.bstride % 8 || a.out.bstride % 8 || a.qkv.plane % 8 || a.out.plane % 8 ||
       reinterpret_cast<uintptr_t>(a.qkv.hi) % 16 || reinterpret_cast<uintptr_t>(a.out.hi) % 16)
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(sizeof(AttnTcSmem)));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};
+  const cudaError_t e = smem_attr_once(attention_tc_kernel, static_cast<int>(sizeof(AttnTcSmem)), attr_done);
+  if (e != cudaSuccess) return e;
   dim3 grid((N + kTQ - 1) / kTQ, a.heads, a.B);
   return launch_pdl(attention_tc_kernel, grid, dim3(128), sizeof(AttnTcSmem), s, a, a.err);
 }

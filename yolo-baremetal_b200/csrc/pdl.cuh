@@ -13,6 +13,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
 #include <utility>
 
 namespace yb {
@@ -34,6 +36,21 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Raises a kernel's dynamic shared memory limit to `bytes` on the current
+// device, once per device (`done` holds one bit per device ordinal), so that
+// one process driving several GPUs sets it on each of them.
+template <typename... KArgs>
+cudaError_t smem_attr_once(void (*kernel)(KArgs...), int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load() & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit);
+  return e;
 }
 
 }  // namespace yb

@@ -8,7 +8,11 @@
 // in stage 1, slot*nc + class in stage 2).  Here that order is made explicit:
 // (score desc, index asc) is a total order, selected with a 4-pass radix select
 // on order-preserving float keys plus an index-ordered scan for ties at the
-// threshold, then a bitonic sort of the k survivors in shared memory.
+// threshold, then the k survivors are ordered by rank (each counts the
+// survivors above it).  Stage-1 keys are computed once into shared memory (up
+// to kCache of them; more are recomputed per pass).  Stage 2 only ranks the
+// pairs that can still make the cut (see the kernel).
+#include <atomic>
 #include <cfloat>
 #include "pdl.cuh"
 #include "kernels.h"
@@ -34,6 +38,8 @@ struct TopkSmem {
   int wtot[32];
   int scratch[8];
 };
+constexpr int kCache = 24576;  // cached keys per stage (dynamic shared memory)
+constexpr int kCand = 4096;    // stage-2 candidates (dynamic shared memory, after the keys)
 
 // Inclusive block scan of v over 1024 threads; *total receives the block sum.
 __device__ int block_scan(int v, TopkSmem& sm, int* total) {
@@ -61,20 +67,22 @@ __device__ int block_scan(int v, TopkSmem& sm, int* total) {
   return v;
 }
 
-// Selects the k largest of get(0..n-1) under (value desc, index asc) and
-// writes their indices, in that order, to out[0..k).
-template <typename Get>
-__device__ void select_topk(const Get& get, int n, int k, int* out, TopkSmem& sm) {
+// Selects the k largest of key(0..n-1) (order-preserving uint32 keys) under
+// (key desc, index asc), writes their indices, in that order, to out[0..k),
+// and returns the k-th largest key.
+template <typename Key>
+__device__ uint32_t select_topk(const Key& key, int n, int k, int* out, TopkSmem& sm) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (k <= 0) return;
+  if (k <= 0) return 0u;
   uint32_t prefix = 0, mask = 0;
   int remaining = k;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += kT) sm.hist[i] = 0;
     __syncthreads();
+#pragma unroll 4
     for (int i = tid; i < n; i += kT) {
-      const uint32_t key = fkey(get(i));
-      if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255u], 1);
+      const uint32_t kv = key(i);
+      if ((kv & mask) == prefix) atomicAdd(&sm.hist[(kv >> shift) & 255u], 1);
     }
     __syncthreads();
     if (warp == 0) {
@@ -121,14 +129,14 @@ __device__ void select_topk(const Get& get, int n, int k, int* out, TopkSmem& sm
   if (tid == 0) sm.scratch[2] = 0;
   __syncthreads();
   for (int i = tid; i < n; i += kT) {
-    if (fkey(get(i)) > T) out[atomicAdd(&sm.scratch[2], 1)] = i;
+    if (key(i) > T) out[atomicAdd(&sm.scratch[2], 1)] = i;
   }
   __syncthreads();
   // Ties at T: the first `remaining` in ascending index order.
   int base = 0;
   for (int c0 = 0; c0 < n && base < remaining; c0 += kT) {
     const int i = c0 + tid;
-    const int flag = (i < n && fkey(get(i)) == T) ? 1 : 0;
+    const int flag = (i < n && key(i) == T) ? 1 : 0;
     int total;
     const int incl = block_scan(flag, sm, &total);
     const int excl = incl - flag;
@@ -136,39 +144,27 @@ __device__ void select_topk(const Get& get, int n, int k, int* out, TopkSmem& sm
     base += total;
   }
   __syncthreads();
-  int P = 1;
-  while (P < k) P <<= 1;
-  for (int i = tid; i < P; i += kT) {
-    unsigned long long v = 0ull;
-    if (i < k) {
-      const int j = out[i];
-      v = (static_cast<unsigned long long>(fkey(get(j))) << 32) | static_cast<unsigned long long>(~static_cast<uint32_t>(j));
-    }
-    sm.sbuf[i] = v;
+  // Order the k survivors: (key, ~index) is unique, so each survivor's rank
+  // is the number of survivors above it.
+  for (int i = tid; i < k; i += kT) {
+    const int j = out[i];
+    sm.sbuf[i] = (static_cast<unsigned long long>(key(j)) << 32) | static_cast<unsigned long long>(~static_cast<uint32_t>(j));
   }
   __syncthreads();
-  for (int size = 2; size <= P; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < (P >> 1); i += kT) {
-        const int lo = 2 * stride * (i / stride) + (i % stride);
-        const int hi = lo + stride;
-        const bool desc = (lo & size) == 0;
-        const unsigned long long x = sm.sbuf[lo], y = sm.sbuf[hi];
-        if ((x < y) == desc) {
-          sm.sbuf[lo] = y;
-          sm.sbuf[hi] = x;
-        }
-      }
-      __syncthreads();
-    }
+  for (int i = tid; i < k; i += kT) {
+    const unsigned long long v = sm.sbuf[i];
+    int rank = 0;
+    for (int j = 0; j < k; ++j) rank += sm.sbuf[j] > v ? 1 : 0;
+    out[rank] = static_cast<int>(~static_cast<uint32_t>(v & 0xffffffffull));
   }
-  for (int i = tid; i < k; i += kT) out[i] = static_cast<int>(~static_cast<uint32_t>(sm.sbuf[i] & 0xffffffffull));
   __syncthreads();
+  return T;
 }
 
 __global__ void __launch_bounds__(kT) topk_kernel(const TopkArgs a) {
-  pdl_wait();
   __shared__ TopkSmem sm;
+  extern __shared__ __align__(16) uint32_t keys[];  // kCache keys, then kCand candidates
+  pdl_wait();
   const int b = blockIdx.x;
   int k = a.max_det < a.N ? a.max_det : a.N;
   if (k > a.cap) k = a.cap;
@@ -190,13 +186,86 @@ __global__ void __launch_bounds__(kT) topk_kernel(const TopkArgs a) {
     }
     return m;
   };
-  select_topk(get1, a.N, k, sm.idx1, sm);
+  const bool cache1 = a.N <= kCache;
+  if (cache1) {
+#pragma unroll 4
+    for (int i = threadIdx.x; i < a.N; i += kT) keys[i] = fkey(get1(i));
+  }
+  __syncthreads();
+  const uint32_t T1 = select_topk([&](int i) { return cache1 ? keys[i] : fkey(get1(i)); }, a.N, k, sm.idx1, sm);
   auto get2 = [&](int f) {
     const int slot = f / nc;
     const int c = f - slot * nc;
     return value(sm.idx1[slot], c);
   };
-  select_topk(get2, k * nc, k, sm.idx2, sm);
+  // Stage 2.  Every selected anchor's best pair scores its stage-1 key, so at
+  // least k pairs score >= T1 (the k-th stage-1 key) and only those can be
+  // kept: the candidates are the pairs within 16 ulps below T1 or above (a
+  // superset, whatever the rounding of the max).  All k * nc keys are
+  // computed once into shared memory; each warp then compacts the candidates
+  // of its contiguous index range, in index order, into cand[] as
+  // (key << 32 | ~index), unique values whose descending order is the
+  // wanted one.  Up to kTopkMax candidates are ordered by rank, up to kCand
+  // by the radix select over the candidates; more (or fewer than k, or
+  // more than kCache pairs) take the radix select over all k * nc pairs.
+  const int n2 = k * nc;
+  const uint32_t tk = T1 > 16u ? T1 - 16u : 0u;
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(keys + kCache);
+  const bool cache2 = n2 <= kCache;
+  int m = -1;
+  if (cache2) {
+#pragma unroll 4
+    for (int f = threadIdx.x; f < n2; f += kT) keys[f] = fkey(get2(f));
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int span = (n2 + 31) / 32, f0 = warp * span, f1 = min(n2, f0 + span);
+    int cnt = 0;
+    for (int f = f0 + lane; f - lane < f1; f += 32)
+      cnt += __popc(__ballot_sync(0xffffffffu, f < f1 && keys[f] >= tk));
+    if (lane == 0) sm.wtot[warp] = cnt;
+    __syncthreads();
+    if (warp == 0) {
+      const int c = sm.wtot[lane];
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      sm.wtot[lane] = incl - c;  // exclusive offsets
+      if (lane == 31) sm.scratch[3] = incl;
+    }
+    __syncthreads();
+    m = sm.scratch[3];
+    if (m >= k && m <= kCand) {
+      int pos = sm.wtot[warp];
+      for (int f = f0 + lane; f - lane < f1; f += 32) {
+        const bool hit = f < f1 && keys[f] >= tk;
+        const unsigned bal = __ballot_sync(0xffffffffu, hit);
+        if (hit)
+          cand[pos + __popc(bal & ((1u << lane) - 1u))] =
+              (static_cast<unsigned long long>(keys[f]) << 32) | static_cast<unsigned long long>(~static_cast<uint32_t>(f));
+        pos += __popc(bal);
+      }
+    }
+    __syncthreads();
+  }
+  if (m >= k && m <= kTopkMax) {
+    for (int i = threadIdx.x; i < m; i += kT) {
+      const unsigned long long v = cand[i];
+      int rank = 0;
+      for (int j = 0; j < m; ++j) rank += cand[j] > v ? 1 : 0;
+      if (rank < k) sm.idx2[rank] = static_cast<int>(~static_cast<uint32_t>(v & 0xffffffffull));
+    }
+    __syncthreads();
+  } else if (m >= k && m <= kCand) {
+    select_topk([&](int i) { return static_cast<uint32_t>(cand[i] >> 32); }, m, k, sm.idx2, sm);
+    for (int t = threadIdx.x; t < k; t += kT)
+      sm.idx2[t] = static_cast<int>(~static_cast<uint32_t>(cand[sm.idx2[t]] & 0xffffffffull));
+    __syncthreads();
+  } else {
+    select_topk([&](int f) { return cache2 ? keys[f] : fkey(get2(f)); }, n2, k, sm.idx2, sm);
+  }
   float* out = a.dets + static_cast<long long>(b) * a.cap * 6;
   for (int t = threadIdx.x; t < a.cap; t += kT) {
     float* row = out + static_cast<long long>(t) * 6;
@@ -224,7 +293,11 @@ cudaError_t launch_topk(const TopkArgs& a, cudaStream_t s) {
   int k = a.max_det < a.N ? a.max_det : a.N;
   if (k > a.cap) k = a.cap;
   if (k > kTopkMax || a.B <= 0) return cudaErrorInvalidValue;
-  return launch_pdl(topk_kernel, dim3(a.B), dim3(kT), 0, s, a);
+  constexpr int kSmem = kCache * 4 + kCand * 8;
+  static std::atomic<uint64_t> attr_done{0};
+  const cudaError_t e = smem_attr_once(topk_kernel, kSmem, attr_done);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(topk_kernel, dim3(a.B), dim3(kT), kSmem, s, a);
 }
 
 }  // namespace yb
