@@ -16,7 +16,9 @@
 // issues the UMMAs; completion is a tcgen05.commit on one mbarrier that every
 // thread waits on with a bound (a timeout sets the error word and ends the
 // kernel after freeing tensor memory).
+#include <atomic>
 #include <climits>
+#include <cmath>
 #include <cstdint>
 
 #include "pdl.cuh"
@@ -263,6 +265,251 @@ __global__ void __launch_bounds__(128, 1) attention_i8_tc_kernel(const I8AttnArg
   }
 }
 
+// ---------------------------------------------------------------------------
+// Wide variant for N <= kWideN keys (the 20 x 20 PSA of a 640 x 640 input):
+// 512 threads, four warpgroups splitting the key columns, and every phase
+// done once.  Q, K and V^T are staged once; S for all keys is computed by one
+// or two UMMAs (N <= 256 each) into TMEM columns [0, Np); each warpgroup
+// reduces its quarter of the columns to a row maximum, then writes its
+// quarter of P = Ph, Pl (int8, shared memory) and its part of l; one thread
+// issues O_h += Ph V, O_l += Pl V over all keys (K 32 per UMMA) into TMEM
+// columns [0, 128), which S no longer needs; each warpgroup finishes 16 of
+// the 64 output channels.  Same integer rules as the kernel above, with two
+// exact shortcuts:
+//   t   the product d * mt / 2^sht in fp32 (d < 2^21 is exact, the error is
+//       below 2^-15 for values up to 256) rounded to nearest even decides t
+//       unless it lies within 2^-14 of a half-integer; then the 64-bit rule;
+//   div the quotient from a double reciprocal of l, corrected by the integer
+//       remainder (and the 64-bit division if it is off by more than 2).
+constexpr int kWideN = 512;
+constexpr int kWideThreads = 512;
+
+struct AttnWideSmem {
+  uint8_t q[kAQ * KD];
+  uint8_t k[kWideN * KD];
+  uint8_t vt[HD * kWideN];
+  uint8_t ph[kAQ * kWideN];
+  uint8_t pl[kAQ * kWideN];
+  int32_t E[256];
+  int8_t pe[9 * HD];
+  int32_t red_max[4][kAQ];
+  int32_t red_sum[4][kAQ];
+  uint64_t bar;
+  uint32_t tmem;
+  int abort;
+};
+
+__device__ __forceinline__ long long div_rne_fast(long long a, long long l, double rl) {
+  long long q = static_cast<long long>(floor(static_cast<double>(a) * rl));
+  long long r = a - q * l;
+  if (r < -2 * l || r >= 3 * l) return div_rne64(a, l);
+  while (r < 0) {
+    --q;
+    r += l;
+  }
+  while (r >= l) {
+    ++q;
+    r -= l;
+  }
+  if (2 * r > l || (2 * r == l && (q & 1))) ++q;
+  return q;
+}
+
+__global__ void __launch_bounds__(kWideThreads, 1) attention_i8_wide_kernel(const I8AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t attn_wide_raw[];
+  AttnWideSmem& S = *reinterpret_cast<AttnWideSmem*>(attn_wide_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = warp >> 2;                 // warpgroup: quarter of the key columns / channels
+  const int row = (warp & 3) * 32 + lane;  // query row = TMEM lane
+  const int N = a.H * a.W;
+  const int Np = (N + 63) & ~63;  // keys padded to 64 (quarters of 16-column loads)
+  const int Nq = Np >> 2;
+  const int q0 = blockIdx.x * kAQ, h = blockIdx.y, b = blockIdx.z;
+  const int blk = 2 * KD + HD;
+  const int8_t* base = a.qkv.p + static_cast<long long>(b) * a.qkv.bstride + h * blk;
+  for (int i = tid; i < 256; i += kWideThreads) S.E[i] = a.E[i];
+  for (int i = tid; i < 9 * HD; i += kWideThreads) S.pe[i] = a.pe_w[(i / HD) * a.dim + h * HD + i % HD];
+  if (tid == 0) {
+    mbar_init(&S.bar, 1);
+    S.abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&S.tmem, 512);
+    tmem_relinquish();
+  }
+  pdl_wait();
+  // Q (zero past N), K and V^T (zero past N), 16-byte loads.
+  for (int i = tid; i < kAQ * 2; i += kWideThreads) {
+    const int r = i >> 1, c = i & 1;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (q0 + r < N) v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(q0 + r) * a.qkv.cstride + 16 * c);
+    *reinterpret_cast<uint4*>(S.q + ops_off(r, 16 * c, KD)) = v;
+  }
+  for (int i = tid; i < Np * 2; i += kWideThreads) {
+    const int j = i >> 1, c = i & 1;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (j < N) v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(j) * a.qkv.cstride + KD + 16 * c);
+    *reinterpret_cast<uint4*>(S.k + ops_off(j, 16 * c, KD)) = v;
+  }
+  for (int i = tid; i < Np * 4; i += kWideThreads) {
+    const int j = i % Np, c = i / Np;  // key j, channels 16c .. 16c + 15
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (j < N) v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(j) * a.qkv.cstride + 2 * KD + 16 * c);
+    const uint8_t* vb = reinterpret_cast<const uint8_t*>(&v);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) S.vt[ops_off(16 * c + e, j, Np)] = vb[e];
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = S.tmem;
+  const uint32_t trow = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+  volatile int* abort_flag = &S.abort;
+  bool ok = true;
+  uint32_t phase = 0;
+  auto wait_mma = [&]() {
+    if (!ok) return;
+    if (!mbar_wait(&S.bar, phase, abort_flag)) {
+      *abort_flag = 1;
+      if (a.err) atomicCAS(a.err, 0, kErrAttnWait);
+      ok = false;
+    }
+    phase ^= 1u;
+    tc_fence_after();
+  };
+  // S = Q K^T for all keys: columns [0, 256) and [256, Np).
+  if (tid == 0) {
+    const uint64_t da = kmajor_desc_noswizzle(smem_u32(S.q), 128, (KD / 16) * 128);
+    for (int k0 = 0; k0 < Np; k0 += 256) {
+      const int nb = Np - k0 < 256 ? Np - k0 : 256;
+      const uint64_t db = kmajor_desc_noswizzle(smem_u32(S.k) + static_cast<uint32_t>(k0 / 8) * 256u, 128,
+                                                (KD / 16) * 128);
+      tc_mma_i8(tbase + static_cast<uint32_t>(k0), da, db, idesc_s8_s32(kAQ, nb), 0u);
+    }
+    tc_commit(&S.bar);
+  }
+  wait_mma();
+  // Row maximum over this warpgroup's quarter of the valid keys.
+  const int c0 = g * Nq;
+  int mx = INT_MIN;
+  for (int cc = 0; cc < Nq; cc += 16) {
+    uint32_t r[16];
+    tc_ld_32x32b_x16(trow + static_cast<uint32_t>(c0 + cc), r);
+    tc_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (c0 + cc + e < N) mx = max(mx, static_cast<int>(r[e]));
+  }
+  S.red_max[g][row] = mx;
+  __syncthreads();
+  mx = max(max(S.red_max[0][row], S.red_max[1][row]), max(S.red_max[2][row], S.red_max[3][row]));
+  // Weights of this quarter: p = E[t], split into Ph = p >> 6 and Pl = p & 63.
+  const float ratio = ldexpf(static_cast<float>(a.mt), -a.sht);
+  int l = 0;
+  for (int cc = 0; cc < Nq; cc += 16) {
+    uint32_t r[16];
+    tc_ld_32x32b_x16(trow + static_cast<uint32_t>(c0 + cc), r);
+    tc_wait_ld();
+    uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      int p = 0;
+      if (c0 + cc + e < N) {
+        const int d = mx - static_cast<int>(r[e]);
+        const float y = static_cast<float>(d) * ratio;
+        int t;
+        if (y >= 256.0f) {
+          t = 255;
+        } else {
+          const float ty = rintf(y);
+          t = static_cast<int>(ty);
+          if (fabsf(y - ty) > 0.49993896484375f) {  // within 2^-14 of a half-integer
+            const long long te = rne64(static_cast<long long>(d) * a.mt, a.sht);
+            t = te > 255 ? 255 : static_cast<int>(te);
+          }
+          t = t > 255 ? 255 : t;
+        }
+        p = S.E[t];
+      }
+      l += p;
+      hw[e >> 2] |= static_cast<uint32_t>(p >> 6) << (8 * (e & 3));
+      lw[e >> 2] |= static_cast<uint32_t>(p & 63) << (8 * (e & 3));
+    }
+    *reinterpret_cast<uint4*>(S.ph + ops_off(row, c0 + cc, Np)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(S.pl + ops_off(row, c0 + cc, Np)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+  S.red_sum[g][row] = l;
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // O_h += Ph V (columns [0, 64)), O_l += Pl V ([64, 128)) over all keys.
+  if (tid == 0 && ok && !*abort_flag) {
+    const uint32_t idesc = idesc_s8_s32(kAQ, HD);
+    const uint32_t sbo = static_cast<uint32_t>(Np / 16) * 128u;
+    const uint64_t dh = kmajor_desc_noswizzle(smem_u32(S.ph), 128, sbo);
+    const uint64_t dl = kmajor_desc_noswizzle(smem_u32(S.pl), 128, sbo);
+    const uint64_t dv = kmajor_desc_noswizzle(smem_u32(S.vt), 128, sbo);
+    for (int s = 0; s < Np / 32; ++s) {
+      const uint64_t off = static_cast<uint64_t>(16 * s);  // 32 keys = two core matrices = 256 bytes
+      tc_mma_i8(tbase, dh + off, dv + off, idesc, s == 0 ? 0u : 1u);
+      tc_mma_i8(tbase + 64, dl + off, dv + off, idesc, s == 0 ? 0u : 1u);
+    }
+    tc_commit(&S.bar);
+  }
+  wait_mma();
+  __syncthreads();
+  const bool good = S.abort == 0;
+  const int qi = q0 + row;
+  const bool valid = qi < N && good;
+  l = S.red_sum[0][row] + S.red_sum[1][row] + S.red_sum[2][row] + S.red_sum[3][row];
+  const double rl = 1.0 / static_cast<double>(l > 0 ? l : 1);
+  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
+  const int d0 = 16 * g;
+  uint32_t oh[16], ol[16];
+  tc_ld_32x32b_x16(trow + static_cast<uint32_t>(d0), oh);
+  tc_ld_32x32b_x16(trow + 64u + static_cast<uint32_t>(d0), ol);
+  tc_wait_ld();
+  if (valid) {
+    // Positional term: depthwise 3x3 of v (channels h*HD + d) around the query.
+    int acc[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = 0;
+    for (int tap = 0; tap < 9; ++tap) {
+      const int iy = y - 1 + tap / 3, ix = x - 1 + tap % 3;
+      if (iy < 0 || iy >= a.H || ix < 0 || ix >= a.W) continue;
+      const uint4 v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride +
+                                                      2 * KD + d0);
+      const int8_t* vb = reinterpret_cast<const int8_t*>(&v);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[e] += static_cast<int>(vb[e]) * static_cast<int>(S.pe[tap * HD + d0 + e]);
+    }
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int ch = h * HD + d0 + e;
+      const long long o = 64LL * static_cast<int32_t>(oh[e]) + static_cast<int32_t>(ol[e]);
+      const long long av = div_rne_fast(rne64(o * a.mo, a.sho), l, rl);
+      const long long pe = rne64((static_cast<long long>(acc[e]) + a.pe_bq[ch]) * a.pe_mult[ch], a.pe_shift[ch]);
+      const long long v = av + pe;
+      const int c = static_cast<int>(v < -127 ? -127 : v > 127 ? 127 : v);
+      w[e >> 2] |= (static_cast<uint32_t>(c) & 0xFFu) << (8 * (e & 3));
+    }
+    int8_t* op = a.out.p + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(qi) * a.out.cstride +
+                 h * HD + d0;
+    *reinterpret_cast<uint4*>(op) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  if (!good) __nanosleep(100000);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_attention_i8(const I8AttnArgs& a, cudaStream_t st) {
@@ -275,6 +522,12 @@ cudaError_t launch_attention_i8(const I8AttnArgs& a, cudaStream_t st) {
   const cudaError_t e = smem_attr_once(attention_i8_tc_kernel, static_cast<int>(sizeof(AttnSmem)), attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid((N + kAQ - 1) / kAQ, a.heads, a.B);
+  if (N <= kWideN) {
+    static std::atomic<uint64_t> wide_done{0};
+    const cudaError_t e2 = smem_attr_once(attention_i8_wide_kernel, static_cast<int>(sizeof(AttnWideSmem)), wide_done);
+    if (e2 != cudaSuccess) return e2;
+    return launch_pdl(attention_i8_wide_kernel, grid, dim3(kWideThreads), sizeof(AttnWideSmem), st, a);
+  }
   return launch_pdl(attention_i8_tc_kernel, grid, dim3(128), sizeof(AttnSmem), st, a);
 }
 

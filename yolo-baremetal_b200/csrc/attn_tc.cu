@@ -18,6 +18,7 @@
 // x 16 bytes, 128 contiguous bytes each, row-group major).  One thread issues
 // the UMMAs; completion is one mbarrier every thread waits on with a bound
 // (a timeout sets the error word and ends the kernel after freeing TMEM).
+#include <atomic>
 #include <cfloat>
 #include <cstdint>
 
@@ -276,6 +277,256 @@ __global__ void __launch_bounds__(128, 3) attention_tc_kernel(const AttnArgs a, 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Wide variant for N <= kWideNF keys (the 20 x 20 PSA of a 640 x 640 input):
+// 512 threads in four warpgroups.  Q, K and V^T (hi and lo planes) are staged
+// once; S for all keys goes to TMEM columns [0, Np) in one pass (N <= 256 per
+// UMMA); the warpgroups reduce quarters of the columns to the row maximum.
+// P then streams in chunks of 64 keys through two shared-memory slots laid
+// over the dead Q and K: every warpgroup writes 16 of a chunk's columns, one
+// thread issues the chunk's 12 UMMAs (Ph Vh + Ph Vl + Pl Vh, 4 K steps) into
+// O at TMEM columns [0, 64) (chunk 0's scores, read by then) and commits to
+// the slot's barrier, which the writers of the chunk two ahead wait on.
+// Each warpgroup finishes 16 of the 64 output channels.
+constexpr int kWideNF = 448;
+constexpr int kWideTF = 512;
+constexpr int kChunkF = 64;
+constexpr uint32_t kSlotBytes = kTQ * kChunkF * 2;  // one plane of one P chunk
+
+struct AttnWideTcSmem {
+  union {
+    struct {
+      uint8_t qh[kTQ * TKD * 2], ql[kTQ * TKD * 2];
+      uint8_t kh[kWideNF * TKD * 2], kl[kWideNF * TKD * 2];
+    } s;
+    uint8_t p[2][2][kSlotBytes];  // [slot][hi, lo]: 128 x 64 bf16
+  } u;
+  uint8_t vh[THD * kWideNF * 2], vl[THD * kWideNF * 2];
+  float red_max[4][kTQ];
+  float red_sum[4][kTQ];
+  uint64_t bar;
+  uint64_t slot_bar[2];
+  uint32_t tmem;
+  int abort;
+};
+
+__global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const AttnArgs a, int* err) {
+  extern __shared__ __align__(1024) uint8_t attn_wtc_raw[];
+  AttnWideTcSmem& S = *reinterpret_cast<AttnWideTcSmem*>(attn_wtc_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = warp >> 2;
+  const int row = (warp & 3) * 32 + lane;
+  const int N = a.H * a.W;
+  const int Np = (N + 63) & ~63;
+  const int Nq = Np >> 2;
+  const int q0 = blockIdx.x * kTQ, h = blockIdx.y, b = blockIdx.z;
+  const int blk = 2 * TKD + THD;
+  const uint16_t* base = a.qkv.hi + static_cast<long long>(b) * a.qkv.bstride + a.qkv.coff + h * blk;
+  const long long pl = a.qkv.plane;
+  if (tid == 0) {
+    mbar_init(&S.bar, 1);
+    mbar_init(&S.slot_bar[0], 1);
+    mbar_init(&S.slot_bar[1], 1);
+    S.abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&S.tmem, 512);
+    tmem_relinquish();
+  }
+  pdl_wait();
+  for (int i = tid; i < kTQ * 4; i += kWideTF) {
+    const int r = i >> 2, c = i & 3;
+    uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
+    if (q0 + r < N) {
+      const uint16_t* p = base + static_cast<long long>(q0 + r) * a.qkv.cstride + 8 * c;
+      vh = *reinterpret_cast<const uint4*>(p);
+      vl = *reinterpret_cast<const uint4*>(p + pl);
+    }
+    *reinterpret_cast<uint4*>(S.u.s.qh + opo(r, 16 * c, 2 * TKD)) = vh;
+    *reinterpret_cast<uint4*>(S.u.s.ql + opo(r, 16 * c, 2 * TKD)) = vl;
+  }
+  for (int i = tid; i < Np * 4; i += kWideTF) {
+    const int j = i >> 2, c = i & 3;
+    uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
+    if (j < N) {
+      const uint16_t* p = base + static_cast<long long>(j) * a.qkv.cstride + TKD + 8 * c;
+      vh = *reinterpret_cast<const uint4*>(p);
+      vl = *reinterpret_cast<const uint4*>(p + pl);
+    }
+    *reinterpret_cast<uint4*>(S.u.s.kh + opo(j, 16 * c, 2 * TKD)) = vh;
+    *reinterpret_cast<uint4*>(S.u.s.kl + opo(j, 16 * c, 2 * TKD)) = vl;
+  }
+  for (int i = tid; i < Np * (THD / 8); i += kWideTF) {
+    const int j = i % Np, c = i / Np;  // key j, channels 8c .. 8c + 7
+    uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
+    if (j < N) {
+      const uint16_t* p = base + static_cast<long long>(j) * a.qkv.cstride + 2 * TKD + 8 * c;
+      vh = *reinterpret_cast<const uint4*>(p);
+      vl = *reinterpret_cast<const uint4*>(p + pl);
+    }
+    const uint16_t* eh = reinterpret_cast<const uint16_t*>(&vh);
+    const uint16_t* el = reinterpret_cast<const uint16_t*>(&vl);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t o = opo(8 * c + e, 2 * j, 2 * Np);
+      *reinterpret_cast<uint16_t*>(S.vh + o) = eh[e];
+      *reinterpret_cast<uint16_t*>(S.vl + o) = el[e];
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = S.tmem;
+  const uint32_t trow = tbase + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+  volatile int* abort_flag = &S.abort;
+  bool ok = true;
+  auto wait_bar = [&](uint64_t* bar, uint32_t parity) {
+    if (!ok) return;
+    if (!mbar_wait(bar, parity, abort_flag)) {
+      *abort_flag = 1;
+      if (err) atomicCAS(err, 0, kErrAttnWaitF);
+      ok = false;
+    }
+    tc_fence_after();
+  };
+  // S = Q K^T, all keys.
+  if (tid == 0) {
+    const uint32_t sbo = (2 * TKD / 16) * 128;
+    const uint64_t qh = kmajor_desc_noswizzle(smem_u32(S.u.s.qh), 128, sbo);
+    const uint64_t ql = kmajor_desc_noswizzle(smem_u32(S.u.s.ql), 128, sbo);
+    for (int k0 = 0; k0 < Np; k0 += 256) {
+      const int nb = Np - k0 < 256 ? Np - k0 : 256;
+      const uint32_t idesc = idesc_bf16_f32(kTQ, nb);
+      const uint32_t ko = static_cast<uint32_t>(k0 / 8) * sbo;
+      const uint64_t kh = kmajor_desc_noswizzle(smem_u32(S.u.s.kh) + ko, 128, sbo);
+      const uint64_t kl = kmajor_desc_noswizzle(smem_u32(S.u.s.kl) + ko, 128, sbo);
+      const uint32_t d = tbase + static_cast<uint32_t>(k0);
+#pragma unroll
+      for (int st = 0; st < TKD / 16; ++st) {
+        const uint64_t off = static_cast<uint64_t>(16 * st);
+        tc_mma_bf16(d, qh + off, kh + off, idesc, st == 0 ? 0u : 1u);
+        tc_mma_bf16(d, qh + off, kl + off, idesc, 1u);
+        tc_mma_bf16(d, ql + off, kh + off, idesc, 1u);
+      }
+    }
+    tc_commit(&S.bar);
+  }
+  wait_bar(&S.bar, 0u);
+  // Row maximum of the scaled scores over this warpgroup's quarter.
+  float mx = -FLT_MAX;
+  for (int cc = 0; cc < Nq; cc += 16) {
+    uint32_t r[16];
+    tc_ld_32x32b_x16(trow + static_cast<uint32_t>(g * Nq + cc), r);
+    tc_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (g * Nq + cc + e < N) mx = fmaxf(mx, __uint_as_float(r[e]) * a.scale);
+  }
+  S.red_max[g][row] = mx;
+  __syncthreads();  // also: Q and K are dead from here (their UMMAs completed)
+  mx = fmaxf(fmaxf(S.red_max[0][row], S.red_max[1][row]), fmaxf(S.red_max[2][row], S.red_max[3][row]));
+  // P in chunks of 64 keys, 16 columns per warpgroup; O += P V per chunk.
+  float l = 0.f;
+  const int nchunks = Np / kChunkF;
+  for (int c = 0; c < nchunks; ++c) {
+    const int slot = c & 1;
+    if (c >= 2) wait_bar(&S.slot_bar[slot], static_cast<uint32_t>(((c >> 1) - 1) & 1));
+    const int col = c * kChunkF + 16 * g;
+    uint32_t r[16];
+    tc_ld_32x32b_x16(trow + static_cast<uint32_t>(col), r);
+    tc_wait_ld();
+    uint32_t hw[8], lw[8];
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      const float p0 = col + e < N ? __expf(__uint_as_float(r[e]) * a.scale - mx) : 0.f;
+      const float p1 = col + e + 1 < N ? __expf(__uint_as_float(r[e + 1]) * a.scale - mx) : 0.f;
+      l += p0;
+      l += p1;
+      split2(p0, p1, hw[e >> 1], lw[e >> 1]);
+    }
+    uint8_t* ph = S.u.p[slot][0];
+    uint8_t* plo = S.u.p[slot][1];
+    *reinterpret_cast<uint4*>(ph + opo(row, 32 * g, 2 * kChunkF)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(ph + opo(row, 32 * g + 16, 2 * kChunkF)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    *reinterpret_cast<uint4*>(plo + opo(row, 32 * g, 2 * kChunkF)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    *reinterpret_cast<uint4*>(plo + opo(row, 32 * g + 16, 2 * kChunkF)) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0 && ok && !*abort_flag) {
+      const uint32_t idesc = idesc_bf16_f32(kTQ, THD);
+      const uint32_t psbo = (2 * kChunkF / 16) * 128;
+      const uint32_t vsbo = static_cast<uint32_t>(2 * Np / 16) * 128u;
+      const uint64_t dph = kmajor_desc_noswizzle(smem_u32(ph), 128, psbo);
+      const uint64_t dpl = kmajor_desc_noswizzle(smem_u32(plo), 128, psbo);
+      const uint32_t vo = static_cast<uint32_t>(c) * 1024u;  // 64 keys = 8 core matrices along K
+      const uint64_t dvh = kmajor_desc_noswizzle(smem_u32(S.vh) + vo, 128, vsbo);
+      const uint64_t dvl = kmajor_desc_noswizzle(smem_u32(S.vl) + vo, 128, vsbo);
+#pragma unroll
+      for (int st = 0; st < kChunkF / 16; ++st) {
+        const uint64_t off = static_cast<uint64_t>(16 * st);
+        tc_mma_bf16(tbase, dph + off, dvh + off, idesc, (c == 0 && st == 0) ? 0u : 1u);
+        tc_mma_bf16(tbase, dph + off, dvl + off, idesc, 1u);
+        tc_mma_bf16(tbase, dpl + off, dvh + off, idesc, 1u);
+      }
+      tc_commit(&S.slot_bar[slot]);
+    }
+  }
+  // The last chunk's UMMAs (and with them every earlier one) have completed.
+  wait_bar(&S.slot_bar[(nchunks - 1) & 1], static_cast<uint32_t>(((nchunks - 1) >> 1) & 1));
+  S.red_sum[g][row] = l;
+  __syncthreads();
+  const bool good = S.abort == 0;
+  const int qi = q0 + row;
+  const bool valid = qi < N && good;
+  l = S.red_sum[0][row] + S.red_sum[1][row] + S.red_sum[2][row] + S.red_sum[3][row];
+  const float inv = l > 1e-12f ? 1.0f / l : 1.0f;
+  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
+  const int d0 = 16 * g;
+  uint32_t ov[16];
+  tc_ld_32x32b_x16(trow + static_cast<uint32_t>(d0), ov);
+  tc_wait_ld();
+  if (valid) {
+    uint16_t* op = a.out.hi + static_cast<long long>(b) * a.out.bstride + static_cast<long long>(qi) * a.out.cstride +
+                   a.out.coff + h * THD;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int dd = d0 + 8 * half;
+      const int ch = h * THD + dd;
+      float pe[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pe[e] = __ldg(a.pe_b + ch + e);
+      for (int ky = 0; ky < 3; ++ky) {
+        const int iy = y - 1 + ky;
+        if (iy < 0 || iy >= a.H) continue;
+        for (int kx = 0; kx < 3; ++kx) {
+          const int ix = x - 1 + kx;
+          if (ix < 0 || ix >= a.W) continue;
+          float v[8];
+          load8(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * TKD + dd, pl, v);
+          const float* w = a.pe_w + (ky * 3 + kx) * (a.heads * THD) + ch;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v[e], __ldg(w + e)));
+        }
+      }
+      float res[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) res[e] = __uint_as_float(ov[8 * half + e]) * inv + pe[e];
+      store8(op + dd, a.out.plane, res);
+    }
+  }
+  if (!good) __nanosleep(100000);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
@@ -288,6 +539,13 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
   const cudaError_t e = smem_attr_once(attention_tc_kernel, static_cast<int>(sizeof(AttnTcSmem)), attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid((N + kTQ - 1) / kTQ, a.heads, a.B);
+  if (N <= kWideNF) {
+    static std::atomic<uint64_t> wide_done{0};
+    const cudaError_t e2 =
+        smem_attr_once(attention_wide_tc_kernel, static_cast<int>(sizeof(AttnWideTcSmem)), wide_done);
+    if (e2 != cudaSuccess) return e2;
+    return launch_pdl(attention_wide_tc_kernel, grid, dim3(kWideTF), sizeof(AttnWideTcSmem), s, a, a.err);
+  }
   return launch_pdl(attention_tc_kernel, grid, dim3(128), sizeof(AttnTcSmem), s, a, a.err);
 }
 
