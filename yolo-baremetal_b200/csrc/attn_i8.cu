@@ -290,10 +290,11 @@ struct AttnWideSmem {
   uint8_t vt[HD * kWideN];
   uint8_t ph[kAQ * kWideN];
   uint8_t pl[kAQ * kWideN];
-  int32_t E[256];
-  int8_t pe[9 * HD];
+  uint32_t E3[257];        // E[t] as (E >> 6) | (E & 63) << 16; E3[256] = 0 (keys past N)
+  alignas(16) uint32_t pw[HD][4];  // positional weights of this head per channel: taps 0-3, 4-7, 8
+  int32_t pq[3][HD];       // positional bias, multiplier, shift of this head
   int32_t red_max[4][kAQ];
-  int32_t red_sum[4][kAQ];
+  int32_t red_sum[4][kAQ];  // packed: sum (p >> 6) in the low half, sum (p & 63) in the high half
   uint64_t bar;
   uint32_t tmem;
   int abort;
@@ -315,6 +316,16 @@ __device__ __forceinline__ long long div_rne_fast(long long a, long long l, doub
   return q;
 }
 
+// Byte transpose of four words: y[e] byte k = byte e of word k.
+__device__ __forceinline__ void transpose4w(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t (&y)[4]) {
+  const uint32_t t0 = __byte_perm(a, b, 0x5140), t1 = __byte_perm(a, b, 0x7362);
+  const uint32_t t2 = __byte_perm(c, d, 0x5140), t3 = __byte_perm(c, d, 0x7362);
+  y[0] = __byte_perm(t0, t2, 0x5410);
+  y[1] = __byte_perm(t0, t2, 0x7632);
+  y[2] = __byte_perm(t1, t3, 0x5410);
+  y[3] = __byte_perm(t1, t3, 0x7632);
+}
+
 __global__ void __launch_bounds__(kWideThreads, 1) attention_i8_wide_kernel(const I8AttnArgs a) {
   extern __shared__ __align__(1024) uint8_t attn_wide_raw[];
   AttnWideSmem& S = *reinterpret_cast<AttnWideSmem*>(attn_wide_raw);
@@ -327,8 +338,23 @@ __global__ void __launch_bounds__(kWideThreads, 1) attention_i8_wide_kernel(cons
   const int q0 = blockIdx.x * kAQ, h = blockIdx.y, b = blockIdx.z;
   const int blk = 2 * KD + HD;
   const int8_t* base = a.qkv.p + static_cast<long long>(b) * a.qkv.bstride + h * blk;
-  for (int i = tid; i < 256; i += kWideThreads) S.E[i] = a.E[i];
-  for (int i = tid; i < 9 * HD; i += kWideThreads) S.pe[i] = a.pe_w[(i / HD) * a.dim + h * HD + i % HD];
+  // Constants of this head (not written by earlier kernels): before pdl_wait.
+  for (int i = tid; i < 257; i += kWideThreads) {
+    const int e = i < 256 ? a.E[i] : 0;
+    S.E3[i] = static_cast<uint32_t>(e >> 6) | (static_cast<uint32_t>(e & 63) << 16);
+  }
+  for (int i = tid; i < HD * 3; i += kWideThreads) {
+    const int d = i / 3, wv = i - (i / 3) * 3;  // word wv: taps 4wv .. 4wv+3 (tap 8 alone)
+    uint32_t word = 0u;
+    for (int k = 0; k < 4 && 4 * wv + k < 9; ++k)
+      word |= (static_cast<uint32_t>(a.pe_w[(4 * wv + k) * a.dim + h * HD + d]) & 0xFFu) << (8 * k);
+    S.pw[d][wv] = word;
+  }
+  for (int i = tid; i < HD; i += kWideThreads) {
+    S.pq[0][i] = a.pe_bq[h * HD + i];
+    S.pq[1][i] = a.pe_mult[h * HD + i];
+    S.pq[2][i] = a.pe_shift[h * HD + i];
+  }
   if (tid == 0) {
     mbar_init(&S.bar, 1);
     S.abort = 0;
@@ -339,7 +365,7 @@ __global__ void __launch_bounds__(kWideThreads, 1) attention_i8_wide_kernel(cons
     tmem_relinquish();
   }
   pdl_wait();
-  // Q (zero past N), K and V^T (zero past N), 16-byte loads.
+  // Q (zero past N), K (zero past N), 16-byte loads.
   for (int i = tid; i < kAQ * 2; i += kWideThreads) {
     const int r = i >> 1, c = i & 1;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -352,13 +378,24 @@ __global__ void __launch_bounds__(kWideThreads, 1) attention_i8_wide_kernel(cons
     if (j < N) v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(j) * a.qkv.cstride + KD + 16 * c);
     *reinterpret_cast<uint4*>(S.k + ops_off(j, 16 * c, KD)) = v;
   }
-  for (int i = tid; i < Np * 4; i += kWideThreads) {
-    const int j = i % Np, c = i / Np;  // key j, channels 16c .. 16c + 15
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (j < N) v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(j) * a.qkv.cstride + 2 * KD + 16 * c);
-    const uint8_t* vb = reinterpret_cast<const uint8_t*>(&v);
+  // V^T: one item = 4 keys x 16 channels, transposed into 16 words of 4 keys.
+  for (int i = tid; i < Np; i += kWideThreads) {
+    const int j0 = (i % (Np >> 2)) * 4, c = i / (Np >> 2);
+    uint4 v[4];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) S.vt[ops_off(16 * c + e, j, Np)] = vb[e];
+    for (int k = 0; k < 4; ++k) {
+      v[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (j0 + k < N)
+        v[k] = *reinterpret_cast<const uint4*>(base + static_cast<long long>(j0 + k) * a.qkv.cstride + 2 * KD + 16 * c);
+    }
+#pragma unroll
+    for (int qd = 0; qd < 4; ++qd) {
+      const auto wq = [&](const uint4& u) { return qd == 0 ? u.x : qd == 1 ? u.y : qd == 2 ? u.z : u.w; };
+      uint32_t y[4];
+      transpose4w(wq(v[0]), wq(v[1]), wq(v[2]), wq(v[3]), y);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) *reinterpret_cast<uint32_t*>(S.vt + ops_off(16 * c + 4 * qd + e, j0, Np)) = y[e];
+    }
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -398,49 +435,58 @@ __global__ void __launch_bounds__(kWideThreads, 1) attention_i8_wide_kernel(cons
     uint32_t r[16];
     tc_ld_32x32b_x16(trow + static_cast<uint32_t>(c0 + cc), r);
     tc_wait_ld();
+    if (c0 + cc + 16 <= N) {
 #pragma unroll
-    for (int e = 0; e < 16; ++e)
-      if (c0 + cc + e < N) mx = max(mx, static_cast<int>(r[e]));
+      for (int e = 0; e < 16; ++e) mx = max(mx, static_cast<int>(r[e]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (c0 + cc + e < N) mx = max(mx, static_cast<int>(r[e]));
+    }
   }
   S.red_max[g][row] = mx;
   __syncthreads();
   mx = max(max(S.red_max[0][row], S.red_max[1][row]), max(S.red_max[2][row], S.red_max[3][row]));
-  // Weights of this quarter: p = E[t], split into Ph = p >> 6 and Pl = p & 63.
+  // Weights of this quarter: t from the fp32 product, clamped to 255 (keys
+  // past N take the zero entry 256); a block of 16 keys with a product
+  // within 2^-14 of a half-integer is redone with the 64-bit rule.
   const float ratio = ldexpf(static_cast<float>(a.mt), -a.sht);
-  int l = 0;
+  uint32_t lsum = 0u;
   for (int cc = 0; cc < Nq; cc += 16) {
     uint32_t r[16];
     tc_ld_32x32b_x16(trow + static_cast<uint32_t>(c0 + cc), r);
     tc_wait_ld();
-    uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+    int t[16];
+    bool amb = false;
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
-      int p = 0;
-      if (c0 + cc + e < N) {
-        const int d = mx - static_cast<int>(r[e]);
-        const float y = static_cast<float>(d) * ratio;
-        int t;
-        if (y >= 256.0f) {
-          t = 255;
-        } else {
-          const float ty = rintf(y);
-          t = static_cast<int>(ty);
-          if (fabsf(y - ty) > 0.49993896484375f) {  // within 2^-14 of a half-integer
-            const long long te = rne64(static_cast<long long>(d) * a.mt, a.sht);
-            t = te > 255 ? 255 : static_cast<int>(te);
-          }
-          t = t > 255 ? 255 : t;
-        }
-        p = S.E[t];
+      const float y = fminf(static_cast<float>(mx - static_cast<int>(r[e])) * ratio, 255.0f);
+      const float ty = rintf(y);
+      amb = amb || fabsf(y - ty) > 0.49993896484375f;
+      t[e] = c0 + cc + e < N ? static_cast<int>(ty) : 256;
+    }
+    if (amb) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        if (t[e] == 256) continue;
+        const long long te = rne64(static_cast<long long>(mx - static_cast<int>(r[e])) * a.mt, a.sht);
+        t[e] = te > 255 ? 255 : static_cast<int>(te);
       }
-      l += p;
-      hw[e >> 2] |= static_cast<uint32_t>(p >> 6) << (8 * (e & 3));
-      lw[e >> 2] |= static_cast<uint32_t>(p & 63) << (8 * (e & 3));
+    }
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      const uint32_t e0 = S.E3[t[4 * q4]], e1 = S.E3[t[4 * q4 + 1]];
+      const uint32_t e2 = S.E3[t[4 * q4 + 2]], e3 = S.E3[t[4 * q4 + 3]];
+      lsum += e0 + e1 + e2 + e3;
+      const uint32_t t01 = __byte_perm(e0, e1, 0x6240), t23 = __byte_perm(e2, e3, 0x6240);
+      hw[q4] = __byte_perm(t01, t23, 0x5410);
+      lw[q4] = __byte_perm(t01, t23, 0x7632);
     }
     *reinterpret_cast<uint4*>(S.ph + ops_off(row, c0 + cc, Np)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     *reinterpret_cast<uint4*>(S.pl + ops_off(row, c0 + cc, Np)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
-  S.red_sum[g][row] = l;
+  S.red_sum[g][row] = static_cast<int32_t>(lsum);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -459,40 +505,64 @@ __global__ void __launch_bounds__(kWideThreads, 1) attention_i8_wide_kernel(cons
     }
     tc_commit(&S.bar);
   }
+  // Meanwhile: the positional term of this row's 16 channels, a depthwise
+  // 3x3 of v around the query (zero outside the image), as dp4a over taps.
+  const int qi = q0 + row;
+  const int d0 = 16 * g;
+  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
+  int acc[16];
+  {
+    uint32_t tw[9][4];
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+      const int iy = y - 1 + tap / 3, ix = x - 1 + tap % 3;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (qi < N && iy >= 0 && iy < a.H && ix >= 0 && ix < a.W)
+        v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * KD + d0);
+      tw[tap][0] = v.x;
+      tw[tap][1] = v.y;
+      tw[tap][2] = v.z;
+      tw[tap][3] = v.w;
+    }
+#pragma unroll
+    for (int qd = 0; qd < 4; ++qd) {
+      uint32_t lo[4], hi[4];
+      transpose4w(tw[0][qd], tw[1][qd], tw[2][qd], tw[3][qd], lo);
+      transpose4w(tw[4][qd], tw[5][qd], tw[6][qd], tw[7][qd], hi);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = d0 + 4 * qd + e;
+        const uint4 w = *reinterpret_cast<const uint4*>(S.pw[d]);
+        int s = __dp4a(static_cast<int>(lo[e]), static_cast<int>(w.x), 0);
+        s = __dp4a(static_cast<int>(hi[e]), static_cast<int>(w.y), s);
+        s += static_cast<int>(static_cast<int8_t>(tw[8][qd] >> (8 * e))) * static_cast<int>(static_cast<int8_t>(w.z));
+        acc[4 * qd + e] = s;
+      }
+    }
+  }
   wait_mma();
   __syncthreads();
   const bool good = S.abort == 0;
-  const int qi = q0 + row;
   const bool valid = qi < N && good;
-  l = S.red_sum[0][row] + S.red_sum[1][row] + S.red_sum[2][row] + S.red_sum[3][row];
+  int l = 0;
+#pragma unroll
+  for (int gg = 0; gg < 4; ++gg) {
+    const uint32_t ls = static_cast<uint32_t>(S.red_sum[gg][row]);
+    l += 64 * static_cast<int>(ls & 0xFFFFu) + static_cast<int>(ls >> 16);
+  }
   const double rl = 1.0 / static_cast<double>(l > 0 ? l : 1);
-  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
-  const int d0 = 16 * g;
   uint32_t oh[16], ol[16];
   tc_ld_32x32b_x16(trow + static_cast<uint32_t>(d0), oh);
   tc_ld_32x32b_x16(trow + 64u + static_cast<uint32_t>(d0), ol);
   tc_wait_ld();
   if (valid) {
-    // Positional term: depthwise 3x3 of v (channels h*HD + d) around the query.
-    int acc[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) acc[e] = 0;
-    for (int tap = 0; tap < 9; ++tap) {
-      const int iy = y - 1 + tap / 3, ix = x - 1 + tap % 3;
-      if (iy < 0 || iy >= a.H || ix < 0 || ix >= a.W) continue;
-      const uint4 v = *reinterpret_cast<const uint4*>(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride +
-                                                      2 * KD + d0);
-      const int8_t* vb = reinterpret_cast<const int8_t*>(&v);
-#pragma unroll
-      for (int e = 0; e < 16; ++e) acc[e] += static_cast<int>(vb[e]) * static_cast<int>(S.pe[tap * HD + d0 + e]);
-    }
     uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
-      const int ch = h * HD + d0 + e;
+      const int d = d0 + e;
       const long long o = 64LL * static_cast<int32_t>(oh[e]) + static_cast<int32_t>(ol[e]);
       const long long av = div_rne_fast(rne64(o * a.mo, a.sho), l, rl);
-      const long long pe = rne64((static_cast<long long>(acc[e]) + a.pe_bq[ch]) * a.pe_mult[ch], a.pe_shift[ch]);
+      const long long pe = rne64((static_cast<long long>(acc[e]) + S.pq[0][d]) * S.pq[1][d], S.pq[2][d]);
       const long long v = av + pe;
       const int c = static_cast<int>(v < -127 ? -127 : v > 127 ? 127 : v);
       w[e >> 2] |= (static_cast<uint32_t>(c) & 0xFFu) << (8 * (e & 3));

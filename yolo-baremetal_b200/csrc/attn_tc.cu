@@ -304,6 +304,8 @@ struct AttnWideTcSmem {
   uint8_t vh[THD * kWideNF * 2], vl[THD * kWideNF * 2];
   float red_max[4][kTQ];
   float red_sum[4][kTQ];
+  float pew[9][THD];  // positional weights of this head, [tap][channel]
+  float peb[THD];
   uint64_t bar;
   uint64_t slot_bar[2];
   uint32_t tmem;
@@ -323,6 +325,8 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
   const int blk = 2 * TKD + THD;
   const uint16_t* base = a.qkv.hi + static_cast<long long>(b) * a.qkv.bstride + a.qkv.coff + h * blk;
   const long long pl = a.qkv.plane;
+  for (int i = tid; i < 9 * THD; i += kWideTF) S.pew[i / THD][i % THD] = a.pe_w[(i / THD) * (a.heads * THD) + h * THD + i % THD];
+  for (int i = tid; i < THD; i += kWideTF) S.peb[i] = a.pe_b[h * THD + i];
   if (tid == 0) {
     mbar_init(&S.bar, 1);
     mbar_init(&S.slot_bar[0], 1);
@@ -495,10 +499,9 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int dd = d0 + 8 * half;
-      const int ch = h * THD + dd;
       float pe[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) pe[e] = __ldg(a.pe_b + ch + e);
+      for (int e = 0; e < 8; ++e) pe[e] = S.peb[dd + e];
       for (int ky = 0; ky < 3; ++ky) {
         const int iy = y - 1 + ky;
         if (iy < 0 || iy >= a.H) continue;
@@ -507,9 +510,9 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
           if (ix < 0 || ix >= a.W) continue;
           float v[8];
           load8(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * TKD + dd, pl, v);
-          const float* w = a.pe_w + (ky * 3 + kx) * (a.heads * THD) + ch;
+          const float* w = S.pew[ky * 3 + kx] + dd;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v[e], __ldg(w + e)));
+          for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v[e], w[e]));
         }
       }
       float res[8];
