@@ -54,6 +54,30 @@ constexpr uint32_t kPatchChunk = 2944;
 __host__ __device__ constexpr uint32_t patch_stage_bytes_i8(int ci_pad) {
   return ((static_cast<uint32_t>(ci_pad / 16) * kPatchChunk) + 1023u) & ~1023u;
 }
+// Stride-2 patch mode: a tile of 16 x 8 output pixels reads input rows
+// 2 oy0 - 1 .. 2 oy0 + 31 (33) and columns 2 ox0 - 1 .. 2 ox0 + 15.  Per
+// 16-channel chunk two boxes with a column traversal stride of 2 (box 18
+// columns -> 9 pixels): plane O holds columns 2 ox0 - 1 + 2i (taps kx = 0 at
+// i = c, kx = 2 at i = c + 1), plane E columns 2 ox0 + 2i (kx = 1 at i = c),
+// so every tap window is 8 consecutive 16-byte pixels per output row and
+// the next output row is two input rows (288 bytes) further.
+constexpr int kP2Rows = 33, kP2Cols = 9;
+constexpr uint32_t kP2Row = kP2Cols * 16;                 // 144 bytes per plane row
+constexpr uint32_t kP2Box = kP2Rows * kP2Row;             // 4752 bytes written by one box copy
+constexpr uint32_t kP2Plane = 4864;                       // plane stride (128-byte multiple)
+constexpr uint32_t kP2Chunk = 2 * kP2Plane;               // O and E planes of one 16-channel chunk
+__host__ __device__ constexpr uint32_t patch2_stage_bytes_i8(int ci_pad) {
+  return ((static_cast<uint32_t>(ci_pad / 16) * kP2Chunk) + 1023u) & ~1023u;
+}
+// Window of tap t (ky = t / 3, kx = t % 3) from the chunk origin.
+__host__ __device__ constexpr uint32_t p2_window(int t) {
+  return ((t % 3) == 1 ? kP2Plane : 0u) + static_cast<uint32_t>(t / 3) * kP2Row + ((t % 3) == 2 ? 16u : 0u);
+}
+// K order of the taps for 16 channels (two taps per 32-byte K step): pairs
+// with the second window above the first (the descriptor's LBO is unsigned).
+__host__ __device__ constexpr int p2_tap(int pos) {
+  return pos == 3 ? 4 : pos == 4 ? 3 : pos == 5 ? 7 : pos == 6 ? 5 : pos == 7 ? 6 : pos;
+}
 
 }  // namespace
 
@@ -159,12 +183,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
   const uint32_t chunk_bytes = static_cast<uint32_t>(a.n_tile) * 128u;
   // Patch mode keeps every weight chunk resident in front of the stages.
   const bool patch = a.patch != 0;
+  const bool patch2 = a.patch == 2;
   const int ci_pad = a.K / (a.kh * a.kw);
   const uint32_t wres_bytes = patch ? static_cast<uint32_t>(a.num_kc) * chunk_bytes : 0u;
-  const uint32_t stage_bytes = patch ? patch_stage_bytes_i8(ci_pad) : kATile + chunk_bytes;
+  const uint32_t stage_bytes = patch2  ? patch2_stage_bytes_i8(ci_pad)
+                               : patch ? patch_stage_bytes_i8(ci_pad)
+                                       : kATile + chunk_bytes;
   uint8_t* stage0 = smem + wres_bytes;
 
-  uint8_t* tail = stage0 + stages * stage_bytes;
+  // Stride-2 patch mode leaves one plane of slack after the last stage.
+  uint8_t* tail = stage0 + stages * stage_bytes + (patch2 ? kP2Plane : 0u);
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;
@@ -263,6 +291,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
         const int ty = rem / a.tiles_x;
         const int tx = rem - ty * a.tiles_x;
         uint8_t* stage = stage0 + s * stage_bytes;
+        if (patch2) {
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ncb) * 2u * kP2Box);
+          for (int cb = 0; cb < ncb; ++cb) {
+            tma_tile_4d(stage + cb * kP2Chunk, &a.tm, 16 * cb, tx * 16 - 1, ty * 32 - 1, b, &full[s]);
+            tma_tile_4d(stage + cb * kP2Chunk + kP2Plane, &a.tm, 16 * cb, tx * 16, ty * 32 - 1, b, &full[s]);
+          }
+          continue;
+        }
         mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(ncb) * kPatchBox);
         for (int cb = 0; cb < ncb; ++cb)
           tma_tile_4d(stage + cb * kPatchChunk, &a.tm, 16 * cb, tx * 8 - 1, ty * 16 - 1, b, &full[s]);
@@ -351,6 +387,40 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
           const uint64_t da0 = kmajor_desc_noswizzle(smem_u32(stage0 + s * stage_bytes), kPatchChunk, kPatchW * 16);
           const uint64_t db0 = sw128_kmajor_desc(smem_u32(smem));
           const uint64_t chunk_units = chunk_bytes >> 4;
+          if (patch2) {
+            // Stride 2: output row stride 2 input rows (SBO 288 bytes).
+            const uint32_t pa = smem_u32(stage0 + s * stage_bytes);
+            if (ci_pad == 16) {
+              // Two taps per K step in the K order p2_tap (second window
+              // above the first); tap 8 pairs with zero weights.
+              for (int s2 = 0; s2 < 5; ++s2) {
+                const int t0 = p2_tap(2 * s2), t1 = 2 * s2 + 1 < 9 ? p2_tap(2 * s2 + 1) : t0;
+                const uint32_t o0 = p2_window(t0), o1 = p2_window(t1);
+                const uint64_t da = kmajor_desc_noswizzle(pa + o0, t1 == t0 ? 16u : o1 - o0, 2 * kP2Row);
+                const int k = 32 * s2;
+                const uint64_t boff =
+                    static_cast<uint64_t>(k / kKB) * chunk_units + static_cast<uint64_t>(((k % kKB) / 32) * 2);
+                tc_mma_i8(d_tmem, da, db0 + boff, idesc, s2 != 0 ? 1u : 0u);
+              }
+            } else {
+              // Per tap, 32 channels per K step: the chunks 2 c2 and 2 c2 + 1.
+              int step = 0;
+              for (int tap = 0; tap < 9; ++tap) {
+                for (int c2 = 0; c2 < ci_pad / 32; ++c2, ++step) {
+                  const uint64_t da =
+                      kmajor_desc_noswizzle(pa + 2u * static_cast<uint32_t>(c2) * kP2Chunk + p2_window(tap), kP2Chunk,
+                                            2 * kP2Row);
+                  const int k = tap * ci_pad + 32 * c2;
+                  const uint64_t boff =
+                      static_cast<uint64_t>(k / kKB) * chunk_units + static_cast<uint64_t>(((k % kKB) / 32) * 2);
+                  tc_mma_i8(d_tmem, da, db0 + boff, idesc, step != 0 ? 1u : 0u);
+                }
+              }
+            }
+            tc_commit(&empty[s]);
+            tc_commit(&acc_full[acc]);
+            continue;
+          }
           if (ci_pad == 16) {
             // At most 16 input channels: two taps per 32-byte K step.  The A
             // operand's second core matrix is the next tap's window (LBO =
@@ -618,6 +688,11 @@ void i8_tiling_pair(int co, I8Tiling* t) {
   t->num_kc = (t->K + kKB - 1) / kKB;
 }
 
+void i8_tiling_pair_s2(int co, I8Tiling* t) {
+  i8_tiling_pair(co, t);
+  t->tap_perm = 1;
+}
+
 void i8_tiling(int co, int ci, int kh, int kw, I8Tiling* t) {
   const int taps = kh * kw;
   if (taps == 1) {
@@ -647,8 +722,9 @@ std::vector<uint8_t> i8_pack_weights(const int8_t* wq, int co, int ci, int kh, i
         for (int kk = 0; kk < kKB; ++kk) {
           const int k = kc * kKB + kk;
           if (k >= t.K) break;
-          const int tap = k / t.ci_pad;
-          const int cc = k - tap * t.ci_pad;
+          const int pos = k / t.ci_pad;
+          const int tap = t.tap_perm ? p2_tap(pos) : pos;
+          const int cc = k - pos * t.ci_pad;
           if (cc >= ci) continue;
           const int ky = tap / kw, kx = tap - (tap / kw) * kw;
           const int8_t v = wq[((static_cast<size_t>(n) * ci + cc) * kh + ky) * kw + kx];
@@ -683,7 +759,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
   // the resident weights.  16 padded channels exist only in patch mode.
   a.patch = 0;
   if (a.kh == 3 && a.kw == 3 && a.stride == 1 && a.pad == 1 && a.Ho == a.H && a.Wo == a.W && a.n_tiles == 1 &&
-      (ci_pad == 16 || ci_pad == 32 || ci_pad == 64) && a.K == 9 * ci_pad && a.n_tile <= 128) {
+      (ci_pad == 16 || ci_pad == 32 || ci_pad == 64) && a.K == 9 * ci_pad && a.n_tile <= 128 && !a.tap_perm) {
     const int wres = a.num_kc * a.n_tile * 128;
     const int pst = static_cast<int>(patch_stage_bytes_i8(ci_pad));
     int st = (kSmemLimit - 1024 - wres - tail) / pst;
@@ -705,6 +781,39 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
         a.tiles_x = (a.Wo + 7) / 8;
         a.m_tiles = a.B * a.tiles_y * a.tiles_x;
         const int smem = 1024 + wres + st * pst + tail;
+        if (a.m_tiles <= 0) return cudaSuccess;
+        const int grid = a.m_tiles < sms ? a.m_tiles : sms;
+        return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, st);
+      }
+    }
+  }
+  // Stride-2 patch mode: 3x3 stride 2 pad 1, one N tile, 16 (two taps per K
+  // step, taps in the p2_tap order), 32 or 64 padded input channels.
+  if (a.kh == 3 && a.kw == 3 && a.stride == 2 && a.pad == 1 && a.Ho == (a.H - 1) / 2 + 1 &&
+      a.Wo == (a.W - 1) / 2 + 1 && a.n_tiles == 1 && (ci_pad == 16 || ci_pad == 32 || ci_pad == 64) &&
+      a.K == 9 * ci_pad && a.n_tile <= 128 && (ci_pad != 16 || a.tap_perm)) {
+    const int wres = a.num_kc * a.n_tile * 128;
+    const int pst = static_cast<int>(patch2_stage_bytes_i8(ci_pad));
+    int st = (kSmemLimit - 1024 - wres - static_cast<int>(kP2Plane) - tail) / pst;
+    st = st > 8 ? 8 : st;
+    const auto tenc = i8_tiled_encoder();
+    if (st >= 3 && tenc) {
+      cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Ci), static_cast<cuuint64_t>(a.W),
+                            static_cast<cuuint64_t>(a.H), static_cast<cuuint64_t>(a.B)};
+      cuuint64_t strides[3] = {static_cast<cuuint64_t>(x_cstride), static_cast<cuuint64_t>(x_cstride) * a.W,
+                               static_cast<cuuint64_t>(x_bstride)};
+      // 18 columns traversed with stride 2: 9 pixels per box row.
+      cuuint32_t box[4] = {16, 2 * kP2Cols, kP2Rows, 1};
+      cuuint32_t estr[4] = {1, 2, 1, 1};
+      const CUresult cr = tenc(&a.tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(x), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (cr == CUDA_SUCCESS) {
+        a.patch = 2;
+        a.tiles_y = (a.Ho + 15) / 16;
+        a.tiles_x = (a.Wo + 7) / 8;
+        a.m_tiles = a.B * a.tiles_y * a.tiles_x;
+        const int smem = 1024 + wres + st * pst + static_cast<int>(kP2Plane) + tail;
         if (a.m_tiles <= 0) return cudaSuccess;
         const int grid = a.m_tiles < sms ? a.m_tiles : sms;
         return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, st);

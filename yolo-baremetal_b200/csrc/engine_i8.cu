@@ -222,6 +222,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
       return fail("int8: padded output must own its tensor: " + P);
     I8Tiling t;
     if (k == 3 && stride == 1 && pad == 1 && ci <= 16 && co_pad <= 128 && !f32.ptr) i8_tiling_pair(co_pad, &t);
+    else if (k == 3 && stride == 2 && pad == 1 && ci <= 16 && co_pad <= 128 && !f32.ptr) i8_tiling_pair_s2(co_pad, &t);
     else i8_tiling(co_pad, ci, k, k, &t);
     if (t.ci_pad != 16) {
       // Fewer than two waves of tiles: narrower N tiles (64 or 128 columns)
@@ -275,6 +276,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     a.n_tiles = t.n_tiles;
     a.m_tiles = static_cast<int>((static_cast<long long>(B) * a.Ho * a.Wo + 127) / 128);
     a.a_cpp = t.a_cpp;
+    a.tap_perm = t.tap_perm;
     a.wpack = static_cast<const uint8_t*>(dw);
     a.bias = static_cast<const int32_t*>(db);
     a.mult = static_cast<const int32_t*>(dm);

@@ -21,10 +21,11 @@ namespace yb {
 struct I8Args {
   int B = 0, H = 0, W = 0, Ci = 0, Co = 0, kh = 1, kw = 1, stride = 1, pad = 0, Ho = 0, Wo = 0;
   int K = 0, num_kc = 0, n_tile = 0, n_tiles = 0, m_tiles = 0, a_cpp = 0;
-  // Patch mode (set by launch_conv_i8 for 3x3 stride-1 convolutions of at
-  // most 64 input channels with one N tile): tiles of 16 x 8 output pixels,
-  // m_tiles = B * tiles_y * tiles_x.
+  // Patch mode (set by launch_conv_i8 for 3x3 convolutions of at most 64
+  // input channels with one N tile; 1: stride 1, 2: stride 2): tiles of
+  // 16 x 8 output pixels, m_tiles = B * tiles_y * tiles_x.
   int patch = 0, tiles_y = 0, tiles_x = 0;
+  int tap_perm = 0;  // the weights hold the taps in the stride-2 patch order (16 channels)
   const uint8_t* wpack = nullptr;
   const int32_t* bias = nullptr;
   const int32_t* mult = nullptr;
@@ -48,11 +49,15 @@ struct I8Args {
 // (ky, kx, ci) in 128-wide chunks; a_cpp channels per TMA copy.
 struct I8Tiling {
   int ci_pad = 0, a_cpp = 0, K = 0, num_kc = 0, n_tile = 0, n_tiles = 0;
+  int tap_perm = 0;  // 1: the stride-2 patch mode's K order of the taps (16 channels)
 };
 void i8_tiling(int co, int ci, int kh, int kw, I8Tiling* t);
 // 3x3 stride-1 convolutions of at most 16 input channels in patch mode: K
 // ordered (tap, channel) with 16 channels per tap, two taps per UMMA.
 void i8_tiling_pair(int co, I8Tiling* t);
+// The same for 3x3 stride-2 convolutions (stride-2 patch mode): the taps in
+// the K order {0, 1, 2, 4, 3, 7, 5, 6, 8}.
+void i8_tiling_pair_s2(int co, I8Tiling* t);
 // wq [co][ci][kh][kw] -> per N tile and K chunk, n_tile 128-byte rows,
 // 128B-swizzled (what the kernel's bulk copies load).
 std::vector<uint8_t> i8_pack_weights(const int8_t* wq, int co, int ci, int kh, int kw, const I8Tiling& t);
