@@ -65,6 +65,24 @@ constexpr uint32_t kPatchBox = kPatchH * kPatchW * 16;  // 2880 bytes written by
 constexpr uint32_t kPatchChunk = 2944;
 __host__ __device__ constexpr uint32_t patch_stage_bytes(int ci) {
   return ((static_cast<uint32_t>(ci / 8) * 2u * kPatchChunk) + 1023u) & ~1023u;
+}
+// Stride-2 patch mode (a_tma == 3): a tile of 16 x 8 output pixels reads
+// input rows 2 oy0 - 1 .. 2 oy0 + 31 (33) and columns 2 ox0 - 1 .. 2 ox0 + 15.
+// Per 8-channel chunk and plane two boxes with a column traversal stride of 2
+// (box 18 columns -> 9 pixels): O holds columns 2 ox0 - 1 + 2i (taps kx = 0
+// at i = c, kx = 2 at i = c + 1), E columns 2 ox0 + 2i (kx = 1 at i = c), so
+// every tap window is 8 consecutive 16-byte pixels per output row and the
+// next output row is two input rows (288 bytes) further.
+constexpr int kP2Rows = 33, kP2Cols = 9;
+constexpr uint32_t kP2Row = kP2Cols * 16;      // 144 bytes per row
+constexpr uint32_t kP2Box = kP2Rows * kP2Row;  // 4752 bytes written by one box copy
+constexpr uint32_t kP2Plane = 4864;            // 128-byte multiple
+constexpr uint32_t kP2Chunk = 2 * kP2Plane;    // O and E of one 8-channel chunk
+__host__ __device__ constexpr uint32_t patch2_stage_bytes(int ci) {
+  return ((static_cast<uint32_t>(ci / 8) * 2u * kP2Chunk) + 1023u) & ~1023u;
+}
+__host__ __device__ constexpr uint32_t p2_window(int t) {
+  return ((t % 3) == 1 ? kP2Plane : 0u) + static_cast<uint32_t>(t / 3) * kP2Row + ((t % 3) == 2 ? 16u : 0u);
 }          // alignment slack + barriers; the bias follows
 
 
@@ -91,14 +109,18 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const bool patch = a.a_tma == 2;
+  const bool patch = a.a_tma >= 2;
+  const bool patch2 = a.a_tma == 3;
   const uint32_t chunk_bytes = static_cast<uint32_t>(a.n_tile) * 256u;
   // Patch mode keeps every weight chunk resident in front of the stages.
   const uint32_t wres_bytes = patch ? static_cast<uint32_t>(a.num_kc) * chunk_bytes : 0u;
-  const uint32_t stage_bytes = patch ? patch_stage_bytes(a.Ci) : 2u * kAPlaneBytes + chunk_bytes;
+  const uint32_t stage_bytes = patch2  ? patch2_stage_bytes(a.Ci)
+                               : patch ? patch_stage_bytes(a.Ci)
+                                       : 2u * kAPlaneBytes + chunk_bytes;
   uint8_t* stage0 = smem + wres_bytes;
 
-  uint8_t* tail = stage0 + stages * stage_bytes;
+  // Stride-2 patch mode leaves one plane of slack after the last stage.
+  uint8_t* tail = stage0 + stages * stage_bytes + (patch2 ? kP2Plane : 0u);
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;
@@ -143,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     tmem_alloc(tmem_slot, ncols);
     tmem_relinquish();
   }
-  if (patch && a.Ci == 8) {
+  if (patch && !patch2 && a.Ci == 8) {
     // The paired K step of tap 8 reads the pixel after its window (against
     // zero weights); for the last patch row that is the pad after the box,
     // which no copy writes.  Zero it so that stale bytes (possibly NaN or
@@ -193,6 +215,18 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const int ty = rem / a.tiles_x;
         const int tx = rem - ty * a.tiles_x;
         uint8_t* stage = stage0 + s * stage_bytes;
+        if (patch2) {
+          mbar_arrive_expect_tx(&full[s], 4u * static_cast<uint32_t>(nch) * kP2Box);
+          for (int ch = 0; ch < nch; ++ch) {
+            uint8_t* hi = stage + ch * kP2Chunk;
+            uint8_t* lo = stage + (nch + ch) * kP2Chunk;
+            tma_tile_4d(hi, &a.tm_hi, 8 * ch, tx * 16 - 1, ty * 32 - 1, b, &full[s]);
+            tma_tile_4d(hi + kP2Plane, &a.tm_hi, 8 * ch, tx * 16, ty * 32 - 1, b, &full[s]);
+            tma_tile_4d(lo, &a.tm_lo, 8 * ch, tx * 16 - 1, ty * 32 - 1, b, &full[s]);
+            tma_tile_4d(lo + kP2Plane, &a.tm_lo, 8 * ch, tx * 16, ty * 32 - 1, b, &full[s]);
+          }
+          continue;
+        }
         mbar_arrive_expect_tx(&full[s], 2u * static_cast<uint32_t>(nch) * kPatchBox);
         for (int ch = 0; ch < nch; ++ch) {
           tma_tile_4d(stage + ch * kPatchChunk, &a.tm_hi, 8 * ch, tx * 8 - 1, ty * 16 - 1, b, &full[s]);
@@ -554,6 +588,34 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           const uint64_t dbh0 = sw128_kmajor_desc(smem_u32(smem));
           const uint64_t dbl0 = sw128_kmajor_desc(smem_u32(smem) + static_cast<uint32_t>(a.n_tile) * 128u);
           const uint64_t chunk_units = chunk_bytes >> 4;
+          if (patch2) {
+            // Stride 2 (Ci a multiple of 16): per tap, 16 channels per K step
+            // = the 8-channel chunks 2 cb and 2 cb + 1 (LBO one chunk); the
+            // output row stride is two input rows (SBO 288 bytes).
+            int step = 0;
+            for (int tap = 0; tap < 9; ++tap) {
+              for (int cb = 0; cb < cbs; ++cb, ++step) {
+                const uint32_t ao = 2u * static_cast<uint32_t>(cb) * kP2Chunk + p2_window(tap);
+                const uint64_t dah = kmajor_desc_noswizzle(pa + ao, kP2Chunk, 2 * kP2Row);
+                const uint64_t dal =
+                    kmajor_desc_noswizzle(pa + static_cast<uint32_t>(nch) * kP2Chunk + ao, kP2Chunk, 2 * kP2Row);
+                const uint64_t boff =
+                    static_cast<uint64_t>(step >> 2) * chunk_units + static_cast<uint64_t>((step & 3) * 2);
+                const uint32_t accum = step != 0 ? 1u : 0u;
+                if (stacked) {
+                  tc_mma_bf16(d_tmem, dah, dbh0 + boff, idesc, accum);
+                  tc_mma_bf16(d_tmem, dal, dbh0 + boff, idesc, 1u);
+                } else {
+                  tc_mma_bf16(d_tmem, dah, dbh0 + boff, idesc, accum);
+                  tc_mma_bf16(d_tmem, dah, dbl0 + boff, idesc, 1u);
+                  tc_mma_bf16(d_tmem, dal, dbh0 + boff, idesc, 1u);
+                }
+              }
+            }
+            tc_commit(&empty[s]);
+            tc_commit(&acc_full[acc]);
+            continue;
+          }
           if (a.Ci == 8) {
             // Eight input channels (16 bytes per pixel and plane): two taps
             // per 16-wide K step.  The A operand's second core matrix is the
@@ -812,16 +874,39 @@ bool encode_patch_plane(CUtensorMap* map, const ConvArgs& a, const uint16_t* bas
 }
 
 int conv_stage_bytes(const ConvArgs& a) {
-  return a.a_tma == 2 ? static_cast<int>(patch_stage_bytes(a.Ci))
-                      : 2 * static_cast<int>(kAPlaneBytes) + static_cast<int>(conv_chunk_bytes(a.n_tile));
+  return a.a_tma == 3   ? static_cast<int>(patch2_stage_bytes(a.Ci))
+         : a.a_tma == 2 ? static_cast<int>(patch_stage_bytes(a.Ci))
+                        : 2 * static_cast<int>(kAPlaneBytes) + static_cast<int>(conv_chunk_bytes(a.n_tile));
 }
 int conv_resident_bytes(const ConvArgs& a) {
-  return a.a_tma == 2 ? a.num_kc * static_cast<int>(conv_chunk_bytes(a.n_tile)) : 0;
+  return a.a_tma >= 2 ? a.num_kc * static_cast<int>(conv_chunk_bytes(a.n_tile)) : 0;
 }
+// Slack after the last stage (stride-2 patch mode).
+int conv_slack_bytes(const ConvArgs& a) { return a.a_tma == 3 ? static_cast<int>(kP2Plane) : 0; }
 int conv_stages(const ConvArgs& a) {
-  const int st = (kSmemLimit - kSmemExtra - bias_bytes(a.n_tile, a.n_tiles) - conv_resident_bytes(a)) /
+  const int st = (kSmemLimit - kSmemExtra - bias_bytes(a.n_tile, a.n_tiles) - conv_resident_bytes(a) -
+                  conv_slack_bytes(a)) /
                  conv_stage_bytes(a);
   return st > 8 ? 8 : st;
+}
+
+// Tiled map over one plane, dims (C, W, H, N), boxes of 8 channels x 18
+// columns (traversed with stride 2: 9 pixels) x 33 rows of one image.
+bool encode_patch2_plane(CUtensorMap* map, const ConvArgs& a, const uint16_t* base) {
+  const auto enc = tiled_encoder();
+  if (!enc) return false;
+  const long long cs = a.src0.cstride;
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (cs * 2) % 16 || (a.src0.bstride * 2) % 16) return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(a.Ci), static_cast<cuuint64_t>(a.W), static_cast<cuuint64_t>(a.H),
+                        static_cast<cuuint64_t>(a.B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(cs * 2), static_cast<cuuint64_t>(cs * 2 * a.W),
+                           static_cast<cuuint64_t>(a.src0.bstride * 2)};
+  cuuint32_t box[4] = {8, 2 * kP2Cols, kP2Rows, 1};
+  cuuint32_t estr[4] = {1, 2, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<uint16_t*>(base), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -844,8 +929,25 @@ bool conv_setup_patch(ConvArgs* a) {
   return true;
 }
 
+bool conv_setup_patch2(ConvArgs* a) {
+  if (a->kh != 3 || a->kw != 3 || a->stride != 2 || a->pad != 1) return false;
+  if (a->lg_up0 || a->lg_up1 || a->c_split != a->Ci || a->Ci % 16 || !a->src0.hi || a->n_tiles != 1) return false;
+  if (a->K != 9 * a->Ci || a->Ho != (a->H - 1) / 2 + 1 || a->Wo != (a->W - 1) / 2 + 1) return false;
+  ConvArgs t = *a;
+  t.a_tma = 3;
+  if (conv_stages(t) < 3) return false;  // resident weights leave too little room
+  const uint16_t* hi = a->src0.hi + a->src0.coff;
+  if (!encode_patch2_plane(&t.tm_hi, t, hi) || !encode_patch2_plane(&t.tm_lo, t, hi + a->src0.plane)) return false;
+  t.a_cpp = 0;
+  t.tiles_y = (a->Ho + 15) / 16;
+  t.tiles_x = (a->Wo + 7) / 8;
+  t.m_tiles = a->B * t.tiles_y * t.tiles_x;
+  *a = t;
+  return true;
+}
+
 void conv_setup_tma(ConvArgs* a) {
-  if (conv_setup_patch(a)) return;
+  if (conv_setup_patch(a) || conv_setup_patch2(a)) return;
   if (a->lg_up0 || a->lg_up1 || a->c_split != a->Ci || a->Ci % 16 || !a->src0.hi) return;
   const int taps = a->kh * a->kw;
   if (a->K != taps * a->Ci) return;
@@ -883,9 +985,13 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
   if (a.a_tma == 2 && (a.n_tiles != 1 || a.kh != 3 || a.kw != 3 || (a.Ci % 16 && a.Ci != 8) || a.tiles_x < 1 || a.tiles_y < 1 ||
                        a.m_tiles != a.B * a.tiles_y * a.tiles_x))
     return cudaErrorInvalidValue;
+  if (a.a_tma == 3 && (a.n_tiles != 1 || a.kh != 3 || a.kw != 3 || a.stride != 2 || a.Ci % 16 || a.tiles_x < 1 ||
+                       a.tiles_y < 1 || a.m_tiles != a.B * a.tiles_y * a.tiles_x))
+    return cudaErrorInvalidValue;
   const int stages = conv_stages(a);
   if (stages < 2) return cudaErrorInvalidValue;
-  const int smem = kSmemExtra + bias_bytes(a.n_tile, a.n_tiles) + conv_resident_bytes(a) + stages * conv_stage_bytes(a);
+  const int smem = kSmemExtra + bias_bytes(a.n_tile, a.n_tiles) + conv_resident_bytes(a) + stages * conv_stage_bytes(a) +
+                   conv_slack_bytes(a);
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
   const int grid = total < num_sms ? total : num_sms;

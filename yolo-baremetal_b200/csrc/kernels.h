@@ -99,7 +99,8 @@ struct ConvArgs {
   // a_tma == 2 (3x3 stride-1 convolutions, see conv_setup_patch): tiles of
   // 16 x 8 output pixels, tiles_y x tiles_x per image; the 18 x 10 input
   // patch of a tile is loaded once per 8-channel chunk and plane, and the
-  // weights stay resident in shared memory.
+  // weights stay resident in shared memory.  a_tma == 3: the same for 3x3
+  // stride-2 convolutions (33 x 17 patch as odd / even column boxes).
   int tiles_y = 0, tiles_x = 0;
   alignas(64) CUtensorMap tm_hi;
   alignas(64) CUtensorMap tm_lo;
