@@ -41,9 +41,10 @@ METRIC = "images/sec YOLO26n 640² FP32 & INT8 at 1/2/4/8 B200; conv TFLOPS/TOPS
 UNIT = "images/s"
 DATA = ("synthetic: seeded U[0,1) 640x640 images (numpy PCG64), seeded random-init YOLO26n weights "
         "(Kaiming conv, BN gamma 1+-0.1, beta/mean N(0,0.1), var U(0.5,1.5)) in the converter .bin layout")
-# DRAM bytes (read + write) of the conv family per image, from the ncu capture
-# summarised in profiles/conv_tc_yolo26n_640.md; None until captured.
-CONV_DRAM_BYTES_PER_IMAGE = None
+# DRAM bytes (read + write) of the conv family per image: 1637.4 MB over the
+# 93 convolution launches of one 64-image forward, ncu capture summarised in
+# profiles/conv_tc_dram_traffic_yolo26n_b64.md.
+CONV_DRAM_BYTES_PER_IMAGE = 1637.4e6 / 64
 
 
 def peaks():
@@ -437,6 +438,9 @@ def run_ours(args):
                 "gpu_launches": n_ops.value * args.steps,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic,
+                             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the 93 conv "
+                                               "launches of one 64-image forward, scaled by images "
+                                               "(profiles/conv_tc_dram_traffic_yolo26n_b64.md)",
                              "kernel": "conv_tc_kernel (all tcgen05 convolution launches of one forward)",
                              "launches": len(conv), "bytes_per_launch": conv_bytes / len(conv),
                              "ms_per_launch": conv_ms / len(conv), "peak_source": src},
