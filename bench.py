@@ -395,6 +395,8 @@ def run_ours(args):
     # resize_rgb_bilinear + preprocess on the device): a quarter of the bytes.
     rgb8 = rgb8_frames(rank, B, H)
     e2e8_s = timed_rgb8(L, model, rgb8, host_out, B, H, args, barrier, max_over_ranks)
+    es_s = timed_stream(model, host_in, B, H, args, barrier, max_over_ranks)
+    es8_s = timed_stream(model, rgb8, B, H, args, barrier, max_over_ranks, rgb8=True)
 
     n_ops = C.c_int()
     yb.check(L.yb_cuda_profile_ops(model.ctx, B, H, H, 300, 0, None, 0, C.byref(n_ops)), "yb_cuda_profile_ops")
@@ -426,15 +428,20 @@ def run_ours(args):
                 "precision": "fp32 activations in HBM; conv products as bf16 hi/lo pairs (3 tcgen05 UMMAs) "
                              "with fp32 accumulation in TMEM",
                 "data": DATA, "config": config(world, B, H),
-                "e2e": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
+                "e2e": {"value": world * B * args.steps / es_s, "unit": UNIT,
                         "h2d_bytes_per_step": world * host_in.numel() * 4,
-                        "d2h_bytes_per_step": world * host_out.numel() * 4},
-                "e2e_rgb8": {"value": world * B * args.steps / e2e8_s, "unit": UNIT,
+                        "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": STREAM_NOTE},
+                "e2e_sync": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
+                             "h2d_bytes_per_step": world * host_in.numel() * 4,
+                             "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": SYNC_NOTE},
+                "e2e_rgb8": {"value": world * B * args.steps / es8_s, "unit": UNIT,
                              "h2d_bytes_per_step": world * rgb8.numel(),
-                             "d2h_bytes_per_step": world * host_out.numel() * 4,
+                             "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": STREAM_NOTE,
+                             "sync_value": world * B * args.steps / e2e8_s,
                              "source": f"{B} seeded uint8 RGB frames {H}x{H} per GPU per step through "
-                                       "yb_cuda_forward_rgb8 (device resize_rgb_bilinear + /255, then the "
-                                       "forward); same metric, 8-bit inputs instead of the fp32 tensor"},
+                                       "yb_cuda_forward_rgb8_submit (device resize_rgb_bilinear + /255, then the "
+                                       "forward); same metric, 8-bit inputs instead of the fp32 tensor; "
+                                       "sync_value: one blocking yb_cuda_forward_rgb8 per step"},
                 "gpu_launches": n_ops.value * args.steps,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic,
@@ -500,6 +507,44 @@ def timed_rgb8(L, model, rgb8, host_out, B, H, args, barrier, max_over_ranks):
     return e
 
 
+def timed_stream(model, src, B, H, args, barrier, max_over_ranks, rgb8=False):
+    """Wall time of K streamed steps (yb_cuda_forward_submit or
+    yb_cuda_forward_rgb8_submit, then yb_cuda_forward_wait): two batches in
+    flight, each step copying its own pinned input to the device and its
+    detections back into one of two pinned output buffers; max over ranks."""
+    import torch
+
+    outs = [torch.empty((B, 300, 6), dtype=torch.float32).pin_memory() for _ in range(2)]
+
+    def run(k):
+        pending = []
+        for i in range(k):
+            if len(pending) == 2:
+                model.wait(pending.pop(0))
+            o = outs[i % 2]
+            if rgb8:
+                pending.append(model.submit_rgb8(src.data_ptr(), B, H, H, o.data_ptr(), H, H))
+            else:
+                pending.append(model.submit(src.data_ptr(), B, H, H, o.data_ptr()))
+        for t in pending:
+            model.wait(t)
+
+    run(max(2, args.warmup // 2))
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    run(args.steps)
+    torch.cuda.synchronize()
+    e = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    return e
+
+
+STREAM_NOTE = ("streaming: yb_cuda_forward_submit / yb_cuda_forward_wait with two batches in flight; every step "
+               "copies its own pinned input to the device and its detections back inside the timed region")
+SYNC_NOTE = "one blocking yb_cuda_forward call per step (pipelined 16-image sub-batches inside the call)"
+
+
 INT8_KINDS = ["conv_i8", "stem_i8", "dw3x3_i8", "maxpool_concat_i8", "attention_i8", "decode", "topk"]
 INT8_CALIB_IMAGES = 32  # seeded U[0,1) calibration images (the benchmark's INT8 recipe)
 
@@ -561,6 +606,8 @@ def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_o
     barrier()
     rgb8 = rgb8_frames(rank, B, H)
     e2e8_s = timed_rgb8(L, model, rgb8, host_out, B, H, args, barrier, max_over_ranks)
+    es_s = timed_stream(model, host_in, B, H, args, barrier, max_over_ranks)
+    es8_s = timed_stream(model, rgb8, B, H, args, barrier, max_over_ranks, rgb8=True)
     # Batch 1 (the single-image INT8 configuration): device-resident latency.
     d1_in, d1_out = model.plan_io(1, H, H)
     torch.cuda.synchronize()
@@ -596,12 +643,16 @@ def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_o
                                       "image-parallel", "images_per_gpu": B, "global_batch": B * world},
                "calibration": {"images": INT8_CALIB_IMAGES, "source": "device (FP32 forwards with statistics), "
                                "seeded U[0,1) images", "scales": len(scales), "seconds": round(calib_s, 3)},
-               "e2e": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
+               "e2e": {"value": world * B * args.steps / es_s, "unit": UNIT,
                        "h2d_bytes_per_step": world * host_in.numel() * 4,
-                       "d2h_bytes_per_step": world * host_out.numel() * 4},
-               "e2e_rgb8": {"value": world * B * args.steps / e2e8_s, "unit": UNIT,
+                       "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": STREAM_NOTE},
+               "e2e_sync": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
+                            "h2d_bytes_per_step": world * host_in.numel() * 4,
+                            "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": SYNC_NOTE},
+               "e2e_rgb8": {"value": world * B * args.steps / es8_s, "unit": UNIT,
                             "h2d_bytes_per_step": world * rgb8.numel(),
-                            "d2h_bytes_per_step": world * host_out.numel() * 4},
+                            "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": STREAM_NOTE,
+                            "sync_value": world * B * args.steps / e2e8_s},
                "batch1": {"ms_per_image": b1_ms, "images_per_s": world / (b1_ms * 1e-3),
                           "note": "device-resident single-image forward, one per GPU"},
                "clocks": clocks,

@@ -130,6 +130,25 @@ status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int H, int W,
 status_t yb_cuda_forward_rgb8(void* ctx, const unsigned char* rgb_hwc, int B, int src_h, int src_w, int resize,
                               int H, int W, float* out_dets, int max_det);
 
+/* Streaming forward for a sequence of batches: queues the input copy, the
+ * forward and the detections' copy of one batch and returns without waiting;
+ * *ticket identifies the batch.  Two batches can be in flight per context
+ * (two captured graphs on their own streams): the input copy of one runs while
+ * the other computes.  A submit while both slots are busy first waits for the
+ * older batch of the slot it reuses.  in_nchw and out_dets (pinned host memory
+ * for the copies to overlap) must stay valid until yb_cuda_forward_wait
+ * returns for the ticket; detections and errors are those of yb_cuda_forward.
+ * The rgb8 form takes uint8 frames as yb_cuda_forward_rgb8 (the device
+ * preprocess runs on the batch's stream).  Replacing weights or the precision
+ * first finishes the batches in flight. */
+status_t yb_cuda_forward_submit(void* ctx, const float* in_nchw, int B, int H, int W, float* out_dets, int max_det,
+                                long long* ticket);
+status_t yb_cuda_forward_rgb8_submit(void* ctx, const unsigned char* rgb_hwc, int B, int src_h, int src_w,
+                                     int resize, int H, int W, float* out_dets, int max_det, long long* ticket);
+/* Waits until the batch of `ticket` is complete (its detections are in its
+ * out_dets).  A ticket that already completed returns SUCCESS. */
+status_t yb_cuda_forward_wait(void* ctx, long long ticket);
+
 /* The device preprocess alone: d_rgb [B, src_h, src_w, 3] uint8 and d_nchw
  * [B, 3, H, W] fp32 in the current device's memory; enqueued on `stream`
  * (NULL = the default stream), does not synchronize. */

@@ -87,7 +87,22 @@ struct Ctx {
   size_t d_rgb_bytes = 0;
   // Scale table of the last yb_cuda_calibrate_int8, in name order.
   std::vector<std::pair<std::string, float>> calib;
+  // Streaming forwards (yb_cuda_forward_submit / _wait): two slots, each a
+  // plan (tag kStreamTag + slot) on its own stream, with its own 8-bit input
+  // staging; ticket 0 marks a free slot.
+  struct StreamSlot {
+    cudaStream_t st = nullptr;
+    cudaEvent_t h2d = nullptr, done = nullptr;
+    long long ticket = 0;
+    Plan* plan = nullptr;
+    uint8_t* d_rgb = nullptr;
+    size_t d_rgb_bytes = 0;
+  };
+  StreamSlot sslot[2];
+  int sslot_next = 0;
+  long long next_ticket = 1;
 };
+constexpr int kStreamTag = 8;
 
 // Sub-batch of a pipelined host forward (yb_cuda_forward with B >= 2 chunks)
 // and the number of plan slots (each with its own stream) it rotates over.
@@ -118,6 +133,26 @@ status_t check_kernel_flag(Ctx* c) {
     return ERROR_DEVICE;
   }
   return SUCCESS;
+}
+
+// Waits for the streaming batch in slot S and frees the slot.
+status_t finish_stream_slot(Ctx* c, Ctx::StreamSlot& S) {
+  if (!S.ticket) return SUCCESS;
+  const cudaError_t e = cudaEventSynchronize(S.done);
+  S.ticket = 0;
+  if (e != cudaSuccess) return cuda_status(e, "streaming forward");
+  c->last = S.plan;
+  return check_kernel_flag(c);
+}
+
+// Finishes every streaming batch in flight (before plans are replaced).
+status_t drain_stream(Ctx* c) {
+  status_t st = SUCCESS;
+  for (auto& S : c->sslot) {
+    const status_t s2 = finish_stream_slot(c, S);
+    if (st == SUCCESS) st = s2;
+  }
+  return st;
 }
 
 status_t plan_for(Ctx* c, int B, int H, int W, int max_det, Plan** p, int slot = 0) {
@@ -325,6 +360,11 @@ extern "C" status_t yb_cuda_init(int device, void** ctx) {
         (e = cudaEventCreateWithFlags(&c->slot_free[i], cudaEventDisableTiming)) != cudaSuccess ||
         (e = cudaStreamCreateWithFlags(&c->slot_stream[i], cudaStreamNonBlocking)) != cudaSuccess)
       return cuda_status(e, "cudaEventCreate");
+  for (auto& S : c->sslot)
+    if ((e = cudaEventCreateWithFlags(&S.h2d, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&S.done, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&S.st, cudaStreamNonBlocking)) != cudaSuccess)
+      return cuda_status(e, "cudaEventCreate");
   *ctx = c.release();
   return SUCCESS;
 }
@@ -334,6 +374,16 @@ extern "C" status_t yb_cuda_destroy(void* ctx) {
   if (!c) return ERROR_NULL_POINTER;
   cudaSetDevice(c->eng->device());
   if (c->inflight) cudaEventSynchronize(c->done);
+  drain_stream(c);
+  for (auto& S : c->sslot) {
+    if (S.st) {
+      cudaStreamSynchronize(S.st);
+      cudaStreamDestroy(S.st);
+    }
+    if (S.h2d) cudaEventDestroy(S.h2d);
+    if (S.done) cudaEventDestroy(S.done);
+    if (S.d_rgb) cudaFree(S.d_rgb);
+  }
   for (auto& ev : c->ev)
     if (ev) cudaEventDestroy(ev);
   if (c->done) cudaEventDestroy(c->done);
@@ -367,6 +417,8 @@ extern "C" status_t yb_cuda_upload_weights(void* ctx, const model_t* m, yb_preci
   if (p == YB_PRECISION_INT8 && !qparams) return ERROR_NULL_POINTER;
   status_t st = ctx_ready(c);
   if (st != SUCCESS) return st;
+  // Plans are replaced below: finish the streaming batches using them.
+  if ((st = drain_stream(c)) != SUCCESS) return st;
   WeightMap w;
   weights_from_model(m, &w);
   std::string why;
@@ -390,6 +442,8 @@ extern "C" status_t yb_cuda_set_int8(void* ctx, const char* const* names, const 
   if (!c) return ERROR_NULL_POINTER;
   status_t st = ctx_ready(c);
   if (st != SUCCESS) return st;
+  // Plans are replaced below: finish the streaming batches using them.
+  if ((st = drain_stream(c)) != SUCCESS) return st;
   return set_int8(c, names, scales, n);
 }
 
@@ -399,6 +453,8 @@ extern "C" status_t yb_cuda_calibrate_int8(void* ctx, const float* images, int n
   if (!c || !images) return ERROR_NULL_POINTER;
   status_t st = ctx_ready(c);
   if (st != SUCCESS) return st;
+  // Plans are replaced below: finish the streaming batches using them.
+  if ((st = drain_stream(c)) != SUCCESS) return st;
   std::map<std::string, float> table;
   std::string why;
   cudaError_t e = c->eng->calibrate(images, n, H, W, &table, &why);
@@ -459,6 +515,8 @@ extern "C" status_t yb_cuda_load_bin(void* ctx, const char* path) {
   if (!c || !path) return ERROR_NULL_POINTER;
   status_t st = ctx_ready(c);
   if (st != SUCCESS) return st;
+  // Plans are replaced below: finish the streaming batches using them.
+  if ((st = drain_stream(c)) != SUCCESS) return st;
   WeightMap w;
   int nc = 0;
   std::string why;
@@ -626,6 +684,83 @@ extern "C" status_t yb_cuda_detections(const float* d_dets, int B, int rows, flo
   return cuda_status(launch_detections(d_dets, B, rows, threshold, capacity, d_out, d_counts,
                                        static_cast<cudaStream_t>(stream)),
                      "detections");
+}
+
+namespace {
+
+// Queues one batch on the next streaming slot: input copy on the copy stream
+// (back to back with other copies), then on the slot's stream the optional
+// preprocess, the plan's graph and the detections' copy to the host.
+status_t stream_submit(Ctx* c, const void* src, size_t src_bytes, bool rgb8, int B, int src_h, int src_w, int resize,
+                       int H, int W, float* out_dets, int max_det, long long* ticket) {
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  const int k = c->sslot_next;
+  Ctx::StreamSlot& S = c->sslot[k];
+  // The slot's previous batch must be done before its input is overwritten.
+  if ((st = finish_stream_slot(c, S)) != SUCCESS) return st;
+  Plan* p = nullptr;
+  if ((st = plan_for(c, B, H, W, max_det, &p, kStreamTag + k)) != SUCCESS) return st;
+  cudaError_t e = cudaSuccess;
+  void* dst = p->d_in;
+  if (rgb8) {
+    if (src_bytes > S.d_rgb_bytes) {
+      if (S.d_rgb) cudaFree(S.d_rgb);
+      S.d_rgb = nullptr;
+      S.d_rgb_bytes = 0;
+      if ((e = cudaMalloc(&S.d_rgb, src_bytes)) != cudaSuccess) return cuda_status(e, "rgb staging");
+      S.d_rgb_bytes = src_bytes;
+    }
+    dst = S.d_rgb;
+  }
+  e = cudaMemcpyAsync(dst, src, src_bytes, cudaMemcpyHostToDevice, c->copy_stream);
+  if (e == cudaSuccess) e = cudaEventRecord(S.h2d, c->copy_stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(S.st, S.h2d, 0);
+  if (e == cudaSuccess && rgb8) e = launch_preprocess(S.d_rgb, B, src_h, src_w, resize, p->d_in, H, W, S.st);
+  if (e == cudaSuccess) e = c->eng->run(p, S.st, nullptr);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(out_dets, p->d_out, static_cast<size_t>(B) * max_det * 6 * 4, cudaMemcpyDeviceToHost, S.st);
+  if (e == cudaSuccess) e = cudaEventRecord(S.done, S.st);
+  if (e != cudaSuccess) return cuda_status(e, "streaming forward");
+  S.plan = p;
+  S.ticket = c->next_ticket++;
+  c->sslot_next = k ^ 1;
+  *ticket = S.ticket;
+  return SUCCESS;
+}
+
+}  // namespace
+
+extern "C" status_t yb_cuda_forward_submit(void* ctx, const float* in_nchw, int B, int H, int W, float* out_dets,
+                                           int max_det, long long* ticket) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !in_nchw || !out_dets || !ticket) return ERROR_NULL_POINTER;
+  if (B < 1) return ERROR_INVALID_DIMS;
+  return stream_submit(c, in_nchw, static_cast<size_t>(B) * 3 * H * W * 4, false, B, 0, 0, 0, H, W, out_dets, max_det,
+                       ticket);
+}
+
+extern "C" status_t yb_cuda_forward_rgb8_submit(void* ctx, const unsigned char* rgb_hwc, int B, int src_h, int src_w,
+                                                int resize, int H, int W, float* out_dets, int max_det,
+                                                long long* ticket) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !rgb_hwc || !out_dets || !ticket) return ERROR_NULL_POINTER;
+  if (B < 1 || src_h < 1 || src_w < 1 || (resize != YB_RESIZE_ALIGN_CORNERS && resize != YB_RESIZE_HALF_PIXEL))
+    return ERROR_INVALID_DIMS;
+  return stream_submit(c, rgb_hwc, static_cast<size_t>(B) * src_h * src_w * 3, true, B, src_h, src_w, resize, H, W,
+                       out_dets, max_det, ticket);
+}
+
+extern "C" status_t yb_cuda_forward_wait(void* ctx, long long ticket) {
+  Ctx* c = as_ctx(ctx);
+  if (!c) return ERROR_NULL_POINTER;
+  cudaError_t e = cudaSetDevice(c->eng->device());
+  if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  for (auto& S : c->sslot)
+    if (S.ticket == ticket && ticket != 0) return finish_stream_slot(c, S);
+  if (ticket > 0 && ticket < c->next_ticket) return SUCCESS;  // already finished
+  set_error("unknown streaming ticket");
+  return ERROR_INVALID_DIMS;
 }
 
 extern "C" status_t yb_cuda_preprocess_rgb8(const unsigned char* d_rgb, int B, int src_h, int src_w, int resize,

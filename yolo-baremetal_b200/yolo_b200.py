@@ -39,6 +39,7 @@ EXPORTS = {
     "yb_cuda.h": ["yb_cuda_init", "yb_cuda_upload_weights", "yb_cuda_load_bin", "yb_cuda_forward",
                   "yb_cuda_set_int8", "yb_cuda_get_int8_stage", "yb_cuda_calibrate_int8",
                   "yb_cuda_int8_scale_entry", "yb_cuda_forward_rgb8", "yb_cuda_preprocess_rgb8",
+                  "yb_cuda_forward_submit", "yb_cuda_forward_rgb8_submit", "yb_cuda_forward_wait",
                   "yb_cuda_get_detections", "yb_cuda_detections",
                   "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_detect_topk_noalloc",
                   "yb_cuda_forward_sharded",
@@ -121,6 +122,11 @@ def lib() -> C.CDLL:
                                            C.c_int, C.c_void_p, C.c_int]
         L.yb_cuda_preprocess_rgb8.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
                                               C.c_int, C.c_void_p]
+        L.yb_cuda_forward_submit.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                             C.POINTER(C.c_longlong)]
+        L.yb_cuda_forward_rgb8_submit.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                  C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_longlong)]
+        L.yb_cuda_forward_wait.argtypes = [C.c_void_p, C.c_longlong]
         L.yb_cuda_calibrate_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                              C.POINTER(C.c_int)]
         L.yb_cuda_int8_scale_entry.argtypes = [C.c_void_p, C.c_int, C.c_char_p, C.c_int, C.POINTER(C.c_float)]
@@ -252,6 +258,25 @@ class Model:
         check(lib().yb_cuda_forward_rgb8(self.ctx, x.ctypes.data, B, sh, sw, resize, H, W, dets.ctypes.data, max_det),
               "yb_cuda_forward_rgb8")
         return dets
+
+    def submit(self, x_ptr: int, B: int, H: int, W: int, out_ptr: int, max_det: int = 300) -> int:
+        """Streaming forward: queues one batch (host pointers to [B,3,H,W] fp32 and [B,max_det,6] fp32, pinned
+        for overlap, valid until wait) and returns its ticket."""
+        t = C.c_longlong()
+        check(lib().yb_cuda_forward_submit(self.ctx, x_ptr, B, H, W, out_ptr, max_det, C.byref(t)),
+              "yb_cuda_forward_submit")
+        return t.value
+
+    def submit_rgb8(self, rgb_ptr: int, B: int, sh: int, sw: int, out_ptr: int, H: int = 640, W: int = 640,
+                    resize: int = 0, max_det: int = 300) -> int:
+        """Streaming forward from uint8 HWC frames [B, sh, sw, 3] (host pointer); returns the ticket."""
+        t = C.c_longlong()
+        check(lib().yb_cuda_forward_rgb8_submit(self.ctx, rgb_ptr, B, sh, sw, resize, H, W, out_ptr, max_det,
+                                                C.byref(t)), "yb_cuda_forward_rgb8_submit")
+        return t.value
+
+    def wait(self, ticket: int) -> None:
+        check(lib().yb_cuda_forward_wait(self.ctx, ticket), "yb_cuda_forward_wait")
 
     def detections(self, batch: int, threshold: float = 0.25, capacity: int = 100):
         """Detection lists of the last forward: (structured array [B, capacity], counts [B])."""
