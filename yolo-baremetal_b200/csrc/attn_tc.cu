@@ -417,6 +417,34 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
     }
     tc_commit(&S.bar);
   }
+  // While the score UMMAs run: the positional term of this row's 16
+  // channels (bias, then taps in (ky, kx) order, the reference's summation),
+  // a depthwise 3x3 of v around the query read from global memory.
+  const int qi = q0 + row;
+  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
+  const int d0 = 16 * g;
+  float pe[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) pe[e] = S.peb[d0 + e];
+  if (qi < N) {
+    for (int ky = 0; ky < 3; ++ky) {
+      const int iy = y - 1 + ky;
+      if (iy < 0 || iy >= a.H) continue;
+      for (int kx = 0; kx < 3; ++kx) {
+        const int ix = x - 1 + kx;
+        if (ix < 0 || ix >= a.W) continue;
+        const uint16_t* vp = base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * TKD + d0;
+        float v0[8], v1[8];
+        load8(vp, pl, v0);
+        load8(vp + 8, pl, v1);
+        const float* w = S.pew[ky * 3 + kx] + d0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v0[e], w[e]));
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pe[8 + e] = __fadd_rn(pe[8 + e], __fmul_rn(v1[e], w[8 + e]));
+      }
+    }
+  }
   wait_bar(&S.bar, 0u);
   // Row maximum of the scaled scores over this warpgroup's quarter.
   float mx = -FLT_MAX;
@@ -484,12 +512,9 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
   S.red_sum[g][row] = l;
   __syncthreads();
   const bool good = S.abort == 0;
-  const int qi = q0 + row;
   const bool valid = qi < N && good;
   l = S.red_sum[0][row] + S.red_sum[1][row] + S.red_sum[2][row] + S.red_sum[3][row];
   const float inv = l > 1e-12f ? 1.0f / l : 1.0f;
-  const int y = qi / a.W, x = qi - (qi / a.W) * a.W;
-  const int d0 = 16 * g;
   uint32_t ov[16];
   tc_ld_32x32b_x16(trow + static_cast<uint32_t>(d0), ov);
   tc_wait_ld();
@@ -498,27 +523,10 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
                    a.out.coff + h * THD;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      const int dd = d0 + 8 * half;
-      float pe[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) pe[e] = S.peb[dd + e];
-      for (int ky = 0; ky < 3; ++ky) {
-        const int iy = y - 1 + ky;
-        if (iy < 0 || iy >= a.H) continue;
-        for (int kx = 0; kx < 3; ++kx) {
-          const int ix = x - 1 + kx;
-          if (ix < 0 || ix >= a.W) continue;
-          float v[8];
-          load8(base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * TKD + dd, pl, v);
-          const float* w = S.pew[ky * 3 + kx] + dd;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v[e], w[e]));
-        }
-      }
       float res[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) res[e] = __uint_as_float(ov[8 * half + e]) * inv + pe[e];
-      store8(op + dd, a.out.plane, res);
+      for (int e = 0; e < 8; ++e) res[e] = __uint_as_float(ov[8 * half + e]) * inv + pe[8 * half + e];
+      store8(op + d0 + 8 * half, a.out.plane, res);
     }
   }
   if (!good) __nanosleep(100000);
