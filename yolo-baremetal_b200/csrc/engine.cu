@@ -538,17 +538,26 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     Buf cat;
     YB_TRY(alloc_buf(in.H, in.W, 4 * c, &cat));
     YB_TRY(add_conv(cv1, src_of(in, 0, in.C), 1, 0, kActNone, ov(cat, 0), SView()));
-    for (int j = 0; j < 3; ++j) {
-      PoolArgs pa;
-      pa.in = tv(cat, j * c);
-      pa.B = B;
-      pa.H = in.H;
-      pa.W = in.W;
-      pa.C = c;
-      pa.k = 5;
-      pa.out = ov(cat, (j + 1) * c);
-      const double n = static_cast<double>(B) * in.H * in.W * c;
-      add_op(kOpPool, 0.0, 8.0 * n, [pa](cudaStream_t s) { return launch_maxpool(pa, s); });
+    if (c % 8 == 0 && sppf_pool_smem_bytes(in.H, in.W) <= kSppfSmemMax) {
+      // The three pools in one launch (the 5x5, 9x9 and 13x13 pools of cv1).
+      const SView src = tv(cat, 0);
+      const SOut p1 = ov(cat, c), p2 = ov(cat, 2 * c), p3 = ov(cat, 3 * c);
+      const int h = in.H, w = in.W;
+      const double n = static_cast<double>(B) * h * w * c;
+      add_op(kOpPool, 0.0, 8.0 * n, [=](cudaStream_t s) { return launch_sppf_pool(src, p1, p2, p3, B, h, w, c, s); });
+    } else {
+      for (int j = 0; j < 3; ++j) {
+        PoolArgs pa;
+        pa.in = tv(cat, j * c);
+        pa.B = B;
+        pa.H = in.H;
+        pa.W = in.W;
+        pa.C = c;
+        pa.k = 5;
+        pa.out = ov(cat, (j + 1) * c);
+        const double n = static_cast<double>(B) * in.H * in.W * c;
+        add_op(kOpPool, 0.0, 8.0 * n, [pa](cudaStream_t s) { return launch_maxpool(pa, s); });
+      }
     }
     YB_TRY(alloc_buf(in.H, in.W, cv2->co, out));
     const bool res = in.C == cv2->co;

@@ -430,12 +430,23 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     QT cat;
     YB_TRY(tensor(4 * c, in.H, in.W, &cat));
     YB_TRY(conv(L + ".cv1", false, cat.sub(0, c), in, 1, 0, false, nullptr));
+    const bool fused = sppf_pool_i8_smem_bytes(in.H, in.W) <= kSppfI8SmemMax;
+    if (fused) {
+      // The three pools in one launch (the 5x5, 9x9 and 13x13 pools of cv1).
+      const I8View iv = cat.sub(0, c).view(), v1 = cat.sub(c, c).view(), v2 = cat.sub(2 * c, c).view(),
+                   v3 = cat.sub(3 * c, c).view();
+      const int h = in.H, wd = in.W;
+      add_op(kOpPool, 0.0, 4.0 * B * h * wd * c,
+             [=](cudaStream_t st) { return launch_sppf_pool_i8(iv, v1, v2, v3, B, h, wd, c, st); });
+    }
     for (int j = 0; j < 3; ++j) {
       const QT src = cat.sub(j * c, c), dst = cat.sub((j + 1) * c, c);
-      const I8View iv = src.view(), ovw = dst.view();
-      const int h = in.H, wd = in.W;
-      add_op(kOpPool, 0.0, 2.0 * B * h * wd * c,
-             [=](cudaStream_t st) { return launch_maxpool_i8(iv, ovw, B, h, wd, c, 5, st); });
+      if (!fused) {
+        const I8View iv = src.view(), ovw = dst.view();
+        const int h = in.H, wd = in.W;
+        add_op(kOpPool, 0.0, 2.0 * B * h * wd * c,
+               [=](cudaStream_t st) { return launch_maxpool_i8(iv, ovw, B, h, wd, c, 5, st); });
+      }
       for (int i = 0; i < c; ++i) (*cat.cs)[cat.c0 + (j + 1) * c + i] = src.scale(i);
     }
     return conv(L + ".cv2", false, out, cat, 1, 0, true, (in.C == out.C) ? &in : nullptr);

@@ -61,6 +61,14 @@ struct StemI8Args {
 cudaError_t launch_stem_i8(const StemI8Args& a, cudaStream_t st);
 cudaError_t init_stem_i8_attributes();
 cudaError_t launch_maxpool_i8(I8View in, I8View out, int B, int H, int W, int C, int k, cudaStream_t st);
+// SPPF's three chained 5x5 pools in one launch: o1, o2, o3 receive the 5x5,
+// 9x9 and 13x13 max pools of `in` (padding excluded), C a multiple of 16; the
+// map of 16 channels is held in shared memory (sppf_pool_i8_smem_bytes(H, W)
+// <= kSppfI8SmemMax).
+constexpr int kSppfI8SmemMax = 220 * 1024;
+int sppf_pool_i8_smem_bytes(int H, int W);
+cudaError_t launch_sppf_pool_i8(I8View in, I8View o1, I8View o2, I8View o3, int B, int H, int W, int C,
+                                cudaStream_t st);
 // Depthwise 3x3 pad 1; wr: [3][C] words of packed int8 taps, one per filter
 // row (byte kx of wr[ky][c] = tap (ky, kx)), bq / mult / shift per channel,
 // lut nullable.

@@ -179,6 +179,13 @@ struct PoolArgs {
   SOut out;
 };
 cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s);
+// SPPF's three chained 5x5 stride-1 pools in one launch: o1, o2, o3 receive
+// the 5x5, 9x9 and 13x13 max pools of `in` (padding excluded), C channels
+// (a multiple of 8).  The whole H x W map of 8 channels is held in shared
+// memory: sppf_pool_smem_bytes(H, W) <= kSppfSmemMax.
+constexpr int kSppfSmemMax = 220 * 1024;
+int sppf_pool_smem_bytes(int H, int W);
+cudaError_t launch_sppf_pool(SView in, SOut o1, SOut o2, SOut o3, int B, int H, int W, int C, cudaStream_t s);
 
 // Multi-head attention of the PSA block (layers.c:310-405): per head h the
 // qkv channels [h*(2kd+hd), +kd) are q, the next kd are k, the next hd are v;

@@ -4,6 +4,7 @@
 // read and write split NHWC views (kernels.h) 8 channels (two 16-byte
 // accesses) at a time.  Summation orders follow the reference loops so that
 // results stay within a few ulps of it.
+#include <atomic>
 #include <cfloat>
 #include <climits>
 #include "pdl.cuh"
@@ -276,6 +277,90 @@ __global__ void __launch_bounds__(256, 2) dw3x3_kernel(const DwArgs a) {
   if (a.amax) amax_warp(a.amax, mpre, mout);
 }
 
+// ------------------------------------------------------------- SPPF pools
+// SPPF's three chained 5x5 stride-1 max pools (layers.c:230-265) in one
+// launch.  With out-of-image positions excluded, pooling twice is the 9x9
+// pool and three times the 13x13 pool (each in-image position of the larger
+// window is reached through an in-image intermediate), and the joined
+// (hi + lo) maxima are the same values.  One CTA per (image, 8 channels)
+// loads the image into shared memory, takes the row maxima over 5, 9 and 13
+// columns, then the column maxima over 5, 9 and 13 rows.
+__global__ void __launch_bounds__(256) sppf_pool_kernel(SView in, SOut o1, SOut o2, SOut o3, int B, int H, int W,
+                                                        int C) {
+  extern __shared__ float4 sppf_smem[];  // [4][H*W][2]: input, row maxima over 5, 9, 13
+  const int HW = H * W;
+  float4* sx = sppf_smem;
+  float4* s5 = sx + 2 * HW;
+  float4* s9 = s5 + 2 * HW;
+  float4* s13 = s9 + 2 * HW;
+  const int groups = C >> 3;
+  const int b = blockIdx.x / groups, c = (blockIdx.x - b * groups) * 8;
+  pdl_wait();
+  for (int p = threadIdx.x; p < HW; p += blockDim.x) {
+    float v[8];
+    load8_rw(in.hi + vaddr(in, b, p) + c, in.plane, v);
+    sx[2 * p] = make_float4(v[0], v[1], v[2], v[3]);
+    sx[2 * p + 1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  __syncthreads();
+  const auto mx4 = [](float4 a, float4 b) {
+    return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
+  };
+  for (int p = threadIdx.x; p < HW; p += blockDim.x) {
+    const int x = p - (p / W) * W;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float4 m5 = sx[2 * p + h], m9 = m5, m13 = m5;
+#pragma unroll
+      for (int d = 1; d <= 6; ++d) {
+        float4 t = make_float4(-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX);
+        if (x - d >= 0) t = sx[2 * (p - d) + h];
+        if (x + d < W) t = mx4(t, sx[2 * (p + d) + h]);
+        m13 = mx4(m13, t);
+        if (d <= 4) m9 = mx4(m9, t);
+        if (d <= 2) m5 = mx4(m5, t);
+      }
+      s5[2 * p + h] = m5;
+      s9[2 * p + h] = m9;
+      s13[2 * p + h] = m13;
+    }
+  }
+  __syncthreads();
+  for (int p = threadIdx.x; p < HW; p += blockDim.x) {
+    const int y = p / W;
+    float o[3][8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float4 m5 = s5[2 * p + h], m9 = s9[2 * p + h], m13 = s13[2 * p + h];
+#pragma unroll
+      for (int d = 1; d <= 6; ++d) {
+        const bool up = y - d >= 0, dn = y + d < H;
+        if (d <= 2) {
+          if (up) m5 = mx4(m5, s5[2 * (p - d * W) + h]);
+          if (dn) m5 = mx4(m5, s5[2 * (p + d * W) + h]);
+        }
+        if (d <= 4) {
+          if (up) m9 = mx4(m9, s9[2 * (p - d * W) + h]);
+          if (dn) m9 = mx4(m9, s9[2 * (p + d * W) + h]);
+        }
+        if (up) m13 = mx4(m13, s13[2 * (p - d * W) + h]);
+        if (dn) m13 = mx4(m13, s13[2 * (p + d * W) + h]);
+      }
+      const float4 r[3] = {m5, m9, m13};
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        o[k][4 * h + 0] = r[k].x;
+        o[k][4 * h + 1] = r[k].y;
+        o[k][4 * h + 2] = r[k].z;
+        o[k][4 * h + 3] = r[k].w;
+      }
+    }
+    store8(o1.hi + vaddr(o1, b, p) + c, o1.plane, o[0]);
+    store8(o2.hi + vaddr(o2, b, p) + c, o2.plane, o[1]);
+    store8(o3.hi + vaddr(o3, b, p) + c, o3.plane, o[2]);
+  }
+}
+
 // ------------------------------------------------------------- calibration
 __global__ void absmax_split_kernel(SView v, int B, int H, int W, int C, unsigned* amax) {
   pdl_wait();
@@ -522,6 +607,23 @@ cudaError_t launch_dwconv3x3(const DwArgs& a, cudaStream_t s) {
   }
   const long long total = static_cast<long long>(a.B) * ((a.H + 3) / 4) * a.W * (a.C / 2);
   return launch_pdl(dw3x3_kernel<4>, dim3(blocks_for(total, 256)), dim3(256), 0, s, a);
+}
+
+int sppf_pool_smem_bytes(int H, int W) { return 4 * H * W * 32; }
+
+cudaError_t launch_sppf_pool(SView in, SOut o1, SOut o2, SOut o3, int B, int H, int W, int C, cudaStream_t s) {
+  const int smem = sppf_pool_smem_bytes(H, W);
+  if (C % 8 || B < 1 || H < 1 || W < 1 || smem > kSppfSmemMax) return cudaErrorInvalidValue;
+  for (const long long v : {static_cast<long long>(in.cstride), static_cast<long long>(in.coff), in.bstride, in.plane,
+                            static_cast<long long>(o1.cstride), static_cast<long long>(o1.coff), o1.bstride, o1.plane,
+                            static_cast<long long>(o2.cstride), static_cast<long long>(o2.coff), o2.bstride, o2.plane,
+                            static_cast<long long>(o3.cstride), static_cast<long long>(o3.coff), o3.bstride, o3.plane})
+    if (v % 8) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr_done{0};
+  const cudaError_t e = smem_attr_once(sppf_pool_kernel, kSppfSmemMax, attr_done);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(sppf_pool_kernel, dim3(static_cast<unsigned>(B * (C / 8))), dim3(256), smem, s, in, o1, o2, o3, B, H,
+                    W, C);
 }
 
 cudaError_t launch_maxpool(const PoolArgs& a, cudaStream_t s) {

@@ -3,6 +3,7 @@
 // All activations are NHWC int8 views {ptr, cstride (per pixel), bstride (per
 // image)}; every rule is the integer arithmetic declared in i8k.h, which the
 // CPU INT8 oracle restates.
+#include <atomic>
 #include <climits>
 #include <cstdint>
 
@@ -386,6 +387,70 @@ __global__ void __launch_bounds__(256) dw3x3_i8_kernel(I8View in, I8View out, in
   }
 }
 
+// ---------------------------------------------------------- SPPF pools
+// The three chained 5x5 stride-1 pools of SPPF in one launch: with
+// out-of-image positions excluded they are the 5x5, 9x9 and 13x13 pools of
+// the input.  One CTA per (image, 16 channels) holds the map in shared
+// memory (one uint4 per pixel), takes row maxima over 5, 9 and 13 columns
+// and then column maxima over 5, 9 and 13 rows, with byte-wise signed max.
+__device__ __forceinline__ uint4 vmax16(uint4 a, uint4 b) {
+  return make_uint4(__vmaxs4(a.x, b.x), __vmaxs4(a.y, b.y), __vmaxs4(a.z, b.z), __vmaxs4(a.w, b.w));
+}
+
+__global__ void __launch_bounds__(256) sppf_pool_i8_kernel(I8View in, I8View o1, I8View o2, I8View o3, int B, int H,
+                                                           int W, int C) {
+  extern __shared__ uint4 sppf8_smem[];  // [4][H*W]: input, row maxima over 5, 9, 13
+  const int HW = H * W;
+  uint4* sx = sppf8_smem;
+  uint4* s5 = sx + HW;
+  uint4* s9 = s5 + HW;
+  uint4* s13 = s9 + HW;
+  const int groups = C >> 4;
+  const int b = blockIdx.x / groups, c = (blockIdx.x - b * groups) * 16;
+  pdl_wait();
+  for (int p = threadIdx.x; p < HW; p += blockDim.x)
+    sx[p] = *reinterpret_cast<const uint4*>(in.p + b * in.bstride + static_cast<long long>(p) * in.cstride + c);
+  __syncthreads();
+  for (int p = threadIdx.x; p < HW; p += blockDim.x) {
+    const int x = p - (p / W) * W;
+    uint4 m5 = sx[p], m9 = m5, m13 = m5;
+#pragma unroll
+    for (int d = 1; d <= 6; ++d) {
+      uint4 t = sx[p];
+      if (x - d >= 0) t = vmax16(t, sx[p - d]);
+      if (x + d < W) t = vmax16(t, sx[p + d]);
+      m13 = vmax16(m13, t);
+      if (d <= 4) m9 = vmax16(m9, t);
+      if (d <= 2) m5 = vmax16(m5, t);
+    }
+    s5[p] = m5;
+    s9[p] = m9;
+    s13[p] = m13;
+  }
+  __syncthreads();
+  for (int p = threadIdx.x; p < HW; p += blockDim.x) {
+    const int y = p / W;
+    uint4 m5 = s5[p], m9 = s9[p], m13 = s13[p];
+#pragma unroll
+    for (int d = 1; d <= 6; ++d) {
+      const bool up = y - d >= 0, dn = y + d < H;
+      if (d <= 2) {
+        if (up) m5 = vmax16(m5, s5[p - d * W]);
+        if (dn) m5 = vmax16(m5, s5[p + d * W]);
+      }
+      if (d <= 4) {
+        if (up) m9 = vmax16(m9, s9[p - d * W]);
+        if (dn) m9 = vmax16(m9, s9[p + d * W]);
+      }
+      if (up) m13 = vmax16(m13, s13[p - d * W]);
+      if (dn) m13 = vmax16(m13, s13[p + d * W]);
+    }
+    *reinterpret_cast<uint4*>(o1.p + b * o1.bstride + static_cast<long long>(p) * o1.cstride + c) = m5;
+    *reinterpret_cast<uint4*>(o2.p + b * o2.bstride + static_cast<long long>(p) * o2.cstride + c) = m9;
+    *reinterpret_cast<uint4*>(o3.p + b * o3.bstride + static_cast<long long>(p) * o3.cstride + c) = m13;
+  }
+}
+
 // ------------------------------------------------- upsample and concat
 // out[b, y, x, 0:c0] = src0[b, y >> lg0, x >> lg0, :]; out[..., c0:] = src1.
 // 16 channels per thread (c0, c1 multiples of 16).
@@ -433,6 +498,21 @@ cudaError_t launch_maxpool_i8(I8View in, I8View out, int B, int H, int W, int C,
   if (C % 16 || in.cstride % 16 || out.cstride % 16) return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(B) * H * W * (C / 16);
   return launch_pdl(maxpool_i8_kernel, dim3(blocks_for(total, 256)), dim3(256), 0, st, in, out, B, H, W, C, k);
+}
+
+int sppf_pool_i8_smem_bytes(int H, int W) { return 4 * H * W * 16; }
+
+cudaError_t launch_sppf_pool_i8(I8View in, I8View o1, I8View o2, I8View o3, int B, int H, int W, int C,
+                                cudaStream_t st) {
+  const int smem = sppf_pool_i8_smem_bytes(H, W);
+  if (C % 16 || B < 1 || H < 1 || W < 1 || smem > kSppfI8SmemMax) return cudaErrorInvalidValue;
+  for (const I8View& v : {in, o1, o2, o3})
+    if (v.cstride % 16 || v.bstride % 16 || reinterpret_cast<uintptr_t>(v.p) % 16) return cudaErrorInvalidValue;
+  static std::atomic<uint64_t> attr_done{0};
+  const cudaError_t e = smem_attr_once(sppf_pool_i8_kernel, kSppfI8SmemMax, attr_done);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(sppf_pool_i8_kernel, dim3(static_cast<unsigned>(B * (C / 16))), dim3(256), smem, st, in, o1, o2, o3,
+                    B, H, W, C);
 }
 
 cudaError_t launch_dw3x3_i8(I8View in, I8View out, int B, int H, int W, int C, const uint32_t* wr, const int32_t* bq,
