@@ -11,6 +11,7 @@
 // an explicitly rounded intrinsic in the reference's evaluation order, so the
 // result is bit-identical to the reference's C (which is compiled without
 // floating-point contraction).
+#include <atomic>
 #include <cstdint>
 
 #include "kernels.h"
@@ -78,6 +79,84 @@ __global__ void preprocess_kernel(const uint8_t* src, int B, int sh, int sw, int
   }
 }
 
+// Table form of the same arithmetic: a CTA takes kPreRows output rows of one
+// image.  The source columns and weights of every output column (x0, x1 and
+// the two weights, which depend on x alone), those of its rows, and the 256
+// possible values of v / 255 are computed once per CTA, with the same
+// intrinsics, so each pixel is loads, the blend and a table lookup.
+constexpr int kPreRows = 4;
+constexpr int kPreMaxW = 4096;
+struct PreAxis {
+  int i0, i1;
+  float f, g;  // weight of i1 and of i0
+};
+
+__device__ __forceinline__ PreAxis pre_axis(int x, int s, int d, int mode) {
+  PreAxis r;
+  if (mode == YB_RESIZE_ALIGN_CORNERS) {
+    const float sx =
+        d == 1 ? 0.f : __fdiv_rn(__fmul_rn(static_cast<float>(x), static_cast<float>(s - 1)), static_cast<float>(d - 1));
+    r.i0 = static_cast<int>(floorf(sx));
+    r.i1 = r.i0 + 1 < s ? r.i0 + 1 : r.i0;
+    r.f = __fsub_rn(sx, static_cast<float>(r.i0));
+  } else {
+    const float fx = __fsub_rn(
+        __fdiv_rn(__fmul_rn(__fadd_rn(static_cast<float>(x), 0.5f), static_cast<float>(s)), static_cast<float>(d)),
+        0.5f);
+    r.i0 = clampi(__float2int_rz(fx), 0, s - 1);
+    r.i1 = r.i0 + 1 < s ? r.i0 + 1 : r.i0;
+    r.f = __fsub_rn(fx, static_cast<float>(r.i0));
+  }
+  r.g = __fsub_rn(1.f, r.f);
+  return r;
+}
+
+__global__ void __launch_bounds__(256) preprocess_rows_kernel(const uint8_t* src, int sh, int sw, int mode, float* dst,
+                                                              int H, int W) {
+  extern __shared__ PreAxis pre_xt[];  // W entries
+  __shared__ PreAxis yt[kPreRows];
+  __shared__ float lut[256];
+  const int b = blockIdx.y, yb0 = blockIdx.x * kPreRows;
+  for (int x = threadIdx.x; x < W; x += blockDim.x) pre_xt[x] = pre_axis(x, sw, W, mode);
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = __fdiv_rn(static_cast<float>(i), 255.0f);
+  if (threadIdx.x < kPreRows) yt[threadIdx.x] = pre_axis(min(yb0 + static_cast<int>(threadIdx.x), H - 1), sh, H, mode);
+  __syncthreads();
+  pdl_wait();
+  const uint8_t* img = src + static_cast<long long>(b) * sh * sw * 3;
+  float* out = dst + static_cast<long long>(b) * 3 * H * W;
+  const long long plane = static_cast<long long>(H) * W;
+  for (int r = 0; r < kPreRows; ++r) {
+    const int y = yb0 + r;
+    if (y >= H) break;
+    const PreAxis Y = yt[r];
+    const uint8_t* row0 = img + static_cast<long long>(Y.i0) * sw * 3;
+    const uint8_t* row1 = img + static_cast<long long>(Y.i1) * sw * 3;
+    for (int x = threadIdx.x; x < W; x += blockDim.x) {
+      const PreAxis X = pre_xt[x];
+      float* o = out + static_cast<long long>(y) * W + x;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const float a = row0[X.i0 * 3 + c], bb = row0[X.i1 * 3 + c];
+        const float d = row1[X.i0 * 3 + c], e = row1[X.i1 * 3 + c];
+        int iv;
+        if (mode == YB_RESIZE_ALIGN_CORNERS) {
+          const float top = __fadd_rn(__fmul_rn(a, X.g), __fmul_rn(bb, X.f));
+          const float bot = __fadd_rn(__fmul_rn(d, X.g), __fmul_rn(e, X.f));
+          const float v = __fadd_rn(__fmul_rn(top, Y.g), __fmul_rn(bot, Y.f));
+          iv = clampi(__float2int_rz(__fadd_rn(v, 0.5f)), 0, 255);
+        } else {
+          float v = __fmul_rn(__fmul_rn(a, X.g), Y.g);
+          v = __fadd_rn(v, __fmul_rn(__fmul_rn(bb, X.f), Y.g));
+          v = __fadd_rn(v, __fmul_rn(__fmul_rn(d, X.g), Y.f));
+          v = __fadd_rn(v, __fmul_rn(__fmul_rn(e, X.f), Y.f));
+          iv = v < 0.f ? 0 : v > 255.f ? 255 : __float2int_rz(v);
+        }
+        o[c * plane] = lut[iv];
+      }
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_preprocess(const uint8_t* src, int B, int sh, int sw, int mode, float* dst, int H, int W,
@@ -86,6 +165,16 @@ cudaError_t launch_preprocess(const uint8_t* src, int B, int sh, int sw, int mod
     return cudaErrorInvalidValue;
   const long long total = static_cast<long long>(B) * H * W;
   if (total == 0) return cudaSuccess;
+  if (W <= kPreMaxW && B <= 65535) {
+    const int smem = W * static_cast<int>(sizeof(PreAxis));
+    if (smem > 48 * 1024) {
+      static std::atomic<uint64_t> attr_done{0};
+      const cudaError_t e = smem_attr_once(preprocess_rows_kernel, kPreMaxW * static_cast<int>(sizeof(PreAxis)), attr_done);
+      if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(preprocess_rows_kernel, dim3(static_cast<unsigned>((H + kPreRows - 1) / kPreRows), B), dim3(256),
+                      smem, s, src, sh, sw, mode, dst, H, W);
+  }
   return launch_pdl(preprocess_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, s, src, B, sh,
                     sw, mode, dst, H, W);
 }
