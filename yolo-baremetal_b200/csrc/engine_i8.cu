@@ -549,6 +549,17 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     YB_TRY(psablock(L + ".m.0.1", heads_for(ch), cat.sub(2 * ch, ch), bo));
     return conv(L + ".cv2", false, out, cat, 1, 0, true, nullptr);
   };
+  // 2x nearest upsample of a into channels [0, a.C) of cat (the rest of cat
+  // was written by the layer that produced it).
+  auto upsample_into = [&](const QT& a, const QT& cat) -> cudaError_t {
+    if (cat.C < a.C || cat.c0 != 0) return fail("int8: upsample target");
+    const I8View av = a.view(), ov = cat.view();
+    const int ca = a.C, h = cat.H, wd = cat.W;
+    add_op(kOpPool, 0.0, 2.0 * B * h * wd * ca,
+           [=](cudaStream_t st) { return launch_concat_i8(av, ca, 1, I8View(), 0, B, h, wd, ov, st); });
+    for (int i = 0; i < ca; ++i) (*cat.cs)[i] = a.scale(i);
+    return cudaSuccess;
+  };
   auto concat_up = [&](const QT& a, int lg, const QT& b, QT* out) -> cudaError_t {
     YB_TRY(tensor(a.C + b.C, b.H, b.W, out));
     const I8View av = a.view(), bv = b.view(), ov = out->view();
@@ -649,12 +660,19 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   step = 3;
   YB_TRY(down(3, b[2]));
   step = 4;
-  YB_TRY(tensor(outw("model.4"), b[3].H, b[3].W, &b[4]));
+  // model.4 and model.6 write their outputs straight into the right-hand
+  // slices of the step-15 and step-12 concats (upsample(model.13) ++ model.4,
+  // upsample(model.10) ++ model.6), which then copy only their upsampled
+  // halves; the later layers read the slices as strided views.
+  QT cat15, cat12;
+  YB_TRY(tensor(outw("model.13") + outw("model.4"), b[3].H, b[3].W, &cat15));
+  b[4] = cat15.sub(outw("model.13"), outw("model.4"));
   YB_TRY(c3k2_plain("model.4", 1, true, b[4], b[3]));
   step = 5;
   YB_TRY(down(5, b[4]));
   step = 6;
-  YB_TRY(tensor(outw("model.6"), b[5].H, b[5].W, &b[6]));
+  YB_TRY(tensor(outw("model.10") + outw("model.6"), b[5].H, b[5].W, &cat12));
+  b[6] = cat12.sub(outw("model.10"), outw("model.6"));
   YB_TRY(c3k2_c3k("model.6", b[6], b[5]));
   step = 7;
   YB_TRY(down(7, b[6]));
@@ -669,12 +687,14 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   YB_TRY(c2psa("model.10", b[10], b[9]));
   // steps 11-12: upsample(buf10) ++ buf6, one concat launch.
   step = 12;
-  YB_TRY(concat_up(b[10], 1, b[6], &b[12]));
+  YB_TRY(upsample_into(b[10], cat12));
+  b[12] = cat12;
   step = 13;
   YB_TRY(tensor(outw("model.13"), b[12].H, b[12].W, &b[13]));
   YB_TRY(c3k2_c3k("model.13", b[13], b[12]));
   step = 15;
-  YB_TRY(concat_up(b[13], 1, b[4], &b[15]));
+  YB_TRY(upsample_into(b[13], cat15));
+  b[15] = cat15;
   step = 16;
   YB_TRY(tensor(outw("model.16"), b[15].H, b[15].W, &b[16]));
   YB_TRY(c3k2_c3k("model.16", b[16], b[15]));
