@@ -560,16 +560,6 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     for (int i = 0; i < ca; ++i) (*cat.cs)[i] = a.scale(i);
     return cudaSuccess;
   };
-  auto concat_up = [&](const QT& a, int lg, const QT& b, QT* out) -> cudaError_t {
-    YB_TRY(tensor(a.C + b.C, b.H, b.W, out));
-    const I8View av = a.view(), bv = b.view(), ov = out->view();
-    const int ca = a.C, cb = b.C, h = b.H, wd = b.W;
-    add_op(kOpPool, 0.0, 2.0 * B * h * wd * (ca + cb),
-           [=](cudaStream_t st) { return launch_concat_i8(av, ca, lg, bv, cb, B, h, wd, ov, st); });
-    for (int i = 0; i < ca; ++i) (*out->cs)[i] = a.scale(i);
-    for (int i = 0; i < cb; ++i) (*out->cs)[ca + i] = b.scale(i);
-    return cudaSuccess;
-  };
 
   // ----------------------------------------------------------- the graph
   if (H % 32 || W % 32) return fail("int8: H and W must be multiples of 32");
@@ -596,11 +586,18 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     xin.set_scale(s_in);
   }
   QT b[23];
-  auto down = [&](int i, const QT& src) -> cudaError_t {
+  // Downsampling conv model.i into b[i]: a new tensor, or `dst` (a slice of
+  // a concat that the conv then fills directly).
+  auto down = [&](int i, const QT& src, const QT* dst = nullptr) -> cudaError_t {
     const std::string P = "model." + std::to_string(i);
     const int co = wdim0(P + ".conv.weight");
     if (!co) return fail("int8: missing " + P);
-    YB_TRY(tensor(co, src.H / 2, src.W / 2, &b[i]));
+    if (dst) {
+      if (dst->C != co || dst->H != src.H / 2 || dst->W != src.W / 2) return fail("int8: concat slice of " + P);
+      b[i] = *dst;
+    } else {
+      YB_TRY(tensor(co, src.H / 2, src.W / 2, &b[i]));
+    }
     return conv(P, false, b[i], src, 2, 1, true, nullptr);
   };
   auto outw = [&](const std::string& L) { return wdim0(L + ".cv2.conv.weight"); };
@@ -683,14 +680,20 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   YB_TRY(tensor(outw("model.9"), b[8].H, b[8].W, &b[9]));
   YB_TRY(sppf("model.9", b[9], b[8]));
   step = 10;
-  YB_TRY(tensor(outw("model.10"), b[9].H, b[9].W, &b[10]));
+  // model.10 and model.20 fill the step-21 concat (model.20 ++ model.10)
+  // directly, as model.13 and model.17 fill the step-18 one: no copies.
+  const int c17 = wdim0("model.17.conv.weight"), c20 = wdim0("model.20.conv.weight");
+  QT cat21, cat18;
+  YB_TRY(tensor(c20 + outw("model.10"), b[9].H, b[9].W, &cat21));
+  b[10] = cat21.sub(c20, outw("model.10"));
   YB_TRY(c2psa("model.10", b[10], b[9]));
   // steps 11-12: upsample(buf10) ++ buf6, one concat launch.
   step = 12;
   YB_TRY(upsample_into(b[10], cat12));
   b[12] = cat12;
   step = 13;
-  YB_TRY(tensor(outw("model.13"), b[12].H, b[12].W, &b[13]));
+  YB_TRY(tensor(c17 + outw("model.13"), b[12].H, b[12].W, &cat18));
+  b[13] = cat18.sub(c17, outw("model.13"));
   YB_TRY(c3k2_c3k("model.13", b[13], b[12]));
   step = 15;
   YB_TRY(upsample_into(b[13], cat15));
@@ -699,16 +702,22 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   YB_TRY(tensor(outw("model.16"), b[15].H, b[15].W, &b[16]));
   YB_TRY(c3k2_c3k("model.16", b[16], b[15]));
   step = 17;
-  YB_TRY(down(17, b[16]));
+  {
+    const QT d17 = cat18.sub(0, c17);
+    YB_TRY(down(17, b[16], &d17));
+  }
   step = 18;
-  YB_TRY(concat_up(b[17], 0, b[13], &b[18]));
+  b[18] = cat18;
   step = 19;
   YB_TRY(tensor(outw("model.19"), b[18].H, b[18].W, &b[19]));
   YB_TRY(c3k2_c3k("model.19", b[19], b[18]));
   step = 20;
-  YB_TRY(down(20, b[19]));
+  {
+    const QT d20 = cat21.sub(0, c20);
+    YB_TRY(down(20, b[19], &d20));
+  }
   step = 21;
-  YB_TRY(concat_up(b[20], 0, b[10], &b[21]));
+  b[21] = cat21;
   step = 22;
   YB_TRY(tensor(outw("model.22"), b[21].H, b[21].W, &b[22]));
   YB_TRY(c3k2_attn("model.22", b[22], b[21]));
