@@ -221,7 +221,11 @@ static int qconv(const i8ctx* x, const char* P, q8* out, const q8* in, int strid
     if (act) build_lut(lut, s_pre, s_out);
     int32_t mr = 0, shr = 1;
     if (st == I8_OK && res && mult_of((double)res->cs[0] / (double)s_out, &mr, &shr) != 0) st = I8_ERR_SCALE;
-    for (int o = 0; o < out->c && st == I8_OK; ++o)
+    /* Output channels in parallel: integer arithmetic, so the result does
+     * not depend on the thread count. */
+    if (st == I8_OK)
+#pragma omp parallel for schedule(dynamic)
+        for (int o = 0; o < out->c; ++o)
         for (int oy = 0; oy < out->h; ++oy)
             for (int ox = 0; ox < out->w; ++ox) {
                 const int64_t y = rne(acc_at(&q, in, o, oy, ox, stride, pad) * q.mult[o], q.shift[o]);
@@ -248,7 +252,9 @@ static int qconv_deq(const i8ctx* x, const char* P, float* out, const q8* in) {
     qconv_t q;
     int st = quantize(&q, w, b, dims[0], dims[1], dims[2], dims[3], in->cs, 0.0);
     const int pad = (dims[2] - 1) / 2;
-    for (int o = 0; o < q.co && st == I8_OK; ++o)
+    if (st == I8_OK)
+#pragma omp parallel for schedule(dynamic)
+        for (int o = 0; o < q.co; ++o)
         for (int oy = 0; oy < in->h; ++oy)
             for (int ox = 0; ox < in->w; ++ox)
                 out[((size_t)o * in->h + oy) * in->w + ox] = (float)acc_at(&q, in, o, oy, ox, 1, pad) * q.deq[o];
@@ -274,12 +280,14 @@ static int qdw(const i8ctx* x, const char* P, q8* out, const q8* in) {
     int8_t lut[256];
     build_lut(lut, s_pre, s_out);
     int st = I8_OK;
-    for (int c = 0; c < C && st == I8_OK; ++c) {
+#pragma omp parallel for schedule(dynamic) reduction(max : st)
+    for (int c = 0; c < C; ++c) {
         qconv_t q;
         const float sc = in->cs[c];
-        st = quantize(&q, w + (size_t)c * 9, b ? b + c : NULL, 1, 1, 3, 3, &sc, (double)s_pre);
+        const int sq = quantize(&q, w + (size_t)c * 9, b ? b + c : NULL, 1, 1, 3, 3, &sc, (double)s_pre);
+        if (sq > st) st = sq;
         q8 ch = q8_view(in, c, 1);
-        for (int oy = 0; oy < in->h && st == I8_OK; ++oy)
+        for (int oy = 0; oy < in->h && sq == I8_OK; ++oy)
             for (int ox = 0; ox < in->w; ++ox) {
                 const int64_t y = rne(acc_at(&q, &ch, 0, oy, ox, 1, 1) * q.mult[0], q.shift[0]);
                 out->d[((size_t)c * in->h + oy) * in->w + ox] = lut[clampi(y, -128, 127) + 128];
@@ -474,13 +482,17 @@ static int qattention(const i8ctx* x, const char* P, int heads, q8* ope, const q
     const float sv = (float)s_qkv;
     for (int ch = 0; ch < dim && st == I8_OK && pw; ++ch)
         st = quantize(&pq[ch], pw + (size_t)ch * 9, pb ? pb + ch : NULL, 1, 1, 3, 3, &sv, (double)s_ope);
-    int64_t* o = (int64_t*)malloc((size_t)hd * sizeof(int64_t));
-    int32_t* S = (int32_t*)malloc((size_t)N * sizeof(int32_t));
     const int blk = 2 * kd + hd;
     for (int h = 0; h < heads && st == I8_OK; ++h) {
         const int8_t* q = qkv.d + (size_t)(h * blk) * N;
         const int8_t* k = qkv.d + (size_t)(h * blk + kd) * N;
         const int8_t* v = qkv.d + (size_t)(h * blk + 2 * kd) * N;
+        /* Query rows in parallel, each with its own score row and sums. */
+#pragma omp parallel
+        {
+        int64_t* o = (int64_t*)malloc((size_t)hd * sizeof(int64_t));
+        int32_t* S = (int32_t*)malloc((size_t)N * sizeof(int32_t));
+#pragma omp for schedule(static)
         for (int i = 0; i < N; ++i) {
             int32_t mx = INT32_MIN;
             for (int j = 0; j < N; ++j) {
@@ -507,13 +519,14 @@ static int qattention(const i8ctx* x, const char* P, int heads, q8* ope, const q
                 ope->d[(size_t)ch * N + i] = (int8_t)clampi(a + pe, -127, 127);
             }
         }
+        free(o);
+        free(S);
+        }
     }
     q8_set_scale(ope, s_ope);
     for (int ch = 0; ch < dim; ++ch)
         if (pq[ch].wq) qconv_free(&pq[ch]);
     free(pq);
-    free(o);
-    free(S);
     q8_free(&qkv);
     return st;
 }

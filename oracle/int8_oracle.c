@@ -100,6 +100,7 @@ int orc_i8_conv(const int8_t* x, int B, int H, int W, int ci, const int8_t* wq, 
                 const int32_t* shift, const int8_t* lut, int co, int kh, int kw, int stride, int pad, int8_t* y) {
     const int Ho = (H + 2 * pad - kh) / stride + 1, Wo = (W + 2 * pad - kw) / stride + 1;
     if (Ho <= 0 || Wo <= 0) return -1;
+#pragma omp parallel for collapse(2) schedule(dynamic)
     for (int b = 0; b < B; ++b)
         for (int oy = 0; oy < Ho; ++oy)
             for (int ox = 0; ox < Wo; ++ox)

@@ -49,7 +49,8 @@ typedef struct {
 } orc_model;
 
 /* Max |x| of the last conv/dwconv call: before the activation, and of its
- * output (the oracle is single-threaded). */
+ * output (each call reduces its threads' maxima into these after its
+ * parallel loop; calls themselves run one at a time). */
 static float g_pre_absmax, g_out_absmax;
 
 static void stat_rec(orc_model* m, const char* name, float v) {
@@ -211,10 +212,14 @@ static void silu(fmap* f) {
     for (size_t i = 0; i < n; ++i) f->d[i] = silu1(f->d[i]);
 }
 
-/* conv2d_forward (layers.c:41-81) + optional SiLU (layers.c:83-90). */
+/* conv2d_forward (layers.c:41-81) + optional SiLU (layers.c:83-90).
+ * Output channels run in parallel (OpenMP); every output element still sums
+ * its terms in the reference's order, so the result does not depend on the
+ * thread count. */
 static void conv(fmap* out, const fmap* in, const orc_tensor* w, const orc_tensor* b, int stride, int pad, int act) {
     const int oc = w->dims[0], ic = w->dims[1], kh = w->dims[2], kw = w->dims[3];
     const int H = in->h, W = in->w, Ho = out->h, Wo = out->w;
+    float pre_m = 0.0f, out_m = 0.0f;
     if (kh == 1 && kw == 1 && stride == 1 && pad == 0) {
         const int P = H * W;
         /* tensor_gemm's AVX2 loop fuses multiply-add on 16- and 8-wide blocks
@@ -222,6 +227,7 @@ static void conv(fmap* out, const fmap* in, const orc_tensor* w, const orc_tenso
          * (tensor.c:83-109, built without FP contraction). */
         const int P16 = (P / 16) * 16;
         const int Pv = P16 + ((P - P16) >= 8 ? 8 : 0);
+#pragma omp parallel for schedule(dynamic) reduction(max : pre_m, out_m)
         for (int o = 0; o < oc; ++o) {
             float* y = out->d + (size_t)o * P;
             for (int p = 0; p < P; ++p) y[p] = 0.0f;
@@ -238,43 +244,61 @@ static void conv(fmap* out, const fmap* in, const orc_tensor* w, const orc_tenso
             if (b)
                 for (int p = 0; p < P; ++p) y[p] += b->data[o];
             for (int p = 0; p < P; ++p)
-                if (fabsf(y[p]) > g_pre_absmax) g_pre_absmax = fabsf(y[p]);
+                if (fabsf(y[p]) > pre_m) pre_m = fabsf(y[p]);
             if (act)
                 for (int p = 0; p < P; ++p) y[p] = silu1(y[p]);
             for (int p = 0; p < P; ++p)
-                if (fabsf(y[p]) > g_out_absmax) g_out_absmax = fabsf(y[p]);
+                if (fabsf(y[p]) > out_m) out_m = fabsf(y[p]);
         }
-        return;
-    }
-    for (int o = 0; o < oc; ++o) {
-        for (int oy = 0; oy < Ho; ++oy) {
-            for (int ox = 0; ox < Wo; ++ox) {
-                float s = b ? b->data[o] : 0.0f;
-                for (int c = 0; c < ic; ++c) {
-                    for (int ky = 0; ky < kh; ++ky) {
-                        const int iy = oy * stride - pad + ky;
-                        if (iy < 0 || iy >= H) continue;
-                        for (int kx = 0; kx < kw; ++kx) {
-                            const int ix = ox * stride - pad + kx;
-                            if (ix < 0 || ix >= W) continue;
-                            const float prod = in->d[((size_t)c * H + iy) * W + ix] *
-                                               w->data[(((size_t)o * ic + c) * kh + ky) * kw + kx];
-                            s = s + prod;
+    } else {
+        /* Direct convolution: the reference sums, per output, the bias and
+         * then the products in (ci, ky, kx) order, skipping taps outside the
+         * image.  Walking (ci, ky, kx) outermost and the output plane inside
+         * adds the same terms to every output in the same order. */
+#pragma omp parallel for schedule(dynamic) reduction(max : pre_m, out_m)
+        for (int o = 0; o < oc; ++o) {
+            float* y = out->d + (size_t)o * Ho * Wo;
+            const float bv = b ? b->data[o] : 0.0f;
+            for (size_t p = 0; p < (size_t)Ho * Wo; ++p) y[p] = bv;
+            for (int c = 0; c < ic; ++c) {
+                const float* xc = in->d + (size_t)c * H * W;
+                for (int ky = 0; ky < kh; ++ky)
+                    for (int kx = 0; kx < kw; ++kx) {
+                        const float wv = w->data[(((size_t)o * ic + c) * kh + ky) * kw + kx];
+                        const int lo = pad - kx, hi = W - 1 + pad - kx;
+                        const int ox0 = lo > 0 ? (lo + stride - 1) / stride : 0;
+                        int ox1 = hi >= 0 ? hi / stride + 1 : 0;
+                        if (ox1 > Wo) ox1 = Wo;
+                        for (int oy = 0; oy < Ho; ++oy) {
+                            const int iy = oy * stride - pad + ky;
+                            if (iy < 0 || iy >= H) continue;
+                            const float* xr = xc + (size_t)iy * W - pad + kx;
+                            float* yr = y + (size_t)oy * Wo;
+                            for (int ox = ox0; ox < ox1; ++ox) {
+                                const float prod = xr[ox * stride] * wv;
+                                yr[ox] = yr[ox] + prod;
+                            }
                         }
                     }
-                }
+            }
+            for (size_t p = 0; p < (size_t)Ho * Wo; ++p) {
+                const float s = y[p];
                 const float r = act ? silu1(s) : s;
-                if (fabsf(s) > g_pre_absmax) g_pre_absmax = fabsf(s);
-                if (fabsf(r) > g_out_absmax) g_out_absmax = fabsf(r);
-                out->d[((size_t)o * Ho + oy) * Wo + ox] = r;
+                if (fabsf(s) > pre_m) pre_m = fabsf(s);
+                if (fabsf(r) > out_m) out_m = fabsf(r);
+                y[p] = r;
             }
         }
     }
+    if (pre_m > g_pre_absmax) g_pre_absmax = pre_m;
+    if (out_m > g_out_absmax) g_out_absmax = out_m;
 }
 
 /* dwconv3x3_same_forward (layers.c:269-290). */
 static void dwconv(fmap* out, const fmap* in, const orc_tensor* w, const orc_tensor* b, int act) {
     const int C = in->c, H = in->h, W = in->w;
+    float pre_m = 0.0f, out_m = 0.0f;
+#pragma omp parallel for schedule(dynamic) reduction(max : pre_m, out_m)
     for (int c = 0; c < C; ++c) {
         for (int y = 0; y < H; ++y) {
             for (int x = 0; x < W; ++x) {
@@ -290,17 +314,20 @@ static void dwconv(fmap* out, const fmap* in, const orc_tensor* w, const orc_ten
                     }
                 }
                 const float r = act ? silu1(s) : s;
-                if (fabsf(s) > g_pre_absmax) g_pre_absmax = fabsf(s);
-                if (fabsf(r) > g_out_absmax) g_out_absmax = fabsf(r);
+                if (fabsf(s) > pre_m) pre_m = fabsf(s);
+                if (fabsf(r) > out_m) out_m = fabsf(r);
                 out->d[((size_t)c * H + y) * W + x] = r;
             }
         }
     }
+    if (pre_m > g_pre_absmax) g_pre_absmax = pre_m;
+    if (out_m > g_out_absmax) g_out_absmax = out_m;
 }
 
 /* pool2d_max_forward, stride 1, padding k/2 excluded (layers.c:191-217). */
 static void maxpool(fmap* out, const fmap* in, int k) {
     const int C = in->c, H = in->h, W = in->w, pad = k / 2;
+#pragma omp parallel for schedule(static)
     for (int c = 0; c < C; ++c)
         for (int y = 0; y < H; ++y)
             for (int x = 0; x < W; ++x) {
@@ -499,6 +526,7 @@ static int attention(orc_model* m, const char* P, int heads, float ratio, fmap* 
         const float* k = qkv.d + (size_t)(h * blk + kd) * N;
         const float* v = qkv.d + (size_t)(h * blk + 2 * kd) * N;
         float* S = (float*)malloc((size_t)N * N * sizeof(float));
+#pragma omp parallel for schedule(static)
         for (int i = 0; i < N; ++i) {
             float* row = S + (size_t)i * N;
             for (int j = 0; j < N; ++j) {
@@ -517,6 +545,7 @@ static int attention(orc_model* m, const char* P, int heads, float ratio, fmap* 
             if (sum > 1e-12f)
                 for (int j = 0; j < N; ++j) row[j] /= sum;
         }
+#pragma omp parallel for schedule(static)
         for (int d = 0; d < hd; ++d)
             for (int j = 0; j < N; ++j) {
                 float s = 0.0f;

@@ -55,6 +55,37 @@ def test_s_width_bit_exact(weights_s0, tmp_path):
     _compare(weights_s0, yw.make_input(5, 64, 64), tmp_path, width_mult=2)
 
 
+def test_full_size_bit_exact(weights_n0, weights_s0, tmp_path):
+    """The benchmark sizes: n width at 640x640 (400-token attention) and at
+    1280x1280 (1600 tokens, 2 heads), and the s width at 1280x1280 (4 heads
+    over 1600 tokens).  The three reference forwards run side by side in
+    threads (the C calls release the GIL; the reference keeps no global
+    state), each compared with the oracle stage by stage, on the logits and
+    on the detections."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import yb_weights as yw
+    from oracle import Oracle, Reference
+
+    cases = [(weights_n0, 640, 1, 1), (weights_n0, 1280, 1, 9), (weights_s0, 1280, 2, 5)]
+
+    def run_ref(i):
+        w, hw, mult, seed = cases[i]
+        path = str(tmp_path / f"ref_{i}.bin")
+        r = Reference.forward(w, yw.make_input(seed, hw, hw), width_mult=mult, stage_path=path)
+        return r, yw.read_records(path)
+
+    with ThreadPoolExecutor(len(cases)) as ex:
+        refs = list(ex.map(run_ref, range(len(cases))))
+    for (w, hw, mult, seed), (r, rs) in zip(cases, refs):
+        o = Oracle(w).forward(yw.make_input(seed, hw, hw), stages=True)
+        assert list(rs.keys()) == list(o["stages"].keys())
+        for k, v in o["stages"].items():
+            assert np.array_equal(v, rs[k]), (hw, mult, k)
+        assert np.array_equal(o["logits"], r["logits"]), (hw, mult)
+        assert np.array_equal(o["dets"], r["dets"]), (hw, mult)
+
+
 def test_postprocess_matches_reference():
     """Random predictions with many exact score ties: the oracle's explicit
     (score desc, index asc) order equals the reference's qsort output."""
