@@ -18,6 +18,17 @@ converter's .bin layout, 64 images per GPU per step.  64 is the batch of the
   cpu_baseline  the reference's own C forward (compiled from its sources under
            oracle/_ref) on the host cores, one process per core.
 
+Further legs in the same JSON line:
+  strong   the batch-64 benchmark as a fixed global batch (64/N images per
+           GPU), device-resident and end to end with the detections gathered
+           into rank 0's host memory;
+  int8     the INT8 forward on the same images (device calibration over 32
+           seeded images), with its own roofline object;
+  config5  the s-width INT8 forward at 1280x1280, global batch 16 (16/N per
+           GPU);
+  int8_conv_sweep / fp32_conv_sweep  the five isolated convolution shapes of
+           the benchmark's sweep, device-resident, TOPS / TFLOP/s and GB/s.
+
 `--impl reference` times that CPU reference alone, on the same workload.
 """
 from __future__ import annotations
@@ -41,10 +52,12 @@ METRIC = "images/sec YOLO26n 640² FP32 & INT8 at 1/2/4/8 B200; conv TFLOPS/TOPS
 UNIT = "images/s"
 DATA = ("synthetic: seeded U[0,1) 640x640 images (numpy PCG64), seeded random-init YOLO26n weights "
         "(Kaiming conv, BN gamma 1+-0.1, beta/mean N(0,0.1), var U(0.5,1.5)) in the converter .bin layout")
-# DRAM bytes (read + write) of the conv family per image: 1637.4 MB over the
-# 93 convolution launches of one 64-image forward, ncu capture summarised in
-# profiles/conv_tc_dram_traffic_yolo26n_b64.md.
+# DRAM bytes (read + write) of the conv family per image, from an ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of every convolution launch
+# of one YOLO26n 640x640 forward, divided by the images of that forward.
 CONV_DRAM_BYTES_PER_IMAGE = 1637.4e6 / 64
+CONV_DRAM_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum over the 93 conv launches of one "
+                    "64-image forward, divided by 64 images and multiplied by this step's images per launch")
 
 
 def peaks():
@@ -318,12 +331,15 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist = None
+    gather_group = None
     if world > 1:
         import datetime
 
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        # Host-memory group for gathering detections into rank 0's host memory.
+        gather_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
     B, H = args.batch, args.hw
     tmpdir = tempfile.mkdtemp(prefix=f"yb_bench_{rank}_")
     weights = make_weights(tmpdir)
@@ -445,9 +461,7 @@ def run_ours(args):
                 "gpu_launches": n_ops.value * args.steps,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic,
-                             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the 93 conv "
-                                               "launches of one 64-image forward, scaled by images "
-                                               "(profiles/conv_tc_dram_traffic_yolo26n_b64.md)",
+                             "traffic_source": CONV_DRAM_SOURCE,
                              "kernel": "conv_tc_kernel (all tcgen05 convolution launches of one forward)",
                              "launches": len(conv), "bytes_per_launch": conv_bytes / len(conv),
                              "ms_per_launch": conv_ms / len(conv), "peak_source": src},
@@ -457,13 +471,24 @@ def run_ours(args):
                 "forward_breakdown_ms": {k: round(v["ms"], 4) for k, v in per_kind.items()},
                 "forward_share": {k: round(v["share"], 4) for k, v in per_kind.items()},
                 "clocks": clocks}
+    if not args.no_strong and args.global_batch % world == 0:
+        st = strong_leg(model, args, world, rank, local, barrier, max_over_ranks, gather_group)
+        if rank == 0:
+            line["strong"] = st
     if not args.no_int8:
         i8 = int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_over_ranks)
         if rank == 0:
             line["int8"] = i8
     model.close()
+    if not args.no_config5 and CONFIG5_GLOBAL % world == 0:
+        c5 = config5_leg(args, world, rank, local, tmpdir, barrier, max_over_ranks)
+        if rank == 0:
+            line["config5"] = c5
     if rank == 0 and not args.no_int8_sweep:
         line["int8_conv_sweep"] = int8_conv_sweep(peaks()[0])
+    if rank == 0 and not args.no_fp32_sweep:
+        hbm, bf16, src = peaks()
+        line["fp32_conv_sweep"] = fp32_conv_sweep(hbm, bf16, src)
     if dist:
         dist.barrier()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -637,6 +662,10 @@ def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_o
             d["launches"] += 1
             d["ms"] += s.ms
         tops = conv_ops / (conv_ms * 1e-3) / 1e12
+        conv_bytes = sum(s.bytes for s in conv)
+        hbm = peaks()[0]
+        i8_achieved = conv_bytes / (conv_ms * 1e-3) / 1e9
+        i8_bytes_img = sum(s.bytes for s in stats) / B
         out = {"metric": "images/sec YOLO26n 640x640 INT8", "value": world * B * args.steps / (dev_ms * 1e-3),
                "unit": UNIT, "ms_per_step": dev_ms / args.steps, "dtype": "int8 (int32 accumulation)",
                "config": {"workload": f"YOLO26n INT8 forward + top-300 decode, {H}x{H}, {B} images per GPU, "
@@ -657,6 +686,18 @@ def int8_leg(model, args, world, rank, stream, host_in, host_out, barrier, max_o
                           "note": "device-resident single-image forward, one per GPU"},
                "clocks": clocks,
                "gpu_launches": n_ops.value * args.steps,
+               "roofline": {"bound": "hbm", "achieved": i8_achieved, "peak": hbm, "unit": "GB/s",
+                            "frac": i8_achieved / hbm, "traffic": None, "peak_source": peaks()[2],
+                            "kernel": "conv_i8_kernel (all tcgen05 kind::i8 convolution launches of one forward)",
+                            "launches": len(conv), "bytes_per_launch": conv_bytes / len(conv),
+                            "ms_per_launch": conv_ms / len(conv),
+                            "note": "algorithmic int8 bytes (input, output and weights once per launch) over "
+                                    "CUDA-event launch times"},
+               "forward_roofline": {"bytes_per_image": i8_bytes_img,
+                                    "achieved_gbs": world * B * args.steps / (dev_ms * 1e-3) * i8_bytes_img / 1e9,
+                                    "frac": world * B * args.steps / (dev_ms * 1e-3) * i8_bytes_img / 1e9 / hbm,
+                                    "note": "whole INT8 forward: algorithmic bytes of every launch per image x "
+                                            "images/s, against the measured HBM copy bandwidth"},
                "conv_tops": {"achieved": tops, "peak_nominal": INT8_PEAK_TOPS_NOMINAL,
                              "frac_of_nominal": tops / INT8_PEAK_TOPS_NOMINAL,
                              "note": "algorithmic int8 ops (2 x MACs) of the conv_i8 launches"},
@@ -733,6 +774,239 @@ def int8_conv_sweep(hbm_gbs, batch=16, reps=30):
             "note": "bit-exact against the CPU INT8 oracle (tests/test_gpu_int8.py); small maps fit in L2"}
 
 
+FP32_SWEEP = INT8_SWEEP  # the same five shapes, FP32 (split-bf16 tcgen05 products, fp32 accumulation)
+
+
+def fp32_conv_sweep(hbm_gbs, bf16_tflops, src, batch=16, reps=30):
+    """Device-resident timing of the FP32 convolution (yb_conv_run: conv +
+    bias + SiLU with the model graph's kernel and operand mode for the shape)
+    on the sweep shapes, `batch` images per launch, CUDA events on a dedicated
+    stream over `reps` launches after 5 warm-up launches.  FLOPs = 2 x MACs;
+    bytes = fp32 input + output + weights once (4 bytes per element)."""
+    import numpy as np
+    import torch
+
+    import yolo_b200 as yb
+
+    L = yb.lib()
+    stream = torch.cuda.Stream()
+    rows = []
+    tot_flops = tot_bytes = tot_ms = 0.0
+    for ci, co, k, stride, hw in FP32_SWEEP:
+        rng = np.random.default_rng(ci * 1000 + co)
+        w = (rng.standard_normal((co, ci, k, k)) * np.sqrt(2.0 / (ci * k * k))).astype(np.float32)
+        b = (rng.standard_normal(co) * 0.1).astype(np.float32)
+        pad = (k - 1) // 2
+        h = C.c_void_p()
+        yb.check(L.yb_conv_create(torch.cuda.current_device(), w.ctypes.data, b.ctypes.data, co, ci, k, k, stride,
+                                  pad, 1, C.byref(h)), "yb_conv_create")
+        cp = L.yb_conv_ci_pad(h)
+        ho = (hw + 2 * pad - k) // stride + 1
+        cop = (co + 7) // 8 * 8
+        if cp == 0:
+            x = torch.randn((batch, ci, hw, hw), device="cuda")
+        else:
+            x = torch.zeros((2, batch, hw, hw, cp), dtype=torch.bfloat16, device="cuda")
+            v = torch.randn((batch, hw, hw, ci), device="cuda")
+            x[0, ..., :ci] = v.to(torch.bfloat16)
+            x[1, ..., :ci] = (v - x[0, ..., :ci].float()).to(torch.bfloat16)
+        y = torch.empty((2, batch, ho, ho, cop), dtype=torch.bfloat16, device="cuda")
+        torch.cuda.synchronize()
+        run = lambda: yb.check(L.yb_conv_run(h, x.data_ptr(), batch, hw, hw, y.data_ptr(),  # noqa: E731
+                                             C.c_void_p(stream.cuda_stream)), "yb_conv_run")
+        for _ in range(5):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        yb.check(L.yb_conv_destroy(h), "yb_conv_destroy")
+        flops = 2.0 * batch * ho * ho * co * ci * k * k
+        nbytes = 4.0 * (batch * hw * hw * ci + batch * ho * ho * co + co * ci * k * k)
+        tot_flops += flops
+        tot_bytes += nbytes
+        tot_ms += ms
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        tf = flops / (ms * 1e-3) / 1e12
+        rows.append({"shape": f"{ci}->{co} {k}x{k} s{stride} @{hw}x{hw}", "ms": round(ms, 5),
+                     "tflops": round(tf, 2), "tflops_frac": round(tf / bf16_tflops, 4), "gbs": round(gbs, 1),
+                     "hbm_frac": round(gbs / hbm_gbs, 3),
+                     "kernel": "stem_kernel (NCHW fp32 input)" if cp == 0 else "conv_tc_kernel"})
+    return {"images_per_launch": batch, "shapes": rows,
+            "tflops_all_shapes": round(tot_flops / (tot_ms * 1e-3) / 1e12, 2),
+            "gbs_all_shapes": round(tot_bytes / (tot_ms * 1e-3) / 1e9, 1),
+            "peak_tflops": bf16_tflops, "peak_gbs": hbm_gbs, "peak_source": src,
+            "note": "FP32 activations as split bf16 pairs, 3 tcgen05 bf16 products per MAC (the tensor pipe "
+                    "executes 3x the algorithmic FLOPs); parity: tests/test_gpu_conv_handle.py"}
+
+
+def strong_leg(model, args, world, rank, local, barrier, max_over_ranks, gather_group):
+    """The batch-64 benchmark as a fixed global batch: 64 images (seeds 1..64)
+    split 64/N per GPU.  Device-resident time (CUDA events, max over ranks)
+    and end to end: each step streams the rank's pinned fp32 input to its GPU
+    (two batches in flight), copies the detections back and gathers every
+    rank's detections into rank 0's host memory."""
+    import torch
+
+    import yb_weights as yw
+
+    G, H = args.global_batch, args.hw
+    per = G // world
+    imgs = yw.make_batch(range(rank * per + 1, rank * per + per + 1), H, H)
+    host_in = torch.from_numpy(imgs).pin_memory()
+    d_in, d_out = model.plan_io(per, H, H)
+    stream = torch.cuda.Stream()
+    dev = host_in.to(f"cuda:{local}")
+    torch.cuda.synchronize()
+    model.forward_device(dev.data_ptr(), d_out, per, H, H, 300, stream.cuda_stream)
+    torch.cuda.synchronize()
+    del dev
+    for _ in range(args.warmup):
+        model.forward_device(d_in, d_out, per, H, H, 300, stream.cuda_stream)
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        model.forward_device(d_in, d_out, per, H, H, 300, stream.cuda_stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    outs = [torch.empty((per, 300, 6), dtype=torch.float32).pin_memory() for _ in range(2)]
+    gathered = [torch.empty((per, 300, 6), dtype=torch.float32) for _ in range(world)] if rank == 0 else None
+
+    def gather(t):
+        if world == 1:
+            gathered[0].copy_(t)
+        else:
+            import torch.distributed as dist
+
+            dist.gather(t, gathered, dst=0, group=gather_group)
+
+    def run(k):
+        pending = []
+        for i in range(k):
+            if len(pending) == 2:
+                t, o = pending.pop(0)
+                model.wait(t)
+                gather(o)
+            o = outs[i % 2]
+            pending.append((model.submit(host_in.data_ptr(), per, H, H, o.data_ptr()), o))
+        for t, o in pending:
+            model.wait(t)
+            gather(o)
+
+    run(max(2, args.warmup // 2))
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    run(args.steps)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    return {"metric": "images/sec YOLO26n 640x640 FP32, global batch 64 split across the GPUs",
+            "value": G * args.steps / (dev_ms * 1e-3), "unit": UNIT, "ms_per_step": dev_ms / args.steps,
+            "scaling": "strong", "images_per_gpu": per, "global_batch": G,
+            "e2e": {"value": G * args.steps / e2e_s, "unit": UNIT,
+                    "h2d_bytes_per_step": G * 3 * H * H * 4, "d2h_bytes_per_step": G * 300 * 6 * 4,
+                    "mode": "streaming submit/wait (two batches in flight) of each rank's pinned fp32 shard, "
+                            "detections copied back and gathered into rank 0's host memory every step"}}
+
+
+CONFIG5_GLOBAL = 16
+CONFIG5_HW = 1280
+CONFIG5_CALIB = 4
+
+
+def config5_leg(args, world, rank, local, tmpdir, barrier, max_over_ranks):
+    """The s-width (channels x2) YOLO26 INT8 forward at 1280x1280, global
+    batch 16 split 16/N per GPU: C2PSA attention over 1600 tokens in 4 heads
+    of 64 channels, 33,600 anchors into the top-300 decode.  Weights: seeded
+    random init (seed 0); INT8 scales from a device calibration over 4 seeded
+    U[0,1) 1280x1280 images.  Device-resident time (CUDA events, max over
+    ranks), end to end through the streaming API, and the conv_i8 roofline."""
+    import torch
+
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    L = yb.lib()
+    G, H = CONFIG5_GLOBAL, CONFIG5_HW
+    per = max(1, G // world)
+    w = os.path.join(tmpdir, "yolo26s_seed0.bin")
+    yw.write_bin(w, yw.random_state("s", 0))
+    m = yb.Model(w, device=local)
+    try:
+        t0 = time.perf_counter()
+        scales = m.calibrate_int8(yw.make_batch(range(30000, 30000 + CONFIG5_CALIB), H, H), apply=True)
+        calib_s = time.perf_counter() - t0
+        imgs = yw.make_batch(range(40000 + rank * per, 40000 + rank * per + per), H, H)
+        host_in = torch.from_numpy(imgs).pin_memory()
+        d_in, d_out = m.plan_io(per, H, H)
+        stream = torch.cuda.Stream()
+        dev = host_in.to(f"cuda:{local}")
+        torch.cuda.synchronize()
+        m.forward_device(dev.data_ptr(), d_out, per, H, H, 300, stream.cuda_stream)
+        torch.cuda.synchronize()
+        del dev
+        for _ in range(args.warmup):
+            m.forward_device(d_in, d_out, per, H, H, 300, stream.cuda_stream)
+        torch.cuda.synchronize()
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(bus_id_of(local) if rank == 0 else None) as clk:
+            ev0.record(stream)
+            for _ in range(args.steps):
+                m.forward_device(d_in, d_out, per, H, H, 300, stream.cuda_stream)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+        barrier()
+        dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+        clocks = clk.summary() if rank == 0 else None
+        es_s = timed_stream(m, host_in, per, H, args, barrier, max_over_ranks)
+        n_ops = C.c_int()
+        yb.check(L.yb_cuda_profile_ops(m.ctx, per, H, H, 300, 0, None, 0, C.byref(n_ops)), "yb_cuda_profile_ops")
+        out = None
+        if rank == 0:
+            stats = (OpStat * n_ops.value)()
+            yb.check(L.yb_cuda_profile_ops(m.ctx, per, H, H, 300, 3, stats, n_ops.value, C.byref(n_ops)),
+                     "yb_cuda_profile_ops")
+            conv = [s for s in stats if s.kind == 0]
+            conv_ms = sum(s.ms for s in conv)
+            conv_bytes = sum(s.bytes for s in conv)
+            conv_ops = sum(s.flops for s in conv)
+            per_kind = {}
+            for s in stats:
+                d = per_kind.setdefault(INT8_KINDS[s.kind], {"launches": 0, "ms": 0.0})
+                d["launches"] += 1
+                d["ms"] += s.ms
+            hbm = peaks()[0]
+            ach = conv_bytes / (conv_ms * 1e-3) / 1e9
+            out = {"metric": "images/sec YOLO26s-width INT8 1280x1280, global batch 16 split across the GPUs",
+                   "value": G * args.steps / (dev_ms * 1e-3) if world <= G else None, "unit": UNIT,
+                   "ms_per_step": dev_ms / args.steps, "scaling": "strong", "images_per_gpu": per,
+                   "global_batch": per * world, "dtype": "int8 (int32 accumulation)",
+                   "calibration": {"images": CONFIG5_CALIB, "hw": H, "seconds": round(calib_s, 3),
+                                   "scales": len(scales), "source": "device (FP32 forwards with statistics)"},
+                   "e2e": {"value": per * world * args.steps / es_s, "unit": UNIT,
+                           "h2d_bytes_per_step": per * world * 3 * H * H * 4,
+                           "d2h_bytes_per_step": per * world * 300 * 6 * 4, "mode": STREAM_NOTE},
+                   "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                                "kernel": "conv_i8_kernel", "launches": len(conv),
+                                "bytes_per_launch": conv_bytes / len(conv), "ms_per_launch": conv_ms / len(conv)},
+                   "conv_tops": conv_ops / (conv_ms * 1e-3) / 1e12,
+                   "forward_breakdown_ms": {k: round(v["ms"], 4) for k, v in per_kind.items()},
+                   "gpu_launches": n_ops.value * args.steps, "clocks": clocks,
+                   "parity": "tests/test_gpu_configs.py (s-width INT8 1280x1280, batch 2, bit-exact)"}
+    finally:
+        m.close()
+    return out
+
+
 class OpStat(C.Structure):
     _fields_ = [("kind", C.c_int), ("step", C.c_int), ("ms", C.c_double), ("flops", C.c_double),
                 ("bytes", C.c_double)]
@@ -749,6 +1023,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-int8-sweep", action="store_true")
     ap.add_argument("--no-int8", action="store_true", help="skip the INT8 model leg")
+    ap.add_argument("--global-batch", type=int, default=64, help="global batch of the strong-scaling leg")
+    ap.add_argument("--no-strong", action="store_true", help="skip the global-batch-64 (strong scaling) leg")
+    ap.add_argument("--no-config5", action="store_true", help="skip the s-width INT8 1280x1280 leg")
+    ap.add_argument("--no-fp32-sweep", action="store_true", help="skip the FP32 convolution sweep")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -202,13 +202,19 @@ status_t yb_cuda_get_head(void* ctx, float* logits, float* boxes, int* n_anchors
  * synchronize.
  *
  * Scratch (the per-anchor best scores) lives in one fixed array of 2^20
- * floats (4 MiB) inside the library's device code, held by every GPU that
- * loads the library until the process exits: B*N above 1048576 anchors, or
- * min(max_det, N) above 1024, returns ERROR_INVALID_DIMS before any launch.
- * The first call on each device looks the array's address up (with that
- * device current); make that first call before any stream capture.  All calls
- * on a device share the array, so calls that overlap in time (other streams,
- * other threads) race: order them on one stream or with events. */
+ * floats (4 MiB) inside the library's device code: B*N above 1048576
+ * anchors, or min(max_det, N) above 1024, returns ERROR_INVALID_DIMS before
+ * any launch.  Under CUDA's lazy module loading (the default since CUDA
+ * 12.2) the array and the kernels are placed on a device when the library's
+ * device code is first used there; from then on the device holds them until
+ * the process exits.  yb_cuda_init does that loading for its device.  A
+ * caller that never creates a context on a device should make one warm-up
+ * call there before its pool allocator reserves the device's memory, and
+ * before any stream capture (the first call on a device also looks the
+ * array's address up, with that device current).  The cached address does
+ * not survive cudaDeviceReset.  All calls on a device share the array, so
+ * calls that overlap in time (other streams, other threads) race: order them
+ * on one stream or with events. */
 status_t yb_cuda_detect_topk_noalloc(const float* d_logits, const float* d_boxes, int B, int N, int nc,
                                      int max_det, float* d_dets, void* stream);
 
@@ -216,9 +222,37 @@ status_t yb_cuda_detect_topk_noalloc(const float* d_logits, const float* d_boxes
  * [g*B/G, (g+1)*B/G) runs on ctxs[g] from its own host thread; results land
  * at the matching rows of out_dets.  Each shard is waited on with a host
  * deadline of timeout_ms (<= 0: no deadline); an expired deadline returns
- * ERROR_TIMEOUT after the other shards have finished or timed out. */
+ * ERROR_TIMEOUT after the other shards have finished or timed out.  After
+ * ERROR_TIMEOUT the input copy of a late shard may still be queued on its
+ * GPU: keep in_nchw valid until the next call on those contexts returns, or
+ * until they are destroyed. */
 status_t yb_cuda_forward_sharded(void* const* ctxs, int G, const float* in_nchw, int B, int H, int W,
                                  float* out_dets, int max_det, int timeout_ms);
+
+/* One FP32 convolution on tensors already in GPU memory: conv2d_forward +
+ * bias + optional SiLU (layers.c:41-90), with the kernel and operand mode
+ * the model graph picks for the same shape.  Additive (the reference's
+ * conv2d_forward takes host tensors and runs one image); used for the
+ * isolated convolution sweep and its tests.
+ *
+ * yb_conv_create: w [co][ci][kh][kw] fp32 (BatchNorm already folded), b [co]
+ * or NULL, kh = kw in {1, 3}, act 0 (none) or 1 (SiLU); packs and uploads to
+ * `device`.  yb_conv_ci_pad returns the channel stride the input must have
+ * (ci rounded up to a multiple of 8, extra channels zero), or 0 when the
+ * handle reads an NCHW fp32 input [B,ci,H,W] (3x3 stride-2 convolutions of
+ * <= 4 input channels with SiLU and 16/32/64 outputs: the first layer's
+ * kernel).  Otherwise d_x is split NHWC: a bf16 plane hi [B,H,W,ci_pad]
+ * followed by a bf16 plane lo of the same size, value = hi + lo.  d_y is
+ * split NHWC [B,Ho,Wo,co8] (co rounded up to 8) the same way.  16-byte
+ * aligned buffers.  Enqueued on `stream` (NULL = default stream); does not
+ * synchronize.  yb_conv_check synchronizes and reads the handle's device
+ * error word (bounded waits that gave up). */
+status_t yb_conv_create(int device, const float* w, const float* b, int co, int ci, int kh, int kw, int stride,
+                        int pad, int act, void** conv);
+int yb_conv_ci_pad(void* conv);
+status_t yb_conv_run(void* conv, const void* d_x, int B, int H, int W, void* d_y, void* stream);
+status_t yb_conv_check(void* conv);
+status_t yb_conv_destroy(void* conv);
 
 /* One kernel launch of a plan, as measured by yb_cuda_profile_ops. */
 typedef struct {

@@ -53,6 +53,19 @@ def weights_n0_soft(workdir):
 
 
 @pytest.fixture(scope="session")
+def weights_n0_o2m(workdir):
+    """Seed-0 weights (class convs scaled by 0.01, so scores rank) with the
+    one-to-one Detect branches removed: only model.23.cv2 / model.23.cv3
+    remain, which the reference falls back to (detect.c:297-299)."""
+    import yb_weights as yw
+
+    path = str(workdir / "yolo26n_seed0_o2m.bin")
+    sd = yw.random_state("n", 0, cls_scale=0.01)
+    yw.write_bin(path, type(sd)((k, v) for k, v in sd.items() if ".one2one_" not in k))
+    return path
+
+
+@pytest.fixture(scope="session")
 def weights_s0(workdir):
     import yb_weights as yw
 

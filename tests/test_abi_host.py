@@ -206,3 +206,18 @@ def test_tensor_view_keeps_its_array_alive():
     gc.collect()
     assert wr() is not None
     assert np.ctypeslib.as_array(t.data, shape=(12,))[11] == 11.0
+
+
+def test_postprocess_topk_limit_is_reported():
+    """detect_postprocess_from_pred keeps at most 1024 rows (the device top-k
+    limit; the reference has none): a larger min(max_det, N, rows) is refused
+    with ERROR_INVALID_DIMS before any device work, with the limit named."""
+    import yolo_b200 as yb
+
+    L = yb.lib()
+    N, nc, rows = 2000, 3, 1500
+    pred = np.zeros((N, 4 + nc), np.float32)
+    out = yb.tensor_view(np.zeros((1, rows, 6, 1), np.float32))
+    st = L.detect_postprocess_from_pred(pred.ctypes.data_as(C.POINTER(C.c_float)), N, nc, 1500, C.byref(out))
+    assert st == yb.ERROR_INVALID_DIMS
+    assert "1024" in yb.last_error()

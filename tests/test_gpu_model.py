@@ -135,3 +135,32 @@ def test_s_width_model(weights_s0):
         assert rel_err(got["stages"][name], want) <= STAGE_RTOL, name
     assert float(np.max(np.abs(logits[0] - ref["logits"]))) <= LOGIT_ATOL
     m.close()
+
+
+def test_detect_cv2_cv3_fallback(weights_n0_o2m):
+    """Without one2one_cv2/cv3 in the checkpoint the Detect head runs the
+    one-to-many cv2/cv3 branches (detect.c:297-299): FP32 stages, logits and
+    detections against the oracle, and the INT8 forward bit-exact with the
+    INT8 oracle under the same table."""
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    o = _oracle(weights_n0_o2m)
+    img = yw.make_input(14, 320, 320)
+    m = yb.Model(weights_n0_o2m)
+    try:
+        got = m.forward(img)
+        logits, _ = m.head(1)
+        ref = o.forward(img)
+        assert float(np.max(np.abs(logits[0] - ref["logits"]))) <= LOGIT_ATOL
+        c = compare_dets(got["dets"][0], ref["dets"])
+        print(f"cv2/cv3 FP32 dets: {c}")
+        assert dets_ok(c) and c["matched"] >= 290
+        scales = m.calibrate_int8(yw.make_batch(range(1300, 1303), 128, 128))
+        q = m.forward(img)["dets"][0]
+        lq, _ = m.head(1)
+        rq = o.forward_i8(img, scales)
+        assert np.array_equal(lq[0], rq["logits"])
+        assert dets_ok(compare_dets(q, rq["dets"]))
+    finally:
+        m.close()

@@ -47,6 +47,20 @@ def test_soft_weights(weights_n0_soft, tmp_path):
     _compare(weights_n0_soft, yw.make_input(7, 128, 128), tmp_path)
 
 
+def test_cv2_cv3_fallback(weights_n0_o2m, weights_n0_soft, tmp_path):
+    """A checkpoint without the one-to-one Detect branches: the reference
+    falls back to model.23.cv2 / cv3 (detect.c:297-299); so does the oracle,
+    bit for bit, and the result differs from the one-to-one branches'."""
+    import yb_weights as yw
+    from oracle import Oracle
+
+    img = yw.make_input(13, 128, 128)
+    _compare(weights_n0_o2m, img, tmp_path)
+    a = Oracle(weights_n0_o2m).forward(img)["dets"]
+    b = Oracle(weights_n0_soft).forward(img)["dets"]
+    assert not np.array_equal(a, b)
+
+
 def test_s_width_bit_exact(weights_s0, tmp_path):
     """The s width (channels x2): the harness re-allocates the reference's
     model_t.buffers wider, since model_create sizes them for n."""

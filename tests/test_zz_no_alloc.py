@@ -1,6 +1,7 @@
 """yb_cuda_detect_topk_noalloc, the top-k entry point that allocates nothing,
 called through the C ABI on head tensors from a full forward and compared
-with that forward's own detections (yb_cuda_forward), on two calls in a row.
+with that forward's own detections (yb_cuda_forward), on two calls in a row,
+then once more on a side stream with the device's free memory unchanged.
 The file name sorts last so the test also runs after every other GPU test in
 the same process; it passes alone as well."""
 import numpy as np
@@ -35,12 +36,24 @@ def test_detect_topk_noalloc_matches_forward(weights_n0):
                                                    d_dets.data_ptr(), None), "yb_cuda_detect_topk_noalloc")
             torch.cuda.synchronize()
             outs.append(d_dets.cpu().numpy())
+        # Once the first call on the device has run, a call on another stream
+        # leaves the device's free memory unchanged: nothing is allocated.
+        side = torch.cuda.Stream()
+        d_dets = torch.full((B, K, 6), float("nan"), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        free0, _ = torch.cuda.mem_get_info()
+        yb.check(L.yb_cuda_detect_topk_noalloc(d_logits.data_ptr(), d_boxes.data_ptr(), B, N, nc, K,
+                                               d_dets.data_ptr(), side.cuda_stream), "yb_cuda_detect_topk_noalloc")
+        side.synchronize()
+        free1, _ = torch.cuda.mem_get_info()
+        assert free1 == free0, (free0, free1)
+        outs.append(d_dets.cpu().numpy())
         for got in outs:
             for i in range(B):
                 c = compare_dets(got[i], want[i])
                 print(f"image {i}: {c}; bit-exact {np.array_equal(got[i], want[i])}")
                 assert dets_ok(c) and c["k"] == min(K, N)
-        assert np.array_equal(outs[0], outs[1])
+        assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
         # Sizes beyond the scratch array are refused before any launch.
         st = L.yb_cuda_detect_topk_noalloc(d_logits.data_ptr(), d_boxes.data_ptr(), 1 << 20, 2, nc, K,
                                            d_dets.data_ptr(), None)

@@ -212,10 +212,9 @@ cudaError_t Engine::set_weights(WeightMap&& w, int num_classes, std::string* why
   nc_ = num_classes;
   const HostTensor* sw = find("model.0.conv.weight");
   const HostTensor* sb = find("model.0.conv.bias");
-  if (!sw || !sb) {
-    *why = "missing model.0.conv.weight/bias";
-    return cudaErrorInvalidValue;
-  }
+  // Any weight file loads, as in the reference (model.c:182-198); a missing
+  // layer is reported when a forward needs it (plan build).
+  if (!sw || !sb) return cudaSuccess;
   stem_.co = sw->dims[0];
   stem_.ci = sw->dims[1];
   stem_.k = sw->dims[2];
@@ -669,6 +668,10 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
   const int H = p->H, W = p->W;
   // step 0: stem (model.0), NCHW input read directly.
   step = 0;
+  if (!stem_.w) {
+    *why = "missing model.0.conv.weight/bias";
+    return cudaErrorInvalidValue;
+  }
   YB_TRY(alloc_raw(static_cast<size_t>(B) * 3 * H * W * 4, &p->d_in));
   {
     YB_TRY(alloc_buf((H + 2 - stem_.k) / 2 + 1, (W + 2 - stem_.k) / 2 + 1, stem_.co, &S[0]));

@@ -345,6 +345,8 @@ extern "C" status_t yb_cuda_init(int device, void** ctx) {
     return ERROR_INVALID_DIMS;
   }
   if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_status(e, "cudaSetDevice");
+  status_t pst = noalloc_prepare_current_device();
+  if (pst != SUCCESS) return pst;
   std::unique_ptr<Ctx> c(new Ctx());
   c->eng.reset(new Engine(device));
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "engine init");
@@ -919,8 +921,11 @@ status_t run_shard(Ctx* c, const float* in, int B, int H, int W, float* out, int
       return ERROR_DEVICE;
     }
     if (expired()) {
-      // The input may still be read by the copy engine: let that copy finish
-      // before returning control of the caller's buffer.
+      // The input may still be read by the copy engine: give that copy up to
+      // a second to finish.  The copy is queued behind earlier work on this
+      // context's stream, so it can outlast the wait; the caller must keep
+      // the input valid until the next call on this context returns (the
+      // header states this).
       const auto t0 = clock::now();
       while (cudaEventQuery(c->h2d_done) == cudaErrorNotReady && clock::now() - t0 < std::chrono::seconds(1))
         std::this_thread::sleep_for(std::chrono::microseconds(50));
@@ -1122,7 +1127,8 @@ extern "C" status_t detect_postprocess_from_pred(const float* pred, int N, int n
   std::vector<float> rows(static_cast<size_t>(cap) * 6, 0.f);
   if (k > 0) {
     if (k > kTopkMax) {
-      set_error("k exceeds the device top-k limit");
+      set_error("min(max_det, N, output rows) = " + std::to_string(k) + " exceeds the device top-k limit of " +
+                std::to_string(kTopkMax) + " (the reference has no limit)");
       return ERROR_INVALID_DIMS;
     }
     DevScope* sc = current_scope();

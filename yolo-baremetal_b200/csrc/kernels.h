@@ -250,6 +250,9 @@ struct TopkArgs {
   int B = 0, N = 0, nc = 0, max_det = 300, cap = 300;
 };
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t s);
+// Sets the top-k kernel's shared-memory attribute on the current device (done
+// once per device), which also loads its code there.
+cudaError_t prepare_topk();
 // Largest k supported by the top-k kernel.
 constexpr int kTopkMax = 1024;
 
@@ -263,6 +266,13 @@ cudaError_t launch_split_to_nchw(SView in, int B, int C, int H, int W, float* ou
 cudaError_t launch_gather_concat(SView src0, int c0, int up0, SView src1, int c1, int B, int H, int W, SOut out,
                                  cudaStream_t s);
 // In-place SiLU on a split view.
-cudaError_t launch_silu(SOut t, int B, int HW, int C, cudaStream_t s);
+// Plain fp32 NCHW kernels behind the standalone layers.h entry points:
+// in-place SiLU over n values; max pool (padding k/2 excluded) and nearest
+// upsample of `planes` = N*C planes of H x W.
+cudaError_t launch_silu_f32(float* x, long long n, cudaStream_t s);
+cudaError_t launch_maxpool_nchw(const float* in, long long planes, int H, int W, int k, int stride, int Ho, int Wo,
+                                float* out, cudaStream_t s);
+cudaError_t launch_upsample_nchw(const float* in, long long planes, int H, int W, int scale, float* out,
+                                 cudaStream_t s);
 
 }  // namespace yb

@@ -316,37 +316,63 @@ extern "C" status_t conv2d_forward(tensor_t* output, const tensor_t* input, cons
   return conv_block_forward(output, input, weight, bias, params, false);
 }
 
+namespace {
+// Runs `fn(d_in, d_out)` on device copies of a whole host fp32 tensor (n_in
+// values in, n_out values out; out may alias in when in_place), then copies
+// the result back: the element-wise and copy layers work on the reference's
+// own NCHW layout, all images, with no split representation in between.
+template <class F>
+status_t nchw_call(const float* in, size_t n_in, float* out, size_t n_out, bool in_place, const char* what, F fn) {
+  DevScope* sc = current_scope();
+  if (!sc) return ERROR_DEVICE;
+  DevMem din, dout;
+  cudaError_t e = din.alloc(n_in * 4);
+  if (e == cudaSuccess && !in_place) e = dout.alloc(n_out * 4);
+  if (e != cudaSuccess) return cuda_status(e, what);
+  float* d_out = in_place ? din.f() : dout.f();
+  e = cudaMemcpyAsync(din.p, in, n_in * 4, cudaMemcpyHostToDevice, sc->stream);
+  if (e == cudaSuccess) e = fn(din.f(), d_out, sc->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, d_out, n_out * 4, cudaMemcpyDeviceToHost, sc->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(sc->stream);
+  return cuda_status(e, what);
+}
+
+size_t numel(const tensor_t* t) {
+  return static_cast<size_t>(t->dims[0]) * t->dims[1] * t->dims[2] * t->dims[3];
+}
+}  // namespace
+
 extern "C" status_t silu_forward(tensor_t* t) {
   if (!t || !t->data) return ERROR_NULL_POINTER;
-  Kit k;
-  DT x = k.upload(t);
-  if (k.ok()) k.err = launch_silu(x.o(), 1, x.H * x.W, x.Cp, k.sc->stream);
-  k.download(x, t);
-  return k.finish("silu");
+  const size_t n = numel(t);
+  if (n == 0) return SUCCESS;
+  return nchw_call(t->data, n, t->data, n, true, "silu",
+                   [n](float* x, float*, cudaStream_t s) { return launch_silu_f32(x, static_cast<long long>(n), s); });
 }
 
 extern "C" status_t pool2d_max_forward(tensor_t* output, const tensor_t* input, int kernel_size, int stride) {
   if (!output || !input || !output->data || !input->data) return ERROR_NULL_POINTER;
-  if (kernel_size < 1 || stride < 1 || output->dims[1] != input->dims[1]) return ERROR_INVALID_DIMS;
-  Kit k;
-  DT x = k.upload(input);
-  DT y = k.tensor(output->dims[2], output->dims[3], input->dims[1]);
-  k.pool(x, 0, kernel_size, stride, y, 0, input->dims[1]);
-  k.download(y, output);
-  return k.finish("max pool");
+  if (kernel_size < 1 || stride < 1 || output->dims[1] != input->dims[1] || output->dims[0] != input->dims[0])
+    return ERROR_INVALID_DIMS;
+  const long long planes = static_cast<long long>(input->dims[0]) * input->dims[1];
+  const int H = input->dims[2], W = input->dims[3], Ho = output->dims[2], Wo = output->dims[3];
+  if (numel(output) == 0) return SUCCESS;
+  return nchw_call(input->data, numel(input), output->data, numel(output), false, "max pool",
+                   [=](float* x, float* y, cudaStream_t s) {
+                     return launch_maxpool_nchw(x, planes, H, W, kernel_size, stride, Ho, Wo, y, s);
+                   });
 }
 
 extern "C" status_t upsample_nearest_forward(tensor_t* output, const tensor_t* input, int scale) {
   if (!output || !input || !output->data || !input->data) return ERROR_NULL_POINTER;
-  if (scale < 1 || output->dims[1] != input->dims[1] || output->dims[2] != input->dims[2] * scale ||
-      output->dims[3] != input->dims[3] * scale)
+  if (scale < 1 || output->dims[0] != input->dims[0] || output->dims[1] != input->dims[1] ||
+      output->dims[2] != input->dims[2] * scale || output->dims[3] != input->dims[3] * scale)
     return ERROR_INVALID_DIMS;
-  Kit k;
-  DT x = k.upload(input);
-  DT y = k.tensor(output->dims[2], output->dims[3], input->dims[1]);
-  if (k.ok()) k.err = launch_gather_concat(x.v(), x.Cp, scale, x.v(), 0, 1, y.H, y.W, y.o(), k.sc->stream);
-  k.download(y, output);
-  return k.finish("upsample");
+  const long long planes = static_cast<long long>(input->dims[0]) * input->dims[1];
+  const int H = input->dims[2], W = input->dims[3];
+  if (numel(output) == 0) return SUCCESS;
+  return nchw_call(input->data, numel(input), output->data, numel(output), false, "upsample",
+                   [=](float* x, float* y, cudaStream_t s) { return launch_upsample_nchw(x, planes, H, W, scale, y, s); });
 }
 
 extern "C" status_t concat_forward(tensor_t* output, const tensor_t* input1, const tensor_t* input2, int dim) {

@@ -25,8 +25,9 @@ namespace yb {
 namespace {
 
 // Capacity of the scratch array, in anchors (B * N): 4 MiB of floats, enough
-// for 124 images of 640x640 (8400 anchors each).  Every GPU that loads the
-// library holds this array until the process exits.
+// for 124 images of 640x640 (8400 anchors each).  Every GPU on which the
+// library's device code has been loaded holds this array until the process
+// exits.
 constexpr long long kScratchAnchors = 1ll << 20;
 
 static __device__ __align__(256) float g_anchor_max[kScratchAnchors];
@@ -60,7 +61,9 @@ __global__ void __launch_bounds__(256) anchor_max_kernel(const float* __restrict
 }
 
 // Device address of the scratch array on the current device, looked up once
-// per device (with that device current) and cached.
+// per device (with that device current) and cached for the life of the
+// process.  The cache does not survive cudaDeviceReset (which also ends every
+// context of this library on that device).
 status_t scratch_on_current_device(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -84,6 +87,23 @@ status_t scratch_on_current_device(float** out) {
 }
 
 }  // namespace
+
+// Loads everything the entry point touches on the current device: the scratch
+// array's address (which brings the library's device image, and with it the
+// array, onto the device under lazy module loading), the anchor-max kernel and
+// the top-k kernel with its shared-memory attribute.  yb_cuda_init calls this,
+// so a process that creates a context on a device before its pool allocator
+// reserves the remaining memory has nothing left to load on the first call.
+status_t noalloc_prepare_current_device() {
+  float* p = nullptr;
+  status_t st = scratch_on_current_device(&p);
+  if (st != SUCCESS) return st;
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, anchor_max_kernel);
+  if (e != cudaSuccess) return cuda_status(e, "anchor_max_kernel attributes");
+  return cuda_status(prepare_topk(), "topk_kernel attributes");
+}
+
 }  // namespace yb
 
 using namespace yb;

@@ -26,6 +26,10 @@ const char* last_error();
 // Maps a CUDA error to status_t, recording `what` and the CUDA message.
 status_t cuda_status(cudaError_t e, const char* what);
 
+// Loads the no-allocation top-k's scratch array and kernels on the current
+// device (noalloc.cu); called by yb_cuda_init.
+status_t noalloc_prepare_current_device();
+
 // RAII device allocation.
 struct DevMem {
   void* p = nullptr;

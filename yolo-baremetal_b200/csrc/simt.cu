@@ -531,20 +531,48 @@ __global__ void gather_concat_kernel(SView s0, int c0, int up0, SView s1, int c1
   out.hi[o + out.plane] = src[i + pl];
 }
 
-__global__ void silu_kernel(SOut t, int B, int HW, int C) {
-  pdl_wait();
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(B) * HW * C;
-  if (idx >= total) return;
-  const int c = static_cast<int>(idx % C);
-  const long long pix = idx / C;
-  const int b = static_cast<int>(pix / HW);
-  const long long p = pix - static_cast<long long>(b) * HW;
-  const long long o = vaddr(t, b, p) + c;
-  uint32_t hi, lo;
-  split1(silu(join1(t.hi[o], t.hi[o + t.plane])), hi, lo);
-  t.hi[o] = static_cast<uint16_t>(hi);
-  t.hi[o + t.plane] = static_cast<uint16_t>(lo);
+// Standalone layers.h element-wise and copy operations on plain fp32 NCHW
+// tensors (the host tensors' own layout, all images): silu_forward
+// (layers.c:10-21), pool2d_max_forward (layers.c:191-217) and
+// upsample_nearest_forward (layers.c:23-39).  Pooling and upsampling copy
+// values, so they are exact; SiLU is x / (1 + expf(-x)) in fp32.
+__global__ void silu_f32_kernel(float* __restrict__ x, long long n) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) x[i] = silu(x[i]);
+}
+
+__global__ void maxpool_nchw_kernel(const float* __restrict__ in, long long planes, int H, int W, int k, int stride,
+                                    int Ho, int Wo, float* __restrict__ out) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= planes * Ho * Wo) return;
+  const int ox = static_cast<int>(i % Wo);
+  const int oy = static_cast<int>((i / Wo) % Ho);
+  const long long pl = i / (static_cast<long long>(Wo) * Ho);
+  const float* src = in + pl * H * W;
+  const int pad = k / 2;
+  float m = -FLT_MAX;
+  for (int ky = 0; ky < k; ++ky) {
+    const int iy = oy * stride - pad + ky;
+    if (iy < 0 || iy >= H) continue;
+    for (int kx = 0; kx < k; ++kx) {
+      const int ix = ox * stride - pad + kx;
+      if (ix < 0 || ix >= W) continue;
+      const float v = src[static_cast<long long>(iy) * W + ix];
+      if (v > m) m = v;
+    }
+  }
+  out[i] = m;
+}
+
+__global__ void upsample_nchw_kernel(const float* __restrict__ in, long long planes, int H, int W, int scale,
+                                     float* __restrict__ out) {
+  const int Ho = H * scale, Wo = W * scale;
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= planes * Ho * Wo) return;
+  const int ox = static_cast<int>(i % Wo);
+  const int oy = static_cast<int>((i / Wo) % Ho);
+  const long long pl = i / (static_cast<long long>(Wo) * Ho);
+  out[i] = in[(pl * H + oy / scale) * W + ox / scale];
 }
 
 }  // namespace
@@ -663,9 +691,25 @@ cudaError_t launch_gather_concat(SView src0, int c0, int up0, SView src1, int c1
   return cudaGetLastError();
 }
 
-cudaError_t launch_silu(SOut t, int B, int HW, int C, cudaStream_t s) {
-  const long long total = static_cast<long long>(B) * HW * C;
-  silu_kernel<<<blocks_for(total, 256), 256, 0, s>>>(t, B, HW, C);
+cudaError_t launch_silu_f32(float* x, long long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  silu_f32_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_maxpool_nchw(const float* in, long long planes, int H, int W, int k, int stride, int Ho, int Wo,
+                                float* out, cudaStream_t s) {
+  const long long total = planes * Ho * Wo;
+  if (total <= 0) return cudaSuccess;
+  maxpool_nchw_kernel<<<blocks_for(total, 256), 256, 0, s>>>(in, planes, H, W, k, stride, Ho, Wo, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_upsample_nchw(const float* in, long long planes, int H, int W, int scale, float* out,
+                                 cudaStream_t s) {
+  const long long total = planes * H * scale * W * scale;
+  if (total <= 0) return cudaSuccess;
+  upsample_nchw_kernel<<<blocks_for(total, 256), 256, 0, s>>>(in, planes, H, W, scale, out);
   return cudaGetLastError();
 }
 

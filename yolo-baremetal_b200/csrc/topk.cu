@@ -289,15 +289,20 @@ __global__ void __launch_bounds__(kT) topk_kernel(const TopkArgs a) {
 
 }  // namespace
 
+namespace {
+constexpr int kTopkSmem = kCache * 4 + kCand * 8;
+std::atomic<uint64_t> g_topk_attr_done{0};
+}  // namespace
+
+cudaError_t prepare_topk() { return smem_attr_once(topk_kernel, kTopkSmem, g_topk_attr_done); }
+
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t s) {
   int k = a.max_det < a.N ? a.max_det : a.N;
   if (k > a.cap) k = a.cap;
   if (k > kTopkMax || a.B <= 0) return cudaErrorInvalidValue;
-  constexpr int kSmem = kCache * 4 + kCand * 8;
-  static std::atomic<uint64_t> attr_done{0};
-  const cudaError_t e = smem_attr_once(topk_kernel, kSmem, attr_done);
+  const cudaError_t e = prepare_topk();
   if (e != cudaSuccess) return e;
-  return launch_pdl(topk_kernel, dim3(a.B), dim3(kT), kSmem, s, a);
+  return launch_pdl(topk_kernel, dim3(a.B), dim3(kT), kTopkSmem, s, a);
 }
 
 }  // namespace yb

@@ -43,7 +43,8 @@ EXPORTS = {
                   "yb_cuda_get_detections", "yb_cuda_detections",
                   "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_detect_topk_noalloc",
                   "yb_cuda_forward_sharded",
-                  "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error"],
+                  "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error",
+                  "yb_conv_create", "yb_conv_ci_pad", "yb_conv_run", "yb_conv_check", "yb_conv_destroy"],
     "yb_int8.h": ["yb_int8_quantize_conv", "yb_int8_conv_create", "yb_int8_conv_ci_pad", "yb_int8_conv_run",
                   "yb_int8_conv_check", "yb_int8_conv_destroy"],
 }
@@ -114,6 +115,12 @@ def lib() -> C.CDLL:
         L.yb_cuda_profile_ops.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                           C.c_int, C.POINTER(C.c_int)]
         L.yb_cuda_destroy.argtypes = [C.c_void_p]
+        L.yb_conv_create.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_int, C.c_int, C.POINTER(C.c_void_p)]
+        L.yb_conv_ci_pad.argtypes = [C.c_void_p]
+        L.yb_conv_run.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.yb_conv_check.argtypes = [C.c_void_p]
+        L.yb_conv_destroy.argtypes = [C.c_void_p]
         L.yb_cuda_set_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         L.yb_cuda_get_detections.argtypes = [C.c_void_p, C.c_float, C.c_int, C.c_void_p, C.c_void_p]
         L.yb_cuda_detections.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p, C.c_void_p,
