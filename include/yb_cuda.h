@@ -104,6 +104,34 @@ status_t yb_cuda_get_int8_stage(void* ctx, int idx, int image, signed char* out_
  * folds BatchNorm like model_load_weights and uploads. */
 status_t yb_cuda_load_bin(void* ctx, const char* path);
 
+/* Device-side weight preparation.  yb_cuda_load_bin_device takes the same
+ * converter .bin (converter.py:116-131) but folds BatchNorm on the GPU
+ * (the rule of utils.c:81-106 / model.c:121-180, explicitly rounded, so the
+ * folded values equal the host fold bit for bit); every later packing of
+ * the weights (FP32 tcgen05 operand images, INT8 quantisation and layouts)
+ * then also runs as GPU kernels.  The host reads the file and keeps only
+ * names and shapes.
+ *
+ * yb_cuda_save_prepared writes a prepared-weight blob: the folded weights
+ * and the packed FP32 operand image of every convolution.
+ * yb_cuda_load_prepared restores a context from such a blob with one copy
+ * of the folded weights and one of each packed image, without folding or
+ * packing (fast start).  ERROR_INVALID_FORMAT for a file that is not a blob
+ * of this version.
+ *
+ * yb_cuda_weight_image copies one prepared weight image to host memory:
+ * kind 0 the folded fp32 tensor `name`; kind 1 the packed FP32 operand image
+ * of convolution prefix `name` (e.g. "model.2.cv1") in n_tile-wide N tiles
+ * (0 = the full tiling, else 64 or 128); kind 2 the packed INT8 operand image
+ * of convolution prefix `name` in the last INT8 plan built.  *bytes receives
+ * the size; out may be NULL to query it.  Either preparation path (host or
+ * device) answers, so the two can be compared. */
+status_t yb_cuda_load_bin_device(void* ctx, const char* path);
+status_t yb_cuda_save_prepared(void* ctx, const char* path);
+status_t yb_cuda_load_prepared(void* ctx, const char* path);
+status_t yb_cuda_weight_image(void* ctx, const char* name, int kind, int n_tile, void* out, size_t cap,
+                              size_t* bytes);
+
 /* Forward on host buffers: in_nchw [B,3,H,W] float32 (H, W multiples of 32),
  * out_dets [B,max_det,6] float32.  The input is copied to HBM, the captured
  * graph for (B,H,W) runs, and the detections come back; the call returns

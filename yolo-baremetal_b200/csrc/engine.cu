@@ -1,5 +1,6 @@
 // Lowering of the YOLO26 graph to sm_100a kernel launches (see engine.h).
 #include "engine.h"
+#include "weight_prep.h"
 
 #include <cmath>
 #include <cstdio>
@@ -174,6 +175,7 @@ Engine::~Engine() {
 }
 
 void Engine::release_plan(Plan* p) {
+  if (p->int8) i8_images_.clear();  // they may point into this plan's buffers
   if (p->graph) cudaGraphExecDestroy(p->graph);
   p->graph = nullptr;
   for (void* q : p->allocs) cudaFree(q);
@@ -199,7 +201,16 @@ const HostTensor* Engine::find(const std::string& name) const {
   return it == hw_.end() ? nullptr : &it->second;
 }
 
-cudaError_t Engine::set_weights(WeightMap&& w, int num_classes, std::string* why) {
+namespace {
+// Copies `n` floats of a weight tensor (host values or device values) into
+// device memory at dst.
+cudaError_t tensor_to_device(const HostTensor& t, float* dst, size_t n) {
+  if (t.dev) return cudaMemcpy(dst, t.dev, n * 4, cudaMemcpyDeviceToDevice);
+  return cudaMemcpy(dst, t.data.data(), n * 4, cudaMemcpyHostToDevice);
+}
+}  // namespace
+
+void Engine::reset_weights() {
   cudaSetDevice(device_);
   for (auto& p : plans_) release_plan(p.get());
   plans_.clear();
@@ -207,9 +218,12 @@ cudaError_t Engine::set_weights(WeightMap&& w, int num_classes, std::string* why
   weight_allocs_.clear();
   convs_.clear();
   dws_.clear();
+  i8_images_.clear();
   stem_ = DevStem();
-  hw_ = std::move(w);
-  nc_ = num_classes;
+  dev_arena_ = nullptr;
+}
+
+cudaError_t Engine::setup_stem() {
   const HostTensor* sw = find("model.0.conv.weight");
   const HostTensor* sb = find("model.0.conv.bias");
   // Any weight file loads, as in the reference (model.c:182-198); a missing
@@ -218,12 +232,95 @@ cudaError_t Engine::set_weights(WeightMap&& w, int num_classes, std::string* why
   stem_.co = sw->dims[0];
   stem_.ci = sw->dims[1];
   stem_.k = sw->dims[2];
-  cudaError_t e = dev_alloc(sw->data.size() * 4, reinterpret_cast<void**>(&stem_.w));
+  cudaError_t e = dev_alloc(sw->count() * 4, reinterpret_cast<void**>(&stem_.w));
   if (e != cudaSuccess) return e;
-  e = dev_alloc(sb->data.size() * 4, reinterpret_cast<void**>(&stem_.bias));
+  e = dev_alloc(sb->count() * 4, reinterpret_cast<void**>(&stem_.bias));
   if (e != cudaSuccess) return e;
-  cudaMemcpy(stem_.w, sw->data.data(), sw->data.size() * 4, cudaMemcpyHostToDevice);
-  return cudaMemcpy(stem_.bias, sb->data.data(), sb->data.size() * 4, cudaMemcpyHostToDevice);
+  e = tensor_to_device(*sw, stem_.w, sw->count());
+  if (e != cudaSuccess) return e;
+  return tensor_to_device(*sb, stem_.bias, sb->count());
+}
+
+cudaError_t Engine::set_weights(WeightMap&& w, int num_classes, std::string* why) {
+  (void)why;
+  reset_weights();
+  hw_ = std::move(w);
+  nc_ = num_classes;
+  return setup_stem();
+}
+
+cudaError_t Engine::set_weights_device(WeightMap&& raw, int num_classes, std::string* why) {
+  reset_weights();
+  hw_.clear();
+  nc_ = num_classes;
+  // Convolutions with BatchNorm records, and the zero biases the fold
+  // creates where a convolution has none (fold_all_bn_map's rule).
+  std::vector<std::string> folds;
+  for (const auto& kv : raw) {
+    if (!ends_with(kv.first, ".conv.weight")) continue;
+    const std::string p = kv.first.substr(0, kv.first.size() - std::strlen(".conv.weight"));
+    if (!raw.count(p + ".bn.weight") || !raw.count(p + ".bn.bias") || !raw.count(p + ".bn.running_mean") ||
+        !raw.count(p + ".bn.running_var"))
+      continue;
+    folds.push_back(p);
+  }
+  for (const std::string& p : folds) {
+    if (raw.count(p + ".conv.bias")) continue;
+    HostTensor b;
+    b.ndim = 4;
+    b.dims[1] = raw[p + ".conv.weight"].dims[0];
+    b.data.assign(static_cast<size_t>(b.dims[1]), 0.0f);
+    raw[p + ".conv.bias"] = std::move(b);
+  }
+  // One arena, every tensor at a 64-byte aligned offset, filled by one copy.
+  std::map<std::string, long long> off;
+  long long total = 0;
+  for (const auto& kv : raw) {
+    off[kv.first] = total;
+    total += (static_cast<long long>(kv.second.data.size()) + 15) / 16 * 16;
+  }
+  std::vector<float> stage(static_cast<size_t>(total > 0 ? total : 1), 0.0f);
+  for (const auto& kv : raw) std::copy(kv.second.data.begin(), kv.second.data.end(), stage.begin() + off[kv.first]);
+  cudaError_t e = dev_alloc(stage.size() * 4, reinterpret_cast<void**>(&dev_arena_));
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpy(dev_arena_, stage.data(), stage.size() * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return e;
+  std::vector<FoldDesc> fd;
+  for (const std::string& p : folds) {
+    FoldDesc d;
+    const HostTensor& w = raw[p + ".conv.weight"];
+    d.w = off[p + ".conv.weight"];
+    d.b = off[p + ".conv.bias"];
+    d.g = off[p + ".bn.weight"];
+    d.be = off[p + ".bn.bias"];
+    d.mu = off[p + ".bn.running_mean"];
+    d.var = off[p + ".bn.running_var"];
+    d.oc = w.dims[0];
+    d.per = static_cast<int>(w.data.size() / static_cast<size_t>(d.oc));
+    fd.push_back(d);
+  }
+  if (!fd.empty()) {
+    FoldDesc* d_fd = nullptr;
+    e = cudaMalloc(&d_fd, fd.size() * sizeof(FoldDesc));
+    if (e == cudaSuccess) e = cudaMemcpy(d_fd, fd.data(), fd.size() * sizeof(FoldDesc), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = launch_fold_bn(d_fd, static_cast<int>(fd.size()), dev_arena_, stream_);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+    if (d_fd) cudaFree(d_fd);
+    if (e != cudaSuccess) return e;
+  }
+  const char* sfx[5] = {".bn.weight", ".bn.bias", ".bn.running_mean", ".bn.running_var", ".bn.num_batches_tracked"};
+  for (const std::string& p : folds)
+    for (const char* x : sfx) raw.erase(p + x);
+  for (auto& kv : raw) {
+    HostTensor t;
+    t.ndim = kv.second.ndim;
+    for (int i = 0; i < 4; ++i) t.dims[i] = kv.second.dims[i];
+    t.n = kv.second.data.size();
+    t.dev = dev_arena_ + off[kv.first];
+    hw_[kv.first] = std::move(t);
+  }
+  (void)why;
+  return setup_stem();
 }
 
 cudaError_t Engine::conv_w(const std::string& prefix, bool plain, DevConv** out, std::string* why) {
@@ -246,24 +343,29 @@ cudaError_t Engine::conv_w(const std::string& prefix, bool plain, DevConv** out,
   d.ci = w->dims[1];
   d.kh = w->dims[2];
   d.kw = w->dims[3];
-  if (d.ci % 8 || d.co % 4 || static_cast<int>(b->data.size()) != d.co) {
+  if (d.ci % 8 || d.co % 4 || static_cast<int>(b->count()) != d.co) {
     *why = "unsupported conv shape at " + prefix;
     return cudaErrorInvalidValue;
   }
   d.K = d.kh * d.kw * d.ci;
   d.num_kc = (d.K + 63) / 64;
   choose_n_tiling(d.co, &d.n_tile, &d.n_tiles);
-  const size_t bytes = pack_conv_weights(w->data.data(), d.co, d.ci, d.kh, d.kw, d.n_tile, nullptr);
-  std::vector<uint8_t> pack(bytes);
-  pack_conv_weights(w->data.data(), d.co, d.ci, d.kh, d.kw, d.n_tile, pack.data());
+  const size_t bytes = pack_conv_weights(nullptr, d.co, d.ci, d.kh, d.kw, d.n_tile, nullptr);
   cudaError_t e = dev_alloc(bytes, reinterpret_cast<void**>(&d.wpack));
   if (e != cudaSuccess) return e;
-  e = cudaMemcpy(d.wpack, pack.data(), bytes, cudaMemcpyHostToDevice);
+  if (w->dev) {
+    e = launch_pack_conv(w->dev, d.co, d.ci, d.kh, d.kw, d.n_tile, d.wpack, bytes, stream_);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+  } else {
+    std::vector<uint8_t> pack(bytes);
+    pack_conv_weights(w->data.data(), d.co, d.ci, d.kh, d.kw, d.n_tile, pack.data());
+    e = cudaMemcpy(d.wpack, pack.data(), bytes, cudaMemcpyHostToDevice);
+  }
   if (e != cudaSuccess) return e;
   e = dev_alloc(static_cast<size_t>(d.n_tile) * d.n_tiles * 4, reinterpret_cast<void**>(&d.bias));
   if (e != cudaSuccess) return e;
   cudaMemset(d.bias, 0, static_cast<size_t>(d.n_tile) * d.n_tiles * 4);
-  e = cudaMemcpy(d.bias, b->data.data(), b->data.size() * 4, cudaMemcpyHostToDevice);
+  e = tensor_to_device(*b, d.bias, b->count());
   if (e != cudaSuccess) return e;
   auto ins = convs_.emplace(prefix, d);
   *out = &ins.first->second;
@@ -276,16 +378,233 @@ cudaError_t Engine::conv_narrow(DevConv* d, int n_tile, const uint8_t** wpack) {
     const std::string wn = d->name + (find(d->name + ".conv.weight") ? ".conv.weight" : ".weight");
     const HostTensor* w = find(wn);
     if (!w) return cudaErrorInvalidValue;
-    const size_t bytes = pack_conv_weights(w->data.data(), d->co, d->ci, d->kh, d->kw, n_tile, nullptr);
-    std::vector<uint8_t> pack(bytes);
-    pack_conv_weights(w->data.data(), d->co, d->ci, d->kh, d->kw, n_tile, pack.data());
+    const size_t bytes = pack_conv_weights(nullptr, d->co, d->ci, d->kh, d->kw, n_tile, nullptr);
     cudaError_t e = dev_alloc(bytes, reinterpret_cast<void**>(&d->wpack_n[slot]));
     if (e != cudaSuccess) return e;
-    e = cudaMemcpy(d->wpack_n[slot], pack.data(), bytes, cudaMemcpyHostToDevice);
+    if (w->dev) {
+      e = launch_pack_conv(w->dev, d->co, d->ci, d->kh, d->kw, n_tile, d->wpack_n[slot], bytes, stream_);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+    } else {
+      std::vector<uint8_t> pack(bytes);
+      pack_conv_weights(w->data.data(), d->co, d->ci, d->kh, d->kw, n_tile, pack.data());
+      e = cudaMemcpy(d->wpack_n[slot], pack.data(), bytes, cudaMemcpyHostToDevice);
+    }
     if (e != cudaSuccess) return e;
   }
   *wpack = d->wpack_n[slot];
   return cudaSuccess;
+}
+
+// ------------------------------------------------------ prepared-weight blob
+namespace {
+constexpr char kBlobMagic[8] = {'Y', 'B', '2', '6', 'P', 'R', 'E', 'P'};
+constexpr int32_t kBlobVersion = 1;
+
+// Convolution prefixes of a weight map, with whether they are plain (P.weight)
+// rather than Conv+BN (P.conv.weight): every 4-D, non-depthwise weight.
+std::vector<std::pair<std::string, bool>> conv_prefixes(const WeightMap& w) {
+  std::vector<std::pair<std::string, bool>> out;
+  for (const auto& kv : w) {
+    const HostTensor& t = kv.second;
+    if (t.ndim != 4 || t.dims[1] == 1) continue;
+    if (ends_with(kv.first, ".conv.weight"))
+      out.emplace_back(kv.first.substr(0, kv.first.size() - std::strlen(".conv.weight")), false);
+    else if (ends_with(kv.first, ".weight") && !ends_with(kv.first, ".bn.weight"))
+      out.emplace_back(kv.first.substr(0, kv.first.size() - std::strlen(".weight")), true);
+  }
+  return out;
+}
+
+bool put(FILE* f, const void* p, size_t n) { return std::fwrite(p, 1, n, f) == n; }
+bool get(FILE* f, void* p, size_t n) { return std::fread(p, 1, n, f) == n; }
+
+bool put_name(FILE* f, const std::string& s) {
+  const int32_t n = static_cast<int32_t>(s.size());
+  return put(f, &n, 4) && put(f, s.data(), s.size());
+}
+bool get_name(FILE* f, std::string* s) {
+  int32_t n = 0;
+  if (!get(f, &n, 4) || n < 0 || n > 4096) return false;
+  s->resize(static_cast<size_t>(n));
+  return get(f, &(*s)[0], static_cast<size_t>(n));
+}
+}  // namespace
+
+cudaError_t Engine::save_blob(const std::string& path, std::string* why) {
+  cudaSetDevice(device_);
+  // Every convolution the graph can use, packed in its full N tiling.
+  std::vector<std::pair<std::string, DevConv*>> images;
+  for (const auto& pc : conv_prefixes(hw_)) {
+    DevConv* d = nullptr;
+    std::string w2;
+    if (conv_w(pc.first, pc.second, &d, &w2) == cudaSuccess) images.emplace_back(pc.first, d);
+  }
+  FILE* f = std::fopen(path.c_str(), "wb");
+  if (!f) {
+    *why = "cannot write " + path;
+    return cudaErrorInvalidValue;
+  }
+  bool ok = put(f, kBlobMagic, 8) && put(f, &kBlobVersion, 4) && put(f, &nc_, 4);
+  const int32_t nt = static_cast<int32_t>(hw_.size()), ni = static_cast<int32_t>(images.size());
+  ok = ok && put(f, &nt, 4) && put(f, &ni, 4);
+  std::vector<float> buf;
+  cudaError_t e = cudaSuccess;
+  for (const auto& kv : hw_) {
+    if (!ok) break;
+    const HostTensor& t = kv.second;
+    const int64_t n = static_cast<int64_t>(t.count());
+    buf.resize(static_cast<size_t>(n));
+    if (t.dev) e = cudaMemcpy(buf.data(), t.dev, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost);
+    else std::copy(t.data.begin(), t.data.end(), buf.begin());
+    if (e != cudaSuccess) break;
+    ok = put_name(f, kv.first) && put(f, &t.ndim, 4) && put(f, t.dims, 16) && put(f, &n, 8) &&
+         put(f, buf.data(), static_cast<size_t>(n) * 4);
+  }
+  std::vector<uint8_t> img;
+  for (const auto& im : images) {
+    if (!ok || e != cudaSuccess) break;
+    const DevConv& d = *im.second;
+    const int64_t bytes = static_cast<int64_t>(pack_conv_weights(nullptr, d.co, d.ci, d.kh, d.kw, d.n_tile, nullptr));
+    img.resize(static_cast<size_t>(bytes));
+    e = cudaMemcpy(img.data(), d.wpack, static_cast<size_t>(bytes), cudaMemcpyDeviceToHost);
+    const int32_t hdr[5] = {d.co, d.ci, d.kh, d.kw, d.n_tile};
+    ok = e == cudaSuccess && put_name(f, im.first) && put(f, hdr, 20) && put(f, &bytes, 8) &&
+         put(f, img.data(), img.size());
+  }
+  std::fclose(f);
+  if (e != cudaSuccess) return e;
+  if (!ok) {
+    *why = "short write to " + path;
+    return cudaErrorInvalidValue;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t Engine::load_blob(const std::string& path, int* num_classes, std::string* why) {
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) {
+    *why = "cannot open " + path;
+    return cudaErrorInvalidValue;
+  }
+  char magic[8];
+  int32_t ver = 0, nc = 0, nt = 0, ni = 0;
+  bool ok = get(f, magic, 8) && std::memcmp(magic, kBlobMagic, 8) == 0 && get(f, &ver, 4) && ver == kBlobVersion &&
+            get(f, &nc, 4) && get(f, &nt, 4) && get(f, &ni, 4) && nt >= 0 && ni >= 0;
+  WeightMap raw;
+  for (int i = 0; ok && i < nt; ++i) {
+    std::string name;
+    HostTensor t;
+    int64_t n = 0;
+    ok = get_name(f, &name) && get(f, &t.ndim, 4) && get(f, t.dims, 16) && get(f, &n, 8) && n >= 0 &&
+         n < (int64_t{1} << 32);
+    if (!ok) break;
+    t.data.resize(static_cast<size_t>(n));
+    ok = get(f, t.data.data(), static_cast<size_t>(n) * 4);
+    raw[name] = std::move(t);
+  }
+  struct Img {
+    std::string name;
+    int32_t hdr[5];
+    std::vector<uint8_t> bytes;
+  };
+  std::vector<Img> imgs(static_cast<size_t>(ok ? ni : 0));
+  for (auto& im : imgs) {
+    int64_t bytes = 0;
+    ok = ok && get_name(f, &im.name) && get(f, im.hdr, 20) && get(f, &bytes, 8) && bytes > 0 &&
+         bytes < (int64_t{1} << 31);
+    if (!ok) break;
+    im.bytes.resize(static_cast<size_t>(bytes));
+    ok = get(f, im.bytes.data(), im.bytes.size());
+  }
+  std::fclose(f);
+  if (!ok) {
+    *why = "not a prepared-weight blob (or truncated): " + path;
+    return cudaErrorInvalidValue;
+  }
+  // The folded tensors: one arena, one copy (no BatchNorm records remain, so
+  // set_weights_device folds nothing).
+  cudaError_t e = set_weights_device(std::move(raw), nc, why);
+  if (e != cudaSuccess) return e;
+  *num_classes = nc;
+  for (const Img& im : imgs) {
+    const bool plain = !find(im.name + ".conv.weight");
+    const HostTensor* w = find(im.name + (plain ? ".weight" : ".conv.weight"));
+    const HostTensor* b = find(im.name + (plain ? ".bias" : ".conv.bias"));
+    DevConv d;
+    d.name = im.name;
+    d.co = im.hdr[0];
+    d.ci = im.hdr[1];
+    d.kh = im.hdr[2];
+    d.kw = im.hdr[3];
+    d.K = d.kh * d.kw * d.ci;
+    d.num_kc = (d.K + 63) / 64;
+    choose_n_tiling(d.co, &d.n_tile, &d.n_tiles);
+    if (!w || !b || w->dims[0] != d.co || w->dims[1] != d.ci || d.n_tile != im.hdr[4] ||
+        im.bytes.size() != pack_conv_weights(nullptr, d.co, d.ci, d.kh, d.kw, d.n_tile, nullptr)) {
+      *why = "prepared-weight blob does not match its tensors at " + im.name;
+      return cudaErrorInvalidValue;
+    }
+    e = dev_alloc(im.bytes.size(), reinterpret_cast<void**>(&d.wpack));
+    if (e == cudaSuccess) e = cudaMemcpy(d.wpack, im.bytes.data(), im.bytes.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = dev_alloc(static_cast<size_t>(d.n_tile) * d.n_tiles * 4, reinterpret_cast<void**>(&d.bias));
+    if (e == cudaSuccess) e = cudaMemset(d.bias, 0, static_cast<size_t>(d.n_tile) * d.n_tiles * 4);
+    if (e == cudaSuccess) e = tensor_to_device(*b, d.bias, b->count());
+    if (e != cudaSuccess) return e;
+    convs_.emplace(im.name, d);
+  }
+  return cudaSuccess;
+}
+
+cudaError_t Engine::weight_image(const std::string& name, int kind, int n_tile, std::vector<uint8_t>* out,
+                                 std::string* why) {
+  cudaSetDevice(device_);
+  const void* src = nullptr;
+  size_t bytes = 0;
+  bool on_device = true;
+  if (kind == 0) {
+    const HostTensor* t = find(name);
+    if (!t) {
+      *why = "no tensor " + name;
+      return cudaErrorInvalidValue;
+    }
+    bytes = t->count() * 4;
+    src = t->dev ? static_cast<const void*>(t->dev) : static_cast<const void*>(t->data.data());
+    on_device = t->dev != nullptr;
+  } else if (kind == 1) {
+    const bool plain = !find(name + ".conv.weight");
+    DevConv* d = nullptr;
+    cudaError_t e = conv_w(name, plain, &d, why);
+    if (e != cudaSuccess) return e;
+    const uint8_t* p = d->wpack;
+    int nt = d->n_tile;
+    if (n_tile != 0 && n_tile != d->n_tile) {
+      if (n_tile != 64 && n_tile != 128) {
+        *why = "n_tile must be 0 (full tiling), 64 or 128";
+        return cudaErrorInvalidValue;
+      }
+      if ((e = conv_narrow(d, n_tile, &p)) != cudaSuccess) return e;
+      nt = n_tile;
+    }
+    src = p;
+    bytes = pack_conv_weights(nullptr, d->co, d->ci, d->kh, d->kw, nt, nullptr);
+  } else if (kind == 2) {
+    auto it = i8_images_.find(name);
+    if (it == i8_images_.end()) {
+      *why = "no INT8 operand image of " + name + " (build an INT8 plan first)";
+      return cudaErrorInvalidValue;
+    }
+    src = it->second.first;
+    bytes = it->second.second;
+  } else {
+    *why = "kind must be 0, 1 or 2";
+    return cudaErrorInvalidValue;
+  }
+  out->resize(bytes);
+  if (!on_device) {
+    std::memcpy(out->data(), src, bytes);
+    return cudaSuccess;
+  }
+  return cudaMemcpy(out->data(), src, bytes, cudaMemcpyDeviceToHost);
 }
 
 cudaError_t Engine::dw_w(const std::string& prefix, DevDw** out, std::string* why) {
@@ -302,15 +621,21 @@ cudaError_t Engine::dw_w(const std::string& prefix, DevDw** out, std::string* wh
   }
   DevDw d;
   d.c = w->dims[0];
-  std::vector<float> t(static_cast<size_t>(9) * d.c);
-  for (int c = 0; c < d.c; ++c)
-    for (int k = 0; k < 9; ++k) t[static_cast<size_t>(k) * d.c + c] = w->data[static_cast<size_t>(c) * 9 + k];
-  cudaError_t e = dev_alloc(t.size() * 4, reinterpret_cast<void**>(&d.w));
+  cudaError_t e = dev_alloc(static_cast<size_t>(9) * d.c * 4, reinterpret_cast<void**>(&d.w));
   if (e != cudaSuccess) return e;
-  cudaMemcpy(d.w, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+  if (w->dev) {
+    e = launch_taps_transpose(w->dev, d.c, d.w, stream_);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+  } else {
+    std::vector<float> t(static_cast<size_t>(9) * d.c);
+    for (int c = 0; c < d.c; ++c)
+      for (int k = 0; k < 9; ++k) t[static_cast<size_t>(k) * d.c + c] = w->data[static_cast<size_t>(c) * 9 + k];
+    e = cudaMemcpy(d.w, t.data(), t.size() * 4, cudaMemcpyHostToDevice);
+  }
+  if (e != cudaSuccess) return e;
   e = dev_alloc(static_cast<size_t>(d.c) * 4, reinterpret_cast<void**>(&d.bias));
   if (e != cudaSuccess) return e;
-  e = cudaMemcpy(d.bias, b->data.data(), static_cast<size_t>(d.c) * 4, cudaMemcpyHostToDevice);
+  e = tensor_to_device(*b, d.bias, static_cast<size_t>(d.c));
   if (e != cudaSuccess) return e;
   auto ins = dws_.emplace(prefix, d);
   *out = &ins.first->second;

@@ -21,7 +21,10 @@ namespace yb {
 struct HostTensor {
   int dims[4] = {1, 1, 1, 1};
   int ndim = 0;
-  std::vector<float> data;
+  std::vector<float> data;  // host values (empty when the values live on the device)
+  float* dev = nullptr;     // device values (device weight preparation), else null
+  size_t n = 0;             // element count when `data` is empty
+  size_t count() const { return dev ? n : data.size(); }
 };
 using WeightMap = std::map<std::string, HostTensor>;
 
@@ -118,6 +121,23 @@ class Engine {
 
   // Takes BN-folded host weights (names as written by the converter).
   cudaError_t set_weights(WeightMap&& w, int num_classes, std::string* why);
+  // Device weight preparation: takes the converter's raw (unfolded) records,
+  // uploads them in one copy and folds BatchNorm on the device; every later
+  // packing (FP32 operand images, INT8 quantisation and layouts) then runs
+  // as kernels on the device values.  The host keeps only names and shapes.
+  cudaError_t set_weights_device(WeightMap&& raw, int num_classes, std::string* why);
+  bool device_prep() const { return dev_arena_ != nullptr; }
+  // Prepared-weight blob: the folded weights and the packed FP32 operand
+  // image (full N tiling) of every convolution, written from device memory;
+  // load_blob restores both without folding or packing.
+  cudaError_t save_blob(const std::string& path, std::string* why);
+  cudaError_t load_blob(const std::string& path, int* num_classes, std::string* why);
+  // Test access: kind 0 = the folded fp32 tensor `name`; kind 1 = the packed
+  // FP32 operand image of convolution prefix `name` in n_tile-wide N tiles
+  // (0: the full tiling); kind 2 = the packed INT8 operand image of
+  // convolution `name` in the last-built INT8 plan.
+  cudaError_t weight_image(const std::string& name, int kind, int n_tile, std::vector<uint8_t>* out,
+                           std::string* why);
   bool has_weights() const { return !hw_.empty(); }
 
   // Plan for (B, H, W, max_det), built and captured on first use.  Plans with
@@ -160,6 +180,8 @@ class Engine {
   cudaError_t conv_narrow(DevConv* d, int n_tile, const uint8_t** wpack);
   cudaError_t dw_w(const std::string& prefix, DevDw** out, std::string* why);
   cudaError_t dev_alloc(size_t bytes, void** p);
+  void reset_weights();
+  cudaError_t setup_stem();
   cudaError_t build(Plan* p, std::string* why);
   cudaError_t build_i8(Plan* p, std::string* why);
   void release_plan(Plan* p);
@@ -176,6 +198,9 @@ class Engine {
   std::vector<void*> weight_allocs_;
   std::vector<std::unique_ptr<Plan>> plans_;
   std::map<std::string, float> i8_scales_;
+  float* dev_arena_ = nullptr;  // folded weights (device preparation)
+  // INT8 packed operand images of the last INT8 plan: prefix -> (ptr, bytes).
+  std::map<std::string, std::pair<const uint8_t*, size_t>> i8_images_;
 };
 
 // Reads the converter's .bin layout (int32 nc, int32 count, records) and folds

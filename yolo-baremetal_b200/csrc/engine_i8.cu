@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "engine.h"
+#include "weight_prep.h"
 #include "i8k.h"
 #include "int8.h"
 #include "kernels.h"
@@ -184,6 +185,63 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     t->base = static_cast<int8_t*>(q);
     return r;
   };
+  // Device weight preparation: quantises w (device values) per output
+  // channel with the same rule as quantize(), into plan-owned device arrays.
+  struct QDev {
+    int8_t* wq = nullptr;
+    int32_t *bq = nullptr, *mult = nullptr, *shift = nullptr;
+    float* deq = nullptr;
+  };
+  auto quantize_dev = [&](const HostTensor& w, const HostTensor* b, const float* cs, int ncs, bool per_out,
+                          double s_t, QDev* q) -> cudaError_t {
+    const int co = w.dims[0], kk = w.dims[2] * w.dims[3];
+    const int per = static_cast<int>(w.count() / static_cast<size_t>(co));
+    void *wq = nullptr, *bq = nullptr, *mu = nullptr, *sh = nullptr, *dq = nullptr, *dcs = nullptr, *bad = nullptr;
+    YB_TRY(dalloc(static_cast<size_t>(co) * per, &wq));
+    YB_TRY(dalloc(static_cast<size_t>(co) * 4, &bq));
+    YB_TRY(dalloc(static_cast<size_t>(co) * 4, &mu));
+    YB_TRY(dalloc(static_cast<size_t>(co) * 4, &sh));
+    YB_TRY(dalloc(static_cast<size_t>(co) * 4, &dq));
+    YB_TRY(upload(cs, static_cast<size_t>(ncs) * 4, &dcs));
+    YB_TRY(dalloc(4, &bad));
+    // dalloc clears on the legacy stream; this plan's stream does not wait
+    // for it, so finish those before the kernel writes.
+    YB_TRY(cudaDeviceSynchronize());
+    QuantArgs qa;
+    qa.w = w.dev;
+    qa.b = b ? b->dev : nullptr;
+    qa.cs = static_cast<const float*>(dcs);
+    qa.co = co;
+    qa.ci = per / kk;
+    qa.kk = kk;
+    qa.per_out = per_out ? 1 : 0;
+    qa.s_t = s_t;
+    qa.wq = static_cast<int8_t*>(wq);
+    qa.bq = static_cast<int32_t*>(bq);
+    qa.mult = static_cast<int32_t*>(mu);
+    qa.shift = static_cast<int32_t*>(sh);
+    qa.deq = static_cast<float*>(dq);
+    qa.bad = static_cast<int*>(bad);
+    YB_TRY(launch_quantize_i8(qa, stream_));
+    int hbad = 0;
+    YB_TRY(cudaMemcpyAsync(&hbad, bad, 4, cudaMemcpyDeviceToHost, stream_));
+    YB_TRY(cudaStreamSynchronize(stream_));
+    if (hbad) return cudaErrorInvalidValue;
+    q->wq = qa.wq;
+    q->bq = qa.bq;
+    q->mult = qa.mult;
+    q->shift = qa.shift;
+    q->deq = qa.deq;
+    return cudaSuccess;
+  };
+  // Copies n device int32 values into a new array of `slots` entries whose
+  // remaining entries hold `fill`.
+  auto padded_i32 = [&](const int32_t* src, int n, int slots, int32_t fill, void** dst) -> cudaError_t {
+    std::vector<int32_t> h(static_cast<size_t>(slots), fill);
+    YB_TRY(upload(h.data(), h.size() * 4, dst));
+    return cudaMemcpy(*dst, src, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToDevice);
+  };
+  i8_images_.clear();
   const int sms = num_sms_;
   int step = 0;  // profile step (model_forward_profile_t index)
   auto add_op = [&](int kind, double flops, double bytes, std::function<cudaError_t(cudaStream_t)> fn) {
@@ -212,9 +270,16 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     if (act && !scale(P + ":pre", &s_pre)) return cudaErrorInvalidValue;
     std::vector<float> cs(ci);
     for (int i = 0; i < ci; ++i) cs[i] = in.scale(i);
+    const double s_t = f32.ptr ? 0.0 : act ? static_cast<double>(s_pre) : static_cast<double>(s_out);
     QWeights q;
-    if (!quantize(*w, b, cs.data(), f32.ptr ? 0.0 : act ? static_cast<double>(s_pre) : static_cast<double>(s_out), &q))
+    QDev qd;
+    if (w->dev) {
+      const cudaError_t r = quantize_dev(*w, b, cs.data(), ci, false, s_t, &qd);
+      if (r == cudaErrorInvalidValue) return fail("int8: requantisation ratio out of range in " + P);
+      YB_TRY(r);
+    } else if (!quantize(*w, b, cs.data(), s_t, &q)) {
       return fail("int8: requantisation ratio out of range in " + P);
+    }
     const int co_pad = round16(co);
     // Padded channels write zeros, so they must land in the tensor's own
     // channel padding, not in a neighbouring concat slice.
@@ -235,24 +300,42 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
         t.n_tiles = (co_pad + nt - 1) / nt;
       }
     }
-    std::vector<int8_t> wpad(static_cast<size_t>(co_pad) * ci * k * k, 0);
-    std::copy(q.wq.begin(), q.wq.end(), wpad.begin());
-    const std::vector<uint8_t> pk = i8_pack_weights(wpad.data(), co_pad, ci, k, k, t);
     const int nq = i8_bias_slots(t);
-    std::vector<int32_t> hb(nq, 0), hm(nq, 0), hs(nq, 1);
-    std::vector<float> hd(nq, 0.f);
-    for (int i = 0; i < co; ++i) {
-      hb[i] = q.bq[i];
-      hm[i] = q.mult[i];
-      hs[i] = q.shift[i];
-      hd[i] = q.deq[i];
-    }
     void *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr, *dd = nullptr, *dl = nullptr;
-    YB_TRY(upload(pk.data(), pk.size(), &dw));
-    YB_TRY(upload(hb.data(), hb.size() * 4, &db));
-    YB_TRY(upload(hm.data(), hm.size() * 4, &dm));
-    YB_TRY(upload(hs.data(), hs.size() * 4, &ds));
-    if (f32.ptr) YB_TRY(upload(hd.data(), hd.size() * 4, &dd));
+    size_t pk_bytes = 0;
+    if (w->dev) {
+      pk_bytes = static_cast<size_t>(t.n_tiles) * t.num_kc * t.n_tile * 128;
+      YB_TRY(dalloc(pk_bytes, &dw));
+      YB_TRY(cudaDeviceSynchronize());
+      YB_TRY(launch_pack_i8(qd.wq, co, ci, k, k, t, static_cast<uint8_t*>(dw), pk_bytes, stream_));
+      YB_TRY(cudaStreamSynchronize(stream_));
+      YB_TRY(padded_i32(qd.bq, co, nq, 0, &db));
+      YB_TRY(padded_i32(qd.mult, co, nq, 0, &dm));
+      YB_TRY(padded_i32(qd.shift, co, nq, 1, &ds));
+      if (f32.ptr) {
+        YB_TRY(dalloc(static_cast<size_t>(nq) * 4, &dd));
+        YB_TRY(cudaMemcpy(dd, qd.deq, static_cast<size_t>(co) * 4, cudaMemcpyDeviceToDevice));
+      }
+    } else {
+      std::vector<int8_t> wpad(static_cast<size_t>(co_pad) * ci * k * k, 0);
+      std::copy(q.wq.begin(), q.wq.end(), wpad.begin());
+      const std::vector<uint8_t> pk = i8_pack_weights(wpad.data(), co_pad, ci, k, k, t);
+      std::vector<int32_t> hb(nq, 0), hm(nq, 0), hs(nq, 1);
+      std::vector<float> hd(nq, 0.f);
+      for (int i = 0; i < co; ++i) {
+        hb[i] = q.bq[i];
+        hm[i] = q.mult[i];
+        hs[i] = q.shift[i];
+        hd[i] = q.deq[i];
+      }
+      pk_bytes = pk.size();
+      YB_TRY(upload(pk.data(), pk.size(), &dw));
+      YB_TRY(upload(hb.data(), hb.size() * 4, &db));
+      YB_TRY(upload(hm.data(), hm.size() * 4, &dm));
+      YB_TRY(upload(hs.data(), hs.size() * 4, &ds));
+      if (f32.ptr) YB_TRY(upload(hd.data(), hd.size() * 4, &dd));
+    }
+    i8_images_[P] = {static_cast<const uint8_t*>(dw), pk_bytes};
     if (act) {
       int8_t lut[256];
       silu_lut(lut, s_pre, s_out);
@@ -319,9 +402,25 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     if (!w || w->dims[0] != C || w->dims[2] != 3 || C % 16) return fail("int8: depthwise " + P);
     float s_out = 0.f, s_pre = 0.f;
     if (!scale(P, &s_out) || !scale(P + ":pre", &s_pre)) return cudaErrorInvalidValue;
+    void *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr, *dl = nullptr;
+    if (w->dev) {
+      std::vector<float> cs(C);
+      for (int c = 0; c < C; ++c) cs[c] = in.scale(c);
+      QDev qd;
+      const cudaError_t r = quantize_dev(*w, b, cs.data(), C, true, s_pre, &qd);
+      if (r == cudaErrorInvalidValue) return fail("int8: depthwise ratio " + P);
+      YB_TRY(r);
+      YB_TRY(dalloc(static_cast<size_t>(3) * C * 4, &dw));
+      YB_TRY(cudaDeviceSynchronize());
+      YB_TRY(launch_pack_dw_i8(qd.wq, C, static_cast<uint32_t*>(dw), stream_));
+      YB_TRY(cudaStreamSynchronize(stream_));
+      db = qd.bq;
+      dm = qd.mult;
+      ds = qd.shift;
+    }
     std::vector<uint32_t> wt(static_cast<size_t>(3) * C, 0u);
     std::vector<int32_t> bq(C), mu(C), sh(C);
-    for (int c = 0; c < C; ++c) {
+    for (int c = 0; c < C && !w->dev; ++c) {
       HostTensor wc;
       wc.dims[0] = 1;
       wc.dims[1] = 1;
@@ -343,11 +442,12 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     }
     int8_t lut[256];
     silu_lut(lut, s_pre, s_out);
-    void *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr, *dl = nullptr;
-    YB_TRY(upload(wt.data(), wt.size() * 4, &dw));
-    YB_TRY(upload(bq.data(), bq.size() * 4, &db));
-    YB_TRY(upload(mu.data(), mu.size() * 4, &dm));
-    YB_TRY(upload(sh.data(), sh.size() * 4, &ds));
+    if (!w->dev) {
+      YB_TRY(upload(wt.data(), wt.size() * 4, &dw));
+      YB_TRY(upload(bq.data(), bq.size() * 4, &db));
+      YB_TRY(upload(mu.data(), mu.size() * 4, &dm));
+      YB_TRY(upload(sh.data(), sh.size() * 4, &ds));
+    }
     YB_TRY(upload(lut, 256, &dl));
     const I8View iv = in.view(), ovw = out.view();
     const int h = in.H, wd = in.W;
@@ -483,7 +583,21 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     std::vector<int8_t> wt(static_cast<size_t>(9) * dim);
     std::vector<int32_t> bq(dim), mu(dim), sh(dim);
     const float sv = static_cast<float>(s_qkv);
-    for (int c = 0; c < dim; ++c) {
+    void *dE = nullptr, *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr;
+    if (pw->dev) {
+      QDev qd;
+      const cudaError_t r = quantize_dev(*pw, pb, &sv, 1, false, static_cast<double>(s_ope), &qd);
+      if (r == cudaErrorInvalidValue) return fail("int8: pe ratio " + P);
+      YB_TRY(r);
+      YB_TRY(dalloc(static_cast<size_t>(9) * dim, &dw));
+      YB_TRY(cudaDeviceSynchronize());
+      YB_TRY(launch_pack_pe_i8(qd.wq, dim, static_cast<int8_t*>(dw), stream_));
+      YB_TRY(cudaStreamSynchronize(stream_));
+      db = qd.bq;
+      dm = qd.mult;
+      ds = qd.shift;
+    }
+    for (int c = 0; c < dim && !pw->dev; ++c) {
       HostTensor wc;
       wc.dims[0] = wc.dims[1] = 1;
       wc.dims[2] = wc.dims[3] = 3;
@@ -498,12 +612,13 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
       mu[c] = q.mult[0];
       sh[c] = q.shift[0];
     }
-    void *dE = nullptr, *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr;
     YB_TRY(upload(E, sizeof E, &dE));
-    YB_TRY(upload(wt.data(), wt.size(), &dw));
-    YB_TRY(upload(bq.data(), bq.size() * 4, &db));
-    YB_TRY(upload(mu.data(), mu.size() * 4, &dm));
-    YB_TRY(upload(sh.data(), sh.size() * 4, &ds));
+    if (!pw->dev) {
+      YB_TRY(upload(wt.data(), wt.size(), &dw));
+      YB_TRY(upload(bq.data(), bq.size() * 4, &db));
+      YB_TRY(upload(mu.data(), mu.size() * 4, &dm));
+      YB_TRY(upload(sh.data(), sh.size() * 4, &ds));
+    }
     aa.E = static_cast<const int32_t*>(dE);
     aa.pe_w = static_cast<const int8_t*>(dw);
     aa.pe_bq = static_cast<const int32_t*>(db);
@@ -606,24 +721,38 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     float s_out = 0.f, s_pre = 0.f;
     if (!scale("model.0", &s_out) || !scale("model.0:pre", &s_pre)) return cudaErrorInvalidValue;
     const float cs[3] = {s_in, s_in, s_in};
-    QWeights q;
-    if (!quantize(*w0, find("model.0.conv.bias"), cs, static_cast<double>(s_pre), &q))
-      return fail("int8: requantisation ratio out of range in model.0");
-    std::vector<uint32_t> wp(static_cast<size_t>(9) * co);
-    for (int o = 0; o < co; ++o)
-      for (int t = 0; t < 9; ++t) {
-        uint32_t v = 0;
-        for (int c = 0; c < 3; ++c)
-          v |= (static_cast<uint32_t>(q.wq[(static_cast<size_t>(o) * 3 + c) * 9 + t]) & 0xFFu) << (8 * c);
-        wp[static_cast<size_t>(t) * co + o] = v;
-      }
+    void *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr, *dl = nullptr;
+    if (w0->dev) {
+      QDev qd;
+      const cudaError_t r = quantize_dev(*w0, find("model.0.conv.bias"), cs, 3, false, static_cast<double>(s_pre), &qd);
+      if (r == cudaErrorInvalidValue) return fail("int8: requantisation ratio out of range in model.0");
+      YB_TRY(r);
+      YB_TRY(dalloc(static_cast<size_t>(9) * co * 4, &dw));
+      YB_TRY(cudaDeviceSynchronize());
+      YB_TRY(launch_pack_stem_i8(qd.wq, co, static_cast<uint32_t*>(dw), stream_));
+      YB_TRY(cudaStreamSynchronize(stream_));
+      db = qd.bq;
+      dm = qd.mult;
+      ds = qd.shift;
+    } else {
+      QWeights q;
+      if (!quantize(*w0, find("model.0.conv.bias"), cs, static_cast<double>(s_pre), &q))
+        return fail("int8: requantisation ratio out of range in model.0");
+      std::vector<uint32_t> wp(static_cast<size_t>(9) * co);
+      for (int o = 0; o < co; ++o)
+        for (int t = 0; t < 9; ++t) {
+          uint32_t v = 0;
+          for (int c = 0; c < 3; ++c)
+            v |= (static_cast<uint32_t>(q.wq[(static_cast<size_t>(o) * 3 + c) * 9 + t]) & 0xFFu) << (8 * c);
+          wp[static_cast<size_t>(t) * co + o] = v;
+        }
+      YB_TRY(upload(wp.data(), wp.size() * 4, &dw));
+      YB_TRY(upload(q.bq.data(), q.bq.size() * 4, &db));
+      YB_TRY(upload(q.mult.data(), q.mult.size() * 4, &dm));
+      YB_TRY(upload(q.shift.data(), q.shift.size() * 4, &ds));
+    }
     int8_t lut[256];
     silu_lut(lut, s_pre, s_out);
-    void *dw = nullptr, *db = nullptr, *dm = nullptr, *ds = nullptr, *dl = nullptr;
-    YB_TRY(upload(wp.data(), wp.size() * 4, &dw));
-    YB_TRY(upload(q.bq.data(), q.bq.size() * 4, &db));
-    YB_TRY(upload(q.mult.data(), q.mult.size() * 4, &dm));
-    YB_TRY(upload(q.shift.data(), q.shift.size() * 4, &ds));
     YB_TRY(upload(lut, 256, &dl));
     YB_TRY(tensor(co, (H - 1) / 2 + 1, (W - 1) / 2 + 1, &b[0]));
     YB_TRY(init_stem_i8_attributes());

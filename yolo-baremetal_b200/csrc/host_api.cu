@@ -536,6 +536,85 @@ extern "C" status_t yb_cuda_load_bin(void* ctx, const char* path) {
   return cuda_status(e, "upload weights");
 }
 
+extern "C" status_t yb_cuda_load_bin_device(void* ctx, const char* path) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !path) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  if ((st = drain_stream(c)) != SUCCESS) return st;
+  WeightMap w;
+  int nc = 0;
+  std::string why;
+  if (!read_weight_bin(path, &w, &nc, &why)) {
+    set_error(why);
+    return why.rfind("cannot open", 0) == 0 ? ERROR_FILE_NOT_FOUND : ERROR_INVALID_FORMAT;
+  }
+  cudaError_t e = c->eng->set_weights_device(std::move(w), nc, &why);
+  c->last = nullptr;
+  if (e == cudaErrorInvalidValue) {
+    set_error(why);
+    return ERROR_INVALID_FORMAT;
+  }
+  return cuda_status(e, "device weight preparation");
+}
+
+extern "C" status_t yb_cuda_save_prepared(void* ctx, const char* path) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !path) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  if ((st = drain_stream(c)) != SUCCESS) return st;
+  std::string why;
+  cudaError_t e = c->eng->save_blob(path, &why);
+  if (e == cudaErrorInvalidValue) {
+    set_error(why);
+    return ERROR_FILE_NOT_FOUND;
+  }
+  return cuda_status(e, "save prepared weights");
+}
+
+extern "C" status_t yb_cuda_load_prepared(void* ctx, const char* path) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !path) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  if ((st = drain_stream(c)) != SUCCESS) return st;
+  std::string why;
+  int nc = 0;
+  cudaError_t e = c->eng->load_blob(path, &nc, &why);
+  c->last = nullptr;
+  if (e == cudaErrorInvalidValue) {
+    set_error(why);
+    return why.rfind("cannot open", 0) == 0 ? ERROR_FILE_NOT_FOUND : ERROR_INVALID_FORMAT;
+  }
+  return cuda_status(e, "load prepared weights");
+}
+
+extern "C" status_t yb_cuda_weight_image(void* ctx, const char* name, int kind, int n_tile, void* out, size_t cap,
+                                         size_t* bytes) {
+  Ctx* c = as_ctx(ctx);
+  if (!c || !name) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  std::vector<uint8_t> img;
+  std::string why;
+  cudaError_t e = c->eng->weight_image(name, kind, n_tile, &img, &why);
+  if (e == cudaErrorInvalidValue) {
+    set_error(why);
+    return ERROR_FILE_NOT_FOUND;
+  }
+  if (e != cudaSuccess) return cuda_status(e, "weight image");
+  if (bytes) *bytes = img.size();
+  if (out) {
+    if (cap < img.size()) {
+      set_error("weight image: buffer too small");
+      return ERROR_INVALID_DIMS;
+    }
+    std::memcpy(out, img.data(), img.size());
+  }
+  return SUCCESS;
+}
+
 extern "C" status_t yb_cuda_forward(void* ctx, const float* in_nchw, int B, int H, int W, float* out_dets,
                                     int max_det, yb_stage_cb dump, void* user, double* step_ms) {
   Ctx* c = as_ctx(ctx);

@@ -44,7 +44,9 @@ EXPORTS = {
                   "yb_cuda_plan_io", "yb_cuda_forward_device", "yb_cuda_get_head", "yb_cuda_detect_topk_noalloc",
                   "yb_cuda_forward_sharded",
                   "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error",
-                  "yb_conv_create", "yb_conv_ci_pad", "yb_conv_run", "yb_conv_check", "yb_conv_destroy"],
+                  "yb_conv_create", "yb_conv_ci_pad", "yb_conv_run", "yb_conv_check", "yb_conv_destroy",
+                  "yb_cuda_load_bin_device", "yb_cuda_save_prepared", "yb_cuda_load_prepared",
+                  "yb_cuda_weight_image"],
     "yb_int8.h": ["yb_int8_quantize_conv", "yb_int8_conv_create", "yb_int8_conv_ci_pad", "yb_int8_conv_run",
                   "yb_int8_conv_check", "yb_int8_conv_destroy"],
 }
@@ -118,6 +120,11 @@ def lib() -> C.CDLL:
         L.yb_conv_create.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_int, C.c_int, C.POINTER(C.c_void_p)]
         L.yb_conv_ci_pad.argtypes = [C.c_void_p]
+        L.yb_cuda_load_bin_device.argtypes = [C.c_void_p, C.c_char_p]
+        L.yb_cuda_save_prepared.argtypes = [C.c_void_p, C.c_char_p]
+        L.yb_cuda_load_prepared.argtypes = [C.c_void_p, C.c_char_p]
+        L.yb_cuda_weight_image.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                           C.POINTER(C.c_size_t)]
         L.yb_conv_run.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.yb_conv_check.argtypes = [C.c_void_p]
         L.yb_conv_destroy.argtypes = [C.c_void_p]
@@ -182,12 +189,28 @@ def tensor_view(a: np.ndarray) -> Tensor:
 class Model:
     """One device replica (yb_cuda_* context) on one GPU."""
 
-    def __init__(self, weights: str, device: int = 0):
+    def __init__(self, weights: str, device: int = 0, prep: str = "host"):
+        """prep: "host" (fold and pack on the host), "device" (fold, pack and
+        quantise on the GPU) or "blob" (weights is a prepared-weight blob)."""
         L = lib()
         self.ctx = C.c_void_p()
         check(L.yb_cuda_init(device, C.byref(self.ctx)), "yb_cuda_init")
-        check(L.yb_cuda_load_bin(self.ctx, weights.encode()), "yb_cuda_load_bin")
+        load = {"host": L.yb_cuda_load_bin, "device": L.yb_cuda_load_bin_device, "blob": L.yb_cuda_load_prepared}[prep]
+        check(load(self.ctx, weights.encode()), f"load ({prep})")
         self.device = device
+
+    def save_prepared(self, path: str) -> None:
+        check(lib().yb_cuda_save_prepared(self.ctx, path.encode()), "yb_cuda_save_prepared")
+
+    def weight_image(self, name: str, kind: int, n_tile: int = 0) -> bytes:
+        """Prepared weight image (kind 0 folded fp32 tensor, 1 packed FP32 conv, 2 packed INT8 conv)."""
+        n = C.c_size_t()
+        check(lib().yb_cuda_weight_image(self.ctx, name.encode(), kind, n_tile, None, 0, C.byref(n)),
+              "yb_cuda_weight_image")
+        buf = C.create_string_buffer(n.value)
+        check(lib().yb_cuda_weight_image(self.ctx, name.encode(), kind, n_tile, buf, n.value, C.byref(n)),
+              "yb_cuda_weight_image")
+        return buf.raw[: n.value]
 
     def close(self) -> None:
         if self.ctx:
