@@ -282,6 +282,15 @@ status_t yb_conv_run(void* conv, const void* d_x, int B, int H, int W, void* d_y
 status_t yb_conv_check(void* conv);
 status_t yb_conv_destroy(void* conv);
 
+/* Test hook of the kernel's bounded waits (no GPU fault involved): the next
+ * yb_conv_run of this handle launches with its producer warps arming no
+ * barrier and issuing no copy, and with a 1 ms bound on every wait.  The
+ * UMMA issuer's first wait runs out; the kernel records the error, drains,
+ * frees its tensor memory and returns, so yb_conv_check reports
+ * ERROR_DEVICE and later runs are unaffected.  ERROR_NOT_IMPLEMENTED for the
+ * first-layer (NCHW input) kernel, which has no barrier waits. */
+status_t yb_conv_debug_withhold(void* conv);
+
 /* One kernel launch of a plan, as measured by yb_cuda_profile_ops. */
 typedef struct {
     int kind;     /* 0 tcgen05 conv, 1 stem conv, 2 depthwise, 3 max pool, 4 attention, 5 decode, 6 top-k */

@@ -26,6 +26,7 @@ struct Fp32Conv {
   int device = 0, num_sms = 148;
   int co = 0, cop = 0, ci = 0, cip = 0, kh = 0, kw = 0, stride = 1, pad = 0, act = kActNone;
   bool stem = false;
+  bool withhold_next = false;  // test hook armed by yb_conv_debug_withhold
   int K = 0, num_kc = 0, n_tile = 0, n_tiles = 0;
   uint8_t* wpack[3] = {nullptr, nullptr, nullptr};  // full tiling, 64-wide, 128-wide N tiles
   float* bias = nullptr;
@@ -200,7 +201,23 @@ extern "C" status_t yb_conv_run(void* conv, const void* d_x, int B, int H, int W
   a.out = out;
   a.err = c->err;
   conv_setup_tma(&a);
+  if (c->withhold_next) {
+    c->withhold_next = false;
+    a.debug_withhold = 1;
+    a.wait_ns = 1000000;  // 1 ms
+  }
   return cuda_status(launch_conv_tc(a, s, c->num_sms), "conv");
+}
+
+extern "C" status_t yb_conv_debug_withhold(void* conv) {
+  auto* c = static_cast<Fp32Conv*>(conv);
+  if (!c) return ERROR_NULL_POINTER;
+  if (c->stem) {
+    set_error("conv: the first-layer kernel has no barrier waits to test");
+    return ERROR_NOT_IMPLEMENTED;
+  }
+  c->withhold_next = true;
+  return SUCCESS;
 }
 
 extern "C" status_t yb_conv_check(void* conv) {

@@ -185,13 +185,17 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   pdl_wait();
 
   const int total_tiles = a.m_tiles * a.n_tiles;
+  const uint64_t wlim = a.wait_ns ? a.wait_ns : kWaitNs;
   // The last K chunk holds K - 64 (num_kc - 1) real values: only its first
   // ks_last 16-wide steps are copied and multiplied.
   const int ks_last = (a.K - (a.num_kc - 1) * kBK + 15) / 16;
   const int HoWo = a.Ho * a.Wo;
   const int M = a.B * HoWo;
 
-  if (warp < kProducerWarps && patch) {
+  if (warp < kProducerWarps && a.debug_withhold) {
+    // Test hook: no barrier is armed and no copy issued; the MMA issuer's
+    // first wait runs out after wlim.
+  } else if (warp < kProducerWarps && patch) {
     // ----------------------------------------------------- patch producer
     // One thread: the resident weights once, then per tile one box copy per
     // 8-channel chunk and plane of its 18 x 10 input patch.
@@ -206,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
         const uint32_t s = it % stages;
         const uint32_t ph = (it / stages) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, wlim)) {
           raise_error(a.err, abort_flag, kErrWaitEmpty);
           break;
         }
@@ -260,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
           const uint32_t s = it % stages;
           const uint32_t ph = (it / stages) & 1u;
-          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, wlim)) {
             raise_error(a.err, abort_flag, kErrWaitEmpty);
             goto tma_producer_done;
           }
@@ -338,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       for (int kc = 0; kc < a.num_kc; ++kc) {
         const uint32_t s = it % stages;
         const uint32_t ph = (it / stages) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, wlim)) {
           raise_error(a.err, abort_flag, kErrWaitEmpty);
           goto producer_done;
         }
@@ -398,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     for (int t = blockIdx.x + grp * gridDim.x, lt = grp; t < total_tiles; t += 2 * gridDim.x, lt += 2) {
       const int acc = lt % nacc;
       const uint32_t aph = (lt / nacc) & 1;
-      if (!mbar_wait(&acc_full[acc], aph, abort_flag)) {
+      if (!mbar_wait(&acc_full[acc], aph, abort_flag, wlim)) {
         raise_error(a.err, abort_flag, kErrWaitAccFull);
         break;
       }
@@ -555,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
         const int acc = lt % nacc;
         const uint32_t aph = (lt / nacc) & 1;
-        if (!mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag)) {
+        if (!mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag, wlim)) {
           raise_error(a.err, abort_flag, kErrWaitAccEmpty);
           break;
         }
@@ -565,14 +569,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         if (patch) {
           // One stage per tile: 9 taps x Ci/16 K steps, each A operand a
           // shifted window of the patch, each B step in the resident weights.
-          if (lt == 0 && !mbar_wait(wbar, 0, abort_flag)) {
+          if (lt == 0 && !mbar_wait(wbar, 0, abort_flag, wlim)) {
             raise_error(a.err, abort_flag, kErrWaitFull);
             break;
           }
           const uint32_t s = it % stages;
           const uint32_t ph = (it / stages) & 1u;
           ++it;
-          if (!mbar_wait(&full[s], ph, abort_flag)) {
+          if (!mbar_wait(&full[s], ph, abort_flag, wlim)) {
             raise_error(a.err, abort_flag, kErrWaitFull);
             break;
           }
@@ -671,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
           const uint32_t s = it % stages;
           const uint32_t ph = (it / stages) & 1u;
-          if (!mbar_wait(&full[s], ph, abort_flag)) {
+          if (!mbar_wait(&full[s], ph, abort_flag, wlim)) {
             raise_error(a.err, abort_flag, kErrWaitFull);
             ok = false;
             break;
@@ -719,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       tc_commit(drain);
       bool drained = mbar_try_wait(drain, 0);
       const uint64_t t0 = globaltimer_ns();
-      while (!drained && globaltimer_ns() - t0 < kWaitNs) drained = mbar_try_wait(drain, 0);
+      while (!drained && globaltimer_ns() - t0 < wlim) drained = mbar_try_wait(drain, 0);
       if (!drained) raise_error(a.err, abort_flag, kErrDrain);
     }
     __syncwarp();

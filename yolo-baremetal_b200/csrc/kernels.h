@@ -102,6 +102,12 @@ struct ConvArgs {
   // weights stay resident in shared memory.  a_tma == 3: the same for 3x3
   // stride-2 convolutions (33 x 17 patch as odd / even column boxes).
   int tiles_y = 0, tiles_x = 0;
+  // Test hook of the bounded waits (0 in every plan): with debug_withhold the
+  // producer warps arm no barrier and issue no copy, and every wait gives up
+  // after wait_ns (0: the default bound), so the MMA issuer's first wait runs
+  // out and the kernel records an error, drains and returns.
+  int debug_withhold = 0;
+  uint64_t wait_ns = 0;
   alignas(64) CUtensorMap tm_hi;
   alignas(64) CUtensorMap tm_lo;
 };

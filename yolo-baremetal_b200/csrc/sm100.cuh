@@ -75,13 +75,16 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 // Waits for the phase with the given parity to complete.  Returns false when
 // the wait gave up: after kWaitNs, or early once *abort is non-zero.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// limit_ns shortens the bound (a kernel's test hook passes about 1 ms).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint32_t hint = limit_ns < 1000000u ? static_cast<uint32_t>(limit_ns) : 1000000u;
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+    if (mbar_try_wait_sleep(bar, parity, hint)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 

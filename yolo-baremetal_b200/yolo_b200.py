@@ -46,7 +46,7 @@ EXPORTS = {
                   "yb_cuda_profile_ops", "yb_cuda_debug_inject_stall", "yb_cuda_destroy", "yb_cuda_last_error",
                   "yb_conv_create", "yb_conv_ci_pad", "yb_conv_run", "yb_conv_check", "yb_conv_destroy",
                   "yb_cuda_load_bin_device", "yb_cuda_save_prepared", "yb_cuda_load_prepared",
-                  "yb_cuda_weight_image"],
+                  "yb_cuda_weight_image", "yb_conv_debug_withhold"],
     "yb_int8.h": ["yb_int8_quantize_conv", "yb_int8_conv_create", "yb_int8_conv_ci_pad", "yb_int8_conv_run",
                   "yb_int8_conv_check", "yb_int8_conv_destroy"],
 }
@@ -127,6 +127,7 @@ def lib() -> C.CDLL:
                                            C.POINTER(C.c_size_t)]
         L.yb_conv_run.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.yb_conv_check.argtypes = [C.c_void_p]
+        L.yb_conv_debug_withhold.argtypes = [C.c_void_p]
         L.yb_conv_destroy.argtypes = [C.c_void_p]
         L.yb_cuda_set_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         L.yb_cuda_get_detections.argtypes = [C.c_void_p, C.c_float, C.c_int, C.c_void_p, C.c_void_p]
