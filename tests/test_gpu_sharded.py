@@ -49,3 +49,41 @@ def test_sharded_deadline_reports_timeout_then_recovers(shard_models):
     st, dets = yb.forward_sharded(shard_models, imgs, timeout_ms=60000)
     yb.check(st, "yb_cuda_forward_sharded after timeout")
     assert np.array_equal(dets, shard_models[0].forward(imgs)["dets"])
+
+
+def test_sharded_across_all_gpus_timed(weights_n0):
+    """The benchmark's global batch of 64 640x640 images split over every
+    visible GPU by yb_cuda_forward_sharded (detections land in one host
+    array), bit-equal to one GPU's forward of the same batch; prints the
+    wall-clock images/s of both (skipped with one GPU)."""
+    import time
+
+    import torch
+
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    G = torch.cuda.device_count()
+    if G < 2:
+        pytest.skip("one GPU visible")
+    ms = [yb.Model(weights_n0, device=d) for d in range(G)]
+    try:
+        imgs = yw.make_batch(range(1, 65), 640, 640)
+        st, dets = yb.forward_sharded(ms, imgs, timeout_ms=60000)
+        yb.check(st, "yb_cuda_forward_sharded")
+        one = ms[0].forward(imgs)["dets"]
+        assert np.array_equal(dets, one)
+        reps = 5
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            yb.check(yb.forward_sharded(ms, imgs, timeout_ms=60000)[0], "sharded")
+        ts = (time.perf_counter() - t0) / reps
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            ms[0].forward(imgs)
+        t1 = (time.perf_counter() - t0) / reps
+        print(f"64 images: {G} GPUs sharded {64 / ts:.0f} images/s ({1e3 * ts:.1f} ms), "
+              f"1 GPU {64 / t1:.0f} images/s ({1e3 * t1:.1f} ms), host buffers")
+    finally:
+        for m in ms:
+            m.close()
