@@ -13,23 +13,25 @@
 // memory.
 //
 // Persistent, warp-specialised CTA (544 threads, one CTA per SM):
-//   warps 0-7   producers: each K chunk of the activation tile is gathered
+//   warps 0-3   producers: each K chunk of the activation tile is gathered
 //               with 16-byte cp.async copies straight from the hi and lo
 //               planes into the 128B-swizzled K-major operand layout (zero
 //               fill for padding and K tails; upsample and two-source concat
 //               in the address computation), several stages deep; each
 //               thread's copies arrive on the stage's mbarrier as they land.
 //               Thread 0 also starts one bulk copy (TMA engine) of the
-//               pre-packed, pre-swizzled weight chunk.
-//   warp 16     allocates tensor memory (2-4 accumulators) and, from one
+//               pre-packed, pre-swizzled weight chunk.  In the TMA modes one
+//               thread issues the tensor copies instead.
+//   warp 16     allocates tensor memory (2-3 accumulators) and, from one
 //               lane, issues the UMMAs; tcgen05.commit frees each smem stage
 //               and publishes each finished accumulator.
-//   warps 8-15  epilogue in two groups of four taking alternate tiles, one
-//               warp per TMEM lane quarter (32 output pixels): tcgen05.ld,
-//               + bias (staged in shared memory), SiLU, + residual, split (or
-//               fp32) NHWC store into the destination channel slice.  Runs
-//               while warp 16 accumulates the next tiles into the other TMEM
-//               buffers.
+//   warps 4-15  epilogue in three groups of four (two when three
+//               accumulators do not fit in tensor memory) taking tiles round
+//               robin, one warp per TMEM lane quarter (32 output pixels):
+//               tcgen05.ld, + bias (staged in shared memory), SiLU,
+//               + residual, split (or fp32) NHWC store into the destination
+//               channel slice.  Runs while warp 16 accumulates the next tiles
+//               into the other TMEM buffers.
 // All barrier waits are bounded (sm100.cuh); a timeout sets *a.err, aborts
 // the other roles, drains outstanding copies and UMMAs and frees tensor
 // memory.
@@ -49,9 +51,10 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kProducerWarps = 8;  // two per sub-partition: the im2col address stream is the long pole
-constexpr int kRowsPerThread = kBM * 8 / (kProducerWarps * 32);  // 16-byte columns per row = 8
-constexpr int kEpilogueWarps = 8;  // two groups of four (one warp per TMEM lane quarter), alternate tiles
+constexpr int kProducerWarps = 4;  // one per sub-partition (the gather producers; one thread in TMA modes)
+constexpr int kRowStep = kProducerWarps * 32 / 8;                // rows per pass: 8 threads per 128-byte row
+constexpr int kRowsPerThread = kBM / kRowStep;
+constexpr int kEpilogueWarps = 12;  // up to three groups of four (one warp per TMEM lane quarter), round-robin tiles
 constexpr int kMaxAcc = 4;         // TMEM accumulators when n_tile allows (4 x n_tile <= 512 columns)
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
@@ -213,8 +216,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   const uint32_t acc_cols = static_cast<uint32_t>(stacked ? 2 * a.n_tile : a.n_tile);
   uint32_t acc_stride = 32;
   while (acc_stride < acc_cols) acc_stride <<= 1;
-  const int nacc = min(kMaxAcc, static_cast<int>(512u / acc_stride));
-  const uint32_t ncols = static_cast<uint32_t>(nacc) * acc_stride;
+  // Three epilogue groups when three accumulators fit (each group then owns
+  // one accumulator, so its waits follow that accumulator's phases in
+  // order), else two, each owning every other accumulator.
+  const int egroups = 3u * acc_stride <= 512u ? 3 : 2;
+  const int nacc = egroups == 3 ? 3 : min(kMaxAcc, static_cast<int>(512u / acc_stride));
+  uint32_t ncols = 32;  // the allocation is a power of two
+  while (ncols < static_cast<uint32_t>(nacc) * acc_stride) ncols <<= 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -223,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     }
     for (int i = 0; i < nacc; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kEpilogueWarps / 2);
+      mbar_init(&acc_empty[i], 4);  // the four warps of one epilogue group
     }
     mbar_init(drain, 1);
     mbar_init(wbar, 1);
@@ -360,9 +368,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   } else if (warp < kProducerWarps) {
     // ------------------------------------------------------------ producers
     // Thread t copies the 16-byte column j = t % 8 (8 K indices) of rows
-    // t / 8 + 32 i, i = 0..3, for both planes.  Per tile each row's pixel
-    // offset in both sources is computed once; per chunk only the tap and
-    // channel of column j change, so a copy costs a few adds and compares.
+    // t / 8 + kRowStep i, i < kRowsPerThread, for both planes.  Per tile each
+    // row's pixel offset in both sources is computed once; per chunk only the
+    // tap and channel of column j change, so a copy costs a few adds and
+    // compares.
     const int ptid = threadIdx.x;
     const int j = ptid & 7;
     const int r0 = ptid >> 3;
@@ -373,14 +382,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     uint32_t row_off[kRowsPerThread];
 #pragma unroll
     for (int i = 0; i < kRowsPerThread; ++i)
-      row_off[i] = sw128_offset(static_cast<uint32_t>(r0 + 32 * i), static_cast<uint32_t>(j));
+      row_off[i] = sw128_offset(static_cast<uint32_t>(r0 + kRowStep * i), static_cast<uint32_t>(j));
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const int mt = t / a.n_tiles;
       const int nt = t - mt * a.n_tiles;
       int iy0[kRowsPerThread], ix0[kRowsPerThread];
       long long off0[kRowsPerThread], off1[kRowsPerThread];
       {
-        // Row r0 of the tile, then step 32 pixels per row without dividing.
+        // Row r0 of the tile, then step kRowStep pixels per row without dividing.
         const int m = mt * kBM + r0;
         int b = m / HoWo;
         int r = m - b * HoWo;
@@ -388,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         int ox = r - oy * a.Wo;
 #pragma unroll
         for (int i = 0; i < kRowsPerThread; ++i) {
-          const bool valid = m + 32 * i < M;
+          const bool valid = m + kRowStep * i < M;
           const int iy = oy * a.stride - a.pad;
           const int ix = ox * a.stride - a.pad;
           iy0[i] = valid ? iy : -(1 << 28);  // never in bounds
@@ -397,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                     static_cast<long long>((iy >> a.lg_up0) * ws0 + (ix >> a.lg_up0)) * a.src0.cstride;
           off1[i] = static_cast<long long>(b) * a.src1.bstride +
                     static_cast<long long>((iy >> a.lg_up1) * ws1 + (ix >> a.lg_up1)) * a.src1.cstride;
-          ox += 32;
+          ox += kRowStep;
           while (ox >= a.Wo) {
             ox -= a.Wo;
             if (++oy == a.Ho) {
@@ -463,12 +472,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     cp_async_wait_all();
   } else if (warp < kMmaWarp) {
     // ------------------------------------------------------------- epilogue
-    const int e_idx = warp - kProducerWarps;  // 0..7
+    const int e_idx = warp - kProducerWarps;  // 0..11
     const int q = e_idx & 3;                  // TMEM lane quarter (= warp % 4)
-    const int grp = e_idx >> 2;               // this group takes every other tile
+    const int grp = e_idx >> 2;               // this group takes every egroups-th tile
     const bool f32out = a.out_f32.ptr != nullptr;
     float mpre = 0.0f, mout = 0.0f;  // calibration statistics (a.amax)
-    for (int t = blockIdx.x + grp * gridDim.x, lt = grp; t < total_tiles; t += 2 * gridDim.x, lt += 2) {
+    for (int t = blockIdx.x + grp * gridDim.x, lt = grp; grp < egroups && t < total_tiles;
+         t += egroups * gridDim.x, lt += egroups) {
       const int acc = lt % nacc;
       const uint32_t aph = (lt / nacc) & 1;
       if (!mbar_wait(&acc_full[acc], aph, abort_flag, wlim)) {
@@ -741,9 +751,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             ok = false;
             break;
           }
-          // The stage's activation tile was written by cp.async; order it
-          // before the tensor core's (async-proxy) operand reads.
-          fence_proxy_async_smem();
+          // A stage written by cp.async (gather mode) is ordered before the
+          // tensor core's (async-proxy) operand reads; TMA writes need no fence.
+          if (!a.a_tma) fence_proxy_async_smem();
           tc_fence_after();
           // Descriptors of the stage's four operand planes; a 16-wide K step
           // advances the start address by 32 bytes (2 in the >>4 field).
@@ -766,14 +776,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             const uint64_t aoff = a_cpp == 16   ? static_cast<uint64_t>(ks * 256)
                                   : a_cpp == 32 ? static_cast<uint64_t>((ks >> 1) * 512 + (ks & 1) * 2)
                                                 : koff;
-            if (stacked) {
-              tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
-              tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
-            } else {
-              tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
-              tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + koff, idesc, 1u);
-              tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
-            }
+            tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
+            tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + koff, idesc, 1u);
+            tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
           }
           tc_commit(&empty[s]);
         }
