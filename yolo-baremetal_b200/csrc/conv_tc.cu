@@ -476,6 +476,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     const int q = e_idx & 3;                  // TMEM lane quarter (= warp % 4)
     const int grp = e_idx >> 2;               // this group takes every egroups-th tile
     const bool f32out = a.out_f32.ptr != nullptr;
+    // 32-byte stores of whole 16-channel runs when every run starts on a
+    // 32-byte boundary (offsets and strides in elements of 2 bytes).
+    const bool v8out = !f32out && (reinterpret_cast<uintptr_t>(a.out.hi) & 31) == 0 && (a.out.cstride & 15) == 0 &&
+                       (a.out.coff & 15) == 0 && (a.out.bstride & 15) == 0 && (a.out.plane & 15) == 0;
     float mpre = 0.0f, mout = 0.0f;  // calibration statistics (a.amax)
     for (int t = blockIdx.x + grp * gridDim.x, lt = grp; grp < egroups && t < total_tiles;
          t += egroups * gridDim.x, lt += egroups) {
@@ -523,15 +527,23 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                                   : static_cast<long long>(b) * a.out.bstride +
                                         static_cast<long long>(p) * a.out.cstride + a.out.coff + n0;
       // Per 16-column unit: one TMEM load, bias and SiLU, residual loads,
-      // then the stores.
+      // then the stores.  The next unit's TMEM load is issued as soon as
+      // this unit's registers are consumed, so its latency overlaps this
+      // unit's arithmetic and stores.
+      uint32_t r[16], r2[16];
+      tc_ld_32x32b_x16(tbase, r);
+      if (stacked) tc_ld_32x32b_x16(tbase + a.n_tile, r2);
       for (int c = 0; c < nvalid; c += 16) {
-        uint32_t r[16], r2[16];
-        tc_ld_32x32b_x16(tbase + c, r);
-        if (stacked) tc_ld_32x32b_x16(tbase + a.n_tile + c, r2);
         tc_wait_ld();
+        tc_ld_dep(r);
+        if (stacked) tc_ld_dep(r2);
         float v[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]) + (stacked ? __uint_as_float(r2[e]) : 0.0f);
+        if (c + 16 < nvalid) {
+          tc_ld_32x32b_x16(tbase + c + 16, r);
+          if (stacked) tc_ld_32x32b_x16(tbase + a.n_tile + c + 16, r2);
+        }
 #pragma unroll
         for (int e = 0; e < 16; e += 4) {
           const float4 bb = *reinterpret_cast<const float4*>(bias_t + c + e);
@@ -583,6 +595,17 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 *reinterpret_cast<float4*>(o + 4) =
                     make_float4(v[8 * g + 4], v[8 * g + 5], v[8 * g + 6], v[8 * g + 7]);
             }
+          }
+        } else if (v8out && second) {
+          // Split to bf16 hi/lo words; each lane writes its pixel's 32-byte
+          // runs (16 channels) with one 32-byte store per plane.
+          uint32_t hw[8], lw[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) split2(v[2 * i], v[2 * i + 1], hw[i], lw[i]);
+          if (valid) {
+            uint16_t* o = a.out.hi + po + c;
+            st_global_v8(o, hw);
+            st_global_v8(o + a.out.plane, lw);
           }
         } else {
           // Split to bf16 hi/lo words (channel pairs), then regroup across
