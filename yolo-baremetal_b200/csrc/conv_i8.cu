@@ -547,6 +547,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
     // min(kEpiGroups, nacc) groups work.
     const int grp = warp >> 2;
     const int ngrp = min(kEpiGroups, nacc);
+    // 32-byte stores of whole 32-channel runs when every run is aligned.
+    const bool v8out = !a.out_f32 && (reinterpret_cast<uintptr_t>(a.out) & 31) == 0 && (a.out_cstride & 31) == 0 &&
+                       (a.out_coff & 31) == 0 && (a.n_tile & 31) == 0;
     for (int t = blockIdx.x + grp * gridDim.x, lt = grp; grp < ngrp && t < total_tiles;
          t += ngrp * gridDim.x, lt += ngrp) {
       const int acc = lt % nacc;
@@ -622,11 +625,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
         }
         uint32_t p0[4] = {0u, 0u, 0u, 0u}, p1[4] = {0u, 0u, 0u, 0u};
         const int mode = (a.lut ? 2 : 0) | (a.res ? 1 : 0);
-        // Two halves of 16 channels: one TMEM load each.
-        auto half = [&](int hh, uint32_t(&pk)[4]) {
-          uint32_t r[16];
-          tc_ld_32x32b_x16(tbase + c + 16 * hh, r);
-          tc_wait_ld();
+        // Two halves of 16 channels: both TMEM loads in flight together, one wait.
+        uint32_t ra[16], rb[16];
+        tc_ld_32x32b_x16(tbase + c, ra);
+        if (two) tc_ld_32x32b_x16(tbase + c + 16, rb);
+        tc_wait_ld();
+        tc_ld_dep(ra);
+        if (two) tc_ld_dep(rb);
+        auto half = [&](int hh, uint32_t(&r)[16], uint32_t(&pk)[4]) {
           const int4* qc = sq + n0 + c + 16 * hh;
           const uint4 rh = rvv[hh];
           const int32_t* sbh = sb + n0 + c + 16 * hh;
@@ -655,8 +661,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
             pk[3] = w.w;
           }
         };
-        half(0, p0);
-        if (two) half(1, p1);
+        half(0, ra, p0);
+        if (two) half(1, rb, p1);
+        if (v8out && two) {
+          // The lane's pixel run of 32 channels in one 32-byte store.
+          if (valid) {
+            const uint32_t w8[8] = {p0[0], p0[1], p0[2], p0[3], p1[0], p1[1], p1[2], p1[3]};
+            st_global_v8(a.out + po + c, w8);
+          }
+          continue;
+        }
         const int h = lane & 1;
 #pragma unroll
         for (int i = 0; i < 2; ++i) {

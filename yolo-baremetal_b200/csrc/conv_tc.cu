@@ -212,7 +212,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   // stacked [B_hi; B_lo] chunk (columns [0, n) += A*B_hi, [n, 2n) += A*B_lo,
   // summed by the epilogue).  Otherwise three UMMAs of N = n_tile, which
   // keeps the epilogue (the long pole there) to one TMEM load per unit.
-  const bool stacked = patch && a.n_tile <= 128;
+  // The im2col / gather modes stack too for 3x3 convolutions with n_tile <=
+  // 64 (MMA-issue bound: measured ~45-64 cycles per UMMA at N <= 128, so two
+  // UMMAs of 2n beat three of n); 1x1 convolutions keep one TMEM load per
+  // unit for their epilogue-bound tiles.
+  const bool stacked = patch ? a.n_tile <= 128 : (a.kh * a.kw > 1 && a.n_tile <= 64);
   const uint32_t acc_cols = static_cast<uint32_t>(stacked ? 2 * a.n_tile : a.n_tile);
   uint32_t acc_stride = 32;
   while (acc_stride < acc_cols) acc_stride <<= 1;
@@ -799,9 +803,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             const uint64_t aoff = a_cpp == 16   ? static_cast<uint64_t>(ks * 256)
                                   : a_cpp == 32 ? static_cast<uint64_t>((ks >> 1) * 512 + (ks & 1) * 2)
                                                 : koff;
-            tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
-            tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + koff, idesc, 1u);
-            tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
+            if (stacked) {
+              tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
+              tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
+            } else {
+              tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
+              tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + koff, idesc, 1u);
+              tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
+            }
           }
           tc_commit(&empty[s]);
         }
