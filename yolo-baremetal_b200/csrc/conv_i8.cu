@@ -315,6 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
     // 16-channel plane of its 18 x 10 input patch (zero outside the image
     // and past the view's channels).
     if (lane == 0) {
+      prefetch_tmap(&a.tm);
       mbar_arrive_expect_tx(wbar, wres_bytes);
       for (int kc = 0; kc < a.num_kc; ++kc)
         bulk_g2s(smem + static_cast<size_t>(kc) * chunk_bytes, a.wpack + static_cast<size_t>(kc) * chunk_bytes,
@@ -323,15 +324,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       const int per = a.tiles_y * a.tiles_x;
       uint32_t it = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
-        const uint32_t s = it % stages;
-        const uint32_t ph = (it / stages) & 1u;
+        const uint32_t itq = a.fd_stages.div(it);
+        const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+        const uint32_t ph = itq & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
           raise_err(a.err, abort_flag, kErrWaitEmpty);
           break;
         }
-        const int b = t / per;
+        const int b = static_cast<int>(a.fd_per.div(static_cast<uint32_t>(t)));
         const int rem = t - b * per;
-        const int ty = rem / a.tiles_x;
+        const int ty = static_cast<int>(a.fd_tx.div(static_cast<uint32_t>(rem)));
         const int tx = rem - ty * a.tiles_x;
         uint8_t* stage = stage0 + s * stage_bytes;
         if (patch2) {
@@ -350,6 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
   } else if (warp == kProdWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      prefetch_tmap(&a.tm);
       const int taps = a.kh * a.kw;
       const int cpp = a.a_cpp;
       const int tps = cpp == 128 ? 1 : 128 / cpp;
@@ -357,18 +360,19 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       const uint32_t sub_bytes = static_cast<uint32_t>(kBM * cpp);
       uint32_t it = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-        const int mt = t / a.n_tiles;
+        const int mt = static_cast<int>(a.fd_ntiles.div(static_cast<uint32_t>(t)));
         const int nt = t - mt * a.n_tiles;
         const int m0 = mt * kBM;
-        const int b = m0 / HoWo;
+        const int b = static_cast<int>(a.fd_howo.div(static_cast<uint32_t>(m0)));
         const int r = m0 - b * HoWo;
-        const int oy = r / a.Wo;
+        const int oy = static_cast<int>(a.fd_wo.div(static_cast<uint32_t>(r)));
         const int ox = r - oy * a.Wo;
         const int w0 = ox * a.stride - a.pad, h0 = oy * a.stride - a.pad;
         const uint8_t* wsrc = a.wpack + static_cast<size_t>(nt) * a.num_kc * chunk_bytes;
         for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
-          const uint32_t s = it % stages;
-          const uint32_t ph = (it / stages) & 1u;
+          const uint32_t itq = a.fd_stages.div(it);
+          const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+          const uint32_t ph = itq & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
             raise_err(a.err, abort_flag, kErrWaitEmpty);
             goto producer_done;
@@ -400,8 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       uint32_t it = 0;
       int lt = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
-        const int acc = lt % nacc;
-        const uint32_t aph = (lt / nacc) & 1;
+        const int lq = nacc == 4 ? lt >> 2 : nacc == 2 ? lt >> 1 : nacc == 3 ? lt / 3 : lt;
+        const int acc = lt - lq * nacc;
+        const uint32_t aph = lq & 1;
         if (!mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag)) {
           raise_err(a.err, abort_flag, kErrWaitAccEmpty);
           break;
@@ -417,8 +422,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
             raise_err(a.err, abort_flag, kErrWaitFull);
             break;
           }
-          const uint32_t s = it % stages;
-          const uint32_t ph = (it / stages) & 1u;
+          const uint32_t itq = a.fd_stages.div(it);
+          const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+          const uint32_t ph = itq & 1u;
           ++it;
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             raise_err(a.err, abort_flag, kErrWaitFull);
@@ -506,8 +512,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
           continue;
         }
         for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
-          const uint32_t s = it % stages;
-          const uint32_t ph = (it / stages) & 1u;
+          const uint32_t itq = a.fd_stages.div(it);
+          const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+          const uint32_t ph = itq & 1u;
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             raise_err(a.err, abort_flag, kErrWaitFull);
             ok = false;
@@ -552,14 +559,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
                        (a.out_coff & 31) == 0 && (a.n_tile & 31) == 0;
     for (int t = blockIdx.x + grp * gridDim.x, lt = grp; grp < ngrp && t < total_tiles;
          t += ngrp * gridDim.x, lt += ngrp) {
-      const int acc = lt % nacc;
-      const uint32_t aph = (lt / nacc) & 1;
+      const int lq = nacc == 4 ? lt >> 2 : nacc == 2 ? lt >> 1 : nacc == 3 ? lt / 3 : lt;
+      const int acc = lt - lq * nacc;
+      const uint32_t aph = lq & 1;
       if (!mbar_wait(&acc_full[acc], aph, abort_flag)) {
         raise_err(a.err, abort_flag, kErrWaitAccFull);
         break;
       }
       tc_fence_after();
-      const int mt = t / a.n_tiles;
+      const int mt = static_cast<int>(a.fd_ntiles.div(static_cast<uint32_t>(t)));
       const int nt = t - mt * a.n_tiles;
       const int n0 = nt * a.n_tile;
       const int nvalid = min(a.n_tile, a.Co - n0);
@@ -568,9 +576,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       if (patch) {
         // Tile of 16 rows x 8 columns; TMEM lane r is pixel (r / 8, r % 8).
         const int per = a.tiles_y * a.tiles_x;
-        const int tb = mt / per;
+        const int tb = static_cast<int>(a.fd_per.div(static_cast<uint32_t>(mt)));
         const int rem = mt - tb * per;
-        const int ty = rem / a.tiles_x;
+        const int ty = static_cast<int>(a.fd_tx.div(static_cast<uint32_t>(rem)));
         const int r = q * 32 + lane;
         const int oy = ty * 16 + (r >> 3), ox = (rem - ty * a.tiles_x) * 8 + (r & 7);
         valid = oy < a.Ho && ox < a.Wo;
@@ -760,8 +768,10 @@ void i8_tiling_pair_s2(int co, I8Tiling* t) {
 void i8_tiling(int co, int ci, int kh, int kw, I8Tiling* t) {
   const int taps = kh * kw;
   if (taps == 1) {
+    // 32 or 64 padded channels: boxes of exactly that width (the TMA
+    // engine's smem writes, zero fill included, bound these convolutions).
     t->ci_pad = (ci + 31) / 32 * 32;
-    t->a_cpp = 128;
+    t->a_cpp = t->ci_pad == 32 || t->ci_pad == 64 ? t->ci_pad : 128;
   } else {
     t->ci_pad = ci <= 32 ? 32 : ci <= 64 ? 64 : (ci + 127) / 128 * 128;
     t->a_cpp = t->ci_pad <= 64 ? t->ci_pad : 128;
@@ -806,6 +816,17 @@ cudaError_t i8_init_kernel() {
   return cudaFuncSetAttribute(conv_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
 }
 
+namespace {
+void fill_fastdiv(I8Args& a, int stages) {
+  a.fd_stages = FastDiv(static_cast<uint32_t>(stages));
+  a.fd_ntiles = FastDiv(static_cast<uint32_t>(a.n_tiles));
+  a.fd_howo = FastDiv(static_cast<uint32_t>(a.Ho * a.Wo));
+  a.fd_wo = FastDiv(static_cast<uint32_t>(a.Wo));
+  a.fd_per = FastDiv(static_cast<uint32_t>(a.tiles_y > 0 && a.tiles_x > 0 ? a.tiles_y * a.tiles_x : 1));
+  a.fd_tx = FastDiv(static_cast<uint32_t>(a.tiles_x > 0 ? a.tiles_x : 1));
+}
+}  // namespace
+
 cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long long x_bstride, cudaStream_t s,
                            int sms, std::string* why) {
   if (a.Co < 16 || a.Co % 16 || a.n_tile < 16 || a.n_tile % 16 || a.n_tiles < 1 || a.n_tile * a.n_tiles < a.Co ||
@@ -847,6 +868,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
         const int smem = 1024 + wres + st * pst + tail;
         if (a.m_tiles <= 0) return cudaSuccess;
         const int grid = a.m_tiles < sms ? a.m_tiles : sms;
+        fill_fastdiv(a, st);
         return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, st);
       }
     }
@@ -880,6 +902,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
         const int smem = 1024 + wres + st * pst + static_cast<int>(kP2Plane) + tail;
         if (a.m_tiles <= 0) return cudaSuccess;
         const int grid = a.m_tiles < sms ? a.m_tiles : sms;
+        fill_fastdiv(a, st);
         return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, st);
       }
     }
@@ -918,6 +941,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
   const int grid = total < sms ? total : sms;
+  fill_fastdiv(a, stages);
   return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, stages);
 }
 

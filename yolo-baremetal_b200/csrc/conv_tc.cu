@@ -281,6 +281,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     // One thread: the resident weights once, then per tile one box copy per
     // 8-channel chunk and plane of its 18 x 10 input patch.
     if (threadIdx.x == 0) {
+      prefetch_tmap(&a.tm_hi);
+      prefetch_tmap(&a.tm_lo);
       mbar_arrive_expect_tx(wbar, wres_bytes);
       for (int kc = 0; kc < a.num_kc; ++kc)
         bulk_g2s(smem + static_cast<size_t>(kc) * chunk_bytes, a.wpack + static_cast<size_t>(kc) * chunk_bytes,
@@ -289,15 +291,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       const int per = a.tiles_y * a.tiles_x;
       uint32_t it = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
-        const uint32_t s = it % stages;
-        const uint32_t ph = (it / stages) & 1u;
+        const uint32_t itq = a.fd_stages.div(it);
+        const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+        const uint32_t ph = itq & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, wlim)) {
           raise_error(a.err, abort_flag, kErrWaitEmpty);
           break;
         }
-        const int b = t / per;
+        const int b = static_cast<int>(a.fd_per.div(static_cast<uint32_t>(t)));
         const int rem = t - b * per;
-        const int ty = rem / a.tiles_x;
+        const int ty = static_cast<int>(a.fd_tx.div(static_cast<uint32_t>(rem)));
         const int tx = rem - ty * a.tiles_x;
         uint8_t* stage = stage0 + s * stage_bytes;
         if (patch2) {
@@ -325,6 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     // im2col copy per filter tap and plane into the chunk's a_cpp-channel
     // sub-tiles, all completing on the stage's full barrier.
     if (threadIdx.x == 0) {
+      prefetch_tmap(&a.tm_hi);
+      prefetch_tmap(&a.tm_lo);
       const int taps = a.kh * a.kw;
       const int cpp = a.a_cpp;
       const int tps = cpp == 64 ? 1 : 64 / cpp;                   // taps per chunk
@@ -332,19 +337,20 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       const uint32_t sub_bytes = static_cast<uint32_t>(kBM * cpp * 2);
       uint32_t it = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-        const int mt = t / a.n_tiles;
+        const int mt = static_cast<int>(a.fd_ntiles.div(static_cast<uint32_t>(t)));
         const int nt = t - mt * a.n_tiles;
         const int m0 = mt * kBM;
-        const int b = m0 / HoWo;
+        const int b = static_cast<int>(a.fd_howo.div(static_cast<uint32_t>(m0)));
         const int r = m0 - b * HoWo;
-        const int oy = r / a.Wo;
+        const int oy = static_cast<int>(a.fd_wo.div(static_cast<uint32_t>(r)));
         const int ox = r - oy * a.Wo;
         const int w0 = ox * a.stride - a.pad;
         const int h0 = oy * a.stride - a.pad;
         const uint8_t* wsrc = a.wpack + static_cast<size_t>(nt) * a.num_kc * chunk_bytes;
         for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
-          const uint32_t s = it % stages;
-          const uint32_t ph = (it / stages) & 1u;
+          const uint32_t itq = a.fd_stages.div(it);
+          const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+          const uint32_t ph = itq & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, wlim)) {
             raise_error(a.err, abort_flag, kErrWaitEmpty);
             goto tma_producer_done;
@@ -388,16 +394,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     for (int i = 0; i < kRowsPerThread; ++i)
       row_off[i] = sw128_offset(static_cast<uint32_t>(r0 + kRowStep * i), static_cast<uint32_t>(j));
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const int mt = t / a.n_tiles;
+      const int mt = static_cast<int>(a.fd_ntiles.div(static_cast<uint32_t>(t)));
       const int nt = t - mt * a.n_tiles;
       int iy0[kRowsPerThread], ix0[kRowsPerThread];
       long long off0[kRowsPerThread], off1[kRowsPerThread];
       {
         // Row r0 of the tile, then step kRowStep pixels per row without dividing.
         const int m = mt * kBM + r0;
-        int b = m / HoWo;
+        int b = static_cast<int>(a.fd_howo.div(static_cast<uint32_t>(m)));
         int r = m - b * HoWo;
-        int oy = r / a.Wo;
+        int oy = static_cast<int>(a.fd_wo.div(static_cast<uint32_t>(r)));
         int ox = r - oy * a.Wo;
 #pragma unroll
         for (int i = 0; i < kRowsPerThread; ++i) {
@@ -422,8 +428,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       }
       const uint8_t* wsrc = a.wpack + static_cast<size_t>(nt) * a.num_kc * chunk_bytes;
       for (int kc = 0; kc < a.num_kc; ++kc) {
-        const uint32_t s = it % stages;
-        const uint32_t ph = (it / stages) & 1u;
+        const uint32_t itq = a.fd_stages.div(it);
+        const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+        const uint32_t ph = itq & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, wlim)) {
           raise_error(a.err, abort_flag, kErrWaitEmpty);
           goto producer_done;
@@ -487,14 +494,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     float mpre = 0.0f, mout = 0.0f;  // calibration statistics (a.amax)
     for (int t = blockIdx.x + grp * gridDim.x, lt = grp; grp < egroups && t < total_tiles;
          t += egroups * gridDim.x, lt += egroups) {
-      const int acc = lt % nacc;
-      const uint32_t aph = (lt / nacc) & 1;
+      const int lq = nacc == 4 ? lt >> 2 : nacc == 2 ? lt >> 1 : nacc == 3 ? lt / 3 : lt;
+      const int acc = lt - lq * nacc;
+      const uint32_t aph = lq & 1;
       if (!mbar_wait(&acc_full[acc], aph, abort_flag, wlim)) {
         raise_error(a.err, abort_flag, kErrWaitAccFull);
         break;
       }
       tc_fence_after();
-      const int mt = t / a.n_tiles;
+      const int mt = static_cast<int>(a.fd_ntiles.div(static_cast<uint32_t>(t)));
       const int nt = t - mt * a.n_tiles;
       const int n0 = nt * a.n_tile;
       const int nvalid = min(a.n_tile, a.Co - n0);
@@ -503,9 +511,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       if (patch) {
         // Tile of 16 rows x 8 columns; TMEM lane r is pixel (r / 8, r % 8).
         const int per = a.tiles_y * a.tiles_x;
-        const int tb = t / per;
+        const int tb = static_cast<int>(a.fd_per.div(static_cast<uint32_t>(t)));
         const int rem = t - tb * per;
-        const int ty = rem / a.tiles_x;
+        const int ty = static_cast<int>(a.fd_tx.div(static_cast<uint32_t>(rem)));
         const int r = q * 32 + lane;
         const int oy = ty * 16 + (r >> 3);
         const int ox = (rem - ty * a.tiles_x) * 8 + (r & 7);
@@ -518,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const int m = mt * kBM + q * 32 + lane;
         valid = m < M;
         if (valid) {
-          b = m / HoWo;
+          b = static_cast<int>(a.fd_howo.div(static_cast<uint32_t>(m)));
           p = m - b * HoWo;
         }
       }
@@ -663,8 +671,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       uint32_t it = 0;
       int lt = 0;
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++lt) {
-        const int acc = lt % nacc;
-        const uint32_t aph = (lt / nacc) & 1;
+        const int lq = nacc == 4 ? lt >> 2 : nacc == 2 ? lt >> 1 : nacc == 3 ? lt / 3 : lt;
+        const int acc = lt - lq * nacc;
+        const uint32_t aph = lq & 1;
         if (!mbar_wait(&acc_empty[acc], aph ^ 1u, abort_flag, wlim)) {
           raise_error(a.err, abort_flag, kErrWaitAccEmpty);
           break;
@@ -679,8 +688,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             raise_error(a.err, abort_flag, kErrWaitFull);
             break;
           }
-          const uint32_t s = it % stages;
-          const uint32_t ph = (it / stages) & 1u;
+          const uint32_t itq = a.fd_stages.div(it);
+          const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+          const uint32_t ph = itq & 1u;
           ++it;
           if (!mbar_wait(&full[s], ph, abort_flag, wlim)) {
             raise_error(a.err, abort_flag, kErrWaitFull);
@@ -771,8 +781,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           continue;
         }
         for (int kc = 0; kc < a.num_kc; ++kc, ++it) {
-          const uint32_t s = it % stages;
-          const uint32_t ph = (it / stages) & 1u;
+          const uint32_t itq = a.fd_stages.div(it);
+          const uint32_t s = it - itq * static_cast<uint32_t>(stages);
+          const uint32_t ph = itq & 1u;
           if (!mbar_wait(&full[s], ph, abort_flag, wlim)) {
             raise_error(a.err, abort_flag, kErrWaitFull);
             ok = false;
@@ -1054,8 +1065,11 @@ void conv_setup_tma(ConvArgs* a) {
   const int taps = a->kh * a->kw;
   if (a->K != taps * a->Ci) return;
   int cpp = 0;
-  if (taps == 1) cpp = 64;  // 64-channel boxes; channels past Ci arrive as zeros
-  else if (a->Ci == 16 || a->Ci == 32) cpp = a->Ci;
+  // 16 or 32 channels take boxes of exactly that width (the TMA engine's
+  // smem writes, zero fill included, bound the small 1x1 convolutions);
+  // otherwise 64-channel boxes, channels past Ci arriving as zeros.
+  if (a->Ci == 16 || a->Ci == 32) cpp = a->Ci;
+  else if (taps == 1) cpp = 64;
   else if (a->Ci % 64 == 0) cpp = 64;
   else return;
   // Window origins reach (extent - 1) + upper corner; the corners must give
@@ -1092,12 +1106,19 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
     return cudaErrorInvalidValue;
   const int stages = conv_stages(a);
   if (stages < 2) return cudaErrorInvalidValue;
+  ConvArgs k = a;
+  k.fd_stages = FastDiv(static_cast<uint32_t>(stages));
+  k.fd_ntiles = FastDiv(static_cast<uint32_t>(a.n_tiles));
+  k.fd_howo = FastDiv(static_cast<uint32_t>(a.Ho * a.Wo));
+  k.fd_wo = FastDiv(static_cast<uint32_t>(a.Wo));
+  k.fd_per = FastDiv(static_cast<uint32_t>(a.tiles_y > 0 && a.tiles_x > 0 ? a.tiles_y * a.tiles_x : 1));
+  k.fd_tx = FastDiv(static_cast<uint32_t>(a.tiles_x > 0 ? a.tiles_x : 1));
   const int smem = kSmemExtra + bias_bytes(a.n_tile, a.n_tiles) + conv_resident_bytes(a) + stages * conv_stage_bytes(a) +
                    conv_slack_bytes(a);
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
   const int grid = total < num_sms ? total : num_sms;
-  return launch_pdl(conv_tc_kernel, dim3(grid), dim3(kThreads), smem, s, a, stages);
+  return launch_pdl(conv_tc_kernel, dim3(grid), dim3(kThreads), smem, s, k, stages);
 }
 
 }  // namespace yb

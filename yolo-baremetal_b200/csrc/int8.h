@@ -8,6 +8,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "fastdiv.h"
+
 namespace yb {
 
 // One launch of the kind::i8 convolution.  Input: NHWC int8 view given to
@@ -41,6 +43,9 @@ struct I8Args {
   int f32_co = 0;                              // channels stored (the rest of the tile is padding)
   const float* deq = nullptr;
   int* err = nullptr;
+  // Divisors of the per-tile index arithmetic, filled by launch_conv_i8:
+  // stages, n_tiles, Ho*Wo, Wo, tiles_y*tiles_x and tiles_x.
+  FastDiv fd_stages, fd_ntiles, fd_howo, fd_wo, fd_per, fd_tx;
   alignas(64) CUtensorMap tm;
 };
 

@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include "detection.h"
+#include "fastdiv.h"
 
 namespace yb {
 
@@ -108,6 +109,9 @@ struct ConvArgs {
   // out and the kernel records an error, drains and returns.
   int debug_withhold = 0;
   uint64_t wait_ns = 0;
+  // Divisors of the per-tile index arithmetic, filled by launch_conv_tc:
+  // stages, n_tiles, Ho*Wo, Wo, tiles_y*tiles_x and tiles_x.
+  FastDiv fd_stages, fd_ntiles, fd_howo, fd_wo, fd_per, fd_tx;
   alignas(64) CUtensorMap tm_hi;
   alignas(64) CUtensorMap tm_lo;
 };

@@ -119,6 +119,12 @@ __device__ __forceinline__ void tma_im2col_4d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
+// Brings a tensor map (a __grid_constant__ kernel parameter) into the TMA
+// unit's descriptor cache ahead of the first copy that uses it.
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 // TMA load of one box of a 4-D tiled tensor map at coordinates (c0..c3),
 // innermost first; out-of-bounds elements arrive as zeros.  c0 * element
 // size must be a multiple of 16 bytes; dst 128-byte aligned.
