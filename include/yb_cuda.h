@@ -79,6 +79,13 @@ status_t yb_cuda_upload_weights(void* ctx, const model_t* m, yb_precision p, con
  * then, as ERROR_INVALID_DIMS naming the tensor. */
 status_t yb_cuda_set_int8(void* ctx, const char* const* names, const float* scales, int n);
 
+/* Fused block kernels (on by default): each Bottleneck of the C3k2 / C3k
+ * blocks whose two 3x3 convolutions map C -> C channels with C = 16 or 32
+ * runs as one launch, its intermediate kept in shared memory.  enable = 0
+ * launches every convolution separately.  Results are bit-identical either
+ * way; plans are rebuilt on the next forward. */
+status_t yb_cuda_set_fusion(void* ctx, int enable);
+
 /* INT8 calibration on the device: FP32 forwards of n images [n,3,H,W]
  * (host, float32; H, W multiples of 32) recording max |x| of every tensor the
  * INT8 plan names (conv outputs after their residual, SiLU pre-activations,

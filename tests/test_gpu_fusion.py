@@ -1,0 +1,109 @@
+"""Fused Bottleneck kernel (bottleneck_tc.cu) against the unfused graph.
+
+Every Bottleneck of the C3k2 / C3k blocks with two 3x3 C -> C convolutions
+(C = 16 or 32; layers.c:92-108 with the shortcut) runs as one launch whose
+intermediate stays in shared memory.  Its K order, split products and
+epilogue arithmetic are those of the separate convolution launches, so the
+forward must be bit-identical with fusion on and off: every stage tensor,
+the pre-sigmoid logits, the decoded boxes and the detections.  The oracle
+parity of the fused graph is covered by the model tests, which run with
+fusion on (the default)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _n_ops(m, B, H, W):
+    import yolo_b200 as yb
+
+    n = C.c_int()
+    yb.check(yb.lib().yb_cuda_profile_ops(m.ctx, B, H, W, 300, 0, None, 0, C.byref(n)), "yb_cuda_profile_ops")
+    return n.value
+
+
+def _run(m, img):
+    B = img.shape[0]
+    out = m.forward(img, stages=B == 1)
+    logits, boxes = m.head(B)
+    return out, logits, boxes
+
+
+@pytest.mark.parametrize("B,H,W", [(1, 640, 640), (3, 256, 320), (2, 96, 160), (1, 64, 96)])
+def test_fused_bitwise_equal(weights_n0, B, H, W):
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    m = yb.Model(weights_n0)
+    try:
+        img = yw.make_input(B, H, W)
+        m.set_fusion(False)
+        a, la, ba = _run(m, img)
+        n_off = _n_ops(m, B, H, W)
+        m.set_fusion(True)
+        b, lb, bb = _run(m, img)
+        n_on = _n_ops(m, B, H, W)
+        print(f"B{B} {H}x{W}: {n_off} launches unfused, {n_on} fused")
+        # YOLO26n: the two C3k bottlenecks of model.6, .13 (32 channels),
+        # .16 (16) and .19 (32) are fused.
+        assert n_off - n_on == 8
+        if B == 1:
+            assert a["stages"].keys() == b["stages"].keys()
+            for k in sorted(a["stages"]):
+                x, y = a["stages"][k], b["stages"][k]
+                if not np.array_equal(x, y):
+                    d = np.abs(x - y)
+                    idx = np.unravel_index(np.argmax(d), d.shape)
+                    print(f"{k}: {np.count_nonzero(d)} of {d.size} differ, max {d.max():.3e} at {idx} "
+                          f"(scale {np.abs(x).max():.3e})")
+            for k in a["stages"]:
+                assert np.array_equal(a["stages"][k], b["stages"][k]), k
+        assert np.array_equal(la, lb)
+        assert np.array_equal(ba, bb)
+        assert np.array_equal(a["dets"], b["dets"])
+    finally:
+        m.close()
+
+
+def test_fused_s_width(weights_s0):
+    """s width: the 32-channel bottlenecks (model.2, model.16's C3k) fuse,
+    the 64-channel ones stay separate launches; bit-identical either way."""
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    m = yb.Model(weights_s0)
+    try:
+        img = yw.make_input(2, 192, 256)
+        m.set_fusion(False)
+        a, la, _ = _run(m, img)
+        m.set_fusion(True)
+        b, lb, _ = _run(m, img)
+        assert np.array_equal(a["dets"], b["dets"])
+        assert np.array_equal(la, lb)
+    finally:
+        m.close()
+
+
+def test_fused_stream_and_int8_unaffected(weights_n0):
+    """Switching fusion rebuilds the plans of the streaming path too, and an
+    INT8 context keeps its own (unfused) graph."""
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    m = yb.Model(weights_n0)
+    try:
+        img = yw.make_input(2, 128, 128)
+        ref = m.forward(img)["dets"]
+        m.set_fusion(False)
+        assert np.array_equal(m.forward(img)["dets"], ref)
+        m.set_fusion(True)
+        scales = m.calibrate_int8(yw.make_batch(range(1000, 1002), 96, 96))
+        q1 = m.forward(img)["dets"]
+        m.set_fusion(False)
+        m.set_int8(scales)
+        q2 = m.forward(img)["dets"]
+        assert np.array_equal(q1, q2)
+    finally:
+        m.close()

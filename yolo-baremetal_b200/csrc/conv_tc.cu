@@ -588,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           if (second) load8_rw(rb + 8, a.res.plane, *reinterpret_cast<float(*)[8]>(&rv[8]));
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            if (e < 8 || second) v[e] += rv[e];
+            if (e < 8 || second) v[e] = __fadd_rn(v[e], rv[e]);
           if (stats) {
 #pragma unroll
             for (int e = 0; e < 16; ++e)
@@ -1085,7 +1085,9 @@ void conv_setup_tma(ConvArgs* a) {
 
 cudaError_t init_conv_kernel_attributes() {
   const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-  return e == cudaSuccess ? init_stem_kernel_attributes() : e;
+  if (e != cudaSuccess) return e;
+  const cudaError_t e2 = init_bottleneck_kernel_attributes();
+  return e2 == cudaSuccess ? init_stem_kernel_attributes() : e2;
 }
 
 cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {

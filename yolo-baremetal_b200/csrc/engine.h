@@ -162,6 +162,12 @@ class Engine {
   void set_int8_scales(std::map<std::string, float> s);
   bool int8_mode() const { return !i8_scales_.empty(); }
 
+  // Fused block kernels (the Bottleneck pairs of the C3k2 / C3k blocks; on
+  // by default).  Off, every convolution is its own launch; the results are
+  // bit-identical either way.  Changing it releases every plan.
+  void set_fusion(bool on);
+  bool fusion() const { return fuse_; }
+
   // FP32 forwards of n images [n,3,H,W] (host) with statistics: the INT8
   // scale table max|x| / 127 (1 for an all-zero tensor) of every tensor the
   // INT8 plan names.  Uses its own batch-1 plan, released on return.
@@ -198,6 +204,7 @@ class Engine {
   std::vector<void*> weight_allocs_;
   std::vector<std::unique_ptr<Plan>> plans_;
   std::map<std::string, float> i8_scales_;
+  bool fuse_ = true;
   float* dev_arena_ = nullptr;  // folded weights (device preparation)
   // INT8 packed operand images of the last INT8 plan: prefix -> (ptr, bytes).
   std::map<std::string, std::pair<const uint8_t*, size_t>> i8_images_;

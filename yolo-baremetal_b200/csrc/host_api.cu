@@ -449,6 +449,17 @@ extern "C" status_t yb_cuda_set_int8(void* ctx, const char* const* names, const 
   return set_int8(c, names, scales, n);
 }
 
+extern "C" status_t yb_cuda_set_fusion(void* ctx, int enable) {
+  Ctx* c = as_ctx(ctx);
+  if (!c) return ERROR_NULL_POINTER;
+  status_t st = ctx_ready(c);
+  if (st != SUCCESS) return st;
+  if ((st = drain_stream(c)) != SUCCESS) return st;
+  c->eng->set_fusion(enable != 0);
+  c->last = nullptr;
+  return SUCCESS;
+}
+
 extern "C" status_t yb_cuda_calibrate_int8(void* ctx, const float* images, int n, int H, int W, int apply,
                                            int* n_scales) {
   Ctx* c = as_ctx(ctx);

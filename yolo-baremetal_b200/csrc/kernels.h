@@ -147,6 +147,33 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms);
 // Must run once per device before the first launch_conv_tc (not under capture).
 cudaError_t init_conv_kernel_attributes();
 
+// Fused Bottleneck (bottleneck_tc.cu; layers.c:92-108 with shortcut):
+// out = in + SiLU(conv2(SiLU(conv1(in)))), both convolutions 3x3 stride 1
+// pad 1 with C -> C channels (C = 16 or 32), weights packed by
+// pack_conv_weights with n_tile = C.  Tiles of 16 x 8 output pixels,
+// tiles_y x tiles_x per image; filled by bottleneck_setup.
+struct BottleneckArgs {
+  int B = 0, H = 0, W = 0, C = 0;
+  SView in;  // channels [coff, coff + C) of the block input (also the residual)
+  SOut out;
+  const uint8_t* w1 = nullptr;
+  const uint8_t* w2 = nullptr;
+  const float* b1 = nullptr;  // [C] or null
+  const float* b2 = nullptr;
+  int* err = nullptr;         // kernel error word (bounded waits that gave up)
+  int tiles_x = 0, tiles_y = 0, tiles = 0;
+  FastDiv fd_per, fd_tx;
+  alignas(64) CUtensorMap tm_hi;
+  alignas(64) CUtensorMap tm_lo;
+};
+bool bottleneck_supported(int C);
+// Encodes the input tensor maps and the tiling; false when the view cannot
+// be read by the fused kernel (the caller then launches the two convolutions).
+bool bottleneck_setup(BottleneckArgs* a);
+cudaError_t launch_bottleneck(const BottleneckArgs& a, cudaStream_t s, int num_sms);
+// Must run once per device before the first launch_bottleneck (not under capture).
+cudaError_t init_bottleneck_kernel_attributes();
+
 // ---------------------------------------------------------------- SIMT kernels
 // First convolution, reading the NCHW host-layout fp32 input directly:
 // 3x3 stride 2 pad 1, Ci <= 4, Co in {16, 32, 64}, + bias + SiLU.

@@ -16,7 +16,7 @@ __device__ __forceinline__ uint32_t f_to_bf16_bits(float v) {
 // v - hi is exact in fp32, so hi + lo reproduces v to ~16 significant bits.
 __device__ __forceinline__ void split1(float v, uint32_t& hi, uint32_t& lo) {
   hi = f_to_bf16_bits(v);
-  lo = f_to_bf16_bits(v - bf16_bits_to_f(hi));
+  lo = f_to_bf16_bits(__fsub_rn(v, bf16_bits_to_f(hi)));
 }
 
 __device__ __forceinline__ float join1(uint16_t hi, uint16_t lo) {
@@ -50,11 +50,15 @@ __device__ __forceinline__ void load8_rw(const uint16_t* hi, long long plane, fl
 }
 
 // Splits two values at once: packed (v0 in the low half) hi and lo words.
+// The remainders use explicitly rounded subtractions so that the compiler
+// never fuses them with the multiply that produced v0 / v1 (an FMA there
+// would take the remainder of the unrounded product): the split of a value
+// is then the same in every kernel, whatever code computed it.
 __device__ __forceinline__ void split2(float v0, float v1, uint32_t& hi, uint32_t& lo) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
   hi = *reinterpret_cast<const uint32_t*>(&h);
-  const float r0 = v0 - __uint_as_float(hi << 16);
-  const float r1 = v1 - __uint_as_float(hi & 0xFFFF0000u);
+  const float r0 = __fsub_rn(v0, __uint_as_float(hi << 16));
+  const float r1 = __fsub_rn(v1, __uint_as_float(hi & 0xFFFF0000u));
   const __nv_bfloat162 l = __floats2bfloat162_rn(r0, r1);
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
@@ -70,6 +74,9 @@ __device__ __forceinline__ void store8(uint16_t* hi, long long plane, const floa
 // SiLU without branches: __expf (ex2.approx based, ~2 ulp) and __fdividef
 // (approximate division; for x below about -87 the denominator overflows
 // and the result is 0, where the exact value is below 1e-36 in magnitude).
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// Callers add to the result with __fadd_rn (never contracted into an FMA
+// with the division's multiply), so that SiLU + residual rounds the same way
+// in every kernel.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, __fadd_rn(1.0f, __expf(-x))); }
 
 }  // namespace yb

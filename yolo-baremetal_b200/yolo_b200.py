@@ -37,7 +37,7 @@ EXPORTS = {
     "detection.h": ["decode_detections"],
     "utils.h": ["timer_start", "timer_stop", "timer_elapsed_ms", "load_named_tensor", "save_named_tensor", "fold_bn"],
     "yb_cuda.h": ["yb_cuda_init", "yb_cuda_upload_weights", "yb_cuda_load_bin", "yb_cuda_forward",
-                  "yb_cuda_set_int8", "yb_cuda_get_int8_stage", "yb_cuda_calibrate_int8",
+                  "yb_cuda_set_int8", "yb_cuda_set_fusion", "yb_cuda_get_int8_stage", "yb_cuda_calibrate_int8",
                   "yb_cuda_int8_scale_entry", "yb_cuda_forward_rgb8", "yb_cuda_preprocess_rgb8",
                   "yb_cuda_forward_submit", "yb_cuda_forward_rgb8_submit", "yb_cuda_forward_wait",
                   "yb_cuda_get_detections", "yb_cuda_detections",
@@ -130,6 +130,7 @@ def lib() -> C.CDLL:
         L.yb_conv_debug_withhold.argtypes = [C.c_void_p]
         L.yb_conv_destroy.argtypes = [C.c_void_p]
         L.yb_cuda_set_int8.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.yb_cuda_set_fusion.argtypes = [C.c_void_p, C.c_int]
         L.yb_cuda_get_detections.argtypes = [C.c_void_p, C.c_float, C.c_int, C.c_void_p, C.c_void_p]
         L.yb_cuda_detections.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_int, C.c_void_p, C.c_void_p,
                                          C.c_void_p]
@@ -255,6 +256,10 @@ class Model:
         names = (C.c_char_p * max(n, 1))(*[k.encode() for k in scales])
         vals = np.ascontiguousarray(list(scales.values()) or [0.0], dtype=np.float32)
         check(lib().yb_cuda_set_int8(self.ctx, names, vals.ctypes.data, n), "yb_cuda_set_int8")
+
+    def set_fusion(self, enable: bool) -> None:
+        """Fused Bottleneck launches on (default) or off; results are bit-identical."""
+        check(lib().yb_cuda_set_fusion(self.ctx, 1 if enable else 0), "yb_cuda_set_fusion")
 
     def calibrate_int8(self, images: np.ndarray, apply: bool = True) -> dict:
         """Device calibration from FP32 forwards of images [n,3,H,W]: {name: scale}; apply switches to INT8."""
