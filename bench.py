@@ -52,12 +52,17 @@ METRIC = "images/sec YOLO26n 640² FP32 & INT8 at 1/2/4/8 B200; conv TFLOPS/TOPS
 UNIT = "images/s"
 DATA = ("synthetic: seeded U[0,1) 640x640 images (numpy PCG64), seeded random-init YOLO26n weights "
         "(Kaiming conv, BN gamma 1+-0.1, beta/mean N(0,0.1), var U(0.5,1.5)) in the converter .bin layout")
-# DRAM bytes (read + write) of the conv family per image, from an ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum) of every convolution launch
-# of one YOLO26n 640x640 forward, divided by the images of that forward.
-CONV_DRAM_BYTES_PER_IMAGE = 1637.4e6 / 64
-CONV_DRAM_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum over the 93 conv launches of one "
-                    "64-image forward, divided by 64 images and multiplied by this step's images per launch")
+# DRAM bytes (read + write) per algorithmic byte of the convolution launches:
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum, one kernel, three
+# launches) of the three longest conv_tc_kernel launches of a 16-image
+# 640x640 forward (model.1, model.2.cv2, model.3): 372.4 MB of DRAM traffic
+# for 472.1 MB of algorithmic bytes (inputs and weights read once, outputs
+# written once).  Below 1: no operand is re-read from DRAM; part of each
+# output is still in L2 when the launch ends.
+CONV_DRAM_PER_ALGO = 372.4 / 472.1
+CONV_DRAM_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the three longest conv_tc_kernel "
+                    "launches of a 16-image forward (model.1, model.2.cv2, model.3; one kernel, 1 + 2 launches): "
+                    "0.79 DRAM bytes per algorithmic byte, applied to this line's algorithmic bytes per launch")
 
 
 def peaks():
@@ -437,7 +442,7 @@ def run_ours(args):
         for d in per_kind.values():
             d["share"] = d["ms"] / all_ms
         value = world * B * args.steps / (dev_ms * 1e-3)
-        traffic = CONV_DRAM_BYTES_PER_IMAGE * B / len(conv) if CONV_DRAM_BYTES_PER_IMAGE else None
+        traffic = CONV_DRAM_PER_ALGO * conv_bytes / len(conv)
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -462,7 +467,8 @@ def run_ours(args):
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                              "frac": achieved / hbm, "traffic": traffic,
                              "traffic_source": CONV_DRAM_SOURCE,
-                             "kernel": "conv_tc_kernel (all tcgen05 convolution launches of one forward)",
+                             "kernel": "all tcgen05 convolution launches of one forward (conv_tc_kernel and the fused "
+                                       "bottleneck_tc_kernel)",
                              "launches": len(conv), "bytes_per_launch": conv_bytes / len(conv),
                              "ms_per_launch": conv_ms / len(conv), "peak_source": src},
                 "conv_tflops": {"achieved": conv_flops / (conv_ms * 1e-3) / 1e12, "peak": bf16,

@@ -372,6 +372,61 @@ cudaError_t Engine::conv_w(const std::string& prefix, bool plain, DevConv** out,
   return cudaSuccess;
 }
 
+cudaError_t Engine::conv_pair(const std::string& pa, const std::string& pb, DevConv** out, std::string* why) {
+  const std::string key = pa + "|" + pb;
+  auto it = convs_.find(key);
+  if (it != convs_.end()) {
+    *out = &it->second;
+    return cudaSuccess;
+  }
+  const HostTensor* wa = find(pa + ".conv.weight");
+  const HostTensor* ba = find(pa + ".conv.bias");
+  const HostTensor* wb = find(pb + ".conv.weight");
+  const HostTensor* bb = find(pb + ".conv.bias");
+  if (!wa || !ba || !wb || !bb) {
+    *why = "missing weights of " + key;
+    return cudaErrorInvalidValue;
+  }
+  DevConv d;
+  d.name = key;
+  d.merged = true;
+  d.co = wa->dims[0] + wb->dims[0];
+  d.ci = wa->dims[1];
+  d.kh = wa->dims[2];
+  d.kw = wa->dims[3];
+  if (wb->dims[1] != d.ci || wb->dims[2] != d.kh || wb->dims[3] != d.kw || d.ci % 8 || wa->dims[0] % 8 ||
+      wb->dims[0] % 8 || static_cast<int>(ba->count()) != wa->dims[0] || static_cast<int>(bb->count()) != wb->dims[0]) {
+    *why = "conv pair shapes at " + key;
+    return cudaErrorInvalidValue;
+  }
+  d.K = d.kh * d.kw * d.ci;
+  d.num_kc = (d.K + 63) / 64;
+  choose_n_tiling(d.co, &d.n_tile, &d.n_tiles);
+  // Both weight tensors side by side in a temporary device buffer, packed
+  // there by the same kernel as the device preparation path.
+  const size_t na = wa->count(), nb = wb->count();
+  float* tmp = nullptr;
+  cudaError_t e = cudaMalloc(&tmp, (na + nb) * 4);
+  if (e != cudaSuccess) return e;
+  e = tensor_to_device(*wa, tmp, na);
+  if (e == cudaSuccess) e = tensor_to_device(*wb, tmp + na, nb);
+  const size_t bytes = pack_conv_weights(nullptr, d.co, d.ci, d.kh, d.kw, d.n_tile, nullptr);
+  if (e == cudaSuccess) e = dev_alloc(bytes, reinterpret_cast<void**>(&d.wpack));
+  if (e == cudaSuccess) e = launch_pack_conv(tmp, d.co, d.ci, d.kh, d.kw, d.n_tile, d.wpack, bytes, stream_);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+  cudaFree(tmp);
+  if (e != cudaSuccess) return e;
+  e = dev_alloc(static_cast<size_t>(d.n_tile) * d.n_tiles * 4, reinterpret_cast<void**>(&d.bias));
+  if (e != cudaSuccess) return e;
+  cudaMemset(d.bias, 0, static_cast<size_t>(d.n_tile) * d.n_tiles * 4);
+  e = tensor_to_device(*ba, d.bias, ba->count());
+  if (e == cudaSuccess) e = tensor_to_device(*bb, d.bias + ba->count(), bb->count());
+  if (e != cudaSuccess) return e;
+  auto ins = convs_.emplace(key, d);
+  *out = &ins.first->second;
+  return cudaSuccess;
+}
+
 cudaError_t Engine::conv_narrow(DevConv* d, int n_tile, const uint8_t** wpack) {
   const int slot = n_tile == 64 ? 0 : 1;
   if (!d->wpack_n[slot]) {
@@ -735,7 +790,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     a.bias = w->bias;
     // Fewer than two waves of tiles: narrower N tiles (64 or 128 columns,
     // im2col operand mode) so that more SMs share the work.
-    if (a.n_tiles * a.m_tiles < 2 * num_sms_ && w->co >= 128 && !fout.ptr) {
+    if (a.n_tiles * a.m_tiles < 2 * num_sms_ && w->co >= 128 && !fout.ptr && !w->merged) {
       const int nt = a.m_tiles * ((w->co + 127) / 128) >= 2 * num_sms_ ? 128 : 64;
       const uint8_t* wp = nullptr;
       YB_TRY(conv_narrow(const_cast<DevConv*>(w), nt, &wp));
@@ -859,11 +914,23 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     YB_TRY(add_conv(cv1, in, 1, 0, kActSiLU, ov(catO, 0), SView()));
     const Src b = src_of(catO, c, c);
     const int cm = k1->co;
-    YB_TRY(alloc_buf(in.H, in.W, cm, &y));
     YB_TRY(alloc_buf(in.H, in.W, cm + k2->co, &catC));
-    YB_TRY(add_conv(k1, b, 1, 0, kActSiLU, ov(y), SView()));
-    YB_TRY(add_conv(k2, b, 1, 0, kActSiLU, ov(catC, cm), SView()));
-    Src cur = src_of(y, 0, cm);
+    Src cur;
+    if (fuse_ && !p->calib && nb >= 2 && k1->ci == k2->ci && k1->kh == k2->kh && k1->kw == k2->kw) {
+      // C3k's cv1 and cv2 read the same input: one launch writes both into
+      // catC, cv1's half first.  The bottleneck chain reads that half, and
+      // its last bottleneck (whose input is the previous one's output)
+      // overwrites it with the chain's result.
+      DevConv* k12;
+      YB_TRY(conv_pair(L + ".m.0.cv1", L + ".m.0.cv2", &k12, why));
+      YB_TRY(add_conv(k12, b, 1, 0, kActSiLU, ov(catC, 0), SView()));
+      cur = src_of(catC, 0, cm);
+    } else {
+      YB_TRY(alloc_buf(in.H, in.W, cm, &y));
+      YB_TRY(add_conv(k1, b, 1, 0, kActSiLU, ov(y), SView()));
+      YB_TRY(add_conv(k2, b, 1, 0, kActSiLU, ov(catC, cm), SView()));
+      cur = src_of(y, 0, cm);
+    }
     for (int i = 0; i < nb; ++i) {
       const std::string pre = L + ".m.0.m." + std::to_string(i);
       if (i == nb - 1) {

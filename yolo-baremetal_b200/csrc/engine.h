@@ -37,6 +37,9 @@ struct DevConv {
   // The same weights packed in narrower N tiles (64 and 128 columns), for
   // launches with too few M tiles to fill the SMs (packed on first use).
   uint8_t* wpack_n[2] = {nullptr, nullptr};
+  // Two convolutions of one input stacked along the output channels
+  // (conv_pair): packed only in the full tiling.
+  bool merged = false;
 };
 struct DevDw {
   float* w = nullptr;  // [9][C]
@@ -182,6 +185,9 @@ class Engine {
  private:
   const HostTensor* find(const std::string& name) const;
   cudaError_t conv_w(const std::string& prefix, bool plain, DevConv** out, std::string* why);
+  // The convolutions `a` and `b` (same input and kernel size) as one, output
+  // channels [0, co_a) from a and [co_a, co_a + co_b) from b.
+  cudaError_t conv_pair(const std::string& a, const std::string& b, DevConv** out, std::string* why);
   // Packing of `d` in N tiles of n_tile (64 or 128) columns, created on first use.
   cudaError_t conv_narrow(DevConv* d, int n_tile, const uint8_t** wpack);
   cudaError_t dw_w(const std::string& prefix, DevDw** out, std::string* why);
