@@ -1,7 +1,8 @@
 """Fused block kernels against the unfused graph.
 
-Every Bottleneck of the C3k2 / C3k blocks with two 3x3 C -> C convolutions
-(C = 16 or 32; layers.c:92-108 with the shortcut) runs as one launch whose
+Every Bottleneck of the C3k2 / C3k blocks whose 3x3 convolutions map
+C -> CM -> C channels with (C, CM) = (16, 16), (32, 32), (32, 16) or
+(16, 8) (layers.c:92-108 with the shortcut) runs as one launch whose
 intermediate stays in shared memory (bottleneck_tc.cu), and the two 1x1
 convolutions of each C3k that read the same input (layers.c:156-189) run as
 one launch with the output channels of both.  K order, split products and
@@ -49,10 +50,11 @@ def test_fused_bitwise_equal(weights_n0, B, H, W):
         n_on = _n_ops(m, B, H, W)
         print(f"B{B} {H}x{W}: {n_off} launches unfused, {n_on} fused")
         # YOLO26n: the two C3k bottlenecks of model.6, .13 (32 channels),
-        # .16 (16) and .19 (32) are fused (8 launches fewer), and the cv1 /
-        # cv2 pair of each of the five C3k blocks (model.6, .8, .13, .16,
-        # .19) is one launch (5 fewer).
-        assert n_off - n_on == 13
+        # .16 (16) and .19 (32) and the e = 0.5 Bottlenecks of model.2
+        # (16 -> 8 -> 16) and model.4 (32 -> 16 -> 32) are fused (10
+        # launches fewer), and the cv1 / cv2 pair of each of the five C3k
+        # blocks (model.6, .8, .13, .16, .19) is one launch (5 fewer).
+        assert n_off - n_on == 15
         if B == 1:
             assert a["stages"].keys() == b["stages"].keys()
             for k in sorted(a["stages"]):

@@ -1,6 +1,7 @@
 // Fused Bottleneck for sm_100a: y = x + SiLU(conv2(SiLU(conv1(x)))) with two
-// 3x3 stride-1 pad-1 convolutions of C -> C channels (C = 16 or 32), in one
-// persistent kernel.  Replaces the pair of conv_block_forward calls and the
+// 3x3 stride-1 pad-1 convolutions, conv1 C -> CM and conv2 CM -> C channels
+// ((C, CM) = (16, 16), (32, 32), (32, 16) or (16, 8): the C3k Bottlenecks
+// and the e = 0.5 Bottlenecks of C3k2), in one persistent kernel.  Replaces the pair of conv_block_forward calls and the
 // residual add of bottleneck_forward (layers.c:92-108) inside the C3k2 and
 // C3k blocks (layers.c:110-189, model.c:208-283, :415-557).
 //
@@ -51,23 +52,28 @@ constexpr uint32_t kInChunk = 4608;                   // box + slack read by dis
 constexpr uint32_t kMidChunk = 2944;                  // 18 x 10 x 16 bytes, 128-byte multiple
 constexpr uint32_t kSmemLimit = 232448;
 
-__host__ __device__ constexpr uint32_t w_bytes(int c) {
-  return static_cast<uint32_t>((9 * c + 63) / 64) * static_cast<uint32_t>(c) * 256u;
+// N tile of a convolution with co output channels (choose_n_tiling for co <= 256).
+__host__ __device__ constexpr int ntile(int co) { return (co + 15) / 16 * 16; }
+// Packed weights of a 3x3 convolution ci -> co: 64-wide K chunks of ntile(co)
+// hi rows then ntile(co) lo rows of 128 bytes.
+__host__ __device__ constexpr uint32_t w_bytes(int ci, int co) {
+  return static_cast<uint32_t>((9 * ci + 63) / 64) * static_cast<uint32_t>(ntile(co)) * 256u;
 }
 __host__ __device__ constexpr uint32_t in_stage_bytes(int c) { return 2u * static_cast<uint32_t>(c / 8) * kInChunk; }
-__host__ __device__ constexpr uint32_t mid_stage_bytes(int c) { return 2u * static_cast<uint32_t>(c / 8) * kMidChunk; }
-__host__ __device__ constexpr uint32_t smem_bytes(int c) {
-  return 1024u + 2u * w_bytes(c) + 2u * in_stage_bytes(c) + 2u * mid_stage_bytes(c) + 256u + 2u * 4u * c;
+__host__ __device__ constexpr uint32_t mid_stage_bytes(int cm) { return 2u * static_cast<uint32_t>(cm / 8) * kMidChunk; }
+__host__ __device__ constexpr uint32_t smem_bytes(int c, int cm) {
+  return 1024u + w_bytes(c, cm) + w_bytes(cm, c) + 2u * in_stage_bytes(c) + 2u * mid_stage_bytes(cm) + 256u +
+         4u * static_cast<uint32_t>(ntile(cm) + c);
 }
-static_assert(smem_bytes(32) <= kSmemLimit, "the 32-channel fused bottleneck exceeds the 227 KB opt-in limit");
+static_assert(smem_bytes(32, 32) <= kSmemLimit, "the 32-channel fused bottleneck exceeds the 227 KB opt-in limit");
 
 // One tile's 9 taps x CBS 16-channel K steps, stacked split products, fully
 // unrolled (compile-time descriptor offsets; see the unfused kernel).  ROWW is
 // the operand's pixel row width, CHUNK the byte stride between its 8-channel
-// chunks; the weights are CBS * 16 output rows per 64-wide K chunk.
-template <int CBS, int ROWW, uint32_t CHUNK>
+// chunks; the weights are NT hi + NT lo rows per 64-wide K chunk.
+template <int CBS, int ROWW, uint32_t CHUNK, int NT>
 __device__ __forceinline__ void window_mma(uint32_t d, uint64_t ah, uint64_t al, uint64_t bh, uint32_t idesc) {
-  constexpr uint64_t chunk_units = static_cast<uint64_t>(CBS) * 16u * 256u / 16u;
+  constexpr uint64_t chunk_units = static_cast<uint64_t>(NT) * 256u / 16u;
 #pragma unroll
   for (int tap = 0; tap < 9; ++tap) {
 #pragma unroll
@@ -81,6 +87,29 @@ __device__ __forceinline__ void window_mma(uint32_t d, uint64_t ah, uint64_t al,
   }
 }
 
+// conv2 with 8 intermediate channels (16 bytes per pixel and plane): two
+// taps per 16-wide K step, as the unfused kernel's 8-channel patch mode --
+// the A descriptor's second core matrix is the next tap's window (LBO = the
+// distance between the windows), tap 8 pairs with zero weights and reads the
+// zeroed pad after the box.  hb / lb: hi / lo intermediate descriptors with
+// LBO 0; K ordered (tap, channel), so the weights hold the two taps back to
+// back.
+template <int NT>
+__device__ __forceinline__ void pair_mma(uint32_t d, uint64_t hb, uint64_t lb, uint64_t bh, uint32_t idesc) {
+  constexpr uint64_t chunk_units = static_cast<uint64_t>(NT) * 256u / 16u;
+#pragma unroll
+  for (int s2 = 0; s2 < 5; ++s2) {
+    const int t0 = 2 * s2, t1 = t0 + 1 < 9 ? t0 + 1 : t0;
+    const uint32_t o0 = static_cast<uint32_t>(((t0 / 3) * kMidW + t0 % 3) * 16);
+    const uint32_t o1 = static_cast<uint32_t>(((t1 / 3) * kMidW + t1 % 3) * 16);
+    const uint32_t lbo = t1 == t0 ? 16u : o1 - o0;
+    const uint64_t off = static_cast<uint64_t>(o0 >> 4) | (static_cast<uint64_t>(lbo >> 4) << 16);
+    const uint64_t bo = static_cast<uint64_t>(s2 >> 2) * chunk_units + static_cast<uint64_t>((s2 & 3) * 2);
+    tc_mma_bf16(d, hb + off, bh + bo, idesc, s2 != 0 ? 1u : 0u);
+    tc_mma_bf16(d, lb + off, bh + bo, idesc, 1u);
+  }
+}
+
 __device__ __forceinline__ void raise_error(int* err, volatile int* abort_flag, int code) {
   *abort_flag = 1;
   if (err) atomicCAS(err, 0, code);
@@ -90,22 +119,27 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-template <int C>
+template <int C, int CM>
 __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid_constant__ BottleneckArgs a) {
-  constexpr int NCH = C / 8;    // 8-channel chunks
-  constexpr int CBS = C / 16;   // 16-channel K steps per tap
-  constexpr uint32_t WB = w_bytes(C);
+  constexpr int NCH = C / 8;     // 8-channel chunks of the input and output
+  constexpr int NCM = CM / 8;    // 8-channel chunks of the intermediate
+  constexpr int CBS = C / 16;    // 16-channel K steps per tap of conv1
+  constexpr int N1 = ntile(CM);  // conv1 N tile (8 intermediate channels: 16, upper half zero weights)
+  constexpr int N2 = C;          // conv2 N tile
+  constexpr uint32_t WB1 = w_bytes(C, CM);
+  constexpr uint32_t WB2 = w_bytes(CM, C);
   constexpr uint32_t INS = in_stage_bytes(C);
-  constexpr uint32_t MIDS = mid_stage_bytes(C);
-  // TMEM: acc1 (two M tiles of 2C stacked columns) per slot, then acc2 (2C).
-  constexpr uint32_t kAcc1 = 4u * C, kAcc2Base = 8u * C, kAcc2 = 2u * C;
-  constexpr uint32_t kCols = 12u * C <= 256u ? 256u : 512u;
+  constexpr uint32_t MIDS = mid_stage_bytes(CM);
+  // TMEM: acc1 (two M tiles of 2 N1 stacked columns) per slot, then acc2 (2 N2).
+  constexpr uint32_t kAcc1 = 4u * N1, kAcc2Base = 8u * N1, kAcc2 = 2u * N2;
+  constexpr uint32_t kCols = 8u * N1 + 4u * N2 <= 256u ? 256u : 512u;
+  static_assert(8u * N1 + 4u * N2 <= 512u, "accumulators exceed tensor memory");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* w1 = smem;
-  uint8_t* w2 = smem + WB;
-  uint8_t* inb = smem + 2 * WB;
+  uint8_t* w2 = smem + WB1;
+  uint8_t* inb = smem + WB1 + WB2;
   uint8_t* midb = inb + 2 * INS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(midb + 2 * MIDS);
   uint64_t* in_full = bars;        // [2]
@@ -120,14 +154,20 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
   uint64_t* drain = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* sb1 = reinterpret_cast<float*>(midb + 2 * MIDS + 256);
-  float* sb2 = sb1 + C;
+  float* sb1 = reinterpret_cast<float*>(midb + 2 * MIDS + 256);  // [N1]
+  float* sb2 = sb1 + N1;                                          // [C]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < C; i += kThreads) {
-    sb1[i] = a.b1 ? a.b1[i] : 0.0f;
-    sb2[i] = a.b2 ? a.b2[i] : 0.0f;
+  for (int i = threadIdx.x; i < N1; i += kThreads) sb1[i] = (a.b1 && i < CM) ? a.b1[i] : 0.0f;
+  for (int i = threadIdx.x; i < C; i += kThreads) sb2[i] = a.b2 ? a.b2[i] : 0.0f;
+  if (CM == 8) {
+    // conv2's paired tap 8 reads the pixel after the intermediate box
+    // (against zero weights): keep that pad zero so no stale NaN survives.
+    for (int i = threadIdx.x; i < 2 * 2 * 4; i += kThreads) {
+      uint8_t* pad = midb + (i >> 3) * MIDS + ((i >> 2) & 1) * kMidChunk + kMidH * kMidW * 16 + (i & 3) * 16;
+      *reinterpret_cast<uint4*>(pad) = make_uint4(0u, 0u, 0u, 0u);
+    }
   }
   // The slack after each input box is read only by discarded conv1 rows;
   // zero it once so that those rows stay finite.
@@ -164,9 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
   if (threadIdx.x == 0) {
     // The packed weights are written at plan build: load them before
     // waiting on the previous kernel.
-    mbar_arrive_expect_tx(wbar, 2u * WB);
-    bulk_g2s(w1, a.w1, WB, wbar);
-    bulk_g2s(w2, a.w2, WB, wbar);
+    mbar_arrive_expect_tx(wbar, WB1 + WB2);
+    bulk_g2s(w1, a.w1, WB1, wbar);
+    bulk_g2s(w2, a.w2, WB2, wbar);
     pdl_trigger();
   }
   pdl_wait();
@@ -203,7 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
   } else if (warp == 1) {
     // -------------------------------------------------------- UMMA issue
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(128, 2 * C);
+      const uint32_t idesc1 = idesc_bf16_f32(128, 2 * N1);
+      const uint32_t idesc2 = idesc_bf16_f32(128, 2 * N2);
       const uint64_t bw1 = sw128_kmajor_desc(smem_u32(w1));
       const uint64_t bw2 = sw128_kmajor_desc(smem_u32(w2));
       bool ok = mbar_wait(wbar, 0, abort_flag, wlim);
@@ -227,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
           const uint64_t ah = kmajor_desc_noswizzle(pa, kInChunk, 128);
           const uint64_t al = kmajor_desc_noswizzle(pa + NCH * kInChunk, kInChunk, 128);
           // M tile m starts 128 pixels (2048 bytes, 128 units) further.
-          window_mma<CBS, kInW, kInChunk>(tmem_base + s * kAcc1, ah, al, bw1, idesc);
-          window_mma<CBS, kInW, kInChunk>(tmem_base + s * kAcc1 + 2 * C, ah + 128, al + 128, bw1, idesc);
+          window_mma<CBS, kInW, kInChunk, N1>(tmem_base + s * kAcc1, ah, al, bw1, idesc1);
+          window_mma<CBS, kInW, kInChunk, N1>(tmem_base + s * kAcc1 + 2 * N1, ah + 128, al + 128, bw1, idesc1);
           tc_commit(&in_empty[s]);
           tc_commit(&acc1_full[s]);
         }
@@ -246,9 +287,16 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
           }
           tc_fence_after();
           const uint32_t pm = smem_u32(midb + s * MIDS);
-          const uint64_t mh = kmajor_desc_noswizzle(pm, kMidChunk, kMidW * 16);
-          const uint64_t ml = kmajor_desc_noswizzle(pm + NCH * kMidChunk, kMidChunk, kMidW * 16);
-          window_mma<CBS, kMidW, kMidChunk>(tmem_base + kAcc2Base + s * kAcc2, mh, ml, bw2, idesc);
+          if (CM == 8) {
+            const uint64_t hb = kmajor_desc_noswizzle(pm, 0, kMidW * 16);
+            const uint64_t lb = kmajor_desc_noswizzle(pm + kMidChunk, 0, kMidW * 16);
+            pair_mma<N2>(tmem_base + kAcc2Base + s * kAcc2, hb, lb, bw2, idesc2);
+          } else {
+            const uint64_t mh = kmajor_desc_noswizzle(pm, kMidChunk, kMidW * 16);
+            const uint64_t ml = kmajor_desc_noswizzle(pm + NCM * kMidChunk, kMidChunk, kMidW * 16);
+            window_mma<(CM >= 16 ? CM / 16 : 1), kMidW, kMidChunk, N2>(tmem_base + kAcc2Base + s * kAcc2, mh, ml, bw2,
+                                                                      idesc2);
+          }
           tc_commit(&mid_empty[s]);
           tc_commit(&acc2_full[s]);
         }
@@ -290,13 +338,13 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
       const int gy = ty * 16 - 1 + py, gx = tx * 8 - 1 + px;
       const bool inside = static_cast<unsigned>(gy) < static_cast<unsigned>(a.H) &&
                           static_cast<unsigned>(gx) < static_cast<unsigned>(a.W);
-      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + s * kAcc1 + m * 2 * C;
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + s * kAcc1 + m * 2 * N1;
       const uint32_t mid = smem_u32(midb + s * MIDS) + mid_off;
 #pragma unroll
-      for (int u = 0; u < CBS; ++u) {
+      for (int u = 0; u < N1 / 16; ++u) {
         uint32_t r[16], r2[16];
         tc_ld_32x32b_x16(tb + u * 16, r);
-        tc_ld_32x32b_x16(tb + C + u * 16, r2);
+        tc_ld_32x32b_x16(tb + N1 + u * 16, r2);
         tc_wait_ld();
         tc_ld_dep(r);
         tc_ld_dep(r2);
@@ -313,9 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
         if (keep) {
           const uint32_t c0 = static_cast<uint32_t>(2 * u) * kMidChunk;
           st_shared_v4(mid + c0, hw[0], hw[1], hw[2], hw[3]);
-          st_shared_v4(mid + c0 + kMidChunk, hw[4], hw[5], hw[6], hw[7]);
-          st_shared_v4(mid + NCH * kMidChunk + c0, lw[0], lw[1], lw[2], lw[3]);
-          st_shared_v4(mid + NCH * kMidChunk + c0 + kMidChunk, lw[4], lw[5], lw[6], lw[7]);
+          st_shared_v4(mid + NCM * kMidChunk + c0, lw[0], lw[1], lw[2], lw[3]);
+          if (CM > 8) {
+            st_shared_v4(mid + c0 + kMidChunk, hw[4], hw[5], hw[6], hw[7]);
+            st_shared_v4(mid + NCM * kMidChunk + c0 + kMidChunk, lw[4], lw[5], lw[6], lw[7]);
+          }
         }
       }
       // The intermediate is read by the tensor cores (async proxy).
@@ -370,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
       for (int u = 0; u < CBS; ++u) {
         uint32_t rr[16], r2[16];
         tc_ld_32x32b_x16(tb + u * 16, rr);
-        tc_ld_32x32b_x16(tb + C + u * 16, r2);
+        tc_ld_32x32b_x16(tb + N2 + u * 16, r2);
         tc_wait_ld();
         tc_ld_dep(rr);
         tc_ld_dep(r2);
@@ -459,11 +509,13 @@ bool encode_in_plane(CUtensorMap* map, const BottleneckArgs& a, const uint16_t* 
 
 }  // namespace
 
-bool bottleneck_supported(int C) { return C == 16 || C == 32; }
+bool bottleneck_supported(int C, int CM) {
+  return (C == 16 && (CM == 16 || CM == 8)) || (C == 32 && (CM == 32 || CM == 16));
+}
 
 bool bottleneck_setup(BottleneckArgs* a) {
-  if (!bottleneck_supported(a->C) || a->B < 1 || a->H < 1 || a->W < 1 || !a->in.hi || !a->out.hi || !a->w1 ||
-      !a->w2)
+  if (!bottleneck_supported(a->C, a->CM) || a->B < 1 || a->H < 1 || a->W < 1 || !a->in.hi || !a->out.hi ||
+      !a->w1 || !a->w2)
     return false;
   if (a->in.coff % 8 || a->out.coff % 8 || a->out.cstride % 8 || a->out.bstride % 8 || a->out.plane % 8 ||
       reinterpret_cast<uintptr_t>(a->out.hi) % 16)
@@ -480,24 +532,34 @@ bool bottleneck_setup(BottleneckArgs* a) {
   return true;
 }
 
+template <int C, int CM>
+cudaError_t set_attr() {
+  return cudaFuncSetAttribute(bottleneck_tc_kernel<C, CM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(smem_bytes(C, CM)));
+}
+
 cudaError_t init_bottleneck_kernel_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(bottleneck_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem_bytes(16)));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(bottleneck_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem_bytes(32)));
+  cudaError_t e = set_attr<16, 16>();
+  if (e == cudaSuccess) e = set_attr<16, 8>();
+  if (e == cudaSuccess) e = set_attr<32, 32>();
+  if (e == cudaSuccess) e = set_attr<32, 16>();
   return e;
 }
 
+template <int C, int CM>
+cudaError_t launch_c(const BottleneckArgs& a, cudaStream_t s, int grid) {
+  return launch_pdl(bottleneck_tc_kernel<C, CM>, dim3(grid), dim3(kThreads), static_cast<int>(smem_bytes(C, CM)), s,
+                    a);
+}
+
 cudaError_t launch_bottleneck(const BottleneckArgs& a, cudaStream_t s, int num_sms) {
-  if (!bottleneck_supported(a.C) || a.tiles != a.B * a.tiles_x * a.tiles_y || a.tiles_x != (a.W + 7) / 8 ||
+  if (!bottleneck_supported(a.C, a.CM) || a.tiles != a.B * a.tiles_x * a.tiles_y || a.tiles_x != (a.W + 7) / 8 ||
       a.tiles_y != (a.H + 15) / 16)
     return cudaErrorInvalidValue;
   if (a.tiles <= 0) return cudaSuccess;
   const int grid = a.tiles < num_sms ? a.tiles : num_sms;
-  if (a.C == 16)
-    return launch_pdl(bottleneck_tc_kernel<16>, dim3(grid), dim3(kThreads), static_cast<int>(smem_bytes(16)), s, a);
-  return launch_pdl(bottleneck_tc_kernel<32>, dim3(grid), dim3(kThreads), static_cast<int>(smem_bytes(32)), s, a);
+  if (a.C == 16) return a.CM == 16 ? launch_c<16, 16>(a, s, grid) : launch_c<16, 8>(a, s, grid);
+  return a.CM == 32 ? launch_c<32, 32>(a, s, grid) : launch_c<32, 16>(a, s, grid);
 }
 
 }  // namespace yb

@@ -833,22 +833,24 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     return add_conv(w, src_of(in, 0, in.C), 2, (w->kh - 1) / 2, kActSiLU, ov(*out), SView());
   };
   // Bottleneck (layers.c:92-108): cv1+SiLU -> cv2+SiLU (+ input).  With
-  // 3x3 C -> C convolutions of 16 or 32 channels and a shortcut, one fused
-  // launch (bottleneck_tc.cu, bit-identical to the pair below) unless the
-  // plan gathers calibration statistics or fusion is switched off.
+  // 3x3 convolutions C -> CM -> C ((C, CM) in bottleneck_supported) and a
+  // shortcut, one fused launch (bottleneck_tc.cu, bit-identical to the pair
+  // below) unless the plan gathers calibration statistics or fusion is
+  // switched off.
   auto bottleneck = [&](const std::string& pre, const Src& in, SOut out, bool shortcut) -> cudaError_t {
     DevConv *w1, *w2;
     YB_TRY(conv(pre + ".cv1", &w1));
     YB_TRY(conv(pre + ".cv2", &w2));
-    const int c = w1->co;
+    const int c = w1->ci, cm = w1->co;
     if (fuse_ && !p->calib && shortcut && !in.c1 && !in.lg0 && in.c0 == c && w1->kh == 3 && w1->kw == 3 &&
-        w2->kh == 3 && w2->kw == 3 && w1->ci == c && w2->ci == c && w2->co == c && bottleneck_supported(c) &&
-        w1->n_tiles == 1 && w1->n_tile == c && w2->n_tiles == 1 && w2->n_tile == c) {
+        w2->kh == 3 && w2->kw == 3 && w2->ci == cm && w2->co == c && bottleneck_supported(c, cm) &&
+        w1->n_tiles == 1 && w1->n_tile == (cm + 15) / 16 * 16 && w2->n_tiles == 1 && w2->n_tile == c) {
       BottleneckArgs ba;
       ba.B = B;
       ba.H = in.H;
       ba.W = in.W;
       ba.C = c;
+      ba.CM = cm;
       ba.in = in.v0;
       ba.out = out;
       ba.w1 = w1->wpack;
@@ -859,7 +861,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       if (bottleneck_setup(&ba)) {
         const double pix = static_cast<double>(B) * in.H * in.W;
         const int sms = num_sms_;
-        add_op(kOpConv, 2.0 * 2.0 * pix * c * 9.0 * c, 4.0 * (2.0 * pix * c + 2.0 * c * (9.0 * c + 1.0)),
+        add_op(kOpConv, 2.0 * 2.0 * pix * c * 9.0 * cm, 4.0 * (2.0 * pix * c + 2.0 * cm * (9.0 * c + 1.0)),
                [ba, sms](cudaStream_t s) { return launch_bottleneck(ba, s, sms); });
         return cudaSuccess;
       }

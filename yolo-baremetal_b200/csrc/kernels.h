@@ -149,11 +149,12 @@ cudaError_t init_conv_kernel_attributes();
 
 // Fused Bottleneck (bottleneck_tc.cu; layers.c:92-108 with shortcut):
 // out = in + SiLU(conv2(SiLU(conv1(in)))), both convolutions 3x3 stride 1
-// pad 1 with C -> C channels (C = 16 or 32), weights packed by
-// pack_conv_weights with n_tile = C.  Tiles of 16 x 8 output pixels,
+// pad 1, conv1 C -> CM and conv2 CM -> C channels ((C, CM) = (16, 16),
+// (32, 32), (32, 16) or (16, 8)), weights packed by pack_conv_weights in
+// their full N tiling (choose_n_tiling).  Tiles of 16 x 8 output pixels,
 // tiles_y x tiles_x per image; filled by bottleneck_setup.
 struct BottleneckArgs {
-  int B = 0, H = 0, W = 0, C = 0;
+  int B = 0, H = 0, W = 0, C = 0, CM = 0;
   SView in;  // channels [coff, coff + C) of the block input (also the residual)
   SOut out;
   const uint8_t* w1 = nullptr;
@@ -166,7 +167,7 @@ struct BottleneckArgs {
   alignas(64) CUtensorMap tm_hi;
   alignas(64) CUtensorMap tm_lo;
 };
-bool bottleneck_supported(int C);
+bool bottleneck_supported(int C, int CM);
 // Encodes the input tensor maps and the tiling; false when the view cannot
 // be read by the fused kernel (the caller then launches the two convolutions).
 bool bottleneck_setup(BottleneckArgs* a);
