@@ -92,24 +92,39 @@ def test_fused_s_width(weights_s0):
         m.close()
 
 
-def test_fused_stream_and_int8_unaffected(weights_n0):
-    """Switching fusion rebuilds the plans of the streaming path too, and an
-    INT8 context keeps its own (unfused) graph."""
+def test_fused_int8_bitwise_equal(weights_n0):
+    """INT8 graph: the Bottlenecks run as bottleneck_i8_kernel (kind::i8,
+    the int8 intermediate in shared memory); every int8 stage tensor, the
+    dequantised logits and the detections are identical with fusion on and
+    off, and switching fusion rebuilds the plans of the streaming path."""
     import yb_weights as yw
     import yolo_b200 as yb
 
     m = yb.Model(weights_n0)
     try:
-        img = yw.make_input(2, 128, 128)
+        img = yw.make_input(2, 256, 320)
+        scales = m.calibrate_int8(yw.make_batch(range(1000, 1002), 96, 96), apply=False)
+        m.set_int8(scales)
+        m.set_fusion(False)
+        a = m.forward(img)["dets"]
+        la, _ = m.head(2)
+        sa = [m.int8_stage(i)[0] for i in range(23)]
+        n_off = _n_ops(m, 2, 256, 320)
+        m.set_fusion(True)
+        b = m.forward(img)["dets"]
+        lb, _ = m.head(2)
+        sb = [m.int8_stage(i)[0] for i in range(23)]
+        n_on = _n_ops(m, 2, 256, 320)
+        print(f"INT8: {n_off} launches unfused, {n_on} fused")
+        # The ten Bottlenecks of model.2, .4, .6, .13, .16 and .19.
+        assert n_off - n_on == 10
+        for i in range(23):
+            assert np.array_equal(sa[i], sb[i]), i
+        assert np.array_equal(la, lb)
+        assert np.array_equal(a, b)
+        m.set_int8(None)
         ref = m.forward(img)["dets"]
         m.set_fusion(False)
         assert np.array_equal(m.forward(img)["dets"], ref)
-        m.set_fusion(True)
-        scales = m.calibrate_int8(yw.make_batch(range(1000, 1002), 96, 96))
-        q1 = m.forward(img)["dets"]
-        m.set_fusion(False)
-        m.set_int8(scales)
-        q2 = m.forward(img)["dets"]
-        assert np.array_equal(q1, q2)
     finally:
         m.close()

@@ -256,9 +256,10 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     long long cstride = 0, bstride = 0;
   };
   // Convolution named P (P.conv.* or, plain, P.*) from `in` into `out`
-  // (or dequantised into f32 when f32.ptr).
+  // (or dequantised into f32 when f32.ptr).  With `cap` the launch
+  // arguments are returned there instead of adding the launch.
   auto conv = [&](const std::string& P, bool plain, const QT& out, const QT& in, int stride, int pad, bool act,
-                  const QT* res, F32Out f32 = F32Out()) -> cudaError_t {
+                  const QT* res, F32Out f32 = F32Out(), I8Args* cap = nullptr) -> cudaError_t {
     const HostTensor* w = find(P + (plain ? ".weight" : ".conv.weight"));
     const HostTensor* b = find(P + (plain ? ".bias" : ".conv.bias"));
     if (!w || w->ndim != 4) return fail("int8: missing weight " + P);
@@ -385,6 +386,11 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
         return fail("int8: residual ratio out of range in " + P);
     }
     a.err = d_err_;
+    if (cap) {
+      *cap = a;
+      if (!f32.ptr) out.set_scale(s_out);
+      return cudaSuccess;
+    }
     const int8_t* x = in.ptr();
     const long long xc = in.cstride, xb = in.bstride;
     const double px = static_cast<double>(B) * a.Ho * a.Wo;
@@ -463,12 +469,53 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     const HostTensor* t = find(n);
     return t ? t->dims[0] : 0;
   };
+  // Bottleneck (layers.c:92-108).  With 3x3 convolutions C -> CM -> C of
+  // the shapes bottleneck_i8.cu fuses and a shortcut, one launch keeping the
+  // int8 intermediate in shared memory (bit-identical) unless fusion is off.
   auto bottleneck = [&](const std::string& P, const QT& out, const QT& in, bool shortcut) -> cudaError_t {
     const HostTensor* w1 = find(P + ".cv1.conv.weight");
     const HostTensor* w2 = find(P + ".cv2.conv.weight");
     if (!w1 || !w2) return fail("int8: missing " + P);
     QT t;
     YB_TRY(tensor(w1->dims[0], in.H, in.W, &t));
+    const int C = in.C, CM = w1->dims[0];
+    if (fuse_ && shortcut && w1->ndim == 4 && w2->ndim == 4 && w1->dims[1] == C && w1->dims[2] == 3 &&
+        w1->dims[3] == 3 && w2->dims[0] == C && w2->dims[1] == CM && w2->dims[2] == 3 && w2->dims[3] == 3 &&
+        out.C == C && out.H == in.H && out.W == in.W && i8_bottleneck_supported(C, CM)) {
+      I8Args a1, a2;
+      YB_TRY(conv(P + ".cv1", false, t, in, 1, 1, true, nullptr, F32Out(), &a1));
+      YB_TRY(conv(P + ".cv2", false, out, t, 1, 1, true, &in, F32Out(), &a2));
+      I8BottleneckArgs f;
+      f.B = B;
+      f.H = in.H;
+      f.W = in.W;
+      f.C = C;
+      f.CM = CM;
+      f.in = in.ptr();
+      f.in_cstride = in.cstride;
+      f.in_bstride = in.bstride;
+      f.out = out.ptr();
+      f.out_cstride = out.cstride;
+      f.out_bstride = out.bstride;
+      f.w1 = a1.wpack;
+      f.b1 = a1.bias;
+      f.m1 = a1.mult;
+      f.s1 = a1.shift;
+      f.lut1 = a1.lut;
+      f.w2 = a2.wpack;
+      f.b2 = a2.bias;
+      f.m2 = a2.mult;
+      f.s2 = a2.shift;
+      f.lut2 = a2.lut;
+      f.res_mult = a2.res_mult;
+      f.res_shift = a2.res_shift;
+      f.err = d_err_;
+      if (a1.n_tiles != 1 || a2.n_tiles != 1 || !i8_bottleneck_setup(&f)) return fail("int8: fused bottleneck " + P);
+      const double px = static_cast<double>(B) * in.H * in.W;
+      add_op(kOpConv, 2.0 * 2.0 * px * C * CM * 9.0, 2.0 * px * C + 18.0 * C * CM,
+             [f, sms](cudaStream_t st) { return launch_i8_bottleneck(f, st, sms); });
+      return cudaSuccess;
+    }
     YB_TRY(conv(P + ".cv1", false, t, in, 1, (w1->dims[2] - 1) / 2, true, nullptr));
     return conv(P + ".cv2", false, out, t, 1, (w2->dims[2] - 1) / 2, true, shortcut ? &in : nullptr);
   };

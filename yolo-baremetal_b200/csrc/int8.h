@@ -49,6 +49,36 @@ struct I8Args {
   alignas(64) CUtensorMap tm;
 };
 
+// Fused INT8 Bottleneck (bottleneck_i8.cu): two 3x3 stride-1 pad-1
+// convolutions C -> CM -> C ((C, CM) = (16, 16), (32, 32), (32, 16) or
+// (16, 8)) with SiLU tables, conv2 adding the residual term of the block
+// input; bit-identical to the two conv_i8_kernel launches.  w1 / w2 and the
+// per-channel arrays are those the INT8 graph builds for the two
+// convolutions (one N tile each).  in / out: NHWC int8 at their first
+// channel; filled by i8_bottleneck_setup.
+struct I8BottleneckArgs {
+  int B = 0, H = 0, W = 0, C = 0, CM = 0;
+  const int8_t* in = nullptr;
+  long long in_cstride = 0, in_bstride = 0;
+  int8_t* out = nullptr;
+  long long out_cstride = 0, out_bstride = 0;
+  const uint8_t* w1 = nullptr;
+  const int32_t *b1 = nullptr, *m1 = nullptr, *s1 = nullptr;
+  const int8_t* lut1 = nullptr;
+  const uint8_t* w2 = nullptr;
+  const int32_t *b2 = nullptr, *m2 = nullptr, *s2 = nullptr;
+  const int8_t* lut2 = nullptr;
+  int res_mult = 0, res_shift = 1;
+  int* err = nullptr;
+  int tiles_x = 0, tiles_y = 0, tiles = 0;
+  FastDiv fd_per, fd_tx;
+  alignas(64) CUtensorMap tm;
+};
+bool i8_bottleneck_supported(int C, int CM);
+bool i8_bottleneck_setup(I8BottleneckArgs* a);
+cudaError_t launch_i8_bottleneck(const I8BottleneckArgs& a, cudaStream_t s, int num_sms);
+cudaError_t init_i8_bottleneck_attributes();
+
 // K layout of a convolution: input channels padded to ci_pad (a multiple of
 // 32; for 3x3 kernels 32, 64 or a multiple of 128), K = kh*kw*ci_pad ordered
 // (ky, kx, ci) in 128-wide chunks; a_cpp channels per TMA copy.
