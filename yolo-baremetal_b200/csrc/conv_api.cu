@@ -145,6 +145,7 @@ extern "C" status_t yb_conv_run(void* conv, const void* d_x, int B, int H, int W
   out.cstride = c->cop;
   if (c->stem) {
     StemArgs sa;
+    sa.err = c->err;
     sa.in = static_cast<const float*>(d_x);
     sa.B = B;
     sa.Ci = c->ci;

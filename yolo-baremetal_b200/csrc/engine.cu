@@ -1097,6 +1097,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
   {
     YB_TRY(alloc_buf((H + 2 - stem_.k) / 2 + 1, (W + 2 - stem_.k) / 2 + 1, stem_.co, &S[0]));
     StemArgs sa;
+    sa.err = d_err_;
     sa.in = p->d_in;
     sa.B = B;
     sa.Ci = stem_.ci;

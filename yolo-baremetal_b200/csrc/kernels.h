@@ -186,8 +186,14 @@ struct StemArgs {
   int act = kActSiLU;
   SOut out;
   unsigned* amax = nullptr;  // calibration statistics, as in ConvArgs
+  int* err = nullptr;        // kernel error word (tensor-core form: a bounded wait that gave up)
 };
+// Runs the tensor-core first layer (stem_tc.cu) when stem_tc_supported(a)
+// (1-3 input channels, 16 or 32 outputs, SiLU, no statistics, 32-byte
+// aligned output), else the CUDA-core kernel.
 cudaError_t launch_stem(const StemArgs& a, cudaStream_t s);
+bool stem_tc_supported(const StemArgs& a);
+cudaError_t launch_stem_tc(const StemArgs& a, cudaStream_t s);
 // Must run once per device before the first launch_stem (not under capture).
 cudaError_t init_stem_kernel_attributes();
 

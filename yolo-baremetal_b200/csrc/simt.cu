@@ -587,6 +587,7 @@ cudaError_t init_stem_kernel_attributes() {
 }
 
 cudaError_t launch_stem(const StemArgs& a, cudaStream_t s) {
+  if (stem_tc_supported(a)) return launch_stem_tc(a, s);
   if (a.Ci < 1 || a.Ci > 4 || a.k != 3 || a.stride != 2 || a.pad != 1 || (a.Co != 16 && a.Co != 32 && a.Co != 64))
     return cudaErrorInvalidValue;
   if (a.Ho != (a.H - 1) / 2 + 1 || a.Wo != (a.W - 1) / 2 + 1) return cudaErrorInvalidValue;
