@@ -176,6 +176,22 @@ def test_int8_s_width(weights_s0):
         m.close()
 
 
+@pytest.mark.parametrize("hw", [(768, 768), (1216, 1280), (1280, 1536)])
+def test_int8_long_attention(model_i8, calib, hw):
+    """Key counts of the streamed-chunk attention kernel (512 < N <= 1920):
+    576 (pass-1 chunks 256, 256, 64), 1520 (not a multiple of 64) and 1920
+    (the largest); every stage bit-exact."""
+    import yb_weights as yw
+
+    o, scales = calib
+    img = yw.make_input(11, *hw)
+    model_i8.forward(img)
+    lg, _ = model_i8.head(1)
+    ref = o.forward_i8(img, scales, stages=True)
+    _check_image(model_i8, ref, 0)
+    assert np.array_equal(lg[0], ref["logits"])
+
+
 def test_int8_1280(model_i8, calib):
     """1280 x 1280: attention over 1600 tokens (13 key blocks), bit-exact."""
     import yb_weights as yw
