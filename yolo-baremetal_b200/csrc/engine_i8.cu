@@ -818,6 +818,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     sa.shift = static_cast<const int32_t*>(ds);
     sa.lut = static_cast<const int8_t*>(dl);
     sa.out = b[0].view();
+    sa.err = d_err_;
     const double po = static_cast<double>(B) * sa.Ho * sa.Wo;
     add_op(kOpStem, 2.0 * po * co * 27, 4.0 * B * 3 * H * W + po * co,
            [sa](cudaStream_t st) { return launch_stem_i8(sa, st); });

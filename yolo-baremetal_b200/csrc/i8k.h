@@ -42,9 +42,9 @@ struct I8AttnArgs {
 cudaError_t launch_quantize_input(const float* in, int B, int C, int H, int W, float s, I8View out, cudaStream_t st);
 
 // The first convolution fused with the input quantisation: 3x3 stride 2
-// pad 1 from the NCHW fp32 input [B, 3, H, W] (quantised in shared memory
-// with the input rule, padding 0) to int8 NHWC [B, Ho, Wo, Co], Co in
-// {16, 32, 64}, with the convolution requantisation and SiLU table.
+// pad 1 from the NCHW fp32 input [B, 3, H, W] (quantised with the input
+// rule, padding 0) to int8 NHWC [B, Ho, Wo, Co], Co in {16, 32, 64}, with
+// the convolution requantisation and SiLU table (stem_i8.cu, kind::i8).
 // w: [9][Co] words, each the taps of input channels 0..2 of one output
 // channel (byte 3 zero); bias / mult / shift / lut as for the kind::i8 conv.
 struct StemI8Args {
@@ -57,6 +57,7 @@ struct StemI8Args {
   const int32_t* shift = nullptr;
   const int8_t* lut = nullptr;
   I8View out;
+  int* err = nullptr;  // kernel error word (a bounded wait that gave up)
 };
 cudaError_t launch_stem_i8(const StemI8Args& a, cudaStream_t st);
 cudaError_t init_stem_i8_attributes();

@@ -34,210 +34,6 @@ __global__ void quantize_input_kernel(const float* in, int B, int C, int H, int 
   }
 }
 
-// ------------------------------------------------------------------ stem
-// Tiles of 8 output rows x 16 P columns (P = 64 / CO pixels per thread), as
-// the fp32 stem: the fp32 input patch (3 channels x 17 rows x (32 P + 4)
-// columns from input column 2 * ox0 - 4) arrives by 16-byte asynchronous
-// copies, is quantised into one word per input pixel (channels 0..2 in
-// bytes 0..2), and the next tile's copy lands while each output is computed
-// as 9 dp4a of such words with the packed weights.  36 KB of shared memory:
-// five or six CTAs per SM hide each other's latency.
-template <int CO>
-struct StemI8Tile {
-  static constexpr int P = 64 / CO;
-  static constexpr int TW = 16 * P, TH = 8;
-  static constexpr int PR = 2 * TH + 1, PC = 2 * TW + 4;
-  static constexpr int kBuf = 3 * PR * PC;  // floats per fp32 patch
-  static constexpr int kSmem = (kBuf + PR * PC + 9 * CO) * 4 + CO * 16 + CO * 8 + 256;
-};
-
-template <int CO>
-__device__ __forceinline__ void stem_i8_fetch(const StemI8Args& a, float* sx, int t, int tiles_x, int tiles_y) {
-  using T = StemI8Tile<CO>;
-  const int b = t / (tiles_x * tiles_y);
-  const int rem = t - b * tiles_x * tiles_y;
-  const int iy0 = (rem / tiles_x) * T::TH * 2 - 1, ix0 = (rem % tiles_x) * T::TW * 2 - 4;
-  const long long plane = static_cast<long long>(a.H) * a.W;
-  const float* inb = a.in + static_cast<long long>(b) * 3 * plane;
-  if ((a.W & 3) == 0) {
-    constexpr int Q = T::PC / 4;
-    for (int i = threadIdx.x; i < 3 * T::PR * Q; i += 128) {
-      const int row = i / Q;
-      const int q = i - row * Q;
-      const int c = row / T::PR;
-      const int rr = row - c * T::PR;
-      const int iy = iy0 + rr, ix = ix0 + 4 * q;
-      const int nvalid = (iy >= 0 && iy < a.H && ix >= 0) ? min(4, a.W - ix) : 0;
-      const float* src = nvalid > 0 ? inb + c * plane + static_cast<long long>(iy) * a.W + ix : inb;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(static_cast<uint32_t>(
-                       __cvta_generic_to_shared(sx + (c * T::PR + rr) * T::PC + 4 * q))),
-                   "l"(src), "r"(nvalid > 0 ? 4 * nvalid : 0)
-                   : "memory");
-    }
-  } else {
-    for (int i = threadIdx.x; i < 3 * T::PR * T::PC; i += 128) {
-      const int c = i / (T::PR * T::PC);
-      const int rr = (i / T::PC) % T::PR;
-      const int cc = i % T::PC;
-      const int iy = iy0 + rr, ix = ix0 + cc;
-      const bool ok = iy >= 0 && iy < a.H && ix >= 0 && ix < a.W;
-      const float* src = ok ? inb + c * plane + static_cast<long long>(iy) * a.W + ix : inb;
-      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(static_cast<uint32_t>(
-                       __cvta_generic_to_shared(sx + (c * T::PR + rr) * T::PC + cc))),
-                   "l"(src), "r"(ok ? 4 : 0)
-                   : "memory");
-    }
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
-// clamp(rint(v / s), -127, 127) as a byte, v / s correctly rounded.  With
-// r = fl(1 / s), y = fl(v * r) lies within 2^-15 of fl(v / s) for |y| <= 200,
-// so when y is further than 2^-12 from a half-integer both round to the same
-// integer, read from the mantissa of y + 1.5 * 2^23 (round half to even,
-// like rintf).  Otherwise (near a rounding boundary, large, or NaN) the exact
-// quotient is used.
-__device__ __forceinline__ uint32_t quant_byte(float v, float s, float r) {
-  const float y = __fmul_rn(v, r);
-  const float m = __fadd_rn(y, 12582912.0f);
-  const float d = __fsub_rn(y, __fsub_rn(m, 12582912.0f));
-  int q;
-  if (fabsf(y) <= 200.f && fabsf(d) < 0.49975586f) {
-    q = __float_as_int(m) - 0x4B400000;
-  } else {
-    const float e = rintf(__fdiv_rn(v, s));
-    q = static_cast<int>(e < -127.f ? -127.f : e > 127.f ? 127.f : e);
-  }
-  return static_cast<uint32_t>(min(max(q, -127), 127)) & 0xFFu;
-}
-
-template <int CO>
-__global__ void __launch_bounds__(128) stem_i8_kernel(const StemI8Args a) {
-  using T = StemI8Tile<CO>;
-  constexpr int P = T::P;
-  extern __shared__ __align__(16) float stem_i8_smem[];
-  float* sxb = stem_i8_smem;
-  uint32_t* sq = reinterpret_cast<uint32_t*>(stem_i8_smem + T::kBuf);  // [PR][PC] packed int8 pixels
-  uint32_t* sw = sq + T::PR * T::PC;                                      // [9][CO]
-  int4* sp = reinterpret_cast<int4*>(sw + 9 * CO);                        // {M, D lo, D hi, shift - 32}
-  int2* sx2 = reinterpret_cast<int2*>(sp + CO);                           // {bias, shift}
-  int8_t* slut = reinterpret_cast<int8_t*>(sx2 + CO);
-  const int tid = threadIdx.x;
-  for (int i = tid; i < 9 * CO; i += 128) sw[i] = a.w[i];
-  for (int i = tid; i < CO; i += 128) {
-    const int m = a.mult[i], b = a.bias[i];
-    const int sh = m == 0 ? 32 : a.shift[i];
-    const long long d = static_cast<long long>(b) * m + ((1LL << (sh - 1)) - 1);
-    sp[i] = make_int4(m, static_cast<int>(static_cast<unsigned long long>(d) & 0xFFFFFFFFull),
-                      static_cast<int>(d >> 32), sh - 32);
-    sx2[i] = make_int2(b, sh);
-  }
-  for (int i = tid; i < 256; i += 128) slut[i] = a.lut[i];
-  pdl_wait();
-  const int tiles_x = (a.Wo + T::TW - 1) / T::TW, tiles_y = (a.Ho + T::TH - 1) / T::TH;
-  const int total = a.B * tiles_x * tiles_y;
-  const int r = tid >> 4, x0 = tid & 15;
-  const float rcp = __frcp_rn(a.s_in);
-  // One fp32 staging buffer: once a tile is quantised, the next tile's copy
-  // goes into it and lands while this tile computes.
-  if (static_cast<int>(blockIdx.x) < total) {
-    stem_i8_fetch<CO>(a, sxb, blockIdx.x, tiles_x, tiles_y);
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-  }
-  __syncthreads();
-  for (int t = blockIdx.x; t < total; t += gridDim.x) {
-    const int tn = t + gridDim.x;
-    for (int i = tid; i < T::PR * T::PC; i += 128)
-      sq[i] = quant_byte(sxb[i], a.s_in, rcp) | (quant_byte(sxb[T::PR * T::PC + i], a.s_in, rcp) << 8) |
-              (quant_byte(sxb[2 * T::PR * T::PC + i], a.s_in, rcp) << 16);
-    __syncthreads();
-    if (tn < total) stem_i8_fetch<CO>(a, sxb, tn, tiles_x, tiles_y);
-    int acc[P][CO];
-#pragma unroll
-    for (int j = 0; j < P; ++j)
-#pragma unroll
-      for (int c = 0; c < CO; ++c) acc[j][c] = 0;
-#pragma unroll
-    for (int ky = 0; ky < 3; ++ky) {
-#pragma unroll
-      for (int kx = 0; kx < 3; ++kx) {
-        int xv[P];
-#pragma unroll
-        for (int j = 0; j < P; ++j) xv[j] = static_cast<int>(sq[(2 * r + ky) * T::PC + 2 * (x0 + 16 * j) + kx + 3]);
-        const uint32_t* wr = sw + (ky * 3 + kx) * CO;
-#pragma unroll
-        for (int c = 0; c < CO; c += 4) {
-          const uint4 w = *reinterpret_cast<const uint4*>(wr + c);
-#pragma unroll
-          for (int j = 0; j < P; ++j) {
-            acc[j][c + 0] = __dp4a(xv[j], static_cast<int>(w.x), acc[j][c + 0]);
-            acc[j][c + 1] = __dp4a(xv[j], static_cast<int>(w.y), acc[j][c + 1]);
-            acc[j][c + 2] = __dp4a(xv[j], static_cast<int>(w.z), acc[j][c + 2]);
-            acc[j][c + 3] = __dp4a(xv[j], static_cast<int>(w.w), acc[j][c + 3]);
-          }
-        }
-      }
-    }
-    const int b = t / (tiles_x * tiles_y);
-    const int rem = t - b * tiles_x * tiles_y;
-    const int oy = (rem / tiles_x) * T::TH + r;
-    // Requantise: acc * M + (bias * M + 2^(sh-1) - 1) >> sh for every
-    // channel (branch-free), exact unless a shift is below 32 or a low word
-    // is all ones (a possible tie); then the thread redoes its pixels in 64
-    // bits.
-    bool exact = false;
-#pragma unroll
-    for (int c = 0; c < CO; ++c) {
-      const int4 q = sp[c];
-      const long long d = (static_cast<long long>(q.z) << 32) | static_cast<unsigned>(q.y);
-#pragma unroll
-      for (int j = 0; j < P; ++j) {
-        const long long pr = static_cast<long long>(acc[j][c]) * q.x + d;
-        exact |= (q.w < 0) | (static_cast<unsigned>(pr) == 0xFFFFFFFFu);
-        const int y = static_cast<int>(pr >> 32) >> (q.w & 31);
-        acc[j][c] = slut[min(max(y, -128), 127) + 128];
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-      const int ox = (rem % tiles_x) * T::TW + x0 + 16 * j;
-      if (oy >= a.Ho || ox >= a.Wo) continue;
-      int8_t* o = a.out.p + static_cast<long long>(b) * a.out.bstride +
-                  (static_cast<long long>(oy) * a.Wo + ox) * a.out.cstride;
-#pragma unroll
-      for (int c = 0; c < CO; c += 16) {
-        uint32_t wv[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int* ov = &acc[j][c + 4 * g];
-          wv[g] = __byte_perm(__byte_perm(ov[0], ov[1], 0x0040), __byte_perm(ov[2], ov[3], 0x0040), 0x5410);
-        }
-        *reinterpret_cast<uint4*>(o + c) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-      }
-    }
-    if (exact) {
-      // Rare: redo this thread's outputs in 64 bits and overwrite them.
-      for (int j = 0; j < P; ++j) {
-        const int ox = (rem % tiles_x) * T::TW + x0 + 16 * j;
-        if (oy >= a.Ho || ox >= a.Wo) continue;
-        int8_t* o = a.out.p + static_cast<long long>(b) * a.out.bstride +
-                    (static_cast<long long>(oy) * a.Wo + ox) * a.out.cstride;
-        for (int c = 0; c < CO; ++c) {
-          int raw = 0;
-          for (int tap = 0; tap < 9; ++tap)
-            raw = __dp4a(static_cast<int>(sq[(2 * r + tap / 3) * T::PC + 2 * (x0 + 16 * j) + tap % 3 + 3]),
-                         static_cast<int>(sw[tap * CO + c]), raw);
-          const int2 bs = sx2[c];
-          const long long y = rne((static_cast<long long>(raw) + bs.x) * sp[c].x, bs.y);
-          o[c] = slut[(y < -128 ? -128 : y > 127 ? 127 : y) + 128];
-        }
-      }
-    }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();  // the next tile has landed; the patch is rewritten next iteration
-  }
-}
-
 // ------------------------------------------------------------ max pool
 // k x k, stride 1, padding k / 2 excluded (the -128 sentinel is below every
 // quantised value); 16 channels per thread.
@@ -547,34 +343,6 @@ cudaError_t launch_nhwc_to_nchw_i8(I8View in, int C, int H, int W, int8_t* out, 
   const long long total = static_cast<long long>(C) * H * W;
   nhwc_to_nchw_i8_kernel<<<blocks_for(total, 256), 256, 0, st>>>(in, C, H, W, out);
   return cudaGetLastError();
-}
-
-cudaError_t init_stem_i8_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(stem_i8_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       StemI8Tile<16>::kSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(stem_i8_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, StemI8Tile<32>::kSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(stem_i8_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, StemI8Tile<64>::kSmem);
-  return e;
-}
-
-cudaError_t launch_stem_i8(const StemI8Args& a, cudaStream_t st) {
-  if ((a.Co != 16 && a.Co != 32 && a.Co != 64) || a.Ho != (a.H - 1) / 2 + 1 || a.Wo != (a.W - 1) / 2 + 1 ||
-      a.out.cstride < a.Co || a.out.cstride % 16 || reinterpret_cast<uintptr_t>(a.out.p) % 16 || !a.lut ||
-      !(a.s_in > 0.f))
-    return cudaErrorInvalidValue;
-  const int tw = 16 * (64 / a.Co);
-  const long long tiles = static_cast<long long>(a.B) * ((a.Ho + 7) / 8) * ((a.Wo + tw - 1) / tw);
-  if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
-  if (tiles == 0) return cudaSuccess;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const unsigned grid = static_cast<unsigned>(tiles < 6LL * sms ? tiles : 6LL * sms);
-  if (a.Co == 16) return launch_pdl(stem_i8_kernel<16>, dim3(grid), dim3(128), StemI8Tile<16>::kSmem, st, a);
-  if (a.Co == 32) return launch_pdl(stem_i8_kernel<32>, dim3(grid), dim3(128), StemI8Tile<32>::kSmem, st, a);
-  return launch_pdl(stem_i8_kernel<64>, dim3(grid), dim3(128), StemI8Tile<64>::kSmem, st, a);
 }
 
 }  // namespace yb
