@@ -178,6 +178,13 @@ void Engine::release_plan(Plan* p) {
   if (p->int8) i8_images_.clear();  // they may point into this plan's buffers
   if (p->graph) cudaGraphExecDestroy(p->graph);
   p->graph = nullptr;
+  for (int L = 1; L < 3; ++L) {
+    if (p->lane_s[L]) cudaStreamDestroy(p->lane_s[L]);
+    if (p->ev_fork[L]) cudaEventDestroy(p->ev_fork[L]);
+    if (p->ev_join[L]) cudaEventDestroy(p->ev_join[L]);
+    p->lane_s[L] = nullptr;
+    p->ev_fork[L] = p->ev_join[L] = nullptr;
+  }
   for (void* q : p->allocs) cudaFree(q);
   p->allocs.clear();
 }
@@ -1152,11 +1159,13 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
   // steps 14-15: upsample(buf13) ++ buf4.
   step = 16;
   YB_TRY(c3k2_c3k(16, src_cat(S[13], 1, S[4], S[4].H, S[4].W), &S[16]));
+  const int after16 = static_cast<int>(ops.size()) - 1;
   step = 17;
   YB_TRY(downconv(17, S[16], &S[17]));
   // step 18: buf17 ++ buf13.
   step = 19;
   YB_TRY(c3k2_c3k(19, src_cat(S[17], 0, S[13], S[13].H, S[13].W), &S[19]));
+  const int after19 = static_cast<int>(ops.size()) - 1;
   step = 20;
   YB_TRY(downconv(20, S[19], &S[20]));
   // step 21: buf20 ++ buf10.
@@ -1191,6 +1200,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     for (int s = 0; s < 3; ++s) {
       const Buf& f = *feats[s];
       const std::string si = std::to_string(s);
+      const size_t first_op = ops.size();
       DevConv *w0, *w1, *w2, *pw0, *pw1, *wf;
       DevDw *dw0, *dw1;
       YB_TRY(conv(b2 + si + ".0", &w0));
@@ -1258,6 +1268,12 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       lv.bstride = static_cast<long long>(N) * nc;
       lv.cstride = nc;
       YB_TRY(add_conv(wf, src_of(p1, 0, p1.C), 1, 0, kActNone, SOut(), SView(), lv));
+      // The P3 and P4 heads read model.16 / model.19 only: side lanes 1 and
+      // 2, beside the rest of the neck (inference plans).
+      if (!p->calib && s < 2) {
+        for (size_t i = first_op; i < ops.size(); ++i) ops[i].lane = s + 1;
+        p->fork_after[s + 1] = s == 0 ? after16 : after19;
+      }
     }
     DecodeArgs de;
     de.dist = p->d_dist;
@@ -1274,6 +1290,7 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       de.stride[s] = strides[s];
     }
     add_op(kOpDecode, 0.0, 4.0 * B * N * (4.0 + nc + 4.0 + 1.0), [de](cudaStream_t st) { return launch_decode(de, st); });
+    ops.back().join = true;
     TopkArgs ta;
     ta.maxscore = p->d_maxscore;
     ta.scores = p->d_logits;
@@ -1368,6 +1385,13 @@ cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::
   p->slot = slot;
   p->int8 = int8_mode();
   cudaError_t e = p->int8 ? build_i8(p.get(), why) : build(p.get(), why);
+  for (int L = 1; L < 3 && e == cudaSuccess; ++L) {
+    if (p->fork_after[L] < 0) continue;
+    e = cudaStreamCreateWithFlags(&p->lane_s[L], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->ev_fork[L], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->ev_join[L], cudaEventDisableTiming);
+    if (e != cudaSuccess) *why = std::string("side streams: ") + cudaGetErrorString(e);
+  }
   if (e != cudaSuccess) {
     release_plan(p.get());
     return e;
@@ -1390,10 +1414,7 @@ cudaError_t Engine::get_plan(int B, int H, int W, int max_det, Plan** out, std::
   cudaGraph_t g = nullptr;
   e = cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal);
   if (e == cudaSuccess) {
-    for (const Op& op : p->ops) {
-      e = op.run(stream_);
-      if (e != cudaSuccess) break;
-    }
+    e = run(p.get(), stream_, nullptr);  // no graph yet: the launches, side streams included
     cudaError_t e2 = cudaStreamEndCapture(stream_, &g);
     if (e == cudaSuccess) e = e2;
   }
@@ -1462,18 +1483,51 @@ cudaError_t Engine::calibrate(const float* images, int n, int H, int W, std::map
 
 cudaError_t Engine::run(Plan* p, cudaStream_t s, cudaEvent_t* ev) {
   if (!ev && p->graph) return cudaGraphLaunch(p->graph, s);
+  // Side lanes only without per-step events (those time every op in order).
+  const bool lanes = !ev;
+  bool started[3] = {true, false, false};
+  auto join_lanes = [&]() -> cudaError_t {
+    for (int L = 1; L < 3; ++L) {
+      if (!started[L]) continue;
+      cudaError_t e = cudaEventRecord(p->ev_join[L], p->lane_s[L]);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(s, p->ev_join[L], 0);
+      if (e != cudaSuccess) return e;
+      started[L] = false;
+    }
+    return cudaSuccess;
+  };
   int cur = -1;
-  for (const Op& op : p->ops) {
+  for (size_t i = 0; i < p->ops.size(); ++i) {
+    const Op& op = p->ops[i];
     if (ev && op.step != cur) {
       if (cur >= 0) cudaEventRecord(ev[2 * cur + 1], s);
       cur = op.step;
       cudaEventRecord(ev[2 * cur], s);
     }
-    cudaError_t e = op.run(s);
+    cudaStream_t st = s;
+    if (lanes && op.join) {
+      cudaError_t e = join_lanes();
+      if (e != cudaSuccess) return e;
+    }
+    if (lanes && op.lane > 0 && p->lane_s[op.lane]) {
+      st = p->lane_s[op.lane];
+      if (!started[op.lane]) {
+        cudaError_t e = cudaStreamWaitEvent(st, p->ev_fork[op.lane], 0);
+        if (e != cudaSuccess) return e;
+        started[op.lane] = true;
+      }
+    }
+    cudaError_t e = op.run(st);
     if (e != cudaSuccess) return e;
+    for (int L = 1; lanes && L < 3; ++L) {
+      if (p->lane_s[L] && p->fork_after[L] == static_cast<int>(i)) {
+        e = cudaEventRecord(p->ev_fork[L], s);
+        if (e != cudaSuccess) return e;
+      }
+    }
   }
   if (ev && cur >= 0) cudaEventRecord(ev[2 * cur + 1], s);
-  return cudaSuccess;
+  return lanes ? join_lanes() : cudaSuccess;
 }
 
 }  // namespace yb

@@ -80,6 +80,8 @@ struct Op {
   int kind = kOpConv;
   double flops = 0;  // algorithmic FLOPs of the launch (2 x MACs)
   double bytes = 0;  // algorithmic HBM bytes: inputs + weights read once, outputs written once
+  int lane = 0;       // 0: the plan's stream; 1, 2: a side stream (see Plan::fork_after)
+  bool join = false;  // every side stream's work completes before this op starts
 };
 
 struct Plan {
@@ -98,6 +100,16 @@ struct Plan {
   Buf stage[23];  // model->buffers[0..22] equivalents (concat/upsample ones unset)
   cudaGraphExec_t graph = nullptr;
   size_t arena_bytes = 0;
+  // Concurrent branches: the ops of side lane L (1, 2) run on lane_s[L] once
+  // op fork_after[L] of the plan's stream has run (their only input), and
+  // the next op marked `join` waits for them.  The Detect head of the P3
+  // and P4 scales runs this way beside the rest of the neck.  Unused (null
+  // streams) in calibration plans; per-op profiling runs every op in order
+  // on one stream.
+  int fork_after[3] = {-1, -1, -1};
+  cudaStream_t lane_s[3] = {nullptr, nullptr, nullptr};
+  cudaEvent_t ev_fork[3] = {nullptr, nullptr, nullptr};
+  cudaEvent_t ev_join[3] = {nullptr, nullptr, nullptr};
   // INT8 plans: stage tensors 01-23 as NHWC int8 with per-channel scales.
   bool int8 = false;
   struct I8Stage {

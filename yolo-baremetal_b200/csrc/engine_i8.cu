@@ -878,6 +878,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   step = 16;
   YB_TRY(tensor(outw("model.16"), b[15].H, b[15].W, &b[16]));
   YB_TRY(c3k2_c3k("model.16", b[16], b[15]));
+  const int after16 = static_cast<int>(p->ops.size()) - 1;
   step = 17;
   {
     const QT d17 = cat18.sub(0, c17);
@@ -888,6 +889,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   step = 19;
   YB_TRY(tensor(outw("model.19"), b[18].H, b[18].W, &b[19]));
   YB_TRY(c3k2_c3k("model.19", b[19], b[18]));
+  const int after19 = static_cast<int>(p->ops.size()) - 1;
   step = 20;
   {
     const QT d20 = cat21.sub(0, c20);
@@ -943,6 +945,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   for (int s = 0; s < 3; ++s) {
     const QT& f = *feats[s];
     const std::string si = std::to_string(s);
+    const size_t first_op = p->ops.size();
     const int c2 = wdim0(b2 + si + ".0.conv.weight"), c3 = wdim0(b3 + si + ".0.1.conv.weight");
     if (!c2 || !c3) return fail("int8: missing detect weights");
     QT s1, s2, d0, p0, d1, p1;
@@ -968,6 +971,12 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     lv.cstride = nc;
     lv.bstride = static_cast<long long>(N) * nc;
     YB_TRY(conv(b3 + si + ".2", true, QT(), p1, 1, 0, false, nullptr, lv));
+    // The P3 and P4 heads read model.16 / model.19 only: side lanes 1 and 2,
+    // beside the rest of the neck.
+    if (s < 2) {
+      for (size_t i = first_op; i < p->ops.size(); ++i) p->ops[i].lane = s + 1;
+      p->fork_after[s + 1] = s == 0 ? after16 : after19;
+    }
   }
   DecodeArgs de;
   de.dist = p->d_dist;
@@ -984,6 +993,7 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     de.stride[s] = strides[s];
   }
   add_op(kOpDecode, 0.0, 4.0 * B * N * (4.0 + nc + 4.0 + 1.0), [de](cudaStream_t st) { return launch_decode(de, st); });
+  p->ops.back().join = true;
   TopkArgs ta;
   ta.maxscore = p->d_maxscore;
   ta.scores = p->d_logits;
