@@ -808,6 +808,11 @@ status_t stream_submit(Ctx* c, const void* src, size_t src_bytes, bool rgb8, int
   e = cudaMemcpyAsync(dst, src, src_bytes, cudaMemcpyHostToDevice, c->copy_stream);
   if (e == cudaSuccess) e = cudaEventRecord(S.h2d, c->copy_stream);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(S.st, S.h2d, 0);
+  // The other slot's batch computes first: the forwards run back to back on
+  // the GPU (two at once only compete for the SMs), while this batch's input
+  // copy overlaps the other's compute.
+  Ctx::StreamSlot& O = c->sslot[k ^ 1];
+  if (e == cudaSuccess && O.ticket) e = cudaStreamWaitEvent(S.st, O.done, 0);
   if (e == cudaSuccess && rgb8) e = launch_preprocess(S.d_rgb, B, src_h, src_w, resize, p->d_in, H, W, S.st);
   if (e == cudaSuccess) e = c->eng->run(p, S.st, nullptr);
   if (e == cudaSuccess)
