@@ -87,3 +87,19 @@ def test_sharded_across_all_gpus_timed(weights_n0):
     finally:
         for m in ms:
             m.close()
+
+
+def test_batch_size_does_not_change_fp32_results(shard_models):
+    """The benchmark batch of 64 640x640 images through one host forward
+    (16-image plans, pipelined) and as two 32-image shards (32-image plans,
+    whose small 20x20 layers get narrower N tiles): bit-equal detections.
+    Every FP32 convolution sums the same products in the same order whatever
+    its N tiling, so the batch size never changes a result."""
+    import yb_weights as yw
+    import yolo_b200 as yb
+
+    imgs = yw.make_batch(range(101, 165), 640, 640)
+    st, dets = yb.forward_sharded(shard_models, imgs, timeout_ms=60000)
+    yb.check(st, "yb_cuda_forward_sharded")
+    single = shard_models[0].forward(imgs)["dets"]
+    assert np.array_equal(dets, single)

@@ -212,11 +212,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   // stacked [B_hi; B_lo] chunk (columns [0, n) += A*B_hi, [n, 2n) += A*B_lo,
   // summed by the epilogue).  Otherwise three UMMAs of N = n_tile, which
   // keeps the epilogue (the long pole there) to one TMEM load per unit.
-  // The im2col / gather modes stack too for 3x3 convolutions with n_tile <=
-  // 64 (MMA-issue bound: measured ~45-64 cycles per UMMA at N <= 128, so two
-  // UMMAs of 2n beat three of n); 1x1 convolutions keep one TMEM load per
-  // unit for their epilogue-bound tiles.
-  const bool stacked = patch ? a.n_tile <= 128 : (a.kh * a.kw > 1 && a.n_tile <= 64);
+  // The im2col / gather modes stack too for 3x3 convolutions of at most 64
+  // output channels (MMA-issue bound: measured ~45-64 cycles per UMMA at
+  // N <= 128, so two UMMAs of 2n beat three of n); 1x1 convolutions keep one
+  // TMEM load per unit for their epilogue-bound tiles.  The choice depends on
+  // the layer, not on its N tiling (which the engine narrows for small
+  // batches), so that every batch size sums the same products in the same
+  // order.
+  const bool stacked = patch ? a.n_tile <= 128 : (a.kh * a.kw > 1 && a.Co <= 64);
   const uint32_t acc_cols = static_cast<uint32_t>(stacked ? 2 * a.n_tile : a.n_tile);
   uint32_t acc_stride = 32;
   while (acc_stride < acc_cols) acc_stride <<= 1;
