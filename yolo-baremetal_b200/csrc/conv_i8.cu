@@ -133,6 +133,10 @@ __device__ __forceinline__ void raise_err(int* err, volatile int* abort_flag, in
   if (err) atomicCAS(err, 0, code);
 }
 
+// EPI: the epilogue, fixed per launch so that each instantiation carries one
+// compact loop: bit 1 the SiLU table, bit 0 the residual, 4 = dequantised
+// fp32 output (the Detect head's last convolutions).
+template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_constant__ I8Args a, const int stages) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -470,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
     const int grp = warp >> 2;
     const int ngrp = min(kEpiGroups, nacc);
     // 32-byte stores of whole 32-channel runs when every run is aligned.
-    const bool v8out = !a.out_f32 && (reinterpret_cast<uintptr_t>(a.out) & 31) == 0 && (a.out_cstride & 31) == 0 &&
+    const bool v8out = EPI != 4 && (reinterpret_cast<uintptr_t>(a.out) & 31) == 0 && (a.out_cstride & 31) == 0 &&
                        (a.out_coff & 31) == 0 && (a.n_tile & 31) == 0;
     for (int t = blockIdx.x + grp * gridDim.x, lt = grp; grp < ngrp && t < total_tiles;
          t += ngrp * gridDim.x, lt += ngrp) {
@@ -510,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       // 32-byte run.
       for (int c = 0; c < nvalid; c += 32) {
         const bool two = c + 16 < nvalid;
-        if (a.out_f32) {
+        if (EPI == 4) {
           uint32_t r[32];
           uint32_t(&r0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[0]);
           uint32_t(&r1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&r[16]);
@@ -541,13 +545,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
           continue;
         }
         uint4 rvv[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
-        if (a.res) {
+        if (EPI & 1) {
           const int8_t* rp = a.res + pm * a.res_cstride + a.res_coff + n0 + c;
           rvv[0] = *reinterpret_cast<const uint4*>(rp);
           if (two) rvv[1] = *reinterpret_cast<const uint4*>(rp + 16);
         }
         uint32_t p0[4] = {0u, 0u, 0u, 0u}, p1[4] = {0u, 0u, 0u, 0u};
-        const int mode = (a.lut ? 2 : 0) | (a.res ? 1 : 0);
+        constexpr int mode = EPI & 3;
         // Two halves of 16 channels: both TMEM loads in flight together, one wait.
         uint32_t ra[16], rb[16];
         tc_ld_32x32b_x16(tbase + c, ra);
@@ -728,11 +732,25 @@ std::vector<uint8_t> i8_pack_weights(const int8_t* wq, int co, int ci, int kh, i
 int i8_bias_slots(const I8Tiling& t) { return t.n_tile * t.n_tiles; }
 
 cudaError_t i8_init_kernel() {
-  const cudaError_t e = cudaFuncSetAttribute(conv_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  cudaError_t e = cudaSuccess;
+  for (auto k : {conv_i8_kernel<0>, conv_i8_kernel<1>, conv_i8_kernel<2>, conv_i8_kernel<3>, conv_i8_kernel<4>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   return e == cudaSuccess ? init_i8_bottleneck_attributes() : e;
 }
 
 namespace {
+// The kernel instantiation for the launch's epilogue.
+using I8ConvKernel = void (*)(I8Args, int);
+I8ConvKernel i8_kernel_for(const I8Args& a) {
+  if (a.out_f32) return conv_i8_kernel<4>;
+  switch ((a.lut ? 2 : 0) | (a.res ? 1 : 0)) {
+    case 0: return conv_i8_kernel<0>;
+    case 1: return conv_i8_kernel<1>;
+    case 2: return conv_i8_kernel<2>;
+    default: return conv_i8_kernel<3>;
+  }
+}
+
 void fill_fastdiv(I8Args& a, int stages) {
   a.fd_stages = FastDiv(static_cast<uint32_t>(stages));
   a.fd_ntiles = FastDiv(static_cast<uint32_t>(a.n_tiles));
@@ -785,7 +803,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
         if (a.m_tiles <= 0) return cudaSuccess;
         const int grid = a.m_tiles < sms ? a.m_tiles : sms;
         fill_fastdiv(a, st);
-        return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, st);
+        return launch_pdl(i8_kernel_for(a), dim3(grid), dim3(kThreads), smem, s, a, st);
       }
     }
   }
@@ -819,7 +837,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
         if (a.m_tiles <= 0) return cudaSuccess;
         const int grid = a.m_tiles < sms ? a.m_tiles : sms;
         fill_fastdiv(a, st);
-        return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, st);
+        return launch_pdl(i8_kernel_for(a), dim3(grid), dim3(kThreads), smem, s, a, st);
       }
     }
   }
@@ -858,7 +876,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
   if (total <= 0) return cudaSuccess;
   const int grid = total < sms ? total : sms;
   fill_fastdiv(a, stages);
-  return launch_pdl(conv_i8_kernel, dim3(grid), dim3(kThreads), smem, s, a, stages);
+  return launch_pdl(i8_kernel_for(a), dim3(grid), dim3(kThreads), smem, s, a, stages);
 }
 
 namespace {
