@@ -173,6 +173,10 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// EPI: the epilogue, fixed per launch so that each instantiation carries one
+// compact loop: bit 0 SiLU, bit 1 the residual, bit 2 fp32 output (the Detect
+// head's last convolutions), bit 3 calibration statistics.
+template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_constant__ ConvArgs a, const int stages) {
   extern __shared__ uint8_t smem_raw[];
   // Swizzle atoms need 1024-byte alignment in the shared window.
@@ -489,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     const int e_idx = warp - kProducerWarps;  // 0..11
     const int q = e_idx & 3;                  // TMEM lane quarter (= warp % 4)
     const int grp = e_idx >> 2;               // this group takes every egroups-th tile
-    const bool f32out = a.out_f32.ptr != nullptr;
+    constexpr bool f32out = (EPI & 4) != 0;
     // 32-byte stores of whole 16-channel runs when every run starts on a
     // 32-byte boundary (offsets and strides in elements of 2 bytes).
     const bool v8out = !f32out && (reinterpret_cast<uintptr_t>(a.out.hi) & 31) == 0 && (a.out.cstride & 15) == 0 &&
@@ -567,13 +571,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           v[e + 2] += bb.z;
           v[e + 3] += bb.w;
         }
-        const bool stats = a.amax != nullptr && valid;
+        const bool stats = (EPI & 8) != 0 && valid;
         if (stats) {
 #pragma unroll
           for (int e = 0; e < 16; ++e)
             if (c + e < nvalid) mpre = fmaxf(mpre, fabsf(v[e]));
         }
-        if (a.act == kActSiLU) {
+        if (EPI & 1) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = silu_fast(v[e]);
         }
@@ -583,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             if (c + e < nvalid) mout = fmaxf(mout, fabsf(v[e]));
         }
         const bool second = c + 8 < nvalid;
-        if (a.res.hi) {
+        if (EPI & 2) {
           const uint16_t* rb = a.res.hi + static_cast<long long>(b) * a.res.bstride +
                                static_cast<long long>(p) * a.res.cstride + a.res.coff + n0 + c;
           float rv[16];
@@ -657,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
-    if (a.amax) {
+    if (EPI & 8) {
       const unsigned am = __activemask();
       const unsigned wp = __reduce_max_sync(am, __float_as_uint(mpre));
       const unsigned wo = __reduce_max_sync(am, __float_as_uint(mout));
@@ -1087,7 +1091,12 @@ void conv_setup_tma(ConvArgs* a) {
 }
 
 cudaError_t init_conv_kernel_attributes() {
-  const cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  cudaError_t e = cudaSuccess;
+  for (auto k : {conv_tc_kernel<0>, conv_tc_kernel<1>, conv_tc_kernel<2>, conv_tc_kernel<3>, conv_tc_kernel<4>,
+                 conv_tc_kernel<5>, conv_tc_kernel<6>, conv_tc_kernel<7>, conv_tc_kernel<8>, conv_tc_kernel<9>,
+                 conv_tc_kernel<10>, conv_tc_kernel<11>, conv_tc_kernel<12>, conv_tc_kernel<13>, conv_tc_kernel<14>,
+                 conv_tc_kernel<15>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
   if (e != cudaSuccess) return e;
   const cudaError_t e2 = init_bottleneck_kernel_attributes();
   return e2 == cudaSuccess ? init_stem_kernel_attributes() : e2;
@@ -1123,7 +1132,14 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
   const int total = a.m_tiles * a.n_tiles;
   if (total <= 0) return cudaSuccess;
   const int grid = total < num_sms ? total : num_sms;
-  return launch_pdl(conv_tc_kernel, dim3(grid), dim3(kThreads), smem, s, k, stages);
+  using ConvKernel = void (*)(ConvArgs, int);
+  static const ConvKernel kernels[16] = {
+      conv_tc_kernel<0>,  conv_tc_kernel<1>,  conv_tc_kernel<2>,  conv_tc_kernel<3>,
+      conv_tc_kernel<4>,  conv_tc_kernel<5>,  conv_tc_kernel<6>,  conv_tc_kernel<7>,
+      conv_tc_kernel<8>,  conv_tc_kernel<9>,  conv_tc_kernel<10>, conv_tc_kernel<11>,
+      conv_tc_kernel<12>, conv_tc_kernel<13>, conv_tc_kernel<14>, conv_tc_kernel<15>};
+  const int epi = (k.act == kActSiLU ? 1 : 0) | (k.res.hi ? 2 : 0) | (k.out_f32.ptr ? 4 : 0) | (k.amax ? 8 : 0);
+  return launch_pdl(kernels[epi], dim3(grid), dim3(kThreads), smem, s, k, stages);
 }
 
 }  // namespace yb
