@@ -301,7 +301,7 @@ struct AttnWideTcSmem {
     } s;
     uint8_t p[2][2][kSlotBytes];  // [slot][hi, lo]: 128 x 64 bf16
   } u;
-  uint8_t vh[THD * kWideNF * 2], vl[THD * kWideNF * 2];
+  uint8_t vh[THD * kWideNF * 2 + 128], vl[THD * kWideNF * 2 + 128];  // V^T row groups 16 Np + 16 bytes apart
   float red_max[4][kTQ];
   float red_sum[4][kTQ];
   float pew[9][THD];  // positional weights of this head, [tap][channel]
@@ -339,45 +339,71 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
     tmem_relinquish();
   }
   pdl_wait();
+  // Q and K rows: 16-byte asynchronous copies of each plane straight into
+  // the K-major operand layout (zero past N).
+  auto copy16 = [](void* dst, const uint16_t* src, bool in) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(in ? 16u : 0u)
+                 : "memory");
+  };
   for (int i = tid; i < kTQ * 4; i += kWideTF) {
     const int r = i >> 2, c = i & 3;
-    uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
-    if (q0 + r < N) {
-      const uint16_t* p = base + static_cast<long long>(q0 + r) * a.qkv.cstride + 8 * c;
-      vh = *reinterpret_cast<const uint4*>(p);
-      vl = *reinterpret_cast<const uint4*>(p + pl);
-    }
-    *reinterpret_cast<uint4*>(S.u.s.qh + opo(r, 16 * c, 2 * TKD)) = vh;
-    *reinterpret_cast<uint4*>(S.u.s.ql + opo(r, 16 * c, 2 * TKD)) = vl;
+    const bool in = q0 + r < N;
+    const uint16_t* p = base + static_cast<long long>(in ? q0 + r : 0) * a.qkv.cstride + 8 * c;
+    copy16(S.u.s.qh + opo(r, 16 * c, 2 * TKD), p, in);
+    copy16(S.u.s.ql + opo(r, 16 * c, 2 * TKD), p + pl, in);
   }
   for (int i = tid; i < Np * 4; i += kWideTF) {
     const int j = i >> 2, c = i & 3;
-    uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
-    if (j < N) {
-      const uint16_t* p = base + static_cast<long long>(j) * a.qkv.cstride + TKD + 8 * c;
-      vh = *reinterpret_cast<const uint4*>(p);
-      vl = *reinterpret_cast<const uint4*>(p + pl);
-    }
-    *reinterpret_cast<uint4*>(S.u.s.kh + opo(j, 16 * c, 2 * TKD)) = vh;
-    *reinterpret_cast<uint4*>(S.u.s.kl + opo(j, 16 * c, 2 * TKD)) = vl;
+    const bool in = j < N;
+    const uint16_t* p = base + static_cast<long long>(in ? j : 0) * a.qkv.cstride + TKD + 8 * c;
+    copy16(S.u.s.kh + opo(j, 16 * c, 2 * TKD), p, in);
+    copy16(S.u.s.kl + opo(j, 16 * c, 2 * TKD), p + pl, in);
   }
-  for (int i = tid; i < Np * (THD / 8); i += kWideTF) {
-    const int j = i % Np, c = i / Np;  // key j, channels 8c .. 8c + 7
-    uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
-    if (j < N) {
-      const uint16_t* p = base + static_cast<long long>(j) * a.qkv.cstride + 2 * TKD + 8 * c;
-      vh = *reinterpret_cast<const uint4*>(p);
-      vl = *reinterpret_cast<const uint4*>(p + pl);
-    }
-    const uint16_t* eh = reinterpret_cast<const uint16_t*>(&vh);
-    const uint16_t* el = reinterpret_cast<const uint16_t*>(&vl);
+  // V^T: item i = key pair i >> 3 (keys 2 jp, 2 jp + 1) x 8 channels
+  // 8 (i & 7) .. + 7; each channel's two keys become one 32-bit word.  The
+  // row groups of 8 channels are 16 Np + 16 bytes apart, so that the stores
+  // of a warp (8 channel groups x 4 key pairs) fall in distinct banks.  Two
+  // items' loads in flight per thread.
+  const uint32_t vsbo = static_cast<uint32_t>(16 * Np + 16);
+  const int nv = (Np / 2) * 8;
+  for (int i0 = tid; i0 < nv; i0 += 2 * kWideTF) {
+    uint4 v[2][4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const uint32_t o = opo(8 * c + e, 2 * j, 2 * Np);
-      *reinterpret_cast<uint16_t*>(S.vh + o) = eh[e];
-      *reinterpret_cast<uint16_t*>(S.vl + o) = el[e];
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + u * kWideTF;
+      const int jp = i >> 3, c8 = i & 7;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int j = 2 * jp + k;
+        v[u][2 * k] = v[u][2 * k + 1] = make_uint4(0u, 0u, 0u, 0u);
+        if (i < nv && j < N) {
+          const uint16_t* p = base + static_cast<long long>(j) * a.qkv.cstride + 2 * TKD + 8 * c8;
+          v[u][2 * k] = *reinterpret_cast<const uint4*>(p);
+          v[u][2 * k + 1] = *reinterpret_cast<const uint4*>(p + pl);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = i0 + u * kWideTF;
+      if (i >= nv) continue;
+      const int jp = i >> 3, c8 = i & 7;
+      const uint32_t col = static_cast<uint32_t>((jp >> 2) * 128 + (jp & 3) * 4);  // keys 2 jp, 2 jp + 1
+#pragma unroll
+      for (int pln = 0; pln < 2; ++pln) {
+        const uint4 ka = v[u][pln], kb = v[u][2 + pln];  // key 2 jp, key 2 jp + 1
+        const uint32_t wa[4] = {ka.x, ka.y, ka.z, ka.w}, wb[4] = {kb.x, kb.y, kb.z, kb.w};
+        uint8_t* vt = (pln == 0 ? S.vh : S.vl) + c8 * vsbo + col;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          // Channel 8 c8 + e: its bf16 of key 2 jp (low half) and 2 jp + 1.
+          const uint32_t w = __byte_perm(wa[e >> 1], wb[e >> 1], (e & 1) ? 0x7632 : 0x5410);
+          *reinterpret_cast<uint32_t*>(vt + e * 16) = w;
+        }
+      }
     }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -427,21 +453,42 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
 #pragma unroll
   for (int e = 0; e < 16; ++e) pe[e] = S.peb[d0 + e];
   if (qi < N) {
+    // One filter row at a time: its three pixels' loads (both planes, 16
+    // channels) in flight together; taps outside the image are skipped, in
+    // the reference's (ky, kx) order.
+#pragma unroll
     for (int ky = 0; ky < 3; ++ky) {
       const int iy = y - 1 + ky;
       if (iy < 0 || iy >= a.H) continue;
+      uint4 raw[3][4];
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        const int ix = x - 1 + kx;
+        const bool in = ix >= 0 && ix < a.W;
+        const uint16_t* vp = base + static_cast<long long>(iy * a.W + (in ? ix : x)) * a.qkv.cstride + 2 * TKD + d0;
+        raw[kx][0] = *reinterpret_cast<const uint4*>(vp);
+        raw[kx][1] = *reinterpret_cast<const uint4*>(vp + pl);
+        raw[kx][2] = *reinterpret_cast<const uint4*>(vp + 8);
+        raw[kx][3] = *reinterpret_cast<const uint4*>(vp + 8 + pl);
+      }
+#pragma unroll
       for (int kx = 0; kx < 3; ++kx) {
         const int ix = x - 1 + kx;
         if (ix < 0 || ix >= a.W) continue;
-        const uint16_t* vp = base + static_cast<long long>(iy * a.W + ix) * a.qkv.cstride + 2 * TKD + d0;
-        float v0[8], v1[8];
-        load8(vp, pl, v0);
-        load8(vp + 8, pl, v1);
         const float* w = S.pew[ky * 3 + kx] + d0;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) pe[e] = __fadd_rn(pe[e], __fmul_rn(v0[e], w[e]));
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint4 h = raw[kx][2 * hf], l = raw[kx][2 * hf + 1];
+          const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) pe[8 + e] = __fadd_rn(pe[8 + e], __fmul_rn(v1[e], w[8 + e]));
+          for (int q = 0; q < 4; ++q) {
+            const int e = 8 * hf + 2 * q;
+            const float v0 = bf16_bits_to_f(hw[q] & 0xFFFFu) + bf16_bits_to_f(lw[q] & 0xFFFFu);
+            const float v1 = bf16_bits_to_f(hw[q] >> 16) + bf16_bits_to_f(lw[q] >> 16);
+            pe[e] = __fadd_rn(pe[e], __fmul_rn(v0, w[e]));
+            pe[e + 1] = __fadd_rn(pe[e + 1], __fmul_rn(v1, w[e + 1]));
+          }
+        }
       }
     }
   }
@@ -491,7 +538,6 @@ __global__ void __launch_bounds__(kWideTF, 1) attention_wide_tc_kernel(const Att
     if (tid == 0 && ok && !*abort_flag) {
       const uint32_t idesc = idesc_bf16_f32(kTQ, THD);
       const uint32_t psbo = (2 * kChunkF / 16) * 128;
-      const uint32_t vsbo = static_cast<uint32_t>(2 * Np / 16) * 128u;
       const uint64_t dph = kmajor_desc_noswizzle(smem_u32(ph), 128, psbo);
       const uint64_t dpl = kmajor_desc_noswizzle(smem_u32(plo), 128, psbo);
       const uint32_t vo = static_cast<uint32_t>(c) * 1024u;  // 64 keys = 8 core matrices along K
