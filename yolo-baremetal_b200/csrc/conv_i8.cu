@@ -20,6 +20,7 @@
 // other roles, drains the tensor core and frees tensor memory.
 #include <cudaTypedefs.h>
 
+#include <cfloat>
 #include <climits>
 #include <cmath>
 #include <cstring>
@@ -512,6 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
       // Units of 32 channels: two TMEM loads, requantise (or dequantise),
       // then lanes 2k and 2k+1 write the two 16-byte halves of one pixel's
       // 32-byte run.
+      float rmax = -FLT_MAX;  // dequantised output with a row maximum
       for (int c = 0; c < nvalid; c += 32) {
         const bool two = c + 16 < nvalid;
         if (EPI == 4) {
@@ -540,6 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
                                        sb[n0 + c + e + 3]) *
                     a.deq[n0 + c + e + 3];
               *reinterpret_cast<float4*>(of + e) = v;
+              if (a.rowmax) rmax = fmaxf(fmaxf(rmax, fmaxf(v.x, v.y)), fmaxf(v.z, v.w));
             }
           }
           continue;
@@ -614,6 +617,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_i8_kernel(const __grid_const
           if (svalid && (h == 0 || two))
             *reinterpret_cast<uint4*>(a.out + spo + c + 16 * h) = make_uint4(w[0], w[1], w[2], w[3]);
         }
+      }
+      // The same sigmoid as the decode kernel's (accurate expf, IEEE division).
+      if (EPI == 4 && a.rowmax && valid) {
+        const long long fb = pm / HoWo;
+        a.rowmax[fb * a.rm_bstride + (pm - fb * HoWo)] = 1.0f / (1.0f + expf(-rmax));
       }
       tc_fence_before();
       __syncwarp();
@@ -766,6 +774,7 @@ cudaError_t launch_conv_i8(I8Args& a, const int8_t* x, long long x_cstride, long
   if (a.Co < 16 || a.Co % 16 || a.n_tile < 16 || a.n_tile % 16 || a.n_tiles < 1 || a.n_tile * a.n_tiles < a.Co ||
       (a.out && (a.out_cstride % 16 || a.out_coff % 16)) || (a.res && (a.res_cstride % 16 || a.res_coff % 16)) ||
       (!a.out && !a.out_f32) || (a.out_f32 && (a.f32_cstride % 4 || a.f32_bstride % 4 || a.f32_co % 4 || !a.deq)) ||
+      (a.rowmax && (!a.out_f32 || a.n_tiles != 1)) ||
       a.res_shift < 1 ||
       a.res_shift > 62 || x_cstride % 16 || x_bstride % 16 || reinterpret_cast<uintptr_t>(x) % 16) {
     if (why) *why = "int8 conv: unsupported view alignment or tile";

@@ -37,6 +37,7 @@
 // memory.
 #include <cudaTypedefs.h>
 
+#include <cfloat>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -552,6 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       uint32_t r[16], r2[16];
       tc_ld_32x32b_x16(tbase, r);
       if (stacked) tc_ld_32x32b_x16(tbase + a.n_tile, r2);
+      float rmax = -FLT_MAX;  // fp32 output with a row maximum
       for (int c = 0; c < nvalid; c += 16) {
         tc_wait_ld();
         tc_ld_dep(r);
@@ -603,6 +605,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           }
         }
         if (f32out) {
+          if (a.out_f32.rowmax) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c + e < nvalid) rmax = fmaxf(rmax, v[e]);
+          }
           if (valid) {
 #pragma unroll
             for (int g = 0; g < 2; ++g) {
@@ -657,6 +664,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           }
         }
       }
+      // The same sigmoid as the decode kernel's (accurate expf, IEEE division).
+      if (f32out && a.out_f32.rowmax && valid)
+        a.out_f32.rowmax[static_cast<long long>(b) * a.out_f32.rm_bstride + p] = 1.0f / (1.0f + expf(-rmax));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -1112,6 +1122,7 @@ cudaError_t launch_conv_tc(const ConvArgs& a, cudaStream_t s, int num_sms) {
   if ((a.lg_up0 || a.lg_up1) && (a.kh != 1 || a.kw != 1 || a.stride != 1 || a.pad != 0))
     return cudaErrorInvalidValue;
   if (a.n_tiles < 1 || a.n_tile * a.n_tiles < a.Co) return cudaErrorInvalidValue;
+  if (a.out_f32.rowmax && (!f32 || a.n_tiles != 1)) return cudaErrorInvalidValue;
   if (a.a_tma == 2 && (a.n_tiles != 1 || a.kh != 3 || a.kw != 3 || (a.Ci % 16 && a.Ci != 8) || a.tiles_x < 1 || a.tiles_y < 1 ||
                        a.m_tiles != a.B * a.tiles_y * a.tiles_x))
     return cudaErrorInvalidValue;

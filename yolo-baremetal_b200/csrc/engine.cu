@@ -1267,6 +1267,8 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
       lv.ptr = p->d_logits + static_cast<size_t>(base[s]) * nc;
       lv.bstride = static_cast<long long>(N) * nc;
       lv.cstride = nc;
+      lv.rowmax = p->d_maxscore + base[s];
+      lv.rm_bstride = N;
       YB_TRY(add_conv(wf, src_of(p1, 0, p1.C), 1, 0, kActNone, SOut(), SView(), lv));
       // The P3 and P4 heads read model.16 / model.19 only: side lanes 1 and
       // 2, beside the rest of the neck (inference plans).
@@ -1284,12 +1286,13 @@ cudaError_t Engine::build(Plan* p, std::string* why) {
     de.N = N;
     de.nc = nc;
     de.nscales = 3;
+    de.max_ready = 1;
     for (int s = 0; s < 3; ++s) {
       de.base[s] = base[s];
       de.w[s] = feats[s]->W;
       de.stride[s] = strides[s];
     }
-    add_op(kOpDecode, 0.0, 4.0 * B * N * (4.0 + nc + 4.0 + 1.0), [de](cudaStream_t st) { return launch_decode(de, st); });
+    add_op(kOpDecode, 0.0, 4.0 * B * N * (4.0 + 4.0), [de](cudaStream_t st) { return launch_decode(de, st); });
     ops.back().join = true;
     TopkArgs ta;
     ta.maxscore = p->d_maxscore;

@@ -254,6 +254,8 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   struct F32Out {
     float* ptr = nullptr;
     long long cstride = 0, bstride = 0;
+    float* rowmax = nullptr;  // sigmoid of each pixel's largest output
+    long long rm_bstride = 0;
   };
   // Convolution named P (P.conv.* or, plain, P.*) from `in` into `out`
   // (or dequantised into f32 when f32.ptr).  With `cap` the launch
@@ -372,6 +374,8 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
       a.f32_bstride = f32.bstride;
       a.f32_co = co;
       a.deq = static_cast<const float*>(dd);
+      a.rowmax = f32.rowmax;
+      a.rm_bstride = f32.rm_bstride;
     } else {
       a.out = out.base;
       a.out_cstride = out.cstride;
@@ -970,6 +974,8 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
     lv.ptr = p->d_logits + static_cast<size_t>(base[s]) * nc;
     lv.cstride = nc;
     lv.bstride = static_cast<long long>(N) * nc;
+    lv.rowmax = p->d_maxscore + base[s];
+    lv.rm_bstride = N;
     YB_TRY(conv(b3 + si + ".2", true, QT(), p1, 1, 0, false, nullptr, lv));
     // The P3 and P4 heads read model.16 / model.19 only: side lanes 1 and 2,
     // beside the rest of the neck.
@@ -987,12 +993,13 @@ cudaError_t Engine::build_i8(Plan* p, std::string* why) {
   de.N = N;
   de.nc = nc;
   de.nscales = 3;
+  de.max_ready = 1;
   for (int s = 0; s < 3; ++s) {
     de.base[s] = base[s];
     de.w[s] = feats[s]->W;
     de.stride[s] = strides[s];
   }
-  add_op(kOpDecode, 0.0, 4.0 * B * N * (4.0 + nc + 4.0 + 1.0), [de](cudaStream_t st) { return launch_decode(de, st); });
+  add_op(kOpDecode, 0.0, 4.0 * B * N * (4.0 + 4.0), [de](cudaStream_t st) { return launch_decode(de, st); });
   p->ops.back().join = true;
   TopkArgs ta;
   ta.maxscore = p->d_maxscore;

@@ -42,6 +42,8 @@ struct I8Args {
   long long f32_cstride = 0, f32_bstride = 0;  // element (b, p, n) at b*f32_bstride + p*f32_cstride + n
   int f32_co = 0;                              // channels stored (the rest of the tile is padding)
   const float* deq = nullptr;
+  float* rowmax = nullptr;  // optional: sigmoid(max over the f32_co outputs) per pixel, one N tile
+  long long rm_bstride = 0;
   int* err = nullptr;
   // Divisors of the per-tile index arithmetic, filled by launch_conv_i8:
   // stages, n_tiles, Ho*Wo, Wo, tiles_y*tiles_x and tiles_x.

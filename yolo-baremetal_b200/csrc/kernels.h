@@ -55,6 +55,11 @@ struct FOut {
   long long bstride = 0;
   int cstride = 0;
   int coff = 0;
+  // Optional: the sigmoid of the largest of a pixel's Co outputs at
+  // rowmax[b * rm_bstride + p] (pixel p of image b; one N tile only), the
+  // Detect head's per-anchor best class score.
+  float* rowmax = nullptr;
+  long long rm_bstride = 0;
 };
 
 enum Act : int { kActNone = 0, kActSiLU = 1 };
@@ -266,6 +271,7 @@ struct DecodeArgs {
   const float* logits = nullptr;
   float* boxes = nullptr;
   float* maxscore = nullptr;
+  int max_ready = 0;  // maxscore already written (by the class convolutions' epilogues)
   int B = 0, N = 0, nc = 0;
   int nscales = 0;
   int base[4] = {0, 0, 0, 0};

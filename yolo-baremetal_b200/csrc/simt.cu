@@ -540,7 +540,7 @@ __global__ void decode_kernel(const DecodeArgs a) {
   const long long total = static_cast<long long>(a.B) * a.N;
   const bool ok = idx < total;
   float m = -FLT_MAX;
-  if (ok) {
+  if (ok && !a.max_ready) {
     const float* lg = a.logits + idx * a.nc;
     if ((a.nc & 3) == 0) {
       const int n4 = a.nc >> 2;
@@ -555,7 +555,7 @@ __global__ void decode_kernel(const DecodeArgs a) {
   m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
   m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
   if (!ok || sub != 0) return;
-  a.maxscore[idx] = sigmoid(m);
+  if (!a.max_ready) a.maxscore[idx] = sigmoid(m);
   const int j = static_cast<int>(idx % a.N);
   int s = 0;
   while (s + 1 < a.nscales && j >= a.base[s + 1]) ++s;
