@@ -71,12 +71,18 @@ __device__ __forceinline__ void store8(uint16_t* hi, long long plane, const floa
   *reinterpret_cast<uint4*>(hi + plane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 }
 
-// SiLU without branches: __expf (ex2.approx based, ~2 ulp) and __fdividef
-// (approximate division; for x below about -87 the denominator overflows
-// and the result is 0, where the exact value is below 1e-36 in magnitude).
-// Callers add to the result with __fadd_rn (never contracted into an FMA
-// with the division's multiply), so that SiLU + residual rounds the same way
-// in every kernel.
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, __fadd_rn(1.0f, __expf(-x))); }
+// SiLU without branches: x * 1 / (1 + 2^(-x log2 e)), with the hardware's
+// approximate base-2 exponential and reciprocal in their flush-to-zero forms
+// (no denormal handling; about 2^-22 relative error each).  For x below
+// about -88 the exponential overflows to +inf and the result is -0 (the exact
+// value is below 1e-36 in magnitude).  The multiplies are explicitly rounded
+// and callers add to the result with __fadd_rn, so that SiLU + residual
+// rounds the same way in every kernel.
+__device__ __forceinline__ float silu_fast(float x) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(x, -1.4426950408889634f)));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, e)));
+  return __fmul_rn(x, r);
+}
 
 }  // namespace yb
