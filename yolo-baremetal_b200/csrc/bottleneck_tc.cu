@@ -349,12 +349,11 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
         tc_ld_dep(r);
         tc_ld_dep(r2);
         float v[16];
+        add_pairs<16>(v, reinterpret_cast<const float*>(r), reinterpret_cast<const float*>(r2));
+        add_pairs<16>(v, v, sb1 + u * 16);
+        silu_fast_n<16>(v);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]) + __uint_as_float(r2[e]);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] += sb1[u * 16 + e];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = inside ? silu_fast(v[e]) : 0.0f;
+        for (int e = 0; e < 16; ++e) v[e] = inside ? v[e] : 0.0f;
         uint32_t hw[8], lw[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) split2(v[2 * i], v[2 * i + 1], hw[i], lw[i]);
@@ -425,12 +424,9 @@ __global__ void __launch_bounds__(kThreads, 1) bottleneck_tc_kernel(const __grid
         tc_ld_dep(rr);
         tc_ld_dep(r2);
         float v[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(rr[e]) + __uint_as_float(r2[e]);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] += sb2[u * 16 + e];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = silu_fast(v[e]);
+        add_pairs<16>(v, reinterpret_cast<const float*>(rr), reinterpret_cast<const float*>(r2));
+        add_pairs<16>(v, v, sb2 + u * 16);
+        silu_fast_n<16>(v);
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
           const uint4 h = rh[2 * u + g];

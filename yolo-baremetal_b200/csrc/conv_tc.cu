@@ -559,8 +559,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         tc_ld_dep(r);
         if (stacked) tc_ld_dep(r2);
         float v[16];
+        if (stacked)
+          add_pairs<16>(v, reinterpret_cast<const float*>(r), reinterpret_cast<const float*>(r2));
+        else
 #pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]) + (stacked ? __uint_as_float(r2[e]) : 0.0f);
+          for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
         if (c + 16 < nvalid) {
           tc_ld_32x32b_x16(tbase + c + 16, r);
           if (stacked) tc_ld_32x32b_x16(tbase + a.n_tile + c + 16, r2);
@@ -568,10 +571,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
 #pragma unroll
         for (int e = 0; e < 16; e += 4) {
           const float4 bb = *reinterpret_cast<const float4*>(bias_t + c + e);
-          v[e + 0] += bb.x;
-          v[e + 1] += bb.y;
-          v[e + 2] += bb.z;
-          v[e + 3] += bb.w;
+          const float2 s0 = __fadd2_rn(make_float2(v[e], v[e + 1]), make_float2(bb.x, bb.y));
+          const float2 s1 = __fadd2_rn(make_float2(v[e + 2], v[e + 3]), make_float2(bb.z, bb.w));
+          v[e] = s0.x;
+          v[e + 1] = s0.y;
+          v[e + 2] = s1.x;
+          v[e + 3] = s1.y;
         }
         const bool stats = (EPI & 8) != 0 && valid;
         if (stats) {
@@ -579,10 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           for (int e = 0; e < 16; ++e)
             if (c + e < nvalid) mpre = fmaxf(mpre, fabsf(v[e]));
         }
-        if (EPI & 1) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = silu_fast(v[e]);
-        }
+        if (EPI & 1) silu_fast_n<16>(v);
         if (stats) {
 #pragma unroll
           for (int e = 0; e < 16; ++e)
@@ -596,8 +598,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           load8_rw(rb, a.res.plane, *reinterpret_cast<float(*)[8]>(&rv[0]));
           if (second) load8_rw(rb + 8, a.res.plane, *reinterpret_cast<float(*)[8]>(&rv[8]));
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (e < 8 || second) v[e] = __fadd_rn(v[e], rv[e]);
+          for (int e = 0; e < 16; e += 2) {
+            if (e < 8 || second) {
+              const float2 t = __fadd2_rn(make_float2(v[e], v[e + 1]), make_float2(rv[e], rv[e + 1]));
+              v[e] = t.x;
+              v[e + 1] = t.y;
+            }
+          }
           if (stats) {
 #pragma unroll
             for (int e = 0; e < 16; ++e)

@@ -331,10 +331,16 @@ __global__ void __launch_bounds__(256, 2) dw3x3_c4_kernel(const DwArgs a) {
   auto join = [&](const uint2 (&h)[3], const uint2 (&l)[3], float (&v)[3][4]) {
 #pragma unroll
     for (int kx = 0; kx < 3; ++kx) {
-      v[kx][0] = bf16_bits_to_f(h[kx].x & 0xFFFFu) + bf16_bits_to_f(l[kx].x & 0xFFFFu);
-      v[kx][1] = __uint_as_float(h[kx].x & 0xFFFF0000u) + __uint_as_float(l[kx].x & 0xFFFF0000u);
-      v[kx][2] = bf16_bits_to_f(h[kx].y & 0xFFFFu) + bf16_bits_to_f(l[kx].y & 0xFFFFu);
-      v[kx][3] = __uint_as_float(h[kx].y & 0xFFFF0000u) + __uint_as_float(l[kx].y & 0xFFFF0000u);
+      const float2 s0 =
+          __fadd2_rn(make_float2(bf16_bits_to_f(h[kx].x & 0xFFFFu), __uint_as_float(h[kx].x & 0xFFFF0000u)),
+                     make_float2(bf16_bits_to_f(l[kx].x & 0xFFFFu), __uint_as_float(l[kx].x & 0xFFFF0000u)));
+      const float2 s1 =
+          __fadd2_rn(make_float2(bf16_bits_to_f(h[kx].y & 0xFFFFu), __uint_as_float(h[kx].y & 0xFFFF0000u)),
+                     make_float2(bf16_bits_to_f(l[kx].y & 0xFFFFu), __uint_as_float(l[kx].y & 0xFFFF0000u)));
+      v[kx][0] = s0.x;
+      v[kx][1] = s0.y;
+      v[kx][2] = s1.x;
+      v[kx][3] = s1.y;
     }
   };
   float win[3][3][4];  // input rows y - 1, y, y + 1 of output row y, slot (row - y0 + 1) % 3
@@ -363,12 +369,16 @@ __global__ void __launch_bounds__(256, 2) dw3x3_c4_kernel(const DwArgs a) {
 #pragma unroll
       for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sum[e] = fmaf(win[(i + ky) % 3][kx][e], wk[ky * 3 + kx][e], sum[e]);
+        for (int e = 0; e < 4; e += 2) {
+          const float* wv = win[(i + ky) % 3][kx];
+          const float2 f = __ffma2_rn(make_float2(wv[e], wv[e + 1]),
+                                      make_float2(wk[ky * 3 + kx][e], wk[ky * 3 + kx][e + 1]),
+                                      make_float2(sum[e], sum[e + 1]));
+          sum[e] = f.x;
+          sum[e + 1] = f.y;
+        }
     if (a.amax) mpre = fmaxf(mpre, fmaxf(fmaxf(fabsf(sum[0]), fabsf(sum[1])), fmaxf(fabsf(sum[2]), fabsf(sum[3]))));
-    if (a.act == kActSiLU) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sum[e] = silu_fast(sum[e]);
-    }
+    if (a.act == kActSiLU) silu_fast_n<4>(sum);
     uint32_t hw0, lw0, hw1, lw1;
     split2(sum[0], sum[1], hw0, lw0);
     split2(sum[2], sum[3], hw1, lw1);

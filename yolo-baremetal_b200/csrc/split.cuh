@@ -31,8 +31,10 @@ __device__ __forceinline__ void load8(const uint16_t* hi, long long plane, float
   const uint32_t lw[4] = {l.x, l.y, l.z, l.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    v[2 * i] = bf16_bits_to_f(hw[i] & 0xFFFFu) + bf16_bits_to_f(lw[i] & 0xFFFFu);
-    v[2 * i + 1] = bf16_bits_to_f(hw[i] >> 16) + bf16_bits_to_f(lw[i] >> 16);
+    const float2 s = __fadd2_rn(make_float2(bf16_bits_to_f(hw[i] & 0xFFFFu), bf16_bits_to_f(hw[i] >> 16)),
+                                make_float2(bf16_bits_to_f(lw[i] & 0xFFFFu), bf16_bits_to_f(lw[i] >> 16)));
+    v[2 * i] = s.x;
+    v[2 * i + 1] = s.y;
   }
 }
 
@@ -44,23 +46,37 @@ __device__ __forceinline__ void load8_rw(const uint16_t* hi, long long plane, fl
   const uint32_t lw[4] = {l.x, l.y, l.z, l.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    v[2 * i] = bf16_bits_to_f(hw[i] & 0xFFFFu) + bf16_bits_to_f(lw[i] & 0xFFFFu);
-    v[2 * i + 1] = bf16_bits_to_f(hw[i] >> 16) + bf16_bits_to_f(lw[i] >> 16);
+    const float2 s = __fadd2_rn(make_float2(bf16_bits_to_f(hw[i] & 0xFFFFu), bf16_bits_to_f(hw[i] >> 16)),
+                                make_float2(bf16_bits_to_f(lw[i] & 0xFFFFu), bf16_bits_to_f(lw[i] >> 16)));
+    v[2 * i] = s.x;
+    v[2 * i + 1] = s.y;
   }
 }
 
 // Splits two values at once: packed (v0 in the low half) hi and lo words.
-// The remainders use explicitly rounded subtractions so that the compiler
-// never fuses them with the multiply that produced v0 / v1 (an FMA there
-// would take the remainder of the unrounded product): the split of a value
-// is then the same in every kernel, whatever code computed it.
+// The remainders are exact (v - hi needs no rounding) and computed as one
+// paired fused multiply-add with -1 (exact too), explicitly rounded so that
+// the compiler never fuses them with the multiply that produced v0 / v1 (an
+// FMA there would take the remainder of the unrounded product): the split of
+// a value is then the same in every kernel, whatever code computed it.
 __device__ __forceinline__ void split2(float v0, float v1, uint32_t& hi, uint32_t& lo) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
   hi = *reinterpret_cast<const uint32_t*>(&h);
-  const float r0 = __fsub_rn(v0, __uint_as_float(hi << 16));
-  const float r1 = __fsub_rn(v1, __uint_as_float(hi & 0xFFFF0000u));
-  const __nv_bfloat162 l = __floats2bfloat162_rn(r0, r1);
+  const float2 r = __ffma2_rn(make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xFFFF0000u)),
+                              make_float2(-1.0f, -1.0f), make_float2(v0, v1));
+  const __nv_bfloat162 l = __floats2bfloat162_rn(r.x, r.y);
   lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// Elementwise sums of N (even) values in pairs (one paired add per two).
+template <int N>
+__device__ __forceinline__ void add_pairs(float (&v)[N], const float* a, const float* b) {
+#pragma unroll
+  for (int e = 0; e < N; e += 2) {
+    const float2 s = __fadd2_rn(make_float2(a[e], a[e + 1]), make_float2(b[e], b[e + 1]));
+    v[e] = s.x;
+    v[e + 1] = s.y;
+  }
 }
 
 __device__ __forceinline__ void store8(uint16_t* hi, long long plane, const float (&v)[8]) {
@@ -78,11 +94,32 @@ __device__ __forceinline__ void store8(uint16_t* hi, long long plane, const floa
 // value is below 1e-36 in magnitude).  The multiplies are explicitly rounded
 // and callers add to the result with __fadd_rn, so that SiLU + residual
 // rounds the same way in every kernel.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float silu_fast(float x) {
-  float e, r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(x, -1.4426950408889634f)));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, e)));
-  return __fmul_rn(x, r);
+  return __fmul_rn(x, rcp_ftz(__fadd_rn(1.0f, ex2_ftz(__fmul_rn(x, -1.4426950408889634f)))));
+}
+// The same for N (even) values, the multiplies and adds paired: equal to
+// silu_fast on each value, bit for bit.
+template <int N>
+__device__ __forceinline__ void silu_fast_n(float (&v)[N]) {
+#pragma unroll
+  for (int e = 0; e < N; e += 2) {
+    const float2 x = make_float2(v[e], v[e + 1]);
+    const float2 t = __fmul2_rn(x, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+    const float2 d = __fadd2_rn(make_float2(1.0f, 1.0f), make_float2(ex2_ftz(t.x), ex2_ftz(t.y)));
+    const float2 y = __fmul2_rn(x, make_float2(rcp_ftz(d.x), rcp_ftz(d.y)));
+    v[e] = y.x;
+    v[e + 1] = y.y;
+  }
 }
 
 }  // namespace yb

@@ -197,10 +197,15 @@ __global__ void __launch_bounds__(kThreads, 4) stem_tc_kernel(const __grid_const
         const float4 b4 = *reinterpret_cast<const float4*>(sbias + 16 * u + 4 * e4);
         const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-        for (int e = 4 * e4; e < 4 * e4 + 4; ++e) v[e] = __uint_as_float(r1[e]) + __uint_as_float(r2[e]) + bb[e - 4 * e4];
+        for (int e = 4 * e4; e < 4 * e4 + 4; e += 2) {
+          const float2 t = __fadd2_rn(make_float2(__uint_as_float(r1[e]), __uint_as_float(r1[e + 1])),
+                                      make_float2(__uint_as_float(r2[e]), __uint_as_float(r2[e + 1])));
+          const float2 u2 = __fadd2_rn(t, make_float2(bb[e - 4 * e4], bb[e + 1 - 4 * e4]));
+          v[e] = u2.x;
+          v[e + 1] = u2.y;
+        }
       }
-#pragma unroll
-      for (int e = 0; e < 16; ++e) v[e] = silu_fast(v[e]);
+      silu_fast_n<16>(v);
       uint32_t h8[8], l8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) split2(v[2 * i], v[2 * i + 1], h8[i], l8[i]);
