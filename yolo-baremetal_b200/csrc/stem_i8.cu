@@ -14,8 +14,12 @@
 // kind::i8 UMMAs against the weights (int32 accumulation in tensor memory);
 // every thread then requantises its pixel's accumulator row (the convolution
 // epilogue's code, i8_requant.cuh) and stores 16 bytes per 16 channels.
-// Several CTAs per SM overlap each other's phases.  The products are exact,
-// so the result equals the dp4a form of the rule bit for bit.
+// The A tile and the accumulator are double-buffered and the epilogue of
+// tile i runs after the UMMAs of tile i + 1 are issued, so each CTA's
+// tensor-core round trip overlaps its own quantisation and requantisation;
+// several CTAs per SM overlap the rest.  The products are exact, so the
+// result equals the dp4a form of the rule bit for bit.
+#include "fastdiv.h"
 #include "i8_requant.cuh"
 #include "i8k.h"
 #include "pdl.cuh"
@@ -25,7 +29,6 @@ namespace yb {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kCtasPerSm = 6;
 constexpr int kTH = 8, kTW = 16;                    // output tile
 constexpr int kPR = 2 * kTH + 1, kPC = 2 * kTW + 4;  // input patch: rows 2 oy0 - 1.., columns 2 ox0 - 4..
 constexpr int kPatch = 3 * kPR * kPC;                // floats per fp32 patch
@@ -56,27 +59,53 @@ __device__ __forceinline__ uint32_t quant_byte(float v, float s, float r) {
   return static_cast<uint32_t>(min(max(q, -127), 127)) & 0xFFu;
 }
 
+// This thread's 16-byte chunks of a patch (the same in every tile): chunk
+// i = tid + 128 k is patch row i / 9 (channel, row) and column 4 (i % 9).
+struct StemI8Chunks {
+  long long goff[4];  // channel plane offset
+  uint32_t sdst[4];   // shared byte offset in a patch buffer
+  int rr[4], q4[4];   // patch row within the channel, first column
+};
+
+__device__ __forceinline__ StemI8Chunks stem_i8_chunks(const StemI8Args& a) {
+  StemI8Chunks ch;
+  const long long plane = static_cast<long long>(a.H) * a.W;
+  constexpr int Q = kPC / 4;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = static_cast<int>(threadIdx.x) + kThreads * k;
+    const int row = i / Q, q = i - row * Q;
+    const int c = row / kPR;
+    ch.rr[k] = row - c * kPR;
+    ch.q4[k] = 4 * q;
+    ch.goff[k] = c * plane;
+    ch.sdst[k] = static_cast<uint32_t>((row * kPC + 4 * q) * 4);
+  }
+  return ch;
+}
+
 // The fp32 input patch of tile t into sx: 16-byte copies when every row
-// starts 16-byte aligned (W a multiple of 4), else 4-byte copies; positions
-// outside the image arrive as zeros.
-__device__ __forceinline__ void stem_fetch(const StemI8Args& a, float* sx, int t, int tiles_x, int tiles_y) {
-  const int b = t / (tiles_x * tiles_y);
-  const int rem = t - b * tiles_x * tiles_y;
-  const int iy0 = (rem / tiles_x) * kTH * 2 - 1, ix0 = (rem % tiles_x) * kTW * 2 - 4;
+// starts 16-byte aligned (W a multiple of 4, the input 16-byte aligned),
+// else 4-byte copies; positions outside the image arrive as zeros.
+__device__ __forceinline__ void stem_fetch(const StemI8Args& a, const StemI8Chunks& ch, float* sx, int t,
+                                           const FastDiv& fd_per, const FastDiv& fd_tx) {
+  const int b = static_cast<int>(fd_per.div(static_cast<uint32_t>(t)));
+  const int rem = t - b * static_cast<int>(fd_per.d);
+  const int ty = static_cast<int>(fd_tx.div(static_cast<uint32_t>(rem)));
+  const int iy0 = ty * kTH * 2 - 1, ix0 = (rem - ty * static_cast<int>(fd_tx.d)) * kTW * 2 - 4;
   const long long plane = static_cast<long long>(a.H) * a.W;
   const float* inb = a.in + static_cast<long long>(b) * 3 * plane;
-  if ((a.W & 3) == 0) {
-    constexpr int Q = kPC / 4;
-    for (int i = threadIdx.x; i < 3 * kPR * Q; i += kThreads) {
-      const int row = i / Q;
-      const int q = i - row * Q;
-      const int c = row / kPR;
-      const int rr = row - c * kPR;
-      const int iy = iy0 + rr, ix = ix0 + 4 * q;
+  if ((a.W & 3) == 0 && (reinterpret_cast<uintptr_t>(a.in) & 15) == 0) {
+    constexpr int kChunks = 3 * kPR * (kPC / 4);  // 459: three per thread, a fourth for the first 75
+    const uint32_t sbase = smem_u32(sx);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (k == 3 && static_cast<int>(threadIdx.x) >= kChunks - 3 * kThreads) break;
+      const int iy = iy0 + ch.rr[k], ix = ix0 + ch.q4[k];
       const int nvalid = (iy >= 0 && iy < a.H && ix >= 0) ? min(4, a.W - ix) : 0;
-      const float* src = nvalid > 0 ? inb + c * plane + static_cast<long long>(iy) * a.W + ix : inb;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sx + (c * kPR + rr) * kPC + 4 * q)),
-                   "l"(src), "r"(nvalid > 0 ? 4 * nvalid : 0)
+      const float* src = nvalid > 0 ? inb + ch.goff[k] + static_cast<long long>(iy) * a.W + ix : a.in;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sbase + ch.sdst[k]), "l"(src),
+                   "r"(nvalid > 0 ? 4 * nvalid : 0)
                    : "memory");
     }
   } else {
@@ -94,19 +123,24 @@ __device__ __forceinline__ void stem_fetch(const StemI8Args& a, float* sx, int t
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// CTAs per SM: shared memory allows six; the 64-channel form's two
+// 64-column accumulators allow four in tensor memory.
+__host__ __device__ constexpr int stem_i8_ctas(int co) { return co == 64 ? 4 : 6; }
+
 template <int CO>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) stem_i8_tc_kernel(const __grid_constant__ StemI8Args a,
-                                                                           int tiles_x, int tiles_y) {
+__global__ void __launch_bounds__(kThreads, stem_i8_ctas(CO)) stem_i8_tc_kernel(const __grid_constant__ StemI8Args a,
+                                                                                 FastDiv fd_per, FastDiv fd_tx) {
   constexpr uint32_t kBLbo = static_cast<uint32_t>(CO) * 16u;  // K-direction core-matrix stride of B
-  constexpr uint32_t kCols = CO < 32 ? 32u : static_cast<uint32_t>(CO);
-  __shared__ __align__(1024) uint8_t sa[kATile];
+  constexpr uint32_t kAcc = static_cast<uint32_t>(CO);          // columns per accumulator
+  constexpr uint32_t kCols = 2 * CO < 32 ? 32u : static_cast<uint32_t>(2 * CO);
+  __shared__ __align__(1024) uint8_t sa[2][kATile];
   __shared__ __align__(128) uint8_t sbw[4 * kBLbo];
   __shared__ __align__(16) float sx[2][kPatch];  // fp32 patches (double buffer)
   __shared__ uint32_t sqw[kPR * kPC];             // quantised patch, one word per input pixel
   __shared__ int4 sq[CO];  // {M, D low, D high, shift - 32}, D = bias * M + 2^(shift-1) - 1
   __shared__ int32_t sbias[CO];
   __shared__ int8_t slut[256];
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar[2];
   __shared__ uint32_t tslot;
 
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -131,7 +165,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) stem_i8_tc_kernel(const 
   }
   for (int i = tid; i < 256; i += kThreads) slut[i] = a.lut[i];
   if (tid == 0) {
-    mbar_init(&mbar, 1);
+    mbar_init(&mbar[0], 1);
+    mbar_init(&mbar[1], 1);
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -148,59 +183,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) stem_i8_tc_kernel(const 
 
   const float rcp = __frcp_rn(a.s_in);
   const uint32_t idesc = idesc_s8_s32(128, CO);
-  const uint32_t sa_addr = smem_u32(sa), sb_addr = smem_u32(sbw);
-  const int tiles = a.B * tiles_x * tiles_y;
+  const uint32_t sb_addr = smem_u32(sbw);
+  const int tiles = a.B * static_cast<int>(fd_per.d);
   const int r = tid >> 4, cx = tid & 15;  // this thread's output pixel in the tile
+  const StemI8Chunks ch = stem_i8_chunks(a);
   volatile int never = 0;
-  int it = 0;
-  if (static_cast<int>(blockIdx.x) < tiles) stem_fetch(a, sx[0], blockIdx.x, tiles_x, tiles_y);
-  for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
-    const int tn = t + gridDim.x;
-    // The next tile's patch goes into the other buffer, quantised two
-    // iterations ago (the barrier at the end of the last iteration).
-    if (tn < tiles) stem_fetch(a, sx[(it + 1) & 1], tn, tiles_x, tiles_y);
-    if (tn < tiles) asm volatile("cp.async.wait_group 1;" ::: "memory");
-    else asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    const float* px = sx[it & 1];
-    for (int i = tid; i < kPR * kPC; i += kThreads)
-      sqw[i] = quant_byte(px[i], a.s_in, rcp) | (quant_byte(px[kPR * kPC + i], a.s_in, rcp) << 8) |
-               (quant_byte(px[2 * kPR * kPC + i], a.s_in, rcp) << 16);
-    __syncthreads();
-    // Tap (ky, kx) of output pixel (r, cx): input row 2 r + ky, column
-    // 2 cx - 1 + kx of the tile's origin, patch column 2 cx + kx + 3.
-    uint32_t wq[16];
-#pragma unroll
-    for (int ky = 0; ky < 3; ++ky)
-#pragma unroll
-      for (int kx = 0; kx < 3; ++kx) wq[ky * 3 + kx] = sqw[(2 * r + ky) * kPC + 2 * cx + kx + 3];
-#pragma unroll
-    for (int k = 9; k < 16; ++k) wq[k] = 0u;
-#pragma unroll
-    for (int kc = 0; kc < 4; ++kc)
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sa_addr + a_off(tid, kc)), "r"(wq[4 * kc]),
-                   "r"(wq[4 * kc + 1]), "r"(wq[4 * kc + 2]), "r"(wq[4 * kc + 3])
-                   : "memory");
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const uint64_t da = kmajor_desc_noswizzle(sa_addr, kALbo, kASbo);
-      const uint64_t db = kmajor_desc_noswizzle(sb_addr, kBLbo, 128);
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks)
-        tc_mma_i8(tmem, da + ((2u * ks * kALbo) >> 4), db + ((2u * ks * kBLbo) >> 4), idesc, ks != 0 ? 1u : 0u);
-      tc_commit(&mbar);
-    }
-    const int b = t / (tiles_x * tiles_y);
-    const int rem = t - b * tiles_x * tiles_y;
-    const int oy = (rem / tiles_x) * kTH + r, ox = (rem % tiles_x) * kTW + cx;
-    if (!mbar_wait(&mbar, static_cast<uint32_t>(it & 1), &never, kWaitNs)) {
+  // Epilogue of this CTA's j-th tile (accumulator j & 1).
+  auto epilogue = [&](int j) {
+    const int t = static_cast<int>(blockIdx.x) + j * static_cast<int>(gridDim.x);
+    if (!mbar_wait(&mbar[j & 1], static_cast<uint32_t>((j >> 1) & 1), &never, kWaitNs)) {
       if (a.err) atomicCAS(a.err, 0, kErrWaitAccFull);
     }
     tc_fence_after();
-    const uint32_t tb = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int b = static_cast<int>(fd_per.div(static_cast<uint32_t>(t)));
+    const int rem = t - b * static_cast<int>(fd_per.d);
+    const int ty = static_cast<int>(fd_tx.div(static_cast<uint32_t>(rem)));
+    const int oy = ty * kTH + r, ox = (rem - ty * static_cast<int>(fd_tx.d)) * kTW + cx;
+    const uint32_t tb = tmem + (j & 1) * kAcc + (static_cast<uint32_t>(warp * 32) << 16);
     const bool valid = oy < a.Ho && ox < a.Wo;
     int8_t* o = a.out.p + static_cast<long long>(b) * a.out.bstride +
                 (static_cast<long long>(oy) * a.Wo + ox) * a.out.cstride;
@@ -225,9 +224,55 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) stem_i8_tc_kernel(const 
       if (valid) *reinterpret_cast<uint4*>(o + 16 * u) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
     tc_fence_before();
-    __syncthreads();  // the accumulator, the A tile and the quantised patch are free for the next tile
+  };
+  int it = 0;
+  if (static_cast<int>(blockIdx.x) < tiles) stem_fetch(a, ch, sx[0], blockIdx.x, fd_per, fd_tx);
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+    const int tn = t + gridDim.x;
+    // The next tile's patch goes into the other buffer, quantised by the last
+    // iteration before its barriers.
+    if (tn < tiles) stem_fetch(a, ch, sx[(it + 1) & 1], tn, fd_per, fd_tx);
+    if (tn < tiles) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // the patch has landed; the last iteration's gathers from sqw are done
+    const float* px = sx[it & 1];
+    for (int i = tid; i < kPR * kPC; i += kThreads)
+      sqw[i] = quant_byte(px[i], a.s_in, rcp) | (quant_byte(px[kPR * kPC + i], a.s_in, rcp) << 8) |
+               (quant_byte(px[2 * kPR * kPC + i], a.s_in, rcp) << 16);
+    __syncthreads();
+    // Tap (ky, kx) of output pixel (r, cx): input row 2 r + ky, column
+    // 2 cx - 1 + kx of the tile's origin, patch column 2 cx + kx + 3.  A
+    // stage it & 1 was last read by the UMMAs of two tiles ago, complete
+    // before the last epilogue.
+    uint32_t wq[16];
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) wq[ky * 3 + kx] = sqw[(2 * r + ky) * kPC + 2 * cx + kx + 3];
+#pragma unroll
+    for (int k = 9; k < 16; ++k) wq[k] = 0u;
+    const uint32_t sa_addr = smem_u32(sa[it & 1]);
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc)
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sa_addr + a_off(tid, kc)), "r"(wq[4 * kc]),
+                   "r"(wq[4 * kc + 1]), "r"(wq[4 * kc + 2]), "r"(wq[4 * kc + 3])
+                   : "memory");
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint64_t da = kmajor_desc_noswizzle(sa_addr, kALbo, kASbo);
+      const uint64_t db = kmajor_desc_noswizzle(sb_addr, kBLbo, 128);
+      const uint32_t d = tmem + (it & 1) * kAcc;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        tc_mma_i8(d, da + ((2u * ks * kALbo) >> 4), db + ((2u * ks * kBLbo) >> 4), idesc, ks != 0 ? 1u : 0u);
+      tc_commit(&mbar[it & 1]);
+    }
+    if (it > 0) epilogue(it - 1);
   }
-  tc_fence_before();
+  if (it > 0) epilogue(it - 1);
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
@@ -246,16 +291,17 @@ cudaError_t launch_stem_i8(const StemI8Args& a, cudaStream_t st) {
     return cudaErrorInvalidValue;
   const int tiles_x = (a.Wo + kTW - 1) / kTW, tiles_y = (a.Ho + kTH - 1) / kTH;
   const long long tiles = static_cast<long long>(a.B) * tiles_x * tiles_y;
-  if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (tiles > 0x7fffffffLL - 4096) return cudaErrorInvalidValue;
   if (tiles == 0) return cudaSuccess;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long cap = static_cast<long long>(kCtasPerSm) * sms;
+  const long long cap = static_cast<long long>(stem_i8_ctas(a.Co)) * sms;
   const unsigned grid = static_cast<unsigned>(tiles < cap ? tiles : cap);
-  if (a.Co == 16) return launch_pdl(stem_i8_tc_kernel<16>, dim3(grid), dim3(kThreads), 0, st, a, tiles_x, tiles_y);
-  if (a.Co == 32) return launch_pdl(stem_i8_tc_kernel<32>, dim3(grid), dim3(kThreads), 0, st, a, tiles_x, tiles_y);
-  return launch_pdl(stem_i8_tc_kernel<64>, dim3(grid), dim3(kThreads), 0, st, a, tiles_x, tiles_y);
+  const FastDiv fd_per(static_cast<uint32_t>(tiles_x * tiles_y)), fd_tx(static_cast<uint32_t>(tiles_x));
+  if (a.Co == 16) return launch_pdl(stem_i8_tc_kernel<16>, dim3(grid), dim3(kThreads), 0, st, a, fd_per, fd_tx);
+  if (a.Co == 32) return launch_pdl(stem_i8_tc_kernel<32>, dim3(grid), dim3(kThreads), 0, st, a, fd_per, fd_tx);
+  return launch_pdl(stem_i8_tc_kernel<64>, dim3(grid), dim3(kThreads), 0, st, a, fd_per, fd_tx);
 }
 
 }  // namespace yb
