@@ -324,6 +324,41 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def parse_cpulist(text):
+    """CPU ids of a sysfs cpulist such as "0-55,112-167"."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if part:
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def bind_to_gpu_numa_node(dev):
+    """Restricts this process to the CPUs of the NUMA node that hosts GPU
+    `dev`'s PCIe link, before any pinned host buffer is allocated: the pages
+    are then placed on that node (first touch) and the host<->device copies
+    do not cross the socket interconnect.  Returns the node, or None where
+    sysfs does not tell it (the process is then left unbound)."""
+    import torch
+
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read())
+        if node < 0:
+            return None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            cpus = parse_cpulist(f.read()) & os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return node
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -335,6 +370,7 @@ def run_ours(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    numa_node = bind_to_gpu_numa_node(local)
     dist = None
     gather_group = None
     if world > 1:
@@ -451,7 +487,8 @@ def run_ours(args):
                 "data": DATA, "config": config(world, B, H),
                 "e2e": {"value": world * B * args.steps / es_s, "unit": UNIT,
                         "h2d_bytes_per_step": world * host_in.numel() * 4,
-                        "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": STREAM_NOTE},
+                        "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": STREAM_NOTE,
+                        "pinned_buffers_numa_node_rank0": numa_node},
                 "e2e_sync": {"value": world * B * args.steps / e2e_s, "unit": UNIT,
                              "h2d_bytes_per_step": world * host_in.numel() * 4,
                              "d2h_bytes_per_step": world * host_out.numel() * 4, "mode": SYNC_NOTE},
