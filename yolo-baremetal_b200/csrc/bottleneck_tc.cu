@@ -82,7 +82,7 @@ __device__ __forceinline__ void window_mma(uint32_t d, uint64_t ah, uint64_t al,
       const uint64_t ao = static_cast<uint64_t>((tap / 3) * ROWW + tap % 3) + static_cast<uint64_t>(cb) * (2u * CHUNK / 16u);
       const uint64_t bo = static_cast<uint64_t>(step >> 2) * chunk_units + static_cast<uint64_t>((step & 3) * 2);
       tc_mma_bf16(d, ah + ao, bh + bo, idesc, step != 0 ? 1u : 0u);
-      tc_mma_bf16(d, al + ao, bh + bo, idesc, 1u);
+      tc_mma_bf16(d, al + ao, bh + bo, idesc_half_n(idesc), 1u);
     }
   }
 }
@@ -106,7 +106,7 @@ __device__ __forceinline__ void pair_mma(uint32_t d, uint64_t hb, uint64_t lb, u
     const uint64_t off = static_cast<uint64_t>(o0 >> 4) | (static_cast<uint64_t>(lbo >> 4) << 16);
     const uint64_t bo = static_cast<uint64_t>(s2 >> 2) * chunk_units + static_cast<uint64_t>((s2 & 3) * 2);
     tc_mma_bf16(d, hb + off, bh + bo, idesc, s2 != 0 ? 1u : 0u);
-    tc_mma_bf16(d, lb + off, bh + bo, idesc, 1u);
+    tc_mma_bf16(d, lb + off, bh + bo, idesc_half_n(idesc), 1u);
   }
 }
 

@@ -111,7 +111,7 @@ __device__ __forceinline__ void patch_tile_mma(uint32_t d, uint64_t dah0, uint64
       const uint32_t accum = step != 0 ? 1u : 0u;
       if (ST) {
         tc_mma_bf16(d, dah0 + ao, dbh0 + boff, idesc, accum);
-        tc_mma_bf16(d, dal0 + ao, dbh0 + boff, idesc, 1u);
+        tc_mma_bf16(d, dal0 + ao, dbh0 + boff, idesc_half_n(idesc), 1u);
       } else {
         tc_mma_bf16(d, dah0 + ao, dbh0 + boff, idesc, accum);
         tc_mma_bf16(d, dah0 + ao, dbl0 + boff, idesc, 1u);
@@ -150,7 +150,7 @@ __device__ __forceinline__ void patch8_tile_mma(uint32_t d, uint64_t hb, uint64_
     const uint32_t accum = s2 != 0 ? 1u : 0u;
     if (ST) {
       tc_mma_bf16(d, hb + off, dbh0 + boff, idesc, accum);
-      tc_mma_bf16(d, lb + off, dbh0 + boff, idesc, 1u);
+      tc_mma_bf16(d, lb + off, dbh0 + boff, idesc_half_n(idesc), 1u);
     } else {
       tc_mma_bf16(d, hb + off, dbh0 + boff, idesc, accum);
       tc_mma_bf16(d, hb + off, dbl0 + boff, idesc, 1u);
@@ -213,9 +213,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   // Accumulators of acc_stride (power of two >= n_tile) columns, as many as
   // fit in the 512 TMEM columns up to kMaxAcc.
   // Patch mode (MMA-issue bound: many small K steps per tile) with
-  // n_tile <= 128: each K step is two UMMAs of N = 2 n_tile against the
-  // stacked [B_hi; B_lo] chunk (columns [0, n) += A*B_hi, [n, 2n) += A*B_lo,
-  // summed by the epilogue).  Otherwise three UMMAs of N = n_tile, which
+  // n_tile <= 128: each K step is two UMMAs against the stacked
+  // [B_hi; B_lo] chunk, A_hi with N = 2 n_tile (columns [0, n) += A_hi*B_hi,
+  // [n, 2n) += A_hi*B_lo) and A_lo with N = n_tile (B_hi only: columns
+  // [0, n) += A_lo*B_hi), summed by the epilogue.  Otherwise three UMMAs of N = n_tile, which
   // keeps the epilogue (the long pole there) to one TMEM load per unit.
   // The im2col / gather modes stack too for 3x3 convolutions of at most 64
   // output channels (MMA-issue bound: measured ~45-64 cycles per UMMA at
@@ -752,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 const uint32_t accum = step != 0 ? 1u : 0u;
                 if (stacked) {
                   tc_mma_bf16(d_tmem, dah, dbh0 + boff, idesc, accum);
-                  tc_mma_bf16(d_tmem, dal, dbh0 + boff, idesc, 1u);
+                  tc_mma_bf16(d_tmem, dal, dbh0 + boff, idesc_half_n(idesc), 1u);
                 } else {
                   tc_mma_bf16(d_tmem, dah, dbh0 + boff, idesc, accum);
                   tc_mma_bf16(d_tmem, dah, dbl0 + boff, idesc, 1u);
@@ -791,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 const uint32_t accum = step != 0 ? 1u : 0u;
                 if (stacked) {
                   tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + boff, idesc, accum);
-                  tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + boff, idesc, 1u);
+                  tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + boff, idesc_half_n(idesc), 1u);
                 } else {
                   tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + boff, idesc, accum);
                   tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + boff, idesc, 1u);
@@ -840,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                                                 : koff;
             if (stacked) {
               tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
-              tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc, 1u);
+              tc_mma_bf16(d_tmem, dal0 + aoff, dbh0 + koff, idesc_half_n(idesc), 1u);
             } else {
               tc_mma_bf16(d_tmem, dah0 + aoff, dbh0 + koff, idesc, (kc | ks) != 0 ? 1u : 0u);
               tc_mma_bf16(d_tmem, dah0 + aoff, dbl0 + koff, idesc, 1u);

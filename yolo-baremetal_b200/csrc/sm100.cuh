@@ -270,6 +270,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// The same instruction descriptor with N halved: against a stacked
+// [B_hi; B_lo] operand (B_hi rows first) the UMMA then reads B_hi only.
+__host__ __device__ constexpr uint32_t idesc_half_n(uint32_t idesc) {
+  return (idesc & ~(0x3Fu << 17)) | ((((idesc >> 17) & 0x3Fu) >> 1) << 17);
+}
+
 // Byte offset of the 16-byte chunk `chunk` (0..7) of row `row` inside a
 // 128B-swizzled K-major tile whose base is 1024-byte aligned.
 __host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
